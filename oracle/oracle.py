@@ -1,0 +1,298 @@
+"""TEST INFRASTRUCTURE -- ctypes access to the two CPU checkers.
+
+* `RefGraph`: the reference's OWN CPU graph compiled from its sources
+  (oracle/_ref/libeg2ref.so, recipe in oracle/Makefile), driven through
+  vendor/embeddinggemma.c/src/gemma2_fast.c:919 `ei_gemma2_embed_batch_fast_ctx`.
+* `Port`: the plain-C restatement oracle/eg2_oracle.c (scalar tier), with
+  per-operator entry points for the GPU operator tests.
+
+Only tests/, __graft_entry__.smoke() and bench.py's CPU-baseline arm import
+this module; the product never does.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+import struct
+import subprocess
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+REF_SO = os.path.join(HERE, "_ref", "libeg2ref.so")
+PORT_SO = os.path.join(HERE, "_build", "libeg2oracle.so")
+
+GGML_F32, GGML_F16, GGML_Q8_0, GGML_BF16 = 0, 1, 8, 30
+
+
+def build(ref: bool = True) -> None:
+    """Compile the restatement, and the reference when its sources exist."""
+    subprocess.run(["make", "-s", "-C", HERE, "port"], check=True)
+    ref_root = os.environ.get("REF_ROOT", "/root/reference")
+    if ref and os.path.isdir(os.path.join(ref_root, "vendor")):
+        subprocess.run(["make", "-s", "-C", HERE, "ref", f"REF_ROOT={ref_root}"], check=True)
+
+
+# ---------------------------------------------------------------------------
+# GGUF v3 reader (numpy memmap), same format as vendor/embeddinggemma.c/src/gguf.c
+# ---------------------------------------------------------------------------
+class Gguf:
+    def __init__(self, path: str):
+        self.path = path
+        self.map = np.memmap(path, dtype=np.uint8, mode="r")
+        buf = self.map
+        pos = 0
+
+        def take(n):
+            nonlocal pos
+            b = bytes(buf[pos:pos + n])
+            pos += n
+            return b
+
+        def u32():
+            return struct.unpack("<I", take(4))[0]
+
+        def u64():
+            return struct.unpack("<Q", take(8))[0]
+
+        def string():
+            return take(u64()).decode()
+
+        sizes = {0: 1, 1: 1, 2: 2, 3: 2, 4: 4, 5: 4, 6: 4, 7: 1, 10: 8, 11: 8, 12: 8}
+        assert take(4) == b"GGUF" and u32() == 3
+        n_t, n_kv = u64(), u64()
+        self.kv = {}
+        for _ in range(n_kv):
+            key, typ = string(), u32()
+            if typ == 8:
+                self.kv[key] = string()
+            elif typ == 9:
+                at, n = u32(), u64()
+                if at == 8:
+                    self.kv[key] = [string() for _ in range(n)]
+                else:
+                    self.kv[key] = take(sizes[at] * n)
+            else:
+                raw = take(sizes[typ])
+                self.kv[key] = int.from_bytes(raw, "little")
+        align = int(self.kv.get("general.alignment", 32))
+        infos = []
+        for _ in range(n_t):
+            name = string()
+            nd = u32()
+            ne = [u64() for _ in range(nd)] + [1] * (4 - nd)
+            typ, off = u32(), u64()
+            infos.append((name, ne, typ, off))
+        data_off = (pos + align - 1) // align * align
+        self.tensors = {}
+        for name, ne, typ, off in infos:
+            n = ne[0] * ne[1] * ne[2] * ne[3]
+            nbytes = {GGML_F32: 4 * n, GGML_F16: 2 * n, GGML_BF16: 2 * n, GGML_Q8_0: n // 32 * 34}[typ]
+            self.tensors[name] = (ne, typ, self.map[data_off + off: data_off + off + nbytes])
+
+    def raw(self, name: str) -> np.ndarray:
+        return self.tensors[name][2]
+
+    def f32(self, name: str) -> np.ndarray:
+        return self.raw(name).view(np.float32)
+
+    def q8(self, name: str):
+        """(int8 codes [rows][k], fp16 scale bits uint16 [rows][k/32])."""
+        ne, typ, raw = self.tensors[name]
+        assert typ == GGML_Q8_0
+        blk = np.asarray(raw).reshape(-1, 34)
+        d = np.ascontiguousarray(blk[:, :2]).view(np.uint16).reshape(ne[1], ne[0] // 32)
+        q = np.ascontiguousarray(blk[:, 2:]).view(np.int8).reshape(ne[1], ne[0])
+        return q, d
+
+    def pointer_table(self):
+        """Tensor pointers in the order oracle/eg2_oracle.h documents."""
+        names = ["token_embd.weight", "per_layer_model_proj.weight", "per_layer_proj_norm.weight"]
+        for l in range(24):
+            names += [f"blk.{l}.{s}.weight" for s in (
+                "attn_norm", "attn_q", "attn_k", "attn_v", "attn_output", "attn_q_norm",
+                "attn_k_norm", "post_attention_norm", "ffn_norm", "ffn_up", "ffn_gate",
+                "ffn_down", "post_ffw_norm", "inp_gate", "proj", "post_norm", "layer_output_scale")]
+        names += ["output_norm.weight", "output.weight"]
+        arr = (C.c_void_p * len(names))()
+        for i, nm in enumerate(names):
+            arr[i] = self.raw(nm).ctypes.data
+        return arr
+
+
+def _ptr(a: np.ndarray):
+    return C.c_void_p(a.ctypes.data)
+
+
+class RefGraph:
+    """The reference's compiled CPU graph (gemma2_fast.c / gemma2.c)."""
+
+    def __init__(self, model_path: str, threads: int = 0):
+        if not os.path.exists(REF_SO):
+            raise FileNotFoundError(f"{REF_SO} missing: run `make -C oracle ref` where the reference exists")
+        self.lib = C.CDLL(REF_SO)
+        L = self.lib
+        L.eg2ref_open.restype = C.c_void_p
+        L.eg2ref_open.argtypes = [C.c_char_p, C.c_int]
+        L.eg2ref_close.argtypes = [C.c_void_p]
+        L.eg2ref_threads.argtypes = [C.c_void_p]
+        L.eg2ref_embed_fast.argtypes = [C.c_void_p, C.c_void_p, C.c_void_p, C.c_size_t, C.c_void_p,
+                                        C.c_char_p, C.c_size_t]
+        L.eg2ref_embed_reference.argtypes = [C.c_void_p, C.c_void_p, C.c_size_t, C.c_void_p,
+                                             C.c_char_p, C.c_size_t]
+        L.eg2ref_normalize_prefix.argtypes = [C.c_void_p, C.c_int]
+        L.eg2ref_quantize_row_q8_0.argtypes = [C.c_void_p, C.c_void_p, C.c_int]
+        L.eg2ref_fp32_to_fp16.argtypes = [C.c_float]
+        L.eg2ref_fp32_to_fp16.restype = C.c_uint16
+        L.eg2ref_gelu_mul_row.argtypes = [C.c_void_p, C.c_void_p, C.c_int]
+        self.handle = L.eg2ref_open(model_path.encode(), threads)
+        self.threads = L.eg2ref_threads(self.handle)
+
+    @property
+    def tier(self) -> str:
+        lvl = self.lib.eg2ref_x86_tier()
+        name = {0: "scalar", 1: "avx2", 2: "avxvnni", 3: "vnni512"}.get(lvl, str(lvl))
+        return name + ("+gemm512" if self.lib.eg2ref_x86_wide512() else "")
+
+    def embed(self, ids: np.ndarray, offsets: np.ndarray) -> np.ndarray:
+        ids = np.ascontiguousarray(ids, dtype=np.int32)
+        offsets = np.ascontiguousarray(offsets, dtype=np.uint64)
+        batch = len(offsets) - 1
+        out = np.zeros((batch, 768), np.float32)
+        err = C.create_string_buffer(256)
+        if not self.lib.eg2ref_embed_fast(self.handle, _ptr(ids), _ptr(offsets), batch, _ptr(out), err, 256):
+            raise RuntimeError(err.value.decode())
+        return out
+
+    def embed_reference_graph(self, ids: np.ndarray) -> np.ndarray:
+        ids = np.ascontiguousarray(ids, dtype=np.int32)
+        out = np.zeros(768, np.float32)
+        err = C.create_string_buffer(256)
+        if not self.lib.eg2ref_embed_reference(self.handle, _ptr(ids), len(ids), _ptr(out), err, 256):
+            raise RuntimeError(err.value.decode())
+        return out
+
+    def normalize_prefix(self, emb: np.ndarray, dims: int) -> np.ndarray:
+        e = np.array(emb, dtype=np.float32, copy=True)
+        if not self.lib.eg2ref_normalize_prefix(_ptr(e), dims):
+            raise ValueError("unsupported dimensions")
+        return e[:dims]
+
+    def quantize_x86(self, x: np.ndarray):
+        x = np.ascontiguousarray(x, dtype=np.float32)
+        blk = np.zeros((x.size // 32, 34), np.uint8)
+        self.lib.eg2ref_quantize_row_q8_0(_ptr(x), _ptr(blk), x.size)
+        d = np.ascontiguousarray(blk[:, :2]).view(np.uint16).ravel()
+        q = np.ascontiguousarray(blk[:, 2:]).view(np.int8).ravel()
+        return q, d
+
+    def gelu_mul(self, g: np.ndarray, u: np.ndarray | None) -> np.ndarray:
+        g = np.array(g, dtype=np.float32, copy=True)
+        up = _ptr(np.ascontiguousarray(u, dtype=np.float32)) if u is not None else None
+        self.lib.eg2ref_gelu_mul_row(_ptr(g), up, g.size)
+        return g
+
+    def close(self):
+        if self.handle:
+            self.lib.eg2ref_close(self.handle)
+            self.handle = None
+
+
+class Port:
+    """The C restatement oracle/eg2_oracle.c (scalar tier)."""
+
+    ROUND_SCALAR, ROUND_X86 = 0, 1
+
+    def __init__(self):
+        if not os.path.exists(PORT_SO):
+            build(ref=False)
+        self.lib = C.CDLL(PORT_SO)
+        L = self.lib
+        vp, i, f = C.c_void_p, C.c_int, C.c_float
+        L.eg2o_fp32_to_fp16.argtypes = [f]
+        L.eg2o_fp32_to_fp16.restype = C.c_uint16
+        L.eg2o_fp16_to_fp32.argtypes = [C.c_uint16]
+        L.eg2o_fp16_to_fp32.restype = f
+        L.eg2o_quantize.argtypes = [vp, vp, vp, i, i]
+        L.eg2o_gelu_mul.argtypes = [vp, vp, i, i]
+        L.eg2o_gemm_q8.argtypes = [vp, vp, vp, vp, i, i, i, vp]
+        L.eg2o_gemm_q8_blockdots.argtypes = [vp, vp, i, i, i, vp]
+        L.eg2o_gemm_bf16.argtypes = [vp, vp, i, i, i, vp]
+        L.eg2o_rms_row.argtypes = [vp, i, vp]
+        L.eg2o_rope_tables.argtypes = [i, vp, vp]
+        L.eg2o_attention.argtypes = [vp, vp, vp, vp, vp, i, i, i, i, vp]
+        L.eg2o_embed_batch.argtypes = [vp, vp, vp, C.c_size_t, vp, i, i, vp]
+
+    def quantize(self, x, mode=ROUND_X86):
+        x = np.ascontiguousarray(x, dtype=np.float32).ravel()
+        q = np.zeros(x.size, np.int8)
+        d = np.zeros(x.size // 32, np.uint16)
+        self.lib.eg2o_quantize(_ptr(x), _ptr(q), _ptr(d), x.size, mode)
+        return q, d
+
+    def gelu_mul(self, g, u, mode=1):
+        g = np.array(g, dtype=np.float32, copy=True).ravel()
+        up = _ptr(np.ascontiguousarray(u, dtype=np.float32).ravel()) if u is not None else None
+        self.lib.eg2o_gelu_mul(_ptr(g), up, g.size, mode)
+        return g
+
+    def gemm_q8(self, wq, wd, xq, xd):
+        m, k = wq.shape
+        n = xq.shape[0]
+        y = np.zeros((n, m), np.float32)
+        self.lib.eg2o_gemm_q8(_ptr(np.ascontiguousarray(wq)), _ptr(np.ascontiguousarray(wd)),
+                              _ptr(np.ascontiguousarray(xq)), _ptr(np.ascontiguousarray(xd)), n, k, m, _ptr(y))
+        return y
+
+    def gemm_q8_blockdots(self, wq, xq):
+        m, k = wq.shape
+        n = xq.shape[0]
+        D = np.zeros((n, m, k // 32), np.int32)
+        self.lib.eg2o_gemm_q8_blockdots(_ptr(np.ascontiguousarray(wq)), _ptr(np.ascontiguousarray(xq)), n, k, m, _ptr(D))
+        return D
+
+    def gemm_bf16(self, w_bits, x):
+        m, k = w_bits.shape
+        n = x.shape[0]
+        y = np.zeros((n, m), np.float32)
+        self.lib.eg2o_gemm_bf16(_ptr(np.ascontiguousarray(w_bits)), _ptr(np.ascontiguousarray(x, dtype=np.float32)),
+                                n, k, m, _ptr(y))
+        return y
+
+    def rms_rows(self, x, w):
+        x = np.array(x, dtype=np.float32, copy=True)
+        d = x.shape[-1]
+        rows = x.reshape(-1, d)
+        wp = _ptr(np.ascontiguousarray(w, dtype=np.float32)) if w is not None else None
+        for r in range(rows.shape[0]):
+            self.lib.eg2o_rms_row(C.c_void_p(rows[r:].ctypes.data), d, wp)
+        return x
+
+    def rope_tables(self, d):
+        c = np.zeros((8192, d // 2), np.float32)
+        s = np.zeros((8192, d // 2), np.float32)
+        self.lib.eg2o_rope_tables(d, _ptr(c), _ptr(s))
+        return c, s
+
+    def attention(self, q, k, v, lo, hi, kv, d, window):
+        n = q.shape[0]
+        a = np.zeros((n, 4 * d), np.float32)
+        self.lib.eg2o_attention(_ptr(np.ascontiguousarray(q, dtype=np.float32)),
+                                _ptr(np.ascontiguousarray(k, dtype=np.float32)),
+                                _ptr(np.ascontiguousarray(v, dtype=np.float32)),
+                                _ptr(np.ascontiguousarray(lo, dtype=np.uint32)),
+                                _ptr(np.ascontiguousarray(hi, dtype=np.uint32)), n, kv, d, window, _ptr(a))
+        return a
+
+    def embed(self, model: Gguf, ids, offsets, quant_mode=ROUND_SCALAR, gelu_mode=0, dump_layers=False):
+        ids = np.ascontiguousarray(ids, dtype=np.int32)
+        offsets = np.ascontiguousarray(offsets, dtype=np.uint64)
+        batch = len(offsets) - 1
+        n = int(offsets[-1])
+        out = np.zeros((batch, 768), np.float32)
+        xl = np.zeros((25, n, 512), np.float32) if dump_layers else None
+        rc = self.lib.eg2o_embed_batch(model.pointer_table(), _ptr(ids), _ptr(offsets), batch, _ptr(out),
+                                       quant_mode, gelu_mode, _ptr(xl) if dump_layers else None)
+        if rc:
+            raise RuntimeError("oracle rejected the wave")
+        return (out, xl) if dump_layers else out
