@@ -1,0 +1,253 @@
+// Device helpers shared by the sm_100a kernels: mbarriers with bounded waits,
+// TMA tile loads, tcgen05 (TMEM allocation, MMA, commit, loads) and the exact
+// scalar arithmetic the reference CPU graph uses.
+#pragma once
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace eg2 {
+
+// Set by any bounded wait that ran out (see wait_bar); read by the host after a
+// wave.  A kernel that sees it set at start skips its work.  Defined here: the
+// library has a single device translation unit (kernels.cu).
+__device__ int g_error = 0;
+enum : int { ERR_NONE = 0, ERR_WAIT_TIMEOUT = 1 };
+
+// ---------------------------------------------------------------- basics
+__device__ __forceinline__ uint32_t smem_u32(const void *p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ uint64_t globaltimer_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+__device__ __forceinline__ bool elect_one() {
+    uint32_t pred = 0;
+    asm volatile(
+        "{\n\t.reg .b32 r;\n\t.reg .pred p;\n\t"
+        "elect.sync r|p, 0xffffffff;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(pred));
+    return pred != 0;
+}
+
+// ---------------------------------------------------------------- mbarrier
+__device__ __forceinline__ void bar_init(uint64_t *bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
+}
+__device__ __forceinline__ void fence_bar_init() {
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+__device__ __forceinline__ void bar_arrive(uint64_t *bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+__device__ __forceinline__ void bar_expect_tx(uint64_t *bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+                 : "memory");
+}
+__device__ __forceinline__ bool bar_try_wait(uint64_t *bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+// Every wait on a barrier is bounded: after ~2 s (or, when abort is given,
+// once another thread of the CTA gave up) it returns false and records
+// ERR_WAIT_TIMEOUT, so a lost arrival can never hang the GPU.  Waits used to
+// drain this CTA's own in-flight copies / MMAs before exit pass abort = nullptr.
+__device__ __forceinline__ bool wait_bar(uint64_t *bar, uint32_t parity, volatile int *abort) {
+    if (bar_try_wait(bar, parity)) return true;
+    const uint64_t start = globaltimer_ns();
+    for (uint32_t i = 1;; ++i) {
+        if (bar_try_wait(bar, parity)) return true;
+        if ((i & 255u) == 0) {
+            if (abort && *abort) return false;
+            if (globaltimer_ns() - start > 2000000000ull) {
+                if (abort) *abort = 1;
+                atomicExch(&g_error, ERR_WAIT_TIMEOUT);
+                return false;
+            }
+        }
+    }
+}
+
+// ---------------------------------------------------------------- TMA
+__device__ __forceinline__ void tma_prefetch(const CUtensorMap *map) {
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
+}
+// 2-D tiled load (no multicast); c0 is the innermost coordinate in elements and
+// every caller passes a multiple of the 128-byte swizzle row, so c0 * element
+// size is always a multiple of 16 bytes.
+__device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, uint64_t *bar, int c0, int c1) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];" ::"r"(
+            smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(c1)
+        : "memory");
+}
+
+// ---------------------------------------------------------------- tcgen05
+__device__ __forceinline__ void tmem_alloc(uint32_t *dst_smem, uint32_t ncols) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(dst_smem)),
+                 "r"(ncols)
+                 : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish() {
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_commit(uint64_t *bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+                 : "memory");
+}
+// D[tmem] (+)= A[smem] . B[smem]^T, int8 x int8 -> int32, one K=32 step.
+__device__ __forceinline__ void mma_i8(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                       uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+// D[tmem] (+)= A . B^T, bf16 x bf16 -> fp32, one K=16 step.
+__device__ __forceinline__ void mma_f16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                        uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+// Instruction descriptors (tcgen05 instruction-descriptor bit layout):
+// [4,6) D format, [7,10) A format, [10,13) B format, [15] A MN-major,
+// [16] B MN-major, [17,23) N>>3, [24,29) M>>4.  A and B always share a type.
+__host__ __device__ constexpr uint32_t idesc_i8(int M, int N) {
+    return (2u << 4) | (1u << 7) | (1u << 10) | (uint32_t(N >> 3) << 17) | (uint32_t(M >> 4) << 24);
+}
+__host__ __device__ constexpr uint32_t idesc_bf16(int M, int N) {
+    return (1u << 4) | (1u << 7) | (1u << 10) | (uint32_t(N >> 3) << 17) | (uint32_t(M >> 4) << 24);
+}
+// Shared-memory matrix descriptor for a K-major operand written by TMA with
+// 128-byte swizzle: rows of 128 B, 8-row atoms of 1024 B (SBO), version 1,
+// layout type 2 (SWIZZLE_128B).  Advancing along K inside the 128-byte row is
+// done by adding the byte offset to the start address (atom bases stay
+// 1024-byte aligned).
+__device__ __forceinline__ uint64_t desc_sw128(uint32_t saddr) {
+    return (uint64_t)((saddr & 0x3FFFFu) >> 4) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) |
+           ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
+}
+// 32 lanes x 32 consecutive 32-bit TMEM columns -> 32 registers per thread.
+// Warp-collective: every lane of the warp must execute it.
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t *r) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+        "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+        "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+          "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]),
+          "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]),
+          "=r"(r[30]), "=r"(r[31])
+        : "r"(taddr));
+}
+__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+// ---------------------------------------------------------------- exact scalar math
+// fp32 -> fp16 bits with the reference's rounding (quants.c:13-37): ties on
+// bit 12 round up in magnitude, which is not round-to-nearest-even.
+__device__ __forceinline__ uint16_t ref_fp32_to_fp16(float f) {
+    const uint32_t x = __float_as_uint(f);
+    const uint32_t sign = (x >> 16) & 0x8000u;
+    uint32_t mant = x & 0x7FFFFFu;
+    const int32_t e = int32_t((x >> 23) & 0xFFu) - 112;
+    if (e <= 0) {
+        if (e < -10) return uint16_t(sign);
+        mant |= 0x800000u;
+        const uint32_t shift = uint32_t(14 - e);
+        uint32_t half = sign | (mant >> shift);
+        if ((mant >> (shift - 1u)) & 1u) half++;
+        return uint16_t(half);
+    }
+    if (e >= 31) return uint16_t(sign | 0x7C00u | (mant ? ((mant >> 13) | 1u) : 0u));
+    uint32_t half = sign | (uint32_t(e) << 10) | (mant >> 13);
+    if (mant & 0x1000u) half++;
+    return uint16_t(half);
+}
+__device__ __forceinline__ float fp16_bits_to_f32(uint16_t h) { return __half2float(__ushort_as_half(h)); }
+
+// Q8_0 block quantization of 32 values held one per lane of a full warp,
+// following gemma2_fast_x86.c:211-234: d = amax/127 (IEEE), scale stored as the
+// reference's fp16 rounding of d, id = 1/d, q = trunc(x*id +- 0.5).
+// Returns the code; *scale_out receives the widened fp16 scale (lane-uniform).
+__device__ __forceinline__ int8_t quant_lane32(float x, float *scale_out) {
+    float amax = fabsf(x);
+#pragma unroll
+    for (int o = 16; o; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+    const float d = __fdiv_rn(amax, 127.0f);
+    const float id = d != 0.0f ? __fdiv_rn(1.0f, d) : 0.0f;
+    *scale_out = fp16_bits_to_f32(ref_fp32_to_fp16(d));
+    const float v = __fmul_rn(x, id);
+    const float t = __fadd_rn(v, copysignf(0.5f, v));
+    int q = __float2int_rz(t);
+    q = q < -128 ? -128 : (q > 127 ? 127 : q);
+    return int8_t(q);
+}
+
+// exp(x) by Cody-Waite reduction and a degree-6 polynomial: the reference's own
+// x86 GELU helper (gemma2_fast_x86.c:291-306), evaluated with the same fused
+// and unfused operations so that results match it bit for bit.
+__device__ __forceinline__ float ref_exp8(float x) {
+    x = fminf(fmaxf(x, -87.0f), 88.0f);
+    const float n = rintf(__fmul_rn(x, 1.44269504088896341f));
+    float r = __fmaf_rn(-n, 0.693359375f, x);
+    r = __fmaf_rn(-n, -2.12194440e-4f, r);
+    float p = 1.0f / 720;
+    p = __fmaf_rn(p, r, 1.0f / 120);
+    p = __fmaf_rn(p, r, 1.0f / 24);
+    p = __fmaf_rn(p, r, 1.0f / 6);
+    p = __fmaf_rn(p, r, 0.5f);
+    p = __fmaf_rn(p, r, 1.0f);
+    p = __fmaf_rn(p, r, 1.0f);
+    return __fmul_rn(p, __uint_as_float(uint32_t(int32_t(n) + 127) << 23));
+}
+// gelu_tanh(x) with tanh(v) = 1 - 2/(exp(2v)+1) (gemma2_fast_x86.c:308-325).
+__device__ __forceinline__ float ref_gelu(float x) {
+    float inner = __fmul_rn(__fmul_rn(0.79788456080286535588f, x), __fmaf_rn(__fmul_rn(0.044715f, x), x, 1.0f));
+    inner = fminf(fmaxf(inner, -9.0f), 9.0f);
+    const float t = __fsub_rn(1.0f, __fdiv_rn(2.0f, __fadd_rn(ref_exp8(__fmul_rn(2.0f, inner)), 1.0f)));
+    return __fmul_rn(__fmul_rn(0.5f, x), __fadd_rn(1.0f, t));
+}
+
+// RMS scale 1/sqrt(sum/d + 1e-6) from a double sum of squares rounded to
+// float, as gemma2_fast.c:587-590,667-671 computes it.
+__device__ __forceinline__ float rms_scale(double sumsq, int d) {
+    const float s = __double2float_rn(sumsq);
+    return __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(s, float(d)), 1e-6f)));
+}
+__device__ __forceinline__ double warp_sum_d(double v) {
+#pragma unroll
+    for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+__device__ __forceinline__ float warp_sum_f(float v) {
+#pragma unroll
+    for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+}  // namespace eg2

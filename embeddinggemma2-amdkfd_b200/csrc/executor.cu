@@ -1,0 +1,587 @@
+// EmbeddingGemma 2 packed-wave executor for B200: the C ABI of
+// include/eg2_executor.h, replacing src/gemma2_kfd.cpp of the reference.
+//
+// Structure (reference -> here):
+//   KFD context, queue, code object (gemma2_kfd.cpp:86-155)
+//       -> one CUDA stream per context on a chosen device, kernel attributes;
+//   GGUF bytes copied to GTT, arena for 2048 tokens (:111-115)
+//       -> Q8_0 weights repacked once into int8 code planes + fp32 block-scale
+//          planes (TMA-friendly rows), q/k/v fused into one projection per
+//          layer; token_embd kept as GGUF blocks for the gather; device arena
+//          sized for 2048 packed tokens;
+//   PM4/AQL command buffers with a wait after every dispatch and chunked
+//   flushes (:156-225) -> one CUDA graph per wave shape (tokens, sequences),
+//          captured on first use and replayed;
+//   host bounds / RoPE tables (:286-296) -> per-token bounds and positions
+//          uploaded per wave; RoPE tables built once with the reference CPU
+//          graph's expression (gemma2_fast.c:116-129);
+//   30 s submit/wait timeout and poisoning (:21,190-214) -> a deadline while
+//          polling the wave's completion event, plus the device error word set
+//          by bounded in-kernel waits; either poisons the context.
+#include <chrono>
+#include <cmath>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <map>
+#include <mutex>
+#include <stdexcept>
+#include <string>
+#include <thread>
+#include <vector>
+
+#include "../../include/eg2_executor.h"
+#include "launch.h"
+
+namespace {
+using namespace eg2;
+
+constexpr unsigned CAP = 2048;  // packed tokens per wave: the reference's KFD cap (gemma2_kfd.cpp:20)
+constexpr int VOCAB = 262144;
+constexpr double TIMEOUT_S = 30.0;  // gemma2_kfd.cpp:21
+
+void ck(cudaError_t e, const char *what) {
+    if (e != cudaSuccess) throw std::runtime_error(std::string(what) + ": " + cudaGetErrorString(e));
+}
+
+// gemma2_kfd.cpp:270-278: the same checks, in the same order, with its messages.
+void validate_wave(const int32_t *ids, const size_t *offsets, size_t batch) {
+    if (!ids || !offsets || !batch || batch > CAP || offsets[0] || offsets[batch] > CAP)
+        throw std::runtime_error("KFD batch requires 1..2048 packed tokens and nonempty sequences");
+    for (size_t s = 0; s < batch; ++s)
+        if (offsets[s + 1] <= offsets[s]) throw std::runtime_error("invalid KFD sequence offsets");
+    const size_t n = offsets[batch];
+    for (size_t i = 0; i < n; ++i)
+        if (ids[i] < 0 || ids[i] >= VOCAB) throw std::runtime_error("token ID out of range");
+}
+
+struct Q8Weight {
+    int8_t *codes = nullptr;  // [rows][k]
+    float *scales = nullptr;  // [k/32][rows]
+    int rows = 0, k = 0;
+    CUtensorMap tmap{};
+    int bn = 64;
+};
+
+struct Layer {
+    int d = 256, kv = 2;
+    Q8Weight qkv, o, up, gate, down, inp_gate, proj;
+    const float *attn_norm = nullptr, *q_norm = nullptr, *k_norm = nullptr, *post_attn_norm = nullptr,
+                *ffn_norm = nullptr, *post_ffw_norm = nullptr, *post_norm = nullptr, *out_scale = nullptr;
+};
+
+struct Profiler {
+    cudaStream_t s;
+    std::vector<std::string> names;
+    std::vector<cudaEvent_t> events;
+    void mark(const char *name) {
+        cudaEvent_t e;
+        ck(cudaEventCreate(&e), "cudaEventCreate");
+        events.push_back(e);
+        names.emplace_back(name);
+        ck(cudaEventRecord(e, s), "cudaEventRecord");
+    }
+    ~Profiler() {
+        for (auto e : events) cudaEventDestroy(e);
+    }
+};
+
+struct Backend {
+    const ei_gguf *model;
+    int device = 0;
+    cudaStream_t stream = nullptr;
+    std::mutex mutex;
+    bool poisoned = false;
+
+    std::vector<void *> allocations;
+    std::vector<Layer> layers;
+    Q8Weight output;
+    const uint8_t *token_embd = nullptr;
+    const void *ple_w = nullptr;
+    const float *ple_norm = nullptr, *output_norm = nullptr;
+    float *rope_cos[2] = {}, *rope_sin[2] = {};
+
+    // arena
+    int *ids = nullptr;
+    unsigned *bounds = nullptr, *pos = nullptr, *offsets = nullptr;
+    float *x = nullptr, *ple = nullptr, *qkv = nullptr, *attn = nullptr, *h = nullptr, *up = nullptr,
+          *gate = nullptr, *y = nullptr, *pooled = nullptr, *xs = nullptr;
+    void *x_hi = nullptr, *x_lo = nullptr, *qh = nullptr, *kh = nullptr, *vh = nullptr;
+    int8_t *xq = nullptr;
+    CUtensorMap tm_xq[3]{}, tm_hi{}, tm_lo{}, tm_ple{};
+
+    // host staging (pinned)
+    uint32_t *h_in = nullptr;  // ids | bounds(2) | pos | offsets
+    float *h_out = nullptr;
+    cudaEvent_t done = nullptr;
+
+    // graphs per wave shape
+    std::map<uint64_t, cudaGraphExec_t> graphs;
+    unsigned staged_n = 0;
+    size_t staged_batch = 0;
+    cudaGraphExec_t staged_graph = nullptr;
+    int kernels_per_wave = 0;
+
+    template <class T>
+    T *dalloc(size_t count) {
+        void *p = nullptr;
+        ck(cudaMalloc(&p, count * sizeof(T) + 256), "cudaMalloc");
+        allocations.push_back(p);
+        return static_cast<T *>(p);
+    }
+
+    const ei_tensor *tensor(const std::string &name) const {
+        for (uint64_t i = 0; i < model->n_tensors; i++) {
+            const ei_tensor &t = model->tensors[i];
+            if (t.name.len == name.size() && !std::memcmp(t.name.str, name.data(), t.name.len)) return &t;
+        }
+        throw std::runtime_error("missing tensor: " + name);
+    }
+    void check_shape(const ei_tensor *t, uint64_t k, uint64_t m, uint32_t type, const std::string &name) const {
+        if (t->ne[0] != k || t->ne[1] != m || t->ne[2] != 1 || t->ne[3] != 1 || t->type != type)
+            throw std::runtime_error("unsupported tensor " + name);
+    }
+    uint64_t kv_u64(const char *key) const {
+        for (uint64_t i = 0; i < model->n_kv; i++) {
+            const ei_kv &kv = model->kv[i];
+            if (kv.key.len == std::strlen(key) && !std::memcmp(kv.key.str, key, kv.key.len)) return kv.v.u64;
+        }
+        return 0;
+    }
+
+    // f32 norm weight -> device (tensor must be F32, as gemma2_kfd.cpp:81-85 requires).
+    const float *norm_weight(const std::string &name, uint64_t len, float *&cursor) {
+        const ei_tensor *t = tensor(name);
+        check_shape(t, len, 1, 0, name);
+        float *dst = cursor;
+        ck(cudaMemcpy(dst, t->data, len * 4, cudaMemcpyHostToDevice), "norm upload");
+        cursor += (len + 63) / 64 * 64;
+        return dst;
+    }
+
+    // GGUF Q8_0 [rows][k] -> SoA planes at row offset `row0` of a fused weight.
+    void repack(const std::string &name, int k, int rows, Q8Weight &w, int row0, uint8_t *staging) {
+        const ei_tensor *t = tensor(name);
+        check_shape(t, uint64_t(k), uint64_t(rows), 8, name);
+        ck(cudaMemcpyAsync(staging, t->data, t->n_bytes, cudaMemcpyHostToDevice, stream), "weight upload");
+        ck(launch_repack_q8(staging, rows, k, w.codes + size_t(row0) * k, w.scales + row0, w.rows, stream), "repack");
+        ck(cudaStreamSynchronize(stream), "repack sync");  // staging is reused by the next tensor
+    }
+    void alloc_q8(Q8Weight &w, int rows, int k) {
+        w.rows = rows, w.k = k;
+        w.codes = dalloc<int8_t>(size_t(rows) * k);
+        w.scales = dalloc<float>(size_t(rows) * (k / 32));
+        w.bn = (rows % 128 == 0 && rows >= 1024) ? 128 : 64;
+    }
+    void finish_q8(Q8Weight &w) {
+        if (!q8_tmap(&w.tmap, w.codes, uint64_t(w.k), uint64_t(w.rows), uint32_t(w.bn)))
+            throw std::runtime_error("cuTensorMapEncodeTiled failed for a weight");
+    }
+
+    Backend(const ei_gguf *g, int dev) : model(g), device(dev) {
+        if (!g) throw std::runtime_error("empty model");
+        // gemma2.c:30-62 hyperparameters.
+        if (kv_u64("gemma-embedding2.block_count") != 24 || kv_u64("gemma-embedding2.embedding_length") != 512 ||
+            kv_u64("gemma-embedding2.feed_forward_length") != 2048 ||
+            kv_u64("gemma-embedding2.embedding_length_out") != 768 ||
+            kv_u64("gemma-embedding2.attention.sliding_window") != 1024)
+            throw std::runtime_error("unsupported EmbeddingGemma 2 hyperparameters");
+        int count = 0;
+        ck(cudaGetDeviceCount(&count), "cudaGetDeviceCount");
+        if (device < 0 || device >= count)
+            throw std::runtime_error("CUDA device " + std::to_string(device) + " not found");
+        ck(cudaSetDevice(device), "cudaSetDevice");
+        cudaDeviceProp prop;
+        ck(cudaGetDeviceProperties(&prop, device), "cudaGetDeviceProperties");
+        if (prop.major != 10 || prop.minor != 0)
+            throw std::runtime_error(std::string("supported CUDA device not found (sm_100 required, got ") +
+                                     prop.name + ")");
+        ck(cudaStreamCreateWithFlags(&stream, cudaStreamNonBlocking), "cudaStreamCreate");
+        ck(cudaEventCreateWithFlags(&done, cudaEventDisableTiming), "cudaEventCreate");
+        ck(init_kernel_attributes(), "kernel attributes");
+
+        // ---- weights
+        const ei_tensor *emb = tensor("token_embd.weight");
+        check_shape(emb, 512, VOCAB, 8, "token_embd.weight");
+        auto *emb_d = dalloc<uint8_t>(emb->n_bytes);
+        ck(cudaMemcpy(emb_d, emb->data, emb->n_bytes, cudaMemcpyHostToDevice), "token_embd upload");
+        token_embd = emb_d;
+        const ei_tensor *plew = tensor("per_layer_model_proj.weight");
+        check_shape(plew, 512, 24 * 512, 30, "per_layer_model_proj.weight");
+        auto *ple_d = dalloc<uint8_t>(plew->n_bytes);
+        ck(cudaMemcpy(ple_d, plew->data, plew->n_bytes, cudaMemcpyHostToDevice), "PLE upload");
+        ple_w = ple_d;
+
+        float *norms = dalloc<float>(size_t(256) * 1024);
+        float *cur = norms;
+        ple_norm = norm_weight("per_layer_proj_norm.weight", 512, cur);
+        output_norm = norm_weight("output_norm.weight", 512, cur);
+        uint8_t *staging = dalloc<uint8_t>(size_t(2048) * 2048 / 32 * 34);
+        layers.resize(24);
+        for (int l = 0; l < 24; ++l) {
+            Layer &L = layers[l];
+            L.d = l % 6 == 5 ? 512 : 256, L.kv = 512 / L.d;
+            const std::string p = "blk." + std::to_string(l) + ".";
+            auto nm = [&](const char *s) { return p + s + ".weight"; };
+            L.attn_norm = norm_weight(nm("attn_norm"), 512, cur);
+            L.q_norm = norm_weight(nm("attn_q_norm"), L.d, cur);
+            L.k_norm = norm_weight(nm("attn_k_norm"), L.d, cur);
+            L.post_attn_norm = norm_weight(nm("post_attention_norm"), 512, cur);
+            L.ffn_norm = norm_weight(nm("ffn_norm"), 512, cur);
+            L.post_ffw_norm = norm_weight(nm("post_ffw_norm"), 512, cur);
+            L.post_norm = norm_weight(nm("post_norm"), 512, cur);
+            L.out_scale = norm_weight(nm("layer_output_scale"), 1, cur);
+            alloc_q8(L.qkv, 4 * L.d + 1024, 512);
+            repack(nm("attn_q"), 512, 4 * L.d, L.qkv, 0, staging);
+            repack(nm("attn_k"), 512, 512, L.qkv, 4 * L.d, staging);
+            repack(nm("attn_v"), 512, 512, L.qkv, 4 * L.d + 512, staging);
+            alloc_q8(L.o, 512, 4 * L.d);
+            repack(nm("attn_output"), 4 * L.d, 512, L.o, 0, staging);
+            alloc_q8(L.up, 2048, 512);
+            repack(nm("ffn_up"), 512, 2048, L.up, 0, staging);
+            alloc_q8(L.gate, 2048, 512);
+            repack(nm("ffn_gate"), 512, 2048, L.gate, 0, staging);
+            alloc_q8(L.down, 512, 2048);
+            repack(nm("ffn_down"), 2048, 512, L.down, 0, staging);
+            alloc_q8(L.inp_gate, 512, 512);
+            repack(nm("inp_gate"), 512, 512, L.inp_gate, 0, staging);
+            alloc_q8(L.proj, 512, 512);
+            repack(nm("proj"), 512, 512, L.proj, 0, staging);
+            for (Q8Weight *w : {&L.qkv, &L.o, &L.up, &L.gate, &L.down, &L.inp_gate, &L.proj}) finish_q8(*w);
+        }
+        alloc_q8(output, 768, 512);
+        repack("output.weight", 512, 768, output, 0, staging);
+        finish_q8(output);
+
+        // ---- RoPE tables for in-sequence positions 0..CAP-1 (gemma2_fast.c:116-129)
+        for (int b = 0; b < 2; ++b) {
+            const int d = b ? 512 : 256;
+            const float base = b ? 1000000.0f : 10000.0f;
+            std::vector<float> c(size_t(CAP) * d / 2), s(size_t(CAP) * d / 2);
+            for (unsigned t = 0; t < CAP; ++t)
+                for (int z = 0; z < d / 2; ++z) {
+                    const float theta = float(t) * powf(base, -2.0f * float(z) / float(d));
+                    c[size_t(t) * d / 2 + z] = cosf(theta);
+                    s[size_t(t) * d / 2 + z] = sinf(theta);
+                }
+            rope_cos[b] = dalloc<float>(c.size());
+            rope_sin[b] = dalloc<float>(s.size());
+            ck(cudaMemcpy(rope_cos[b], c.data(), c.size() * 4, cudaMemcpyHostToDevice), "rope upload");
+            ck(cudaMemcpy(rope_sin[b], s.data(), s.size() * 4, cudaMemcpyHostToDevice), "rope upload");
+        }
+
+        // ---- arena for CAP packed tokens
+        ids = dalloc<int>(CAP);
+        bounds = dalloc<unsigned>(2 * CAP);
+        pos = dalloc<unsigned>(CAP);
+        offsets = dalloc<unsigned>(CAP + 1);
+        x = dalloc<float>(size_t(CAP) * 512);
+        x_hi = dalloc<uint16_t>(size_t(CAP) * 512);
+        x_lo = dalloc<uint16_t>(size_t(CAP) * 512);
+        ple = dalloc<float>(size_t(CAP) * 24 * 512);
+        xq = dalloc<int8_t>(size_t(CAP) * 2048);
+        xs = dalloc<float>(size_t(64) * CAP);
+        qkv = dalloc<float>(size_t(CAP) * 3072);
+        qh = dalloc<uint16_t>(size_t(CAP) * 2048);
+        kh = dalloc<uint16_t>(size_t(CAP) * 512);
+        vh = dalloc<uint16_t>(size_t(CAP) * 512);
+        attn = dalloc<float>(size_t(CAP) * 2048);
+        h = dalloc<float>(size_t(CAP) * 512);
+        up = dalloc<float>(size_t(CAP) * 2048);
+        gate = dalloc<float>(size_t(CAP) * 2048);
+        y = dalloc<float>(size_t(CAP) * 768);
+        pooled = dalloc<float>(size_t(CAP) * 768);
+        const int ks[3] = {512, 1024, 2048};
+        for (int i = 0; i < 3; ++i)
+            if (!q8_tmap(&tm_xq[i], xq, uint64_t(ks[i]), CAP, 128)) throw std::runtime_error("tensor map (activations)");
+        if (!bf16_tmap(&tm_hi, x_hi, 512, CAP, 128) || !bf16_tmap(&tm_lo, x_lo, 512, CAP, 128) ||
+            !bf16_tmap(&tm_ple, ple_w, 512, 24 * 512, 256))
+            throw std::runtime_error("tensor map (PLE)");
+        ck(cudaMallocHost(&h_in, sizeof(uint32_t) * (5 * CAP + 1)), "cudaMallocHost");
+        ck(cudaMallocHost(&h_out, sizeof(float) * CAP * 768), "cudaMallocHost");
+        ck(cudaStreamSynchronize(stream), "weight upload");
+        clear_device_error();
+        if (std::getenv("EG2_B200_VERBOSE")) {
+            size_t free_b = 0, total_b = 0;
+            cudaMemGetInfo(&free_b, &total_b);
+            std::fprintf(stderr, "B200: device %d (%s), %zu allocations, %.1f MiB free, cap %u packed tokens\n", device,
+                         prop.name, allocations.size(), free_b / 1048576.0, CAP);
+        }
+    }
+
+    ~Backend() {
+        if (device >= 0) cudaSetDevice(device);
+        if (stream) cudaStreamSynchronize(stream);
+        for (auto &kv : graphs) cudaGraphExecDestroy(kv.second);
+        for (void *p : allocations) cudaFree(p);
+        if (h_in) cudaFreeHost(h_in);
+        if (h_out) cudaFreeHost(h_out);
+        if (done) cudaEventDestroy(done);
+        if (stream) cudaStreamDestroy(stream);
+    }
+
+    const CUtensorMap &xq_map(int k) const { return tm_xq[k == 512 ? 0 : k == 1024 ? 1 : 2]; }
+    void gemm(const Q8Weight &w, float *out, int ldo, int n, cudaStream_t s) {
+        ck(launch_q8gemm(xq_map(w.k), w.tmap, w.bn, xs, CAP, w.scales, out, ldo, n, w.rows, w.k, s), "q8 GEMM");
+    }
+
+    // The whole wave as a launch sequence (captured into a graph, or run eagerly
+    // under the profiler).  Returns the number of kernels launched.
+    int enqueue(unsigned n, unsigned batch, cudaStream_t s, Profiler *prof) {
+        int launches = 0;
+        auto mark = [&](const char *name) {
+            if (prof) prof->mark(name);
+        };
+        const int N = int(n);
+        mark("start");
+        ck(launch_embed(x, x_hi, x_lo, token_embd, ids, N, s), "embed"), ++launches;
+        mark("embed");
+        ck(launch_ple(tm_hi, tm_lo, tm_ple, ple, ple_norm, N, s), "PLE"), ++launches;
+        mark("ple_proj");
+        ck(launch_norm_quant(xq, xs, CAP, nullptr, x, layers[0].attn_norm, N, 512, s), "norm"), ++launches;
+        mark("norm_quant");
+        for (int l = 0; l < 24; ++l) {
+            const Layer &L = layers[l];
+            const int rb = L.d == 512 ? 1 : 0;
+            gemm(L.qkv, qkv, L.qkv.rows, N, s), ++launches;
+            mark("gemm_qkv");
+            ck(launch_qkv_post(qh, kh, vh, qkv, L.q_norm, L.k_norm, rope_cos[rb], rope_sin[rb], pos, N, L.d, s),
+               "qkv_post"),
+                ++launches;
+            mark("qkv_post");
+            ck(launch_attention(attn, qh, kh, vh, bounds, N, L.d, L.d == 512 ? 0 : 512, s), "attention"), ++launches;
+            mark(L.d == 512 ? "attention_global" : "attention_local");
+            ck(launch_norm_quant(xq, xs, CAP, nullptr, attn, nullptr, N, 4 * L.d, s), "quant"), ++launches;
+            mark("quant_attn");
+            gemm(L.o, h, 512, N, s), ++launches;
+            mark("gemm_o");
+            ck(launch_post_add(x, h, L.post_attn_norm, nullptr, xq, xs, CAP, L.ffn_norm, N, s), "post_add"), ++launches;
+            mark("post_add");
+            gemm(L.up, up, 2048, N, s), ++launches;
+            gemm(L.gate, gate, 2048, N, s), ++launches;
+            mark("gemm_up_gate");
+            ck(launch_gate_quant(xq, xs, CAP, gate, up, N, 2048, 2048, 0, s), "gelu"), ++launches;
+            mark("gelu_quant");
+            gemm(L.down, h, 512, N, s), ++launches;
+            mark("gemm_down");
+            ck(launch_post_add(x, h, L.post_ffw_norm, nullptr, xq, xs, CAP, nullptr, N, s), "post_add"), ++launches;
+            mark("post_add");
+            gemm(L.inp_gate, h, 512, N, s), ++launches;
+            mark("gemm_inp_gate");
+            ck(launch_gate_quant(xq, xs, CAP, h, ple, N, 512, 24 * 512, l * 512, s), "ple gate"), ++launches;
+            mark("ple_gate_quant");
+            gemm(L.proj, h, 512, N, s), ++launches;
+            mark("gemm_proj");
+            const float *next = l + 1 < 24 ? layers[l + 1].attn_norm : output_norm;
+            ck(launch_post_add(x, h, L.post_norm, L.out_scale, xq, xs, CAP, next, N, s), "post_add"), ++launches;
+            mark("post_add");
+        }
+        gemm(output, y, 768, N, s), ++launches;
+        mark("gemm_output");
+        ck(launch_pool_l2(pooled, y, offsets, int(batch), 768, s), "pool"), ++launches;
+        mark("pool_l2");
+        return launches;
+    }
+
+    cudaGraphExec_t graph_for(unsigned n, size_t batch) {
+        const uint64_t key = (uint64_t(n) << 32) | uint64_t(batch);
+        auto it = graphs.find(key);
+        if (it != graphs.end()) return it->second;
+        if (graphs.size() >= 256) {  // bound the cache
+            ck(cudaStreamSynchronize(stream), "graph cache flush");
+            for (auto &kv : graphs) cudaGraphExecDestroy(kv.second);
+            graphs.clear();
+        }
+        cudaGraph_t graph = nullptr;
+        ck(cudaStreamBeginCapture(stream, cudaStreamCaptureModeThreadLocal), "begin capture");
+        int launches = 0;
+        try {
+            launches = enqueue(n, unsigned(batch), stream, nullptr);
+        } catch (...) {
+            cudaStreamEndCapture(stream, &graph);
+            if (graph) cudaGraphDestroy(graph);
+            throw;
+        }
+        ck(cudaStreamEndCapture(stream, &graph), "end capture");
+        cudaGraphExec_t exec = nullptr;
+        const cudaError_t e = cudaGraphInstantiate(&exec, graph, 0);
+        cudaGraphDestroy(graph);
+        ck(e, "graph instantiate");
+        kernels_per_wave = launches;
+        graphs[key] = exec;
+        return exec;
+    }
+
+    // gemma2_kfd.cpp:271-296: validation, bounds and positions, then upload.
+    void stage(const int32_t *in_ids, const size_t *in_off, size_t batch) {
+        if (poisoned) throw std::runtime_error("KFD context failed; restart process before reuse");
+        validate_wave(in_ids, in_off, batch);
+        const unsigned n = unsigned(in_off[batch]);
+        uint32_t *hid = h_in, *hb = h_in + CAP, *hp = h_in + 3 * CAP, *ho = h_in + 4 * CAP;
+        std::memcpy(hid, in_ids, n * sizeof(int32_t));
+        for (size_t s = 0; s < batch; ++s) {
+            ho[s] = uint32_t(in_off[s]);
+            for (size_t t = in_off[s]; t < in_off[s + 1]; ++t) {
+                hb[2 * t] = uint32_t(in_off[s]), hb[2 * t + 1] = uint32_t(in_off[s + 1]);
+                hp[t] = uint32_t(t - in_off[s]);
+            }
+        }
+        ho[batch] = n;
+        ck(cudaSetDevice(device), "cudaSetDevice");
+        ck(cudaMemcpyAsync(ids, hid, n * 4, cudaMemcpyHostToDevice, stream), "ids upload");
+        ck(cudaMemcpyAsync(bounds, hb, n * 8, cudaMemcpyHostToDevice, stream), "bounds upload");
+        ck(cudaMemcpyAsync(pos, hp, n * 4, cudaMemcpyHostToDevice, stream), "positions upload");
+        ck(cudaMemcpyAsync(offsets, ho, (batch + 1) * 4, cudaMemcpyHostToDevice, stream), "offsets upload");
+        staged_graph = graph_for(n, batch);
+        staged_n = n, staged_batch = batch;
+    }
+
+    void launch(int repeats) {
+        if (poisoned) throw std::runtime_error("KFD context failed; restart process before reuse");
+        if (!staged_graph) throw std::runtime_error("no wave staged");
+        for (int r = 0; r < repeats; ++r) ck(cudaGraphLaunch(staged_graph, stream), "graph launch");
+    }
+
+    // Wait with the reference's deadline; any failure poisons the context.
+    void wait_done() {
+        poisoned = true;
+        ck(cudaEventRecord(done, stream), "event record");
+        const auto t0 = std::chrono::steady_clock::now();
+        for (unsigned spin = 0;; ++spin) {
+            const cudaError_t q = cudaEventQuery(done);
+            if (q == cudaSuccess) break;
+            if (q != cudaErrorNotReady) ck(q, "GPU wave");
+            if (std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count() > TIMEOUT_S)
+                throw std::runtime_error("GPU wave timed out");
+            if (spin > 64) std::this_thread::sleep_for(std::chrono::microseconds(20));
+        }
+        const int derr = read_device_error();
+        if (derr) throw std::runtime_error("device wait timed out inside a kernel (error " + std::to_string(derr) + ")");
+        poisoned = false;
+    }
+
+    void finish(float *out) {
+        if (poisoned) throw std::runtime_error("KFD context failed; restart process before reuse");
+        if (!staged_graph) throw std::runtime_error("no wave staged");
+        ck(cudaMemcpyAsync(h_out, pooled, staged_batch * 768 * 4, cudaMemcpyDeviceToHost, stream), "readback");
+        wait_done();
+        // gemma2_kfd.cpp:337-343: finite, non-zero; the embedding is already L2-normalised on the device.
+        for (size_t s = 0; s < staged_batch; ++s) {
+            double ss = 0;
+            for (int z = 0; z < 768; ++z) {
+                const float f = h_out[s * 768 + z];
+                if (!std::isfinite(f)) throw std::runtime_error("nonfinite GPU output");
+                ss += double(f) * f;
+            }
+            if (ss <= 0) throw std::runtime_error("zero GPU embedding");
+        }
+        std::memcpy(out, h_out, staged_batch * 768 * sizeof(float));
+    }
+
+    void batch(const int32_t *in_ids, const size_t *in_off, size_t n_seq, float *out) {
+        if (!out) throw std::runtime_error("KFD batch requires 1..2048 packed tokens and nonempty sequences");
+        stage(in_ids, in_off, n_seq);
+        launch(1);
+        finish(out);
+    }
+
+    int profile(char names[][32], double *ms, int max) {
+        if (!staged_graph) throw std::runtime_error("no wave staged");
+        std::map<std::string, double> acc;
+        std::vector<std::string> order;
+        {
+            Profiler prof{stream};
+            enqueue(staged_n, unsigned(staged_batch), stream, &prof);
+            wait_done();
+            for (size_t i = 1; i < prof.events.size(); ++i) {
+                float t = 0;
+                ck(cudaEventElapsedTime(&t, prof.events[i - 1], prof.events[i]), "elapsed");
+                if (!acc.count(prof.names[i])) order.push_back(prof.names[i]);
+                acc[prof.names[i]] += t;
+            }
+        }
+        int k = 0;
+        for (auto &nm : order) {
+            if (k >= max) break;
+            std::snprintf(names[k], 32, "%s", nm.c_str());
+            ms[k++] = acc[nm];
+        }
+        return k;
+    }
+};
+
+template <class F>
+bool guarded(char *err, size_t len, F &&f) {
+    try {
+        f();
+        return true;
+    } catch (const std::exception &e) {
+        if (err && len) std::snprintf(err, len, "KFD: %s", e.what());
+        return false;
+    }
+}
+Backend *as_backend(void *ctx) {
+    if (!ctx) throw std::runtime_error("empty context");
+    return static_cast<Backend *>(ctx);
+}
+}  // namespace
+
+extern "C" void *ei_gemma2_kfd_create_on(const ei_gguf *g, int device, char *err, size_t len) {
+    Backend *b = nullptr;
+    guarded(err, len, [&] { b = new Backend(g, device); });
+    return b;
+}
+extern "C" void *ei_gemma2_kfd_create(const ei_gguf *g, char *err, size_t len) {
+    const char *env = std::getenv("EG2_B200_DEVICE");
+    return ei_gemma2_kfd_create_on(g, env ? std::atoi(env) : 0, err, len);
+}
+extern "C" void ei_gemma2_kfd_free(void *ctx) { delete static_cast<Backend *>(ctx); }
+extern "C" bool ei_gemma2_kfd_batch(void *ctx, const int32_t *ids, const size_t *offsets, size_t batch, float *out,
+                                    char *err, size_t len) {
+    return guarded(err, len, [&] {
+        Backend *b = as_backend(ctx);
+        std::lock_guard<std::mutex> guard(b->mutex);
+        b->batch(ids, offsets, batch, out);
+    });
+}
+extern "C" bool eg2_b200_validate(const int32_t *ids, const size_t *offsets, size_t batch, char *err, size_t len) {
+    return guarded(err, len, [&] { validate_wave(ids, offsets, batch); });
+}
+extern "C" bool eg2_b200_stage(void *ctx, const int32_t *ids, const size_t *offsets, size_t batch, char *err,
+                               size_t len) {
+    return guarded(err, len, [&] {
+        Backend *b = as_backend(ctx);
+        std::lock_guard<std::mutex> guard(b->mutex);
+        b->stage(ids, offsets, batch);
+    });
+}
+extern "C" bool eg2_b200_launch(void *ctx, int repeats, char *err, size_t len) {
+    return guarded(err, len, [&] {
+        Backend *b = as_backend(ctx);
+        std::lock_guard<std::mutex> guard(b->mutex);
+        ck(cudaSetDevice(b->device), "cudaSetDevice");
+        b->launch(repeats);
+    });
+}
+extern "C" bool eg2_b200_finish(void *ctx, float *out, char *err, size_t len) {
+    return guarded(err, len, [&] {
+        Backend *b = as_backend(ctx);
+        std::lock_guard<std::mutex> guard(b->mutex);
+        if (!out) throw std::runtime_error("null output");
+        ck(cudaSetDevice(b->device), "cudaSetDevice");
+        b->finish(out);
+    });
+}
+extern "C" void *eg2_b200_stream(void *ctx) { return ctx ? static_cast<Backend *>(ctx)->stream : nullptr; }
+extern "C" int eg2_b200_kernels_per_wave(void *ctx) { return ctx ? static_cast<Backend *>(ctx)->kernels_per_wave : 0; }
+extern "C" int eg2_b200_device(void *ctx) { return ctx ? static_cast<Backend *>(ctx)->device : -1; }
+extern "C" int eg2_b200_profile(void *ctx, char names[][32], double *ms, int max) {
+    int k = -1;
+    guarded(nullptr, 0, [&] {
+        Backend *b = as_backend(ctx);
+        std::lock_guard<std::mutex> guard(b->mutex);
+        ck(cudaSetDevice(b->device), "cudaSetDevice");
+        k = b->profile(names, ms, max);
+    });
+    return k;
+}

@@ -1,0 +1,306 @@
+// All device code of the library, its launchers, and the exported operator
+// ABI (include/eg2_ops.h).  Built for sm_100a only.
+#include <mutex>
+
+#include "../../include/eg2_ops.h"
+#include "attention.cuh"
+#include "launch.h"
+#include "opsabi.cuh"
+#include "ple.cuh"
+#include "q8gemm.cuh"
+#include "rowops.cuh"
+
+namespace eg2 {
+
+// ---------------------------------------------------------------- tensor maps
+using EncodeTiled = CUresult (*)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
+                                 const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
+                                 CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+static EncodeTiled encode_fn() {
+    static EncodeTiled fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void *p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiled>(p);
+    });
+    return fn;
+}
+
+bool encode_tmap_2d(CUtensorMap *map, CUtensorMapDataType dtype, const void *base, uint64_t inner, uint64_t outer,
+                    uint64_t row_bytes, uint32_t box_inner, uint32_t box_outer) {
+    EncodeTiled fn = encode_fn();
+    if (!fn || (reinterpret_cast<uintptr_t>(base) & 15) || (row_bytes & 15)) return false;
+    const cuuint64_t dims[2] = {inner, outer}, strides[1] = {row_bytes};
+    const cuuint32_t box[2] = {box_inner, box_outer}, estr[2] = {1, 1};
+    return fn(map, dtype, 2, const_cast<void *>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+              CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+bool q8_tmap(CUtensorMap *map, const int8_t *base, uint64_t k, uint64_t rows, uint32_t box_rows) {
+    return encode_tmap_2d(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, base, k, rows, k, 128, box_rows);
+}
+bool bf16_tmap(CUtensorMap *map, const void *base, uint64_t k, uint64_t rows, uint32_t box_rows) {
+    return encode_tmap_2d(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, base, k, rows, k * 2, 64, box_rows);
+}
+
+// ---------------------------------------------------------------- launchers
+template <int BN>
+static cudaError_t q8gemm_go(const CUtensorMap &a, const CUtensorMap &b, const Q8GemmParams &p, cudaStream_t s) {
+    const size_t smem = q8gemm_smem_bytes(BN, p.K);
+    dim3 grid(p.N / BN, (p.M + 127) / 128);
+    q8gemm_kernel<BN><<<grid, Q8Cfg<BN>::THREADS, smem, s>>>(a, b, p);
+    return cudaGetLastError();
+}
+cudaError_t launch_q8gemm(const CUtensorMap &a, const CUtensorMap &b, int bn, const float *sa, int sa_stride,
+                          const float *sb, float *out, int ldo, int M, int N, int K, cudaStream_t s) {
+    if (M <= 0) return cudaSuccess;
+    if (K <= 0 || K % 128 || K > 2048 || N <= 0 || N % bn || (bn != 64 && bn != 128) || sa_stride < M || ldo < N)
+        return cudaErrorInvalidValue;
+    if (q8gemm_smem_bytes(bn, K) > 227 * 1024) return cudaErrorInvalidValue;
+    const Q8GemmParams p{sa, sa_stride, sb, out, ldo, M, N, K};
+    return bn == 128 ? q8gemm_go<128>(a, b, p, s) : q8gemm_go<64>(a, b, p, s);
+}
+
+cudaError_t launch_ple(const CUtensorMap &hi, const CUtensorMap &lo, const CUtensorMap &w, float *ple,
+                       const float *norm, int M, cudaStream_t s) {
+    if (M <= 0) return cudaSuccess;
+    const PleParams p{ple, norm, M};
+    ple_kernel<<<dim3(24, (M + 127) / 128), PleCfg::THREADS, PleCfg::SMEM, s>>>(hi, lo, w, p);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_embed(float *x, void *x_hi, void *x_lo, const void *emb, const int *ids, int n, cudaStream_t s) {
+    if (n <= 0) return cudaSuccess;
+    if ((x_hi == nullptr) != (x_lo == nullptr)) return cudaErrorInvalidValue;
+    embed_kernel<<<(n + 7) / 8, 256, 0, s>>>(x, static_cast<__nv_bfloat16 *>(x_hi), static_cast<__nv_bfloat16 *>(x_lo),
+                                             static_cast<const uint8_t *>(emb), ids, n);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_norm_quant(int8_t *q, float *qs, int qs_stride, float *y, const float *x, const float *w, int rows,
+                              int width, cudaStream_t s) {
+    if (rows <= 0) return cudaSuccess;
+    if (qs_stride < rows) return cudaErrorInvalidValue;
+    const dim3 grid((rows + 7) / 8), block(256);
+    switch (width) {
+        case 256: norm_quant_kernel<256><<<grid, block, 0, s>>>(q, qs, qs_stride, y, x, w, rows); break;
+        case 512: norm_quant_kernel<512><<<grid, block, 0, s>>>(q, qs, qs_stride, y, x, w, rows); break;
+        case 1024: norm_quant_kernel<1024><<<grid, block, 0, s>>>(q, qs, qs_stride, y, x, w, rows); break;
+        case 2048: norm_quant_kernel<2048><<<grid, block, 0, s>>>(q, qs, qs_stride, y, x, w, rows); break;
+        default: return cudaErrorInvalidValue;
+    }
+    return cudaGetLastError();
+}
+
+cudaError_t launch_qkv_post(void *q, void *k, void *v, const float *qkv, const float *qn, const float *kn,
+                            const float *rc, const float *rs, const unsigned *pos, int n, int d, cudaStream_t s) {
+    if (n <= 0) return cudaSuccess;
+    if (d != 256 && d != 512) return cudaErrorInvalidValue;
+    const int rows_per_tok = 4 + 2 * (512 / d), warps = n * rows_per_tok;
+    const dim3 grid((warps + 7) / 8), block(256);
+    auto *qh = static_cast<__half *>(q), *kh = static_cast<__half *>(k), *vh = static_cast<__half *>(v);
+    if (d == 256) qkv_post_kernel<256><<<grid, block, 0, s>>>(qh, kh, vh, qkv, qn, kn, rc, rs, pos, n);
+    else qkv_post_kernel<512><<<grid, block, 0, s>>>(qh, kh, vh, qkv, qn, kn, rc, rs, pos, n);
+    return cudaGetLastError();
+}
+
+template <int D>
+static cudaError_t attention_go(const AttnParams &p, cudaStream_t s) {
+    const dim3 grid((p.n + AttnCfg<D>::BQ - 1) / AttnCfg<D>::BQ, 4, D / AttnCfg<D>::DV);
+    attention_kernel<D><<<grid, AttnCfg<D>::THREADS, AttnCfg<D>::SMEM, s>>>(p);
+    return cudaGetLastError();
+}
+cudaError_t launch_attention(float *out, const void *q, const void *k, const void *v, const unsigned *bounds, int n,
+                             int d, int window, cudaStream_t s) {
+    if (n <= 0) return cudaSuccess;
+    const AttnParams p{out, static_cast<const __half *>(q), static_cast<const __half *>(k),
+                       static_cast<const __half *>(v), bounds, n, window};
+    if (d == 256) return attention_go<256>(p, s);
+    if (d == 512) return attention_go<512>(p, s);
+    return cudaErrorInvalidValue;
+}
+
+cudaError_t launch_post_add(float *x, const float *h, const float *w, const float *scale, int8_t *q, float *qs,
+                            int qs_stride, const float *next_w, int rows, cudaStream_t s) {
+    if (rows <= 0) return cudaSuccess;
+    if (qs_stride < rows) return cudaErrorInvalidValue;
+    post_add_kernel<<<(rows + 7) / 8, 256, 0, s>>>(x, h, w, scale, q, qs, qs_stride, next_w, rows);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_gate_quant(int8_t *q, float *qs, int qs_stride, const float *x, const float *other, int rows,
+                              int width, int other_stride, int other_offset, cudaStream_t s) {
+    if (rows <= 0) return cudaSuccess;
+    if (width <= 0 || width % 32 || qs_stride < rows || other_offset + width > other_stride) return cudaErrorInvalidValue;
+    const int groups = (width / 32 + 7) / 8, warps = rows * groups;
+    gate_quant_kernel<<<(warps + 7) / 8, 256, 0, s>>>(q, qs, qs_stride, x, other, rows, width, other_stride,
+                                                      other_offset);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_pool_l2(float *out, const float *y, const unsigned *offsets, int batch, int width, cudaStream_t s) {
+    if (batch <= 0) return cudaSuccess;
+    if (width <= 0 || width % 8 || width > 8192) return cudaErrorInvalidValue;
+    pool_l2_kernel<<<batch, 256, width * sizeof(float), s>>>(out, y, offsets, width);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_repack_q8(const void *blocks, int rows, int k, int8_t *codes, float *scales, int scale_stride,
+                             cudaStream_t s) {
+    const long long nblk = (long long)rows * (k / 32);
+    if (nblk <= 0) return cudaSuccess;
+    repack_q8_kernel<<<unsigned((nblk + 255) / 256), 256, 0, s>>>(static_cast<const uint8_t *>(blocks), rows, k, codes,
+                                                                  scales, scale_stride);
+    return cudaGetLastError();
+}
+
+cudaError_t init_kernel_attributes() {
+    cudaError_t e;
+    if ((e = cudaFuncSetAttribute(q8gemm_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024))) return e;
+    if ((e = cudaFuncSetAttribute(q8gemm_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024))) return e;
+    if ((e = cudaFuncSetAttribute(ple_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(PleCfg::SMEM)))) return e;
+    if ((e = cudaFuncSetAttribute(attention_kernel<256>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  int(AttnCfg<256>::SMEM))))
+        return e;
+    return cudaFuncSetAttribute(attention_kernel<512>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                int(AttnCfg<512>::SMEM));
+}
+
+int read_device_error() {
+    int v = 0;
+    if (cudaMemcpyFromSymbol(&v, g_error, sizeof(int)) != cudaSuccess) return -1;
+    return v;
+}
+void clear_device_error() {
+    const int z = 0;
+    cudaMemcpyToSymbol(g_error, &z, sizeof(int));
+}
+
+}  // namespace eg2
+
+// ---------------------------------------------------------------- operator ABI
+using namespace eg2;
+static inline cudaStream_t S(void *s) { return static_cast<cudaStream_t>(s); }
+static inline int rc(cudaError_t e) { return int(e); }
+// Operators used outside the executor opt into their shared memory on first use
+// on the current device.
+static cudaError_t ensure_attributes() {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e) return e;
+    static std::mutex mu;
+    static bool done[64] = {};
+    std::lock_guard<std::mutex> g(mu);
+    if (dev < 64 && done[dev]) return cudaSuccess;
+    e = init_kernel_attributes();
+    if (!e && dev < 64) done[dev] = true;
+    return e;
+}
+
+extern "C" {
+int eg2_launch_gather(const EgGather *p, void *s) {
+    if (!p->n) return 0;
+    abi_gather_kernel<<<(p->n * 512 + 255) / 256, 256, 0, S(s)>>>(*p);
+    return rc(cudaGetLastError());
+}
+int eg2_launch_mm(const EgMM *p, void *s) {
+    if (!(p->type == 0 || p->type == 1 || p->type == 8 || p->type == 30) || (p->type == 8 && p->k % 32))
+        return rc(cudaErrorInvalidValue);
+    if (!p->n || !p->m) return 0;
+    abi_mm_kernel<<<dim3((p->m + 15) / 16, (p->n + 15) / 16), 256, 0, S(s)>>>(*p);
+    return rc(cudaGetLastError());
+}
+int eg2_launch_norm(const EgNorm *p, void *s) {
+    if (!p->rows) return 0;
+    abi_norm_kernel<<<p->rows, 32, 0, S(s)>>>(*p);
+    return rc(cudaGetLastError());
+}
+int eg2_launch_rope(const EgRope *p, void *s) {
+    if (!p->n) return 0;
+    abi_rope_kernel<<<(p->n * p->heads * (p->d / 2) + 255) / 256, 256, 0, S(s)>>>(*p);
+    return rc(cudaGetLastError());
+}
+int eg2_launch_attention(const EgAttention *p, unsigned d, void *s) {
+    if (!p->n) return 0;
+    if (d == 256) abi_attention_kernel<256><<<p->n * 4, 32, 0, S(s)>>>(*p);
+    else if (d == 512) abi_attention_kernel<512><<<p->n * 4, 32, 0, S(s)>>>(*p);
+    else return rc(cudaErrorInvalidValue);
+    return rc(cudaGetLastError());
+}
+int eg2_launch_element(const EgElement *p, void *s) {
+    if (!p->n) return 0;
+    abi_element_kernel<<<(p->n + 255) / 256, 256, 0, S(s)>>>(*p);
+    return rc(cudaGetLastError());
+}
+int eg2_launch_pool(const EgPool *p, void *s) {
+    if (!p->batch) return 0;
+    abi_pool_kernel<<<(p->batch * 768 + 255) / 256, 256, 0, S(s)>>>(*p);
+    return rc(cudaGetLastError());
+}
+int eg2_launch_norm_residual(const EgNormResidual *p, void *s) {
+    if (!p->rows) return 0;
+    abi_norm_residual_kernel<<<p->rows, 32, 0, S(s)>>>(*p);
+    return rc(cudaGetLastError());
+}
+int eg2_launch_norm_rope(const EgNormRope *p, void *s) {
+    if (!p->rows) return 0;
+    abi_norm_rope_kernel<<<p->rows, 32, 0, S(s)>>>(*p);
+    return rc(cudaGetLastError());
+}
+
+int eg2_launch_embed(const EgEmbed *p, void *s) {
+    return rc(launch_embed(p->x, p->x_hi, p->x_lo, p->token_embd, p->ids, int(p->n), S(s)));
+}
+int eg2_launch_ple_proj(const EgPleProj *p, void *s) {
+    if (cudaError_t e = ensure_attributes()) return rc(e);
+    if (!p->n) return 0;
+    CUtensorMap hi, lo, w;
+    if (!bf16_tmap(&hi, p->x_hi, 512, p->n, 128) || !bf16_tmap(&lo, p->x_lo, 512, p->n, 128) ||
+        !bf16_tmap(&w, p->weight, 512, 24 * 512, 256))
+        return rc(cudaErrorInvalidValue);
+    return rc(launch_ple(hi, lo, w, p->ple, p->norm, int(p->n), S(s)));
+}
+int eg2_launch_norm_quant(const EgNormQuant *p, void *s) {
+    return rc(launch_norm_quant(p->q, p->scale, int(p->scale_stride), p->y, p->x, p->weight, int(p->rows),
+                                int(p->width), S(s)));
+}
+int eg2_launch_q8_mm(const EgQ8MM *p, void *s) {
+    if (cudaError_t e = ensure_attributes()) return rc(e);
+    if (!p->n) return 0;
+    if (p->k % 128 || p->m % 64 || !p->m) return rc(cudaErrorInvalidValue);
+    const int bn = (p->m % 128 == 0 && p->m >= 1024) ? 128 : 64;
+    CUtensorMap a, b;
+    if (!q8_tmap(&a, p->xq, p->k, p->n, 128) || !q8_tmap(&b, p->wq, p->k, p->m, uint32_t(bn)))
+        return rc(cudaErrorInvalidValue);
+    return rc(launch_q8gemm(a, b, bn, p->xs, int(p->xs_stride), p->ws, p->out, int(p->m), int(p->n), int(p->m),
+                            int(p->k), S(s)));
+}
+int eg2_launch_qkv_post(const EgQkvPost *p, void *s) {
+    return rc(launch_qkv_post(p->q, p->k, p->v, p->qkv, p->q_norm, p->k_norm, p->rope_cos, p->rope_sin, p->pos,
+                              int(p->n), int(p->d), S(s)));
+}
+int eg2_launch_attention_f16(const EgAttentionF16 *p, void *s) {
+    if (cudaError_t e = ensure_attributes()) return rc(e);
+    return rc(launch_attention(p->out, p->q, p->k, p->v, p->bounds, int(p->n), int(p->d), int(p->window), S(s)));
+}
+int eg2_launch_post_add(const EgPostAdd *p, void *s) {
+    return rc(launch_post_add(p->x, p->h, p->weight, p->scale, p->q, p->qscale, int(p->scale_stride), p->next_weight,
+                              int(p->rows), S(s)));
+}
+int eg2_launch_gate_quant(const EgGateQuant *p, void *s) {
+    return rc(launch_gate_quant(p->q, p->scale, int(p->scale_stride), p->x, p->other, int(p->rows), int(p->width),
+                                int(p->other_stride), int(p->other_offset), S(s)));
+}
+int eg2_launch_pool_l2(const EgPoolL2 *p, void *s) {
+    return rc(launch_pool_l2(p->out, p->y, p->offsets, int(p->batch), int(p->width), S(s)));
+}
+int eg2_repack_q8(const void *blocks_dev, unsigned rows, unsigned k, int8_t *codes, float *scales, void *s) {
+    if (k % 32) return rc(cudaErrorInvalidValue);
+    return rc(launch_repack_q8(blocks_dev, int(rows), int(k), codes, scales, int(rows), S(s)));
+}
+int eg2_read_error(void) { return read_device_error(); }
+void eg2_clear_error(void) { clear_device_error(); }
+}

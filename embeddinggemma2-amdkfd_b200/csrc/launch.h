@@ -1,0 +1,42 @@
+// Host-side launchers of the sm_100a kernels (internal to the library).
+#pragma once
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace eg2 {
+
+// cuTensorMapEncodeTiled through the runtime's driver entry point.
+bool encode_tmap_2d(CUtensorMap *map, CUtensorMapDataType dtype, const void *base, uint64_t inner, uint64_t outer,
+                    uint64_t row_bytes, uint32_t box_inner, uint32_t box_outer);
+// Q8 operand over a row-major int8 buffer [rows][k]: box 128 B x box_rows, 128-byte swizzle.
+bool q8_tmap(CUtensorMap *map, const int8_t *base, uint64_t k, uint64_t rows, uint32_t box_rows);
+// BF16 operand over [rows][k] bf16: box 64 elements x box_rows, 128-byte swizzle.
+bool bf16_tmap(CUtensorMap *map, const void *base, uint64_t k, uint64_t rows, uint32_t box_rows);
+
+// Kernel launches (all asynchronous on `s`).
+cudaError_t launch_q8gemm(const CUtensorMap &a, const CUtensorMap &b, int bn, const float *sa, int sa_stride,
+                          const float *sb, float *out, int ldo, int M, int N, int K, cudaStream_t s);
+cudaError_t launch_ple(const CUtensorMap &hi, const CUtensorMap &lo, const CUtensorMap &w, float *ple,
+                       const float *norm, int M, cudaStream_t s);
+cudaError_t launch_embed(float *x, void *x_hi, void *x_lo, const void *emb, const int *ids, int n, cudaStream_t s);
+cudaError_t launch_norm_quant(int8_t *q, float *qs, int qs_stride, float *y, const float *x, const float *w, int rows,
+                              int width, cudaStream_t s);
+cudaError_t launch_qkv_post(void *q, void *k, void *v, const float *qkv, const float *qn, const float *kn,
+                            const float *rc, const float *rs, const unsigned *pos, int n, int d, cudaStream_t s);
+cudaError_t launch_attention(float *out, const void *q, const void *k, const void *v, const unsigned *bounds, int n,
+                             int d, int window, cudaStream_t s);
+cudaError_t launch_post_add(float *x, const float *h, const float *w, const float *scale, int8_t *q, float *qs,
+                            int qs_stride, const float *next_w, int rows, cudaStream_t s);
+cudaError_t launch_gate_quant(int8_t *q, float *qs, int qs_stride, const float *x, const float *other, int rows,
+                              int width, int other_stride, int other_offset, cudaStream_t s);
+cudaError_t launch_pool_l2(float *out, const float *y, const unsigned *offsets, int batch, int width, cudaStream_t s);
+cudaError_t launch_repack_q8(const void *blocks, int rows, int k, int8_t *codes, float *scales, int scale_stride,
+                             cudaStream_t s);
+// Opt every kernel into its shared-memory size on the current device, before
+// any graph capture.
+cudaError_t init_kernel_attributes();
+int read_device_error();
+void clear_device_error();
+
+}  // namespace eg2

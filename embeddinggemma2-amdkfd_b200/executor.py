@@ -1,0 +1,188 @@
+"""Python mirror of the executor C ABI (include/eg2_executor.h).
+
+Same names, argument meaning and error behaviour as the reference's
+`ei_gemma2_kfd_create / _free / _batch` (src/gemma2_kfd.h:7-10): host arrays
+in, L2-normalised batch x 768 float32 embeddings out, failures raised as
+`ExecutorError("KFD: ...")` carrying the library's message.
+"""
+from __future__ import annotations
+
+import ctypes as C
+
+import numpy as np
+
+from . import _lib
+
+EMBED_DIM = 768
+MAX_TOKENS = 2048
+VOCAB = 262144
+
+
+class ExecutorError(RuntimeError):
+    pass
+
+
+def _err():
+    return C.create_string_buffer(512)
+
+
+def _wave(ids, offsets):
+    ids = np.ascontiguousarray(ids, dtype=np.int32)
+    offsets = np.ascontiguousarray(offsets, dtype=np.uint64)
+    return ids, offsets, len(offsets) - 1
+
+
+def validate(ids, offsets) -> None:
+    """The reference's host-side wave checks (gemma2_kfd.cpp:270-278), no GPU needed."""
+    ids, offsets, batch = _wave(ids, offsets)
+    err = _err()
+    if not _lib.load().eg2_b200_validate(ids.ctypes.data if ids.size else None,
+                                         offsets.ctypes.data if offsets.size else None, max(batch, 0), err,
+                                         len(err)):
+        raise ExecutorError(err.value.decode())
+
+
+class GGUFModel:
+    """A GGUF file mapped by the library's own loader into an `ei_gguf`."""
+
+    def __init__(self, path: str):
+        lib = _lib.load()
+        self._buf = C.create_string_buffer(lib.eg2_gguf_struct_size())
+        err = _err()
+        if not lib.eg2_gguf_open(self._buf, path.encode(), err, len(err)):
+            self._buf = None
+            raise ExecutorError(err.value.decode())
+        self.path = path
+
+    @property
+    def handle(self):
+        return C.cast(self._buf, C.c_void_p)
+
+    def close(self):
+        if getattr(self, "_buf", None) is not None:
+            _lib.load().eg2_gguf_close(self._buf)
+            self._buf = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+class Gemma2Executor:
+    """One packed-wave executor on one B200 (ei_gemma2_kfd_create_on)."""
+
+    def __init__(self, model: GGUFModel, device: int | None = None):
+        lib = _lib.load()
+        self.model = model  # borrowed by the context: keep it alive
+        err = _err()
+        if device is None:
+            ctx = lib.ei_gemma2_kfd_create(model.handle, err, len(err))
+        else:
+            ctx = lib.ei_gemma2_kfd_create_on(model.handle, int(device), err, len(err))
+        if not ctx:
+            raise ExecutorError(err.value.decode())
+        self.ctx = ctx
+        self.lib = lib
+        self._staged_batch = 0
+
+    def batch(self, ids, offsets) -> np.ndarray:
+        """Embed one packed wave: ids int32[n], offsets (batch+1) with offsets[0]=0."""
+        ids, offsets, batch = _wave(ids, offsets)
+        out = np.zeros((max(batch, 1), EMBED_DIM), np.float32)
+        err = _err()
+        ok = self.lib.ei_gemma2_kfd_batch(self.ctx, ids.ctypes.data if ids.size else None,
+                                          offsets.ctypes.data if offsets.size else None, max(batch, 0),
+                                          out.ctypes.data, err, len(err))
+        if not ok:
+            raise ExecutorError(err.value.decode())
+        return out[:batch]
+
+    # split form, for device-resident timing
+    def stage(self, ids, offsets):
+        ids, offsets, batch = _wave(ids, offsets)
+        err = _err()
+        if not self.lib.eg2_b200_stage(self.ctx, ids.ctypes.data, offsets.ctypes.data, batch, err, len(err)):
+            raise ExecutorError(err.value.decode())
+        self._staged_batch = batch
+
+    def launch(self, repeats: int = 1):
+        err = _err()
+        if not self.lib.eg2_b200_launch(self.ctx, int(repeats), err, len(err)):
+            raise ExecutorError(err.value.decode())
+
+    def finish(self) -> np.ndarray:
+        out = np.zeros((max(self._staged_batch, 1), EMBED_DIM), np.float32)
+        err = _err()
+        if not self.lib.eg2_b200_finish(self.ctx, out.ctypes.data, err, len(err)):
+            raise ExecutorError(err.value.decode())
+        return out[:self._staged_batch]
+
+    @property
+    def stream(self) -> int:
+        return int(self.lib.eg2_b200_stream(self.ctx) or 0)
+
+    @property
+    def kernels_per_wave(self) -> int:
+        return int(self.lib.eg2_b200_kernels_per_wave(self.ctx))
+
+    @property
+    def device(self) -> int:
+        return int(self.lib.eg2_b200_device(self.ctx))
+
+    def profile(self) -> dict:
+        """Milliseconds per kernel group of one eager run of the staged wave."""
+        names = (C.c_char * 32 * 64)()
+        ms = (C.c_double * 64)()
+        k = self.lib.eg2_b200_profile(self.ctx, names, ms, 64)
+        if k < 0:
+            raise ExecutorError("KFD: profile failed")
+        return {bytes(names[i]).split(b"\0", 1)[0].decode(): float(ms[i]) for i in range(k)}
+
+    def close(self):
+        if getattr(self, "ctx", None):
+            self.lib.ei_gemma2_kfd_free(self.ctx)
+            self.ctx = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+def _sum_squares_sse2(row: np.ndarray) -> np.float32:
+    """kernels.c:82-93 order: two 4-lane float accumulators over 8-element chunks."""
+    sq = (row * row).astype(np.float32)
+    n8 = sq.size // 8 * 8
+    lanes = sq[:n8].reshape(-1, 2, 4)
+    s0 = np.zeros(4, np.float32)
+    s1 = np.zeros(4, np.float32)
+    for c in range(lanes.shape[0]):
+        s0 = (s0 + lanes[c, 0]).astype(np.float32)
+        s1 = (s1 + lanes[c, 1]).astype(np.float32)
+    v = (s0 + s1).astype(np.float32)
+    ss = np.float32(np.float32(v[0] + v[2]) + np.float32(v[1] + v[3]))
+    for z in range(n8, sq.size):
+        ss = np.float32(ss + sq[z])
+    return ss
+
+
+def normalize_prefix(embedding: np.ndarray, dimensions: int) -> np.ndarray:
+    """Matryoshka truncation as the server applies it
+    (vendor/embeddinggemma.c/src/kernels.c:398-407, server.c:1133): keep the
+    first `dimensions` in {128, 256, 512, 768} and L2-renormalise when shorter,
+    in the reference's float order."""
+    if dimensions not in (128, 256, 512, 768):
+        raise ValueError("dimensions must be one of 128, 256, 512, 768")
+    e = np.array(embedding, dtype=np.float32, copy=True)
+    if dimensions == EMBED_DIM:
+        return e
+    e = np.ascontiguousarray(e[..., :dimensions])
+    flat = e.reshape(-1, dimensions)
+    for row in flat:
+        ss = _sum_squares_sse2(row)
+        if ss != 0:
+            row *= np.float32(np.float32(1.0) / np.sqrt(ss, dtype=np.float32))
+    return e

@@ -1,0 +1,70 @@
+/* EmbeddingGemma 2 packed-wave executor on NVIDIA B200 (sm_100a).
+ *
+ * Drop-in for the reference's executor C ABI, src/gemma2_kfd.h:7-10
+ * (implemented at src/gemma2_kfd.cpp:358-366), with the same argument meaning,
+ * ownership and error behaviour:
+ *   - `g` is borrowed and must outlive the context;
+ *   - ids / offsets / out are caller-owned HOST memory; `out` receives
+ *     batch x 768 floats, already L2-normalised;
+ *   - offsets[0] == 0, strictly increasing, 1..2048 packed tokens, token ids in
+ *     [0, 262144); violations fail with the reference's messages;
+ *   - synchronous: returns after the embeddings are on the host;
+ *   - errors return NULL / false with "KFD: <reason>" written into err, as the
+ *     reference does (the engine turns that into HTTP 400);
+ *   - after a device failure or timeout the context is poisoned and every later
+ *     call fails with "... restart process before reuse";
+ *   - one internal mutex serialises calls on a context.
+ */
+#ifndef EG2_EXECUTOR_H
+#define EG2_EXECUTOR_H
+#include "eg2_gguf.h"
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Replaces src/gemma2_kfd.h:7.  Uses CUDA device 0, or EG2_B200_DEVICE. */
+void *ei_gemma2_kfd_create(const ei_gguf *g, char *err, size_t len);
+/* Replaces src/gemma2_kfd.h:8. */
+void ei_gemma2_kfd_free(void *ctx);
+/* Replaces src/gemma2_kfd.h:9-10. */
+bool ei_gemma2_kfd_batch(void *ctx, const int32_t *ids, const size_t *offsets, size_t batch,
+                         float *out, char *err, size_t len);
+
+/* One executor per GPU: the counterpart of the CUDA backend's per-device
+ * create (vendor/embeddinggemma.c/src/gemma2_cuda.h:14), which the engine's
+ * one-executor-per-device routing (engine.c:1199-1220) needs. */
+void *ei_gemma2_kfd_create_on(const ei_gguf *g, int device, char *err, size_t len);
+
+/* The host-side checks of src/gemma2_kfd.cpp:270-278 alone (offsets, token
+ * count, id range), with the same messages; no device work.  true = valid. */
+bool eg2_b200_validate(const int32_t *ids, const size_t *offsets, size_t batch, char *err, size_t len);
+
+/* ---- split form of ei_gemma2_kfd_batch (same validation and kernels) ------
+ * stage: validate, build per-token bounds/positions, copy ids and tables to
+ *        the device and select (capturing on first use) the CUDA graph for
+ *        this wave shape;
+ * launch: replay that graph `repeats` times on the context stream (no sync);
+ * finish: wait (with the reference's 30 s deadline), copy the embeddings to
+ *        `out` and check them (finite, non-zero).
+ * Used by benchmarks to time the device work with inputs already resident.
+ * No counterpart in the reference (its batch call is monolithic). */
+bool eg2_b200_stage(void *ctx, const int32_t *ids, const size_t *offsets, size_t batch, char *err,
+                    size_t len);
+bool eg2_b200_launch(void *ctx, int repeats, char *err, size_t len);
+bool eg2_b200_finish(void *ctx, float *out, char *err, size_t len);
+/* The cudaStream_t the context launches on (for CUDA-event timing). */
+void *eg2_b200_stream(void *ctx);
+/* Kernels launched per wave by the staged graph. */
+int eg2_b200_kernels_per_wave(void *ctx);
+/* Time one eager replay of the staged wave per kernel group with CUDA events
+ * (the counterpart of EG2_KFD_PROFILE, gemma2_kfd.cpp:173-186,346-352).
+ * names/ms receive up to `max` entries; returns the number written, -1 on error. */
+int eg2_b200_profile(void *ctx, char names[][32], double *ms, int max);
+/* Device the context runs on. */
+int eg2_b200_device(void *ctx);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

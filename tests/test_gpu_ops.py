@@ -1,0 +1,368 @@
+"""Operator parity on the GPU, through the C ABI (include/eg2_ops.h).
+
+Part 1 ports the reference's operator test (tests/kernels.cpp:57-137): the
+kernels/abi.h operators against CPU sums with its tolerances.  Part 2 checks
+each fused executor operator against the CPU restatement of the reference
+graph (oracle/eg2_oracle.c) on identical inputs: Q8 codes, scales and every
+value the reference computes with exactly-rounded operations must match bit
+for bit; tensor-core accumulations are compared within stated tolerances.
+"""
+import numpy as np
+import pytest
+
+from conftest import cosine
+
+torch = pytest.importorskip("torch")
+pytestmark = pytest.mark.gpu
+
+DEV = "cuda:0"
+
+
+@pytest.fixture(scope="module")
+def ops(eg2):
+    import importlib
+    return importlib.import_module("embeddinggemma2-amdkfd_b200.ops")
+
+
+def T(a, dtype=None):
+    t = torch.from_numpy(np.array(a, copy=True))
+    return t.to(DEV) if dtype is None else t.to(DEV, dtype)
+
+
+def host(t):
+    torch.cuda.synchronize()
+    return t.cpu().numpy()
+
+
+def f16_to_f32(bits):
+    return np.asarray(bits, np.uint16).view(np.float16).astype(np.float32)
+
+
+# --------------------------------------------------------------------------- Part 1
+def test_abi_mm_types_and_sizes(ops):
+    """tests/kernels.cpp:57-80: 4 weight types x n in {1,17,33,65}, k=64, m=35, 2e-5."""
+    k, m = 64, 35
+    for type_ in (0, 1, 8, 30):
+        for n in (1, 17, 33, 65):
+            x = ((np.arange(n * k) % 19) - 9).astype(np.float32) * np.float32(0.03125)
+            w = ((np.arange(k * m) % 23) - 11).astype(np.float32) * np.float32(0.125)
+            if type_ == 0:
+                wb = w.view(np.uint8)
+            elif type_ == 1:
+                wb = w.astype(np.float16).view(np.uint8)
+            elif type_ == 30:
+                wb = (w.view(np.uint32) >> 16).astype(np.uint16).view(np.uint8)
+            else:
+                blk = np.zeros((k * m // 32, 34), np.uint8)
+                blk[:, 0], blk[:, 1] = 0, 0x30  # fp16 0.125
+                z = np.arange(k * m).reshape(-1, 32)
+                blk[:, 2:] = (((z % 23) - 11).astype(np.int8)).view(np.uint8)
+                wb = blk.ravel()
+            out = torch.zeros(n * m, device=DEV)
+            ops.mm(out, T(x), T(wb), n, k, m, type_)
+            ref = x.reshape(n, k).astype(np.float64) @ w.reshape(m, k).astype(np.float64).T
+            np.testing.assert_allclose(host(out).reshape(n, m), ref, atol=2e-5, rtol=0)
+
+
+def test_abi_norm(ops):
+    """tests/kernels.cpp:81-91."""
+    for d in (256, 512):
+        w = (0.5 + (np.arange(d) % 7) * 0.1).astype(np.float32)
+        x = np.sin(np.arange(3 * d, dtype=np.float32) * np.float32(0.13)).astype(np.float32)
+        out = torch.zeros(3 * d, device=DEV)
+        ops.norm(out, T(x), T(w), 3, d, 1.0)
+        xr = x.reshape(3, d).astype(np.float64)
+        ref = xr * w / np.sqrt((xr * xr).sum(1, keepdims=True) / d + 1e-6)
+        np.testing.assert_allclose(host(out).reshape(3, d), ref, atol=2e-5, rtol=0)
+
+
+def test_abi_fused_vs_unfused(ops):
+    """tests/kernels.cpp:92-113: norm_residual == norm + element, norm_rope == norm + rope (2e-6)."""
+    for d in (256, 512):
+        w = (0.5 + (np.arange(d) % 7) * 0.1).astype(np.float32)
+        i = np.arange(6 * d, dtype=np.float32)
+        x = np.sin(i * np.float32(0.13)).astype(np.float32)
+        res = np.cos(i * np.float32(0.17)).astype(np.float32)
+        y, r1, r2 = torch.zeros(6 * d, device=DEV), T(res), T(res)
+        ops.norm(y, T(x), T(w), 6, d, 1.0)
+        ops.element(r1, r1, y, 6 * d, 0, 0, 0.7)
+        ops.norm_residual(r2, T(x), T(w), 6, d, 0.7)
+        np.testing.assert_allclose(host(r2), host(r1), atol=2e-6, rtol=0)
+        table = np.zeros((3, d), np.float32)
+        tz = np.outer(np.arange(3), np.arange(d // 2)).astype(np.float32) * np.float32(0.01)
+        table[:, :d // 2], table[:, d // 2:] = np.cos(tz), np.sin(tz)
+        y = torch.zeros(6 * d, device=DEV)
+        xt = T(x)
+        ops.norm(y, xt, T(w), 6, d, 1.0)
+        ops.rope(y, T(table), 3, 2, d)
+        ops.norm_rope(xt, T(w), T(table), 6, d, 2)
+        np.testing.assert_allclose(host(xt), host(y), atol=2e-6, rtol=0)
+
+
+def test_abi_attention(ops):
+    """tests/kernels.cpp:114-137: GQA, two packed sequences, window 0/1 vs a double softmax."""
+    bounds = np.array([[0, 3] if t < 3 else [3, 8] for t in range(8)], np.uint32).ravel()
+    q = (np.sin(np.arange(8 * 2048, dtype=np.float32) * np.float32(0.07)) * np.float32(0.1)).astype(np.float32)
+    k = (np.cos(np.arange(8 * 512, dtype=np.float32) * np.float32(0.11)) * np.float32(0.1)).astype(np.float32)
+    v = np.sin(np.arange(8 * 512, dtype=np.float32) * np.float32(0.03)).astype(np.float32)
+    for d in (256, 512):
+        for window in (0, 1):
+            out = torch.zeros(8 * 4 * d, device=DEV)
+            ops.attention(out, T(q), T(k), T(v), T(bounds), 8, window, d)
+            got = host(out)
+            for t in range(8):
+                for h in range(4):
+                    lo, hi, kh = int(bounds[2 * t]), int(bounds[2 * t + 1]), h // (4 // (512 // d))
+                    if window:
+                        if t > window:
+                            lo = max(lo, t - window)
+                        hi = min(hi, t + window + 1)
+                    qv = q[(t * 4 + h) * d:(t * 4 + h + 1) * d].astype(np.float64)
+                    ks = np.stack([k[s * 512 + kh * d:s * 512 + kh * d + d] for s in range(lo, hi)]).astype(np.float64)
+                    vs = np.stack([v[s * 512 + kh * d:s * 512 + kh * d + d] for s in range(lo, hi)]).astype(np.float64)
+                    e = np.exp(ks @ qv)
+                    ref = (e / e.sum()) @ vs
+                    np.testing.assert_allclose(got[(t * 4 + h) * d:(t * 4 + h + 1) * d], ref, atol=2e-5, rtol=0)
+
+
+# --------------------------------------------------------------------------- Part 2
+def _rand_rows(rng, rows, width, scale=3.0):
+    x = (rng.standard_normal((rows, width)) * rng.uniform(0.05, scale, (rows, 1))).astype(np.float32)
+    x[0, :32] = 0.0  # an all-zero block
+    x[1, :32] = np.float32(0.5) * np.arange(32, dtype=np.float32)  # exact halves
+    return x
+
+
+def _check_q8(q_gpu, s_gpu, rows, width, stride, q_ref, d_ref):
+    q_gpu = q_gpu.reshape(-1)[:rows * width].reshape(rows, width)
+    np.testing.assert_array_equal(q_gpu, q_ref.reshape(rows, width))
+    s = s_gpu.reshape(-1, stride)[: width // 32, :rows].T  # [rows][blocks]
+    np.testing.assert_array_equal(s, f16_to_f32(d_ref).reshape(rows, width // 32))
+
+
+@pytest.mark.parametrize("width,weighted", [(512, True), (512, False), (1024, False), (2048, False)])
+def test_norm_quant_bit_exact(ops, port, width, weighted):
+    rng = np.random.default_rng(width + weighted)
+    rows, stride = 77, 96
+    x = _rand_rows(rng, rows, width)
+    w = (1.0 + 0.1 * rng.standard_normal(width)).astype(np.float32) if weighted else None
+    ref = port.rms_rows(x, w) if weighted else x
+    q_ref, d_ref = port.quantize(ref, port.ROUND_X86)
+    q = torch.zeros(rows * width, dtype=torch.int8, device=DEV)
+    s = torch.zeros(width // 32 * stride, device=DEV)
+    ops.norm_quant(q, s, stride, T(x), T(w) if weighted else None, rows, width)
+    _check_q8(host(q), host(s), rows, width, stride, q_ref, d_ref)
+
+
+def _q8_operands(rng, rows, k, pow2=False):
+    q = rng.integers(-127, 128, size=(rows, k), dtype=np.int8)
+    if pow2:
+        d = np.float16(2.0) ** rng.integers(0, 3, size=(rows, k // 32)).astype(np.float16)
+    else:
+        d = (np.abs(rng.standard_normal((rows, k // 32))) * 0.01 + 1e-4).astype(np.float16)
+    return q, d.view(np.uint16)
+
+
+def _gpu_q8_mm(ops, xq, xd, wq, wd, stride):
+    n, k = xq.shape
+    m = wq.shape[0]
+    xs = np.zeros((k // 32, stride), np.float32)
+    xs[:, :n] = f16_to_f32(xd).T
+    ws = np.ascontiguousarray(f16_to_f32(wd).T)  # [k/32][m]
+    out = torch.zeros(n * m, device=DEV)
+    ops.q8_mm(out, T(xq), T(xs), stride, T(wq), T(ws), n, k, m)
+    return host(out).reshape(n, m)
+
+
+@pytest.mark.parametrize("n,k,m", [(130, 512, 2048), (2048, 512, 3072), (200, 1024, 512), (2048, 2048, 512),
+                                   (77, 512, 768), (1, 512, 512), (257, 512, 4096)])
+def test_q8_mm_matches_reference_gemm(ops, port, n, k, m):
+    rng = np.random.default_rng(n * 7 + k + m)
+    xq, xd = _q8_operands(rng, n, k)
+    wq, wd = _q8_operands(rng, m, k)
+    got = _gpu_q8_mm(ops, xq, xd, wq, wd, ((n + 127) // 128) * 128)
+    ref = port.gemm_q8(wq, wd, xq, xd)
+    err = np.abs(got - ref).max() / np.abs(ref).max()
+    assert err < 2e-6, err
+
+
+@pytest.mark.parametrize("n,k,m", [(150, 512, 2048), (64, 2048, 512), (300, 1024, 512)])
+def test_q8_mm_int32_block_accumulators_exact(ops, port, n, k, m):
+    """With power-of-two block scales every term and partial sum is an exact
+    integer in fp32, so the output equals sum_b D_b * 2^e exactly: any error
+    in an int32 block accumulator would show."""
+    rng = np.random.default_rng(n + k + m)
+    xq, xd = _q8_operands(rng, n, k, pow2=True)
+    wq, wd = _q8_operands(rng, m, k, pow2=True)
+    got = _gpu_q8_mm(ops, xq, xd, wq, wd, 512)
+    D = port.gemm_q8_blockdots(wq, xq).astype(np.int64)  # [n][m][kb]
+    sc = (f16_to_f32(xd)[:, None, :] * f16_to_f32(wd)[None, :, :]).astype(np.int64)
+    exact = (D * sc).sum(-1)
+    assert np.abs(exact).max() < 2 ** 24
+    np.testing.assert_array_equal(got.astype(np.int64), exact)
+
+
+@pytest.mark.parametrize("width,stride,offset", [(2048, 2048, 0), (512, 12288, 7 * 512)])
+def test_gate_quant_bit_exact(ops, port, width, stride, offset):
+    rng = np.random.default_rng(width)
+    rows = 65
+    x = (rng.standard_normal((rows, width)) * 3).astype(np.float32)
+    other = rng.standard_normal((rows, stride)).astype(np.float32)
+    g = port.gelu_mul(x, other[:, offset:offset + width], mode=1).reshape(rows, width)
+    q_ref, d_ref = port.quantize(g, port.ROUND_X86)
+    qstride = 128
+    q = torch.zeros(rows * width, dtype=torch.int8, device=DEV)
+    s = torch.zeros(width // 32 * qstride, device=DEV)
+    ops.gate_quant(q, s, qstride, T(x), T(other), rows, width, stride, offset)
+    _check_q8(host(q), host(s), rows, width, qstride, q_ref, d_ref)
+
+
+@pytest.mark.parametrize("next_norm,scaled", [(True, False), (False, False), (True, True)])
+def test_post_add_bit_exact(ops, port, next_norm, scaled):
+    rng = np.random.default_rng(3 + next_norm + 2 * scaled)
+    rows, stride = 90, 128
+    x = (rng.standard_normal((rows, 512)) * 2).astype(np.float32)
+    h = (rng.standard_normal((rows, 512)) * 5).astype(np.float32)
+    w = rng.normal(0, 0.1, 512).astype(np.float32)
+    nw = (1 + 0.1 * rng.standard_normal(512)).astype(np.float32)
+    sc = np.array([0.73], np.float32)
+    hn = port.rms_rows(h, w)
+    x_ref = ((x + hn) * (sc[0] if scaled else np.float32(1.0))).astype(np.float32)
+    nxt = port.rms_rows(x_ref, nw) if next_norm else x_ref
+    q_ref, d_ref = port.quantize(nxt, port.ROUND_X86)
+    xt = T(x)
+    q = torch.zeros(rows * 512, dtype=torch.int8, device=DEV)
+    s = torch.zeros(16 * stride, device=DEV)
+    ops.post_add(xt, T(h), T(w), T(sc) if scaled else None, q, s, stride, T(nw) if next_norm else None, rows)
+    np.testing.assert_array_equal(host(xt), x_ref)
+    _check_q8(host(q), host(s), rows, 512, stride, q_ref, d_ref)
+
+
+@pytest.mark.parametrize("d", [256, 512])
+def test_qkv_post_bit_exact(ops, port, d):
+    rng = np.random.default_rng(d)
+    n, kv = 70, 512 // d
+    qkv = (rng.standard_normal((n, 4 * d + 1024)) * 4).astype(np.float32)
+    qn = (1 + 0.1 * rng.standard_normal(d)).astype(np.float32)
+    kn = (1 + 0.1 * rng.standard_normal(d)).astype(np.float32)
+    pos = rng.integers(0, 2048, n).astype(np.uint32)
+    c, s = port.rope_tables(d)
+    c, s = np.ascontiguousarray(c[:2048]), np.ascontiguousarray(s[:2048])
+
+    def rope(r, p):
+        a, b = r[:, : d // 2], r[:, d // 2:]
+        cc, ss = c[p], s[p]
+        return np.concatenate([a * cc - b * ss, a * ss + b * cc], 1).astype(np.float32)
+
+    q_ref = np.stack([rope(port.rms_rows(qkv[:, h * d:(h + 1) * d], qn), pos) for h in range(4)], 1)
+    k_ref = np.stack([rope(port.rms_rows(qkv[:, 4 * d + h * d:4 * d + (h + 1) * d], kn), pos) for h in range(kv)], 1)
+    v_ref = np.stack([port.rms_rows(qkv[:, 4 * d + 512 + h * d:4 * d + 512 + (h + 1) * d], None) for h in range(kv)], 1)
+    qo = torch.zeros(n * 4 * d, dtype=torch.float16, device=DEV)
+    ko = torch.zeros(n * kv * d, dtype=torch.float16, device=DEV)
+    vo = torch.zeros(n * kv * d, dtype=torch.float16, device=DEV)
+    ops.qkv_post(qo, ko, vo, T(qkv), T(qn), T(kn), T(c), T(s), T(pos), n, d)
+    np.testing.assert_array_equal(host(qo).reshape(q_ref.shape), q_ref.astype(np.float16))
+    np.testing.assert_array_equal(host(ko).reshape(k_ref.shape), k_ref.astype(np.float16))
+    np.testing.assert_array_equal(host(vo).reshape(v_ref.shape), v_ref.astype(np.float16))
+
+
+def _bounds(lengths):
+    off = np.concatenate([[0], np.cumsum(lengths)]).astype(np.int64)
+    lo = np.concatenate([[off[i]] * lengths[i] for i in range(len(lengths))]).astype(np.uint32)
+    hi = np.concatenate([[off[i + 1]] * lengths[i] for i in range(len(lengths))]).astype(np.uint32)
+    return lo, hi
+
+
+@pytest.mark.parametrize("d,window,lengths", [(256, 512, [10, 19, 35, 66]), (512, 0, [10, 19, 35, 66]),
+                                              (256, 512, [1300, 3, 128]), (512, 0, [700, 129])])
+def test_attention_f16_vs_reference_attention(ops, port, d, window, lengths):
+    rng = np.random.default_rng(d + sum(lengths))
+    n, kv = sum(lengths), 512 // d
+    q = rng.standard_normal((n, 4, d)).astype(np.float16)
+    k = (rng.standard_normal((n, kv, d)) * 0.1).astype(np.float16)
+    v = rng.standard_normal((n, kv, d)).astype(np.float16)
+    lo, hi = _bounds(lengths)
+    ref = port.attention(q.astype(np.float32), k.astype(np.float32), v.astype(np.float32), lo, hi, kv, d, window)
+    bounds = np.stack([lo, hi], 1).ravel()
+    out = torch.zeros(n * 4 * d, device=DEV)
+    ops.attention_f16(out, T(q), T(k), T(v), T(bounds), n, d, window)
+    got = host(out).reshape(n, 4 * d)
+    np.testing.assert_allclose(got, ref, atol=3e-3, rtol=0)
+    assert cosine(got.ravel(), ref.ravel()) > 0.99999
+
+
+def test_embed_bit_exact(ops, model_baseline):
+    import oracle
+    g = oracle.Gguf(model_baseline)
+    raw = np.asarray(g.raw("token_embd.weight"))
+    rng = np.random.default_rng(1)
+    ids = rng.integers(0, 262144, 300).astype(np.int32)
+    blk = raw.reshape(262144, 16, 34)[ids]
+    d = f16_to_f32(np.ascontiguousarray(blk[:, :, :2]).view(np.uint16)[..., 0])
+    qv = np.ascontiguousarray(blk[:, :, 2:]).view(np.int8).astype(np.float32)
+    ref = ((d[:, :, None] * qv) * np.float32(np.sqrt(np.float32(512)))).astype(np.float32).reshape(300, 512)
+    x = torch.zeros(300 * 512, device=DEV)
+    hi = torch.zeros(300 * 512, dtype=torch.bfloat16, device=DEV)
+    lo = torch.zeros(300 * 512, dtype=torch.bfloat16, device=DEV)
+    ops.embed(x, hi, lo, T(raw), T(ids), 300)
+    np.testing.assert_array_equal(host(x).reshape(300, 512), ref)
+    xr = torch.from_numpy(ref).to(DEV).ravel()
+    assert torch.equal(hi, xr.to(torch.bfloat16))
+    assert torch.equal(lo, (xr - xr.to(torch.bfloat16).float()).to(torch.bfloat16))
+
+
+def test_ple_proj_vs_reference(ops, port, model_baseline):
+    import oracle
+    g = oracle.Gguf(model_baseline)
+    rng = np.random.default_rng(2)
+    n = 150
+    x = rng.standard_normal((n, 512)).astype(np.float32)
+    w_bits = np.asarray(g.raw("per_layer_model_proj.weight")).view(np.uint16).reshape(12288, 512)
+    nw = np.array(g.f32("per_layer_proj_norm.weight"))
+    ref = port.gemm_bf16(w_bits, x) / np.float32(np.sqrt(np.float32(512)))
+    ref = port.rms_rows(ref.astype(np.float32).reshape(n * 24, 512), nw).reshape(n, 12288)
+    xt = torch.from_numpy(x).to(DEV)
+    hi = xt.to(torch.bfloat16)
+    lo = (xt - hi.float()).to(torch.bfloat16)
+    ple = torch.zeros(n * 12288, device=DEV)
+    ops.ple_proj(ple, hi, lo, T(w_bits), T(nw), n)
+    got = host(ple).reshape(n, 12288)
+    np.testing.assert_allclose(got, ref, atol=5e-4, rtol=2e-4)
+
+
+def _pool_l2_ref(y, off):
+    from importlib import import_module
+    sumsq = import_module("embeddinggemma2-amdkfd_b200.executor")._sum_squares_sse2
+    out = []
+    for s in range(len(off) - 1):
+        lo, hi = int(off[s]), int(off[s + 1])
+        o = np.zeros(y.shape[1], np.float32)
+        ln = np.float32(hi - lo)
+        for t in range(lo, hi):
+            o = (o + (y[t] / ln).astype(np.float32)).astype(np.float32)
+        ss = sumsq(o)
+        out.append((o * np.float32(np.float32(1) / np.sqrt(ss, dtype=np.float32))).astype(np.float32))
+    return np.stack(out)
+
+
+def test_pool_l2_bit_exact(ops):
+    rng = np.random.default_rng(4)
+    lengths = [10, 19, 35, 66, 1]
+    off = np.concatenate([[0], np.cumsum(lengths)]).astype(np.uint32)
+    y = rng.standard_normal((off[-1], 768)).astype(np.float32)
+    out = torch.zeros(len(lengths) * 768, device=DEV)
+    ops.pool_l2(out, T(y), T(off), len(lengths), 768)
+    np.testing.assert_array_equal(host(out).reshape(len(lengths), 768), _pool_l2_ref(y, off))
+
+
+def test_repack_q8(ops, model_baseline):
+    import oracle
+    g = oracle.Gguf(model_baseline)
+    raw = np.asarray(g.raw("blk.3.ffn_down.weight"))
+    q_ref, d_ref = g.q8("blk.3.ffn_down.weight")
+    codes = torch.zeros(512 * 2048, dtype=torch.int8, device=DEV)
+    scales = torch.zeros(64 * 512, device=DEV)
+    ops.repack_q8(T(raw), 512, 2048, codes, scales)
+    np.testing.assert_array_equal(host(codes).reshape(512, 2048), q_ref)
+    np.testing.assert_array_equal(host(scales).reshape(64, 512).T, f16_to_f32(d_ref))
+    assert ops.read_error() == 0
