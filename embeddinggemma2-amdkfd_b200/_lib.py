@@ -130,7 +130,7 @@ class EgNormQuant(C.Structure):
 
 class EgQ8MM(C.Structure):
     _fields_ = [("out", P), ("xq", P), ("xs", P), ("xs_stride", u32), ("wq", P), ("ws", P),
-                ("n", u32), ("k", u32), ("m", u32)]
+                ("n", u32), ("k", u32), ("m", u32), ("exact", u32)]
 
 
 class EgQkvPost(C.Structure):

@@ -7,9 +7,14 @@
 // Flash-style: a CTA owns 64 query tokens of one head and one 256-wide slice of
 // the value dimension (d = 512 uses two slices, each recomputing Q.K^T); four
 // warps own 16 queries each.  Q.K^T and P.V run on fp16 tensor-core MMAs with
-// fp32 accumulation and an online softmax; key blocks of 64 cover only the
-// union of the tile's key ranges.  Shared-memory rows are XOR-swizzled in
-// 16-byte chunks so ldmatrix is conflict-free.
+// fp32 accumulation and an online softmax.  The CTA visits the sequences
+// present in its query tile one after another, and each sequence's key blocks
+// of 64 start at multiples of 64 from the sequence's first token: a row's keys
+// are therefore grouped and summed the same way wherever its sequence sits in
+// the packed wave (blocks of other sequences are fully masked for it and leave
+// its state bit-for-bit unchanged), so packed and solo results are identical.
+// Shared-memory rows are XOR-swizzled in 16-byte chunks so ldmatrix is
+// conflict-free.
 #pragma once
 #include "common.cuh"
 
@@ -72,7 +77,6 @@ __global__ void __launch_bounds__(AttnCfg<D>::THREADS) attention_kernel(const At
     extern __shared__ __align__(128) uint8_t smem[];
     uint8_t *qs = smem, *ks = smem + C::Q_BYTES, *vs = ks + C::K_BYTES;
     int *qlo = reinterpret_cast<int *>(vs + C::V_BYTES), *qhi = qlo + C::BQ;
-    __shared__ int range[2];
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int t0 = blockIdx.x * C::BQ, head = blockIdx.y, dv0 = blockIdx.z * C::DV;
@@ -91,19 +95,13 @@ __global__ void __launch_bounds__(AttnCfg<D>::THREADS) attention_kernel(const At
         }
         qlo[threadIdx.x] = lo, qhi[threadIdx.x] = hi;
     }
-    if (threadIdx.x == 0) range[0] = 1 << 30, range[1] = 0;
-    __syncthreads();
-    if (threadIdx.x < C::BQ && t0 + int(threadIdx.x) < p.n) {
-        atomicMin(&range[0], qlo[threadIdx.x]);
-        atomicMax(&range[1], qhi[threadIdx.x]);
-    }
     // Q tile (64 x D) -> shared.
     for (int i = threadIdx.x; i < C::BQ * C::QCH; i += C::THREADS) {
         const int r = i / C::QCH, ch = i % C::QCH, t = t0 + r;
         cp_async16(qs + swz(r, ch * 8, C::QCH), p.q + (size_t(t < p.n ? t : 0) * 4 + head) * D + ch * 8, t < p.n);
     }
     __syncthreads();
-    const int klo = range[0] & ~7, khi = range[1];
+    const int tlast = min(t0 + C::BQ, p.n);
 
     // Each thread: query rows g and g+8 of its warp's 16.
     const int g = lane >> 2, tq = lane & 3;
@@ -115,7 +113,16 @@ __global__ void __launch_bounds__(AttnCfg<D>::THREADS) attention_kernel(const At
     float m0 = -1e30f, m1 = -1e30f, l0 = 0.0f, l1 = 0.0f;
     const uint32_t qbase = smem_u32(qs), kbase = smem_u32(ks), vbase = smem_u32(vs);
 
-    for (int kb = klo; kb < khi; kb += C::BKEY) {
+    for (int seq_lo = int(p.bounds[2 * t0]); seq_lo < tlast;) {
+      const int seq_hi = int(p.bounds[2 * seq_lo + 1]);
+      if (seq_hi <= seq_lo) break;  // malformed bounds: never loop without progress
+      int kmin = seq_lo, kmax = seq_hi;
+      if (p.window) {
+          const int r_first = max(seq_lo, t0), r_last = min(seq_hi, tlast);
+          kmin = max(seq_lo, r_first - p.window);
+          kmax = min(seq_hi, r_last + p.window);
+      }
+      for (int kb = seq_lo + (kmin - seq_lo) / C::BKEY * C::BKEY; kb < kmax; kb += C::BKEY) {
         __syncthreads();  // previous tiles fully consumed
         for (int i = threadIdx.x; i < C::BKEY * C::QCH; i += C::THREADS) {
             const int r = i / C::QCH, ch = i % C::QCH, s = kb + r;
@@ -194,6 +201,8 @@ __global__ void __launch_bounds__(AttnCfg<D>::THREADS) attention_kernel(const At
                 mma16816(o[db + 1], pa[k2][0], pa[k2][1], pa[k2][2], pa[k2][3], b2, b3);
             }
         }
+      }
+      seq_lo = seq_hi;
     }
     l0 += __shfl_xor_sync(0xffffffffu, l0, 1);
     l0 += __shfl_xor_sync(0xffffffffu, l0, 2);

@@ -59,7 +59,7 @@ struct Q8Weight {
     int8_t *codes = nullptr;  // [rows][k]
     float *scales = nullptr;  // [k/32][rows]
     int rows = 0, k = 0;
-    CUtensorMap tmap{};
+    CUtensorMap tmap{}, tscale{};
     int bn = 64;
 };
 
@@ -108,7 +108,8 @@ struct Backend {
           *gate = nullptr, *y = nullptr, *pooled = nullptr, *xs = nullptr;
     void *x_hi = nullptr, *x_lo = nullptr, *qh = nullptr, *kh = nullptr, *vh = nullptr;
     int8_t *xq = nullptr;
-    CUtensorMap tm_xq[3]{}, tm_hi{}, tm_lo{}, tm_ple{};
+    CUtensorMap tm_xq[3]{}, tm_xs[3]{}, tm_hi{}, tm_lo{}, tm_ple{};
+    bool gemm_exact = false;  // EG2_B200_GEMM=exact: the reference scalar tile's rounding order
 
     // host staging (pinned)
     uint32_t *h_in = nullptr;  // ids | bounds(2) | pos | offsets
@@ -174,7 +175,8 @@ struct Backend {
         w.bn = (rows % 128 == 0 && rows >= 1024) ? 128 : 64;
     }
     void finish_q8(Q8Weight &w) {
-        if (!q8_tmap(&w.tmap, w.codes, uint64_t(w.k), uint64_t(w.rows), uint32_t(w.bn)))
+        if (!q8_tmap(&w.tmap, w.codes, uint64_t(w.k), uint64_t(w.rows), uint32_t(w.bn)) ||
+            !scale_tmap(&w.tscale, w.scales, uint64_t(w.rows), uint64_t(w.k / 32), uint32_t(w.bn)))
             throw std::runtime_error("cuTensorMapEncodeTiled failed for a weight");
     }
 
@@ -293,7 +295,10 @@ struct Backend {
         pooled = dalloc<float>(size_t(CAP) * 768);
         const int ks[3] = {512, 1024, 2048};
         for (int i = 0; i < 3; ++i)
-            if (!q8_tmap(&tm_xq[i], xq, uint64_t(ks[i]), CAP, 128)) throw std::runtime_error("tensor map (activations)");
+            if (!q8_tmap(&tm_xq[i], xq, uint64_t(ks[i]), CAP, 128) ||
+                !scale_tmap(&tm_xs[i], xs, CAP, uint64_t(ks[i] / 32), 128))
+                throw std::runtime_error("tensor map (activations)");
+        if (const char *m = std::getenv("EG2_B200_GEMM")) gemm_exact = !std::strcmp(m, "exact");
         if (!bf16_tmap(&tm_hi, x_hi, 512, CAP, 128) || !bf16_tmap(&tm_lo, x_lo, 512, CAP, 128) ||
             !bf16_tmap(&tm_ple, ple_w, 512, 24 * 512, 256))
             throw std::runtime_error("tensor map (PLE)");
@@ -320,9 +325,11 @@ struct Backend {
         if (stream) cudaStreamDestroy(stream);
     }
 
-    const CUtensorMap &xq_map(int k) const { return tm_xq[k == 512 ? 0 : k == 1024 ? 1 : 2]; }
+    static int kidx(int k) { return k == 512 ? 0 : k == 1024 ? 1 : 2; }
     void gemm(const Q8Weight &w, float *out, int ldo, int n, cudaStream_t s) {
-        ck(launch_q8gemm(xq_map(w.k), w.tmap, w.bn, xs, CAP, w.scales, out, ldo, n, w.rows, w.k, s), "q8 GEMM");
+        ck(launch_q8gemm(tm_xq[kidx(w.k)], w.tmap, tm_xs[kidx(w.k)], w.tscale, w.bn, gemm_exact, out, ldo, n, w.rows,
+                         w.k, s),
+           "q8 GEMM");
     }
 
     // The whole wave as a launch sequence (captured into a graph, or run eagerly

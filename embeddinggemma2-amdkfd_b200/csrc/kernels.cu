@@ -30,38 +30,57 @@ static EncodeTiled encode_fn() {
 }
 
 bool encode_tmap_2d(CUtensorMap *map, CUtensorMapDataType dtype, const void *base, uint64_t inner, uint64_t outer,
-                    uint64_t row_bytes, uint32_t box_inner, uint32_t box_outer) {
+                    uint64_t row_bytes, uint32_t box_inner, uint32_t box_outer, bool swizzle128) {
     EncodeTiled fn = encode_fn();
     if (!fn || (reinterpret_cast<uintptr_t>(base) & 15) || (row_bytes & 15)) return false;
     const cuuint64_t dims[2] = {inner, outer}, strides[1] = {row_bytes};
     const cuuint32_t box[2] = {box_inner, box_outer}, estr[2] = {1, 1};
     return fn(map, dtype, 2, const_cast<void *>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-              CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+              swizzle128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 bool q8_tmap(CUtensorMap *map, const int8_t *base, uint64_t k, uint64_t rows, uint32_t box_rows) {
-    return encode_tmap_2d(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, base, k, rows, k, 128, box_rows);
+    return encode_tmap_2d(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, base, k, rows, k, 128, box_rows, true);
 }
 bool bf16_tmap(CUtensorMap *map, const void *base, uint64_t k, uint64_t rows, uint32_t box_rows) {
-    return encode_tmap_2d(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, base, k, rows, k * 2, 64, box_rows);
+    return encode_tmap_2d(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, base, k, rows, k * 2, 64, box_rows, true);
+}
+bool scale_tmap(CUtensorMap *map, const float *base, uint64_t stride, uint64_t kb, uint32_t box_cols) {
+    return encode_tmap_2d(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, base, stride, kb, stride * 4, box_cols,
+                          uint32_t(kb), false);
+}
+
+static int sm_count() {
+    static int counts[64] = {};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
+    if (!counts[dev]) {
+        int c = 0;
+        cudaDeviceGetAttribute(&c, cudaDevAttrMultiProcessorCount, dev);
+        counts[dev] = c > 0 ? c : 148;
+    }
+    return counts[dev];
 }
 
 // ---------------------------------------------------------------- launchers
-template <int BN>
-static cudaError_t q8gemm_go(const CUtensorMap &a, const CUtensorMap &b, const Q8GemmParams &p, cudaStream_t s) {
-    const size_t smem = q8gemm_smem_bytes(BN, p.K);
-    dim3 grid(p.N / BN, (p.M + 127) / 128);
-    q8gemm_kernel<BN><<<grid, Q8Cfg<BN>::THREADS, smem, s>>>(a, b, p);
+template <int BN, bool EXACT>
+static cudaError_t q8gemm_go(const CUtensorMap &a, const CUtensorMap &b, const CUtensorMap &sa,
+                             const CUtensorMap &sb, const Q8GemmParams &p, cudaStream_t s) {
+    const Q8Smem L = q8gemm_smem(BN, p.K);
+    const int grid = p.num_tiles < sm_count() ? p.num_tiles : sm_count();
+    q8gemm_kernel<BN, EXACT><<<grid, Q8Cfg<BN>::THREADS, L.total, s>>>(a, b, sa, sb, p);
     return cudaGetLastError();
 }
-cudaError_t launch_q8gemm(const CUtensorMap &a, const CUtensorMap &b, int bn, const float *sa, int sa_stride,
-                          const float *sb, float *out, int ldo, int M, int N, int K, cudaStream_t s) {
+cudaError_t launch_q8gemm(const CUtensorMap &a, const CUtensorMap &b, const CUtensorMap &sa, const CUtensorMap &sb,
+                          int bn, bool exact, float *out, int ldo, int M, int N, int K, cudaStream_t s) {
     if (M <= 0) return cudaSuccess;
-    if (K <= 0 || K % 128 || K > 2048 || N <= 0 || N % bn || (bn != 64 && bn != 128) || sa_stride < M || ldo < N)
+    if (K <= 0 || K % 128 || K > 2048 || N <= 0 || N % bn || (bn != 64 && bn != 128) || ldo < N)
         return cudaErrorInvalidValue;
-    if (q8gemm_smem_bytes(bn, K) > 227 * 1024) return cudaErrorInvalidValue;
-    const Q8GemmParams p{sa, sa_stride, sb, out, ldo, M, N, K};
-    return bn == 128 ? q8gemm_go<128>(a, b, p, s) : q8gemm_go<64>(a, b, p, s);
+    if (q8gemm_smem(bn, K).total > 227 * 1024) return cudaErrorInvalidValue;
+    Q8GemmParams p{out, ldo, M, N, K, N / bn, 0};
+    p.num_tiles = ((M + 127) / 128) * p.tiles_n;
+    if (bn == 128) return exact ? q8gemm_go<128, true>(a, b, sa, sb, p, s) : q8gemm_go<128, false>(a, b, sa, sb, p, s);
+    return exact ? q8gemm_go<64, true>(a, b, sa, sb, p, s) : q8gemm_go<64, false>(a, b, sa, sb, p, s);
 }
 
 cudaError_t launch_ple(const CUtensorMap &hi, const CUtensorMap &lo, const CUtensorMap &w, float *ple,
@@ -159,8 +178,14 @@ cudaError_t launch_repack_q8(const void *blocks, int rows, int k, int8_t *codes,
 
 cudaError_t init_kernel_attributes() {
     cudaError_t e;
-    if ((e = cudaFuncSetAttribute(q8gemm_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024))) return e;
-    if ((e = cudaFuncSetAttribute(q8gemm_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024))) return e;
+    if ((e = cudaFuncSetAttribute(q8gemm_kernel<64, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024)))
+        return e;
+    if ((e = cudaFuncSetAttribute(q8gemm_kernel<128, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024)))
+        return e;
+    if ((e = cudaFuncSetAttribute(q8gemm_kernel<64, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024)))
+        return e;
+    if ((e = cudaFuncSetAttribute(q8gemm_kernel<128, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024)))
+        return e;
     if ((e = cudaFuncSetAttribute(ple_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(PleCfg::SMEM)))) return e;
     if ((e = cudaFuncSetAttribute(attention_kernel<256>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                   int(AttnCfg<256>::SMEM))))
@@ -270,13 +295,15 @@ int eg2_launch_norm_quant(const EgNormQuant *p, void *s) {
 int eg2_launch_q8_mm(const EgQ8MM *p, void *s) {
     if (cudaError_t e = ensure_attributes()) return rc(e);
     if (!p->n) return 0;
-    if (p->k % 128 || p->m % 64 || !p->m) return rc(cudaErrorInvalidValue);
-    const int bn = (p->m % 128 == 0 && p->m >= 1024) ? 128 : 64;
-    CUtensorMap a, b;
-    if (!q8_tmap(&a, p->xq, p->k, p->n, 128) || !q8_tmap(&b, p->wq, p->k, p->m, uint32_t(bn)))
+    if (p->k % 128 || p->k > 2048 || p->m % 64 || !p->m || p->xs_stride < p->n || p->xs_stride % 4)
         return rc(cudaErrorInvalidValue);
-    return rc(launch_q8gemm(a, b, bn, p->xs, int(p->xs_stride), p->ws, p->out, int(p->m), int(p->n), int(p->m),
-                            int(p->k), S(s)));
+    const int bn = (p->m % 128 == 0 && p->m >= 1024) ? 128 : 64;
+    CUtensorMap a, b, sa, sb;
+    if (!q8_tmap(&a, p->xq, p->k, p->n, 128) || !q8_tmap(&b, p->wq, p->k, p->m, uint32_t(bn)) ||
+        !scale_tmap(&sa, p->xs, p->xs_stride, p->k / 32, 128) || !scale_tmap(&sb, p->ws, p->m, p->k / 32, uint32_t(bn)))
+        return rc(cudaErrorInvalidValue);
+    return rc(launch_q8gemm(a, b, sa, sb, bn, p->exact != 0, p->out, int(p->m), int(p->n), int(p->m), int(p->k),
+                            S(s)));
 }
 int eg2_launch_qkv_post(const EgQkvPost *p, void *s) {
     return rc(launch_qkv_post(p->q, p->k, p->v, p->qkv, p->q_norm, p->k_norm, p->rope_cos, p->rope_sin, p->pos,

@@ -8,15 +8,18 @@ namespace eg2 {
 
 // cuTensorMapEncodeTiled through the runtime's driver entry point.
 bool encode_tmap_2d(CUtensorMap *map, CUtensorMapDataType dtype, const void *base, uint64_t inner, uint64_t outer,
-                    uint64_t row_bytes, uint32_t box_inner, uint32_t box_outer);
+                    uint64_t row_bytes, uint32_t box_inner, uint32_t box_outer, bool swizzle128);
 // Q8 operand over a row-major int8 buffer [rows][k]: box 128 B x box_rows, 128-byte swizzle.
 bool q8_tmap(CUtensorMap *map, const int8_t *base, uint64_t k, uint64_t rows, uint32_t box_rows);
 // BF16 operand over [rows][k] bf16: box 64 elements x box_rows, 128-byte swizzle.
 bool bf16_tmap(CUtensorMap *map, const void *base, uint64_t k, uint64_t rows, uint32_t box_rows);
+// Block-major fp32 scale plane [kb][stride]: box box_cols x kb, no swizzle.
+bool scale_tmap(CUtensorMap *map, const float *base, uint64_t stride, uint64_t kb, uint32_t box_cols);
 
 // Kernel launches (all asynchronous on `s`).
-cudaError_t launch_q8gemm(const CUtensorMap &a, const CUtensorMap &b, int bn, const float *sa, int sa_stride,
-                          const float *sb, float *out, int ldo, int M, int N, int K, cudaStream_t s);
+// exact: the reference scalar tile's rounding order (bit-identical outputs).
+cudaError_t launch_q8gemm(const CUtensorMap &a, const CUtensorMap &b, const CUtensorMap &sa, const CUtensorMap &sb,
+                          int bn, bool exact, float *out, int ldo, int M, int N, int K, cudaStream_t s);
 cudaError_t launch_ple(const CUtensorMap &hi, const CUtensorMap &lo, const CUtensorMap &w, float *ple,
                        const float *norm, int M, cudaStream_t s);
 cudaError_t launch_embed(float *x, void *x_hi, void *x_lo, const void *emb, const int *ids, int n, cudaStream_t s);

@@ -4,92 +4,109 @@
 // 32-element block b of activation row t and weight row r -- the reference's
 // gemm_q8 (vendor/embeddinggemma.c/src/gemma2_fast.c:242-253, scalar tile
 // :193-204).  One tcgen05.mma with K = 32 is exactly one Q8_0 block, so each
-// block's int32 dot lands exactly (no rounding) in its own TMEM buffer; the
-// epilogue warps convert, scale by the two fp16-exact block scales and
-// accumulate in fp32 registers, in ascending block order.
+// block's int32 dot lands exactly in its own TMEM buffer; the epilogue warps
+// rescale and accumulate in fp32 registers, blocks in ascending order:
+//     t   = round(D_b * ws)            (one FMA, see below)
+//     acc = acc + round(t * xs)        EXACT: the reference scalar tile's order,
+//                                      ((float)dot * dw) * dx then sum +=
+//     acc = fma(t, xs, acc)            otherwise (one rounding fewer)
+// The int32 -> fp32 conversion uses the exact bias trick: with
+// B = 1.5 * 2^23, the bits of D + 0x4B400000 are the float B + D for
+// |D| < 2^22 (|D| <= 32 * 128 * 128 here), and fma(B + D, ws, -B * ws) rounds
+// (B + D) * ws - B * ws = D * ws once; -B * ws is exact because ws is an fp16
+// value.  So D * ws costs one integer add and one FMA, computed in pairs with
+// fma.rn.f32x2.
 //
-// CTA tile 128 tokens x BN weight rows.  Warp roles:
-//   warp 0       TMA producer: int8 tiles [128 x 128 B] of A and [BN x 128 B] of
-//                B per stage, 128-byte swizzle, STAGES-deep ring;
-//   warp 1       TMEM owner and MMA issuer (one elected lane): 4 MMAs per stage,
-//                block j into TMEM buffer j % NBUF, commit -> acc_full[buf];
-//   warps 2..9   epilogue: warp w reads TMEM lanes 32*(w%4).. (its hardware
-//                quadrant) and half (w-2)/4 of the BN columns.
-// The scale panels of the tile (activations [Kb][128], weights [Kb][BN]) are
-// staged in shared memory once per CTA.
+// Persistent CTAs (one per SM) walk the 128 x BN output tiles; warp roles:
+//   warp 0     TMA producer: per tile the scale panels (activation scales
+//              [K/32][128], weight scales [K/32][BN]) into a double buffer, then
+//              int8 A/B tiles of 128 B (one 128-byte swizzle row) per stage;
+//   warp 1     TMEM owner and MMA issuer: block j of the running block counter
+//              into TMEM buffer j % NBUF, commit -> acc_full[buf];
+//   warps 2..  epilogue: 4 * BN/32 warps; warp w reads TMEM lanes 32*(w%4)..
+//              (its hardware quadrant) and 32 of the BN columns.
+// The stage ring, TMEM buffer ring and panel buffers continue across tiles, so
+// loads and MMAs of the next tile overlap the epilogue of the current one.
 #pragma once
 #include "common.cuh"
 
 namespace eg2 {
 
 struct Q8GemmParams {
-    const float *sa;  // activation block scales, [K/32][sa_stride]
-    int sa_stride;
-    const float *sb;  // weight block scales, [K/32][N]
-    float *out;       // [M][ldo] fp32
+    float *out;  // [M][ldo] fp32
     int ldo;
     int M, N, K;
+    int tiles_n, num_tiles;
 };
 
 template <int BN>
 struct Q8Cfg {
-    static constexpr int BM = 128, BK = 128, STAGES = 4, NBUF = 4;
-    static constexpr int EPI_WARPS = 8, THREADS = (2 + EPI_WARPS) * 32;
-    static constexpr int CW = BN / 2;  // columns per epilogue thread
+    static constexpr int BM = 128, BK = 128, STAGES = 4, NBUF = 512 / BN, CW = 32;
+    static constexpr int EPI_WARPS = 4 * (BN / CW), EPI_THREADS = EPI_WARPS * 32;
+    static constexpr int THREADS = (2 + EPI_WARPS) * 32;
     static constexpr int A_BYTES = BM * BK, B_BYTES = BN * BK, STAGE_BYTES = A_BYTES + B_BYTES;
-    static constexpr int TMEM_COLS = NBUF * BN;
     static_assert(BN == 64 || BN == 128, "BN");
-    static_assert(TMEM_COLS == 256 || TMEM_COLS == 512, "TMEM allocation must be a power of two");
 };
 
-__host__ __device__ inline size_t q8gemm_smem_bytes(int bn, int K) {
-    const int kb = K / 32;
-    return 1024 /*alignment slack*/ + size_t(4) * (128 * 128 + bn * 128) + size_t(kb) * 128 * 4 +
-           size_t(kb) * bn * 4 + 256;
+// Shared-memory plan (offsets from the 1024-aligned base) for BN and K.
+struct Q8Smem {
+    int stages, pbufs, kb;
+    size_t stage_bytes, sa_bytes, sb_bytes, prep_bytes, panel_bytes, total;
+    __host__ __device__ size_t panel(int b) const { return size_t(stages) * stage_bytes + size_t(b) * panel_bytes; }
+    __host__ __device__ size_t bars() const { return size_t(stages) * stage_bytes + size_t(pbufs) * panel_bytes; }
+};
+__host__ __device__ inline Q8Smem q8gemm_smem(int bn, int K) {
+    Q8Smem s;
+    s.stages = 4;
+    s.kb = K / 32;
+    s.stage_bytes = size_t(128) * 128 + size_t(bn) * 128;
+    s.sa_bytes = size_t(s.kb) * 128 * 4;
+    s.sb_bytes = size_t(s.kb) * bn * 4;
+    s.prep_bytes = size_t(s.kb) * bn * 8;  // {ws pair, -B*ws pair} per column pair
+    s.panel_bytes = (s.sa_bytes + s.sb_bytes + s.prep_bytes + 1023) / 1024 * 1024;
+    const size_t limit = 227 * 1024, fixed = 1024 + 512;
+    s.pbufs = 2;
+    if (fixed + 4 * s.stage_bytes + 2 * s.panel_bytes > limit) s.pbufs = 1;
+    if (fixed + 4 * s.stage_bytes + s.pbufs * s.panel_bytes > limit) s.stages = 3;
+    s.total = fixed + size_t(s.stages) * s.stage_bytes + size_t(s.pbufs) * s.panel_bytes;
+    return s;
 }
 
-template <int BN>
+template <int BN, bool EXACT>
 __global__ void __launch_bounds__(Q8Cfg<BN>::THREADS, 1)
     q8gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                  const __grid_constant__ CUtensorMap tmSA, const __grid_constant__ CUtensorMap tmSB,
                   const Q8GemmParams p) {
     using C = Q8Cfg<BN>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    const int Kb = p.K / 32, ksteps = p.K / C::BK;
-    float *sa_s = reinterpret_cast<float *>(smem + C::STAGES * C::STAGE_BYTES);
-    float *sb_s = sa_s + Kb * C::BM;
-    uint64_t *full = reinterpret_cast<uint64_t *>(sb_s + Kb * BN);
-    uint64_t *empty = full + C::STAGES;
-    uint64_t *accf = empty + C::STAGES;
-    uint64_t *acce = accf + C::NBUF;
-    uint64_t *mdone = acce + C::NBUF;
+    const Q8Smem L = q8gemm_smem(BN, p.K);
+    const int Kb = L.kb, ksteps = p.K / C::BK, STAGES = L.stages, PBUFS = L.pbufs;
+    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + L.bars());
+    uint64_t *full = bars, *empty = bars + 4, *accf = bars + 8, *acce = accf + C::NBUF;
+    uint64_t *pfull = acce + C::NBUF, *pempty = pfull + 2, *pprep = pempty + 2, *mdone = pprep + 2;
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(mdone + 1);
     volatile int *abort = reinterpret_cast<volatile int *>(tmem_slot + 1);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int m0 = blockIdx.y * C::BM, n0 = blockIdx.x * BN;
-    auto a_tile = [&](int s) { return smem + s * C::STAGE_BYTES; };
-    auto b_tile = [&](int s) { return smem + s * C::STAGE_BYTES + C::A_BYTES; };
+    auto a_tile = [&](int s) { return smem + size_t(s) * L.stage_bytes; };
+    auto b_tile = [&](int s) { return smem + size_t(s) * L.stage_bytes + C::A_BYTES; };
+    auto sa_pan = [&](int b) { return reinterpret_cast<float *>(smem + L.panel(b)); };
+    auto sb_pan = [&](int b) { return reinterpret_cast<float *>(smem + L.panel(b) + L.sa_bytes); };
+    auto prep_pan = [&](int b) { return reinterpret_cast<float4 *>(smem + L.panel(b) + L.sa_bytes + L.sb_bytes); };
 
     if (threadIdx.x == 0) {
-        for (int s = 0; s < C::STAGES; ++s) bar_init(&full[s], 1), bar_init(&empty[s], 1);
+        for (int s = 0; s < STAGES; ++s) bar_init(&full[s], 1), bar_init(&empty[s], 1);
         for (int b = 0; b < C::NBUF; ++b) bar_init(&accf[b], 1), bar_init(&acce[b], C::EPI_WARPS);
+        for (int b = 0; b < PBUFS; ++b)
+            bar_init(&pfull[b], 1), bar_init(&pempty[b], C::EPI_WARPS), bar_init(&pprep[b], C::EPI_WARPS);
         bar_init(mdone, 1);
         *abort = g_error != 0;
         fence_bar_init();
     }
     if (warp == 1) {
-        tmem_alloc(tmem_slot, C::TMEM_COLS);
+        tmem_alloc(tmem_slot, 512);
         tmem_relinquish();
-    }
-    // Scale panels of this tile (coalesced rows of the block-major planes).
-    for (int i = threadIdx.x; i < Kb * C::BM; i += C::THREADS) {
-        const int j = i / C::BM, r = i % C::BM;
-        sa_s[i] = (m0 + r < p.M) ? p.sa[size_t(j) * p.sa_stride + m0 + r] : 0.0f;
-    }
-    for (int i = threadIdx.x; i < Kb * BN; i += C::THREADS) {
-        const int j = i / BN, c = i % BN;
-        sb_s[i] = p.sb[size_t(j) * p.N + n0 + c];
     }
     tc_fence_before();
     __syncthreads();
@@ -97,48 +114,67 @@ __global__ void __launch_bounds__(Q8Cfg<BN>::THREADS, 1)
     const uint32_t tmem = *tmem_slot;
 
     if (warp == 0) {
+        // ------------------------------------------------------------ producer
         if (elect_one() && !*abort) {
-            tma_prefetch(&tmA);
-            tma_prefetch(&tmB);
-            int issued = 0;
-            for (int ks = 0; ks < ksteps; ++ks, ++issued) {
-                const int s = ks % C::STAGES;
-                const uint32_t ph = (ks / C::STAGES) & 1;
-                if (!wait_bar(&empty[s], ph ^ 1, abort)) break;
-                bar_expect_tx(&full[s], C::STAGE_BYTES);
-                tma_load_2d(a_tile(s), &tmA, &full[s], ks * C::BK, m0);
-                tma_load_2d(b_tile(s), &tmB, &full[s], ks * C::BK, n0);
+            tma_prefetch(&tmA), tma_prefetch(&tmB), tma_prefetch(&tmSA), tma_prefetch(&tmSB);
+            int g = 0, issued = 0, it = 0, panels = 0;
+            bool ok = true;
+            for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x, ++it) {
+                const int m0 = (tile / p.tiles_n) * C::BM, n0 = (tile % p.tiles_n) * BN;
+                const int pb = it % PBUFS;
+                if (!wait_bar(&pempty[pb], ((it / PBUFS) & 1) ^ 1, abort)) break;
+                bar_expect_tx(&pfull[pb], uint32_t(L.sa_bytes + L.sb_bytes));
+                tma_load_2d(sa_pan(pb), &tmSA, &pfull[pb], m0, 0);
+                tma_load_2d(sb_pan(pb), &tmSB, &pfull[pb], n0, 0);
+                ++panels;
+                for (int ks = 0; ks < ksteps; ++ks, ++g) {
+                    const int s = g % STAGES;
+                    if (!wait_bar(&empty[s], ((g / STAGES) & 1) ^ 1, abort)) {
+                        ok = false;
+                        break;
+                    }
+                    bar_expect_tx(&full[s], C::STAGE_BYTES);
+                    tma_load_2d(a_tile(s), &tmA, &full[s], ks * C::BK, m0);
+                    tma_load_2d(b_tile(s), &tmB, &full[s], ks * C::BK, n0);
+                    ++issued;
+                }
             }
-            // Drain: the last load into each stage has landed before exit.
-            for (int ks = issued > C::STAGES ? issued - C::STAGES : 0; ks < issued; ++ks)
-                wait_bar(&full[ks % C::STAGES], (ks / C::STAGES) & 1, nullptr);
+            // Drain: the last load into every stage / panel buffer has landed before exit.
+            for (int k = issued > STAGES ? issued - STAGES : 0; k < issued; ++k)
+                wait_bar(&full[k % STAGES], (k / STAGES) & 1, nullptr);
+            for (int k = panels > PBUFS ? panels - PBUFS : 0; k < panels; ++k)
+                wait_bar(&pfull[k % PBUFS], (k / PBUFS) & 1, nullptr);
         }
         __syncwarp();
     } else if (warp == 1) {
+        // ------------------------------------------------------------ MMA issuer
         if (elect_one() && !*abort) {
             constexpr uint32_t idesc = idesc_i8(128, BN);
-            int blk = 0;
+            int g = 0, blk = 0;
             bool ok = true;
-            for (int ks = 0; ks < ksteps && ok; ++ks) {
-                const int s = ks % C::STAGES;
-                const uint32_t ph = (ks / C::STAGES) & 1;
-                if (!wait_bar(&full[s], ph, abort)) break;
-                tc_fence_after();
-                const uint32_t a_addr = smem_u32(a_tile(s)), b_addr = smem_u32(b_tile(s));
-#pragma unroll
-                for (int kk = 0; kk < C::BK / 32; ++kk, ++blk) {
-                    const int buf = blk % C::NBUF;
-                    const uint32_t bph = (blk / C::NBUF) & 1;
-                    if (!wait_bar(&acce[buf], bph ^ 1, abort)) {
+            for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x) {
+                for (int ks = 0; ks < ksteps && ok; ++ks, ++g) {
+                    const int s = g % STAGES;
+                    if (!wait_bar(&full[s], (g / STAGES) & 1, abort)) {
                         ok = false;
                         break;
                     }
                     tc_fence_after();
-                    mma_i8(tmem + uint32_t(buf * BN), desc_sw128(a_addr + kk * 32), desc_sw128(b_addr + kk * 32),
-                           idesc, 0u);
-                    tc_commit(&accf[buf]);
+                    const uint32_t a_addr = smem_u32(a_tile(s)), b_addr = smem_u32(b_tile(s));
+#pragma unroll
+                    for (int kk = 0; kk < C::BK / 32; ++kk, ++blk) {
+                        const int buf = blk % C::NBUF;
+                        if (!wait_bar(&acce[buf], ((blk / C::NBUF) & 1) ^ 1, abort)) {
+                            ok = false;
+                            break;
+                        }
+                        tc_fence_after();
+                        mma_i8(tmem + uint32_t(buf * BN), desc_sw128(a_addr + kk * 32), desc_sw128(b_addr + kk * 32),
+                               idesc, 0u);
+                        tc_commit(&accf[buf]);
+                    }
+                    tc_commit(&empty[s]);
                 }
-                tc_commit(&empty[s]);
             }
             // Drain: every MMA issued above has completed before TMEM is freed.
             tc_commit(mdone);
@@ -146,52 +182,81 @@ __global__ void __launch_bounds__(Q8Cfg<BN>::THREADS, 1)
         }
         __syncwarp();
     } else {
-        const int ew = warp - 2, quad = warp & 3, half = ew >> 2;
-        const int row = quad * 32 + lane, colbase = half * C::CW;
+        // ------------------------------------------------------------ epilogue
+        const int ew = warp - 2, quad = warp & 3, cgrp = ew >> 2;
+        const int row = quad * 32 + lane, colbase = cgrp * C::CW;
         const uint32_t taddr = tmem + (uint32_t(quad * 32) << 16) + uint32_t(colbase);
-        float acc[C::CW];
-#pragma unroll
-        for (int c = 0; c < C::CW; ++c) acc[c] = 0.0f;
+        const int et = threadIdx.x - 64;  // 0 .. EPI_THREADS-1
+        constexpr float BIAS = 12582912.0f;  // 1.5 * 2^23
+        int blk = 0, it = 0;
         bool ok = true;
-        for (int blk = 0; blk < Kb; ++blk) {
-            const int buf = blk % C::NBUF;
-            const uint32_t bph = (blk / C::NBUF) & 1;
-            // tcgen05.ld is warp-collective: leave the loop as a whole warp.
-            if (!__all_sync(0xffffffffu, wait_bar(&accf[buf], bph, abort))) {
-                ok = false;
-                break;
+        for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x, ++it) {
+            const int m0 = (tile / p.tiles_n) * C::BM, n0 = (tile % p.tiles_n) * BN;
+            const int pb = it % PBUFS;
+            if (!__all_sync(0xffffffffu, wait_bar(&pfull[pb], (it / PBUFS) & 1, abort))) break;
+            // Column constants of this tile: {ws[c], ws[c+1], -B*ws[c], -B*ws[c+1]} per pair.
+            {
+                const float *sb = sb_pan(pb);
+                float4 *prep = prep_pan(pb);
+                for (int i = et; i < Kb * BN / 2; i += C::EPI_THREADS) {
+                    const int j = i / (BN / 2), c2 = i % (BN / 2);
+                    const float w0 = sb[j * BN + 2 * c2], w1 = sb[j * BN + 2 * c2 + 1];
+                    prep[i] = make_float4(w0, w1, -BIAS * w0, -BIAS * w1);
+                }
+                // Bounded barrier among the epilogue warps (an mbarrier, not bar.sync, so
+                // that a warp leaving on a timeout cannot strand the others).
+                __syncwarp();
+                if (lane == 0) bar_arrive(&pprep[pb]);
+                if (!__all_sync(0xffffffffu, wait_bar(&pprep[pb], (it / PBUFS) & 1, abort))) break;
             }
-            tc_fence_after();
-            uint32_t d[C::CW];
+            const float *sa_p = sa_pan(pb);
+            const float4 *prep = prep_pan(pb) + colbase / 2;
+            float2 acc[C::CW / 2];
 #pragma unroll
-            for (int c = 0; c < C::CW; c += 32) tmem_ld32(taddr + uint32_t(buf * BN + c), &d[c]);
-            tmem_wait_ld();
-            tc_fence_before();
+            for (int c = 0; c < C::CW / 2; ++c) acc[c] = make_float2(0.0f, 0.0f);
+            for (int j = 0; j < Kb; ++j, ++blk) {
+                const int buf = blk % C::NBUF;
+                // tcgen05.ld is warp-collective: leave the loop as a whole warp.
+                if (!__all_sync(0xffffffffu, wait_bar(&accf[buf], (blk / C::NBUF) & 1, abort))) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                uint32_t d[C::CW];
+                tmem_ld32(taddr + uint32_t(buf * BN), d);
+                tmem_wait_ld();
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) bar_arrive(&acce[buf]);
+                const float sa = sa_p[j * C::BM + row];
+                const float2 sa2 = make_float2(sa, sa);
+                const float4 *pj = prep + j * (BN / 2);
+#pragma unroll
+                for (int c = 0; c < C::CW / 2; ++c) {
+                    const float4 w = pj[c];
+                    const float2 x = make_float2(__int_as_float(int(d[2 * c]) + 0x4B400000),
+                                                 __int_as_float(int(d[2 * c + 1]) + 0x4B400000));
+                    const float2 t = __ffma2_rn(x, make_float2(w.x, w.y), make_float2(w.z, w.w));
+                    if (EXACT) acc[c] = __fadd2_rn(acc[c], __fmul2_rn(t, sa2));
+                    else acc[c] = __ffma2_rn(t, sa2, acc[c]);
+                }
+            }
             __syncwarp();
-            if (lane == 0) bar_arrive(&acce[buf]);
-            const float sa = sa_s[blk * C::BM + row];
-            const float4 *sb4 = reinterpret_cast<const float4 *>(sb_s + blk * BN + colbase);
+            if (lane == 0) bar_arrive(&pempty[pb]);
+            const int m = m0 + row;
+            if (ok && m < p.M) {
+                float4 *o = reinterpret_cast<float4 *>(p.out + size_t(m) * p.ldo + n0 + colbase);
 #pragma unroll
-            for (int c = 0; c < C::CW; c += 4) {
-                const float4 s4 = sb4[c / 4];
-                acc[c + 0] = __fmaf_rn(float(int32_t(d[c + 0])), __fmul_rn(sa, s4.x), acc[c + 0]);
-                acc[c + 1] = __fmaf_rn(float(int32_t(d[c + 1])), __fmul_rn(sa, s4.y), acc[c + 1]);
-                acc[c + 2] = __fmaf_rn(float(int32_t(d[c + 2])), __fmul_rn(sa, s4.z), acc[c + 2]);
-                acc[c + 3] = __fmaf_rn(float(int32_t(d[c + 3])), __fmul_rn(sa, s4.w), acc[c + 3]);
+                for (int c = 0; c < C::CW / 4; ++c)
+                    o[c] = make_float4(acc[2 * c].x, acc[2 * c].y, acc[2 * c + 1].x, acc[2 * c + 1].y);
             }
-        }
-        const int m = m0 + row;
-        if (ok && m < p.M) {
-            float4 *o = reinterpret_cast<float4 *>(p.out + size_t(m) * p.ldo + n0 + colbase);
-#pragma unroll
-            for (int c = 0; c < C::CW; c += 4) o[c / 4] = make_float4(acc[c], acc[c + 1], acc[c + 2], acc[c + 3]);
         }
     }
     tc_fence_before();
     __syncthreads();
     if (warp == 1) {
         tc_fence_after();
-        tmem_dealloc(tmem, C::TMEM_COLS);
+        tmem_dealloc(tmem, 512);
     }
 }
 

@@ -78,8 +78,8 @@ def norm_quant(q, scale, scale_stride, x, weight, rows, width, y=None):
                                                     rows, width))
 
 
-def q8_mm(out, xq, xs, xs_stride, wq, ws, n, k, m):
-    _call("eg2_launch_q8_mm", _lib.EgQ8MM(_p(out), _p(xq), _p(xs), xs_stride, _p(wq), _p(ws), n, k, m))
+def q8_mm(out, xq, xs, xs_stride, wq, ws, n, k, m, exact=False):
+    _call("eg2_launch_q8_mm", _lib.EgQ8MM(_p(out), _p(xq), _p(xs), xs_stride, _p(wq), _p(ws), n, k, m, int(exact)))
 
 
 def qkv_post(q, k, v, qkv, q_norm, k_norm, rope_cos, rope_sin, pos, n, d):

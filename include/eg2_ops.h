@@ -51,10 +51,14 @@ typedef struct {
     const float *x, *weight; unsigned rows, width;
 } EgNormQuant;
 /* out[t][r] = sum_b (int32 dot of block b) * xs[b][t] * ws[b][r]
- * (gemma2_fast.c:242-253): tcgen05 kind::i8, int32 block accumulators in TMEM. */
+ * (gemma2_fast.c:242-253): tcgen05 kind::i8, int32 block accumulators in TMEM.
+ * k % 128 == 0, k <= 2048, m % 64 == 0, xs_stride >= n and a multiple of 4.
+ * exact != 0 rounds like the reference's scalar tile (((float)dot * dw) * dx,
+ * then +=), giving bit-identical outputs; exact == 0 fuses the last multiply
+ * and add (one rounding fewer). */
 typedef struct {
     float *out; const int8_t *xq; const float *xs; unsigned xs_stride;
-    const int8_t *wq; const float *ws; unsigned n, k, m;
+    const int8_t *wq; const float *ws; unsigned n, k, m, exact;
 } EgQ8MM;
 /* Per head RMS (q, k weighted; v plain) and NEOX RoPE from host tables at the
  * token's in-sequence position (ROW_QKV_POST, gemma2_fast.c:692-706).  qkv is

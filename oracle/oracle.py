@@ -188,8 +188,8 @@ class RefGraph:
 
     def gelu_mul(self, g: np.ndarray, u: np.ndarray | None) -> np.ndarray:
         g = np.array(g, dtype=np.float32, copy=True)
-        up = _ptr(np.ascontiguousarray(u, dtype=np.float32)) if u is not None else None
-        self.lib.eg2ref_gelu_mul_row(_ptr(g), up, g.size)
+        u = np.ascontiguousarray(u, dtype=np.float32) if u is not None else None  # kept alive
+        self.lib.eg2ref_gelu_mul_row(_ptr(g), _ptr(u) if u is not None else None, g.size)
         return g
 
     def close(self):
@@ -232,38 +232,40 @@ class Port:
 
     def gelu_mul(self, g, u, mode=1):
         g = np.array(g, dtype=np.float32, copy=True).ravel()
-        up = _ptr(np.ascontiguousarray(u, dtype=np.float32).ravel()) if u is not None else None
-        self.lib.eg2o_gelu_mul(_ptr(g), up, g.size, mode)
+        u = np.ascontiguousarray(u, dtype=np.float32).ravel() if u is not None else None  # kept alive
+        self.lib.eg2o_gelu_mul(_ptr(g), _ptr(u) if u is not None else None, g.size, mode)
         return g
 
     def gemm_q8(self, wq, wd, xq, xd):
         m, k = wq.shape
         n = xq.shape[0]
         y = np.zeros((n, m), np.float32)
-        self.lib.eg2o_gemm_q8(_ptr(np.ascontiguousarray(wq)), _ptr(np.ascontiguousarray(wd)),
-                              _ptr(np.ascontiguousarray(xq)), _ptr(np.ascontiguousarray(xd)), n, k, m, _ptr(y))
+        wq, wd, xq, xd = (np.ascontiguousarray(a) for a in (wq, wd, xq, xd))
+        self.lib.eg2o_gemm_q8(_ptr(wq), _ptr(wd), _ptr(xq), _ptr(xd), n, k, m, _ptr(y))
         return y
 
     def gemm_q8_blockdots(self, wq, xq):
         m, k = wq.shape
         n = xq.shape[0]
         D = np.zeros((n, m, k // 32), np.int32)
-        self.lib.eg2o_gemm_q8_blockdots(_ptr(np.ascontiguousarray(wq)), _ptr(np.ascontiguousarray(xq)), n, k, m, _ptr(D))
+        wq, xq = np.ascontiguousarray(wq), np.ascontiguousarray(xq)
+        self.lib.eg2o_gemm_q8_blockdots(_ptr(wq), _ptr(xq), n, k, m, _ptr(D))
         return D
 
     def gemm_bf16(self, w_bits, x):
         m, k = w_bits.shape
         n = x.shape[0]
         y = np.zeros((n, m), np.float32)
-        self.lib.eg2o_gemm_bf16(_ptr(np.ascontiguousarray(w_bits)), _ptr(np.ascontiguousarray(x, dtype=np.float32)),
-                                n, k, m, _ptr(y))
+        w_bits, x = np.ascontiguousarray(w_bits), np.ascontiguousarray(x, dtype=np.float32)
+        self.lib.eg2o_gemm_bf16(_ptr(w_bits), _ptr(x), n, k, m, _ptr(y))
         return y
 
     def rms_rows(self, x, w):
         x = np.array(x, dtype=np.float32, copy=True)
         d = x.shape[-1]
         rows = x.reshape(-1, d)
-        wp = _ptr(np.ascontiguousarray(w, dtype=np.float32)) if w is not None else None
+        w = np.ascontiguousarray(w, dtype=np.float32) if w is not None else None  # kept alive
+        wp = _ptr(w) if w is not None else None
         for r in range(rows.shape[0]):
             self.lib.eg2o_rms_row(C.c_void_p(rows[r:].ctypes.data), d, wp)
         return x
@@ -277,11 +279,9 @@ class Port:
     def attention(self, q, k, v, lo, hi, kv, d, window):
         n = q.shape[0]
         a = np.zeros((n, 4 * d), np.float32)
-        self.lib.eg2o_attention(_ptr(np.ascontiguousarray(q, dtype=np.float32)),
-                                _ptr(np.ascontiguousarray(k, dtype=np.float32)),
-                                _ptr(np.ascontiguousarray(v, dtype=np.float32)),
-                                _ptr(np.ascontiguousarray(lo, dtype=np.uint32)),
-                                _ptr(np.ascontiguousarray(hi, dtype=np.uint32)), n, kv, d, window, _ptr(a))
+        q, k, v = (np.ascontiguousarray(t, dtype=np.float32) for t in (q, k, v))
+        lo, hi = np.ascontiguousarray(lo, dtype=np.uint32), np.ascontiguousarray(hi, dtype=np.uint32)
+        self.lib.eg2o_attention(_ptr(q), _ptr(k), _ptr(v), _ptr(lo), _ptr(hi), n, kv, d, window, _ptr(a))
         return a
 
     def embed(self, model: Gguf, ids, offsets, quant_mode=ROUND_SCALAR, gelu_mode=0, dump_layers=False):

@@ -63,20 +63,23 @@ def test_long_and_two_wave_goldens(executor, eg2):
 
 
 def test_packed_equals_solo_and_reorder(executor, syn):
-    """tests/http_parity.py:62-69: packed vs solo and reorder invariance."""
-    ids, off = syn.wave((8, 17, 33, 64, 200), seed=31)
+    """tests/http_parity.py:62-69 (packed vs solo >= 0.99999, reorder
+    invariance).  Every operation of a token depends only on its own sequence
+    and is evaluated the same way wherever the sequence sits in the wave, so
+    here the embeddings are bit-identical."""
+    ids, off = syn.wave((8, 17, 33, 64, 200, 700), seed=31)
     packed = executor.batch(ids, off)
     for s in range(len(off) - 1):
         seq = ids[off[s]:off[s + 1]]
         solo = executor.batch(seq, np.array([0, len(seq)], np.uint64))[0]
-        assert float(cosine(solo, packed[s])) > 0.99999
-    order = [3, 0, 4, 2, 1]
+        np.testing.assert_array_equal(solo, packed[s])
+    order = [3, 0, 5, 4, 2, 1]
     seqs = [ids[off[s]:off[s + 1]] for s in order]
     ids2 = np.concatenate(seqs)
     off2 = np.concatenate([[0], np.cumsum([len(s) for s in seqs])]).astype(np.uint64)
     re = executor.batch(ids2, off2)
     for i, s in enumerate(order):
-        assert float(cosine(re[i], packed[s])) > 0.99999
+        np.testing.assert_array_equal(re[i], packed[s])
 
 
 def test_repeatable_and_graph_reuse(executor, syn):

@@ -163,21 +163,37 @@ def _q8_operands(rng, rows, k, pow2=False):
     return q, d.view(np.uint16)
 
 
-def _gpu_q8_mm(ops, xq, xd, wq, wd, stride):
+def _gpu_q8_mm(ops, xq, xd, wq, wd, stride, exact=False):
     n, k = xq.shape
     m = wq.shape[0]
     xs = np.zeros((k // 32, stride), np.float32)
     xs[:, :n] = f16_to_f32(xd).T
     ws = np.ascontiguousarray(f16_to_f32(wd).T)  # [k/32][m]
     out = torch.zeros(n * m, device=DEV)
-    ops.q8_mm(out, T(xq), T(xs), stride, T(wq), T(ws), n, k, m)
+    ops.q8_mm(out, T(xq), T(xs), stride, T(wq), T(ws), n, k, m, exact)
     return host(out).reshape(n, m)
 
 
-@pytest.mark.parametrize("n,k,m", [(130, 512, 2048), (2048, 512, 3072), (200, 1024, 512), (2048, 2048, 512),
-                                   (77, 512, 768), (1, 512, 512), (257, 512, 4096)])
-def test_q8_mm_matches_reference_gemm(ops, port, n, k, m):
+SHAPES = [(130, 512, 2048), (2048, 512, 3072), (200, 1024, 512), (2048, 2048, 512),
+          (77, 512, 768), (1, 512, 512), (257, 512, 4096), (2048, 512, 512)]
+
+
+@pytest.mark.parametrize("n,k,m", SHAPES)
+def test_q8_mm_exact_mode_bit_identical(ops, port, n, k, m):
+    """exact=1 evaluates ((float)dot * dw) * dx and sum += in ascending block
+    order like the reference's scalar tile (gemma2_fast.c:193-204), so the
+    fp32 outputs are identical, not merely close."""
     rng = np.random.default_rng(n * 7 + k + m)
+    xq, xd = _q8_operands(rng, n, k)
+    wq, wd = _q8_operands(rng, m, k)
+    got = _gpu_q8_mm(ops, xq, xd, wq, wd, ((n + 127) // 128) * 128, exact=True)
+    np.testing.assert_array_equal(got, port.gemm_q8(wq, wd, xq, xd))
+
+
+@pytest.mark.parametrize("n,k,m", SHAPES)
+def test_q8_mm_fast_mode_within_tolerance(ops, port, n, k, m):
+    """exact=0 fuses the last multiply-add: within 2e-6 of the output range."""
+    rng = np.random.default_rng(n * 7 + k + m + 1)
     xq, xd = _q8_operands(rng, n, k)
     wq, wd = _q8_operands(rng, m, k)
     got = _gpu_q8_mm(ops, xq, xd, wq, wd, ((n + 127) // 128) * 128)
@@ -195,11 +211,13 @@ def test_q8_mm_int32_block_accumulators_exact(ops, port, n, k, m):
     xq, xd = _q8_operands(rng, n, k, pow2=True)
     wq, wd = _q8_operands(rng, m, k, pow2=True)
     got = _gpu_q8_mm(ops, xq, xd, wq, wd, 512)
+    got_exact = _gpu_q8_mm(ops, xq, xd, wq, wd, 512, exact=True)
     D = port.gemm_q8_blockdots(wq, xq).astype(np.int64)  # [n][m][kb]
     sc = (f16_to_f32(xd)[:, None, :] * f16_to_f32(wd)[None, :, :]).astype(np.int64)
     exact = (D * sc).sum(-1)
     assert np.abs(exact).max() < 2 ** 24
     np.testing.assert_array_equal(got.astype(np.int64), exact)
+    np.testing.assert_array_equal(got_exact.astype(np.int64), exact)
 
 
 @pytest.mark.parametrize("width,stride,offset", [(2048, 2048, 0), (512, 12288, 7 * 512)])
