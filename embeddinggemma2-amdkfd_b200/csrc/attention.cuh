@@ -163,9 +163,11 @@ __global__ void __launch_bounds__(AttnCfg<D>::THREADS) attention_kernel(const At
         for (int j = 0; j < 8; ++j) {
 #pragma unroll
             for (int e = 0; e < 2; ++e) {
+                // Keys past the current sequence belong to the next one: they are
+                // counted in that sequence's own pass, never here.
                 const int s = kb + j * 8 + tq * 2 + e;
-                if (s < lo0 || s >= hi0) sacc[j][e] = -INFINITY;
-                if (s < lo1 || s >= hi1) sacc[j][2 + e] = -INFINITY;
+                if (s < lo0 || s >= hi0 || s >= seq_hi) sacc[j][e] = -INFINITY;
+                if (s < lo1 || s >= hi1 || s >= seq_hi) sacc[j][2 + e] = -INFINITY;
                 mx0 = fmaxf(mx0, sacc[j][e]);
                 mx1 = fmaxf(mx1, sacc[j][2 + e]);
             }

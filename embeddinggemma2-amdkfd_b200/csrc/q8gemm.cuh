@@ -237,8 +237,12 @@ __global__ void __launch_bounds__(Q8Cfg<BN>::THREADS, 1)
                     const float2 x = make_float2(__int_as_float(int(d[2 * c]) + 0x4B400000),
                                                  __int_as_float(int(d[2 * c + 1]) + 0x4B400000));
                     const float2 t = __ffma2_rn(x, make_float2(w.x, w.y), make_float2(w.z, w.w));
-                    if (EXACT) acc[c] = __fadd2_rn(acc[c], __fmul2_rn(t, sa2));
-                    else acc[c] = __ffma2_rn(t, sa2, acc[c]);
+                    if (EXACT) {  // scalar _rn intrinsics are never contracted into an FMA
+                        acc[c].x = __fadd_rn(acc[c].x, __fmul_rn(t.x, sa));
+                        acc[c].y = __fadd_rn(acc[c].y, __fmul_rn(t.y, sa));
+                    } else {
+                        acc[c] = __ffma2_rn(t, sa2, acc[c]);
+                    }
                 }
             }
             __syncwarp();
