@@ -172,7 +172,7 @@ struct Backend {
         w.rows = rows, w.k = k;
         w.codes = dalloc<int8_t>(size_t(rows) * k);
         w.scales = dalloc<float>(size_t(rows) * (k / 32));
-        w.bn = (rows % 128 == 0 && rows >= 1024) ? 128 : 64;
+        w.bn = 64;  // 8 TMEM accumulator buffers in flight
     }
     void finish_q8(Q8Weight &w) {
         if (!q8_tmap(&w.tmap, w.codes, uint64_t(w.k), uint64_t(w.rows), uint32_t(w.bn)) ||

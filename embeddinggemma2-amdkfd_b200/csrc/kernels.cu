@@ -74,12 +74,10 @@ static cudaError_t q8gemm_go(const CUtensorMap &a, const CUtensorMap &b, const C
 cudaError_t launch_q8gemm(const CUtensorMap &a, const CUtensorMap &b, const CUtensorMap &sa, const CUtensorMap &sb,
                           int bn, bool exact, float *out, int ldo, int M, int N, int K, cudaStream_t s) {
     if (M <= 0) return cudaSuccess;
-    if (K <= 0 || K % 128 || K > 2048 || N <= 0 || N % bn || (bn != 64 && bn != 128) || ldo < N)
-        return cudaErrorInvalidValue;
+    if (K <= 0 || K % 128 || K > 2048 || N <= 0 || N % bn || bn != 64 || ldo < N) return cudaErrorInvalidValue;
     if (q8gemm_smem(bn, K).total > 227 * 1024) return cudaErrorInvalidValue;
     Q8GemmParams p{out, ldo, M, N, K, N / bn, 0};
     p.num_tiles = ((M + 127) / 128) * p.tiles_n;
-    if (bn == 128) return exact ? q8gemm_go<128, true>(a, b, sa, sb, p, s) : q8gemm_go<128, false>(a, b, sa, sb, p, s);
     return exact ? q8gemm_go<64, true>(a, b, sa, sb, p, s) : q8gemm_go<64, false>(a, b, sa, sb, p, s);
 }
 
@@ -180,11 +178,7 @@ cudaError_t init_kernel_attributes() {
     cudaError_t e;
     if ((e = cudaFuncSetAttribute(q8gemm_kernel<64, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024)))
         return e;
-    if ((e = cudaFuncSetAttribute(q8gemm_kernel<128, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024)))
-        return e;
     if ((e = cudaFuncSetAttribute(q8gemm_kernel<64, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024)))
-        return e;
-    if ((e = cudaFuncSetAttribute(q8gemm_kernel<128, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024)))
         return e;
     if ((e = cudaFuncSetAttribute(ple_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(PleCfg::SMEM)))) return e;
     if ((e = cudaFuncSetAttribute(attention_kernel<256>, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -297,7 +291,7 @@ int eg2_launch_q8_mm(const EgQ8MM *p, void *s) {
     if (!p->n) return 0;
     if (p->k % 128 || p->k > 2048 || p->m % 64 || !p->m || p->xs_stride < p->n || p->xs_stride % 4)
         return rc(cudaErrorInvalidValue);
-    const int bn = (p->m % 128 == 0 && p->m >= 1024) ? 128 : 64;
+    const int bn = 64;  // 8 TMEM accumulator buffers in flight
     CUtensorMap a, b, sa, sb;
     if (!q8_tmap(&a, p->xq, p->k, p->n, 128) || !q8_tmap(&b, p->wq, p->k, p->m, uint32_t(bn)) ||
         !scale_tmap(&sa, p->xs, p->xs_stride, p->k / 32, 128) || !scale_tmap(&sb, p->ws, p->m, p->k / 32, uint32_t(bn)))

@@ -23,8 +23,8 @@
 //              int8 A/B tiles of 128 B (one 128-byte swizzle row) per stage;
 //   warp 1     TMEM owner and MMA issuer: block j of the running block counter
 //              into TMEM buffer j % NBUF, commit -> acc_full[buf];
-//   warps 2..  epilogue: 4 * BN/32 warps; warp w reads TMEM lanes 32*(w%4)..
-//              (its hardware quadrant) and 32 of the BN columns.
+//   warps 2..9 epilogue: warp w reads TMEM lanes 32*(w%4).. (its hardware
+//              quadrant) and 32 of the 64 columns.
 // The stage ring, TMEM buffer ring and panel buffers continue across tiles, so
 // loads and MMAs of the next tile overlap the epilogue of the current one.
 #pragma once
@@ -45,7 +45,7 @@ struct Q8Cfg {
     static constexpr int EPI_WARPS = 4 * (BN / CW), EPI_THREADS = EPI_WARPS * 32;
     static constexpr int THREADS = (2 + EPI_WARPS) * 32;
     static constexpr int A_BYTES = BM * BK, B_BYTES = BN * BK, STAGE_BYTES = A_BYTES + B_BYTES;
-    static_assert(BN == 64 || BN == 128, "BN");
+    static_assert(BN == 64, "tuned for N = 64: 8 TMEM accumulator buffers, 8 epilogue warps");
 };
 
 // Shared-memory plan (offsets from the 1024-aligned base) for BN and K.
@@ -214,28 +214,40 @@ __global__ void __launch_bounds__(Q8Cfg<BN>::THREADS, 1)
             float2 acc[C::CW / 2];
 #pragma unroll
             for (int c = 0; c < C::CW / 2; ++c) acc[c] = make_float2(0.0f, 0.0f);
-            for (int j = 0; j < Kb; ++j, ++blk) {
-                const int buf = blk % C::NBUF;
-                // tcgen05.ld is warp-collective: leave the loop as a whole warp.
-                if (!__all_sync(0xffffffffu, wait_bar(&accf[buf], (blk / C::NBUF) & 1, abort))) {
-                    ok = false;
-                    break;
-                }
+            // TMEM loads are software-pipelined: block j+1 is in flight while block
+            // j is scaled, so the load latency overlaps the arithmetic (ping-pong
+            // register buffers dA / dB; Kb is even).
+            uint32_t dA[C::CW], dB[C::CW];
+            if (!__all_sync(0xffffffffu, wait_bar(&accf[blk % C::NBUF], (blk / C::NBUF) & 1, abort))) {
+                ok = false;
+            } else {
                 tc_fence_after();
-                uint32_t d[C::CW];
-                tmem_ld32(taddr + uint32_t(buf * BN), d);
+                tmem_ld32(taddr + uint32_t((blk % C::NBUF) * BN), dA);
+            }
+            auto step = [&](int j, const uint32_t (&dc)[C::CW], uint32_t (&dn)[C::CW]) {
+                const int buf = blk % C::NBUF;
                 tmem_wait_ld();
                 tc_fence_before();
                 __syncwarp();
                 if (lane == 0) bar_arrive(&acce[buf]);
+                if (j + 1 < Kb) {
+                    const int nb = (blk + 1) % C::NBUF;
+                    // tcgen05.ld is warp-collective: decide as a whole warp.
+                    if (!__all_sync(0xffffffffu, wait_bar(&accf[nb], ((blk + 1) / C::NBUF) & 1, abort))) {
+                        ok = false;
+                    } else {
+                        tc_fence_after();
+                        tmem_ld32(taddr + uint32_t(nb * BN), dn);
+                    }
+                }
                 const float sa = sa_p[j * C::BM + row];
                 const float2 sa2 = make_float2(sa, sa);
                 const float4 *pj = prep + j * (BN / 2);
 #pragma unroll
                 for (int c = 0; c < C::CW / 2; ++c) {
                     const float4 w = pj[c];
-                    const float2 x = make_float2(__int_as_float(int(d[2 * c]) + 0x4B400000),
-                                                 __int_as_float(int(d[2 * c + 1]) + 0x4B400000));
+                    const float2 x = make_float2(__int_as_float(int(dc[2 * c]) + 0x4B400000),
+                                                 __int_as_float(int(dc[2 * c + 1]) + 0x4B400000));
                     const float2 t = __ffma2_rn(x, make_float2(w.x, w.y), make_float2(w.z, w.w));
                     if (EXACT) {  // scalar _rn intrinsics are never contracted into an FMA
                         acc[c].x = __fadd_rn(acc[c].x, __fmul_rn(t.x, sa));
@@ -244,7 +256,13 @@ __global__ void __launch_bounds__(Q8Cfg<BN>::THREADS, 1)
                         acc[c] = __ffma2_rn(t, sa2, acc[c]);
                     }
                 }
+                ++blk;
+            };
+            for (int j = 0; j < Kb && ok; j += 2) {
+                step(j, dA, dB);
+                if (ok) step(j + 1, dB, dA);
             }
+            tmem_wait_ld();  // no load may be left in flight on any exit path
             __syncwarp();
             if (lane == 0) bar_arrive(&pempty[pb]);
             const int m = m0 + row;
