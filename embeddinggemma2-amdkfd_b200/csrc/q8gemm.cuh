@@ -23,8 +23,9 @@
 //              int8 A/B tiles of 128 B (one 128-byte swizzle row) per stage;
 //   warp 1     TMEM owner and MMA issuer: block j of the running block counter
 //              into TMEM buffer j % NBUF, commit -> acc_full[buf];
-//   warps 2..9 epilogue: warp w reads TMEM lanes 32*(w%4).. (its hardware
-//              quadrant) and 32 of the 64 columns.
+//   warps 2..17 epilogue: warp w reads TMEM lanes 32*(w%4).. (its hardware
+//              quadrant) and 16 of the 64 columns; four warps per SM
+//              sub-partition keep the per-block scaling latency hidden.
 // The stage ring, TMEM buffer ring and panel buffers continue across tiles, so
 // loads and MMAs of the next tile overlap the epilogue of the current one.
 #pragma once
@@ -41,11 +42,11 @@ struct Q8GemmParams {
 
 template <int BN>
 struct Q8Cfg {
-    static constexpr int BM = 128, BK = 128, STAGES = 4, NBUF = 512 / BN, CW = 32;
+    static constexpr int BM = 128, BK = 128, STAGES = 4, NBUF = 512 / BN, CW = 16;
     static constexpr int EPI_WARPS = 4 * (BN / CW), EPI_THREADS = EPI_WARPS * 32;
     static constexpr int THREADS = (2 + EPI_WARPS) * 32;
     static constexpr int A_BYTES = BM * BK, B_BYTES = BN * BK, STAGE_BYTES = A_BYTES + B_BYTES;
-    static_assert(BN == 64, "tuned for N = 64: 8 TMEM accumulator buffers, 8 epilogue warps");
+    static_assert(BN == 64, "tuned for N = 64: 8 TMEM accumulator buffers, 16 epilogue warps");
 };
 
 // Shared-memory plan (offsets from the 1024-aligned base) for BN and K.
@@ -222,7 +223,7 @@ __global__ void __launch_bounds__(Q8Cfg<BN>::THREADS, 1)
                 ok = false;
             } else {
                 tc_fence_after();
-                tmem_ld32(taddr + uint32_t((blk % C::NBUF) * BN), dA);
+                tmem_ld16(taddr + uint32_t((blk % C::NBUF) * BN), dA);
             }
             auto step = [&](int j, const uint32_t (&dc)[C::CW], uint32_t (&dn)[C::CW]) {
                 const int buf = blk % C::NBUF;
@@ -237,15 +238,18 @@ __global__ void __launch_bounds__(Q8Cfg<BN>::THREADS, 1)
                         ok = false;
                     } else {
                         tc_fence_after();
-                        tmem_ld32(taddr + uint32_t(nb * BN), dn);
+                        tmem_ld16(taddr + uint32_t(nb * BN), dn);
                     }
                 }
                 const float sa = sa_p[j * C::BM + row];
                 const float2 sa2 = make_float2(sa, sa);
                 const float4 *pj = prep + j * (BN / 2);
+                float4 wv[C::CW / 2];  // all column constants first: one round of shared-memory latency
+#pragma unroll
+                for (int c = 0; c < C::CW / 2; ++c) wv[c] = pj[c];
 #pragma unroll
                 for (int c = 0; c < C::CW / 2; ++c) {
-                    const float4 w = pj[c];
+                    const float4 w = wv[c];
                     const float2 x = make_float2(__int_as_float(int(dc[2 * c]) + 0x4B400000),
                                                  __int_as_float(int(dc[2 * c + 1]) + 0x4B400000));
                     const float2 t = __ffma2_rn(x, make_float2(w.x, w.y), make_float2(w.z, w.w));
