@@ -17,17 +17,21 @@
 // value.  So D * ws costs one integer add and one FMA, computed in pairs with
 // fma.rn.f32x2.
 //
-// Persistent CTAs (one per SM) walk the 128 x BN output tiles; warp roles:
-//   warp 0     TMA producer: per tile the scale panels (activation scales
-//              [K/32][128], weight scales [K/32][BN]) into a double buffer, then
-//              int8 A/B tiles of 128 B (one 128-byte swizzle row) per stage;
-//   warp 1     TMEM owner and MMA issuer: block j of the running block counter
-//              into TMEM buffer j % NBUF, commit -> acc_full[buf];
+// Persistent CTAs (one per SM) walk the 128 x 64 output tiles; warp roles:
+//   warp 0      TMA producer: per tile the scale panels (activation scales
+//               [K/32][128], weight scales [K/32][64]) into a double buffer, then
+//               int8 A/B tiles of 128 B (one 128-byte swizzle row) per stage;
+//   warp 1      TMEM owner and MMA issuer: each Q8 block j is four N=16 MMAs,
+//               one per 16-column sub-tile q, into TMEM columns
+//               q*128 + (j % 8)*16; commit -> acc_full[j % 8];
 //   warps 2..17 epilogue: warp w reads TMEM lanes 32*(w%4).. (its hardware
-//              quadrant) and 16 of the 64 columns; four warps per SM
-//              sub-partition keep the per-block scaling latency hidden.
-// The stage ring, TMEM buffer ring and panel buffers continue across tiles, so
-// loads and MMAs of the next tile overlap the epilogue of the current one.
+//               quadrant) of sub-tile q = (w-2)/4.
+// Because a sub-tile's eight block slots are adjacent TMEM columns, one
+// 32-column tcgen05.ld brings a warp the accumulators of two consecutive
+// blocks: the load latency that follows an MMA's completion is paid once per
+// two blocks instead of once per block.  The stage ring, TMEM slots and panel
+// buffers continue across tiles, so loads and MMAs of the next tile overlap the
+// epilogue of the current one.
 #pragma once
 #include "common.cuh"
 
@@ -42,7 +46,8 @@ struct Q8GemmParams {
 
 template <int BN>
 struct Q8Cfg {
-    static constexpr int BM = 128, BK = 128, STAGES = 4, NBUF = 512 / BN, CW = 16;
+    static constexpr int BM = 128, BK = 128, STAGES = 4, CW = 16, NSUB = BN / CW, NBUF = 512 / BN;
+    static constexpr int GRP = 2;  // blocks fetched by one epilogue TMEM load (registers: 18 warps -> 96/thread)
     static constexpr int EPI_WARPS = 4 * (BN / CW), EPI_THREADS = EPI_WARPS * 32;
     static constexpr int THREADS = (2 + EPI_WARPS) * 32;
     static constexpr int A_BYTES = BM * BK, B_BYTES = BN * BK, STAGE_BYTES = A_BYTES + B_BYTES;
@@ -150,7 +155,7 @@ __global__ void __launch_bounds__(Q8Cfg<BN>::THREADS, 1)
     } else if (warp == 1) {
         // ------------------------------------------------------------ MMA issuer
         if (elect_one() && !*abort) {
-            constexpr uint32_t idesc = idesc_i8(128, BN);
+            constexpr uint32_t idesc = idesc_i8(128, C::CW);
             int g = 0, blk = 0;
             bool ok = true;
             for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x) {
@@ -170,8 +175,11 @@ __global__ void __launch_bounds__(Q8Cfg<BN>::THREADS, 1)
                             break;
                         }
                         tc_fence_after();
-                        mma_i8(tmem + uint32_t(buf * BN), desc_sw128(a_addr + kk * 32), desc_sw128(b_addr + kk * 32),
-                               idesc, 0u);
+                        const uint64_t ad = desc_sw128(a_addr + kk * 32);
+#pragma unroll
+                        for (int q = 0; q < C::NSUB; ++q)  // sub-tile q: weight rows 16q.., 2 KB into the B tile
+                            mma_i8(tmem + uint32_t(q * C::NBUF * C::CW + buf * C::CW), ad,
+                                   desc_sw128(b_addr + q * C::CW * 128 + kk * 32), idesc, 0u);
                         tc_commit(&accf[buf]);
                     }
                     tc_commit(&empty[s]);
@@ -184,9 +192,9 @@ __global__ void __launch_bounds__(Q8Cfg<BN>::THREADS, 1)
         __syncwarp();
     } else {
         // ------------------------------------------------------------ epilogue
-        const int ew = warp - 2, quad = warp & 3, cgrp = ew >> 2;
-        const int row = quad * 32 + lane, colbase = cgrp * C::CW;
-        const uint32_t taddr = tmem + (uint32_t(quad * 32) << 16) + uint32_t(colbase);
+        const int ew = warp - 2, quad = warp & 3, sub = ew >> 2;
+        const int row = quad * 32 + lane, colbase = sub * C::CW;
+        const uint32_t taddr = tmem + (uint32_t(quad * 32) << 16) + uint32_t(sub * C::NBUF * C::CW);
         const int et = threadIdx.x - 64;  // 0 .. EPI_THREADS-1
         constexpr float BIAS = 12582912.0f;  // 1.5 * 2^23
         int blk = 0, it = 0;
@@ -215,58 +223,51 @@ __global__ void __launch_bounds__(Q8Cfg<BN>::THREADS, 1)
             float2 acc[C::CW / 2];
 #pragma unroll
             for (int c = 0; c < C::CW / 2; ++c) acc[c] = make_float2(0.0f, 0.0f);
-            // TMEM loads are software-pipelined: block j+1 is in flight while block
-            // j is scaled, so the load latency overlaps the arithmetic (ping-pong
-            // register buffers dA / dB; Kb is even).
-            uint32_t dA[C::CW], dB[C::CW];
-            if (!__all_sync(0xffffffffu, wait_bar(&accf[blk % C::NBUF], (blk / C::NBUF) & 1, abort))) {
-                ok = false;
-            } else {
+            // One 32-column TMEM load per two blocks (GRP); the per-block column
+            // constants are read after the load completed, so no shared-memory
+            // access queues behind an outstanding TMEM load.
+            for (int j = 0; j < Kb && ok; j += C::GRP) {
+                bool ready = true;
+#pragma unroll
+                for (int g = 0; g < C::GRP; ++g)
+                    ready = ready && wait_bar(&accf[(blk + g) % C::NBUF], ((blk + g) / C::NBUF) & 1, abort);
+                // tcgen05.ld is warp-collective: decide as a whole warp.
+                if (!__all_sync(0xffffffffu, ready)) {
+                    ok = false;
+                    break;
+                }
                 tc_fence_after();
-                tmem_ld16(taddr + uint32_t((blk % C::NBUF) * BN), dA);
-            }
-            auto step = [&](int j, const uint32_t (&dc)[C::CW], uint32_t (&dn)[C::CW]) {
-                const int buf = blk % C::NBUF;
+                uint32_t d[C::GRP * C::CW];
+                tmem_ld32(taddr + uint32_t((blk % C::NBUF) * C::CW), d);
                 tmem_wait_ld();
                 tc_fence_before();
                 __syncwarp();
-                if (lane == 0) bar_arrive(&acce[buf]);
-                if (j + 1 < Kb) {
-                    const int nb = (blk + 1) % C::NBUF;
-                    // tcgen05.ld is warp-collective: decide as a whole warp.
-                    if (!__all_sync(0xffffffffu, wait_bar(&accf[nb], ((blk + 1) / C::NBUF) & 1, abort))) {
-                        ok = false;
-                    } else {
-                        tc_fence_after();
-                        tmem_ld16(taddr + uint32_t(nb * BN), dn);
+                if (lane == 0) {
+#pragma unroll
+                    for (int g = 0; g < C::GRP; ++g) bar_arrive(&acce[(blk + g) % C::NBUF]);
+                }
+#pragma unroll
+                for (int g = 0; g < C::GRP; ++g) {
+                    const float sa = sa_p[(j + g) * C::BM + row];
+                    const float2 sa2 = make_float2(sa, sa);
+                    const float4 *pj = prep + (j + g) * (BN / 2);
+#pragma unroll
+                    for (int c = 0; c < C::CW / 2; ++c) {
+                        const float4 w = pj[c];
+                        const uint32_t *dc = d + g * C::CW;
+                        const float2 x = make_float2(__int_as_float(int(dc[2 * c]) + 0x4B400000),
+                                                     __int_as_float(int(dc[2 * c + 1]) + 0x4B400000));
+                        const float2 t = __ffma2_rn(x, make_float2(w.x, w.y), make_float2(w.z, w.w));
+                        if (EXACT) {  // scalar _rn intrinsics are never contracted into an FMA
+                            acc[c].x = __fadd_rn(acc[c].x, __fmul_rn(t.x, sa));
+                            acc[c].y = __fadd_rn(acc[c].y, __fmul_rn(t.y, sa));
+                        } else {
+                            acc[c] = __ffma2_rn(t, sa2, acc[c]);
+                        }
                     }
                 }
-                const float sa = sa_p[j * C::BM + row];
-                const float2 sa2 = make_float2(sa, sa);
-                const float4 *pj = prep + j * (BN / 2);
-                float4 wv[C::CW / 2];  // all column constants first: one round of shared-memory latency
-#pragma unroll
-                for (int c = 0; c < C::CW / 2; ++c) wv[c] = pj[c];
-#pragma unroll
-                for (int c = 0; c < C::CW / 2; ++c) {
-                    const float4 w = wv[c];
-                    const float2 x = make_float2(__int_as_float(int(dc[2 * c]) + 0x4B400000),
-                                                 __int_as_float(int(dc[2 * c + 1]) + 0x4B400000));
-                    const float2 t = __ffma2_rn(x, make_float2(w.x, w.y), make_float2(w.z, w.w));
-                    if (EXACT) {  // scalar _rn intrinsics are never contracted into an FMA
-                        acc[c].x = __fadd_rn(acc[c].x, __fmul_rn(t.x, sa));
-                        acc[c].y = __fadd_rn(acc[c].y, __fmul_rn(t.y, sa));
-                    } else {
-                        acc[c] = __ffma2_rn(t, sa2, acc[c]);
-                    }
-                }
-                ++blk;
-            };
-            for (int j = 0; j < Kb && ok; j += 2) {
-                step(j, dA, dB);
-                if (ok) step(j + 1, dB, dA);
+                blk += C::GRP;
             }
-            tmem_wait_ld();  // no load may be left in flight on any exit path
             __syncwarp();
             if (lane == 0) bar_arrive(&pempty[pb]);
             const int m = m0 + row;
