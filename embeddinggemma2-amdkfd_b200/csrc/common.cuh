@@ -20,6 +20,14 @@ enum : int { ERR_NONE = 0, ERR_WAIT_TIMEOUT = 1 };
 __device__ __forceinline__ uint32_t smem_u32(const void *p) {
     return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }
+// Rounds the dynamic shared-memory base up to a 1024-byte boundary (the
+// 128-byte swizzle atom repeats every 1024 bytes) by pointer arithmetic on the
+// shared array itself, so the compiler still knows every derived pointer is
+// shared memory and emits LDS/STS (an integer round trip would turn each access
+// into a generic load tracked on the long scoreboard).
+__device__ __forceinline__ uint8_t *align_smem_1024(uint8_t *raw) {
+    return raw + ((1024u - (smem_u32(raw) & 1023u)) & 1023u);
+}
 __device__ __forceinline__ uint64_t globaltimer_ns() {
     uint64_t t;
     asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));

@@ -35,7 +35,7 @@ __global__ void __launch_bounds__(PleCfg::THREADS, 1)
                const __grid_constant__ CUtensorMap tmW, const PleParams p) {
     using C = PleCfg;
     extern __shared__ uint8_t smem_raw[];
-    uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t *smem = align_smem_1024(smem_raw);
     double *partial = reinterpret_cast<double *>(smem + C::STAGES * C::STAGE_BYTES);  // [2][128]
     uint64_t *full = reinterpret_cast<uint64_t *>(partial + 2 * C::BM);
     uint64_t *empty = full + C::STAGES;

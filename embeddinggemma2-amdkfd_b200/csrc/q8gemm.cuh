@@ -85,7 +85,7 @@ __global__ void __launch_bounds__(Q8Cfg<BN>::THREADS, 1)
                   const Q8GemmParams p) {
     using C = Q8Cfg<BN>;
     extern __shared__ uint8_t smem_raw[];
-    uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t *smem = align_smem_1024(smem_raw);
     const Q8Smem L = q8gemm_smem(BN, p.K);
     const int Kb = L.kb, ksteps = p.K / C::BK, STAGES = L.stages, PBUFS = L.pbufs;
     uint64_t *bars = reinterpret_cast<uint64_t *>(smem + L.bars());
