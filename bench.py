@@ -132,15 +132,29 @@ def cpu_baseline_run(model_path, lengths, steps, warmup, seed):
     return res
 
 
-def dist_init(n_gpus):
+def dist_init(backend="nccl"):
+    """One process per GPU (torchrun env); the group carries only the barrier and
+    the max-over-ranks time, never embedding data."""
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
     if world > 1:
         import datetime
         import torch.distributed as dist
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300))
+        dist.init_process_group(backend, timeout=datetime.timedelta(seconds=120))
     return rank, world, local
+
+
+def rank_wave(lengths, rank):
+    """Each rank embeds its own wave of the same shape (weak scaling): the units
+    are whole waves, so ranks share nothing on the data path."""
+    syn = importlib.import_module("embeddinggemma2-amdkfd_b200.synthetic")
+    return syn.wave(lengths, seed=100 + rank)
+
+
+def whole_job_rate(tokens_per_rank, world, steps, ms_max):
+    """Tokens all ranks embedded / the slowest rank's time."""
+    return tokens_per_rank * world * steps / (ms_max * 1e-3)
 
 
 def reference_arm(args, rank, world):
@@ -171,7 +185,7 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
-    rank, world, local = dist_init(args.gpus)
+    rank, world, local = dist_init()
     if args.impl == "reference":
         reference_arm(args, rank, world)
         return finalize(world)
@@ -184,7 +198,7 @@ def main():
     torch.cuda.set_device(local)
     model = eg2.GGUFModel(model_path)
     ex = eg2.Gemma2Executor(model, local)
-    ids, off = syn.wave(lengths, seed=100 + rank)
+    ids, off = rank_wave(lengths, rank)
     n, batch = int(off[-1]), len(off) - 1
     stream = torch.cuda.ExternalStream(ex.stream, device=local)
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=local)
@@ -210,7 +224,7 @@ def main():
     out_dev = ex.finish()
     step_ms = [s.elapsed_time(e) for s, e in zip(starts, ends)]
     dev_ms = sum(step_ms)
-    dev_ms_max = reduce_max(dev_ms, world, local)
+    dev_ms_max = reduce_max(dev_ms, world, f"cuda:{local}")
 
     # ---- e2e: the public C ABI with host buffers every step
     for _ in range(args.warmup):
@@ -222,7 +236,7 @@ def main():
         out = ex.batch(ids, off)
     e2e_ms = (time.perf_counter() - t0) * 1000.0
     barrier(world)
-    e2e_ms_max = reduce_max(e2e_ms, world, local)
+    e2e_ms_max = reduce_max(e2e_ms, world, f"cuda:{local}")
     assert np.isfinite(out).all() and np.allclose(out, out_dev, atol=1e-6)
 
     # ---- dominant kernel: per-group event timing of one eager wave
@@ -232,10 +246,9 @@ def main():
     pk, src = peaks()
     int8_peak = 2.0 * pk["bf16_tflops_sustained"]
     achieved = q8_gemm_ops(n) / (gemm_ms * 1e-3) / 1e12
-    total_tokens = n * world
     line = {
         "metric": METRIC,
-        "value": total_tokens * args.steps / (dev_ms_max * 1e-3),
+        "value": whole_job_rate(n, world, args.steps, dev_ms_max),
         "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": dev_ms_max / args.steps, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "int8+fp32", "data": "synthetic",
@@ -243,7 +256,7 @@ def main():
                    "BASELINE weight distributions)", "tokens_per_wave_per_gpu": n, "sequences_per_wave": batch,
                    "parallelism": f"replicas x{world} (whole waves per GPU, no collective)",
                    "l2": "256 MiB write between timed steps; per-wave working set > L2 (151 MB weights, 100 MB PLE)"},
-        "e2e": {"value": total_tokens * args.steps / (e2e_ms_max * 1e-3), "unit": "tokens/s",
+        "e2e": {"value": whole_job_rate(n, world, args.steps, e2e_ms_max), "unit": "tokens/s",
                 "h2d_bytes_per_step": n * 4 + n * 8 + n * 4 + (batch + 1) * 4,
                 "d2h_bytes_per_step": batch * 768 * 4},
         "gpu_launches": ex.kernels_per_wave * args.steps,
@@ -269,12 +282,12 @@ def barrier(world):
         dist.barrier()
 
 
-def reduce_max(v, world, local):
+def reduce_max(v, world, device):
     if world == 1:
         return v
     import torch
     import torch.distributed as dist
-    t = torch.tensor([v], dtype=torch.float64, device=f"cuda:{local}")
+    t = torch.tensor([v], dtype=torch.float64, device=device)
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
     return float(t.item())
 
