@@ -202,6 +202,14 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t *r) {
         : "r"(taddr));
 }
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+// After tcgen05.wait::ld: marks the destination registers of the completed
+// loads as redefined here, so the compiler cannot move their first use above
+// the wait (the tcgen05.ld statement itself only names them as outputs).
+template <int N>
+__device__ __forceinline__ void reg_fence(uint32_t (&r)[N]) {
+#pragma unroll
+    for (int i = 0; i < N; ++i) asm volatile("" : "+r"(r[i]));
+}
 
 // ---------------------------------------------------------------- exact scalar math
 // fp32 -> fp16 bits with the reference's rounding (quants.c:13-37): ties on

@@ -60,7 +60,6 @@ struct Q8Weight {
     float *scales = nullptr;  // [k/32][rows]
     int rows = 0, k = 0;
     CUtensorMap tmap{}, tscale{};
-    int bn = 64;
 };
 
 struct Layer {
@@ -172,11 +171,10 @@ struct Backend {
         w.rows = rows, w.k = k;
         w.codes = dalloc<int8_t>(size_t(rows) * k);
         w.scales = dalloc<float>(size_t(rows) * (k / 32));
-        w.bn = 64;  // 8 TMEM accumulator buffers in flight
     }
     void finish_q8(Q8Weight &w) {
-        if (!q8_tmap(&w.tmap, w.codes, uint64_t(w.k), uint64_t(w.rows), uint32_t(w.bn)) ||
-            !scale_tmap(&w.tscale, w.scales, uint64_t(w.rows), uint64_t(w.k / 32), uint32_t(w.bn)))
+        if (w.rows % 128 || !q8_tmap(&w.tmap, w.codes, uint64_t(w.k), uint64_t(w.rows), 128) ||
+            !scale_tmap(&w.tscale, w.scales, uint64_t(w.rows), uint64_t(w.k / 32), 128))
             throw std::runtime_error("cuTensorMapEncodeTiled failed for a weight");
     }
 
@@ -295,8 +293,8 @@ struct Backend {
         pooled = dalloc<float>(size_t(CAP) * 768);
         const int ks[3] = {512, 1024, 2048};
         for (int i = 0; i < 3; ++i)
-            if (!q8_tmap(&tm_xq[i], xq, uint64_t(ks[i]), CAP, 128) ||
-                !scale_tmap(&tm_xs[i], xs, CAP, uint64_t(ks[i] / 32), 128))
+            if (!q8_tmap(&tm_xq[i], xq, uint64_t(ks[i]), CAP, 64) ||
+                !scale_tmap(&tm_xs[i], xs, CAP, uint64_t(ks[i] / 32), 64))
                 throw std::runtime_error("tensor map (activations)");
         if (const char *m = std::getenv("EG2_B200_GEMM")) gemm_exact = !std::strcmp(m, "exact");
         if (!bf16_tmap(&tm_hi, x_hi, 512, CAP, 128) || !bf16_tmap(&tm_lo, x_lo, 512, CAP, 128) ||
@@ -327,8 +325,8 @@ struct Backend {
 
     static int kidx(int k) { return k == 512 ? 0 : k == 1024 ? 1 : 2; }
     void gemm(const Q8Weight &w, float *out, int ldo, int n, cudaStream_t s) {
-        ck(launch_q8gemm(tm_xq[kidx(w.k)], w.tmap, tm_xs[kidx(w.k)], w.tscale, w.bn, gemm_exact, out, ldo, n, w.rows,
-                         w.k, s),
+        ck(launch_q8gemm(w.tmap, tm_xq[kidx(w.k)], w.tscale, tm_xs[kidx(w.k)], gemm_exact, out, ldo, n, w.rows, w.k,
+                         s),
            "q8 GEMM");
     }
 

@@ -63,22 +63,22 @@ static int sm_count() {
 }
 
 // ---------------------------------------------------------------- launchers
-template <int BN, bool EXACT>
-static cudaError_t q8gemm_go(const CUtensorMap &a, const CUtensorMap &b, const CUtensorMap &sa,
-                             const CUtensorMap &sb, const Q8GemmParams &p, cudaStream_t s) {
-    const Q8Smem L = q8gemm_smem(BN, p.K);
+template <bool EXACT>
+static cudaError_t q8gemm_go(const CUtensorMap &w, const CUtensorMap &x, const CUtensorMap &sw,
+                             const CUtensorMap &sx, const Q8GemmParams &p, cudaStream_t s) {
+    const Q8Smem L = q8gemm_smem(p.K);
     const int grid = p.num_tiles < sm_count() ? p.num_tiles : sm_count();
-    q8gemm_kernel<BN, EXACT><<<grid, Q8Cfg<BN>::THREADS, L.total, s>>>(a, b, sa, sb, p);
+    q8gemm_kernel<EXACT><<<grid, Q8Cfg::THREADS, L.total, s>>>(w, x, sw, sx, p);
     return cudaGetLastError();
 }
-cudaError_t launch_q8gemm(const CUtensorMap &a, const CUtensorMap &b, const CUtensorMap &sa, const CUtensorMap &sb,
-                          int bn, bool exact, float *out, int ldo, int M, int N, int K, cudaStream_t s) {
-    if (M <= 0) return cudaSuccess;
-    if (K <= 0 || K % 128 || K > 2048 || N <= 0 || N % bn || bn != 64 || ldo < N) return cudaErrorInvalidValue;
-    if (q8gemm_smem(bn, K).total > 227 * 1024) return cudaErrorInvalidValue;
-    Q8GemmParams p{out, ldo, M, N, K, N / bn, 0};
-    p.num_tiles = ((M + 127) / 128) * p.tiles_n;
-    return exact ? q8gemm_go<64, true>(a, b, sa, sb, p, s) : q8gemm_go<64, false>(a, b, sa, sb, p, s);
+cudaError_t launch_q8gemm(const CUtensorMap &w, const CUtensorMap &x, const CUtensorMap &sw, const CUtensorMap &sx,
+                          bool exact, float *out, int ldo, int T, int R, int K, cudaStream_t s) {
+    if (T <= 0) return cudaSuccess;
+    if (K <= 0 || K % 128 || K > 2048 || R <= 0 || R % Q8Cfg::BM || ldo < R) return cudaErrorInvalidValue;
+    if (q8gemm_smem(K).total > 227 * 1024) return cudaErrorInvalidValue;
+    Q8GemmParams p{out, ldo, T, R, K, (T + Q8Cfg::BN - 1) / Q8Cfg::BN, 0};
+    p.num_tiles = (R / Q8Cfg::BM) * p.tiles_t;
+    return exact ? q8gemm_go<true>(w, x, sw, sx, p, s) : q8gemm_go<false>(w, x, sw, sx, p, s);
 }
 
 cudaError_t launch_ple(const CUtensorMap &hi, const CUtensorMap &lo, const CUtensorMap &w, float *ple,
@@ -176,9 +176,9 @@ cudaError_t launch_repack_q8(const void *blocks, int rows, int k, int8_t *codes,
 
 cudaError_t init_kernel_attributes() {
     cudaError_t e;
-    if ((e = cudaFuncSetAttribute(q8gemm_kernel<64, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024)))
+    if ((e = cudaFuncSetAttribute(q8gemm_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024)))
         return e;
-    if ((e = cudaFuncSetAttribute(q8gemm_kernel<64, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024)))
+    if ((e = cudaFuncSetAttribute(q8gemm_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024)))
         return e;
     if ((e = cudaFuncSetAttribute(ple_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(PleCfg::SMEM)))) return e;
     if ((e = cudaFuncSetAttribute(attention_kernel<256>, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -289,15 +289,14 @@ int eg2_launch_norm_quant(const EgNormQuant *p, void *s) {
 int eg2_launch_q8_mm(const EgQ8MM *p, void *s) {
     if (cudaError_t e = ensure_attributes()) return rc(e);
     if (!p->n) return 0;
-    if (p->k % 128 || p->k > 2048 || p->m % 64 || !p->m || p->xs_stride < p->n || p->xs_stride % 4)
+    if (p->k % 128 || p->k > 2048 || p->m % 128 || !p->m || p->xs_stride < p->n || p->xs_stride % 4)
         return rc(cudaErrorInvalidValue);
-    const int bn = 64;  // 8 TMEM accumulator buffers in flight
-    CUtensorMap a, b, sa, sb;
-    if (!q8_tmap(&a, p->xq, p->k, p->n, 128) || !q8_tmap(&b, p->wq, p->k, p->m, uint32_t(bn)) ||
-        !scale_tmap(&sa, p->xs, p->xs_stride, p->k / 32, 128) || !scale_tmap(&sb, p->ws, p->m, p->k / 32, uint32_t(bn)))
+    CUtensorMap w, x, sw, sx;  // weights on the MMA's M side (128 rows), tokens on N (64)
+    if (!q8_tmap(&w, p->wq, p->k, p->m, uint32_t(Q8Cfg::BM)) || !q8_tmap(&x, p->xq, p->k, p->n, uint32_t(Q8Cfg::BN)) ||
+        !scale_tmap(&sw, p->ws, p->m, p->k / 32, uint32_t(Q8Cfg::BM)) ||
+        !scale_tmap(&sx, p->xs, p->xs_stride, p->k / 32, uint32_t(Q8Cfg::BN)))
         return rc(cudaErrorInvalidValue);
-    return rc(launch_q8gemm(a, b, sa, sb, bn, p->exact != 0, p->out, int(p->m), int(p->n), int(p->m), int(p->k),
-                            S(s)));
+    return rc(launch_q8gemm(w, x, sw, sx, p->exact != 0, p->out, int(p->m), int(p->n), int(p->m), int(p->k), S(s)));
 }
 int eg2_launch_qkv_post(const EgQkvPost *p, void *s) {
     return rc(launch_qkv_post(p->q, p->k, p->v, p->qkv, p->q_norm, p->k_norm, p->rope_cos, p->rope_sin, p->pos,

@@ -17,9 +17,12 @@ bool bf16_tmap(CUtensorMap *map, const void *base, uint64_t k, uint64_t rows, ui
 bool scale_tmap(CUtensorMap *map, const float *base, uint64_t stride, uint64_t kb, uint32_t box_cols);
 
 // Kernel launches (all asynchronous on `s`).
+// out[T][ldo] = tokens x weight rows.  Maps: weight codes [R][K] with box
+// 128 rows, token codes [T][K] with box 64 rows, weight scales [K/32][R] box
+// 128, token scales [K/32][stride] box 64.  R must be a multiple of 128.
 // exact: the reference scalar tile's rounding order (bit-identical outputs).
-cudaError_t launch_q8gemm(const CUtensorMap &a, const CUtensorMap &b, const CUtensorMap &sa, const CUtensorMap &sb,
-                          int bn, bool exact, float *out, int ldo, int M, int N, int K, cudaStream_t s);
+cudaError_t launch_q8gemm(const CUtensorMap &w, const CUtensorMap &x, const CUtensorMap &sw, const CUtensorMap &sx,
+                          bool exact, float *out, int ldo, int T, int R, int K, cudaStream_t s);
 cudaError_t launch_ple(const CUtensorMap &hi, const CUtensorMap &lo, const CUtensorMap &w, float *ple,
                        const float *norm, int M, cudaStream_t s);
 cudaError_t launch_embed(float *x, void *x_hi, void *x_lo, const void *emb, const int *ids, int n, cudaStream_t s);

@@ -120,6 +120,7 @@ __global__ void __launch_bounds__(PleCfg::THREADS, 1)
                 uint32_t d[32];
                 tmem_ld32(taddr + uint32_t(c), d);
                 tmem_wait_ld();
+                reg_fence(d);
 #pragma unroll
                 for (int i = 0; i < 32; ++i) {
                     const float v = __fdiv_rn(__uint_as_float(d[i]), inv_sqrt);
@@ -139,6 +140,7 @@ __global__ void __launch_bounds__(PleCfg::THREADS, 1)
                 uint32_t d[32];
                 tmem_ld32(taddr + uint32_t(c), d);
                 tmem_wait_ld();
+                reg_fence(d);
                 if (!store) continue;
 #pragma unroll
                 for (int i = 0; i < 32; i += 4) {
