@@ -33,6 +33,14 @@ __device__ __forceinline__ uint64_t globaltimer_ns() {
     asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
     return t;
 }
+// CTA-wide and named barriers in their non-aligned form: arrivals are counted
+// per thread, so they stay correct when a warp reaches them diverged (after an
+// elect_one() role or a lane-0 branch).  __syncthreads() is the aligned form,
+// whose count is undefined for a diverged warp.
+__device__ __forceinline__ void cta_sync() { asm volatile("barrier.sync 0;" ::: "memory"); }
+__device__ __forceinline__ void named_sync(int id, int threads) {
+    asm volatile("barrier.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
+}
 __device__ __forceinline__ bool elect_one() {
     uint32_t pred = 0;
     asm volatile(

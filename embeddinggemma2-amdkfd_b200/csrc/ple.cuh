@@ -39,8 +39,8 @@ __global__ void __launch_bounds__(PleCfg::THREADS, 1)
     double *partial = reinterpret_cast<double *>(smem + C::STAGES * C::STAGE_BYTES);  // [2][128]
     uint64_t *full = reinterpret_cast<uint64_t *>(partial + 2 * C::BM);
     uint64_t *empty = full + C::STAGES;
-    uint64_t *accf = empty + C::STAGES;
-    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(accf + 1);
+    uint64_t *accf = empty + C::STAGES, *edone = accf + 1;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(edone + 1);
     volatile int *abort = reinterpret_cast<volatile int *>(tmem_slot + 1);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -51,7 +51,7 @@ __global__ void __launch_bounds__(PleCfg::THREADS, 1)
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < C::STAGES; ++s) bar_init(&full[s], 1), bar_init(&empty[s], 1);
-        bar_init(accf, 1);
+        bar_init(accf, 1), bar_init(edone, C::EPI_WARPS);
         *abort = g_error != 0;
         fence_bar_init();
     }
@@ -60,7 +60,7 @@ __global__ void __launch_bounds__(PleCfg::THREADS, 1)
         tmem_relinquish();
     }
     tc_fence_before();
-    __syncthreads();
+    cta_sync();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
     constexpr int KSTEPS = C::K / C::BK;
@@ -107,6 +107,11 @@ __global__ void __launch_bounds__(PleCfg::THREADS, 1)
             wait_bar(accf, 0, nullptr);
         }
         __syncwarp();
+        // TMEM is released only after every epilogue warp has finished reading it.
+        wait_bar(edone, 0, nullptr);
+        __syncwarp();
+        tc_fence_after();
+        tmem_dealloc(tmem, 512);
     } else {
         const int quad = warp & 3, half = (warp - 2) >> 2;
         const int row = quad * 32 + lane, colbase = half * 256;
@@ -129,7 +134,7 @@ __global__ void __launch_bounds__(PleCfg::THREADS, 1)
             }
         }
         partial[half * C::BM + row] = ss;
-        asm volatile("bar.sync 1, %0;" ::"n"(C::EPI_WARPS * 32) : "memory");
+        named_sync(1, C::EPI_WARPS * 32);
         const float scale = rms_scale(partial[row] + partial[C::BM + row], 512);
         const int m = m0 + row;
         const bool store = m < p.M;  // per lane; the TMEM loads stay warp-collective
@@ -153,12 +158,9 @@ __global__ void __launch_bounds__(PleCfg::THREADS, 1)
                 }
             }
         }
-    }
-    tc_fence_before();
-    __syncthreads();
-    if (warp == 1) {
-        tc_fence_after();
-        tmem_dealloc(tmem, 512);
+        __syncwarp();
+        tc_fence_before();
+        if (lane == 0) bar_arrive(edone);
     }
 }
 

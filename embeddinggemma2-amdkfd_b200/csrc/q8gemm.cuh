@@ -37,7 +37,9 @@
 //               per thread).
 // The stage ring, TMEM slots and panel buffers continue across tiles, so loads
 // and MMAs of the next tile overlap the epilogue of the current one.  Every
-// wait is a bounded mbarrier wait that sets the device error word and exits.
+// wait is a bounded mbarrier wait that sets the device error word and exits;
+// the MMA warp frees TMEM once the epilogue warps have all arrived on
+// epilogue_done (there is no CTA-wide barrier after the roles diverge).
 #pragma once
 #include "common.cuh"
 
@@ -93,8 +95,8 @@ __global__ void __launch_bounds__(Q8Cfg::THREADS, 1)
     const int Kb = L.kb, ksteps = p.K / C::BK, STAGES = L.stages, PBUFS = L.pbufs;
     uint64_t *bars = reinterpret_cast<uint64_t *>(smem + L.bars());
     uint64_t *full = bars, *empty = bars + 4, *accf = bars + 8, *acce = accf + C::NBUF;
-    uint64_t *pfull = acce + C::NBUF, *pempty = pfull + 2, *mdone = pempty + 2;
-    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(mdone + 1);
+    uint64_t *pfull = acce + C::NBUF, *pempty = pfull + 2, *mdone = pempty + 2, *edone = mdone + 1;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(edone + 1);
     volatile int *abort = reinterpret_cast<volatile int *>(tmem_slot + 1);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -107,7 +109,7 @@ __global__ void __launch_bounds__(Q8Cfg::THREADS, 1)
         for (int s = 0; s < STAGES; ++s) bar_init(&full[s], 1), bar_init(&empty[s], 1);
         for (int b = 0; b < C::NBUF; ++b) bar_init(&accf[b], 1), bar_init(&acce[b], C::EPI_WARPS);
         for (int b = 0; b < PBUFS; ++b) bar_init(&pfull[b], 1), bar_init(&pempty[b], C::EPI_WARPS);
-        bar_init(mdone, 1);
+        bar_init(mdone, 1), bar_init(edone, C::EPI_WARPS);
         *abort = g_error != 0;
         fence_bar_init();
     }
@@ -116,7 +118,7 @@ __global__ void __launch_bounds__(Q8Cfg::THREADS, 1)
         tmem_relinquish();
     }
     tc_fence_before();
-    __syncthreads();
+    cta_sync();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
 
@@ -191,6 +193,11 @@ __global__ void __launch_bounds__(Q8Cfg::THREADS, 1)
             wait_bar(mdone, 0, nullptr);
         }
         __syncwarp();
+        // TMEM is released only after every epilogue warp has finished reading it.
+        wait_bar(edone, 0, nullptr);
+        __syncwarp();
+        tc_fence_after();
+        tmem_dealloc(tmem, 512);
     } else {
         // ------------------------------------------------------------ epilogue
         const int quad = warp & 3, half = (warp - 2) >> 2;
@@ -208,12 +215,13 @@ __global__ void __launch_bounds__(Q8Cfg::THREADS, 1)
             tmem_ld32(tbase + uint32_t((b % C::NBUF) * C::HALF), r);
             return true;
         };
-        // Complete that load and hand the slot back to the MMA warp.
+        // Complete that load and hand the slot back to the MMA warp (the wait
+        // is warp-collective, so every lane's load has completed when lane 0
+        // arrives).
         auto finish = [&](uint32_t(&r)[C::HALF], int b) {
             tmem_wait_ld();
             reg_fence(r);
             tc_fence_before();
-            __syncwarp();
             if (lane == 0) bar_arrive(&acce[b % C::NBUF]);
         };
 
@@ -229,29 +237,27 @@ __global__ void __launch_bounds__(Q8Cfg::THREADS, 1)
 
             // Rescale and accumulate block j held in r.
             auto math = [&](const uint32_t(&r)[C::HALF], int j) {
-                {
-                    const float ws = sw[j * C::BM];
-                    const float2 w2 = make_float2(ws, ws), c2 = make_float2(-BIAS * ws, -BIAS * ws);
-                    const float4 *xs = sx + j * (C::BN / 4);
+                const float ws = sw[j * C::BM];
+                const float2 w2 = make_float2(ws, ws), c2 = make_float2(-BIAS * ws, -BIAS * ws);
+                const float4 *xs = sx + j * (C::BN / 4);
 #pragma unroll
-                    for (int c4 = 0; c4 < C::HALF / 4; ++c4) {
-                        const float4 x4 = xs[c4];
-                        const uint32_t *d = r + 4 * c4;
-                        const float2 xa = make_float2(__int_as_float(int(d[0]) + 0x4B400000),
-                                                      __int_as_float(int(d[1]) + 0x4B400000));
-                        const float2 xb = make_float2(__int_as_float(int(d[2]) + 0x4B400000),
-                                                      __int_as_float(int(d[3]) + 0x4B400000));
-                        const float2 ta = __ffma2_rn(xa, w2, c2), tb = __ffma2_rn(xb, w2, c2);
-                        float2 &aa = acc[2 * c4], &ab = acc[2 * c4 + 1];
-                        if (EXACT) {  // scalar _rn intrinsics are never contracted into an FMA
-                            aa.x = __fadd_rn(aa.x, __fmul_rn(ta.x, x4.x));
-                            aa.y = __fadd_rn(aa.y, __fmul_rn(ta.y, x4.y));
-                            ab.x = __fadd_rn(ab.x, __fmul_rn(tb.x, x4.z));
-                            ab.y = __fadd_rn(ab.y, __fmul_rn(tb.y, x4.w));
-                        } else {
-                            aa = __ffma2_rn(ta, make_float2(x4.x, x4.y), aa);
-                            ab = __ffma2_rn(tb, make_float2(x4.z, x4.w), ab);
-                        }
+                for (int c4 = 0; c4 < C::HALF / 4; ++c4) {
+                    const float4 x4 = xs[c4];
+                    const uint32_t *d = r + 4 * c4;
+                    const float2 xa = make_float2(__int_as_float(int(d[0]) + 0x4B400000),
+                                                  __int_as_float(int(d[1]) + 0x4B400000));
+                    const float2 xb = make_float2(__int_as_float(int(d[2]) + 0x4B400000),
+                                                  __int_as_float(int(d[3]) + 0x4B400000));
+                    const float2 ta = __ffma2_rn(xa, w2, c2), tb = __ffma2_rn(xb, w2, c2);
+                    float2 &aa = acc[2 * c4], &ab = acc[2 * c4 + 1];
+                    if (EXACT) {  // scalar _rn intrinsics are never contracted into an FMA
+                        aa.x = __fadd_rn(aa.x, __fmul_rn(ta.x, x4.x));
+                        aa.y = __fadd_rn(aa.y, __fmul_rn(ta.y, x4.y));
+                        ab.x = __fadd_rn(ab.x, __fmul_rn(tb.x, x4.z));
+                        ab.y = __fadd_rn(ab.y, __fmul_rn(tb.y, x4.w));
+                    } else {
+                        aa = __ffma2_rn(ta, make_float2(x4.x, x4.y), aa);
+                        ab = __ffma2_rn(tb, make_float2(x4.z, x4.w), ab);
                     }
                 }
             };
@@ -292,12 +298,9 @@ __global__ void __launch_bounds__(Q8Cfg::THREADS, 1)
                 if (2 * c + 1 < tmax) o[size_t(2 * c + 1) * p.ldo] = acc[c].y;
             }
         }
-    }
-    tc_fence_before();
-    __syncthreads();
-    if (warp == 1) {
-        tc_fence_after();
-        tmem_dealloc(tmem, 512);
+        __syncwarp();
+        tc_fence_before();
+        if (lane == 0) bar_arrive(edone);
     }
 }
 
