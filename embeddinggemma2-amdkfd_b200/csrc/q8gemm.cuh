@@ -28,13 +28,16 @@
 //               buffer, then int8 weight/token tiles of 128 B (one 128-byte
 //               swizzle row = four Q8_0 blocks) per stage of a 4-deep ring;
 //   warp 1      TMEM owner and MMA issuer: block j is two N=32 MMAs (token
-//               halves h = 0, 1) into TMEM columns h*256 + (j % 8)*32;
-//               commit -> acc_full[j % 8];
+//               halves h = 0, 1) into TMEM columns h*256 + (j % 8)*32.  The
+//               eight slots form two groups of four, one stage's blocks each:
+//               the warp waits once per stage for its group to be free and
+//               commits once per stage -> acc_full[group];
 //   warps 2..9  epilogue: warp w reads TMEM lanes 32*(w%4).. (its hardware
-//               quadrant) of token half h = (w-2)/4, one 32-column tcgen05.ld
-//               per block; the load of block j+1 is in flight while block j
-//               is rescaled (two register sets: ten warps leave 168 registers
-//               per thread).
+//               quadrant) of token half h = (w-2)/4.  Per group it waits once,
+//               fetches the four blocks as two 64-column tcgen05.ld, frees the
+//               group after the second, and rescales from registers.
+// Barrier round trips cost on the order of 100 ns each, so they are paid per
+// stage of four blocks, not per block.
 // The stage ring, TMEM slots and panel buffers continue across tiles, so loads
 // and MMAs of the next tile overlap the epilogue of the current one.  Every
 // wait is a bounded mbarrier wait that sets the device error word and exits;
@@ -58,6 +61,7 @@ struct Q8Cfg {
     static constexpr int BK = 128;   // bytes of K per stage: four Q8_0 blocks
     static constexpr int HALF = 32;  // token columns of one epilogue warp (one N=32 MMA)
     static constexpr int NBUF = 8;   // block slots: 2 halves x 8 slots x 32 columns = 512
+    static constexpr int GROUP = 4;  // slots per handshake group = Q8_0 blocks per stage
     static constexpr int EPI_WARPS = 8, THREADS = (2 + EPI_WARPS) * 32;
     static constexpr int A_BYTES = BM * BK, B_BYTES = BN * BK, STAGE_BYTES = A_BYTES + B_BYTES;
 };
@@ -94,8 +98,8 @@ __global__ void __launch_bounds__(Q8Cfg::THREADS, 1)
     const Q8Smem L = q8gemm_smem(p.K);
     const int Kb = L.kb, ksteps = p.K / C::BK, STAGES = L.stages, PBUFS = L.pbufs;
     uint64_t *bars = reinterpret_cast<uint64_t *>(smem + L.bars());
-    uint64_t *full = bars, *empty = bars + 4, *accf = bars + 8, *acce = accf + C::NBUF;
-    uint64_t *pfull = acce + C::NBUF, *pempty = pfull + 2, *mdone = pempty + 2, *edone = mdone + 1;
+    uint64_t *full = bars, *empty = bars + 4, *accf = bars + 8, *acce = accf + 2;  // accf/acce: per slot group
+    uint64_t *pfull = acce + 2, *pempty = pfull + 2, *mdone = pempty + 2, *edone = mdone + 1;
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(edone + 1);
     volatile int *abort = reinterpret_cast<volatile int *>(tmem_slot + 1);
 
@@ -107,7 +111,7 @@ __global__ void __launch_bounds__(Q8Cfg::THREADS, 1)
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < STAGES; ++s) bar_init(&full[s], 1), bar_init(&empty[s], 1);
-        for (int b = 0; b < C::NBUF; ++b) bar_init(&accf[b], 1), bar_init(&acce[b], C::EPI_WARPS);
+        for (int b = 0; b < 2; ++b) bar_init(&accf[b], 1), bar_init(&acce[b], C::EPI_WARPS);
         for (int b = 0; b < PBUFS; ++b) bar_init(&pfull[b], 1), bar_init(&pempty[b], C::EPI_WARPS);
         bar_init(mdone, 1), bar_init(edone, C::EPI_WARPS);
         *abort = g_error != 0;
@@ -159,7 +163,7 @@ __global__ void __launch_bounds__(Q8Cfg::THREADS, 1)
         // ------------------------------------------------------------ MMA issuer
         if (elect_one() && !*abort) {
             constexpr uint32_t idesc = idesc_i8(C::BM, C::HALF);
-            int g = 0, blk = 0;
+            int g = 0;
             bool ok = true;
             for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x) {
                 for (int ks = 0; ks < ksteps && ok; ++ks, ++g) {
@@ -168,23 +172,23 @@ __global__ void __launch_bounds__(Q8Cfg::THREADS, 1)
                         ok = false;
                         break;
                     }
+                    const int grp = g & 1;  // this stage's blocks use TMEM slots 4*grp .. 4*grp+3
+                    if (!wait_bar(&acce[grp], ((g >> 1) & 1) ^ 1, abort)) {
+                        ok = false;
+                        break;
+                    }
                     tc_fence_after();
                     const uint32_t w_addr = smem_u32(w_tile(s)), x_addr = smem_u32(x_tile(s));
 #pragma unroll
-                    for (int kk = 0; kk < C::BK / 32; ++kk, ++blk) {
-                        const int slot = blk % C::NBUF;
-                        if (!wait_bar(&acce[slot], ((blk / C::NBUF) & 1) ^ 1, abort)) {
-                            ok = false;
-                            break;
-                        }
-                        tc_fence_after();
+                    for (int kk = 0; kk < C::GROUP; ++kk) {
+                        const int slot = grp * C::GROUP + kk;
                         const uint64_t wd = desc_sw128(w_addr + kk * 32);
 #pragma unroll
                         for (int h = 0; h < 2; ++h)  // token half h: rows 32h.. of the token tile, 4 KB in
                             mma_i8(tmem + uint32_t(h * C::NBUF * C::HALF + slot * C::HALF), wd,
                                    desc_sw128(x_addr + h * C::HALF * 128 + kk * 32), idesc, 0u);
-                        tc_commit(&accf[slot]);
                     }
+                    tc_commit(&accf[grp]);
                     tc_commit(&empty[s]);
                 }
             }
@@ -207,24 +211,12 @@ __global__ void __launch_bounds__(Q8Cfg::THREADS, 1)
         int blk = 0, it = 0;
         bool ok = true;
 
-        // Wait for block b and start its 32-column TMEM load (asynchronous).
-        auto issue = [&](uint32_t(&r)[C::HALF], int b) -> bool {
-            const bool ready = wait_bar(&accf[b % C::NBUF], (b / C::NBUF) & 1, abort);
-            if (!__all_sync(0xffffffffu, ready)) return false;  // tcgen05.ld is warp-collective
-            tc_fence_after();
-            tmem_ld32(tbase + uint32_t((b % C::NBUF) * C::HALF), r);
-            return true;
-        };
-        // Complete that load and hand the slot back to the MMA warp (the wait
-        // is warp-collective, so every lane's load has completed when lane 0
-        // arrives).
-        auto finish = [&](uint32_t(&r)[C::HALF], int b) {
+        // Blocks b, b+1 of a completed group into r (64 columns).
+        auto load2 = [&](uint32_t(&r)[2 * C::HALF], int b) {
+            tmem_ld64(tbase + uint32_t((b % C::NBUF) * C::HALF), r);
             tmem_wait_ld();
             reg_fence(r);
-            tc_fence_before();
-            if (lane == 0) bar_arrive(&acce[b % C::NBUF]);
         };
-
         for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x, ++it) {
             const int r0 = (tile / p.tiles_t) * C::BM, t0 = (tile % p.tiles_t) * C::BN;
             const int pb = it % PBUFS;
@@ -262,29 +254,25 @@ __global__ void __launch_bounds__(Q8Cfg::THREADS, 1)
                 }
             };
 
-            // Two register sets: the load of block j+1 is in flight while block
-            // j is rescaled.  Kb is a multiple of 4.
-            uint32_t ra[C::HALF], rb[C::HALF];
-            if (!issue(ra, blk)) {
-                ok = false;
-                break;
-            }
-            finish(ra, blk);
-            for (int j = 0; j < Kb; j += 2) {
-                if (!issue(rb, blk + 1)) {
+            // Per group of four blocks (one stage): one wait, two 64-column loads,
+            // the group handed back to the MMA warp before the last two blocks
+            // are rescaled from registers.  Kb is a multiple of 4.
+            uint32_t r2[2 * C::HALF];
+            for (int j = 0; j < Kb; j += C::GROUP, blk += C::GROUP) {
+                const int grp = (blk / C::GROUP) & 1, use = blk / (2 * C::GROUP);
+                if (!__all_sync(0xffffffffu, wait_bar(&accf[grp], use & 1, abort))) {  // tcgen05.ld is warp-collective
                     ok = false;
                     break;
                 }
-                math(ra, j);
-                finish(rb, blk + 1);
-                const bool more = j + 2 < Kb;
-                if (more && !issue(ra, blk + 2)) {
-                    ok = false;
-                    break;
-                }
-                math(rb, j + 1);
-                if (more) finish(ra, blk + 2);
-                blk += 2;
+                tc_fence_after();
+                load2(r2, blk);
+                math(*reinterpret_cast<uint32_t(*)[C::HALF]>(r2), j);
+                math(*reinterpret_cast<uint32_t(*)[C::HALF]>(r2 + C::HALF), j + 1);
+                load2(r2, blk + 2);
+                tc_fence_before();
+                if (lane == 0) bar_arrive(&acce[grp]);
+                math(*reinterpret_cast<uint32_t(*)[C::HALF]>(r2), j + 2);
+                math(*reinterpret_cast<uint32_t(*)[C::HALF]>(r2 + C::HALF), j + 3);
             }
             __syncwarp();
             if (lane == 0) bar_arrive(&pempty[pb]);
