@@ -242,24 +242,6 @@ __device__ __forceinline__ uint16_t ref_fp32_to_fp16(float f) {
 }
 __device__ __forceinline__ float fp16_bits_to_f32(uint16_t h) { return __half2float(__ushort_as_half(h)); }
 
-// Q8_0 block quantization of 32 values held one per lane of a full warp,
-// following gemma2_fast_x86.c:211-234: d = amax/127 (IEEE), scale stored as the
-// reference's fp16 rounding of d, id = 1/d, q = trunc(x*id +- 0.5).
-// Returns the code; *scale_out receives the widened fp16 scale (lane-uniform).
-__device__ __forceinline__ int8_t quant_lane32(float x, float *scale_out) {
-    float amax = fabsf(x);
-#pragma unroll
-    for (int o = 16; o; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
-    const float d = __fdiv_rn(amax, 127.0f);
-    const float id = d != 0.0f ? __fdiv_rn(1.0f, d) : 0.0f;
-    *scale_out = fp16_bits_to_f32(ref_fp32_to_fp16(d));
-    const float v = __fmul_rn(x, id);
-    const float t = __fadd_rn(v, copysignf(0.5f, v));
-    int q = __float2int_rz(t);
-    q = q < -128 ? -128 : (q > 127 ? 127 : q);
-    return int8_t(q);
-}
-
 // exp(x) by Cody-Waite reduction and a degree-6 polynomial: the reference's own
 // x86 GELU helper (gemma2_fast_x86.c:291-306), evaluated with the same fused
 // and unfused operations so that results match it bit for bit.

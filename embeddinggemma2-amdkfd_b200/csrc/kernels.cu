@@ -151,8 +151,10 @@ cudaError_t launch_post_add(float *x, const float *h, const float *w, const floa
 cudaError_t launch_gate_quant(int8_t *q, float *qs, int qs_stride, const float *x, const float *other, int rows,
                               int width, int other_stride, int other_offset, cudaStream_t s) {
     if (rows <= 0) return cudaSuccess;
-    if (width <= 0 || width % 32 || qs_stride < rows || other_offset + width > other_stride) return cudaErrorInvalidValue;
-    const int groups = (width / 32 + 7) / 8, warps = rows * groups;
+    if (width <= 0 || width % 128 || qs_stride < rows || other_stride % 4 || other_offset % 4 ||
+        other_offset + width > other_stride)
+        return cudaErrorInvalidValue;
+    const int wpr = (width / 128 + 3) / 4, warps = rows * wpr;
     gate_quant_kernel<<<(warps + 7) / 8, 256, 0, s>>>(q, qs, qs_stride, x, other, rows, width, other_stride,
                                                       other_offset);
     return cudaGetLastError();

@@ -1,9 +1,9 @@
 // Bandwidth-bound row kernels of the executor.  Each follows the reference's
 // CPU graph operation by operation (vendor/embeddinggemma.c/src/gemma2_fast.c)
 // with IEEE-rounded intrinsics and no contraction, so that on identical inputs
-// the Q8 codes and scales they emit are the reference's.  One warp owns one
-// row; every 32-element Q8_0 block is one coalesced 128-byte access with one
-// lane per element, and block amax / row sums are warp shuffles.
+// the Q8 codes and scales they emit are the reference's.  Row sums of squares
+// are accumulated in double like the reference's and reduced with warp
+// shuffles.
 #pragma once
 #include "common.cuh"
 
@@ -33,50 +33,98 @@ __global__ void embed_kernel(float *__restrict__ x, __nv_bfloat16 *__restrict__ 
     }
 }
 
+// Layout of the quantizing kernels: a warp reads a row 512 bytes at a time,
+// each lane 4 consecutive floats (one float4), so one warp-wide access covers
+// four Q8_0 blocks and each block lives in an aligned group of 8 lanes.  The
+// block's amax is 3 shuffles inside the group, and each lane stores its four
+// codes as one 32-bit word.
+
+// Q8_0 code of x with id = 1/d: trunc(x*id +- 0.5) (gemma2_fast_x86.c:225-230).
+__device__ __forceinline__ uint32_t q8_code(float x, float id) {
+    const float v = __fmul_rn(x, id);
+    int q = __float2int_rz(__fadd_rn(v, copysignf(0.5f, v)));
+    q = q < -128 ? -128 : (q > 127 ? 127 : q);
+    return uint32_t(q) & 0xFFu;
+}
+// One 32-element block held as v in each lane of an aligned 8-lane group
+// (gemma2_fast_x86.c:211-234): d = amax/127 (IEEE), the scale stored is the
+// reference's fp16 rounding of d, id = 1/d.  Returns the lane's four codes;
+// *scale_out receives the widened fp16 scale (uniform over the group).
+__device__ __forceinline__ uint32_t quant_oct(const float4 v, float *scale_out) {
+    float amax = fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
+#pragma unroll
+    for (int o = 1; o < 8; o <<= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+    const float d = __fdiv_rn(amax, 127.0f);
+    const float id = d != 0.0f ? __fdiv_rn(1.0f, d) : 0.0f;
+    *scale_out = fp16_bits_to_f32(ref_fp32_to_fp16(d));
+    return q8_code(v.x, id) | q8_code(v.y, id) << 8 | q8_code(v.z, id) << 16 | q8_code(v.w, id) << 24;
+}
+__device__ __forceinline__ double sumsq4(double ss, const float4 v) {
+    ss = __dadd_rn(ss, __dmul_rn(double(v.x), double(v.x)));
+    ss = __dadd_rn(ss, __dmul_rn(double(v.y), double(v.y)));
+    ss = __dadd_rn(ss, __dmul_rn(double(v.z), double(v.z)));
+    return __dadd_rn(ss, __dmul_rn(double(v.w), double(v.w)));
+}
+// v * (sc * w), elementwise, in the reference's order (rms_row: r[z] *= scale * w[z]).
+__device__ __forceinline__ float4 scale_w4(const float4 v, float sc, const float4 w) {
+    return make_float4(__fmul_rn(v.x, __fmul_rn(sc, w.x)), __fmul_rn(v.y, __fmul_rn(sc, w.y)),
+                       __fmul_rn(v.z, __fmul_rn(sc, w.z)), __fmul_rn(v.w, __fmul_rn(sc, w.w)));
+}
+// Quantize the warp's IT float4 chunks of row t (chunk i*32 + lane covers
+// blocks 4i .. 4i+3) into codes and block-major scales.
+template <int IT>
+__device__ __forceinline__ void quant_row(const float4 (&v)[IT], int8_t *__restrict__ q, float *__restrict__ qs,
+                                          int qs_stride, int t, int width, int lane) {
+    uint32_t *qr = reinterpret_cast<uint32_t *>(q + size_t(t) * width);
+#pragma unroll
+    for (int i = 0; i < IT; ++i) {
+        float sc;
+        qr[i * 32 + lane] = quant_oct(v[i], &sc);
+        if ((lane & 7) == 0) qs[size_t(4 * i + (lane >> 3)) * qs_stride + t] = sc;
+    }
+}
+
 // ROW_NORM_QUANT / ROW_QUANT (gemma2_fast.c:685-691,728-730): optional RMS norm
-// with weight w, then Q8_0 quantization of the row, 32 lanes per block.
+// with weight w, then Q8_0 quantization of the row.  Warp per row.
 template <int WIDTH>
 __global__ void norm_quant_kernel(int8_t *__restrict__ q, float *__restrict__ qs, int qs_stride,
                                   float *__restrict__ y, const float *__restrict__ x, const float *__restrict__ w,
                                   int rows) {
     const int t = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5), lane = threadIdx.x & 31;
-    if (t >= rows) return;
-    constexpr int NB = WIDTH / 32;
-    const float *xr = x + size_t(t) * WIDTH;
-    float v[NB];
+    if (t >= rows) return;  // warp-uniform
+    constexpr int IT = WIDTH / 128;
+    const float4 *xr = reinterpret_cast<const float4 *>(x + size_t(t) * WIDTH);
+    float4 v[IT];
 #pragma unroll
-    for (int b = 0; b < NB; ++b) v[b] = xr[b * 32 + lane];
+    for (int i = 0; i < IT; ++i) v[i] = xr[i * 32 + lane];
     if (w) {
         double ss = 0.0;
 #pragma unroll
-        for (int b = 0; b < NB; ++b) ss = __dadd_rn(ss, __dmul_rn(double(v[b]), double(v[b])));
+        for (int i = 0; i < IT; ++i) ss = sumsq4(ss, v[i]);
         const float sc = rms_scale(warp_sum_d(ss), WIDTH);
+        const float4 *wr = reinterpret_cast<const float4 *>(w);
 #pragma unroll
-        for (int b = 0; b < NB; ++b) v[b] = __fmul_rn(v[b], __fmul_rn(sc, w[b * 32 + lane]));
+        for (int i = 0; i < IT; ++i) v[i] = scale_w4(v[i], sc, wr[i * 32 + lane]);
         if (y) {
+            float4 *yr = reinterpret_cast<float4 *>(y + size_t(t) * WIDTH);
 #pragma unroll
-            for (int b = 0; b < NB; ++b) y[size_t(t) * WIDTH + b * 32 + lane] = v[b];
+            for (int i = 0; i < IT; ++i) yr[i * 32 + lane] = v[i];
         }
     }
-#pragma unroll
-    for (int b = 0; b < NB; ++b) {
-        float s;
-        const int8_t c = quant_lane32(v[b], &s);
-        q[size_t(t) * WIDTH + b * 32 + lane] = c;
-        if (lane == 0) qs[size_t(b) * qs_stride + t] = s;
-    }
+    quant_row<IT>(v, q, qs, qs_stride, t, WIDTH, lane);
 }
 
 // ROW_QKV_POST (gemma2_fast.c:692-706): warp per (token, head row).  Rows
 // 0..3 are q heads (weighted RMS + RoPE), then kv k heads (weighted RMS +
 // RoPE), then kv v heads (plain RMS).  RoPE: r[z] = a*c - b*s,
-// r[z+d/2] = a*s + b*c with host tables (gemma2_fast.c:672-679).
+// r[z+d/2] = a*s + b*c with host tables (gemma2_fast.c:672-679).  Each lane
+// handles 4 consecutive z of each half.
 template <int D>
 __global__ void qkv_post_kernel(__half *__restrict__ qo, __half *__restrict__ ko, __half *__restrict__ vo,
                                 const float *__restrict__ qkv, const float *__restrict__ qn,
                                 const float *__restrict__ kn, const float *__restrict__ rc,
                                 const float *__restrict__ rs, const unsigned *__restrict__ pos, int n) {
-    constexpr int KV = 512 / D, HR = 4 + 2 * KV, PER = D / 64;  // PER pairs per lane
+    constexpr int KV = 512 / D, HR = 4 + 2 * KV, PER = D / 256;  // float4 chunks per lane per half
     const int gw = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5), lane = threadIdx.x & 31;
     if (gw >= n * HR) return;
     const int t = gw / HR, hr = gw % HR;
@@ -94,93 +142,113 @@ __global__ void qkv_post_kernel(__half *__restrict__ qo, __half *__restrict__ ko
         src = qkv + size_t(t) * (4 * D + 1024) + 4 * D + 512 + h * D, w = nullptr;
         dst = vo + (size_t(t) * KV + h) * D, rope = false;
     }
-    float a[PER], b[PER];
+    const float4 *s4 = reinterpret_cast<const float4 *>(src);
+    float4 a[PER], b[PER];
     double ss = 0.0;
 #pragma unroll
     for (int i = 0; i < PER; ++i) {
-        a[i] = src[i * 32 + lane];
-        b[i] = src[D / 2 + i * 32 + lane];
-        ss = __dadd_rn(ss, __dmul_rn(double(a[i]), double(a[i])));
+        a[i] = s4[i * 32 + lane];
+        b[i] = s4[D / 8 + i * 32 + lane];
+        ss = sumsq4(ss, a[i]);
     }
 #pragma unroll
-    for (int i = 0; i < PER; ++i) ss = __dadd_rn(ss, __dmul_rn(double(b[i]), double(b[i])));
+    for (int i = 0; i < PER; ++i) ss = sumsq4(ss, b[i]);
     const float sc = rms_scale(warp_sum_d(ss), D);
     const size_t p = size_t(pos[t]) * (D / 2);
+    const float4 one = make_float4(1.0f, 1.0f, 1.0f, 1.0f);
 #pragma unroll
     for (int i = 0; i < PER; ++i) {
-        const int z = i * 32 + lane;
-        const float ya = __fmul_rn(a[i], __fmul_rn(sc, w ? w[z] : 1.0f));
-        const float yb = __fmul_rn(b[i], __fmul_rn(sc, w ? w[z + D / 2] : 1.0f));
-        float oa = ya, ob = yb;
+        const int z = 4 * (i * 32 + lane);
+        const float4 ya = scale_w4(a[i], sc, w ? *reinterpret_cast<const float4 *>(w + z) : one);
+        const float4 yb = scale_w4(b[i], sc, w ? *reinterpret_cast<const float4 *>(w + z + D / 2) : one);
+        float4 oa = ya, ob = yb;
         if (rope) {
-            const float c = rc[p + z], s = rs[p + z];
-            oa = __fsub_rn(__fmul_rn(ya, c), __fmul_rn(yb, s));
-            ob = __fadd_rn(__fmul_rn(ya, s), __fmul_rn(yb, c));
+            const float4 c = *reinterpret_cast<const float4 *>(rc + p + z);
+            const float4 s = *reinterpret_cast<const float4 *>(rs + p + z);
+            oa = make_float4(__fsub_rn(__fmul_rn(ya.x, c.x), __fmul_rn(yb.x, s.x)),
+                             __fsub_rn(__fmul_rn(ya.y, c.y), __fmul_rn(yb.y, s.y)),
+                             __fsub_rn(__fmul_rn(ya.z, c.z), __fmul_rn(yb.z, s.z)),
+                             __fsub_rn(__fmul_rn(ya.w, c.w), __fmul_rn(yb.w, s.w)));
+            ob = make_float4(__fadd_rn(__fmul_rn(ya.x, s.x), __fmul_rn(yb.x, c.x)),
+                             __fadd_rn(__fmul_rn(ya.y, s.y), __fmul_rn(yb.y, c.y)),
+                             __fadd_rn(__fmul_rn(ya.z, s.z), __fmul_rn(yb.z, c.z)),
+                             __fadd_rn(__fmul_rn(ya.w, s.w), __fmul_rn(yb.w, c.w)));
         }
-        dst[z] = __float2half_rn(oa);
-        dst[z + D / 2] = __float2half_rn(ob);
+        __half2 h0 = __floats2half2_rn(oa.x, oa.y), h1 = __floats2half2_rn(oa.z, oa.w);
+        __half2 h2 = __floats2half2_rn(ob.x, ob.y), h3 = __floats2half2_rn(ob.z, ob.w);
+        *reinterpret_cast<uint2 *>(dst + z) = make_uint2(*reinterpret_cast<uint32_t *>(&h0), *reinterpret_cast<uint32_t *>(&h1));
+        *reinterpret_cast<uint2 *>(dst + z + D / 2) =
+            make_uint2(*reinterpret_cast<uint32_t *>(&h2), *reinterpret_cast<uint32_t *>(&h3));
     }
 }
 
 // ROW_POST_ADD (gemma2_fast.c:707-713): x = (x + rms(h) * w) * scale, then the
 // next GEMM operand from the updated x: RMS-norm with next_w and quantize
 // (ROW_NORM_QUANT) or, next_w == nullptr, plain quantization (ROW_QUANT).
+// Warp per 512-wide row.
 __global__ void post_add_kernel(float *__restrict__ x, const float *__restrict__ h, const float *__restrict__ w,
                                 const float *__restrict__ scale, int8_t *__restrict__ q, float *__restrict__ qs,
                                 int qs_stride, const float *__restrict__ next_w, int rows) {
     const int t = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5), lane = threadIdx.x & 31;
     if (t >= rows) return;
-    float hv[16], xv[16];
+    constexpr int IT = 512 / 128;
+    float4 *xr = reinterpret_cast<float4 *>(x + size_t(t) * 512);
+    const float4 *hr = reinterpret_cast<const float4 *>(h + size_t(t) * 512);
+    const float4 *wr = reinterpret_cast<const float4 *>(w);
+    float4 hv[IT], xv[IT];
     double ss = 0.0;
 #pragma unroll
-    for (int b = 0; b < 16; ++b) {
-        hv[b] = h[size_t(t) * 512 + b * 32 + lane];
-        xv[b] = x[size_t(t) * 512 + b * 32 + lane];
-        ss = __dadd_rn(ss, __dmul_rn(double(hv[b]), double(hv[b])));
+    for (int i = 0; i < IT; ++i) {
+        hv[i] = hr[i * 32 + lane];
+        xv[i] = xr[i * 32 + lane];
+        ss = sumsq4(ss, hv[i]);
     }
     const float sc = rms_scale(warp_sum_d(ss), 512);
     const float ls = scale ? *scale : 1.0f;
     double ss2 = 0.0;
 #pragma unroll
-    for (int b = 0; b < 16; ++b) {
-        const float hn = __fmul_rn(hv[b], __fmul_rn(sc, w[b * 32 + lane]));
-        xv[b] = __fmul_rn(__fadd_rn(xv[b], hn), ls);
-        x[size_t(t) * 512 + b * 32 + lane] = xv[b];
-        ss2 = __dadd_rn(ss2, __dmul_rn(double(xv[b]), double(xv[b])));
+    for (int i = 0; i < IT; ++i) {
+        const float4 hn = scale_w4(hv[i], sc, wr[i * 32 + lane]);
+        xv[i] = make_float4(__fmul_rn(__fadd_rn(xv[i].x, hn.x), ls), __fmul_rn(__fadd_rn(xv[i].y, hn.y), ls),
+                            __fmul_rn(__fadd_rn(xv[i].z, hn.z), ls), __fmul_rn(__fadd_rn(xv[i].w, hn.w), ls));
+        xr[i * 32 + lane] = xv[i];
+        ss2 = sumsq4(ss2, xv[i]);
     }
     if (next_w) {
         const float sc2 = rms_scale(warp_sum_d(ss2), 512);
+        const float4 *nw = reinterpret_cast<const float4 *>(next_w);
 #pragma unroll
-        for (int b = 0; b < 16; ++b) xv[b] = __fmul_rn(xv[b], __fmul_rn(sc2, next_w[b * 32 + lane]));
+        for (int i = 0; i < IT; ++i) xv[i] = scale_w4(xv[i], sc2, nw[i * 32 + lane]);
     }
-#pragma unroll
-    for (int b = 0; b < 16; ++b) {
-        float s;
-        const int8_t c = quant_lane32(xv[b], &s);
-        q[size_t(t) * 512 + b * 32 + lane] = c;
-        if (lane == 0) qs[size_t(b) * qs_stride + t] = s;
-    }
+    quant_row<IT>(xv, q, qs, qs_stride, t, 512, lane);
 }
 
 // ROW_GELU_QUANT / ROW_PLE_GATE_QUANT (gemma2_fast.c:714-727):
-// g = gelu_tanh(x) * other, then Q8_0.  Warp per (row, 8 blocks).
+// g = gelu_tanh(x) * other, then Q8_0.  Warp per (row, up to 16 blocks);
+// width, other_stride and other_offset are multiples of 128, 4 and 4.
 __global__ void gate_quant_kernel(int8_t *__restrict__ q, float *__restrict__ qs, int qs_stride,
                                   const float *__restrict__ x, const float *__restrict__ other, int rows, int width,
                                   int other_stride, int other_offset) {
-    const int nb = width / 32, groups = (nb + 7) / 8;
+    constexpr int PER = 4;  // float4 steps (4 blocks each) per warp
+    const int steps = width / 128, wpr = (steps + PER - 1) / PER;
     const int gw = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5), lane = threadIdx.x & 31;
-    if (gw >= rows * groups) return;
-    const int t = gw / groups, b0 = (gw % groups) * 8;
+    if (gw >= rows * wpr) return;  // warp-uniform
+    const int t = gw / wpr, i0 = (gw % wpr) * PER;
+    const float4 *xr = reinterpret_cast<const float4 *>(x + size_t(t) * width);
+    const float4 *orow = reinterpret_cast<const float4 *>(other + size_t(t) * other_stride + other_offset);
+    uint32_t *qr = reinterpret_cast<uint32_t *>(q + size_t(t) * width);
+    float4 xv[PER], ov[PER];
 #pragma unroll
-    for (int bb = 0; bb < 8; ++bb) {
-        const int b = b0 + bb;
-        if (b >= nb) break;
-        const float g = __fmul_rn(ref_gelu(x[size_t(t) * width + b * 32 + lane]),
-                                  other[size_t(t) * other_stride + other_offset + b * 32 + lane]);
-        float s;
-        const int8_t c = quant_lane32(g, &s);
-        q[size_t(t) * width + b * 32 + lane] = c;
-        if (lane == 0) qs[size_t(b) * qs_stride + t] = s;
+    for (int i = 0; i < PER; ++i)
+        if (i0 + i < steps) xv[i] = xr[(i0 + i) * 32 + lane], ov[i] = orow[(i0 + i) * 32 + lane];
+#pragma unroll
+    for (int i = 0; i < PER; ++i) {
+        if (i0 + i >= steps) break;  // warp-uniform
+        const float4 g = make_float4(__fmul_rn(ref_gelu(xv[i].x), ov[i].x), __fmul_rn(ref_gelu(xv[i].y), ov[i].y),
+                                     __fmul_rn(ref_gelu(xv[i].z), ov[i].z), __fmul_rn(ref_gelu(xv[i].w), ov[i].w));
+        float sc;
+        qr[(i0 + i) * 32 + lane] = quant_oct(g, &sc);
+        if ((lane & 7) == 0) qs[size_t(4 * (i0 + i) + (lane >> 3)) * qs_stride + t] = sc;
     }
 }
 

@@ -45,14 +45,14 @@ typedef struct { float *x; uint16_t *x_hi, *x_lo; const void *token_embd; const 
 typedef struct { float *ple; const uint16_t *x_hi, *x_lo, *weight; const float *norm; unsigned n; } EgPleProj;
 /* Row RMS-norm then Q8_0 quantization (ROW_NORM_QUANT, gemma2_fast.c:685-691);
  * weight NULL: quantization only (ROW_QUANT, :728-730).  y (optional) gets the
- * normalised row. */
+ * normalised row.  width is 256, 512, 1024 or 2048. */
 typedef struct {
     int8_t *q; float *scale; unsigned scale_stride; float *y;
     const float *x, *weight; unsigned rows, width;
 } EgNormQuant;
 /* out[t][r] = sum_b (int32 dot of block b) * xs[b][t] * ws[b][r]
  * (gemma2_fast.c:242-253): tcgen05 kind::i8, int32 block accumulators in TMEM.
- * k % 128 == 0, k <= 2048, m % 64 == 0, xs_stride >= n and a multiple of 4.
+ * k % 128 == 0, k <= 2048, m % 128 == 0, xs_stride >= n and a multiple of 4.
  * exact != 0 rounds like the reference's scalar tile (((float)dot * dw) * dx,
  * then +=), giving bit-identical outputs; exact == 0 fuses the last multiply
  * and add (one rounding fewer). */
@@ -82,7 +82,8 @@ typedef struct {
     int8_t *q; float *qscale; unsigned scale_stride; const float *next_weight; unsigned rows;
 } EgPostAdd;
 /* g = gelu_tanh(x[t][z]) * other[t * other_stride + other_offset + z], then Q8
- * (ROW_GELU_QUANT / ROW_PLE_GATE_QUANT, gemma2_fast.c:714-727). */
+ * (ROW_GELU_QUANT / ROW_PLE_GATE_QUANT, gemma2_fast.c:714-727).  width % 128
+ * == 0; other_stride and other_offset multiples of 4. */
 typedef struct {
     int8_t *q; float *scale; unsigned scale_stride;
     const float *x, *other; unsigned rows, width, other_stride, other_offset;
