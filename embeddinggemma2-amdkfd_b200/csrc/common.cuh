@@ -242,6 +242,13 @@ __device__ __forceinline__ uint16_t ref_fp32_to_fp16(float f) {
 }
 __device__ __forceinline__ float fp16_bits_to_f32(uint16_t h) { return __half2float(__ushort_as_half(h)); }
 
+// Q8_0 code of x with id = 1/d: trunc(x*id +- 0.5) (gemma2_fast_x86.c:225-230).
+__device__ __forceinline__ uint32_t q8_code(float x, float id) {
+    const float v = __fmul_rn(x, id);
+    int q = __float2int_rz(__fadd_rn(v, copysignf(0.5f, v)));
+    q = q < -128 ? -128 : (q > 127 ? 127 : q);
+    return uint32_t(q) & 0xFFu;
+}
 // exp(x) by Cody-Waite reduction and a degree-6 polynomial: the reference's own
 // x86 GELU helper (gemma2_fast_x86.c:291-306), evaluated with the same fused
 // and unfused operations so that results match it bit for bit.

@@ -163,7 +163,8 @@ cudaError_t launch_gate_quant(int8_t *q, float *qs, int qs_stride, const float *
 cudaError_t launch_pool_l2(float *out, const float *y, const unsigned *offsets, int batch, int width, cudaStream_t s) {
     if (batch <= 0) return cudaSuccess;
     if (width <= 0 || width % 8 || width > 8192) return cudaErrorInvalidValue;
-    pool_l2_kernel<<<batch, 256, width * sizeof(float), s>>>(out, y, offsets, width);
+    pool_mean_kernel<<<dim3((width + 127) / 128, batch), 128, 0, s>>>(out, y, offsets, width);
+    pool_l2_kernel<<<batch, 32, 0, s>>>(out, width);
     return cudaGetLastError();
 }
 

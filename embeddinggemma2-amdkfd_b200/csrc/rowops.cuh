@@ -39,13 +39,6 @@ __global__ void embed_kernel(float *__restrict__ x, __nv_bfloat16 *__restrict__ 
 // block's amax is 3 shuffles inside the group, and each lane stores its four
 // codes as one 32-bit word.
 
-// Q8_0 code of x with id = 1/d: trunc(x*id +- 0.5) (gemma2_fast_x86.c:225-230).
-__device__ __forceinline__ uint32_t q8_code(float x, float id) {
-    const float v = __fmul_rn(x, id);
-    int q = __float2int_rz(__fadd_rn(v, copysignf(0.5f, v)));
-    q = q < -128 ? -128 : (q > 127 ? 127 : q);
-    return uint32_t(q) & 0xFFu;
-}
 // One 32-element block held as v in each lane of an aligned 8-lane group
 // (gemma2_fast_x86.c:211-234): d = amax/127 (IEEE), the scale stored is the
 // reference's fp16 rounding of d, id = 1/d.  Returns the lane's four codes;
@@ -252,38 +245,45 @@ __global__ void gate_quant_kernel(int8_t *__restrict__ q, float *__restrict__ qs
     }
 }
 
-// Mean pool then L2 (gemma2_fast.c:1000-1008): o[z] += y[t][z] / len in token
-// order, then the SSE2 sum of squares of kernels.c:82-93 (two 4-lane
-// accumulators over 8-element chunks) and x *= 1/sqrt(ss) (kernels.c:393-396).
-__global__ void pool_l2_kernel(float *__restrict__ out, const float *__restrict__ y,
-                               const unsigned *__restrict__ offsets, int width) {
-    extern __shared__ float pooled[];  // [width]
-    __shared__ float lanes[8];
-    __shared__ float inv;
-    const int s = blockIdx.x;
+// Mean pool then L2 (gemma2_fast.c:1000-1008), in two launches.
+// pool_mean_kernel: o[z] = sum over the sequence's tokens, in token order, of
+// y[t][z] / len -- one thread per (sequence, column), loads batched 8 tokens
+// ahead of the in-order adds; the result goes straight into out.
+__global__ void pool_mean_kernel(float *__restrict__ out, const float *__restrict__ y,
+                                 const unsigned *__restrict__ offsets, int width) {
+    const int s = blockIdx.y, z = blockIdx.x * blockDim.x + threadIdx.x;
+    if (z >= width) return;
     const unsigned lo = offsets[s], hi = offsets[s + 1];
     const float len = float(hi - lo);
-    for (int z = threadIdx.x; z < width; z += blockDim.x) {
-        float o = 0.0f;
-        for (unsigned t = lo; t < hi; ++t) o = __fadd_rn(o, __fdiv_rn(y[size_t(t) * width + z], len));
-        pooled[z] = o;
+    const float *col = y + z;
+    float o = 0.0f;
+    unsigned t = lo;
+    for (; t + 8 <= hi; t += 8) {
+        float v[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) v[i] = col[size_t(t + i) * width];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) o = __fadd_rn(o, __fdiv_rn(v[i], len));
     }
-    __syncthreads();
-    if (threadIdx.x < 8) {
-        const int j = threadIdx.x;  // lanes 0..3 -> sum0, 4..7 -> sum1
-        float acc = 0.0f;
-        for (int i = 0; i + 7 < width; i += 8) acc = __fadd_rn(acc, __fmul_rn(pooled[i + j], pooled[i + j]));
-        lanes[j] = acc;
-    }
-    __syncthreads();
-    if (threadIdx.x == 0) {
-        float v[4];
-        for (int j = 0; j < 4; ++j) v[j] = __fadd_rn(lanes[j], lanes[4 + j]);
-        const float ss = __fadd_rn(__fadd_rn(v[0], v[2]), __fadd_rn(v[1], v[3]));
-        inv = ss != 0.0f ? __fdiv_rn(1.0f, __fsqrt_rn(ss)) : 1.0f;
-    }
-    __syncthreads();
-    for (int z = threadIdx.x; z < width; z += blockDim.x) out[size_t(s) * width + z] = __fmul_rn(pooled[z], inv);
+    for (; t < hi; ++t) o = __fadd_rn(o, __fdiv_rn(col[size_t(t) * width], len));
+    out[size_t(s) * width + z] = o;
+}
+// pool_l2_kernel: one warp per sequence; the SSE2 sum of squares of
+// kernels.c:82-93 (lanes 0..7 are its two 4-lane accumulators over 8-element
+// chunks, each summed in chunk order), then x *= 1/sqrt(ss) (kernels.c:393-396).
+__global__ void pool_l2_kernel(float *__restrict__ out, int width) {
+    const int s = blockIdx.x, lane = threadIdx.x;
+    float *o = out + size_t(s) * width;
+    float acc = 0.0f;
+    if (lane < 8)
+        for (int i = 0; i + 7 < width; i += 8) acc = __fadd_rn(acc, __fmul_rn(o[i + lane], o[i + lane]));
+    float v[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+        v[j] = __fadd_rn(__shfl_sync(0xffffffffu, acc, j), __shfl_sync(0xffffffffu, acc, 4 + j));
+    const float ss = __fadd_rn(__fadd_rn(v[0], v[2]), __fadd_rn(v[1], v[3]));
+    const float inv = ss != 0.0f ? __fdiv_rn(1.0f, __fsqrt_rn(ss)) : 1.0f;
+    for (int z = lane; z < width; z += 32) o[z] = __fmul_rn(o[z], inv);
 }
 
 // GGUF Q8_0 blocks [rows][k/32] (34 B each) -> int8 codes [rows][k] and fp32
