@@ -101,13 +101,17 @@ cudaError_t launch_norm_quant(int8_t *q, float *qs, int qs_stride, float *y, con
                               int width, cudaStream_t s) {
     if (rows <= 0) return cudaSuccess;
     if (qs_stride < rows) return cudaErrorInvalidValue;
-    const dim3 grid((rows + 7) / 8), block(256);
-    switch (width) {
-        case 256: norm_quant_kernel<256><<<grid, block, 0, s>>>(q, qs, qs_stride, y, x, w, rows); break;
-        case 512: norm_quant_kernel<512><<<grid, block, 0, s>>>(q, qs, qs_stride, y, x, w, rows); break;
-        case 1024: norm_quant_kernel<1024><<<grid, block, 0, s>>>(q, qs, qs_stride, y, x, w, rows); break;
-        case 2048: norm_quant_kernel<2048><<<grid, block, 0, s>>>(q, qs, qs_stride, y, x, w, rows); break;
-        default: return cudaErrorInvalidValue;
+    if (width != 256 && width != 512 && width != 1024 && width != 2048) return cudaErrorInvalidValue;
+    if (!w) {  // ROW_QUANT: no row reduction, warp per (row, four blocks)
+        const int warps = rows * (width / 128);
+        quant_rows_kernel<<<(warps + 7) / 8, 256, 0, s>>>(q, qs, qs_stride, x, rows, width);
+        return cudaGetLastError();
+    }
+    switch (width) {  // ROW_NORM_QUANT: CTA per row, one float4 per thread
+        case 256: norm_quant_kernel<256><<<rows, 64, 0, s>>>(q, qs, qs_stride, y, x, w); break;
+        case 512: norm_quant_kernel<512><<<rows, 128, 0, s>>>(q, qs, qs_stride, y, x, w); break;
+        case 1024: norm_quant_kernel<1024><<<rows, 256, 0, s>>>(q, qs, qs_stride, y, x, w); break;
+        default: norm_quant_kernel<2048><<<rows, 512, 0, s>>>(q, qs, qs_stride, y, x, w); break;
     }
     return cudaGetLastError();
 }
@@ -144,7 +148,7 @@ cudaError_t launch_post_add(float *x, const float *h, const float *w, const floa
                             int qs_stride, const float *next_w, int rows, cudaStream_t s) {
     if (rows <= 0) return cudaSuccess;
     if (qs_stride < rows) return cudaErrorInvalidValue;
-    post_add_kernel<<<(rows + 7) / 8, 256, 0, s>>>(x, h, w, scale, q, qs, qs_stride, next_w, rows);
+    post_add_kernel<<<rows, 128, 0, s>>>(x, h, w, scale, q, qs, qs_stride, next_w);
     return cudaGetLastError();
 }
 
@@ -154,7 +158,7 @@ cudaError_t launch_gate_quant(int8_t *q, float *qs, int qs_stride, const float *
     if (width <= 0 || width % 128 || qs_stride < rows || other_stride % 4 || other_offset % 4 ||
         other_offset + width > other_stride)
         return cudaErrorInvalidValue;
-    const int wpr = (width / 128 + 3) / 4, warps = rows * wpr;
+    const int warps = rows * (width / 128);
     gate_quant_kernel<<<(warps + 7) / 8, 256, 0, s>>>(q, qs, qs_stride, x, other, rows, width, other_stride,
                                                       other_offset);
     return cudaGetLastError();

@@ -63,48 +63,50 @@ __device__ __forceinline__ float4 scale_w4(const float4 v, float sc, const float
     return make_float4(__fmul_rn(v.x, __fmul_rn(sc, w.x)), __fmul_rn(v.y, __fmul_rn(sc, w.y)),
                        __fmul_rn(v.z, __fmul_rn(sc, w.z)), __fmul_rn(v.w, __fmul_rn(sc, w.w)));
 }
-// Quantize the warp's IT float4 chunks of row t (chunk i*32 + lane covers
-// blocks 4i .. 4i+3) into codes and block-major scales.
-template <int IT>
-__device__ __forceinline__ void quant_row(const float4 (&v)[IT], int8_t *__restrict__ q, float *__restrict__ qs,
-                                          int qs_stride, int t, int width, int lane) {
-    uint32_t *qr = reinterpret_cast<uint32_t *>(q + size_t(t) * width);
+// Sum of a per-thread double over the CTA: warp shuffles, then the per-warp
+// partials added in warp order by every thread.  red holds WARPS doubles.
+template <int WARPS>
+__device__ __forceinline__ double cta_sum_d(double v, double *red) {
+    v = warp_sum_d(v);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
+    __syncthreads();
+    double s = red[0];
 #pragma unroll
-    for (int i = 0; i < IT; ++i) {
-        float sc;
-        qr[i * 32 + lane] = quant_oct(v[i], &sc);
-        if ((lane & 7) == 0) qs[size_t(4 * i + (lane >> 3)) * qs_stride + t] = sc;
-    }
+    for (int i = 1; i < WARPS; ++i) s = __dadd_rn(s, red[i]);
+    return s;
 }
 
-// ROW_NORM_QUANT / ROW_QUANT (gemma2_fast.c:685-691,728-730): optional RMS norm
-// with weight w, then Q8_0 quantization of the row.  Warp per row.
+// ROW_NORM_QUANT (gemma2_fast.c:685-691): RMS norm with weight w, then Q8_0.
+// CTA per row, one float4 per thread (WIDTH / 4 threads).
 template <int WIDTH>
-__global__ void norm_quant_kernel(int8_t *__restrict__ q, float *__restrict__ qs, int qs_stride,
-                                  float *__restrict__ y, const float *__restrict__ x, const float *__restrict__ w,
-                                  int rows) {
-    const int t = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5), lane = threadIdx.x & 31;
-    if (t >= rows) return;  // warp-uniform
-    constexpr int IT = WIDTH / 128;
-    const float4 *xr = reinterpret_cast<const float4 *>(x + size_t(t) * WIDTH);
-    float4 v[IT];
-#pragma unroll
-    for (int i = 0; i < IT; ++i) v[i] = xr[i * 32 + lane];
-    if (w) {
-        double ss = 0.0;
-#pragma unroll
-        for (int i = 0; i < IT; ++i) ss = sumsq4(ss, v[i]);
-        const float sc = rms_scale(warp_sum_d(ss), WIDTH);
-        const float4 *wr = reinterpret_cast<const float4 *>(w);
-#pragma unroll
-        for (int i = 0; i < IT; ++i) v[i] = scale_w4(v[i], sc, wr[i * 32 + lane]);
-        if (y) {
-            float4 *yr = reinterpret_cast<float4 *>(y + size_t(t) * WIDTH);
-#pragma unroll
-            for (int i = 0; i < IT; ++i) yr[i * 32 + lane] = v[i];
-        }
-    }
-    quant_row<IT>(v, q, qs, qs_stride, t, WIDTH, lane);
+__global__ void __launch_bounds__(WIDTH / 4) norm_quant_kernel(int8_t *__restrict__ q, float *__restrict__ qs,
+                                                               int qs_stride, float *__restrict__ y,
+                                                               const float *__restrict__ x,
+                                                               const float *__restrict__ w) {
+    constexpr int WARPS = WIDTH / 128;
+    __shared__ double red[WARPS];
+    const int t = blockIdx.x, i = threadIdx.x, lane = i & 31;
+    float4 v = reinterpret_cast<const float4 *>(x + size_t(t) * WIDTH)[i];
+    const float sc = rms_scale(cta_sum_d<WARPS>(sumsq4(0.0, v), red), WIDTH);
+    v = scale_w4(v, sc, reinterpret_cast<const float4 *>(w)[i]);
+    if (y) reinterpret_cast<float4 *>(y + size_t(t) * WIDTH)[i] = v;
+    float s;
+    reinterpret_cast<uint32_t *>(q + size_t(t) * WIDTH)[i] = quant_oct(v, &s);
+    if ((lane & 7) == 0) qs[size_t(i >> 3) * qs_stride + t] = s;
+}
+
+// ROW_QUANT (gemma2_fast.c:728-730): Q8_0 of rows of width `width` (a multiple
+// of 128).  Warp per (row, four blocks).
+__global__ void quant_rows_kernel(int8_t *__restrict__ q, float *__restrict__ qs, int qs_stride,
+                                  const float *__restrict__ x, int rows, int width) {
+    const int steps = width / 128;
+    const int gw = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+    if (gw >= rows * steps) return;  // warp-uniform
+    const int t = gw / steps, st = gw % steps;
+    const size_t c = size_t(t) * (width / 4) + st * 32 + lane;
+    float s;
+    reinterpret_cast<uint32_t *>(q)[c] = quant_oct(reinterpret_cast<const float4 *>(x)[c], &s);
+    if ((lane & 7) == 0) qs[size_t(4 * st + (lane >> 3)) * qs_stride + t] = s;
 }
 
 // ROW_QKV_POST (gemma2_fast.c:692-706): warp per (token, head row).  Rows
@@ -178,51 +180,38 @@ __global__ void qkv_post_kernel(__half *__restrict__ qo, __half *__restrict__ ko
 // ROW_POST_ADD (gemma2_fast.c:707-713): x = (x + rms(h) * w) * scale, then the
 // next GEMM operand from the updated x: RMS-norm with next_w and quantize
 // (ROW_NORM_QUANT) or, next_w == nullptr, plain quantization (ROW_QUANT).
-// Warp per 512-wide row.
-__global__ void post_add_kernel(float *__restrict__ x, const float *__restrict__ h, const float *__restrict__ w,
-                                const float *__restrict__ scale, int8_t *__restrict__ q, float *__restrict__ qs,
-                                int qs_stride, const float *__restrict__ next_w, int rows) {
-    const int t = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5), lane = threadIdx.x & 31;
-    if (t >= rows) return;
-    constexpr int IT = 512 / 128;
-    float4 *xr = reinterpret_cast<float4 *>(x + size_t(t) * 512);
-    const float4 *hr = reinterpret_cast<const float4 *>(h + size_t(t) * 512);
-    const float4 *wr = reinterpret_cast<const float4 *>(w);
-    float4 hv[IT], xv[IT];
-    double ss = 0.0;
-#pragma unroll
-    for (int i = 0; i < IT; ++i) {
-        hv[i] = hr[i * 32 + lane];
-        xv[i] = xr[i * 32 + lane];
-        ss = sumsq4(ss, hv[i]);
-    }
-    const float sc = rms_scale(warp_sum_d(ss), 512);
+// CTA of 128 threads per 512-wide row, one float4 per thread.
+__global__ void __launch_bounds__(128) post_add_kernel(float *__restrict__ x, const float *__restrict__ h,
+                                                       const float *__restrict__ w, const float *__restrict__ scale,
+                                                       int8_t *__restrict__ q, float *__restrict__ qs, int qs_stride,
+                                                       const float *__restrict__ next_w) {
+    __shared__ double red[2][4];
+    const int t = blockIdx.x, i = threadIdx.x, lane = i & 31;
+    float4 *xp = reinterpret_cast<float4 *>(x + size_t(t) * 512) + i;
+    const float4 hv = reinterpret_cast<const float4 *>(h + size_t(t) * 512)[i];
+    float4 xv = *xp;
+    const float sc = rms_scale(cta_sum_d<4>(sumsq4(0.0, hv), red[0]), 512);
     const float ls = scale ? *scale : 1.0f;
-    double ss2 = 0.0;
-#pragma unroll
-    for (int i = 0; i < IT; ++i) {
-        const float4 hn = scale_w4(hv[i], sc, wr[i * 32 + lane]);
-        xv[i] = make_float4(__fmul_rn(__fadd_rn(xv[i].x, hn.x), ls), __fmul_rn(__fadd_rn(xv[i].y, hn.y), ls),
-                            __fmul_rn(__fadd_rn(xv[i].z, hn.z), ls), __fmul_rn(__fadd_rn(xv[i].w, hn.w), ls));
-        xr[i * 32 + lane] = xv[i];
-        ss2 = sumsq4(ss2, xv[i]);
-    }
+    const float4 hn = scale_w4(hv, sc, reinterpret_cast<const float4 *>(w)[i]);
+    xv = make_float4(__fmul_rn(__fadd_rn(xv.x, hn.x), ls), __fmul_rn(__fadd_rn(xv.y, hn.y), ls),
+                     __fmul_rn(__fadd_rn(xv.z, hn.z), ls), __fmul_rn(__fadd_rn(xv.w, hn.w), ls));
+    *xp = xv;
     if (next_w) {
-        const float sc2 = rms_scale(warp_sum_d(ss2), 512);
-        const float4 *nw = reinterpret_cast<const float4 *>(next_w);
-#pragma unroll
-        for (int i = 0; i < IT; ++i) xv[i] = scale_w4(xv[i], sc2, nw[i * 32 + lane]);
+        const float sc2 = rms_scale(cta_sum_d<4>(sumsq4(0.0, xv), red[1]), 512);
+        xv = scale_w4(xv, sc2, reinterpret_cast<const float4 *>(next_w)[i]);
     }
-    quant_row<IT>(xv, q, qs, qs_stride, t, 512, lane);
+    float s;
+    reinterpret_cast<uint32_t *>(q + size_t(t) * 512)[i] = quant_oct(xv, &s);
+    if ((lane & 7) == 0) qs[size_t(i >> 3) * qs_stride + t] = s;
 }
 
 // ROW_GELU_QUANT / ROW_PLE_GATE_QUANT (gemma2_fast.c:714-727):
-// g = gelu_tanh(x) * other, then Q8_0.  Warp per (row, up to 16 blocks);
-// width, other_stride and other_offset are multiples of 128, 4 and 4.
+// g = gelu_tanh(x) * other, then Q8_0.  Warp per (row, four blocks); width,
+// other_stride and other_offset are multiples of 128, 4 and 4.
 __global__ void gate_quant_kernel(int8_t *__restrict__ q, float *__restrict__ qs, int qs_stride,
                                   const float *__restrict__ x, const float *__restrict__ other, int rows, int width,
                                   int other_stride, int other_offset) {
-    constexpr int PER = 4;  // float4 steps (4 blocks each) per warp
+    constexpr int PER = 1;  // float4 steps (4 blocks each) per warp
     const int steps = width / 128, wpr = (steps + PER - 1) / PER;
     const int gw = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5), lane = threadIdx.x & 31;
     if (gw >= rows * wpr) return;  // warp-uniform
