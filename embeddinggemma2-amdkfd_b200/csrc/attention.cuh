@@ -78,6 +78,8 @@ __global__ void __launch_bounds__(AttnCfg<D>::THREADS) attention_kernel(const At
     uint8_t *qs = smem, *ks = smem + C::Q_BYTES, *vs = ks + C::K_BYTES;
     int *qlo = reinterpret_cast<int *>(vs + C::V_BYTES), *qhi = qlo + C::BQ;
 
+    pdl_wait();
+    pdl_trigger();
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int t0 = blockIdx.x * C::BQ, head = blockIdx.y, dv0 = blockIdx.z * C::DV;
     const int kh = head / (4 / KV);

@@ -41,6 +41,13 @@ __device__ __forceinline__ void cta_sync() { asm volatile("barrier.sync 0;" ::: 
 __device__ __forceinline__ void named_sync(int id, int threads) {
     asm volatile("barrier.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
 }
+// Programmatic dependent launch: every kernel of the wave is launched so that
+// it may start while its predecessor in the stream is still running.
+// pdl_wait() blocks until that predecessor has completed and its memory is
+// visible; nothing that reads or overwrites its inputs/outputs may come
+// before it.  pdl_trigger() lets the successor be scheduled.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 __device__ __forceinline__ bool elect_one() {
     uint32_t pred = 0;
     asm volatile(

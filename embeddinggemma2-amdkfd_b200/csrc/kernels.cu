@@ -1,5 +1,6 @@
 // All device code of the library, its launchers, and the exported operator
 // ABI (include/eg2_ops.h).  Built for sm_100a only.
+#include <cstdlib>
 #include <mutex>
 
 #include "../../include/eg2_ops.h"
@@ -63,13 +64,32 @@ static int sm_count() {
 }
 
 // ---------------------------------------------------------------- launchers
+// Wave kernels are launched with programmatic stream serialization: a kernel
+// may be scheduled while its predecessor still runs; it executes its prologue
+// and then blocks in pdl_wait() until the predecessor's results are visible
+// (every wave kernel calls pdl_wait() before touching global data).
+// EG2_B200_PDL=0 launches them in plain stream order instead.
+template <typename... KArgs, typename... Args>
+static cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s,
+                              Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid, cfg.blockDim = block, cfg.dynamicSmemBytes = smem, cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    static const bool enabled = [] {
+        const char *e = std::getenv("EG2_B200_PDL");
+        return !(e && e[0] == '0');
+    }();
+    cfg.attrs = attr, cfg.numAttrs = enabled ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
+}
 template <bool EXACT>
 static cudaError_t q8gemm_go(const CUtensorMap &w, const CUtensorMap &x, const CUtensorMap &sw,
                              const CUtensorMap &sx, const Q8GemmParams &p, cudaStream_t s) {
     const Q8Smem L = q8gemm_smem(p.K);
     const int grid = p.num_tiles < sm_count() ? p.num_tiles : sm_count();
-    q8gemm_kernel<EXACT><<<grid, Q8Cfg::THREADS, L.total, s>>>(w, x, sw, sx, p);
-    return cudaGetLastError();
+    return launch_pdl(q8gemm_kernel<EXACT>, dim3(grid), dim3(Q8Cfg::THREADS), L.total, s, w, x, sw, sx, p);
 }
 cudaError_t launch_q8gemm(const CUtensorMap &w, const CUtensorMap &x, const CUtensorMap &sw, const CUtensorMap &sx,
                           bool exact, float *out, int ldo, int T, int R, int K, cudaStream_t s) {
@@ -85,16 +105,14 @@ cudaError_t launch_ple(const CUtensorMap &hi, const CUtensorMap &lo, const CUten
                        const float *norm, int M, cudaStream_t s) {
     if (M <= 0) return cudaSuccess;
     const PleParams p{ple, norm, M};
-    ple_kernel<<<dim3(24, (M + 127) / 128), PleCfg::THREADS, PleCfg::SMEM, s>>>(hi, lo, w, p);
-    return cudaGetLastError();
+    return launch_pdl(ple_kernel, dim3(24, (M + 127) / 128), dim3(PleCfg::THREADS), PleCfg::SMEM, s, hi, lo, w, p);
 }
 
 cudaError_t launch_embed(float *x, void *x_hi, void *x_lo, const void *emb, const int *ids, int n, cudaStream_t s) {
     if (n <= 0) return cudaSuccess;
     if ((x_hi == nullptr) != (x_lo == nullptr)) return cudaErrorInvalidValue;
-    embed_kernel<<<(n + 7) / 8, 256, 0, s>>>(x, static_cast<__nv_bfloat16 *>(x_hi), static_cast<__nv_bfloat16 *>(x_lo),
-                                             static_cast<const uint8_t *>(emb), ids, n);
-    return cudaGetLastError();
+    return launch_pdl(embed_kernel, dim3((n + 7) / 8), dim3(256), 0, s, x, static_cast<__nv_bfloat16 *>(x_hi),
+                      static_cast<__nv_bfloat16 *>(x_lo), static_cast<const uint8_t *>(emb), ids, n);
 }
 
 cudaError_t launch_norm_quant(int8_t *q, float *qs, int qs_stride, float *y, const float *x, const float *w, int rows,
@@ -104,16 +122,14 @@ cudaError_t launch_norm_quant(int8_t *q, float *qs, int qs_stride, float *y, con
     if (width != 256 && width != 512 && width != 1024 && width != 2048) return cudaErrorInvalidValue;
     if (!w) {  // ROW_QUANT: no row reduction, warp per (row, four blocks)
         const int warps = rows * (width / 128);
-        quant_rows_kernel<<<(warps + 7) / 8, 256, 0, s>>>(q, qs, qs_stride, x, rows, width);
-        return cudaGetLastError();
+        return launch_pdl(quant_rows_kernel, dim3((warps + 7) / 8), dim3(256), 0, s, q, qs, qs_stride, x, rows, width);
     }
     switch (width) {  // ROW_NORM_QUANT: CTA per row, one float4 per thread
-        case 256: norm_quant_kernel<256><<<rows, 64, 0, s>>>(q, qs, qs_stride, y, x, w); break;
-        case 512: norm_quant_kernel<512><<<rows, 128, 0, s>>>(q, qs, qs_stride, y, x, w); break;
-        case 1024: norm_quant_kernel<1024><<<rows, 256, 0, s>>>(q, qs, qs_stride, y, x, w); break;
-        default: norm_quant_kernel<2048><<<rows, 512, 0, s>>>(q, qs, qs_stride, y, x, w); break;
+        case 256: return launch_pdl(norm_quant_kernel<256>, dim3(rows), dim3(64), 0, s, q, qs, qs_stride, y, x, w);
+        case 512: return launch_pdl(norm_quant_kernel<512>, dim3(rows), dim3(128), 0, s, q, qs, qs_stride, y, x, w);
+        case 1024: return launch_pdl(norm_quant_kernel<1024>, dim3(rows), dim3(256), 0, s, q, qs, qs_stride, y, x, w);
+        default: return launch_pdl(norm_quant_kernel<2048>, dim3(rows), dim3(512), 0, s, q, qs, qs_stride, y, x, w);
     }
-    return cudaGetLastError();
 }
 
 cudaError_t launch_qkv_post(void *q, void *k, void *v, const float *qkv, const float *qn, const float *kn,
@@ -123,16 +139,14 @@ cudaError_t launch_qkv_post(void *q, void *k, void *v, const float *qkv, const f
     const int rows_per_tok = 4 + 2 * (512 / d), warps = n * rows_per_tok;
     const dim3 grid((warps + 7) / 8), block(256);
     auto *qh = static_cast<__half *>(q), *kh = static_cast<__half *>(k), *vh = static_cast<__half *>(v);
-    if (d == 256) qkv_post_kernel<256><<<grid, block, 0, s>>>(qh, kh, vh, qkv, qn, kn, rc, rs, pos, n);
-    else qkv_post_kernel<512><<<grid, block, 0, s>>>(qh, kh, vh, qkv, qn, kn, rc, rs, pos, n);
-    return cudaGetLastError();
+    if (d == 256) return launch_pdl(qkv_post_kernel<256>, grid, block, 0, s, qh, kh, vh, qkv, qn, kn, rc, rs, pos, n);
+    return launch_pdl(qkv_post_kernel<512>, grid, block, 0, s, qh, kh, vh, qkv, qn, kn, rc, rs, pos, n);
 }
 
 template <int D>
 static cudaError_t attention_go(const AttnParams &p, cudaStream_t s) {
     const dim3 grid((p.n + AttnCfg<D>::BQ - 1) / AttnCfg<D>::BQ, 4, D / AttnCfg<D>::DV);
-    attention_kernel<D><<<grid, AttnCfg<D>::THREADS, AttnCfg<D>::SMEM, s>>>(p);
-    return cudaGetLastError();
+    return launch_pdl(attention_kernel<D>, grid, dim3(AttnCfg<D>::THREADS), AttnCfg<D>::SMEM, s, p);
 }
 cudaError_t launch_attention(float *out, const void *q, const void *k, const void *v, const unsigned *bounds, int n,
                              int d, int window, cudaStream_t s) {
@@ -148,8 +162,7 @@ cudaError_t launch_post_add(float *x, const float *h, const float *w, const floa
                             int qs_stride, const float *next_w, int rows, cudaStream_t s) {
     if (rows <= 0) return cudaSuccess;
     if (qs_stride < rows) return cudaErrorInvalidValue;
-    post_add_kernel<<<rows, 128, 0, s>>>(x, h, w, scale, q, qs, qs_stride, next_w);
-    return cudaGetLastError();
+    return launch_pdl(post_add_kernel, dim3(rows), dim3(128), 0, s, x, h, w, scale, q, qs, qs_stride, next_w);
 }
 
 cudaError_t launch_gate_quant(int8_t *q, float *qs, int qs_stride, const float *x, const float *other, int rows,
@@ -159,17 +172,17 @@ cudaError_t launch_gate_quant(int8_t *q, float *qs, int qs_stride, const float *
         other_offset + width > other_stride)
         return cudaErrorInvalidValue;
     const int warps = rows * (width / 128);
-    gate_quant_kernel<<<(warps + 7) / 8, 256, 0, s>>>(q, qs, qs_stride, x, other, rows, width, other_stride,
-                                                      other_offset);
-    return cudaGetLastError();
+    return launch_pdl(gate_quant_kernel, dim3((warps + 7) / 8), dim3(256), 0, s, q, qs, qs_stride, x, other, rows, width,
+                      other_stride, other_offset);
 }
 
 cudaError_t launch_pool_l2(float *out, const float *y, const unsigned *offsets, int batch, int width, cudaStream_t s) {
     if (batch <= 0) return cudaSuccess;
     if (width <= 0 || width % 8 || width > 8192) return cudaErrorInvalidValue;
-    pool_mean_kernel<<<dim3((width + 127) / 128, batch), 128, 0, s>>>(out, y, offsets, width);
-    pool_l2_kernel<<<batch, 32, 0, s>>>(out, width);
-    return cudaGetLastError();
+    if (cudaError_t e = launch_pdl(pool_mean_kernel, dim3((width + 127) / 128, batch), dim3(128), 0, s, out, y, offsets,
+                                   width))
+        return e;
+    return launch_pdl(pool_l2_kernel, dim3(batch), dim3(32), 0, s, out, width);
 }
 
 cudaError_t launch_repack_q8(const void *blocks, int rows, int k, int8_t *codes, float *scales, int scale_stride,

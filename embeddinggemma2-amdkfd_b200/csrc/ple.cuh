@@ -52,13 +52,15 @@ __global__ void __launch_bounds__(PleCfg::THREADS, 1)
     if (threadIdx.x == 0) {
         for (int s = 0; s < C::STAGES; ++s) bar_init(&full[s], 1), bar_init(&empty[s], 1);
         bar_init(accf, 1), bar_init(edone, C::EPI_WARPS);
-        *abort = g_error != 0;
         fence_bar_init();
     }
     if (warp == 1) {
         tmem_alloc(tmem_slot, 512);
         tmem_relinquish();
     }
+    pdl_wait();  // the prologue above overlaps the previous kernel's tail
+    pdl_trigger();
+    if (threadIdx.x == 0) *abort = g_error != 0;
     tc_fence_before();
     cta_sync();
     tc_fence_after();

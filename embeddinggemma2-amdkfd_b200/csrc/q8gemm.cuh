@@ -114,13 +114,15 @@ __global__ void __launch_bounds__(Q8Cfg::THREADS, 1)
         for (int b = 0; b < 2; ++b) bar_init(&accf[b], 1), bar_init(&acce[b], C::EPI_WARPS);
         for (int b = 0; b < PBUFS; ++b) bar_init(&pfull[b], 1), bar_init(&pempty[b], C::EPI_WARPS);
         bar_init(mdone, 1), bar_init(edone, C::EPI_WARPS);
-        *abort = g_error != 0;
         fence_bar_init();
     }
     if (warp == 1) {
         tmem_alloc(tmem_slot, 512);
         tmem_relinquish();
     }
+    pdl_wait();  // the prologue above overlaps the previous kernel's tail
+    pdl_trigger();
+    if (threadIdx.x == 0) *abort = g_error != 0;
     tc_fence_before();
     cta_sync();
     tc_fence_after();

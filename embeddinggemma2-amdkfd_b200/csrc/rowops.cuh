@@ -14,6 +14,8 @@ namespace eg2 {
 __global__ void embed_kernel(float *__restrict__ x, __nv_bfloat16 *__restrict__ x_hi,
                              __nv_bfloat16 *__restrict__ x_lo, const uint8_t *__restrict__ emb,
                              const int *__restrict__ ids, int n) {
+    pdl_wait();
+    pdl_trigger();
     const int t = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5), lane = threadIdx.x & 31;
     if (t >= n) return;
     const uint8_t *row = emb + size_t(ids[t]) * 16 * 34;
@@ -83,6 +85,8 @@ __global__ void __launch_bounds__(WIDTH / 4) norm_quant_kernel(int8_t *__restric
                                                                int qs_stride, float *__restrict__ y,
                                                                const float *__restrict__ x,
                                                                const float *__restrict__ w) {
+    pdl_wait();
+    pdl_trigger();
     constexpr int WARPS = WIDTH / 128;
     __shared__ double red[WARPS];
     const int t = blockIdx.x, i = threadIdx.x, lane = i & 31;
@@ -99,6 +103,8 @@ __global__ void __launch_bounds__(WIDTH / 4) norm_quant_kernel(int8_t *__restric
 // of 128).  Warp per (row, four blocks).
 __global__ void quant_rows_kernel(int8_t *__restrict__ q, float *__restrict__ qs, int qs_stride,
                                   const float *__restrict__ x, int rows, int width) {
+    pdl_wait();
+    pdl_trigger();
     const int steps = width / 128;
     const int gw = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5), lane = threadIdx.x & 31;
     if (gw >= rows * steps) return;  // warp-uniform
@@ -119,6 +125,8 @@ __global__ void qkv_post_kernel(__half *__restrict__ qo, __half *__restrict__ ko
                                 const float *__restrict__ qkv, const float *__restrict__ qn,
                                 const float *__restrict__ kn, const float *__restrict__ rc,
                                 const float *__restrict__ rs, const unsigned *__restrict__ pos, int n) {
+    pdl_wait();
+    pdl_trigger();
     constexpr int KV = 512 / D, HR = 4 + 2 * KV, PER = D / 256;  // float4 chunks per lane per half
     const int gw = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5), lane = threadIdx.x & 31;
     if (gw >= n * HR) return;
@@ -185,6 +193,8 @@ __global__ void __launch_bounds__(128) post_add_kernel(float *__restrict__ x, co
                                                        const float *__restrict__ w, const float *__restrict__ scale,
                                                        int8_t *__restrict__ q, float *__restrict__ qs, int qs_stride,
                                                        const float *__restrict__ next_w) {
+    pdl_wait();
+    pdl_trigger();
     __shared__ double red[2][4];
     const int t = blockIdx.x, i = threadIdx.x, lane = i & 31;
     float4 *xp = reinterpret_cast<float4 *>(x + size_t(t) * 512) + i;
@@ -211,6 +221,8 @@ __global__ void __launch_bounds__(128) post_add_kernel(float *__restrict__ x, co
 __global__ void gate_quant_kernel(int8_t *__restrict__ q, float *__restrict__ qs, int qs_stride,
                                   const float *__restrict__ x, const float *__restrict__ other, int rows, int width,
                                   int other_stride, int other_offset) {
+    pdl_wait();
+    pdl_trigger();
     constexpr int PER = 1;  // float4 steps (4 blocks each) per warp
     const int steps = width / 128, wpr = (steps + PER - 1) / PER;
     const int gw = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5), lane = threadIdx.x & 31;
@@ -240,6 +252,8 @@ __global__ void gate_quant_kernel(int8_t *__restrict__ q, float *__restrict__ qs
 // ahead of the in-order adds; the result goes straight into out.
 __global__ void pool_mean_kernel(float *__restrict__ out, const float *__restrict__ y,
                                  const unsigned *__restrict__ offsets, int width) {
+    pdl_wait();
+    pdl_trigger();
     const int s = blockIdx.y, z = blockIdx.x * blockDim.x + threadIdx.x;
     if (z >= width) return;
     const unsigned lo = offsets[s], hi = offsets[s + 1];
@@ -261,6 +275,8 @@ __global__ void pool_mean_kernel(float *__restrict__ out, const float *__restric
 // kernels.c:82-93 (lanes 0..7 are its two 4-lane accumulators over 8-element
 // chunks, each summed in chunk order), then x *= 1/sqrt(ss) (kernels.c:393-396).
 __global__ void pool_l2_kernel(float *__restrict__ out, int width) {
+    pdl_wait();
+    pdl_trigger();
     const int s = blockIdx.x, lane = threadIdx.x;
     float *o = out + size_t(s) * width;
     float acc = 0.0f;
