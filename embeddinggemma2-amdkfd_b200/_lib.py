@@ -47,6 +47,7 @@ SIGNATURES = {
     "eg2_launch_ple_proj": (i32, [vp, vp]),
     "eg2_launch_norm_quant": (i32, [vp, vp]),
     "eg2_launch_q8_mm": (i32, [vp, vp]),
+    "eg2_launch_q8_geglu": (i32, [vp, vp]),
     "eg2_launch_qkv_post": (i32, [vp, vp]),
     "eg2_launch_attention_f16": (i32, [vp, vp]),
     "eg2_launch_post_add": (i32, [vp, vp]),
@@ -133,6 +134,11 @@ class EgQ8MM(C.Structure):
                 ("n", u32), ("k", u32), ("m", u32), ("exact", u32)]
 
 
+class EgQ8GeGLU(C.Structure):
+    _fields_ = [("q", P), ("scale", P), ("scale_stride", u32), ("xq", P), ("xs", P), ("xs_stride", u32), ("wq", P),
+                ("ws", P), ("n", u32), ("k", u32), ("m", u32), ("exact", u32)]
+
+
 class EgQkvPost(C.Structure):
     _fields_ = [("q", P), ("k", P), ("v", P), ("qkv", P), ("q_norm", P), ("k_norm", P),
                 ("rope_cos", P), ("rope_sin", P), ("pos", P), ("n", u32), ("d", u32)]
@@ -158,5 +164,5 @@ class EgPoolL2(C.Structure):
 
 
 STRUCTS = {c.__name__: c for c in (EgGather, EgMM, EgNorm, EgRope, EgAttention, EgElement, EgPool, EgNormResidual,
-                                   EgNormRope, EgEmbed, EgPleProj, EgNormQuant, EgQ8MM, EgQkvPost, EgAttentionF16,
+                                   EgNormRope, EgEmbed, EgPleProj, EgNormQuant, EgQ8MM, EgQ8GeGLU, EgQkvPost, EgAttentionF16,
                                    EgPostAdd, EgGateQuant, EgPoolL2)}

@@ -64,7 +64,7 @@ struct Q8Weight {
 
 struct Layer {
     int d = 256, kv = 2;
-    Q8Weight qkv, o, up, gate, down, inp_gate, proj;
+    Q8Weight qkv, o, gu, down, inp_gate, proj;  // gu: gate/up interleaved in 64-row chunks
     const float *attn_norm = nullptr, *q_norm = nullptr, *k_norm = nullptr, *post_attn_norm = nullptr,
                 *ffn_norm = nullptr, *post_ffw_norm = nullptr, *post_norm = nullptr, *out_scale = nullptr;
 };
@@ -103,11 +103,11 @@ struct Backend {
     // arena
     int *ids = nullptr;
     unsigned *bounds = nullptr, *pos = nullptr, *offsets = nullptr;
-    float *x = nullptr, *ple = nullptr, *qkv = nullptr, *attn = nullptr, *h = nullptr, *up = nullptr,
-          *gate = nullptr, *y = nullptr, *pooled = nullptr, *xs = nullptr;
+    float *x = nullptr, *ple = nullptr, *qkv = nullptr, *attn = nullptr, *h = nullptr, *y = nullptr, *pooled = nullptr,
+          *xs = nullptr, *gs = nullptr;
     void *x_hi = nullptr, *x_lo = nullptr, *qh = nullptr, *kh = nullptr, *vh = nullptr;
-    int8_t *xq = nullptr;
-    CUtensorMap tm_xq[3]{}, tm_xs[3]{}, tm_hi{}, tm_lo{}, tm_ple{};
+    int8_t *xq = nullptr, *gq = nullptr;  // Q8 activations; gq/gs: the GeGLU output (FFN down operand)
+    CUtensorMap tm_xq[3]{}, tm_xs[3]{}, tm_gq{}, tm_gs{}, tm_hi{}, tm_lo{}, tm_ple{};
     bool gemm_exact = false;  // EG2_B200_GEMM=exact: the reference scalar tile's rounding order
 
     // host staging (pinned)
@@ -166,6 +166,25 @@ struct Backend {
         ck(cudaMemcpyAsync(staging, t->data, t->n_bytes, cudaMemcpyHostToDevice, stream), "weight upload");
         ck(launch_repack_q8(staging, rows, k, w.codes + size_t(row0) * k, w.scales + row0, w.rows, stream), "repack");
         ck(cudaStreamSynchronize(stream), "repack sync");  // staging is reused by the next tensor
+    }
+    // Gate and up matrices [rows][k] into one weight interleaved in 64-row chunks
+    // (the fused GeGLU GEMM's layout): rows 128c.. = gate rows 64c.., rows
+    // 128c+64.. = up rows 64c...
+    void repack_geglu(const std::string &gate, const std::string &up, int k, int rows, Q8Weight &w,
+                      uint8_t *staging) {
+        const size_t chunk_bytes = size_t(64) * (k / 32) * 34;
+        for (int half = 0; half < 2; ++half) {
+            const ei_tensor *t = tensor(half ? up : gate);
+            check_shape(t, uint64_t(k), uint64_t(rows), 8, half ? up : gate);
+            ck(cudaMemcpyAsync(staging, t->data, t->n_bytes, cudaMemcpyHostToDevice, stream), "weight upload");
+            for (int c = 0; c < rows / 64; ++c) {
+                const int row0 = 128 * c + 64 * half;
+                ck(launch_repack_q8(staging + c * chunk_bytes, 64, k, w.codes + size_t(row0) * k, w.scales + row0,
+                                    w.rows, stream),
+                   "repack");
+            }
+            ck(cudaStreamSynchronize(stream), "repack sync");
+        }
     }
     void alloc_q8(Q8Weight &w, int rows, int k) {
         w.rows = rows, w.k = k;
@@ -237,17 +256,15 @@ struct Backend {
             repack(nm("attn_v"), 512, 512, L.qkv, 4 * L.d + 512, staging);
             alloc_q8(L.o, 512, 4 * L.d);
             repack(nm("attn_output"), 4 * L.d, 512, L.o, 0, staging);
-            alloc_q8(L.up, 2048, 512);
-            repack(nm("ffn_up"), 512, 2048, L.up, 0, staging);
-            alloc_q8(L.gate, 2048, 512);
-            repack(nm("ffn_gate"), 512, 2048, L.gate, 0, staging);
+            alloc_q8(L.gu, 4096, 512);
+            repack_geglu(nm("ffn_gate"), nm("ffn_up"), 512, 2048, L.gu, staging);
             alloc_q8(L.down, 512, 2048);
             repack(nm("ffn_down"), 2048, 512, L.down, 0, staging);
             alloc_q8(L.inp_gate, 512, 512);
             repack(nm("inp_gate"), 512, 512, L.inp_gate, 0, staging);
             alloc_q8(L.proj, 512, 512);
             repack(nm("proj"), 512, 512, L.proj, 0, staging);
-            for (Q8Weight *w : {&L.qkv, &L.o, &L.up, &L.gate, &L.down, &L.inp_gate, &L.proj}) finish_q8(*w);
+            for (Q8Weight *w : {&L.qkv, &L.o, &L.gu, &L.down, &L.inp_gate, &L.proj}) finish_q8(*w);
         }
         alloc_q8(output, 768, 512);
         repack("output.weight", 512, 768, output, 0, staging);
@@ -287,8 +304,8 @@ struct Backend {
         vh = dalloc<uint16_t>(size_t(CAP) * 512);
         attn = dalloc<float>(size_t(CAP) * 2048);
         h = dalloc<float>(size_t(CAP) * 512);
-        up = dalloc<float>(size_t(CAP) * 2048);
-        gate = dalloc<float>(size_t(CAP) * 2048);
+        gq = dalloc<int8_t>(size_t(CAP) * 2048);
+        gs = dalloc<float>(size_t(64) * CAP);
         y = dalloc<float>(size_t(CAP) * 768);
         pooled = dalloc<float>(size_t(CAP) * 768);
         const int ks[3] = {512, 1024, 2048};
@@ -296,6 +313,8 @@ struct Backend {
             if (!q8_tmap(&tm_xq[i], xq, uint64_t(ks[i]), CAP, 64) ||
                 !scale_tmap(&tm_xs[i], xs, CAP, uint64_t(ks[i] / 32), 64))
                 throw std::runtime_error("tensor map (activations)");
+        if (!q8_tmap(&tm_gq, gq, 2048, CAP, 64) || !scale_tmap(&tm_gs, gs, CAP, 64, 64))
+            throw std::runtime_error("tensor map (GeGLU activations)");
         if (const char *m = std::getenv("EG2_B200_GEMM")) gemm_exact = !std::strcmp(m, "exact");
         if (!bf16_tmap(&tm_hi, x_hi, 512, CAP, 128) || !bf16_tmap(&tm_lo, x_lo, 512, CAP, 128) ||
             !bf16_tmap(&tm_ple, ple_w, 512, 24 * 512, 256))
@@ -362,12 +381,16 @@ struct Backend {
             mark("gemm_o");
             ck(launch_post_add(x, h, L.post_attn_norm, nullptr, xq, xs, CAP, L.ffn_norm, N, s), "post_add"), ++launches;
             mark("post_add");
-            gemm(L.up, up, 2048, N, s), ++launches;
-            gemm(L.gate, gate, 2048, N, s), ++launches;
-            mark("gemm_up_gate");
-            ck(launch_gate_quant(xq, xs, CAP, gate, up, N, 2048, 2048, 0, s), "gelu"), ++launches;
-            mark("gelu_quant");
-            gemm(L.down, h, 512, N, s), ++launches;
+            // ffn_gate and ffn_up in one GEMM whose epilogue applies gelu(gate) * up
+            // and quantizes (ROW_GELU_QUANT fused); the result is the down operand.
+            ck(launch_q8gemm_geglu(L.gu.tmap, tm_xq[0], L.gu.tscale, tm_xs[0], gemm_exact, gq, gs, CAP, N, L.gu.rows,
+                                   L.gu.k, s),
+               "GeGLU GEMM"),
+                ++launches;
+            mark("gemm_geglu");
+            ck(launch_q8gemm(L.down.tmap, tm_gq, L.down.tscale, tm_gs, gemm_exact, h, 512, N, L.down.rows, L.down.k, s),
+               "q8 GEMM"),
+                ++launches;
             mark("gemm_down");
             ck(launch_post_add(x, h, L.post_ffw_norm, nullptr, xq, xs, CAP, nullptr, N, s), "post_add"), ++launches;
             mark("post_add");

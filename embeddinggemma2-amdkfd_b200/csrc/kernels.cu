@@ -84,21 +84,31 @@ static cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, s
     cfg.attrs = attr, cfg.numAttrs = enabled ? 1 : 0;
     return cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
 }
-template <bool EXACT>
+template <bool EXACT, bool GEGLU>
 static cudaError_t q8gemm_go(const CUtensorMap &w, const CUtensorMap &x, const CUtensorMap &sw,
                              const CUtensorMap &sx, const Q8GemmParams &p, cudaStream_t s) {
-    const Q8Smem L = q8gemm_smem(p.K);
+    const Q8Smem L = q8gemm_smem(p.K, GEGLU);
+    if (L.total > 227 * 1024) return cudaErrorInvalidValue;
     const int grid = p.num_tiles < sm_count() ? p.num_tiles : sm_count();
-    return launch_pdl(q8gemm_kernel<EXACT>, dim3(grid), dim3(Q8Cfg::THREADS), L.total, s, w, x, sw, sx, p);
+    return launch_pdl(q8gemm_kernel<EXACT, GEGLU>, dim3(grid), dim3(Q8Cfg::THREADS), L.total, s, w, x, sw, sx, p);
 }
 cudaError_t launch_q8gemm(const CUtensorMap &w, const CUtensorMap &x, const CUtensorMap &sw, const CUtensorMap &sx,
                           bool exact, float *out, int ldo, int T, int R, int K, cudaStream_t s) {
     if (T <= 0) return cudaSuccess;
     if (K <= 0 || K % 128 || K > 2048 || R <= 0 || R % Q8Cfg::BM || ldo < R) return cudaErrorInvalidValue;
-    if (q8gemm_smem(K).total > 227 * 1024) return cudaErrorInvalidValue;
-    Q8GemmParams p{out, ldo, T, R, K, (T + Q8Cfg::BN - 1) / Q8Cfg::BN, 0};
+    Q8GemmParams p{out, ldo, T, R, K, (T + Q8Cfg::BN - 1) / Q8Cfg::BN, 0, nullptr, nullptr, 0};
     p.num_tiles = (R / Q8Cfg::BM) * p.tiles_t;
-    return exact ? q8gemm_go<true>(w, x, sw, sx, p, s) : q8gemm_go<false>(w, x, sw, sx, p, s);
+    return exact ? q8gemm_go<true, false>(w, x, sw, sx, p, s) : q8gemm_go<false, false>(w, x, sw, sx, p, s);
+}
+cudaError_t launch_q8gemm_geglu(const CUtensorMap &w, const CUtensorMap &x, const CUtensorMap &sw,
+                                const CUtensorMap &sx, bool exact, int8_t *q8, float *q8s, int q8s_stride, int T, int R,
+                                int K, cudaStream_t s) {
+    if (T <= 0) return cudaSuccess;
+    if (K <= 0 || K % 128 || K > 2048 || R <= 0 || R % Q8Cfg::BM || q8s_stride < T || !q8 || !q8s)
+        return cudaErrorInvalidValue;
+    Q8GemmParams p{nullptr, 0, T, R, K, (T + Q8Cfg::BN - 1) / Q8Cfg::BN, 0, q8, q8s, q8s_stride};
+    p.num_tiles = (R / Q8Cfg::BM) * p.tiles_t;
+    return exact ? q8gemm_go<true, true>(w, x, sw, sx, p, s) : q8gemm_go<false, true>(w, x, sw, sx, p, s);
 }
 
 cudaError_t launch_ple(const CUtensorMap &hi, const CUtensorMap &lo, const CUtensorMap &w, float *ple,
@@ -196,10 +206,9 @@ cudaError_t launch_repack_q8(const void *blocks, int rows, int k, int8_t *codes,
 
 cudaError_t init_kernel_attributes() {
     cudaError_t e;
-    if ((e = cudaFuncSetAttribute(q8gemm_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024)))
-        return e;
-    if ((e = cudaFuncSetAttribute(q8gemm_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024)))
-        return e;
+    for (auto k : {q8gemm_kernel<false, false>, q8gemm_kernel<true, false>, q8gemm_kernel<false, true>,
+                   q8gemm_kernel<true, true>})
+        if ((e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024))) return e;
     if ((e = cudaFuncSetAttribute(ple_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(PleCfg::SMEM)))) return e;
     if ((e = cudaFuncSetAttribute(attention_kernel<256>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                   int(AttnCfg<256>::SMEM))))
@@ -317,6 +326,21 @@ int eg2_launch_q8_mm(const EgQ8MM *p, void *s) {
         !scale_tmap(&sx, p->xs, p->xs_stride, p->k / 32, uint32_t(Q8Cfg::BN)))
         return rc(cudaErrorInvalidValue);
     return rc(launch_q8gemm(w, x, sw, sx, p->exact != 0, p->out, int(p->m), int(p->n), int(p->m), int(p->k), S(s)));
+}
+int eg2_launch_q8_geglu(const EgQ8GeGLU *p, void *s) {
+    if (cudaError_t e = ensure_attributes()) return rc(e);
+    if (!p->n) return 0;
+    if (p->k % 128 || p->k > 2048 || p->m % 64 || !p->m || p->xs_stride < p->n || p->xs_stride % 4 ||
+        p->scale_stride < p->n)
+        return rc(cudaErrorInvalidValue);
+    const unsigned rows = 2 * p->m;  // interleaved gate/up weight rows
+    CUtensorMap w, x, sw, sx;
+    if (!q8_tmap(&w, p->wq, p->k, rows, uint32_t(Q8Cfg::BM)) || !q8_tmap(&x, p->xq, p->k, p->n, uint32_t(Q8Cfg::BN)) ||
+        !scale_tmap(&sw, p->ws, rows, p->k / 32, uint32_t(Q8Cfg::BM)) ||
+        !scale_tmap(&sx, p->xs, p->xs_stride, p->k / 32, uint32_t(Q8Cfg::BN)))
+        return rc(cudaErrorInvalidValue);
+    return rc(launch_q8gemm_geglu(w, x, sw, sx, p->exact != 0, p->q, p->scale, int(p->scale_stride), int(p->n),
+                                  int(rows), int(p->k), S(s)));
 }
 int eg2_launch_qkv_post(const EgQkvPost *p, void *s) {
     return rc(launch_qkv_post(p->q, p->k, p->v, p->qkv, p->q_norm, p->k_norm, p->rope_cos, p->rope_sin, p->pos,

@@ -23,6 +23,12 @@ bool scale_tmap(CUtensorMap *map, const float *base, uint64_t stride, uint64_t k
 // exact: the reference scalar tile's rounding order (bit-identical outputs).
 cudaError_t launch_q8gemm(const CUtensorMap &w, const CUtensorMap &x, const CUtensorMap &sw, const CUtensorMap &sx,
                           bool exact, float *out, int ldo, int T, int R, int K, cudaStream_t s);
+// GeGLU epilogue (ROW_GELU_QUANT fused): the weight is gate/up interleaved in
+// 64-row chunks (rows 128c..128c+63 = gate rows 64c.., the next 64 = up rows
+// 64c..); writes Q8_0 codes [T][R/2] of gelu(gate) * up and block-major scales.
+cudaError_t launch_q8gemm_geglu(const CUtensorMap &w, const CUtensorMap &x, const CUtensorMap &sw,
+                                const CUtensorMap &sx, bool exact, int8_t *q8, float *q8s, int q8s_stride, int T, int R,
+                                int K, cudaStream_t s);
 cudaError_t launch_ple(const CUtensorMap &hi, const CUtensorMap &lo, const CUtensorMap &w, float *ple,
                        const float *norm, int M, cudaStream_t s);
 cudaError_t launch_embed(float *x, void *x_hi, void *x_lo, const void *emb, const int *ids, int n, cudaStream_t s);

@@ -49,10 +49,13 @@
 namespace eg2 {
 
 struct Q8GemmParams {
-    float *out;   // [T][ldo] fp32
+    float *out;   // [T][ldo] fp32 (plain mode)
     int ldo;
     int T, R, K;  // tokens, weight rows (= output columns, a multiple of 128), depth
     int tiles_t, num_tiles;
+    int8_t *q8;   // GeGLU mode: Q8_0 codes [T][R/2] of gelu(gate) * up
+    float *q8s;   // and their block-major scales, q8s[b * q8s_stride + t]
+    int q8s_stride;
 };
 
 struct Q8Cfg {
@@ -66,14 +69,16 @@ struct Q8Cfg {
     static constexpr int A_BYTES = BM * BK, B_BYTES = BN * BK, STAGE_BYTES = A_BYTES + B_BYTES;
 };
 
-// Shared-memory plan (offsets from the 1024-aligned base) for depth K.
+// Shared-memory plan (offsets from the 1024-aligned base) for depth K; the
+// GeGLU mode adds the 64 x 128 fp32 tile used to pair gate and up rows.
 struct Q8Smem {
     int stages, pbufs, kb;
-    size_t stage_bytes, sw_bytes, sx_bytes, panel_bytes, total;
+    size_t stage_bytes, sw_bytes, sx_bytes, panel_bytes, gbuf_bytes, total;
     __host__ __device__ size_t panel(int b) const { return size_t(stages) * stage_bytes + size_t(b) * panel_bytes; }
-    __host__ __device__ size_t bars() const { return size_t(stages) * stage_bytes + size_t(pbufs) * panel_bytes; }
+    __host__ __device__ size_t gbuf() const { return size_t(stages) * stage_bytes + size_t(pbufs) * panel_bytes; }
+    __host__ __device__ size_t bars() const { return gbuf() + gbuf_bytes; }
 };
-__host__ __device__ inline Q8Smem q8gemm_smem(int K) {
+__host__ __device__ inline Q8Smem q8gemm_smem(int K, bool geglu = false) {
     Q8Smem s;
     s.stages = 4;
     s.kb = K / 32;
@@ -81,13 +86,18 @@ __host__ __device__ inline Q8Smem q8gemm_smem(int K) {
     s.sw_bytes = size_t(s.kb) * Q8Cfg::BM * 4;
     s.sx_bytes = size_t(s.kb) * Q8Cfg::BN * 4;
     s.panel_bytes = (s.sw_bytes + s.sx_bytes + 1023) / 1024 * 1024;
-    const size_t limit = 227 * 1024, fixed = 1024 + 512;
+    s.gbuf_bytes = geglu ? (size_t(Q8Cfg::BN) * (Q8Cfg::BM + 1) * 4 + 1023) / 1024 * 1024 : 0;
+    const size_t limit = 227 * 1024, fixed = 1024 + 512 + s.gbuf_bytes;
     s.pbufs = fixed + 4 * s.stage_bytes + 2 * s.panel_bytes > limit ? 1 : 2;
     s.total = fixed + size_t(s.stages) * s.stage_bytes + size_t(s.pbufs) * s.panel_bytes;
     return s;
 }
 
-template <bool EXACT>
+// GEGLU: the weight rows of every 128-row tile are 64 gate rows followed by
+// the 64 up rows of the same output columns (ROW_GELU_QUANT fused,
+// gemma2_fast.c:714-720): the epilogue pairs them through shared memory and
+// writes Q8_0 codes of gelu_tanh(gate) * up instead of fp32 outputs.
+template <bool EXACT, bool GEGLU>
 __global__ void __launch_bounds__(Q8Cfg::THREADS, 1)
     q8gemm_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmX,
                   const __grid_constant__ CUtensorMap tmSW, const __grid_constant__ CUtensorMap tmSX,
@@ -95,12 +105,13 @@ __global__ void __launch_bounds__(Q8Cfg::THREADS, 1)
     using C = Q8Cfg;
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = align_smem_1024(smem_raw);
-    const Q8Smem L = q8gemm_smem(p.K);
+    const Q8Smem L = q8gemm_smem(p.K, GEGLU);
     const int Kb = L.kb, ksteps = p.K / C::BK, STAGES = L.stages, PBUFS = L.pbufs;
     uint64_t *bars = reinterpret_cast<uint64_t *>(smem + L.bars());
     uint64_t *full = bars, *empty = bars + 4, *accf = bars + 8, *acce = accf + 2;  // accf/acce: per slot group
     uint64_t *pfull = acce + 2, *pempty = pfull + 2, *mdone = pempty + 2, *edone = mdone + 1;
-    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(edone + 1);
+    uint64_t *gfull = edone + 1, *gdone = gfull + 1;  // GeGLU pairing tile written / consumed
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(gdone + 1);
     volatile int *abort = reinterpret_cast<volatile int *>(tmem_slot + 1);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -114,6 +125,7 @@ __global__ void __launch_bounds__(Q8Cfg::THREADS, 1)
         for (int b = 0; b < 2; ++b) bar_init(&accf[b], 1), bar_init(&acce[b], C::EPI_WARPS);
         for (int b = 0; b < PBUFS; ++b) bar_init(&pfull[b], 1), bar_init(&pempty[b], C::EPI_WARPS);
         bar_init(mdone, 1), bar_init(edone, C::EPI_WARPS);
+        bar_init(gfull, C::EPI_WARPS), bar_init(gdone, C::EPI_WARPS);
         fence_bar_init();
     }
     if (warp == 1) {
@@ -279,6 +291,59 @@ __global__ void __launch_bounds__(Q8Cfg::THREADS, 1)
             __syncwarp();
             if (lane == 0) bar_arrive(&pempty[pb]);
             if (!ok) break;
+            if (GEGLU) {
+                // Pair gate (lanes 0..63) and up (lanes 64..127) of each output
+                // column through shared memory G[token][row] (row stride GS,
+                // padded against bank conflicts).  Then each lane pair owns one
+                // (token, 32-column block) of the tile's 64 tokens x 64 output
+                // columns: each lane computes g = gelu(gate) * up for 16
+                // columns (16 independent chains), the pair exchanges its amax
+                // with one shuffle, and each lane stores its 16 codes.
+                constexpr int GS = C::BM + 1;
+                float *G = reinterpret_cast<float *>(smem + L.gbuf());
+#pragma unroll
+                for (int c = 0; c < C::HALF / 2; ++c) {
+                    const int tok = half * C::HALF + 2 * c;
+                    G[tok * GS + r_local] = acc[c].x;
+                    G[(tok + 1) * GS + r_local] = acc[c].y;
+                }
+                __syncwarp();
+                if (lane == 0) bar_arrive(gfull);
+                if (!__all_sync(0xffffffffu, wait_bar(gfull, it & 1, abort))) {
+                    ok = false;
+                    break;
+                }
+                const int u = ((warp - 2) * 32 + lane) >> 1, part = lane & 1;  // 128 units, 2 lanes each
+                const int tok = u >> 1, cb = u & 1, t = t0 + tok, col0 = r0 / 2;
+                const float *gr = G + tok * GS + cb * 32 + part * 16;
+                float g[16];
+                float amax = 0.0f;
+#pragma unroll
+                for (int j = 0; j < 16; ++j) {
+                    g[j] = __fmul_rn(ref_gelu(gr[j]), gr[64 + j]);
+                    amax = fmaxf(amax, fabsf(g[j]));
+                }
+                amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
+                const float d = __fdiv_rn(amax, 127.0f);
+                const float id = d != 0.0f ? __fdiv_rn(1.0f, d) : 0.0f;
+                if (t < p.T) {
+                    uint32_t w4[4];
+#pragma unroll
+                    for (int j = 0; j < 4; ++j)
+                        w4[j] = q8_code(g[4 * j], id) | q8_code(g[4 * j + 1], id) << 8 |
+                                q8_code(g[4 * j + 2], id) << 16 | q8_code(g[4 * j + 3], id) << 24;
+                    *reinterpret_cast<uint4 *>(p.q8 + size_t(t) * (p.R / 2) + col0 + cb * 32 + part * 16) =
+                        make_uint4(w4[0], w4[1], w4[2], w4[3]);
+                    if (part == 0) p.q8s[size_t(col0 / 32 + cb) * p.q8s_stride + t] = fp16_bits_to_f32(ref_fp32_to_fp16(d));
+                }
+                __syncwarp();
+                if (lane == 0) bar_arrive(gdone);
+                if (!__all_sync(0xffffffffu, wait_bar(gdone, it & 1, abort))) {  // G is rewritten next tile
+                    ok = false;
+                    break;
+                }
+                continue;
+            }
             // out[t][r]: for each token the warp's 32 lanes write 128 consecutive bytes.
             float *o = p.out + size_t(t0 + half * C::HALF) * p.ldo + r0 + r_local;
             const int tmax = p.T - (t0 + half * C::HALF);

@@ -82,6 +82,11 @@ def q8_mm(out, xq, xs, xs_stride, wq, ws, n, k, m, exact=False):
     _call("eg2_launch_q8_mm", _lib.EgQ8MM(_p(out), _p(xq), _p(xs), xs_stride, _p(wq), _p(ws), n, k, m, int(exact)))
 
 
+def q8_geglu(q, scale, scale_stride, xq, xs, xs_stride, wq, ws, n, k, m, exact=False):
+    _call("eg2_launch_q8_geglu", _lib.EgQ8GeGLU(_p(q), _p(scale), scale_stride, _p(xq), _p(xs), xs_stride, _p(wq),
+                                                _p(ws), n, k, m, int(exact)))
+
+
 def qkv_post(q, k, v, qkv, q_norm, k_norm, rope_cos, rope_sin, pos, n, d):
     _call("eg2_launch_qkv_post", _lib.EgQkvPost(_p(q), _p(k), _p(v), _p(qkv), _p(q_norm), _p(k_norm),
                                                 _p(rope_cos), _p(rope_sin), _p(pos), n, d))

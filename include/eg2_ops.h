@@ -60,6 +60,19 @@ typedef struct {
     float *out; const int8_t *xq; const float *xs; unsigned xs_stride;
     const int8_t *wq; const float *ws; unsigned n, k, m, exact;
 } EgQ8MM;
+/* GeGLU projection with its quantization fused (gemma2_fast.c:978-979 and
+ * ROW_GELU_QUANT :714-720): g[t][c] = gelu_tanh(gate[t][c]) * up[t][c] with
+ * gate = x . Wg^T and up = x . Wu^T computed as in EgQ8MM, then Q8_0 of g:
+ * codes q [n][m], scales scale[b * scale_stride + t].  The weight operand is
+ * the two matrices interleaved in 64-row chunks: rows 128c .. 128c+63 of
+ * wq/ws are gate rows 64c .., rows 128c+64 .. 128c+127 the up rows 64c ..
+ * (2m rows, m % 64 == 0; scales [k/32][2m]).  Identical to EgQ8MM on each
+ * half followed by EgGateQuant. */
+typedef struct {
+    int8_t *q; float *scale; unsigned scale_stride;
+    const int8_t *xq; const float *xs; unsigned xs_stride;
+    const int8_t *wq; const float *ws; unsigned n, k, m, exact;
+} EgQ8GeGLU;
 /* Per head RMS (q, k weighted; v plain) and NEOX RoPE from host tables at the
  * token's in-sequence position (ROW_QKV_POST, gemma2_fast.c:692-706).  qkv is
  * the fused projection [n][4d | 512 | 512]; outputs are fp16 [n][heads][d]. */
@@ -110,6 +123,7 @@ int eg2_launch_embed(const EgEmbed *p, void *stream);
 int eg2_launch_ple_proj(const EgPleProj *p, void *stream);
 int eg2_launch_norm_quant(const EgNormQuant *p, void *stream);
 int eg2_launch_q8_mm(const EgQ8MM *p, void *stream);
+int eg2_launch_q8_geglu(const EgQ8GeGLU *p, void *stream);
 int eg2_launch_qkv_post(const EgQkvPost *p, void *stream);
 int eg2_launch_attention_f16(const EgAttentionF16 *p, void *stream);
 int eg2_launch_post_add(const EgPostAdd *p, void *stream);

@@ -220,6 +220,39 @@ def test_q8_mm_int32_block_accumulators_exact(ops, port, n, k, m):
     np.testing.assert_array_equal(got_exact.astype(np.int64), exact)
 
 
+@pytest.mark.parametrize("n,k,m,exact", [(130, 512, 2048, False), (2048, 512, 2048, False), (77, 1024, 128, True),
+                                         (300, 512, 2048, True)])
+def test_q8_geglu_equals_unfused(ops, n, k, m, exact):
+    """The GeGLU GEMM (gate/up interleaved in 64-row chunks, gelu(gate) * up
+    and Q8_0 in the epilogue) reproduces q8_mm(gate), q8_mm(up), gate_quant
+    bit for bit."""
+    rng = np.random.default_rng(n + k + m + exact)
+    xq, xd = _q8_operands(rng, n, k)
+    gq, gd = _q8_operands(rng, m, k)
+    uq, ud = _q8_operands(rng, m, k)
+    stride = (n + 127) // 128 * 128
+    xs = np.zeros((k // 32, stride), np.float32)
+    xs[:, :n] = f16_to_f32(xd).T
+    # unfused reference path on the GPU
+    gate = torch.from_numpy(_gpu_q8_mm(ops, xq, xd, gq, gd, stride, exact)).to(DEV)
+    up = torch.from_numpy(_gpu_q8_mm(ops, xq, xd, uq, ud, stride, exact)).to(DEV)
+    q_ref = torch.zeros(n * m, dtype=torch.int8, device=DEV)
+    s_ref = torch.zeros(m // 32 * stride, device=DEV)
+    ops.gate_quant(q_ref, s_ref, stride, gate.ravel(), up.ravel(), n, m, m, 0)
+    # fused
+    wq = np.zeros((2 * m, k), np.int8)
+    wd = np.zeros((2 * m, k // 32), np.uint16)
+    for c in range(m // 64):
+        wq[128 * c:128 * c + 64], wd[128 * c:128 * c + 64] = gq[64 * c:64 * c + 64], gd[64 * c:64 * c + 64]
+        wq[128 * c + 64:128 * c + 128], wd[128 * c + 64:128 * c + 128] = uq[64 * c:64 * c + 64], ud[64 * c:64 * c + 64]
+    ws = np.ascontiguousarray(f16_to_f32(wd).T)
+    q = torch.zeros(n * m, dtype=torch.int8, device=DEV)
+    sc = torch.zeros(m // 32 * stride, device=DEV)
+    ops.q8_geglu(q, sc, stride, T(xq), T(xs), stride, T(wq), T(ws), n, k, m, exact)
+    np.testing.assert_array_equal(host(q), host(q_ref))
+    np.testing.assert_array_equal(host(sc).reshape(-1, stride)[:, :n], host(s_ref).reshape(-1, stride)[:, :n])
+
+
 @pytest.mark.parametrize("width,stride,offset", [(2048, 2048, 0), (512, 12288, 7 * 512)])
 def test_gate_quant_bit_exact(ops, port, width, stride, offset):
     rng = np.random.default_rng(width)
