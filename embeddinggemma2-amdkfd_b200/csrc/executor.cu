@@ -172,17 +172,11 @@ struct Backend {
     // 128c+64.. = up rows 64c...
     void repack_geglu(const std::string &gate, const std::string &up, int k, int rows, Q8Weight &w,
                       uint8_t *staging) {
-        const size_t chunk_bytes = size_t(64) * (k / 32) * 34;
         for (int half = 0; half < 2; ++half) {
             const ei_tensor *t = tensor(half ? up : gate);
             check_shape(t, uint64_t(k), uint64_t(rows), 8, half ? up : gate);
             ck(cudaMemcpyAsync(staging, t->data, t->n_bytes, cudaMemcpyHostToDevice, stream), "weight upload");
-            for (int c = 0; c < rows / 64; ++c) {
-                const int row0 = 128 * c + 64 * half;
-                ck(launch_repack_q8(staging + c * chunk_bytes, 64, k, w.codes + size_t(row0) * k, w.scales + row0,
-                                    w.rows, stream),
-                   "repack");
-            }
+            ck(launch_repack_q8(staging, rows, k, w.codes, w.scales, w.rows, stream, 64, half), "repack");
             ck(cudaStreamSynchronize(stream), "repack sync");
         }
     }

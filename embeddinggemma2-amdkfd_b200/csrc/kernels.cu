@@ -196,11 +196,12 @@ cudaError_t launch_pool_l2(float *out, const float *y, const unsigned *offsets, 
 }
 
 cudaError_t launch_repack_q8(const void *blocks, int rows, int k, int8_t *codes, float *scales, int scale_stride,
-                             cudaStream_t s) {
+                             cudaStream_t s, int chunk, int phase) {
     const long long nblk = (long long)rows * (k / 32);
     if (nblk <= 0) return cudaSuccess;
+    if (chunk < 0 || (chunk > 0 && rows % chunk)) return cudaErrorInvalidValue;
     repack_q8_kernel<<<unsigned((nblk + 255) / 256), 256, 0, s>>>(static_cast<const uint8_t *>(blocks), rows, k, codes,
-                                                                  scales, scale_stride);
+                                                                  scales, scale_stride, chunk, phase);
     return cudaGetLastError();
 }
 

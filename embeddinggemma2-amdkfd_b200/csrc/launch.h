@@ -43,8 +43,10 @@ cudaError_t launch_post_add(float *x, const float *h, const float *w, const floa
 cudaError_t launch_gate_quant(int8_t *q, float *qs, int qs_stride, const float *x, const float *other, int rows,
                               int width, int other_stride, int other_offset, cudaStream_t s);
 cudaError_t launch_pool_l2(float *out, const float *y, const unsigned *offsets, int batch, int width, cudaStream_t s);
+// chunk > 0: rows interleaved with another matrix in chunk-row blocks, this
+// one at position `phase` (0 or 1) of each pair.
 cudaError_t launch_repack_q8(const void *blocks, int rows, int k, int8_t *codes, float *scales, int scale_stride,
-                             cudaStream_t s);
+                             cudaStream_t s, int chunk = 0, int phase = 0);
 // Opt every kernel into its shared-memory size on the current device, before
 // any graph capture.
 cudaError_t init_kernel_attributes();

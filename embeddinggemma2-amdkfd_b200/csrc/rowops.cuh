@@ -292,17 +292,20 @@ __global__ void pool_l2_kernel(float *__restrict__ out, int width) {
 }
 
 // GGUF Q8_0 blocks [rows][k/32] (34 B each) -> int8 codes [rows][k] and fp32
-// scales block-major, scales[b * scale_stride + row].
+// scales block-major, scales[b * scale_stride + row].  With chunk > 0, source
+// row r goes to destination row (r / chunk) * 2 * chunk + phase * chunk +
+// r % chunk (two matrices interleaved in chunk-row blocks).
 __global__ void repack_q8_kernel(const uint8_t *__restrict__ blocks, int rows, int k, int8_t *__restrict__ codes,
-                                 float *__restrict__ scales, int scale_stride) {
+                                 float *__restrict__ scales, int scale_stride, int chunk, int phase) {
     const int kb = k / 32;
     const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;  // one thread per block
     if (i >= (long long)rows * kb) return;
     const int r = int(i / kb), b = int(i % kb);
+    const int dr = chunk > 0 ? (r / chunk) * 2 * chunk + phase * chunk + r % chunk : r;
     const uint8_t *src = blocks + size_t(i) * 34;
     const uint16_t db = uint16_t(src[0]) | uint16_t(src[1]) << 8;
-    scales[size_t(b) * scale_stride + r] = fp16_bits_to_f32(db);
-    int8_t *dst = codes + size_t(r) * k + b * 32;
+    scales[size_t(b) * scale_stride + dr] = fp16_bits_to_f32(db);
+    int8_t *dst = codes + size_t(dr) * k + b * 32;
 #pragma unroll
     for (int z = 0; z < 32; ++z) dst[z] = int8_t(src[2 + z]);
 }
