@@ -53,6 +53,12 @@ def q8_gemm_ops(n_tokens: int) -> float:
     return 2.0 * per_tok * n_tokens
 
 
+# DRAM bytes (read + write) per q8gemm launch, averaged over the 145 GEMM
+# launches of one config-1 wave in one ncu capture (cold cache); the command
+# and the totals are in profiles/q8gemm_wave_dram.md.
+GEMM_DRAM_BYTES_PER_LAUNCH = 3.07e6
+
+
 def peaks():
     path = os.path.join(ROOT, "MEASURED_PEAKS.json")
     if os.path.exists(path):
@@ -263,7 +269,8 @@ def main():
         "roofline": {"kernel": "q8gemm_kernel (all Q8_0 GEMM launches of a wave)", "bound": "tensor",
                      "achieved": achieved, "peak": int8_peak, "unit": "TOP/s", "frac": achieved / int8_peak,
                      "peak_source": f"2 x bf16_tflops_sustained of {src} MEASURED_PEAKS (dense int8 = 2x bf16)",
-                     "traffic": None},
+                     "traffic": GEMM_DRAM_BYTES_PER_LAUNCH,
+                     "traffic_note": "dram read+write bytes per launch, ncu capture averaged over one wave's GEMMs"},
         "profile_ms": {k: round(v, 4) for k, v in prof.items()},
     }
     c = clocks.summary()
