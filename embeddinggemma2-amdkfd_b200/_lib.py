@@ -23,6 +23,7 @@ SIGNATURES = {
     # include/eg2_executor.h
     "ei_gemma2_kfd_create": (vp, [vp, cstr, sz]),
     "ei_gemma2_kfd_create_on": (vp, [vp, i32, cstr, sz]),
+    "eg2_b200_create": (vp, [vp, i32, u32, cstr, sz]),
     "ei_gemma2_kfd_free": (None, [vp]),
     "ei_gemma2_kfd_batch": (b, [vp, vp, vp, sz, vp, cstr, sz]),
     "eg2_b200_validate": (b, [vp, vp, sz, cstr, sz]),
@@ -50,6 +51,7 @@ SIGNATURES = {
     "eg2_launch_q8_geglu": (i32, [vp, vp]),
     "eg2_launch_qkv_post": (i32, [vp, vp]),
     "eg2_launch_attention_f16": (i32, [vp, vp]),
+    "eg2_launch_attention_exact": (i32, [vp, u32, vp]),
     "eg2_launch_post_add": (i32, [vp, vp]),
     "eg2_launch_gate_quant": (i32, [vp, vp]),
     "eg2_launch_pool_l2": (i32, [vp, vp]),

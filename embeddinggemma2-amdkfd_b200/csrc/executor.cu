@@ -108,7 +108,11 @@ struct Backend {
     void *x_hi = nullptr, *x_lo = nullptr, *qh = nullptr, *kh = nullptr, *vh = nullptr;
     int8_t *xq = nullptr, *gq = nullptr;  // Q8 activations; gq/gs: the GeGLU output (FFN down operand)
     CUtensorMap tm_xq[3]{}, tm_xs[3]{}, tm_gq{}, tm_gs{}, tm_hi{}, tm_lo{}, tm_ple{};
-    bool gemm_exact = false;  // EG2_B200_GEMM=exact: the reference scalar tile's rounding order
+    // Parity mode (EG2_B200_EXACT): GEMMs in the reference scalar tile's rounding
+    // order, PLE projection and attention on the CUDA-core exact-order kernels
+    // with fp32 q/k/v; every other kernel is bit-exact in both modes.
+    bool exact = false;
+    float *qf = nullptr, *kf = nullptr, *vf = nullptr;
 
     // host staging (pinned)
     uint32_t *h_in = nullptr;  // ids | bounds(2) | pos | offsets
@@ -191,7 +195,7 @@ struct Backend {
             throw std::runtime_error("cuTensorMapEncodeTiled failed for a weight");
     }
 
-    Backend(const ei_gguf *g, int dev) : model(g), device(dev) {
+    Backend(const ei_gguf *g, int dev, unsigned flags) : model(g), device(dev), exact(flags & EG2_B200_EXACT) {
         if (!g) throw std::runtime_error("empty model");
         // gemma2.c:30-62 hyperparameters.
         if (kv_u64("gemma-embedding2.block_count") != 24 || kv_u64("gemma-embedding2.embedding_length") != 512 ||
@@ -302,6 +306,11 @@ struct Backend {
         gs = dalloc<float>(size_t(64) * CAP);
         y = dalloc<float>(size_t(CAP) * 768);
         pooled = dalloc<float>(size_t(CAP) * 768);
+        if (exact) {
+            qf = dalloc<float>(size_t(CAP) * 2048);
+            kf = dalloc<float>(size_t(CAP) * 512);
+            vf = dalloc<float>(size_t(CAP) * 512);
+        }
         const int ks[3] = {512, 1024, 2048};
         for (int i = 0; i < 3; ++i)
             if (!q8_tmap(&tm_xq[i], xq, uint64_t(ks[i]), CAP, 64) ||
@@ -309,7 +318,6 @@ struct Backend {
                 throw std::runtime_error("tensor map (activations)");
         if (!q8_tmap(&tm_gq, gq, 2048, CAP, 64) || !scale_tmap(&tm_gs, gs, CAP, 64, 64))
             throw std::runtime_error("tensor map (GeGLU activations)");
-        if (const char *m = std::getenv("EG2_B200_GEMM")) gemm_exact = !std::strcmp(m, "exact");
         if (!bf16_tmap(&tm_hi, x_hi, 512, CAP, 128) || !bf16_tmap(&tm_lo, x_lo, 512, CAP, 128) ||
             !bf16_tmap(&tm_ple, ple_w, 512, 24 * 512, 256))
             throw std::runtime_error("tensor map (PLE)");
@@ -338,7 +346,7 @@ struct Backend {
 
     static int kidx(int k) { return k == 512 ? 0 : k == 1024 ? 1 : 2; }
     void gemm(const Q8Weight &w, float *out, int ldo, int n, cudaStream_t s) {
-        ck(launch_q8gemm(w.tmap, tm_xq[kidx(w.k)], w.tscale, tm_xs[kidx(w.k)], gemm_exact, out, ldo, n, w.rows, w.k,
+        ck(launch_q8gemm(w.tmap, tm_xq[kidx(w.k)], w.tscale, tm_xs[kidx(w.k)], exact, out, ldo, n, w.rows, w.k,
                          s),
            "q8 GEMM");
     }
@@ -354,7 +362,10 @@ struct Backend {
         mark("start");
         ck(launch_embed(x, x_hi, x_lo, token_embd, ids, N, s), "embed"), ++launches;
         mark("embed");
-        ck(launch_ple(tm_hi, tm_lo, tm_ple, ple, ple_norm, N, s), "PLE"), ++launches;
+        if (exact)
+            ck(launch_ple_exact(ple, x, ple_w, ple_norm, N, s), "PLE"), launches += 2;
+        else
+            ck(launch_ple(tm_hi, tm_lo, tm_ple, ple, ple_norm, N, s), "PLE"), ++launches;
         mark("ple_proj");
         ck(launch_norm_quant(xq, xs, CAP, nullptr, x, layers[0].attn_norm, N, 512, s), "norm"), ++launches;
         mark("norm_quant");
@@ -363,11 +374,23 @@ struct Backend {
             const int rb = L.d == 512 ? 1 : 0;
             gemm(L.qkv, qkv, L.qkv.rows, N, s), ++launches;
             mark("gemm_qkv");
-            ck(launch_qkv_post(qh, kh, vh, qkv, L.q_norm, L.k_norm, rope_cos[rb], rope_sin[rb], pos, N, L.d, s),
-               "qkv_post"),
-                ++launches;
-            mark("qkv_post");
-            ck(launch_attention(attn, qh, kh, vh, bounds, N, L.d, L.d == 512 ? 0 : 512, s), "attention"), ++launches;
+            if (exact) {
+                ck(launch_qkv_post(qf, kf, vf, qkv, L.q_norm, L.k_norm, rope_cos[rb], rope_sin[rb], pos, N, L.d, s,
+                                   true),
+                   "qkv_post"),
+                    ++launches;
+                mark("qkv_post");
+                ck(launch_attention_exact(attn, qf, kf, vf, bounds, N, L.d, L.d == 512 ? 0 : 512, s), "attention"),
+                    ++launches;
+            } else {
+                ck(launch_qkv_post(qh, kh, vh, qkv, L.q_norm, L.k_norm, rope_cos[rb], rope_sin[rb], pos, N, L.d, s,
+                                   false),
+                   "qkv_post"),
+                    ++launches;
+                mark("qkv_post");
+                ck(launch_attention(attn, qh, kh, vh, bounds, N, L.d, L.d == 512 ? 0 : 512, s), "attention"),
+                    ++launches;
+            }
             mark(L.d == 512 ? "attention_global" : "attention_local");
             ck(launch_norm_quant(xq, xs, CAP, nullptr, attn, nullptr, N, 4 * L.d, s), "quant"), ++launches;
             mark("quant_attn");
@@ -377,12 +400,12 @@ struct Backend {
             mark("post_add");
             // ffn_gate and ffn_up in one GEMM whose epilogue applies gelu(gate) * up
             // and quantizes (ROW_GELU_QUANT fused); the result is the down operand.
-            ck(launch_q8gemm_geglu(L.gu.tmap, tm_xq[0], L.gu.tscale, tm_xs[0], gemm_exact, gq, gs, CAP, N, L.gu.rows,
+            ck(launch_q8gemm_geglu(L.gu.tmap, tm_xq[0], L.gu.tscale, tm_xs[0], exact, gq, gs, CAP, N, L.gu.rows,
                                    L.gu.k, s),
                "GeGLU GEMM"),
                 ++launches;
             mark("gemm_geglu");
-            ck(launch_q8gemm(L.down.tmap, tm_gq, L.down.tscale, tm_gs, gemm_exact, h, 512, N, L.down.rows, L.down.k, s),
+            ck(launch_q8gemm(L.down.tmap, tm_gq, L.down.tscale, tm_gs, exact, h, 512, N, L.down.rows, L.down.k, s),
                "q8 GEMM"),
                 ++launches;
             mark("gemm_down");
@@ -548,10 +571,13 @@ Backend *as_backend(void *ctx) {
 }
 }  // namespace
 
-extern "C" void *ei_gemma2_kfd_create_on(const ei_gguf *g, int device, char *err, size_t len) {
+extern "C" void *eg2_b200_create(const ei_gguf *g, int device, unsigned flags, char *err, size_t len) {
     Backend *b = nullptr;
-    guarded(err, len, [&] { b = new Backend(g, device); });
+    guarded(err, len, [&] { b = new Backend(g, device, flags); });
     return b;
+}
+extern "C" void *ei_gemma2_kfd_create_on(const ei_gguf *g, int device, char *err, size_t len) {
+    return eg2_b200_create(g, device, 0u, err, len);
 }
 extern "C" void *ei_gemma2_kfd_create(const ei_gguf *g, char *err, size_t len) {
     const char *env = std::getenv("EG2_B200_DEVICE");

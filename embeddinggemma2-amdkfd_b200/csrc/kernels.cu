@@ -5,6 +5,7 @@
 
 #include "../../include/eg2_ops.h"
 #include "attention.cuh"
+#include "exact.cuh"
 #include "launch.h"
 #include "opsabi.cuh"
 #include "ple.cuh"
@@ -143,14 +144,38 @@ cudaError_t launch_norm_quant(int8_t *q, float *qs, int qs_stride, float *y, con
 }
 
 cudaError_t launch_qkv_post(void *q, void *k, void *v, const float *qkv, const float *qn, const float *kn,
-                            const float *rc, const float *rs, const unsigned *pos, int n, int d, cudaStream_t s) {
+                            const float *rc, const float *rs, const unsigned *pos, int n, int d, cudaStream_t s,
+                            bool f32_out) {
     if (n <= 0) return cudaSuccess;
     if (d != 256 && d != 512) return cudaErrorInvalidValue;
     const int rows_per_tok = 4 + 2 * (512 / d), warps = n * rows_per_tok;
     const dim3 grid((warps + 7) / 8), block(256);
+    if (f32_out) {
+        auto *qf = static_cast<float *>(q), *kf = static_cast<float *>(k), *vf = static_cast<float *>(v);
+        if (d == 256)
+            return launch_pdl(qkv_post_kernel<256, float>, grid, block, 0, s, qf, kf, vf, qkv, qn, kn, rc, rs, pos, n);
+        return launch_pdl(qkv_post_kernel<512, float>, grid, block, 0, s, qf, kf, vf, qkv, qn, kn, rc, rs, pos, n);
+    }
     auto *qh = static_cast<__half *>(q), *kh = static_cast<__half *>(k), *vh = static_cast<__half *>(v);
-    if (d == 256) return launch_pdl(qkv_post_kernel<256>, grid, block, 0, s, qh, kh, vh, qkv, qn, kn, rc, rs, pos, n);
-    return launch_pdl(qkv_post_kernel<512>, grid, block, 0, s, qh, kh, vh, qkv, qn, kn, rc, rs, pos, n);
+    if (d == 256) return launch_pdl(qkv_post_kernel<256, __half>, grid, block, 0, s, qh, kh, vh, qkv, qn, kn, rc, rs, pos, n);
+    return launch_pdl(qkv_post_kernel<512, __half>, grid, block, 0, s, qh, kh, vh, qkv, qn, kn, rc, rs, pos, n);
+}
+
+cudaError_t launch_attention_exact(float *out, const float *q, const float *k, const float *v, const unsigned *bounds,
+                                   int n, int d, int window, cudaStream_t s) {
+    if (n <= 0) return cudaSuccess;
+    if (n > 2048) return cudaErrorInvalidValue;  // key scores of one row live in shared memory
+    if (d == 256) return launch_pdl(attention_exact_kernel<256>, dim3(n, 4), dim3(128), 0, s, out, q, k, v, bounds, n, window);
+    if (d == 512) return launch_pdl(attention_exact_kernel<512>, dim3(n, 4), dim3(128), 0, s, out, q, k, v, bounds, n, window);
+    return cudaErrorInvalidValue;
+}
+
+cudaError_t launch_ple_exact(float *ple, const float *x, const void *w, const float *norm, int n, cudaStream_t s) {
+    if (n <= 0) return cudaSuccess;
+    if (cudaError_t e = launch_pdl(ple_exact_kernel, dim3(24 * 512 / PleExactCfg::BR, (n + PleExactCfg::BT - 1) / PleExactCfg::BT),
+                                   dim3(PleExactCfg::THREADS), 0, s, ple, x, static_cast<const uint16_t *>(w), n))
+        return e;
+    return launch_pdl(ple_norm_kernel, dim3(n * 24), dim3(128), 0, s, ple, norm);
 }
 
 template <int D>
@@ -345,7 +370,10 @@ int eg2_launch_q8_geglu(const EgQ8GeGLU *p, void *s) {
 }
 int eg2_launch_qkv_post(const EgQkvPost *p, void *s) {
     return rc(launch_qkv_post(p->q, p->k, p->v, p->qkv, p->q_norm, p->k_norm, p->rope_cos, p->rope_sin, p->pos,
-                              int(p->n), int(p->d), S(s)));
+                              int(p->n), int(p->d), S(s), false));
+}
+int eg2_launch_attention_exact(const EgAttention *p, unsigned d, void *s) {
+    return rc(launch_attention_exact(p->out, p->q, p->k, p->v, p->bounds, int(p->n), int(d), int(p->window), S(s)));
 }
 int eg2_launch_attention_f16(const EgAttentionF16 *p, void *s) {
     if (cudaError_t e = ensure_attributes()) return rc(e);

@@ -34,8 +34,14 @@ cudaError_t launch_ple(const CUtensorMap &hi, const CUtensorMap &lo, const CUten
 cudaError_t launch_embed(float *x, void *x_hi, void *x_lo, const void *emb, const int *ids, int n, cudaStream_t s);
 cudaError_t launch_norm_quant(int8_t *q, float *qs, int qs_stride, float *y, const float *x, const float *w, int rows,
                               int width, cudaStream_t s);
+// q/k/v outputs are fp16, or fp32 when f32_out (parity mode).
 cudaError_t launch_qkv_post(void *q, void *k, void *v, const float *qkv, const float *qn, const float *kn,
-                            const float *rc, const float *rs, const unsigned *pos, int n, int d, cudaStream_t s);
+                            const float *rc, const float *rs, const unsigned *pos, int n, int d, cudaStream_t s,
+                            bool f32_out);
+// Parity mode: the reference's scalar attention and PLE orders on CUDA cores.
+cudaError_t launch_attention_exact(float *out, const float *q, const float *k, const float *v, const unsigned *bounds,
+                                   int n, int d, int window, cudaStream_t s);
+cudaError_t launch_ple_exact(float *ple, const float *x, const void *w, const float *norm, int n, cudaStream_t s);
 cudaError_t launch_attention(float *out, const void *q, const void *k, const void *v, const unsigned *bounds, int n,
                              int d, int window, cudaStream_t s);
 cudaError_t launch_post_add(float *x, const float *h, const float *w, const float *scale, int8_t *q, float *qs,

@@ -120,8 +120,9 @@ __global__ void quant_rows_kernel(int8_t *__restrict__ q, float *__restrict__ qs
 // RoPE), then kv v heads (plain RMS).  RoPE: r[z] = a*c - b*s,
 // r[z+d/2] = a*s + b*c with host tables (gemma2_fast.c:672-679).  Each lane
 // handles 4 consecutive z of each half.
-template <int D>
-__global__ void qkv_post_kernel(__half *__restrict__ qo, __half *__restrict__ ko, __half *__restrict__ vo,
+// OutT is __half (the fast path's attention operands) or float (parity mode).
+template <int D, typename OutT>
+__global__ void qkv_post_kernel(OutT *__restrict__ qo, OutT *__restrict__ ko, OutT *__restrict__ vo,
                                 const float *__restrict__ qkv, const float *__restrict__ qn,
                                 const float *__restrict__ kn, const float *__restrict__ rc,
                                 const float *__restrict__ rs, const unsigned *__restrict__ pos, int n) {
@@ -133,7 +134,7 @@ __global__ void qkv_post_kernel(__half *__restrict__ qo, __half *__restrict__ ko
     const int t = gw / HR, hr = gw % HR;
     const float *src;
     const float *w;
-    __half *dst;
+    OutT *dst;
     bool rope = true;
     if (hr < 4) {
         src = qkv + size_t(t) * (4 * D + 1024) + hr * D, w = qn, dst = qo + (size_t(t) * 4 + hr) * D;
@@ -177,11 +178,17 @@ __global__ void qkv_post_kernel(__half *__restrict__ qo, __half *__restrict__ ko
                              __fadd_rn(__fmul_rn(ya.z, s.z), __fmul_rn(yb.z, c.z)),
                              __fadd_rn(__fmul_rn(ya.w, s.w), __fmul_rn(yb.w, c.w)));
         }
-        __half2 h0 = __floats2half2_rn(oa.x, oa.y), h1 = __floats2half2_rn(oa.z, oa.w);
-        __half2 h2 = __floats2half2_rn(ob.x, ob.y), h3 = __floats2half2_rn(ob.z, ob.w);
-        *reinterpret_cast<uint2 *>(dst + z) = make_uint2(*reinterpret_cast<uint32_t *>(&h0), *reinterpret_cast<uint32_t *>(&h1));
-        *reinterpret_cast<uint2 *>(dst + z + D / 2) =
-            make_uint2(*reinterpret_cast<uint32_t *>(&h2), *reinterpret_cast<uint32_t *>(&h3));
+        if constexpr (sizeof(OutT) == 4) {
+            *reinterpret_cast<float4 *>(dst + z) = oa;
+            *reinterpret_cast<float4 *>(dst + z + D / 2) = ob;
+        } else {
+            __half2 h0 = __floats2half2_rn(oa.x, oa.y), h1 = __floats2half2_rn(oa.z, oa.w);
+            __half2 h2 = __floats2half2_rn(ob.x, ob.y), h3 = __floats2half2_rn(ob.z, ob.w);
+            *reinterpret_cast<uint2 *>(dst + z) =
+                make_uint2(*reinterpret_cast<uint32_t *>(&h0), *reinterpret_cast<uint32_t *>(&h1));
+            *reinterpret_cast<uint2 *>(dst + z + D / 2) =
+                make_uint2(*reinterpret_cast<uint32_t *>(&h2), *reinterpret_cast<uint32_t *>(&h3));
+        }
     }
 }
 

@@ -18,6 +18,9 @@ MAX_TOKENS = 2048
 VOCAB = 262144
 
 
+EG2_B200_EXACT = 1  # include/eg2_executor.h
+
+
 class ExecutorError(RuntimeError):
     pass
 
@@ -73,11 +76,16 @@ class GGUFModel:
 class Gemma2Executor:
     """One packed-wave executor on one B200 (ei_gemma2_kfd_create_on)."""
 
-    def __init__(self, model: GGUFModel, device: int | None = None):
+    def __init__(self, model: GGUFModel, device: int | None = None, exact: bool = False):
+        """exact=True: parity mode (eg2_b200_create with EG2_B200_EXACT), every
+        operation in the reference CPU graph's own float order."""
         lib = _lib.load()
         self.model = model  # borrowed by the context: keep it alive
         err = _err()
-        if device is None:
+        if exact:
+            ctx = lib.eg2_b200_create(model.handle, 0 if device is None else int(device), EG2_B200_EXACT, err,
+                                      len(err))
+        elif device is None:
             ctx = lib.ei_gemma2_kfd_create(model.handle, err, len(err))
         else:
             ctx = lib.ei_gemma2_kfd_create_on(model.handle, int(device), err, len(err))

@@ -92,6 +92,11 @@ def qkv_post(q, k, v, qkv, q_norm, k_norm, rope_cos, rope_sin, pos, n, d):
                                                 _p(rope_cos), _p(rope_sin), _p(pos), n, d))
 
 
+def attention_exact(out, q, k, v, bounds, n, d, window):
+    """fp32 attention in the reference CPU graph's scalar order (parity mode)."""
+    _call("eg2_launch_attention_exact", _lib.EgAttention(_p(out), _p(q), _p(k), _p(v), _p(bounds), n, window), d)
+
+
 def attention_f16(out, q, k, v, bounds, n, d, window):
     _call("eg2_launch_attention_f16", _lib.EgAttentionF16(_p(out), _p(q), _p(k), _p(v), _p(bounds), n, d, window))
 

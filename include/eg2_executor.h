@@ -36,6 +36,15 @@ bool ei_gemma2_kfd_batch(void *ctx, const int32_t *ids, const size_t *offsets, s
  * one-executor-per-device routing (engine.c:1199-1220) needs. */
 void *ei_gemma2_kfd_create_on(const ei_gguf *g, int device, char *err, size_t len);
 
+/* ei_gemma2_kfd_create_on with options.  EG2_B200_EXACT selects parity mode:
+ * every operation in the reference CPU graph's own float order (GEMMs in the
+ * scalar tile's rounding, attention and the PLE projection on exact-order
+ * CUDA-core kernels instead of the fp16/bf16 tensor-core ones), for checking
+ * results against the reference; about 3x slower.  No counterpart in the
+ * reference's executor ABI. */
+#define EG2_B200_EXACT 1u
+void *eg2_b200_create(const ei_gguf *g, int device, unsigned flags, char *err, size_t len);
+
 /* The host-side checks of src/gemma2_kfd.cpp:270-278 alone (offsets, token
  * count, id range), with the same messages; no device work.  true = valid. */
 bool eg2_b200_validate(const int32_t *ids, const size_t *offsets, size_t batch, char *err, size_t len);

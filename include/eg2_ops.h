@@ -126,6 +126,11 @@ int eg2_launch_q8_mm(const EgQ8MM *p, void *stream);
 int eg2_launch_q8_geglu(const EgQ8GeGLU *p, void *stream);
 int eg2_launch_qkv_post(const EgQkvPost *p, void *stream);
 int eg2_launch_attention_f16(const EgAttentionF16 *p, void *stream);
+/* The reference CPU graph's scalar attention order on fp32 q/k/v
+ * (gemma2_fast.c:768-894 scalar branch, the executor's parity mode): one
+ * sequential dot per key, softmax with the C library's expf rounding, outputs
+ * summed in key order.  EgAttention fields as in Part 1; n <= 2048. */
+int eg2_launch_attention_exact(const EgAttention *p, unsigned d, void *stream);
 int eg2_launch_post_add(const EgPostAdd *p, void *stream);
 int eg2_launch_gate_quant(const EgGateQuant *p, void *stream);
 int eg2_launch_pool_l2(const EgPoolL2 *p, void *stream);

@@ -114,3 +114,34 @@ def test_matryoshka_prefixes_match_reference(eg2):
     for d in (128, 256, 512):
         assert np.array_equal(eg2.normalize_prefix(e, d), g[f"long_prefix_{d}"])
     assert np.array_equal(eg2.normalize_prefix(e, 768), e)
+
+
+def test_device_expf_matches_c_library(tmp_path):
+    """The expf the parity-mode attention evaluates (csrc/ref_expf.h, shared
+    with the device code) equals the C library's expf -- which the reference's
+    scalar attention calls -- on a strided sample of all float bit patterns
+    in (-inf, 0] (the full range was checked when the header was written)."""
+    src = tmp_path / "t.c"
+    src.write_text(r"""
+#include <stdio.h>
+#include "ref_expf.h"
+static const uint64_t tab[32] = {EG2_EXP2_TAB};
+int main(void) {
+    long long n = 0, bad = 0;
+    for (uint64_t u = 0x80000000u; u <= 0xFF800000u; u += 97) {
+        uint32_t b = (uint32_t)u; float x; memcpy(&x, &b, 4);
+        ++n;
+        float a = eg2_ref_expf(x, tab), r = expf(x);
+        if (memcmp(&a, &r, 4) != 0) { if (bad < 3) printf("x=%a %a %a\n", x, a, r); ++bad; }
+    }
+    printf("%lld %lld\n", n, bad);
+    return bad != 0;
+}
+""")
+    exe = tmp_path / "t"
+    subprocess.run(["gcc", "-O2", "-std=c11", "-I", os.path.join(ROOT, "embeddinggemma2-amdkfd_b200", "csrc"), str(src),
+                    "-o", str(exe), "-lm"], check=True)
+    out = subprocess.run([str(exe)], capture_output=True, text=True)
+    assert out.returncode == 0, out.stdout
+    n, bad = map(int, out.stdout.split()[-2:])
+    assert n > 20_000_000 and bad == 0

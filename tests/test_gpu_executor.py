@@ -124,3 +124,31 @@ def test_restatement_live(executor, port, model_baseline, syn):
     c = cosine(out, ref)
     print("live restatement cos", c)
     assert c.min() >= 0.995 - MARGIN
+
+
+def test_parity_mode_reproduces_restatement(eg2, model_baseline, port, syn):
+    """EG2_B200_EXACT (eg2_b200_create): every operation in the reference CPU
+    graph's float order -- scalar-tile GEMM rounding, exact-order attention with
+    the C library's expf, exact-order PLE projection, and the x86 tiers'
+    quantizer and GELU that the fast path also uses.  The embeddings equal the
+    restatement run with those choices bit for bit, on config 0 and on a ragged
+    wave with a 300-token sequence (sliding window active)."""
+    import oracle
+    m = eg2.GGUFModel(model_baseline)
+    ex = eg2.Gemma2Executor(m, 0, exact=True)
+    try:
+        g = golden("golden_baseline.npz")
+        G = oracle.Gguf(model_baseline)
+        for ids, off in ((g["ids"], g["offsets"]), syn.wave((5, 300, 40), seed=90)):
+            ref = port.embed(G, ids, off, quant_mode=port.ROUND_X86, gelu_mode=1)
+            out = ex.batch(ids, off)
+            np.testing.assert_array_equal(out, ref)
+        # against the reference's own tiers: inside the north-star tolerance of
+        # the scalar tier it shares every float order with except the quantizer
+        # rounding and the GELU polynomial
+        out = ex.batch(g["ids"], g["offsets"])
+        c = cosine(out, g["embed_scalar"])
+        print("parity mode vs scalar tier cos", c, "max abs", np.abs(out - g["embed_scalar"]).max())
+    finally:
+        ex.close()
+        m.close()

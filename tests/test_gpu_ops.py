@@ -342,6 +342,22 @@ def test_attention_f16_vs_reference_attention(ops, port, d, window, lengths):
     assert cosine(got.ravel(), ref.ravel()) > 0.99999
 
 
+@pytest.mark.parametrize("d,window,lengths", [(256, 512, [10, 700, 3]), (512, 0, [300, 64]), (256, 512, [1100])])
+def test_attention_exact_bit_identical(ops, port, d, window, lengths):
+    """Parity-mode attention: the reference's scalar loop order and the C
+    library's expf rounding give outputs identical to the restatement."""
+    rng = np.random.default_rng(d + sum(lengths) + 1)
+    n, kv = sum(lengths), 512 // d
+    q = (rng.standard_normal((n, 4, d)) * 0.3).astype(np.float32)
+    k = (rng.standard_normal((n, kv, d)) * 0.3).astype(np.float32)
+    v = rng.standard_normal((n, kv, d)).astype(np.float32)
+    lo, hi = _bounds(lengths)
+    ref = port.attention(q, k, v, lo, hi, kv, d, window)
+    out = torch.zeros(n * 4 * d, device=DEV)
+    ops.attention_exact(out, T(q), T(k), T(v), T(np.stack([lo, hi], 1).ravel()), n, d, window)
+    np.testing.assert_array_equal(host(out).reshape(n, 4 * d), ref.reshape(n, 4 * d))
+
+
 def test_embed_bit_exact(ops, model_baseline):
     import oracle
     g = oracle.Gguf(model_baseline)
