@@ -128,7 +128,7 @@ class EgPleProj(C.Structure):
 
 class EgNormQuant(C.Structure):
     _fields_ = [("q", P), ("scale", P), ("scale_stride", u32), ("y", P), ("x", P), ("weight", P),
-                ("rows", u32), ("width", u32)]
+                ("rows", u32), ("width", u32), ("tier", u32)]
 
 
 class EgQ8MM(C.Structure):
@@ -138,7 +138,7 @@ class EgQ8MM(C.Structure):
 
 class EgQ8GeGLU(C.Structure):
     _fields_ = [("q", P), ("scale", P), ("scale_stride", u32), ("xq", P), ("xs", P), ("xs_stride", u32), ("wq", P),
-                ("ws", P), ("n", u32), ("k", u32), ("m", u32), ("exact", u32)]
+                ("ws", P), ("n", u32), ("k", u32), ("m", u32), ("exact", u32), ("tier", u32)]
 
 
 class EgQkvPost(C.Structure):
@@ -153,12 +153,12 @@ class EgAttentionF16(C.Structure):
 
 class EgPostAdd(C.Structure):
     _fields_ = [("x", P), ("h", P), ("weight", P), ("scale", P), ("q", P), ("qscale", P),
-                ("scale_stride", u32), ("next_weight", P), ("rows", u32)]
+                ("scale_stride", u32), ("next_weight", P), ("rows", u32), ("tier", u32)]
 
 
 class EgGateQuant(C.Structure):
     _fields_ = [("q", P), ("scale", P), ("scale_stride", u32), ("x", P), ("other", P), ("rows", u32),
-                ("width", u32), ("other_stride", u32), ("other_offset", u32)]
+                ("width", u32), ("other_stride", u32), ("other_offset", u32), ("tier", u32)]
 
 
 class EgPoolL2(C.Structure):

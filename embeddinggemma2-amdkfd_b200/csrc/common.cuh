@@ -8,6 +8,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include "ref_tanhf.h"
+
 namespace eg2 {
 
 // Set by any bounded wait that ran out (see wait_bar); read by the host after a
@@ -249,10 +251,18 @@ __device__ __forceinline__ uint16_t ref_fp32_to_fp16(float f) {
 }
 __device__ __forceinline__ float fp16_bits_to_f32(uint16_t h) { return __half2float(__ushort_as_half(h)); }
 
-// Q8_0 code of x with id = 1/d: trunc(x*id +- 0.5) (gemma2_fast_x86.c:225-230).
-__device__ __forceinline__ uint32_t q8_code(float x, float id) {
+// Which of the reference's CPU tiers the quantizer rounding and the GELU follow:
+// TIER_X86 -- the x86 tiers (gemma2_fast_x86.c), the fast path's choice;
+// TIER_SCALAR -- the scalar tier (EI_GEMMA2_CPU_X86=scalar: quants.c rounding,
+// kernels.c tanhf GELU), selectable in parity mode.
+enum : int { TIER_X86 = 0, TIER_SCALAR = 1 };
+
+// Q8_0 code of x with id = 1/d: trunc(x*id +- 0.5) on the x86 tiers
+// (gemma2_fast_x86.c:225-230), roundf(x*id) on the scalar tier (quants.c:97-177
+// generic branch); both clamp to [-128, 127].
+__device__ __forceinline__ uint32_t q8_code(float x, float id, int tier = TIER_X86) {
     const float v = __fmul_rn(x, id);
-    int q = __float2int_rz(__fadd_rn(v, copysignf(0.5f, v)));
+    int q = tier == TIER_SCALAR ? int(roundf(v)) : __float2int_rz(__fadd_rn(v, copysignf(0.5f, v)));
     q = q < -128 ? -128 : (q > 127 ? 127 : q);
     return uint32_t(q) & 0xFFu;
 }
@@ -279,6 +289,16 @@ __device__ __forceinline__ float ref_gelu(float x) {
     inner = fminf(fmaxf(inner, -9.0f), 9.0f);
     const float t = __fsub_rn(1.0f, __fdiv_rn(2.0f, __fadd_rn(ref_exp8(__fmul_rn(2.0f, inner)), 1.0f)));
     return __fmul_rn(__fmul_rn(0.5f, x), __fadd_rn(1.0f, t));
+}
+// gelu_tanh(x) = 0.5 x (1 + tanh(0.7978845608 x (1 + 0.044715 x^2))) with the C
+// library's tanhf, in the scalar tier's operation order (kernels.c:367-371).
+__device__ __forceinline__ float ref_gelu_scalar(float x) {
+    const float inner = __fmul_rn(__fmul_rn(0.79788456080286535587989211986876f, x),
+                                  __fadd_rn(1.0f, __fmul_rn(__fmul_rn(0.044715f, x), x)));
+    return __fmul_rn(__fmul_rn(0.5f, x), __fadd_rn(1.0f, eg2_ref_tanhf(inner)));
+}
+__device__ __forceinline__ float gelu_tier(float x, int tier) {
+    return tier == TIER_SCALAR ? ref_gelu_scalar(x) : ref_gelu(x);
 }
 
 // RMS scale 1/sqrt(sum/d + 1e-6) from a double sum of squares rounded to

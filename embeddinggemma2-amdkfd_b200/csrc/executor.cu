@@ -112,6 +112,9 @@ struct Backend {
     // order, PLE projection and attention on the CUDA-core exact-order kernels
     // with fp32 q/k/v; every other kernel is bit-exact in both modes.
     bool exact = false;
+    // EG2_B200_SCALAR_TIER: the scalar CPU tier's quantizer rounding and GELU
+    // (roundf, tanhf) instead of the x86 tiers' (the fast path's choice).
+    int tier = 0;
     float *qf = nullptr, *kf = nullptr, *vf = nullptr;
 
     // host staging (pinned)
@@ -195,7 +198,8 @@ struct Backend {
             throw std::runtime_error("cuTensorMapEncodeTiled failed for a weight");
     }
 
-    Backend(const ei_gguf *g, int dev, unsigned flags) : model(g), device(dev), exact(flags & EG2_B200_EXACT) {
+    Backend(const ei_gguf *g, int dev, unsigned flags)
+        : model(g), device(dev), exact(flags & EG2_B200_EXACT), tier(flags & EG2_B200_SCALAR_TIER ? 1 : 0) {
         if (!g) throw std::runtime_error("empty model");
         // gemma2.c:30-62 hyperparameters.
         if (kv_u64("gemma-embedding2.block_count") != 24 || kv_u64("gemma-embedding2.embedding_length") != 512 ||
@@ -367,7 +371,7 @@ struct Backend {
         else
             ck(launch_ple(tm_hi, tm_lo, tm_ple, ple, ple_norm, N, s), "PLE"), ++launches;
         mark("ple_proj");
-        ck(launch_norm_quant(xq, xs, CAP, nullptr, x, layers[0].attn_norm, N, 512, s), "norm"), ++launches;
+        ck(launch_norm_quant(xq, xs, CAP, nullptr, x, layers[0].attn_norm, N, 512, s, tier), "norm"), ++launches;
         mark("norm_quant");
         for (int l = 0; l < 24; ++l) {
             const Layer &L = layers[l];
@@ -392,16 +396,16 @@ struct Backend {
                     ++launches;
             }
             mark(L.d == 512 ? "attention_global" : "attention_local");
-            ck(launch_norm_quant(xq, xs, CAP, nullptr, attn, nullptr, N, 4 * L.d, s), "quant"), ++launches;
+            ck(launch_norm_quant(xq, xs, CAP, nullptr, attn, nullptr, N, 4 * L.d, s, tier), "quant"), ++launches;
             mark("quant_attn");
             gemm(L.o, h, 512, N, s), ++launches;
             mark("gemm_o");
-            ck(launch_post_add(x, h, L.post_attn_norm, nullptr, xq, xs, CAP, L.ffn_norm, N, s), "post_add"), ++launches;
+            ck(launch_post_add(x, h, L.post_attn_norm, nullptr, xq, xs, CAP, L.ffn_norm, N, s, tier), "post_add"), ++launches;
             mark("post_add");
             // ffn_gate and ffn_up in one GEMM whose epilogue applies gelu(gate) * up
             // and quantizes (ROW_GELU_QUANT fused); the result is the down operand.
             ck(launch_q8gemm_geglu(L.gu.tmap, tm_xq[0], L.gu.tscale, tm_xs[0], exact, gq, gs, CAP, N, L.gu.rows,
-                                   L.gu.k, s),
+                                   L.gu.k, s, tier),
                "GeGLU GEMM"),
                 ++launches;
             mark("gemm_geglu");
@@ -409,16 +413,16 @@ struct Backend {
                "q8 GEMM"),
                 ++launches;
             mark("gemm_down");
-            ck(launch_post_add(x, h, L.post_ffw_norm, nullptr, xq, xs, CAP, nullptr, N, s), "post_add"), ++launches;
+            ck(launch_post_add(x, h, L.post_ffw_norm, nullptr, xq, xs, CAP, nullptr, N, s, tier), "post_add"), ++launches;
             mark("post_add");
             gemm(L.inp_gate, h, 512, N, s), ++launches;
             mark("gemm_inp_gate");
-            ck(launch_gate_quant(xq, xs, CAP, h, ple, N, 512, 24 * 512, l * 512, s), "ple gate"), ++launches;
+            ck(launch_gate_quant(xq, xs, CAP, h, ple, N, 512, 24 * 512, l * 512, s, tier), "ple gate"), ++launches;
             mark("ple_gate_quant");
             gemm(L.proj, h, 512, N, s), ++launches;
             mark("gemm_proj");
             const float *next = l + 1 < 24 ? layers[l + 1].attn_norm : output_norm;
-            ck(launch_post_add(x, h, L.post_norm, L.out_scale, xq, xs, CAP, next, N, s), "post_add"), ++launches;
+            ck(launch_post_add(x, h, L.post_norm, L.out_scale, xq, xs, CAP, next, N, s, tier), "post_add"), ++launches;
             mark("post_add");
         }
         gemm(output, y, 768, N, s), ++launches;

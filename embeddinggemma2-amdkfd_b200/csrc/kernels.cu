@@ -103,11 +103,11 @@ cudaError_t launch_q8gemm(const CUtensorMap &w, const CUtensorMap &x, const CUte
 }
 cudaError_t launch_q8gemm_geglu(const CUtensorMap &w, const CUtensorMap &x, const CUtensorMap &sw,
                                 const CUtensorMap &sx, bool exact, int8_t *q8, float *q8s, int q8s_stride, int T, int R,
-                                int K, cudaStream_t s) {
+                                int K, cudaStream_t s, int tier) {
     if (T <= 0) return cudaSuccess;
     if (K <= 0 || K % 128 || K > 2048 || R <= 0 || R % Q8Cfg::BM || q8s_stride < T || !q8 || !q8s)
         return cudaErrorInvalidValue;
-    Q8GemmParams p{nullptr, 0, T, R, K, (T + Q8Cfg::BN - 1) / Q8Cfg::BN, 0, q8, q8s, q8s_stride};
+    Q8GemmParams p{nullptr, 0, T, R, K, (T + Q8Cfg::BN - 1) / Q8Cfg::BN, 0, q8, q8s, q8s_stride, tier};
     p.num_tiles = (R / Q8Cfg::BM) * p.tiles_t;
     return exact ? q8gemm_go<true, true>(w, x, sw, sx, p, s) : q8gemm_go<false, true>(w, x, sw, sx, p, s);
 }
@@ -127,19 +127,22 @@ cudaError_t launch_embed(float *x, void *x_hi, void *x_lo, const void *emb, cons
 }
 
 cudaError_t launch_norm_quant(int8_t *q, float *qs, int qs_stride, float *y, const float *x, const float *w, int rows,
-                              int width, cudaStream_t s) {
+                              int width, cudaStream_t s, int tier) {
     if (rows <= 0) return cudaSuccess;
     if (qs_stride < rows) return cudaErrorInvalidValue;
     if (width != 256 && width != 512 && width != 1024 && width != 2048) return cudaErrorInvalidValue;
     if (!w) {  // ROW_QUANT: no row reduction, warp per (row, four blocks)
         const int warps = rows * (width / 128);
-        return launch_pdl(quant_rows_kernel, dim3((warps + 7) / 8), dim3(256), 0, s, q, qs, qs_stride, x, rows, width);
+        return launch_pdl(quant_rows_kernel, dim3((warps + 7) / 8), dim3(256), 0, s, q, qs, qs_stride, x, rows, width,
+                          tier);
     }
     switch (width) {  // ROW_NORM_QUANT: CTA per row, one float4 per thread
-        case 256: return launch_pdl(norm_quant_kernel<256>, dim3(rows), dim3(64), 0, s, q, qs, qs_stride, y, x, w);
-        case 512: return launch_pdl(norm_quant_kernel<512>, dim3(rows), dim3(128), 0, s, q, qs, qs_stride, y, x, w);
-        case 1024: return launch_pdl(norm_quant_kernel<1024>, dim3(rows), dim3(256), 0, s, q, qs, qs_stride, y, x, w);
-        default: return launch_pdl(norm_quant_kernel<2048>, dim3(rows), dim3(512), 0, s, q, qs, qs_stride, y, x, w);
+        case 256: return launch_pdl(norm_quant_kernel<256>, dim3(rows), dim3(64), 0, s, q, qs, qs_stride, y, x, w, tier);
+        case 512: return launch_pdl(norm_quant_kernel<512>, dim3(rows), dim3(128), 0, s, q, qs, qs_stride, y, x, w, tier);
+        case 1024:
+            return launch_pdl(norm_quant_kernel<1024>, dim3(rows), dim3(256), 0, s, q, qs, qs_stride, y, x, w, tier);
+        default:
+            return launch_pdl(norm_quant_kernel<2048>, dim3(rows), dim3(512), 0, s, q, qs, qs_stride, y, x, w, tier);
     }
 }
 
@@ -194,21 +197,21 @@ cudaError_t launch_attention(float *out, const void *q, const void *k, const voi
 }
 
 cudaError_t launch_post_add(float *x, const float *h, const float *w, const float *scale, int8_t *q, float *qs,
-                            int qs_stride, const float *next_w, int rows, cudaStream_t s) {
+                            int qs_stride, const float *next_w, int rows, cudaStream_t s, int tier) {
     if (rows <= 0) return cudaSuccess;
     if (qs_stride < rows) return cudaErrorInvalidValue;
-    return launch_pdl(post_add_kernel, dim3(rows), dim3(128), 0, s, x, h, w, scale, q, qs, qs_stride, next_w);
+    return launch_pdl(post_add_kernel, dim3(rows), dim3(128), 0, s, x, h, w, scale, q, qs, qs_stride, next_w, tier);
 }
 
 cudaError_t launch_gate_quant(int8_t *q, float *qs, int qs_stride, const float *x, const float *other, int rows,
-                              int width, int other_stride, int other_offset, cudaStream_t s) {
+                              int width, int other_stride, int other_offset, cudaStream_t s, int tier) {
     if (rows <= 0) return cudaSuccess;
     if (width <= 0 || width % 128 || qs_stride < rows || other_stride % 4 || other_offset % 4 ||
         other_offset + width > other_stride)
         return cudaErrorInvalidValue;
     const int warps = rows * (width / 128);
     return launch_pdl(gate_quant_kernel, dim3((warps + 7) / 8), dim3(256), 0, s, q, qs, qs_stride, x, other, rows, width,
-                      other_stride, other_offset);
+                      other_stride, other_offset, tier);
 }
 
 cudaError_t launch_pool_l2(float *out, const float *y, const unsigned *offsets, int batch, int width, cudaStream_t s) {
@@ -339,7 +342,7 @@ int eg2_launch_ple_proj(const EgPleProj *p, void *s) {
 }
 int eg2_launch_norm_quant(const EgNormQuant *p, void *s) {
     return rc(launch_norm_quant(p->q, p->scale, int(p->scale_stride), p->y, p->x, p->weight, int(p->rows),
-                                int(p->width), S(s)));
+                                int(p->width), S(s), int(p->tier)));
 }
 int eg2_launch_q8_mm(const EgQ8MM *p, void *s) {
     if (cudaError_t e = ensure_attributes()) return rc(e);
@@ -366,7 +369,7 @@ int eg2_launch_q8_geglu(const EgQ8GeGLU *p, void *s) {
         !scale_tmap(&sx, p->xs, p->xs_stride, p->k / 32, uint32_t(Q8Cfg::BN)))
         return rc(cudaErrorInvalidValue);
     return rc(launch_q8gemm_geglu(w, x, sw, sx, p->exact != 0, p->q, p->scale, int(p->scale_stride), int(p->n),
-                                  int(rows), int(p->k), S(s)));
+                                  int(rows), int(p->k), S(s), int(p->tier)));
 }
 int eg2_launch_qkv_post(const EgQkvPost *p, void *s) {
     return rc(launch_qkv_post(p->q, p->k, p->v, p->qkv, p->q_norm, p->k_norm, p->rope_cos, p->rope_sin, p->pos,
@@ -381,11 +384,11 @@ int eg2_launch_attention_f16(const EgAttentionF16 *p, void *s) {
 }
 int eg2_launch_post_add(const EgPostAdd *p, void *s) {
     return rc(launch_post_add(p->x, p->h, p->weight, p->scale, p->q, p->qscale, int(p->scale_stride), p->next_weight,
-                              int(p->rows), S(s)));
+                              int(p->rows), S(s), int(p->tier)));
 }
 int eg2_launch_gate_quant(const EgGateQuant *p, void *s) {
     return rc(launch_gate_quant(p->q, p->scale, int(p->scale_stride), p->x, p->other, int(p->rows), int(p->width),
-                                int(p->other_stride), int(p->other_offset), S(s)));
+                                int(p->other_stride), int(p->other_offset), S(s), int(p->tier)));
 }
 int eg2_launch_pool_l2(const EgPoolL2 *p, void *s) {
     return rc(launch_pool_l2(p->out, p->y, p->offsets, int(p->batch), int(p->width), S(s)));

@@ -16,7 +16,9 @@ bool bf16_tmap(CUtensorMap *map, const void *base, uint64_t k, uint64_t rows, ui
 // Block-major fp32 scale plane [kb][stride]: box box_cols x kb, no swizzle.
 bool scale_tmap(CUtensorMap *map, const float *base, uint64_t stride, uint64_t kb, uint32_t box_cols);
 
-// Kernel launches (all asynchronous on `s`).
+// Kernel launches (all asynchronous on `s`).  `tier` (TIER_X86 / TIER_SCALAR
+// in common.cuh) selects the quantizer rounding and GELU of the reference tier
+// to reproduce.
 // out[T][ldo] = tokens x weight rows.  Maps: weight codes [R][K] with box
 // 128 rows, token codes [T][K] with box 64 rows, weight scales [K/32][R] box
 // 128, token scales [K/32][stride] box 64.  R must be a multiple of 128.
@@ -28,12 +30,12 @@ cudaError_t launch_q8gemm(const CUtensorMap &w, const CUtensorMap &x, const CUte
 // 64c..); writes Q8_0 codes [T][R/2] of gelu(gate) * up and block-major scales.
 cudaError_t launch_q8gemm_geglu(const CUtensorMap &w, const CUtensorMap &x, const CUtensorMap &sw,
                                 const CUtensorMap &sx, bool exact, int8_t *q8, float *q8s, int q8s_stride, int T, int R,
-                                int K, cudaStream_t s);
+                                int K, cudaStream_t s, int tier = 0);
 cudaError_t launch_ple(const CUtensorMap &hi, const CUtensorMap &lo, const CUtensorMap &w, float *ple,
                        const float *norm, int M, cudaStream_t s);
 cudaError_t launch_embed(float *x, void *x_hi, void *x_lo, const void *emb, const int *ids, int n, cudaStream_t s);
 cudaError_t launch_norm_quant(int8_t *q, float *qs, int qs_stride, float *y, const float *x, const float *w, int rows,
-                              int width, cudaStream_t s);
+                              int width, cudaStream_t s, int tier = 0);
 // q/k/v outputs are fp16, or fp32 when f32_out (parity mode).
 cudaError_t launch_qkv_post(void *q, void *k, void *v, const float *qkv, const float *qn, const float *kn,
                             const float *rc, const float *rs, const unsigned *pos, int n, int d, cudaStream_t s,
@@ -45,9 +47,9 @@ cudaError_t launch_ple_exact(float *ple, const float *x, const void *w, const fl
 cudaError_t launch_attention(float *out, const void *q, const void *k, const void *v, const unsigned *bounds, int n,
                              int d, int window, cudaStream_t s);
 cudaError_t launch_post_add(float *x, const float *h, const float *w, const float *scale, int8_t *q, float *qs,
-                            int qs_stride, const float *next_w, int rows, cudaStream_t s);
+                            int qs_stride, const float *next_w, int rows, cudaStream_t s, int tier = 0);
 cudaError_t launch_gate_quant(int8_t *q, float *qs, int qs_stride, const float *x, const float *other, int rows,
-                              int width, int other_stride, int other_offset, cudaStream_t s);
+                              int width, int other_stride, int other_offset, cudaStream_t s, int tier = 0);
 cudaError_t launch_pool_l2(float *out, const float *y, const unsigned *offsets, int batch, int width, cudaStream_t s);
 // chunk > 0: rows interleaved with another matrix in chunk-row blocks, this
 // one at position `phase` (0 or 1) of each pair.

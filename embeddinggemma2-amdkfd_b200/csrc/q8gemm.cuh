@@ -56,6 +56,7 @@ struct Q8GemmParams {
     int8_t *q8;   // GeGLU mode: Q8_0 codes [T][R/2] of gelu(gate) * up
     float *q8s;   // and their block-major scales, q8s[b * q8s_stride + t]
     int q8s_stride;
+    int tier;     // GeGLU mode: TIER_X86 or TIER_SCALAR GELU and quantizer rounding
 };
 
 struct Q8Cfg {
@@ -320,7 +321,7 @@ __global__ void __launch_bounds__(Q8Cfg::THREADS, 1)
                 float amax = 0.0f;
 #pragma unroll
                 for (int j = 0; j < 16; ++j) {
-                    g[j] = __fmul_rn(ref_gelu(gr[j]), gr[64 + j]);
+                    g[j] = __fmul_rn(gelu_tier(gr[j], p.tier), gr[64 + j]);
                     amax = fmaxf(amax, fabsf(g[j]));
                 }
                 amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
@@ -330,8 +331,8 @@ __global__ void __launch_bounds__(Q8Cfg::THREADS, 1)
                     uint32_t w4[4];
 #pragma unroll
                     for (int j = 0; j < 4; ++j)
-                        w4[j] = q8_code(g[4 * j], id) | q8_code(g[4 * j + 1], id) << 8 |
-                                q8_code(g[4 * j + 2], id) << 16 | q8_code(g[4 * j + 3], id) << 24;
+                        w4[j] = q8_code(g[4 * j], id, p.tier) | q8_code(g[4 * j + 1], id, p.tier) << 8 |
+                                q8_code(g[4 * j + 2], id, p.tier) << 16 | q8_code(g[4 * j + 3], id, p.tier) << 24;
                     *reinterpret_cast<uint4 *>(p.q8 + size_t(t) * (p.R / 2) + col0 + cb * 32 + part * 16) =
                         make_uint4(w4[0], w4[1], w4[2], w4[3]);
                     if (part == 0) p.q8s[size_t(col0 / 32 + cb) * p.q8s_stride + t] = fp16_bits_to_f32(ref_fp32_to_fp16(d));

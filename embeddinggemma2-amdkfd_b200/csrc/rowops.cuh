@@ -45,14 +45,15 @@ __global__ void embed_kernel(float *__restrict__ x, __nv_bfloat16 *__restrict__ 
 // (gemma2_fast_x86.c:211-234): d = amax/127 (IEEE), the scale stored is the
 // reference's fp16 rounding of d, id = 1/d.  Returns the lane's four codes;
 // *scale_out receives the widened fp16 scale (uniform over the group).
-__device__ __forceinline__ uint32_t quant_oct(const float4 v, float *scale_out) {
+__device__ __forceinline__ uint32_t quant_oct(const float4 v, float *scale_out, int tier) {
     float amax = fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
 #pragma unroll
     for (int o = 1; o < 8; o <<= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
     const float d = __fdiv_rn(amax, 127.0f);
     const float id = d != 0.0f ? __fdiv_rn(1.0f, d) : 0.0f;
     *scale_out = fp16_bits_to_f32(ref_fp32_to_fp16(d));
-    return q8_code(v.x, id) | q8_code(v.y, id) << 8 | q8_code(v.z, id) << 16 | q8_code(v.w, id) << 24;
+    return q8_code(v.x, id, tier) | q8_code(v.y, id, tier) << 8 | q8_code(v.z, id, tier) << 16 |
+           q8_code(v.w, id, tier) << 24;
 }
 __device__ __forceinline__ double sumsq4(double ss, const float4 v) {
     ss = __dadd_rn(ss, __dmul_rn(double(v.x), double(v.x)));
@@ -84,7 +85,7 @@ template <int WIDTH>
 __global__ void __launch_bounds__(WIDTH / 4) norm_quant_kernel(int8_t *__restrict__ q, float *__restrict__ qs,
                                                                int qs_stride, float *__restrict__ y,
                                                                const float *__restrict__ x,
-                                                               const float *__restrict__ w) {
+                                                               const float *__restrict__ w, int tier) {
     pdl_wait();
     pdl_trigger();
     constexpr int WARPS = WIDTH / 128;
@@ -95,14 +96,14 @@ __global__ void __launch_bounds__(WIDTH / 4) norm_quant_kernel(int8_t *__restric
     v = scale_w4(v, sc, reinterpret_cast<const float4 *>(w)[i]);
     if (y) reinterpret_cast<float4 *>(y + size_t(t) * WIDTH)[i] = v;
     float s;
-    reinterpret_cast<uint32_t *>(q + size_t(t) * WIDTH)[i] = quant_oct(v, &s);
+    reinterpret_cast<uint32_t *>(q + size_t(t) * WIDTH)[i] = quant_oct(v, &s, tier);
     if ((lane & 7) == 0) qs[size_t(i >> 3) * qs_stride + t] = s;
 }
 
 // ROW_QUANT (gemma2_fast.c:728-730): Q8_0 of rows of width `width` (a multiple
 // of 128).  Warp per (row, four blocks).
 __global__ void quant_rows_kernel(int8_t *__restrict__ q, float *__restrict__ qs, int qs_stride,
-                                  const float *__restrict__ x, int rows, int width) {
+                                  const float *__restrict__ x, int rows, int width, int tier) {
     pdl_wait();
     pdl_trigger();
     const int steps = width / 128;
@@ -111,7 +112,7 @@ __global__ void quant_rows_kernel(int8_t *__restrict__ q, float *__restrict__ qs
     const int t = gw / steps, st = gw % steps;
     const size_t c = size_t(t) * (width / 4) + st * 32 + lane;
     float s;
-    reinterpret_cast<uint32_t *>(q)[c] = quant_oct(reinterpret_cast<const float4 *>(x)[c], &s);
+    reinterpret_cast<uint32_t *>(q)[c] = quant_oct(reinterpret_cast<const float4 *>(x)[c], &s, tier);
     if ((lane & 7) == 0) qs[size_t(4 * st + (lane >> 3)) * qs_stride + t] = s;
 }
 
@@ -199,7 +200,7 @@ __global__ void qkv_post_kernel(OutT *__restrict__ qo, OutT *__restrict__ ko, Ou
 __global__ void __launch_bounds__(128) post_add_kernel(float *__restrict__ x, const float *__restrict__ h,
                                                        const float *__restrict__ w, const float *__restrict__ scale,
                                                        int8_t *__restrict__ q, float *__restrict__ qs, int qs_stride,
-                                                       const float *__restrict__ next_w) {
+                                                       const float *__restrict__ next_w, int tier) {
     pdl_wait();
     pdl_trigger();
     __shared__ double red[2][4];
@@ -218,7 +219,7 @@ __global__ void __launch_bounds__(128) post_add_kernel(float *__restrict__ x, co
         xv = scale_w4(xv, sc2, reinterpret_cast<const float4 *>(next_w)[i]);
     }
     float s;
-    reinterpret_cast<uint32_t *>(q + size_t(t) * 512)[i] = quant_oct(xv, &s);
+    reinterpret_cast<uint32_t *>(q + size_t(t) * 512)[i] = quant_oct(xv, &s, tier);
     if ((lane & 7) == 0) qs[size_t(i >> 3) * qs_stride + t] = s;
 }
 
@@ -227,7 +228,7 @@ __global__ void __launch_bounds__(128) post_add_kernel(float *__restrict__ x, co
 // other_stride and other_offset are multiples of 128, 4 and 4.
 __global__ void gate_quant_kernel(int8_t *__restrict__ q, float *__restrict__ qs, int qs_stride,
                                   const float *__restrict__ x, const float *__restrict__ other, int rows, int width,
-                                  int other_stride, int other_offset) {
+                                  int other_stride, int other_offset, int tier) {
     pdl_wait();
     pdl_trigger();
     constexpr int PER = 1;  // float4 steps (4 blocks each) per warp
@@ -245,10 +246,12 @@ __global__ void gate_quant_kernel(int8_t *__restrict__ q, float *__restrict__ qs
 #pragma unroll
     for (int i = 0; i < PER; ++i) {
         if (i0 + i >= steps) break;  // warp-uniform
-        const float4 g = make_float4(__fmul_rn(ref_gelu(xv[i].x), ov[i].x), __fmul_rn(ref_gelu(xv[i].y), ov[i].y),
-                                     __fmul_rn(ref_gelu(xv[i].z), ov[i].z), __fmul_rn(ref_gelu(xv[i].w), ov[i].w));
+        const float4 g = make_float4(__fmul_rn(gelu_tier(xv[i].x, tier), ov[i].x),
+                                     __fmul_rn(gelu_tier(xv[i].y, tier), ov[i].y),
+                                     __fmul_rn(gelu_tier(xv[i].z, tier), ov[i].z),
+                                     __fmul_rn(gelu_tier(xv[i].w, tier), ov[i].w));
         float sc;
-        qr[(i0 + i) * 32 + lane] = quant_oct(g, &sc);
+        qr[(i0 + i) * 32 + lane] = quant_oct(g, &sc, tier);
         if ((lane & 7) == 0) qs[size_t(4 * (i0 + i) + (lane >> 3)) * qs_stride + t] = sc;
     }
 }

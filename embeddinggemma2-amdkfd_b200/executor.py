@@ -18,7 +18,7 @@ MAX_TOKENS = 2048
 VOCAB = 262144
 
 
-EG2_B200_EXACT = 1  # include/eg2_executor.h
+EG2_B200_EXACT, EG2_B200_SCALAR_TIER = 1, 2  # include/eg2_executor.h
 
 
 class ExecutorError(RuntimeError):
@@ -76,15 +76,19 @@ class GGUFModel:
 class Gemma2Executor:
     """One packed-wave executor on one B200 (ei_gemma2_kfd_create_on)."""
 
-    def __init__(self, model: GGUFModel, device: int | None = None, exact: bool = False):
+    def __init__(self, model: GGUFModel, device: int | None = None, exact: bool = False, tier: str = "x86"):
         """exact=True: parity mode (eg2_b200_create with EG2_B200_EXACT), every
-        operation in the reference CPU graph's own float order."""
+        operation in the reference CPU graph's own float order; tier="scalar"
+        adds the scalar CPU tier's quantizer rounding and GELU
+        (EG2_B200_SCALAR_TIER), so the wave reproduces that tier."""
         lib = _lib.load()
         self.model = model  # borrowed by the context: keep it alive
         err = _err()
+        if tier not in ("x86", "scalar"):
+            raise ValueError("tier must be 'x86' or 'scalar'")
         if exact:
-            ctx = lib.eg2_b200_create(model.handle, 0 if device is None else int(device), EG2_B200_EXACT, err,
-                                      len(err))
+            flags = EG2_B200_EXACT | (EG2_B200_SCALAR_TIER if tier == "scalar" else 0)
+            ctx = lib.eg2_b200_create(model.handle, 0 if device is None else int(device), flags, err, len(err))
         elif device is None:
             ctx = lib.ei_gemma2_kfd_create(model.handle, err, len(err))
         else:

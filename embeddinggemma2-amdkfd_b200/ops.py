@@ -73,18 +73,18 @@ def ple_proj(ple, x_hi, x_lo, weight, norm_w, n):
     _call("eg2_launch_ple_proj", _lib.EgPleProj(_p(ple), _p(x_hi), _p(x_lo), _p(weight), _p(norm_w), n))
 
 
-def norm_quant(q, scale, scale_stride, x, weight, rows, width, y=None):
+def norm_quant(q, scale, scale_stride, x, weight, rows, width, y=None, tier=0):
     _call("eg2_launch_norm_quant", _lib.EgNormQuant(_p(q), _p(scale), scale_stride, _p(y), _p(x), _p(weight),
-                                                    rows, width))
+                                                    rows, width, tier))
 
 
 def q8_mm(out, xq, xs, xs_stride, wq, ws, n, k, m, exact=False):
     _call("eg2_launch_q8_mm", _lib.EgQ8MM(_p(out), _p(xq), _p(xs), xs_stride, _p(wq), _p(ws), n, k, m, int(exact)))
 
 
-def q8_geglu(q, scale, scale_stride, xq, xs, xs_stride, wq, ws, n, k, m, exact=False):
+def q8_geglu(q, scale, scale_stride, xq, xs, xs_stride, wq, ws, n, k, m, exact=False, tier=0):
     _call("eg2_launch_q8_geglu", _lib.EgQ8GeGLU(_p(q), _p(scale), scale_stride, _p(xq), _p(xs), xs_stride, _p(wq),
-                                                _p(ws), n, k, m, int(exact)))
+                                                _p(ws), n, k, m, int(exact), tier))
 
 
 def qkv_post(q, k, v, qkv, q_norm, k_norm, rope_cos, rope_sin, pos, n, d):
@@ -101,14 +101,14 @@ def attention_f16(out, q, k, v, bounds, n, d, window):
     _call("eg2_launch_attention_f16", _lib.EgAttentionF16(_p(out), _p(q), _p(k), _p(v), _p(bounds), n, d, window))
 
 
-def post_add(x, h, weight, scale, q, qscale, scale_stride, next_weight, rows):
+def post_add(x, h, weight, scale, q, qscale, scale_stride, next_weight, rows, tier=0):
     _call("eg2_launch_post_add", _lib.EgPostAdd(_p(x), _p(h), _p(weight), _p(scale), _p(q), _p(qscale),
-                                                scale_stride, _p(next_weight), rows))
+                                                scale_stride, _p(next_weight), rows, tier))
 
 
-def gate_quant(q, scale, scale_stride, x, other, rows, width, other_stride, other_offset):
+def gate_quant(q, scale, scale_stride, x, other, rows, width, other_stride, other_offset, tier=0):
     _call("eg2_launch_gate_quant", _lib.EgGateQuant(_p(q), _p(scale), scale_stride, _p(x), _p(other), rows, width,
-                                                    other_stride, other_offset))
+                                                    other_stride, other_offset, tier))
 
 
 def pool_l2(out, y, offsets, batch, width):

@@ -43,6 +43,10 @@ void *ei_gemma2_kfd_create_on(const ei_gguf *g, int device, char *err, size_t le
  * results against the reference; about 3x slower.  No counterpart in the
  * reference's executor ABI. */
 #define EG2_B200_EXACT 1u
+/* With EG2_B200_EXACT: the quantizer rounding (roundf) and GELU (tanhf) of the
+ * reference's scalar CPU tier (EI_GEMMA2_CPU_X86=scalar) instead of the x86
+ * tiers' (trunc(x +- 0.5), exp polynomial), which the fast path uses. */
+#define EG2_B200_SCALAR_TIER 2u
 void *eg2_b200_create(const ei_gguf *g, int device, unsigned flags, char *err, size_t len);
 
 /* The host-side checks of src/gemma2_kfd.cpp:270-278 alone (offsets, token

@@ -49,6 +49,7 @@ typedef struct { float *ple; const uint16_t *x_hi, *x_lo, *weight; const float *
 typedef struct {
     int8_t *q; float *scale; unsigned scale_stride; float *y;
     const float *x, *weight; unsigned rows, width;
+    unsigned tier; /* 0: x86 tiers' quantizer rounding, 1: scalar tier's (roundf) */
 } EgNormQuant;
 /* out[t][r] = sum_b (int32 dot of block b) * xs[b][t] * ws[b][r]
  * (gemma2_fast.c:242-253): tcgen05 kind::i8, int32 block accumulators in TMEM.
@@ -72,6 +73,7 @@ typedef struct {
     int8_t *q; float *scale; unsigned scale_stride;
     const int8_t *xq; const float *xs; unsigned xs_stride;
     const int8_t *wq; const float *ws; unsigned n, k, m, exact;
+    unsigned tier; /* as in EgGateQuant */
 } EgQ8GeGLU;
 /* Per head RMS (q, k weighted; v plain) and NEOX RoPE from host tables at the
  * token's in-sequence position (ROW_QKV_POST, gemma2_fast.c:692-706).  qkv is
@@ -93,6 +95,7 @@ typedef struct {
 typedef struct {
     float *x; const float *h, *weight, *scale;
     int8_t *q; float *qscale; unsigned scale_stride; const float *next_weight; unsigned rows;
+    unsigned tier; /* as in EgNormQuant */
 } EgPostAdd;
 /* g = gelu_tanh(x[t][z]) * other[t * other_stride + other_offset + z], then Q8
  * (ROW_GELU_QUANT / ROW_PLE_GATE_QUANT, gemma2_fast.c:714-727).  width % 128
@@ -100,6 +103,7 @@ typedef struct {
 typedef struct {
     int8_t *q; float *scale; unsigned scale_stride;
     const float *x, *other; unsigned rows, width, other_stride, other_offset;
+    unsigned tier; /* 0: x86 tiers' GELU and rounding, 1: scalar tier's (tanhf, roundf) */
 } EgGateQuant;
 /* out[s] = L2(mean over the sequence's rows of y) (gemma2_fast.c:1000-1008). */
 typedef struct { float *out; const float *y; const unsigned *offsets; unsigned batch, width; } EgPoolL2;

@@ -145,3 +145,36 @@ int main(void) {
     assert out.returncode == 0, out.stdout
     n, bad = map(int, out.stdout.split()[-2:])
     assert n > 20_000_000 and bad == 0
+
+
+def test_device_tanhf_matches_c_library(tmp_path):
+    """The tanhf of the scalar-tier GELU (csrc/ref_tanhf.h, shared with the
+    device code) equals the C library's tanhf -- which the reference's scalar
+    tier calls -- on a strided sample of all finite floats of both signs (the
+    full range was checked when the header was written)."""
+    src = tmp_path / "t.c"
+    src.write_text(r"""
+#include <math.h>
+#include <stdio.h>
+#include "ref_tanhf.h"
+int main(void) {
+    long long n = 0, bad = 0;
+    for (uint64_t u = 0; u < 0x7f800000u; u += 89) {
+        for (int s = 0; s < 2; ++s) {
+            float x = eg2_bitsf((uint32_t)u | (s ? 0x80000000u : 0u));
+            ++n;
+            if (eg2_fbits(eg2_ref_tanhf(x)) != eg2_fbits(tanhf(x))) ++bad;
+        }
+    }
+    printf("%lld %lld\n", n, bad);
+    return bad != 0;
+}
+""")
+    exe = tmp_path / "t"
+    subprocess.run(["gcc", "-O2", "-std=c11", "-ffp-contract=off", "-I",
+                    os.path.join(ROOT, "embeddinggemma2-amdkfd_b200", "csrc"), str(src), "-o", str(exe), "-lm"],
+                   check=True)
+    out = subprocess.run([str(exe)], capture_output=True, text=True)
+    assert out.returncode == 0, out.stdout
+    n, bad = map(int, out.stdout.split()[-2:])
+    assert n > 40_000_000 and bad == 0

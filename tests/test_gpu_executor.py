@@ -152,3 +152,26 @@ def test_parity_mode_reproduces_restatement(eg2, model_baseline, port, syn):
     finally:
         ex.close()
         m.close()
+
+
+@pytest.mark.parametrize("norm", ["baseline", "plus1"])
+def test_parity_mode_scalar_tier_equals_reference(eg2, syn, norm, port):
+    """Parity mode with the scalar tier's quantizer rounding and tanhf GELU
+    (EG2_B200_EXACT | EG2_B200_SCALAR_TIER): the embeddings equal, bit for bit,
+    the reference's own scalar tier (EI_GEMMA2_CPU_X86=scalar, compiled from its
+    sources; golden fixtures) -- on the BASELINE model and on the 1 + N(0, 0.1)
+    model whose reference tiers disagree entirely -- and the live restatement
+    on a ragged wave."""
+    import oracle
+    path = syn.model_path(1234, norm)
+    m = eg2.GGUFModel(path)
+    ex = eg2.Gemma2Executor(m, 0, exact=True, tier="scalar")
+    try:
+        g = golden(f"golden_{norm}.npz")
+        np.testing.assert_array_equal(ex.batch(g["ids"], g["offsets"]), g["embed_scalar"])
+        if norm == "baseline":
+            ids, off = syn.wave((5, 300, 40), seed=91)
+            np.testing.assert_array_equal(ex.batch(ids, off), port.embed(oracle.Gguf(path), ids, off))
+    finally:
+        ex.close()
+        m.close()

@@ -140,17 +140,25 @@ def _check_q8(q_gpu, s_gpu, rows, width, stride, q_ref, d_ref):
     np.testing.assert_array_equal(s, f16_to_f32(d_ref).reshape(rows, width // 32))
 
 
+TIERS = [0, 1]  # x86 tiers' quantizer/GELU (the fast path) and the scalar tier's (parity mode option)
+
+
+def _round_mode(port, tier):
+    return port.ROUND_SCALAR if tier else port.ROUND_X86
+
+
+@pytest.mark.parametrize("tier", TIERS)
 @pytest.mark.parametrize("width,weighted", [(512, True), (512, False), (1024, False), (2048, False)])
-def test_norm_quant_bit_exact(ops, port, width, weighted):
+def test_norm_quant_bit_exact(ops, port, width, weighted, tier):
     rng = np.random.default_rng(width + weighted)
     rows, stride = 77, 96
     x = _rand_rows(rng, rows, width)
     w = (1.0 + 0.1 * rng.standard_normal(width)).astype(np.float32) if weighted else None
     ref = port.rms_rows(x, w) if weighted else x
-    q_ref, d_ref = port.quantize(ref, port.ROUND_X86)
+    q_ref, d_ref = port.quantize(ref, _round_mode(port, tier))
     q = torch.zeros(rows * width, dtype=torch.int8, device=DEV)
     s = torch.zeros(width // 32 * stride, device=DEV)
-    ops.norm_quant(q, s, stride, T(x), T(w) if weighted else None, rows, width)
+    ops.norm_quant(q, s, stride, T(x), T(w) if weighted else None, rows, width, tier=tier)
     _check_q8(host(q), host(s), rows, width, stride, q_ref, d_ref)
 
 
@@ -220,9 +228,9 @@ def test_q8_mm_int32_block_accumulators_exact(ops, port, n, k, m):
     np.testing.assert_array_equal(got_exact.astype(np.int64), exact)
 
 
-@pytest.mark.parametrize("n,k,m,exact", [(130, 512, 2048, False), (2048, 512, 2048, False), (77, 1024, 128, True),
-                                         (300, 512, 2048, True)])
-def test_q8_geglu_equals_unfused(ops, n, k, m, exact):
+@pytest.mark.parametrize("n,k,m,exact,tier", [(130, 512, 2048, False, 0), (2048, 512, 2048, False, 0),
+                                              (77, 1024, 128, True, 1), (300, 512, 2048, True, 1)])
+def test_q8_geglu_equals_unfused(ops, n, k, m, exact, tier):
     """The GeGLU GEMM (gate/up interleaved in 64-row chunks, gelu(gate) * up
     and Q8_0 in the epilogue) reproduces q8_mm(gate), q8_mm(up), gate_quant
     bit for bit."""
@@ -238,7 +246,7 @@ def test_q8_geglu_equals_unfused(ops, n, k, m, exact):
     up = torch.from_numpy(_gpu_q8_mm(ops, xq, xd, uq, ud, stride, exact)).to(DEV)
     q_ref = torch.zeros(n * m, dtype=torch.int8, device=DEV)
     s_ref = torch.zeros(m // 32 * stride, device=DEV)
-    ops.gate_quant(q_ref, s_ref, stride, gate.ravel(), up.ravel(), n, m, m, 0)
+    ops.gate_quant(q_ref, s_ref, stride, gate.ravel(), up.ravel(), n, m, m, 0, tier=tier)
     # fused
     wq = np.zeros((2 * m, k), np.int8)
     wd = np.zeros((2 * m, k // 32), np.uint16)
@@ -248,28 +256,32 @@ def test_q8_geglu_equals_unfused(ops, n, k, m, exact):
     ws = np.ascontiguousarray(f16_to_f32(wd).T)
     q = torch.zeros(n * m, dtype=torch.int8, device=DEV)
     sc = torch.zeros(m // 32 * stride, device=DEV)
-    ops.q8_geglu(q, sc, stride, T(xq), T(xs), stride, T(wq), T(ws), n, k, m, exact)
+    ops.q8_geglu(q, sc, stride, T(xq), T(xs), stride, T(wq), T(ws), n, k, m, exact, tier=tier)
     np.testing.assert_array_equal(host(q), host(q_ref))
     np.testing.assert_array_equal(host(sc).reshape(-1, stride)[:, :n], host(s_ref).reshape(-1, stride)[:, :n])
 
 
+@pytest.mark.parametrize("tier", TIERS)
 @pytest.mark.parametrize("width,stride,offset", [(2048, 2048, 0), (512, 12288, 7 * 512)])
-def test_gate_quant_bit_exact(ops, port, width, stride, offset):
+def test_gate_quant_bit_exact(ops, port, width, stride, offset, tier):
+    """GELU-tanh gate then Q8_0; the scalar tier's GELU calls the C library's
+    tanhf (restated exactly in csrc/ref_tanhf.h)."""
     rng = np.random.default_rng(width)
     rows = 65
     x = (rng.standard_normal((rows, width)) * 3).astype(np.float32)
     other = rng.standard_normal((rows, stride)).astype(np.float32)
-    g = port.gelu_mul(x, other[:, offset:offset + width], mode=1).reshape(rows, width)
-    q_ref, d_ref = port.quantize(g, port.ROUND_X86)
+    g = port.gelu_mul(x, other[:, offset:offset + width], mode=0 if tier else 1).reshape(rows, width)
+    q_ref, d_ref = port.quantize(g, _round_mode(port, tier))
     qstride = 128
     q = torch.zeros(rows * width, dtype=torch.int8, device=DEV)
     s = torch.zeros(width // 32 * qstride, device=DEV)
-    ops.gate_quant(q, s, qstride, T(x), T(other), rows, width, stride, offset)
+    ops.gate_quant(q, s, qstride, T(x), T(other), rows, width, stride, offset, tier=tier)
     _check_q8(host(q), host(s), rows, width, qstride, q_ref, d_ref)
 
 
+@pytest.mark.parametrize("tier", TIERS)
 @pytest.mark.parametrize("next_norm,scaled", [(True, False), (False, False), (True, True)])
-def test_post_add_bit_exact(ops, port, next_norm, scaled):
+def test_post_add_bit_exact(ops, port, next_norm, scaled, tier):
     rng = np.random.default_rng(3 + next_norm + 2 * scaled)
     rows, stride = 90, 128
     x = (rng.standard_normal((rows, 512)) * 2).astype(np.float32)
@@ -280,11 +292,12 @@ def test_post_add_bit_exact(ops, port, next_norm, scaled):
     hn = port.rms_rows(h, w)
     x_ref = ((x + hn) * (sc[0] if scaled else np.float32(1.0))).astype(np.float32)
     nxt = port.rms_rows(x_ref, nw) if next_norm else x_ref
-    q_ref, d_ref = port.quantize(nxt, port.ROUND_X86)
+    q_ref, d_ref = port.quantize(nxt, _round_mode(port, tier))
     xt = T(x)
     q = torch.zeros(rows * 512, dtype=torch.int8, device=DEV)
     s = torch.zeros(16 * stride, device=DEV)
-    ops.post_add(xt, T(h), T(w), T(sc) if scaled else None, q, s, stride, T(nw) if next_norm else None, rows)
+    ops.post_add(xt, T(h), T(w), T(sc) if scaled else None, q, s, stride, T(nw) if next_norm else None, rows,
+                 tier=tier)
     np.testing.assert_array_equal(host(xt), x_ref)
     _check_q8(host(q), host(s), rows, 512, stride, q_ref, d_ref)
 
