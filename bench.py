@@ -147,7 +147,11 @@ def dist_init(backend="nccl"):
     if world > 1:
         import datetime
         import torch.distributed as dist
-        dist.init_process_group(backend, timeout=datetime.timedelta(seconds=120))
+        kw = {}
+        if backend == "nccl":
+            import torch
+            kw["device_id"] = torch.device(f"cuda:{local}")
+        dist.init_process_group(backend, timeout=datetime.timedelta(seconds=120), **kw)
     return rank, world, local
 
 

@@ -143,7 +143,7 @@ def write_gguf(path: str, seed: int = 1234, norm: str = "plus1") -> str:
     pad = (-len(head)) % ALIGN
     rng = np.random.Generator(np.random.PCG64(seed))
     h = hashlib.sha256()
-    tmp = path + ".part"
+    tmp = f"{path}.{os.getpid()}.part"  # one writer per process; os.replace is atomic
     with open(tmp, "wb") as f:
         for chunk in (head, b"\0" * pad):
             f.write(chunk)
