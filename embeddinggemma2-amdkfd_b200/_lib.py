@@ -54,6 +54,7 @@ SIGNATURES = {
     "eg2_launch_attention_exact": (i32, [vp, u32, vp]),
     "eg2_launch_post_add": (i32, [vp, vp]),
     "eg2_launch_gate_quant": (i32, [vp, vp]),
+    "eg2_launch_gelu_mul": (i32, [vp, vp]),
     "eg2_launch_pool_l2": (i32, [vp, vp]),
     "eg2_repack_q8": (i32, [vp, u32, u32, vp, vp, vp]),
     "eg2_read_error": (i32, []),
@@ -161,10 +162,14 @@ class EgGateQuant(C.Structure):
                 ("width", u32), ("other_stride", u32), ("other_offset", u32), ("tier", u32)]
 
 
+class EgGeluMul(C.Structure):
+    _fields_ = [("g", P), ("u", P), ("n", C.c_uint64), ("tier", u32)]
+
+
 class EgPoolL2(C.Structure):
     _fields_ = [("out", P), ("y", P), ("offsets", P), ("batch", u32), ("width", u32)]
 
 
 STRUCTS = {c.__name__: c for c in (EgGather, EgMM, EgNorm, EgRope, EgAttention, EgElement, EgPool, EgNormResidual,
                                    EgNormRope, EgEmbed, EgPleProj, EgNormQuant, EgQ8MM, EgQ8GeGLU, EgQkvPost, EgAttentionF16,
-                                   EgPostAdd, EgGateQuant, EgPoolL2)}
+                                   EgPostAdd, EgGateQuant, EgGeluMul, EgPoolL2)}

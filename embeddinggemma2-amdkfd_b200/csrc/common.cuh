@@ -283,11 +283,27 @@ __device__ __forceinline__ float ref_exp8(float x) {
     p = __fmaf_rn(p, r, 1.0f);
     return __fmul_rn(p, __uint_as_float(uint32_t(int32_t(n) + 127) << 23));
 }
+// a / b without a branch, by Markstein's sequence (P. Markstein, "IA-64 and
+// Elementary Functions", 2000, ch. 8): y ~ 1/b from the hardware reciprocal
+// approximation, one Newton step y += y (1 - b y), then the quotient q = a y
+// corrected once with its exact FMA residual, q += (a - b q) y.  IEEE division
+// compiles to a range check and a slow-path branch per quotient, which keeps
+// the compiler from interleaving a thread's independent GELU chains.  Used only
+// where it equals the correctly rounded quotient: a = 2 and b in [1, 2^26), the
+// GELU's 1 + exp(2v) with |v| <= 9, checked against IEEE division on B200 for
+// every float b in that range (tests/test_gpu_ops.py).
+__device__ __forceinline__ float fdiv_markstein(float a, float b) {
+    float y;
+    asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(b));
+    y = __fmaf_rn(y, __fmaf_rn(-b, y, 1.0f), y);
+    const float q = __fmul_rn(a, y);
+    return __fmaf_rn(__fmaf_rn(-b, q, a), y, q);
+}
 // gelu_tanh(x) with tanh(v) = 1 - 2/(exp(2v)+1) (gemma2_fast_x86.c:308-325).
 __device__ __forceinline__ float ref_gelu(float x) {
     float inner = __fmul_rn(__fmul_rn(0.79788456080286535588f, x), __fmaf_rn(__fmul_rn(0.044715f, x), x, 1.0f));
     inner = fminf(fmaxf(inner, -9.0f), 9.0f);
-    const float t = __fsub_rn(1.0f, __fdiv_rn(2.0f, __fadd_rn(ref_exp8(__fmul_rn(2.0f, inner)), 1.0f)));
+    const float t = __fsub_rn(1.0f, fdiv_markstein(2.0f, __fadd_rn(ref_exp8(__fmul_rn(2.0f, inner)), 1.0f)));
     return __fmul_rn(__fmul_rn(0.5f, x), __fadd_rn(1.0f, t));
 }
 // gelu_tanh(x) = 0.5 x (1 + tanh(0.7978845608 x (1 + 0.044715 x^2))) with the C

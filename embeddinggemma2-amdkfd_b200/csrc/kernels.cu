@@ -203,6 +203,14 @@ cudaError_t launch_post_add(float *x, const float *h, const float *w, const floa
     return launch_pdl(post_add_kernel, dim3(rows), dim3(128), 0, s, x, h, w, scale, q, qs, qs_stride, next_w, tier);
 }
 
+cudaError_t launch_gelu_mul(float *g, const float *u, size_t n, cudaStream_t s, int tier) {
+    if (n == 0) return cudaSuccess;
+    if (!g || (tier != TIER_SCALAR && n % 8)) return cudaErrorInvalidValue;
+    const size_t blocks = (n + 255) / 256, cap = size_t(sm_count()) * 16;
+    return launch_pdl(tier == TIER_SCALAR ? gelu_mul_kernel<TIER_SCALAR> : gelu_mul_kernel<TIER_X86>,
+                      dim3(unsigned(blocks < cap ? blocks : cap)), dim3(256), 0, s, g, u, n);
+}
+
 cudaError_t launch_gate_quant(int8_t *q, float *qs, int qs_stride, const float *x, const float *other, int rows,
                               int width, int other_stride, int other_offset, cudaStream_t s, int tier) {
     if (rows <= 0) return cudaSuccess;
@@ -210,8 +218,9 @@ cudaError_t launch_gate_quant(int8_t *q, float *qs, int qs_stride, const float *
         other_offset + width > other_stride)
         return cudaErrorInvalidValue;
     const int warps = rows * (width / 128);
-    return launch_pdl(gate_quant_kernel, dim3((warps + 7) / 8), dim3(256), 0, s, q, qs, qs_stride, x, other, rows, width,
-                      other_stride, other_offset, tier);
+    return launch_pdl(tier == TIER_SCALAR ? gate_quant_kernel<TIER_SCALAR> : gate_quant_kernel<TIER_X86>,
+                      dim3((warps + 7) / 8), dim3(256), 0, s, q, qs, qs_stride, x, other, rows, width, other_stride,
+                      other_offset);
 }
 
 cudaError_t launch_pool_l2(float *out, const float *y, const unsigned *offsets, int batch, int width, cudaStream_t s) {
@@ -389,6 +398,9 @@ int eg2_launch_post_add(const EgPostAdd *p, void *s) {
 int eg2_launch_gate_quant(const EgGateQuant *p, void *s) {
     return rc(launch_gate_quant(p->q, p->scale, int(p->scale_stride), p->x, p->other, int(p->rows), int(p->width),
                                 int(p->other_stride), int(p->other_offset), S(s), int(p->tier)));
+}
+int eg2_launch_gelu_mul(const EgGeluMul *p, void *s) {
+    return rc(launch_gelu_mul(p->g, p->u, size_t(p->n), S(s), int(p->tier)));
 }
 int eg2_launch_pool_l2(const EgPoolL2 *p, void *s) {
     return rc(launch_pool_l2(p->out, p->y, p->offsets, int(p->batch), int(p->width), S(s)));

@@ -48,6 +48,7 @@ cudaError_t launch_attention(float *out, const void *q, const void *k, const voi
                              int d, int window, cudaStream_t s);
 cudaError_t launch_post_add(float *x, const float *h, const float *w, const float *scale, int8_t *q, float *qs,
                             int qs_stride, const float *next_w, int rows, cudaStream_t s, int tier = 0);
+cudaError_t launch_gelu_mul(float *g, const float *u, size_t n, cudaStream_t s, int tier = 0);
 cudaError_t launch_gate_quant(int8_t *q, float *qs, int qs_stride, const float *x, const float *other, int rows,
                               int width, int other_stride, int other_offset, cudaStream_t s, int tier = 0);
 cudaError_t launch_pool_l2(float *out, const float *y, const unsigned *offsets, int batch, int width, cudaStream_t s);

@@ -26,7 +26,8 @@
 //   warp 0      TMA producer: per tile the scale panels (weight scales
 //               [K/32][128], activation scales [K/32][64]) into a double
 //               buffer, then int8 weight/token tiles of 128 B (one 128-byte
-//               swizzle row = four Q8_0 blocks) per stage of a 4-deep ring;
+//               swizzle row = four Q8_0 blocks) per stage of a ring of up
+//               to six stages;
 //   warp 1      TMEM owner and MMA issuer: block j is two N=32 MMAs (token
 //               halves h = 0, 1) into TMEM columns h*256 + (j % 8)*32.  The
 //               eight slots form two groups of four, one stage's blocks each:
@@ -67,6 +68,7 @@ struct Q8Cfg {
     static constexpr int NBUF = 8;   // block slots: 2 halves x 8 slots x 32 columns = 512
     static constexpr int GROUP = 4;  // slots per handshake group = Q8_0 blocks per stage
     static constexpr int EPI_WARPS = 8, THREADS = (2 + EPI_WARPS) * 32;
+    static constexpr int MAX_STAGES = 6;  // depth of the TMA ring when shared memory allows
     static constexpr int A_BYTES = BM * BK, B_BYTES = BN * BK, STAGE_BYTES = A_BYTES + B_BYTES;
 };
 
@@ -81,17 +83,48 @@ struct Q8Smem {
 };
 __host__ __device__ inline Q8Smem q8gemm_smem(int K, bool geglu = false) {
     Q8Smem s;
-    s.stages = 4;
     s.kb = K / 32;
     s.stage_bytes = size_t(Q8Cfg::STAGE_BYTES);
     s.sw_bytes = size_t(s.kb) * Q8Cfg::BM * 4;
     s.sx_bytes = size_t(s.kb) * Q8Cfg::BN * 4;
     s.panel_bytes = (s.sw_bytes + s.sx_bytes + 1023) / 1024 * 1024;
     s.gbuf_bytes = geglu ? (size_t(Q8Cfg::BN) * (Q8Cfg::BM + 1) * 4 + 1023) / 1024 * 1024 : 0;
+    // The deepest ring (MAX_STAGES down to 2) that fits, with two panel buffers
+    // when they fit beside it, else one.
     const size_t limit = 227 * 1024, fixed = 1024 + 512 + s.gbuf_bytes;
-    s.pbufs = fixed + 4 * s.stage_bytes + 2 * s.panel_bytes > limit ? 1 : 2;
+    for (s.stages = Q8Cfg::MAX_STAGES; s.stages > 2; --s.stages)
+        if (fixed + size_t(s.stages) * s.stage_bytes + s.panel_bytes <= limit) break;
+    s.pbufs = fixed + size_t(s.stages) * s.stage_bytes + 2 * s.panel_bytes <= limit ? 2 : 1;
     s.total = fixed + size_t(s.stages) * s.stage_bytes + size_t(s.pbufs) * s.panel_bytes;
     return s;
+}
+
+// One unit of the GeGLU tail: g = gelu(gate) * up for 16 columns of one
+// (token, 32-column block) -- gate at gr[0..15], up at gr[64..79] -- then the
+// block's Q8_0 codes, the lane pair (part 0, 1) sharing its amax by one
+// shuffle; stores only when store is set (all lanes take part in the shuffle).
+// The tier is a template argument so the 16 independent chains compile without
+// a branch per element.
+template <int TIER>
+__device__ __forceinline__ void geglu_unit(const float *gr, int part, bool store, int8_t *q8, float *q8s) {
+    float g[16];
+    float amax = 0.0f;
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+        g[j] = __fmul_rn(gelu_tier(gr[j], TIER), gr[64 + j]);
+        amax = fmaxf(amax, fabsf(g[j]));
+    }
+    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
+    const float d = __fdiv_rn(amax, 127.0f);
+    const float id = d != 0.0f ? __fdiv_rn(1.0f, d) : 0.0f;
+    if (!store) return;
+    uint32_t w4[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+        w4[j] = q8_code(g[4 * j], id, TIER) | q8_code(g[4 * j + 1], id, TIER) << 8 |
+                q8_code(g[4 * j + 2], id, TIER) << 16 | q8_code(g[4 * j + 3], id, TIER) << 24;
+    *reinterpret_cast<uint4 *>(q8) = make_uint4(w4[0], w4[1], w4[2], w4[3]);
+    if (part == 0) *q8s = fp16_bits_to_f32(ref_fp32_to_fp16(d));
 }
 
 // GEGLU: the weight rows of every 128-row tile are 64 gate rows followed by
@@ -109,7 +142,8 @@ __global__ void __launch_bounds__(Q8Cfg::THREADS, 1)
     const Q8Smem L = q8gemm_smem(p.K, GEGLU);
     const int Kb = L.kb, ksteps = p.K / C::BK, STAGES = L.stages, PBUFS = L.pbufs;
     uint64_t *bars = reinterpret_cast<uint64_t *>(smem + L.bars());
-    uint64_t *full = bars, *empty = bars + 4, *accf = bars + 8, *acce = accf + 2;  // accf/acce: per slot group
+    uint64_t *full = bars, *empty = bars + C::MAX_STAGES, *accf = bars + 2 * C::MAX_STAGES;
+    uint64_t *acce = accf + 2;  // accf/acce: per slot group
     uint64_t *pfull = acce + 2, *pempty = pfull + 2, *mdone = pempty + 2, *edone = mdone + 1;
     uint64_t *gfull = edone + 1, *gdone = gfull + 1;  // GeGLU pairing tile written / consumed
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(gdone + 1);
@@ -317,26 +351,12 @@ __global__ void __launch_bounds__(Q8Cfg::THREADS, 1)
                 const int u = ((warp - 2) * 32 + lane) >> 1, part = lane & 1;  // 128 units, 2 lanes each
                 const int tok = u >> 1, cb = u & 1, t = t0 + tok, col0 = r0 / 2;
                 const float *gr = G + tok * GS + cb * 32 + part * 16;
-                float g[16];
-                float amax = 0.0f;
-#pragma unroll
-                for (int j = 0; j < 16; ++j) {
-                    g[j] = __fmul_rn(gelu_tier(gr[j], p.tier), gr[64 + j]);
-                    amax = fmaxf(amax, fabsf(g[j]));
-                }
-                amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
-                const float d = __fdiv_rn(amax, 127.0f);
-                const float id = d != 0.0f ? __fdiv_rn(1.0f, d) : 0.0f;
-                if (t < p.T) {
-                    uint32_t w4[4];
-#pragma unroll
-                    for (int j = 0; j < 4; ++j)
-                        w4[j] = q8_code(g[4 * j], id, p.tier) | q8_code(g[4 * j + 1], id, p.tier) << 8 |
-                                q8_code(g[4 * j + 2], id, p.tier) << 16 | q8_code(g[4 * j + 3], id, p.tier) << 24;
-                    *reinterpret_cast<uint4 *>(p.q8 + size_t(t) * (p.R / 2) + col0 + cb * 32 + part * 16) =
-                        make_uint4(w4[0], w4[1], w4[2], w4[3]);
-                    if (part == 0) p.q8s[size_t(col0 / 32 + cb) * p.q8s_stride + t] = fp16_bits_to_f32(ref_fp32_to_fp16(d));
-                }
+                int8_t *qo = p.q8 + size_t(t) * (p.R / 2) + col0 + cb * 32 + part * 16;
+                float *so = p.q8s + size_t(col0 / 32 + cb) * p.q8s_stride + t;
+                if (p.tier == TIER_SCALAR)
+                    geglu_unit<TIER_SCALAR>(gr, part, t < p.T, qo, so);
+                else
+                    geglu_unit<TIER_X86>(gr, part, t < p.T, qo, so);
                 __syncwarp();
                 if (lane == 0) bar_arrive(gdone);
                 if (!__all_sync(0xffffffffu, wait_bar(gdone, it & 1, abort))) {  // G is rewritten next tile

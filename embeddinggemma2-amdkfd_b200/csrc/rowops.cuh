@@ -225,10 +225,13 @@ __global__ void __launch_bounds__(128) post_add_kernel(float *__restrict__ x, co
 
 // ROW_GELU_QUANT / ROW_PLE_GATE_QUANT (gemma2_fast.c:714-727):
 // g = gelu_tanh(x) * other, then Q8_0.  Warp per (row, four blocks); width,
-// other_stride and other_offset are multiples of 128, 4 and 4.
+// other_stride and other_offset are multiples of 128, 4 and 4.  TIER selects
+// the GELU and rounding at compile time (no branch per element).
+template <int TIER>
 __global__ void gate_quant_kernel(int8_t *__restrict__ q, float *__restrict__ qs, int qs_stride,
                                   const float *__restrict__ x, const float *__restrict__ other, int rows, int width,
-                                  int other_stride, int other_offset, int tier) {
+                                  int other_stride, int other_offset) {
+    constexpr int tier = TIER;
     pdl_wait();
     pdl_trigger();
     constexpr int PER = 1;  // float4 steps (4 blocks each) per warp
@@ -253,6 +256,20 @@ __global__ void gate_quant_kernel(int8_t *__restrict__ q, float *__restrict__ qs
         float sc;
         qr[(i0 + i) * 32 + lane] = quant_oct(g, &sc, tier);
         if ((lane & 7) == 0) qs[size_t(4 * (i0 + i) + (lane >> 3)) * qs_stride + t] = sc;
+    }
+}
+
+// g[z] = gelu_tanh(g[z]) * (u ? u[z] : 1) for z < n: the reference's GELU rows
+// (x86 tiers: g2x_gelu_mul_row, gemma2_fast_x86.c:308-319, whose vector form the
+// host restricts to whole 8-element groups; scalar tier: ei_gelu_mul_inplace
+// with tanhf, kernels.c:367-371).  Grid-stride over elements.
+template <int TIER>
+__global__ void gelu_mul_kernel(float *__restrict__ g, const float *__restrict__ u, size_t n) {
+    pdl_wait();
+    pdl_trigger();
+    for (size_t z = size_t(blockIdx.x) * blockDim.x + threadIdx.x; z < n; z += size_t(gridDim.x) * blockDim.x) {
+        const float gl = gelu_tier(g[z], TIER);
+        g[z] = u ? __fmul_rn(gl, u[z]) : gl;
     }
 }
 

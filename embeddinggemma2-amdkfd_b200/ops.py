@@ -111,6 +111,11 @@ def gate_quant(q, scale, scale_stride, x, other, rows, width, other_stride, othe
                                                     other_stride, other_offset, tier))
 
 
+def gelu_mul(g, u, n, tier=0):
+    """g[:n] = gelu_tanh(g[:n]) * u[:n] in place (u None: gelu only)."""
+    _call("eg2_launch_gelu_mul", _lib.EgGeluMul(_p(g), _p(u), n, tier))
+
+
 def pool_l2(out, y, offsets, batch, width):
     _call("eg2_launch_pool_l2", _lib.EgPoolL2(_p(out), _p(y), _p(offsets), batch, width))
 

@@ -105,6 +105,11 @@ typedef struct {
     const float *x, *other; unsigned rows, width, other_stride, other_offset;
     unsigned tier; /* 0: x86 tiers' GELU and rounding, 1: scalar tier's (tanhf, roundf) */
 } EgGateQuant;
+/* g[z] = gelu_tanh(g[z]) * (u ? u[z] : 1) for z < n, in place: the reference's
+ * GELU rows, g2x_gelu_mul_row (gemma2_fast_x86.c:308-325) on the x86 tiers
+ * (tier 0; n % 8 == 0, the whole-vector part that the graph uses) and
+ * ei_gelu_mul_inplace (kernels.h:26, tanhf form) on the scalar tier (tier 1). */
+typedef struct { float *g; const float *u; uint64_t n; unsigned tier; } EgGeluMul;
 /* out[s] = L2(mean over the sequence's rows of y) (gemma2_fast.c:1000-1008). */
 typedef struct { float *out; const float *y; const unsigned *offsets; unsigned batch, width; } EgPoolL2;
 
@@ -137,6 +142,7 @@ int eg2_launch_attention_f16(const EgAttentionF16 *p, void *stream);
 int eg2_launch_attention_exact(const EgAttention *p, unsigned d, void *stream);
 int eg2_launch_post_add(const EgPostAdd *p, void *stream);
 int eg2_launch_gate_quant(const EgGateQuant *p, void *stream);
+int eg2_launch_gelu_mul(const EgGeluMul *p, void *stream);
 int eg2_launch_pool_l2(const EgPoolL2 *p, void *stream);
 /* Repack GGUF Q8_0 blocks (34 B, device memory) into the SoA weight operand:
  * codes [rows][k] and fp32 scales [k/32][rows]. */

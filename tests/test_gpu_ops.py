@@ -279,6 +279,55 @@ def test_gate_quant_bit_exact(ops, port, width, stride, offset, tier):
     _check_q8(host(q), host(s), rows, width, qstride, q_ref, d_ref)
 
 
+def _gelu_inputs(step):
+    """Every step-th float bit pattern with |x| <= 6.5 (past it the GELU's inner
+    argument is clamped), both signs, plus zeros, infinities, NaN, extremes."""
+    mag = np.arange(0, 0x40D00001, step, dtype=np.uint32)
+    x = np.concatenate([mag, mag | np.uint32(0x80000000)]).view(np.float32)
+    special = np.array([0.0, -0.0, np.inf, -np.inf, np.nan, 1e30, -1e30, 3.4e38, -3.4e38, 1e-45, -1e-45],
+                       np.float32)
+    x = np.concatenate([special, x])
+    return x[: x.size - x.size % 8]
+
+
+@pytest.mark.parametrize("tier,step", [(0, 61), (1, 4093)])
+def test_gelu_mul_bit_exact(ops, port, tier, step):
+    """GELU rows against the CPU restatement, bit for bit, over a dense sweep of
+    the GELU's input range: tier 0 is the x86 rows' exp polynomial with IEEE
+    division (here the branch-free division), tier 1 the tanhf form."""
+    x = _gelu_inputs(step)
+    u = np.random.default_rng(5).standard_normal(x.size).astype(np.float32)
+    for uu in (u, None):
+        ref = port.gelu_mul(x, uu, mode=0 if tier else 1)
+        g = T(x)
+        ops.gelu_mul(g, None if uu is None else T(uu), x.size, tier=tier)
+        out = host(g)
+        same = (out.view(np.uint32) == ref.view(np.uint32)) | (np.isnan(out) & np.isnan(ref))
+        assert same.all(), (x[~same][:8], out[~same][:8], ref[~same][:8])
+
+
+def test_gelu_mul_rejects_partial_vector_on_x86_tier(ops):
+    g = torch.zeros(12, device=DEV)
+    with pytest.raises(RuntimeError):
+        ops.gelu_mul(g, None, 12, tier=0)
+
+
+def test_fdiv_markstein_equals_ieee_division(tmp_path):
+    """The GELU's branch-free division equals IEEE division for every float
+    denominator the GELU can produce (tests/cuda/fdiv_check.cu)."""
+    import os
+    import shutil
+    import subprocess
+    nvcc = shutil.which("nvcc") or "/usr/local/cuda/bin/nvcc"
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    exe = str(tmp_path / "fdiv_check")
+    subprocess.run([nvcc, "-gencode", "arch=compute_100a,code=sm_100a", "-O3", "-std=c++17",
+                    "-I", os.path.join(root, "embeddinggemma2-amdkfd_b200", "csrc"), "-o", exe,
+                    os.path.join(root, "tests", "cuda", "fdiv_check.cu")], check=True)
+    r = subprocess.run([exe], capture_output=True, text=True, timeout=120)
+    assert r.returncode == 0 and " 0 differ" in r.stdout, r.stdout + r.stderr
+
+
 @pytest.mark.parametrize("tier", TIERS)
 @pytest.mark.parametrize("next_norm,scaled", [(True, False), (False, False), (True, True)])
 def test_post_add_bit_exact(ops, port, next_norm, scaled, tier):
