@@ -299,6 +299,16 @@ __device__ __forceinline__ float fdiv_markstein(float a, float b) {
     const float q = __fmul_rn(a, y);
     return __fmaf_rn(__fmaf_rn(-b, q, a), y, q);
 }
+// v / sqrtf(512) with the rounding of IEEE division, without its branch: the
+// double product with RN(1/b) is within 2^-52 of the quotient, and a quotient
+// of two floats lies at least 2^-49 (relative) from any float rounding
+// midpoint (b's odd 24-bit significand makes an exact midpoint impossible), so
+// rounding the product to float gives the correctly rounded quotient.  Checked
+// on B200 against IEEE division for every float v (tests/test_gpu_ops.py).
+__device__ __forceinline__ float div_sqrt512(float v) {
+    constexpr double INV = 1.0 / double(22.627416997969522f);
+    return __double2float_rn(__dmul_rn(double(v), INV));
+}
 // gelu_tanh(x) with tanh(v) = 1 - 2/(exp(2v)+1) (gemma2_fast_x86.c:308-325).
 __device__ __forceinline__ float ref_gelu(float x) {
     float inner = __fmul_rn(__fmul_rn(0.79788456080286535588f, x), __fmaf_rn(__fmul_rn(0.044715f, x), x, 1.0f));

@@ -120,9 +120,10 @@ __global__ void __launch_bounds__(PleCfg::THREADS, 1)
         const uint32_t taddr = tmem + (uint32_t(quad * 32) << 16) + uint32_t(colbase);
         const bool ok = __all_sync(0xffffffffu, wait_bar(accf, 0, abort));  // warp-uniform before tcgen05.ld
         tc_fence_after();
-        const float inv_sqrt = 22.627416997969522f;  // sqrtf(512.0f)
+        auto scaled = [](uint32_t bits) { return div_sqrt512(__uint_as_float(bits)); };  // = v / sqrtf(512)
         double ss = 0.0;
         if (ok) {
+            double s4[4] = {0.0, 0.0, 0.0, 0.0};
             for (int c = 0; c < 256; c += 32) {
                 uint32_t d[32];
                 tmem_ld32(taddr + uint32_t(c), d);
@@ -130,34 +131,40 @@ __global__ void __launch_bounds__(PleCfg::THREADS, 1)
                 reg_fence(d);
 #pragma unroll
                 for (int i = 0; i < 32; ++i) {
-                    const float v = __fdiv_rn(__uint_as_float(d[i]), inv_sqrt);
-                    ss = __dadd_rn(ss, __dmul_rn(double(v), double(v)));
+                    const double v = double(scaled(d[i]));
+                    s4[i & 3] = __dadd_rn(s4[i & 3], __dmul_rn(v, v));
                 }
             }
+            ss = __dadd_rn(__dadd_rn(s4[0], s4[1]), __dadd_rn(s4[2], s4[3]));
         }
         partial[half * C::BM + row] = ss;
         named_sync(1, C::EPI_WARPS * 32);
         const float scale = rms_scale(partial[row] + partial[C::BM + row], 512);
-        const int m = m0 + row;
-        const bool store = m < p.M;  // per lane; the TMEM loads stay warp-collective
         if (ok) {
-            float *o = p.ple + size_t(store ? m : 0) * (24 * 512) + slice * 512 + colbase;
+            // Each 32-column chunk of the warp's 32 token rows goes through a
+            // padded shared-memory tile (the stage buffers are free once every MMA
+            // has completed) so that each store instruction writes four whole
+            // 128-byte row segments.
+            float *st = reinterpret_cast<float *>(smem) + (warp - 2) * (32 * 33);
+            const int srow = lane >> 3, scol = (lane & 7) * 4;
             const float *w = p.norm + colbase;
             for (int c = 0; c < 256; c += 32) {
                 uint32_t d[32];
                 tmem_ld32(taddr + uint32_t(c), d);
                 tmem_wait_ld();
                 reg_fence(d);
-                if (!store) continue;
 #pragma unroll
-                for (int i = 0; i < 32; i += 4) {
-                    float4 r;
-                    r.x = __fmul_rn(__fdiv_rn(__uint_as_float(d[i + 0]), inv_sqrt), __fmul_rn(scale, w[c + i + 0]));
-                    r.y = __fmul_rn(__fdiv_rn(__uint_as_float(d[i + 1]), inv_sqrt), __fmul_rn(scale, w[c + i + 1]));
-                    r.z = __fmul_rn(__fdiv_rn(__uint_as_float(d[i + 2]), inv_sqrt), __fmul_rn(scale, w[c + i + 2]));
-                    r.w = __fmul_rn(__fdiv_rn(__uint_as_float(d[i + 3]), inv_sqrt), __fmul_rn(scale, w[c + i + 3]));
-                    *reinterpret_cast<float4 *>(o + c + i) = r;
+                for (int i = 0; i < 32; ++i) st[lane * 33 + i] = __fmul_rn(scaled(d[i]), __fmul_rn(scale, w[c + i]));
+                __syncwarp();
+#pragma unroll
+                for (int rr = 0; rr < 32; rr += 4) {
+                    const int r = rr + srow, m = m0 + quad * 32 + r;
+                    const float *src = st + r * 33 + scol;
+                    if (m < p.M)
+                        *reinterpret_cast<float4 *>(p.ple + size_t(m) * (24 * 512) + slice * 512 + colbase + c + scol) =
+                            make_float4(src[0], src[1], src[2], src[3]);
                 }
+                __syncwarp();
             }
         }
         __syncwarp();
