@@ -309,6 +309,25 @@ __device__ __forceinline__ float div_sqrt512(float v) {
     constexpr double INV = 1.0 / double(22.627416997969522f);
     return __double2float_rn(__dmul_rn(double(v), INV));
 }
+// a / 127 rounded as IEEE division rounds it (same argument as div_sqrt512:
+// 127 has an odd significand).  Checked for every non-negative float.
+__device__ __forceinline__ float div127(float a) {
+    constexpr double INV = 1.0 / 127.0;
+    return __double2float_rn(__dmul_rn(double(a), INV));
+}
+// 1 / d rounded as IEEE division rounds it, for d > 0, without the division's
+// slow-path branch: the double reciprocal approximation refined by two Newton
+// steps is within 2^-52 of 1/d, which lies at least 2^-49 (relative) from any
+// float rounding midpoint, so its rounding to float is the correctly rounded
+// reciprocal.  Checked against IEEE division for every positive float and +inf.
+__device__ __forceinline__ float rcp_rn(float d) {
+    const double x = double(d);
+    double y;
+    asm("rcp.approx.ftz.f64 %0, %1;" : "=d"(y) : "d"(x));
+    y = __fma_rn(y, __fma_rn(-x, y, 1.0), y);
+    y = __fma_rn(y, __fma_rn(-x, y, 1.0), y);
+    return d == INFINITY ? 0.0f : __double2float_rn(y);  // the Newton steps turn 1/inf into NaN
+}
 // gelu_tanh(x) with tanh(v) = 1 - 2/(exp(2v)+1) (gemma2_fast_x86.c:308-325).
 __device__ __forceinline__ float ref_gelu(float x) {
     float inner = __fmul_rn(__fmul_rn(0.79788456080286535588f, x), __fmaf_rn(__fmul_rn(0.044715f, x), x, 1.0f));

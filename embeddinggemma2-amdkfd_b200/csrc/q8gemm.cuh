@@ -115,8 +115,8 @@ __device__ __forceinline__ void geglu_unit(const float *gr, int part, bool store
         amax = fmaxf(amax, fabsf(g[j]));
     }
     amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
-    const float d = __fdiv_rn(amax, 127.0f);
-    const float id = d != 0.0f ? __fdiv_rn(1.0f, d) : 0.0f;
+    const float d = div127(amax);
+    const float id = d != 0.0f ? rcp_rn(d) : 0.0f;
     if (!store) return;
     uint32_t w4[4];
 #pragma unroll

@@ -42,15 +42,15 @@ __global__ void embed_kernel(float *__restrict__ x, __nv_bfloat16 *__restrict__ 
 // codes as one 32-bit word.
 
 // One 32-element block held as v in each lane of an aligned 8-lane group
-// (gemma2_fast_x86.c:211-234): d = amax/127 (IEEE), the scale stored is the
+// (gemma2_fast_x86.c:211-234): d = amax/127 (IEEE rounding), the scale stored is the
 // reference's fp16 rounding of d, id = 1/d.  Returns the lane's four codes;
 // *scale_out receives the widened fp16 scale (uniform over the group).
 __device__ __forceinline__ uint32_t quant_oct(const float4 v, float *scale_out, int tier) {
     float amax = fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
 #pragma unroll
     for (int o = 1; o < 8; o <<= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
-    const float d = __fdiv_rn(amax, 127.0f);
-    const float id = d != 0.0f ? __fdiv_rn(1.0f, d) : 0.0f;
+    const float d = div127(amax);
+    const float id = d != 0.0f ? rcp_rn(d) : 0.0f;
     *scale_out = fp16_bits_to_f32(ref_fp32_to_fp16(d));
     return q8_code(v.x, id, tier) | q8_code(v.y, id, tier) << 8 | q8_code(v.z, id, tier) << 16 |
            q8_code(v.w, id, tier) << 24;
