@@ -13,8 +13,9 @@
 namespace eg2 {
 
 // Set by any bounded wait that ran out (see wait_bar); read by the host after a
-// wave.  A kernel that sees it set at start skips its work.  Defined here: the
-// library has a single device translation unit (kernels.cu).
+// wave, which then reports the wave as failed.  Kernels do not read it: every
+// wait is bounded, so a kernel that follows a failed one still terminates.
+// Defined here: the library has a single device translation unit (kernels.cu).
 __device__ int g_error = 0;
 enum : int { ERR_NONE = 0, ERR_WAIT_TIMEOUT = 1 };
 

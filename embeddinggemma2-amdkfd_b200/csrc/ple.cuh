@@ -60,7 +60,7 @@ __global__ void __launch_bounds__(PleCfg::THREADS, 1)
     }
     pdl_wait();  // the prologue above overlaps the previous kernel's tail
     pdl_trigger();
-    if (threadIdx.x == 0) *abort = g_error != 0;
+    if (threadIdx.x == 0) *abort = 0;
     tc_fence_before();
     cta_sync();
     tc_fence_after();

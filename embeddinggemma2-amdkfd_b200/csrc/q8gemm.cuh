@@ -156,6 +156,9 @@ __global__ void __launch_bounds__(Q8Cfg::THREADS, 1)
     auto sx_pan = [&](int b) { return reinterpret_cast<float *>(smem + L.panel(b) + L.sw_bytes); };
 
     if (threadIdx.x == 0) {
+        // Descriptor fetches overlap the rest of the prologue.
+        tma_prefetch(&tmW), tma_prefetch(&tmX), tma_prefetch(&tmSW), tma_prefetch(&tmSX);
+        *abort = 0;
         for (int s = 0; s < STAGES; ++s) bar_init(&full[s], 1), bar_init(&empty[s], 1);
         for (int b = 0; b < 2; ++b) bar_init(&accf[b], 1), bar_init(&acce[b], C::EPI_WARPS);
         for (int b = 0; b < PBUFS; ++b) bar_init(&pfull[b], 1), bar_init(&pempty[b], C::EPI_WARPS);
@@ -169,7 +172,6 @@ __global__ void __launch_bounds__(Q8Cfg::THREADS, 1)
     }
     pdl_wait();  // the prologue above overlaps the previous kernel's tail
     pdl_trigger();
-    if (threadIdx.x == 0) *abort = g_error != 0;
     tc_fence_before();
     cta_sync();
     tc_fence_after();
@@ -177,18 +179,12 @@ __global__ void __launch_bounds__(Q8Cfg::THREADS, 1)
 
     if (warp == 0) {
         // ------------------------------------------------------------ producer
-        if (elect_one() && !*abort) {
-            tma_prefetch(&tmW), tma_prefetch(&tmX), tma_prefetch(&tmSW), tma_prefetch(&tmSX);
+        if (elect_one()) {
             int g = 0, issued = 0, it = 0, panels = 0;
             bool ok = true;
             for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x, ++it) {
                 const int r0 = (tile / p.tiles_t) * C::BM, t0 = (tile % p.tiles_t) * C::BN;
                 const int pb = it % PBUFS;
-                if (!wait_bar(&pempty[pb], ((it / PBUFS) & 1) ^ 1, abort)) break;
-                bar_expect_tx(&pfull[pb], uint32_t(L.sw_bytes + L.sx_bytes));
-                tma_load_2d(sw_pan(pb), &tmSW, &pfull[pb], r0, 0);
-                tma_load_2d(sx_pan(pb), &tmSX, &pfull[pb], t0, 0);
-                ++panels;
                 for (int ks = 0; ks < ksteps; ++ks, ++g) {
                     const int s = g % STAGES;
                     if (!wait_bar(&empty[s], ((g / STAGES) & 1) ^ 1, abort)) {
@@ -199,6 +195,16 @@ __global__ void __launch_bounds__(Q8Cfg::THREADS, 1)
                     tma_load_2d(w_tile(s), &tmW, &full[s], ks * C::BK, r0);
                     tma_load_2d(x_tile(s), &tmX, &full[s], ks * C::BK, t0);
                     ++issued;
+                    if (ks == 0) {  // the scale panel is first needed by the epilogue: after the first stage
+                        if (!wait_bar(&pempty[pb], ((it / PBUFS) & 1) ^ 1, abort)) {
+                            ok = false;
+                            break;
+                        }
+                        bar_expect_tx(&pfull[pb], uint32_t(L.sw_bytes + L.sx_bytes));
+                        tma_load_2d(sw_pan(pb), &tmSW, &pfull[pb], r0, 0);
+                        tma_load_2d(sx_pan(pb), &tmSX, &pfull[pb], t0, 0);
+                        ++panels;
+                    }
                 }
             }
             // Drain: the last load into every stage / panel buffer has landed before exit.
