@@ -120,6 +120,7 @@ struct Backend {
     // host staging (pinned)
     uint32_t *h_in = nullptr;  // ids | bounds(2) | pos | offsets
     float *h_out = nullptr;
+    int *h_err = nullptr;      // the device error word, read back with each wave
     cudaEvent_t done = nullptr;
 
     // graphs per wave shape
@@ -289,11 +290,14 @@ struct Backend {
             ck(cudaMemcpy(rope_sin[b], s.data(), s.size() * 4, cudaMemcpyHostToDevice), "rope upload");
         }
 
-        // ---- arena for CAP packed tokens
-        ids = dalloc<int>(CAP);
-        bounds = dalloc<unsigned>(2 * CAP);
-        pos = dalloc<unsigned>(CAP);
-        offsets = dalloc<unsigned>(CAP + 1);
+        // ---- arena for CAP packed tokens.  The per-wave inputs share one block
+        // laid out like the pinned staging buffer (ids | bounds | pos | offsets),
+        // so a wave uploads them with a single copy.
+        unsigned *in_block = dalloc<unsigned>(5 * CAP + 1);
+        ids = reinterpret_cast<int *>(in_block);
+        bounds = in_block + CAP;
+        pos = in_block + 3 * CAP;
+        offsets = in_block + 4 * CAP;
         x = dalloc<float>(size_t(CAP) * 512);
         x_hi = dalloc<uint16_t>(size_t(CAP) * 512);
         x_lo = dalloc<uint16_t>(size_t(CAP) * 512);
@@ -326,6 +330,7 @@ struct Backend {
             !bf16_tmap(&tm_ple, ple_w, 512, 24 * 512, 256))
             throw std::runtime_error("tensor map (PLE)");
         ck(cudaMallocHost(&h_in, sizeof(uint32_t) * (5 * CAP + 1)), "cudaMallocHost");
+        ck(cudaMallocHost(&h_err, sizeof(int)), "cudaMallocHost");
         ck(cudaMallocHost(&h_out, sizeof(float) * CAP * 768), "cudaMallocHost");
         ck(cudaStreamSynchronize(stream), "weight upload");
         clear_device_error();
@@ -343,6 +348,7 @@ struct Backend {
         for (auto &kv : graphs) cudaGraphExecDestroy(kv.second);
         for (void *p : allocations) cudaFree(p);
         if (h_in) cudaFreeHost(h_in);
+        if (h_err) cudaFreeHost(h_err);
         if (h_out) cudaFreeHost(h_out);
         if (done) cudaEventDestroy(done);
         if (stream) cudaStreamDestroy(stream);
@@ -466,7 +472,7 @@ struct Backend {
         if (poisoned) throw std::runtime_error("KFD context failed; restart process before reuse");
         validate_wave(in_ids, in_off, batch);
         const unsigned n = unsigned(in_off[batch]);
-        uint32_t *hid = h_in, *hb = h_in + CAP, *hp = h_in + 3 * CAP, *ho = h_in + 4 * CAP;
+        uint32_t *hid = h_in, *hb = h_in + CAP, *hp = h_in + 3 * CAP, *ho = h_in + 4 * CAP;  // device layout
         std::memcpy(hid, in_ids, n * sizeof(int32_t));
         for (size_t s = 0; s < batch; ++s) {
             ho[s] = uint32_t(in_off[s]);
@@ -477,10 +483,7 @@ struct Backend {
         }
         ho[batch] = n;
         ck(cudaSetDevice(device), "cudaSetDevice");
-        ck(cudaMemcpyAsync(ids, hid, n * 4, cudaMemcpyHostToDevice, stream), "ids upload");
-        ck(cudaMemcpyAsync(bounds, hb, n * 8, cudaMemcpyHostToDevice, stream), "bounds upload");
-        ck(cudaMemcpyAsync(pos, hp, n * 4, cudaMemcpyHostToDevice, stream), "positions upload");
-        ck(cudaMemcpyAsync(offsets, ho, (batch + 1) * 4, cudaMemcpyHostToDevice, stream), "offsets upload");
+        ck(cudaMemcpyAsync(ids, h_in, (4 * CAP + batch + 1) * 4, cudaMemcpyHostToDevice, stream), "wave upload");
         staged_graph = graph_for(n, batch);
         staged_n = n, staged_batch = batch;
     }
@@ -494,17 +497,19 @@ struct Backend {
     // Wait with the reference's deadline; any failure poisons the context.
     void wait_done() {
         poisoned = true;
+        ck(read_device_error_async(h_err, stream), "error readback");
         ck(cudaEventRecord(done, stream), "event record");
+        // Poll without sleeping for the length of a few waves, then back off.
         const auto t0 = std::chrono::steady_clock::now();
-        for (unsigned spin = 0;; ++spin) {
+        for (;;) {
             const cudaError_t q = cudaEventQuery(done);
             if (q == cudaSuccess) break;
             if (q != cudaErrorNotReady) ck(q, "GPU wave");
-            if (std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count() > TIMEOUT_S)
-                throw std::runtime_error("GPU wave timed out");
-            if (spin > 64) std::this_thread::sleep_for(std::chrono::microseconds(20));
+            const double waited = std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
+            if (waited > TIMEOUT_S) throw std::runtime_error("GPU wave timed out");
+            if (waited > 0.02) std::this_thread::sleep_for(std::chrono::microseconds(50));
         }
-        const int derr = read_device_error();
+        const int derr = *h_err;
         if (derr) throw std::runtime_error("device wait timed out inside a kernel (error " + std::to_string(derr) + ")");
         poisoned = false;
     }

@@ -260,6 +260,9 @@ int read_device_error() {
     if (cudaMemcpyFromSymbol(&v, g_error, sizeof(int)) != cudaSuccess) return -1;
     return v;
 }
+cudaError_t read_device_error_async(int *host, cudaStream_t s) {
+    return cudaMemcpyFromSymbolAsync(host, g_error, sizeof(int), 0, cudaMemcpyDeviceToHost, s);
+}
 void clear_device_error() {
     const int z = 0;
     cudaMemcpyToSymbol(g_error, &z, sizeof(int));

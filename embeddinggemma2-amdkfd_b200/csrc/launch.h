@@ -60,6 +60,8 @@ cudaError_t launch_repack_q8(const void *blocks, int rows, int k, int8_t *codes,
 // any graph capture.
 cudaError_t init_kernel_attributes();
 int read_device_error();
+// Enqueues a copy of the error word into host (pinned) memory on stream s.
+cudaError_t read_device_error_async(int *host, cudaStream_t s);
 void clear_device_error();
 
 }  // namespace eg2
