@@ -59,6 +59,11 @@ def q8_gemm_ops(n_tokens: int) -> float:
 GEMM_DRAM_BYTES_PER_LAUNCH = 3.07e6
 
 
+# The executor uploads each wave's inputs as one block: ids, bounds (2 words),
+# positions, offsets (2048 tokens each) and the sequence count.
+H2D_BYTES_PER_WAVE = (5 * 2048 + 2) * 4
+
+
 def peaks():
     path = os.path.join(ROOT, "MEASURED_PEAKS.json")
     if os.path.exists(path):
@@ -267,7 +272,7 @@ def main():
                    "parallelism": f"replicas x{world} (whole waves per GPU, no collective)",
                    "l2": "256 MiB write between timed steps; per-wave working set > L2 (151 MB weights, 100 MB PLE)"},
         "e2e": {"value": whole_job_rate(n, world, args.steps, e2e_ms_max), "unit": "tokens/s",
-                "h2d_bytes_per_step": n * 4 + n * 8 + n * 4 + (batch + 1) * 4,
+                "h2d_bytes_per_step": H2D_BYTES_PER_WAVE,
                 "d2h_bytes_per_step": batch * 768 * 4},
         "gpu_launches": ex.kernels_per_wave * args.steps,
         "roofline": {"kernel": "q8gemm_kernel (all Q8_0 GEMM launches of a wave)", "bound": "tensor",

@@ -37,6 +37,11 @@ namespace {
 using namespace eg2;
 
 constexpr unsigned CAP = 2048;  // packed tokens per wave: the reference's KFD cap (gemma2_kfd.cpp:20)
+// Waves run padded to a multiple of BUCKET tokens: the padding is one extra
+// sequence that the pooling skips, and every kernel is per token or per
+// sequence, so the real tokens' results do not change.  One CUDA graph per
+// bucket then serves every wave shape (at most CAP / BUCKET graphs).
+constexpr unsigned BUCKET = 64;
 constexpr int VOCAB = 262144;
 constexpr double TIMEOUT_S = 30.0;  // gemma2_kfd.cpp:21
 
@@ -102,7 +107,7 @@ struct Backend {
 
     // arena
     int *ids = nullptr;
-    unsigned *bounds = nullptr, *pos = nullptr, *offsets = nullptr;
+    unsigned *bounds = nullptr, *pos = nullptr, *offsets = nullptr, *seq_count = nullptr;
     float *x = nullptr, *ple = nullptr, *qkv = nullptr, *attn = nullptr, *h = nullptr, *y = nullptr, *pooled = nullptr,
           *xs = nullptr, *gs = nullptr;
     void *x_hi = nullptr, *x_lo = nullptr, *qh = nullptr, *kh = nullptr, *vh = nullptr;
@@ -118,7 +123,7 @@ struct Backend {
     float *qf = nullptr, *kf = nullptr, *vf = nullptr;
 
     // host staging (pinned)
-    uint32_t *h_in = nullptr;  // ids | bounds(2) | pos | offsets
+    uint32_t *h_in = nullptr;  // ids | bounds(2) | pos | offsets | sequence count
     float *h_out = nullptr;
     int *h_err = nullptr;      // the device error word, read back with each wave
     cudaEvent_t done = nullptr;
@@ -293,11 +298,12 @@ struct Backend {
         // ---- arena for CAP packed tokens.  The per-wave inputs share one block
         // laid out like the pinned staging buffer (ids | bounds | pos | offsets),
         // so a wave uploads them with a single copy.
-        unsigned *in_block = dalloc<unsigned>(5 * CAP + 1);
+        unsigned *in_block = dalloc<unsigned>(5 * CAP + 2);
         ids = reinterpret_cast<int *>(in_block);
         bounds = in_block + CAP;
         pos = in_block + 3 * CAP;
         offsets = in_block + 4 * CAP;
+        seq_count = in_block + 5 * CAP + 1;
         x = dalloc<float>(size_t(CAP) * 512);
         x_hi = dalloc<uint16_t>(size_t(CAP) * 512);
         x_lo = dalloc<uint16_t>(size_t(CAP) * 512);
@@ -329,7 +335,7 @@ struct Backend {
         if (!bf16_tmap(&tm_hi, x_hi, 512, CAP, 128) || !bf16_tmap(&tm_lo, x_lo, 512, CAP, 128) ||
             !bf16_tmap(&tm_ple, ple_w, 512, 24 * 512, 256))
             throw std::runtime_error("tensor map (PLE)");
-        ck(cudaMallocHost(&h_in, sizeof(uint32_t) * (5 * CAP + 1)), "cudaMallocHost");
+        ck(cudaMallocHost(&h_in, sizeof(uint32_t) * (5 * CAP + 2)), "cudaMallocHost");
         ck(cudaMallocHost(&h_err, sizeof(int)), "cudaMallocHost");
         ck(cudaMallocHost(&h_out, sizeof(float) * CAP * 768), "cudaMallocHost");
         ck(cudaStreamSynchronize(stream), "weight upload");
@@ -363,7 +369,7 @@ struct Backend {
 
     // The whole wave as a launch sequence (captured into a graph, or run eagerly
     // under the profiler).  Returns the number of kernels launched.
-    int enqueue(unsigned n, unsigned batch, cudaStream_t s, Profiler *prof) {
+    int enqueue(unsigned n, cudaStream_t s, Profiler *prof) {
         int launches = 0;
         auto mark = [&](const char *name) {
             if (prof) prof->mark(name);
@@ -433,13 +439,15 @@ struct Backend {
         }
         gemm(output, y, 768, N, s), ++launches;
         mark("gemm_output");
-        ck(launch_pool_l2(pooled, y, offsets, int(batch), 768, s), "pool"), launches += 2;
+        // The grid covers every sequence a wave of n tokens can hold; the
+        // wave's own count is read on the device.
+        ck(launch_pool_l2(pooled, y, offsets, int(n), 768, s, seq_count), "pool"), launches += 2;
         mark("pool_l2");
         return launches;
     }
 
-    cudaGraphExec_t graph_for(unsigned n, size_t batch) {
-        const uint64_t key = (uint64_t(n) << 32) | uint64_t(batch);
+    cudaGraphExec_t graph_for(unsigned n) {
+        const uint64_t key = n;
         auto it = graphs.find(key);
         if (it != graphs.end()) return it->second;
         if (graphs.size() >= 256) {  // bound the cache
@@ -451,7 +459,7 @@ struct Backend {
         ck(cudaStreamBeginCapture(stream, cudaStreamCaptureModeThreadLocal), "begin capture");
         int launches = 0;
         try {
-            launches = enqueue(n, unsigned(batch), stream, nullptr);
+            launches = enqueue(n, stream, nullptr);
         } catch (...) {
             cudaStreamEndCapture(stream, &graph);
             if (graph) cudaGraphDestroy(graph);
@@ -482,10 +490,14 @@ struct Backend {
             }
         }
         ho[batch] = n;
+        // Padding to the bucket: one sequence [n, n_pad) of token 0, never pooled.
+        const unsigned n_pad = (n + BUCKET - 1) / BUCKET * BUCKET;
+        for (unsigned t = n; t < n_pad; ++t) hid[t] = 0, hb[2 * t] = n, hb[2 * t + 1] = n_pad, hp[t] = t - n;
+        h_in[5 * CAP + 1] = uint32_t(batch);
         ck(cudaSetDevice(device), "cudaSetDevice");
-        ck(cudaMemcpyAsync(ids, h_in, (4 * CAP + batch + 1) * 4, cudaMemcpyHostToDevice, stream), "wave upload");
-        staged_graph = graph_for(n, batch);
-        staged_n = n, staged_batch = batch;
+        ck(cudaMemcpyAsync(ids, h_in, (5 * CAP + 2) * 4, cudaMemcpyHostToDevice, stream), "wave upload");
+        staged_graph = graph_for(n_pad);
+        staged_n = n_pad, staged_batch = batch;
     }
 
     void launch(int repeats) {
@@ -545,7 +557,7 @@ struct Backend {
         std::vector<std::string> order;
         {
             Profiler prof{stream};
-            enqueue(staged_n, unsigned(staged_batch), stream, &prof);
+            enqueue(staged_n, stream, &prof);
             wait_done();
             for (size_t i = 1; i < prof.events.size(); ++i) {
                 float t = 0;

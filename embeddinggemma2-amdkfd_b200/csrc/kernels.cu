@@ -223,13 +223,14 @@ cudaError_t launch_gate_quant(int8_t *q, float *qs, int qs_stride, const float *
                       other_offset);
 }
 
-cudaError_t launch_pool_l2(float *out, const float *y, const unsigned *offsets, int batch, int width, cudaStream_t s) {
+cudaError_t launch_pool_l2(float *out, const float *y, const unsigned *offsets, int batch, int width, cudaStream_t s,
+                           const unsigned *count) {
     if (batch <= 0) return cudaSuccess;
     if (width <= 0 || width % 8 || width > 8192) return cudaErrorInvalidValue;
     if (cudaError_t e = launch_pdl(pool_mean_kernel, dim3((width + 127) / 128, batch), dim3(128), 0, s, out, y, offsets,
-                                   width))
+                                   width, count))
         return e;
-    return launch_pdl(pool_l2_kernel, dim3(batch), dim3(32), 0, s, out, width);
+    return launch_pdl(pool_l2_kernel, dim3(batch), dim3(32), 0, s, out, width, count);
 }
 
 cudaError_t launch_repack_q8(const void *blocks, int rows, int k, int8_t *codes, float *scales, int scale_stride,

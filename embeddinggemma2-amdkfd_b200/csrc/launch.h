@@ -51,7 +51,10 @@ cudaError_t launch_post_add(float *x, const float *h, const float *w, const floa
 cudaError_t launch_gelu_mul(float *g, const float *u, size_t n, cudaStream_t s, int tier = 0);
 cudaError_t launch_gate_quant(int8_t *q, float *qs, int qs_stride, const float *x, const float *other, int rows,
                               int width, int other_stride, int other_offset, cudaStream_t s, int tier = 0);
-cudaError_t launch_pool_l2(float *out, const float *y, const unsigned *offsets, int batch, int width, cudaStream_t s);
+// Mean pool then L2 of `batch` sequences; with count set (device memory), only
+// the first *count of them (batch is then an upper bound, the launch grid).
+cudaError_t launch_pool_l2(float *out, const float *y, const unsigned *offsets, int batch, int width, cudaStream_t s,
+                           const unsigned *count = nullptr);
 // chunk > 0: rows interleaved with another matrix in chunk-row blocks, this
 // one at position `phase` (0 or 1) of each pair.
 cudaError_t launch_repack_q8(const void *blocks, int rows, int k, int8_t *codes, float *scales, int scale_stride,

@@ -276,13 +276,14 @@ __global__ void gelu_mul_kernel(float *__restrict__ g, const float *__restrict__
 // Mean pool then L2 (gemma2_fast.c:1000-1008), in two launches.
 // pool_mean_kernel: o[z] = sum over the sequence's tokens, in token order, of
 // y[t][z] / len -- one thread per (sequence, column), loads batched 8 tokens
-// ahead of the in-order adds; the result goes straight into out.
+// ahead of the in-order adds; the result goes straight into out.  With count
+// set, sequences from *count on (beyond the wave's batch) are skipped.
 __global__ void pool_mean_kernel(float *__restrict__ out, const float *__restrict__ y,
-                                 const unsigned *__restrict__ offsets, int width) {
+                                 const unsigned *__restrict__ offsets, int width, const unsigned *__restrict__ count) {
     pdl_wait();
     pdl_trigger();
     const int s = blockIdx.y, z = blockIdx.x * blockDim.x + threadIdx.x;
-    if (z >= width) return;
+    if (z >= width || (count && unsigned(s) >= *count)) return;
     const unsigned lo = offsets[s], hi = offsets[s + 1];
     const float len = float(hi - lo);
     const float *col = y + z;
@@ -301,10 +302,11 @@ __global__ void pool_mean_kernel(float *__restrict__ out, const float *__restric
 // pool_l2_kernel: one warp per sequence; the SSE2 sum of squares of
 // kernels.c:82-93 (lanes 0..7 are its two 4-lane accumulators over 8-element
 // chunks, each summed in chunk order), then x *= 1/sqrt(ss) (kernels.c:393-396).
-__global__ void pool_l2_kernel(float *__restrict__ out, int width) {
+__global__ void pool_l2_kernel(float *__restrict__ out, int width, const unsigned *__restrict__ count) {
     pdl_wait();
     pdl_trigger();
     const int s = blockIdx.x, lane = threadIdx.x;
+    if (count && unsigned(s) >= *count) return;  // warp-uniform
     float *o = out + size_t(s) * width;
     float acc = 0.0f;
     if (lane < 8)
