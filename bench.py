@@ -4,7 +4,10 @@
 
 One step = one packed wave through the whole 24-layer graph on each GPU
 (config 1: 16 sequences x 128 tokens = 2048 tokens; config 2: 1 x 2048;
-config 0: the 4-sequence parity wave).  Every rank holds its own weight
+config 0: the 4-sequence parity wave).  Config 3 runs the mixed-length request
+load (256 requests x 16 texts, packed into waves) through the executor and
+reports tokens/s and request latency; config 4 is the Q8_0 GEMM microbench at
+the model's shapes.  Every rank holds its own weight
 replica and embeds its own wave (weak scaling, no data-path collective); the
 process group only provides the barrier and the max-over-ranks time.
 
@@ -36,7 +39,11 @@ sys.path.insert(0, os.path.join(ROOT, "oracle"))
 METRIC = "embedded tokens/s per box (2048-token waves)"
 CONFIGS = {0: ("config0: 4 sequences, bodies 8/17/33/64 + BOS/EOS (130 tokens)", (8, 17, 33, 64)),
            1: ("config1: 16 x 128-token sequences = one 2048-token wave", (126,) * 16),
-           2: ("config2: 1 x 2048-token sequence", (2046,))}
+           2: ("config2: 1 x 2048-token sequence", (2046,)),
+           3: ("config3: mixed load, 256 requests x 16 texts, lognormal lengths (median 48), packed waves", None),
+           4: ("config4: Q8_0 GEMM microbench at the model's shapes, M = 2048 tokens", None)}
+METRIC_MIXED = "embedded tokens/s per box (mixed-length requests, executor level)"
+METRIC_GEMM = "Q8_0 GEMM TOP/s (model shapes, M = 2048)"
 
 
 def q8_gemm_ops(n_tokens: int) -> float:
@@ -172,9 +179,71 @@ def whole_job_rate(tokens_per_rank, world, steps, ms_max):
     return tokens_per_rank * world * steps / (ms_max * 1e-3)
 
 
+def reference_arm_mixed(args):
+    """Config 3 on the reference's CPU graph: the first `steps` packed waves of
+    rank 0's requests (a bounded sample of the load), tokens / wall time."""
+    import oracle
+    syn = importlib.import_module("embeddinggemma2-amdkfd_b200.synthetic")
+    lens, _ = syn.mixed_load(256, 16)
+    waves = pack_waves(lens, list(range(len(lens))))[:max(1, args.steps)]
+    ref = oracle.RefGraph(syn.model_path(1234, "baseline"), 0)
+    inputs = [wave_inputs(w, seed=1000 + i) for i, w in enumerate(waves)]
+    ref.embed(*inputs[0])
+    t0 = time.perf_counter()
+    for ids, off in inputs:
+        ref.embed(ids, off)
+    sec = time.perf_counter() - t0
+    tokens = sum(int(off[-1]) for _, off in inputs)
+    cpu = {"value": tokens / sec, "unit": "tokens/s", "cores": ref.threads, "kind": "reference", "tier": ref.tier,
+           "sample": f"first {len(waves)} packed waves of the config-3 load ({tokens} tokens), "
+                     f"ei_gemma2_embed_batch_fast_ctx with {ref.threads} threads"}
+    ref.close()
+    line = {"metric": METRIC_MIXED, "value": cpu["value"], "unit": "tokens/s", "n_gpus": args.gpus, "steps": len(waves),
+            "warmup": 1, "ms_per_step": sec * 1e3 / len(waves), "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "int8+fp32", "data": "synthetic", "config": {"workload": CONFIGS[3][0]},
+            "impl": "reference", "cpu_baseline": cpu,
+            "e2e": {"value": cpu["value"], "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def reference_arm_gemm(args):
+    """Config 4 on the CPU: the restatement of the reference's gemm_q8 (scalar
+    C, oracle/eg2_oracle.c) per shape on 64 tokens, scaled to TOP/s."""
+    import oracle
+    oracle.build(ref=False)
+    port = oracle.Port()
+    rng = np.random.default_rng(4)
+    M, tot_ops, tot_s, rows = 64, 0.0, 0.0, []
+    for k, n, name in GEMM_SHAPES:
+        xq = rng.integers(-127, 128, size=(M, k), dtype=np.int8)
+        wq = rng.integers(-127, 128, size=(n, k), dtype=np.int8)
+        xd = np.full((M, k // 32), 0x3C00, np.uint16)
+        wd = np.full((n, k // 32), 0x3C00, np.uint16)
+        port.gemm_q8(wq, wd, xq, xd)
+        t0 = time.perf_counter()
+        port.gemm_q8(wq, wd, xq, xd)
+        sec = time.perf_counter() - t0
+        ops_ = 2.0 * M * n * k
+        tot_ops, tot_s = tot_ops + ops_, tot_s + sec
+        rows.append({"shape": f"{k}->{n}", "use": name, "top_s": ops_ / sec / 1e12})
+    v = tot_ops / tot_s / 1e12
+    cpu = {"value": v, "unit": "TOP/s", "cores": 1, "kind": "port",
+           "sample": "64 tokens per shape through the scalar C restatement of gemm_q8, one thread"}
+    line = {"metric": METRIC_GEMM, "value": v, "unit": "TOP/s", "n_gpus": 1, "steps": 1, "warmup": 1,
+            "ms_per_step": tot_s * 1e3, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "int8 (int32 block sums, fp32 scaling)", "data": "synthetic",
+            "config": {"workload": CONFIGS[4][0], "M": M}, "impl": "reference", "cpu_baseline": cpu, "shapes": rows,
+            "e2e": {"value": v, "unit": "TOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
 def reference_arm(args, rank, world):
     if rank != 0:
         return
+    if args.config == 3:
+        return reference_arm_mixed(args)
+    if args.config == 4:
+        return reference_arm_gemm(args)
     syn = importlib.import_module("embeddinggemma2-amdkfd_b200.synthetic")
     desc, lengths = CONFIGS[args.config]
     model = syn.model_path(1234, "baseline")
@@ -187,6 +256,185 @@ def reference_arm(args, rank, world):
                        "BASELINE weight distributions)", "tokens_per_wave": n},
             "impl": "reference", "cpu_baseline": cpu,
             "e2e": {"value": cpu["value"], "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+# ---------------------------------------------------------------- config 3
+def pack_waves(lens, requests, cap=2048):
+    """Texts of the given requests, in order, packed greedily into waves of at
+    most cap tokens.  Returns [(request, text, packed_length)] per wave."""
+    waves, cur, used = [], [], 0
+    for r in requests:
+        for j, body in enumerate(lens[r]):
+            n = int(body) + 2
+            if used + n > cap:
+                waves.append(cur)
+                cur, used = [], 0
+            cur.append((r, j, n))
+            used += n
+    if cur:
+        waves.append(cur)
+    return waves
+
+
+def wave_inputs(wave, seed):
+    """Token ids and offsets of a packed wave (BOS + random body + EOS per text)."""
+    syn = importlib.import_module("embeddinggemma2-amdkfd_b200.synthetic")
+    return syn.wave([n - 2 for _, _, n in wave], seed=seed)
+
+
+def mixed_load_run(args, rank, world, local):
+    """Config 3 at the executor: this rank's requests (r % world == rank), all
+    queued at t = 0, packed into waves and embedded through ei_gemma2_kfd_batch
+    with host buffers, each text truncated to its request's dimensions and
+    renormalised (Matryoshka).  A request completes when its last text does."""
+    import torch
+    eg2 = importlib.import_module("embeddinggemma2-amdkfd_b200")
+    syn = eg2.synthetic
+    lens, dims = syn.mixed_load(256, 16)
+    mine = [r for r in range(len(lens)) if r % world == rank]
+    waves = pack_waves(lens, mine)
+    inputs = [wave_inputs(w, seed=1000 + 7919 * rank + i) for i, w in enumerate(waves)]
+    torch.cuda.set_device(local)
+    model = eg2.GGUFModel(syn.model_path(1234, "baseline"))
+    ex = eg2.Gemma2Executor(model, local)
+
+    def run_all():
+        remaining = {r: len(lens[r]) for r in mine}
+        done_at, t0 = {}, time.perf_counter()
+        for w, (ids, off) in zip(waves, inputs):
+            out = ex.batch(ids, off)
+            now = time.perf_counter()
+            for i, (r, _, _) in enumerate(w):
+                eg2.normalize_prefix(out[i], int(dims[r]))
+                remaining[r] -= 1
+                if remaining[r] == 0:
+                    done_at[r] = (now - t0) * 1000.0
+        return (time.perf_counter() - t0) * 1000.0, done_at
+
+    run_all()  # warm-up: captures the CUDA graph of every bucket the load uses
+    barrier(world)
+    with ClockSampler(local) as clocks:
+        ms, done_at = run_all()
+    barrier(world)
+    ms_max = reduce_max(ms, world, f"cuda:{local}")
+    tokens = sum(n for w in waves for _, _, n in w)
+    lat = list(done_at.values())
+    if world > 1:
+        import torch.distributed as dist
+        tot = torch.tensor([float(tokens)], device=f"cuda:{local}")
+        dist.all_reduce(tot)
+        tokens = int(tot.item())
+        gathered = [None] * world
+        dist.all_gather_object(gathered, lat)
+        lat = [x for g in gathered for x in g]
+    line = {"metric": METRIC_MIXED, "value": tokens / (ms_max * 1e-3), "unit": "tokens/s", "n_gpus": world,
+            "steps": 1, "warmup": 1, "ms_per_step": ms_max, "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "int8+fp32", "data": "synthetic",
+            "config": {"workload": CONFIGS[3][0], "requests": len(lens), "texts_per_request": len(lens[0]),
+                       "tokens": tokens, "waves_per_rank": len(waves),
+                       "arrival": "all requests queued at t = 0 (offline load); one executor per GPU",
+                       "parallelism": f"replicas x{world}, request r served by rank r % {world}"},
+            "latency_ms": {"p50": float(np.percentile(lat, 50)), "p99": float(np.percentile(lat, 99)),
+                           "max": float(max(lat))},
+            "clocks": clocks.summary()}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    del ex
+    model.close()
+
+
+# ---------------------------------------------------------------- config 4
+GEMM_SHAPES = [(512, 2048, "q|k|v local"), (512, 3072, "q|k|v global"), (1024, 512, "attn_output local"),
+               (2048, 512, "attn_output global, ffn_down"), (512, 4096, "ffn gate|up (GeGLU epilogue)"),
+               (512, 512, "inp_gate, proj"), (512, 768, "output")]
+
+
+def gemm_microbench(args, local):
+    """Config 4: each Q8_0 GEMM shape of the model at M = 2048 tokens, timed as a
+    CUDA graph of `steps` launches (inputs resident, each launch re-reads its
+    operands), plus an exactness check of the int32 block sums (unit scales:
+    every output is an exact integer sum) against numpy on 64 tokens."""
+    import torch
+    ops = importlib.import_module("embeddinggemma2-amdkfd_b200.ops")
+    torch.cuda.set_device(local)
+    dev = f"cuda:{local}"
+    M = 2048
+    rng = np.random.default_rng(4)
+    pk, src = peaks()
+    peak = 2.0 * pk["bf16_tflops"]
+    rows, tot_ops, tot_s, exact_all = [], 0.0, 0.0, True
+    for k, n, name in GEMM_SHAPES:
+        geglu = "GeGLU" in name
+        xq = rng.integers(-127, 128, size=(M, k), dtype=np.int8)
+        wq = rng.integers(-127, 128, size=(n, k), dtype=np.int8)
+        xs1 = torch.ones(k // 32 * M, device=dev)
+        ws1 = torch.ones(k // 32 * n, device=dev)
+        xt, wt = torch.from_numpy(xq).to(dev), torch.from_numpy(wq).to(dev)
+        if geglu:
+            q = torch.zeros(M * n // 2, dtype=torch.int8, device=dev)
+            sc = torch.zeros(n // 64 * M, device=dev)
+            launch = lambda: ops.q8_geglu(q, sc, M, xt, xs1, M, wt, ws1, M, k, n // 2)
+        else:
+            out = torch.zeros(M * n, device=dev)
+            launch = lambda: ops.q8_mm(out, xt, xs1, M, wt, ws1, M, k, n)
+            launch()
+            torch.cuda.synchronize()
+            got = out.view(M, n)[:64].cpu().numpy().astype(np.int64)
+            ref = xq[:64].astype(np.int64) @ wq.astype(np.int64).T
+            exact = bool(np.array_equal(got, ref))
+            exact_all &= exact
+        for _ in range(args.warmup):
+            launch()
+        g = torch.cuda.CUDAGraph()
+        s = torch.cuda.Stream(device=dev)
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
+            with torch.cuda.graph(g, stream=s):
+                for _ in range(args.steps):
+                    launch()
+        torch.cuda.synchronize()
+        g.replay()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        g.replay()
+        e1.record()
+        torch.cuda.synchronize()
+        us = e0.elapsed_time(e1) * 1000.0 / args.steps
+        ops_ = 2.0 * M * n * k
+        tot_ops, tot_s = tot_ops + ops_, tot_s + us * 1e-6
+        rows.append({"shape": f"{k}->{n}", "use": name, "us": round(us, 2), "top_s": round(ops_ / us / 1e6, 1),
+                     "frac_of_peak": round(ops_ / us / 1e6 / peak, 4),
+                     "int32_block_sums_exact": None if geglu else exact})
+        del g
+    # BF16 PLE projection 512 -> 12288 (fp32 activations split hi + lo).
+    x = torch.randn(M, 512, device=dev)
+    hi = x.to(torch.bfloat16)
+    lo = (x - hi.float()).to(torch.bfloat16)
+    w = (torch.randn(12288, 512, device=dev) / 22.6).to(torch.bfloat16)
+    nw = torch.ones(512, device=dev)
+    ple = torch.zeros(M * 12288, device=dev)
+    pl = lambda: ops.ple_proj(ple, hi.view(torch.uint16), lo.view(torch.uint16), w.view(torch.uint16), nw, M)
+    for _ in range(args.warmup):
+        pl()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        pl()
+    e1.record()
+    torch.cuda.synchronize()
+    ple_us = e0.elapsed_time(e1) * 1000.0 / args.steps
+    line = {"metric": METRIC_GEMM, "value": tot_ops / tot_s / 1e12, "unit": "TOP/s", "n_gpus": 1,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": tot_s * 1e3, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "int8 (int32 block sums, fp32 scaling)",
+            "data": "synthetic", "config": {"workload": CONFIGS[4][0], "M": M},
+            "peak": {"value": peak, "unit": "TOP/s", "source": f"2 x bf16_tflops of {src} MEASURED_PEAKS"},
+            "int32_block_sums_exact": exact_all, "shapes": rows,
+            "ple_bf16": {"shape": "512->12288", "us": round(ple_us, 2),
+                         "tflop_s_executed": round(2.0 * 2 * M * 12288 * 512 / ple_us / 1e6, 1),
+                         "note": "eager launches; hi + lo halves, so 2x the algorithmic 25.8 GFLOP"}}
     print(json.dumps(line), flush=True)
 
 
@@ -203,6 +451,13 @@ def main():
     rank, world, local = dist_init()
     if args.impl == "reference":
         reference_arm(args, rank, world)
+        return finalize(world)
+    if args.config == 3:
+        mixed_load_run(args, rank, world, local)
+        return finalize(world)
+    if args.config == 4:
+        if rank == 0:
+            gemm_microbench(args, local)
         return finalize(world)
 
     import torch
