@@ -285,9 +285,10 @@ def wave_inputs(wave, seed):
 
 def mixed_load_run(args, rank, world, local):
     """Config 3 at the executor: this rank's requests (r % world == rank), all
-    queued at t = 0, packed into waves and embedded through ei_gemma2_kfd_batch
-    with host buffers, each text truncated to its request's dimensions and
-    renormalised (Matryoshka).  A request completes when its last text does."""
+    queued at t = 0, packed into waves and embedded with host buffers through
+    the two-slot pipelined form of ei_gemma2_kfd_batch, each text truncated to
+    its request's dimensions and renormalised (Matryoshka).  A request
+    completes when its last text does."""
     import torch
     eg2 = importlib.import_module("embeddinggemma2-amdkfd_b200")
     syn = eg2.synthetic
@@ -300,16 +301,28 @@ def mixed_load_run(args, rank, world, local):
     ex = eg2.Gemma2Executor(model, local)
 
     def run_all():
+        """Two waves in flight (eg2_b200_submit / eg2_b200_collect): the host
+        truncates one wave's embeddings while the GPU runs the next."""
         remaining = {r: len(lens[r]) for r in mine}
         done_at, t0 = {}, time.perf_counter()
-        for w, (ids, off) in zip(waves, inputs):
-            out = ex.batch(ids, off)
+
+        def complete(slot, w):
+            out = ex.collect(slot)
             now = time.perf_counter()
             for i, (r, _, _) in enumerate(w):
                 eg2.normalize_prefix(out[i], int(dims[r]))
                 remaining[r] -= 1
                 if remaining[r] == 0:
                     done_at[r] = (now - t0) * 1000.0
+
+        pending = None
+        for w, (ids, off) in zip(waves, inputs):
+            slot = ex.submit(ids, off)
+            if pending:
+                complete(*pending)
+            pending = (slot, w)
+        if pending:
+            complete(*pending)
         return (time.perf_counter() - t0) * 1000.0, done_at
 
     run_all()  # warm-up: captures the CUDA graph of every bucket the load uses

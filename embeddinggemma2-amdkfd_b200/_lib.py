@@ -30,6 +30,8 @@ SIGNATURES = {
     "eg2_b200_stage": (b, [vp, vp, vp, sz, cstr, sz]),
     "eg2_b200_launch": (b, [vp, i32, cstr, sz]),
     "eg2_b200_finish": (b, [vp, vp, cstr, sz]),
+    "eg2_b200_submit": (i32, [vp, vp, vp, sz, cstr, sz]),
+    "eg2_b200_collect": (b, [vp, i32, vp, cstr, sz]),
     "eg2_b200_stream": (vp, [vp]),
     "eg2_b200_kernels_per_wave": (i32, [vp]),
     "eg2_b200_profile": (i32, [vp, vp, vp, i32]),

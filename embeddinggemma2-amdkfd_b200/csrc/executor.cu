@@ -123,10 +123,20 @@ struct Backend {
     float *qf = nullptr, *kf = nullptr, *vf = nullptr;
 
     // host staging (pinned)
-    uint32_t *h_in = nullptr;  // ids | bounds(2) | pos | offsets | sequence count
-    float *h_out = nullptr;
-    int *h_err = nullptr;      // the device error word, read back with each wave
-    cudaEvent_t done = nullptr;
+    // Host staging (pinned), one set per pipeline slot: a wave can be submitted
+    // to one slot while the wave of the other slot is still on the GPU (stream
+    // order keeps the single device input block and output buffer safe).
+    static constexpr int SLOTS = 2;
+    struct Slot {
+        uint32_t *in = nullptr;  // ids | bounds(2) | pos | offsets | sequence count
+        float *out = nullptr;
+        int *err = nullptr;  // the device error word, read back with the wave
+        cudaEvent_t done = nullptr;
+        size_t batch = 0;
+        bool busy = false;
+    };
+    Slot slots[SLOTS];
+    int next_slot = 0;
 
     // graphs per wave shape
     std::map<uint64_t, cudaGraphExec_t> graphs;
@@ -224,7 +234,7 @@ struct Backend {
             throw std::runtime_error(std::string("supported CUDA device not found (sm_100 required, got ") +
                                      prop.name + ")");
         ck(cudaStreamCreateWithFlags(&stream, cudaStreamNonBlocking), "cudaStreamCreate");
-        ck(cudaEventCreateWithFlags(&done, cudaEventDisableTiming), "cudaEventCreate");
+        for (Slot &sl : slots) ck(cudaEventCreateWithFlags(&sl.done, cudaEventDisableTiming), "cudaEventCreate");
         ck(init_kernel_attributes(), "kernel attributes");
 
         // ---- weights
@@ -335,9 +345,11 @@ struct Backend {
         if (!bf16_tmap(&tm_hi, x_hi, 512, CAP, 128) || !bf16_tmap(&tm_lo, x_lo, 512, CAP, 128) ||
             !bf16_tmap(&tm_ple, ple_w, 512, 24 * 512, 256))
             throw std::runtime_error("tensor map (PLE)");
-        ck(cudaMallocHost(&h_in, sizeof(uint32_t) * (5 * CAP + 2)), "cudaMallocHost");
-        ck(cudaMallocHost(&h_err, sizeof(int)), "cudaMallocHost");
-        ck(cudaMallocHost(&h_out, sizeof(float) * CAP * 768), "cudaMallocHost");
+        for (Slot &sl : slots) {
+            ck(cudaMallocHost(&sl.in, sizeof(uint32_t) * (5 * CAP + 2)), "cudaMallocHost");
+            ck(cudaMallocHost(&sl.err, sizeof(int)), "cudaMallocHost");
+            ck(cudaMallocHost(&sl.out, sizeof(float) * CAP * 768), "cudaMallocHost");
+        }
         ck(cudaStreamSynchronize(stream), "weight upload");
         clear_device_error();
         if (std::getenv("EG2_B200_VERBOSE")) {
@@ -353,10 +365,12 @@ struct Backend {
         if (stream) cudaStreamSynchronize(stream);
         for (auto &kv : graphs) cudaGraphExecDestroy(kv.second);
         for (void *p : allocations) cudaFree(p);
-        if (h_in) cudaFreeHost(h_in);
-        if (h_err) cudaFreeHost(h_err);
-        if (h_out) cudaFreeHost(h_out);
-        if (done) cudaEventDestroy(done);
+        for (Slot &sl : slots) {
+            if (sl.in) cudaFreeHost(sl.in);
+            if (sl.err) cudaFreeHost(sl.err);
+            if (sl.out) cudaFreeHost(sl.out);
+            if (sl.done) cudaEventDestroy(sl.done);
+        }
         if (stream) cudaStreamDestroy(stream);
     }
 
@@ -475,12 +489,12 @@ struct Backend {
         return exec;
     }
 
-    // gemma2_kfd.cpp:271-296: validation, bounds and positions, then upload.
-    void stage(const int32_t *in_ids, const size_t *in_off, size_t batch) {
-        if (poisoned) throw std::runtime_error("KFD context failed; restart process before reuse");
+    // gemma2_kfd.cpp:271-296: validation, bounds and positions into a slot's
+    // staging buffer, padded to the bucket; returns the padded token count.
+    unsigned fill(Slot &sl, const int32_t *in_ids, const size_t *in_off, size_t batch) {
         validate_wave(in_ids, in_off, batch);
         const unsigned n = unsigned(in_off[batch]);
-        uint32_t *hid = h_in, *hb = h_in + CAP, *hp = h_in + 3 * CAP, *ho = h_in + 4 * CAP;  // device layout
+        uint32_t *hid = sl.in, *hb = sl.in + CAP, *hp = sl.in + 3 * CAP, *ho = sl.in + 4 * CAP;  // device layout
         std::memcpy(hid, in_ids, n * sizeof(int32_t));
         for (size_t s = 0; s < batch; ++s) {
             ho[s] = uint32_t(in_off[s]);
@@ -493,9 +507,19 @@ struct Backend {
         // Padding to the bucket: one sequence [n, n_pad) of token 0, never pooled.
         const unsigned n_pad = (n + BUCKET - 1) / BUCKET * BUCKET;
         for (unsigned t = n; t < n_pad; ++t) hid[t] = 0, hb[2 * t] = n, hb[2 * t + 1] = n_pad, hp[t] = t - n;
-        h_in[5 * CAP + 1] = uint32_t(batch);
+        sl.in[5 * CAP + 1] = uint32_t(batch);
         ck(cudaSetDevice(device), "cudaSetDevice");
-        ck(cudaMemcpyAsync(ids, h_in, (5 * CAP + 2) * 4, cudaMemcpyHostToDevice, stream), "wave upload");
+        ck(cudaMemcpyAsync(ids, sl.in, (5 * CAP + 2) * 4, cudaMemcpyHostToDevice, stream), "wave upload");
+        return n_pad;
+    }
+
+    // Split form for device-resident timing: stage once, launch the staged graph
+    // any number of times, finish.  Not to be interleaved with submit/collect.
+    void stage(const int32_t *in_ids, const size_t *in_off, size_t batch) {
+        if (poisoned) throw std::runtime_error("KFD context failed; restart process before reuse");
+        for (const Slot &sl : slots)
+            if (sl.busy) throw std::runtime_error("a submitted wave is not collected yet");
+        const unsigned n_pad = fill(slots[0], in_ids, in_off, batch);
         staged_graph = graph_for(n_pad);
         staged_n = n_pad, staged_batch = batch;
     }
@@ -506,49 +530,81 @@ struct Backend {
         for (int r = 0; r < repeats; ++r) ck(cudaGraphLaunch(staged_graph, stream), "graph launch");
     }
 
-    // Wait with the reference's deadline; any failure poisons the context.
-    void wait_done() {
+    // Enqueue a slot's readback (embeddings, error word) and completion event.
+    void enqueue_readback(Slot &sl, size_t batch) {
+        if (batch) ck(cudaMemcpyAsync(sl.out, pooled, batch * 768 * 4, cudaMemcpyDeviceToHost, stream), "readback");
+        ck(read_device_error_async(sl.err, stream), "error readback");
+        ck(cudaEventRecord(sl.done, stream), "event record");
+    }
+
+    // Wait for a slot with the reference's deadline; any failure poisons the context.
+    void wait_slot(Slot &sl) {
         poisoned = true;
-        ck(read_device_error_async(h_err, stream), "error readback");
-        ck(cudaEventRecord(done, stream), "event record");
         // Poll without sleeping for the length of a few waves, then back off.
         const auto t0 = std::chrono::steady_clock::now();
         for (;;) {
-            const cudaError_t q = cudaEventQuery(done);
+            const cudaError_t q = cudaEventQuery(sl.done);
             if (q == cudaSuccess) break;
             if (q != cudaErrorNotReady) ck(q, "GPU wave");
             const double waited = std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
             if (waited > TIMEOUT_S) throw std::runtime_error("GPU wave timed out");
             if (waited > 0.02) std::this_thread::sleep_for(std::chrono::microseconds(50));
         }
-        const int derr = *h_err;
+        const int derr = *sl.err;
         if (derr) throw std::runtime_error("device wait timed out inside a kernel (error " + std::to_string(derr) + ")");
         poisoned = false;
     }
 
-    void finish(float *out) {
-        if (poisoned) throw std::runtime_error("KFD context failed; restart process before reuse");
-        if (!staged_graph) throw std::runtime_error("no wave staged");
-        ck(cudaMemcpyAsync(h_out, pooled, staged_batch * 768 * 4, cudaMemcpyDeviceToHost, stream), "readback");
-        wait_done();
-        // gemma2_kfd.cpp:337-343: finite, non-zero; the embedding is already L2-normalised on the device.
-        for (size_t s = 0; s < staged_batch; ++s) {
+    // gemma2_kfd.cpp:337-343: finite, non-zero; the embedding is already
+    // L2-normalised on the device.
+    void deliver(const Slot &sl, size_t batch, float *out) {
+        for (size_t s = 0; s < batch; ++s) {
             double ss = 0;
             for (int z = 0; z < 768; ++z) {
-                const float f = h_out[s * 768 + z];
+                const float f = sl.out[s * 768 + z];
                 if (!std::isfinite(f)) throw std::runtime_error("nonfinite GPU output");
                 ss += double(f) * f;
             }
             if (ss <= 0) throw std::runtime_error("zero GPU embedding");
         }
-        std::memcpy(out, h_out, staged_batch * 768 * sizeof(float));
+        std::memcpy(out, sl.out, batch * 768 * sizeof(float));
+    }
+
+    void finish(float *out) {
+        if (poisoned) throw std::runtime_error("KFD context failed; restart process before reuse");
+        if (!staged_graph) throw std::runtime_error("no wave staged");
+        enqueue_readback(slots[0], staged_batch);
+        wait_slot(slots[0]);
+        deliver(slots[0], staged_batch, out);
+    }
+
+    // Pipelined form: submit enqueues upload, graph and readback on the next
+    // slot and returns its index; collect waits for that slot and delivers.
+    // A slot must be collected before it is submitted to again.
+    int submit(const int32_t *in_ids, const size_t *in_off, size_t batch) {
+        if (poisoned) throw std::runtime_error("KFD context failed; restart process before reuse");
+        const int id = next_slot;
+        Slot &sl = slots[id];
+        if (sl.busy) throw std::runtime_error("pipeline slot busy: collect its wave first");
+        const unsigned n_pad = fill(sl, in_ids, in_off, batch);
+        ck(cudaGraphLaunch(graph_for(n_pad), stream), "graph launch");
+        enqueue_readback(sl, batch);
+        sl.batch = batch, sl.busy = true;
+        next_slot = (next_slot + 1) % SLOTS;
+        return id;
+    }
+
+    void collect(int id, float *out) {
+        if (id < 0 || id >= SLOTS || !slots[id].busy) throw std::runtime_error("no wave submitted to this slot");
+        Slot &sl = slots[id];
+        sl.busy = false;
+        wait_slot(sl);
+        deliver(sl, sl.batch, out);
     }
 
     void batch(const int32_t *in_ids, const size_t *in_off, size_t n_seq, float *out) {
         if (!out) throw std::runtime_error("KFD batch requires 1..2048 packed tokens and nonempty sequences");
-        stage(in_ids, in_off, n_seq);
-        launch(1);
-        finish(out);
+        collect(submit(in_ids, in_off, n_seq), out);
     }
 
     int profile(char names[][32], double *ms, int max) {
@@ -558,7 +614,8 @@ struct Backend {
         {
             Profiler prof{stream};
             enqueue(staged_n, stream, &prof);
-            wait_done();
+            enqueue_readback(slots[0], 0);
+            wait_slot(slots[0]);
             for (size_t i = 1; i < prof.events.size(); ++i) {
                 float t = 0;
                 ck(cudaEventElapsedTime(&t, prof.events[i - 1], prof.events[i]), "elapsed");
@@ -639,6 +696,25 @@ extern "C" bool eg2_b200_finish(void *ctx, float *out, char *err, size_t len) {
         if (!out) throw std::runtime_error("null output");
         ck(cudaSetDevice(b->device), "cudaSetDevice");
         b->finish(out);
+    });
+}
+extern "C" int eg2_b200_submit(void *ctx, const int32_t *ids, const size_t *offsets, size_t batch, char *err,
+                               size_t len) {
+    int slot = -1;
+    guarded(err, len, [&] {
+        Backend *b = as_backend(ctx);
+        std::lock_guard<std::mutex> guard(b->mutex);
+        slot = b->submit(ids, offsets, batch);
+    });
+    return slot;
+}
+extern "C" bool eg2_b200_collect(void *ctx, int slot, float *out, char *err, size_t len) {
+    return guarded(err, len, [&] {
+        Backend *b = as_backend(ctx);
+        std::lock_guard<std::mutex> guard(b->mutex);
+        if (!out) throw std::runtime_error("null output");
+        ck(cudaSetDevice(b->device), "cudaSetDevice");
+        b->collect(slot, out);
     });
 }
 extern "C" void *eg2_b200_stream(void *ctx) { return ctx ? static_cast<Backend *>(ctx)->stream : nullptr; }

@@ -98,6 +98,7 @@ class Gemma2Executor:
         self.ctx = ctx
         self.lib = lib
         self._staged_batch = 0
+        self._slot_batch = {}
 
     def batch(self, ids, offsets) -> np.ndarray:
         """Embed one packed wave: ids int32[n], offsets (batch+1) with offsets[0]=0."""
@@ -108,6 +109,27 @@ class Gemma2Executor:
                                           offsets.ctypes.data if offsets.size else None, max(batch, 0),
                                           out.ctypes.data, err, len(err))
         if not ok:
+            raise ExecutorError(err.value.decode())
+        return out[:batch]
+
+    # pipelined form: two slots, collect a slot before submitting to it again
+    def submit(self, ids, offsets) -> int:
+        """Stage and enqueue one packed wave; returns the slot to collect."""
+        ids, offsets, batch = _wave(ids, offsets)
+        err = _err()
+        slot = self.lib.eg2_b200_submit(self.ctx, ids.ctypes.data if ids.size else None,
+                                        offsets.ctypes.data if offsets.size else None, max(batch, 0), err, len(err))
+        if slot < 0:
+            raise ExecutorError(err.value.decode())
+        self._slot_batch[slot] = batch
+        return slot
+
+    def collect(self, slot: int) -> np.ndarray:
+        """Wait for a submitted wave and return its embeddings."""
+        batch = self._slot_batch.get(slot, 0)
+        out = np.zeros((max(batch, 1), EMBED_DIM), np.float32)
+        err = _err()
+        if not self.lib.eg2_b200_collect(self.ctx, slot, out.ctypes.data, err, len(err)):
             raise ExecutorError(err.value.decode())
         return out[:batch]
 

@@ -66,6 +66,16 @@ bool eg2_b200_stage(void *ctx, const int32_t *ids, const size_t *offsets, size_t
                     size_t len);
 bool eg2_b200_launch(void *ctx, int repeats, char *err, size_t len);
 bool eg2_b200_finish(void *ctx, float *out, char *err, size_t len);
+/* Pipelined form of ei_gemma2_kfd_batch with two slots (the role of the
+ * reference server's per-GPU pipeline slots, inference_service.c): submit
+ * validates and stages the wave, enqueues its upload, graph and readback, and
+ * returns the slot index (or -1 with err set); collect waits for that slot with
+ * the batch call's deadline and checks and copies its batch x 768 embeddings.
+ * Submits alternate between the two slots; a slot must be collected before it
+ * is submitted to again, so the host can prepare or post-process one wave while
+ * the GPU runs the other.  Same validation and errors as ei_gemma2_kfd_batch. */
+int eg2_b200_submit(void *ctx, const int32_t *ids, const size_t *offsets, size_t batch, char *err, size_t len);
+bool eg2_b200_collect(void *ctx, int slot, float *out, char *err, size_t len);
 /* The cudaStream_t the context launches on (for CUDA-event timing). */
 void *eg2_b200_stream(void *ctx);
 /* Kernels launched per wave by the staged graph. */

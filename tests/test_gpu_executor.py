@@ -62,6 +62,26 @@ def test_long_and_two_wave_goldens(executor, eg2):
     assert c2.min() >= 0.99 - MARGIN
 
 
+def test_submit_collect_pipeline_equals_batch(executor, syn):
+    """Two waves in flight through the pipelined pair give exactly the batch
+    call's embeddings; a slot cannot be submitted to again before collection."""
+    waves = [syn.wave(lens, seed=s) for s, lens in enumerate([(40, 7, 300), (126,) * 16, (5,), (900, 900)])]
+    expect = [executor.batch(ids, off) for ids, off in waves]
+    s0 = executor.submit(*waves[0])
+    s1 = executor.submit(*waves[1])
+    assert s0 != s1
+    with pytest.raises(Exception):
+        executor.submit(*waves[2])  # slot s0 is still in flight
+    np.testing.assert_array_equal(executor.collect(s0), expect[0])
+    s2 = executor.submit(*waves[2])
+    np.testing.assert_array_equal(executor.collect(s1), expect[1])
+    s3 = executor.submit(*waves[3])
+    np.testing.assert_array_equal(executor.collect(s2), expect[2])
+    np.testing.assert_array_equal(executor.collect(s3), expect[3])
+    with pytest.raises(Exception):
+        executor.collect(s3)  # already collected
+
+
 def test_packed_equals_solo_and_reorder(executor, syn):
     """tests/http_parity.py:62-69 (packed vs solo >= 0.99999, reorder
     invariance).  Every operation of a token depends only on its own sequence
