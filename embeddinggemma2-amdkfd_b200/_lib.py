@@ -61,6 +61,7 @@ SIGNATURES = {
     "eg2_repack_q8": (i32, [vp, u32, u32, vp, vp, vp]),
     "eg2_read_error": (i32, []),
     "eg2_clear_error": (None, []),
+    "eg2_selftest_wait_timeout": (i32, [vp]),
 }
 
 _lib = None

@@ -261,6 +261,17 @@ int read_device_error() {
     if (cudaMemcpyFromSymbol(&v, g_error, sizeof(int)) != cudaSuccess) return -1;
     return v;
 }
+// One bounded wait on a barrier that nothing arrives at: it runs out after its
+// limit (about 2 s), records ERR_WAIT_TIMEOUT in the error word and returns, as
+// any timed-out wait of the wave kernels would.  For tests of the failure path.
+__global__ void wait_timeout_selftest_kernel() {
+    __shared__ uint64_t bar;
+    if (threadIdx.x == 0) {
+        bar_init(&bar, 1);
+        fence_bar_init();
+        wait_bar(&bar, 0, nullptr);
+    }
+}
 cudaError_t read_device_error_async(int *host, cudaStream_t s) {
     return cudaMemcpyFromSymbolAsync(host, g_error, sizeof(int), 0, cudaMemcpyDeviceToHost, s);
 }
@@ -412,6 +423,10 @@ int eg2_launch_pool_l2(const EgPoolL2 *p, void *s) {
 int eg2_repack_q8(const void *blocks_dev, unsigned rows, unsigned k, int8_t *codes, float *scales, void *s) {
     if (k % 32) return rc(cudaErrorInvalidValue);
     return rc(launch_repack_q8(blocks_dev, int(rows), int(k), codes, scales, int(rows), S(s)));
+}
+int eg2_selftest_wait_timeout(void *s) {
+    wait_timeout_selftest_kernel<<<1, 32, 0, S(s)>>>();
+    return rc(cudaGetLastError());
 }
 int eg2_read_error(void) { return read_device_error(); }
 void eg2_clear_error(void) { clear_device_error(); }

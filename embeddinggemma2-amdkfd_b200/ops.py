@@ -132,3 +132,10 @@ def read_error() -> int:
 
 def clear_error():
     _lib.load().eg2_clear_error()
+
+
+def selftest_wait_timeout(stream=None):
+    """Enqueue a kernel whose bounded wait runs out (sets the error word)."""
+    rc = _lib.load().eg2_selftest_wait_timeout(C.c_void_p(stream) if stream is not None else _stream())
+    if rc:
+        raise RuntimeError(f"eg2_selftest_wait_timeout failed with CUDA error {rc}")

@@ -151,6 +151,12 @@ int eg2_repack_q8(const void *blocks_dev, unsigned rows, unsigned k, int8_t *cod
  * wait that ran out sets it; 0 means no error.  eg2_clear_error resets it. */
 int eg2_read_error(void);
 void eg2_clear_error(void);
+/* Failure-path self test (no counterpart in the reference): enqueues a kernel
+ * whose one bounded wait can never complete, so that after its limit (about
+ * 2 s) it sets the error word (1, a timed-out wait) and returns; the GPU and the
+ * context stay usable.  Queued before a wave on an executor's stream, it makes
+ * that wave fail as a real timeout would. */
+int eg2_selftest_wait_timeout(void *stream);
 #ifdef __cplusplus
 }
 #endif
