@@ -53,6 +53,8 @@ SIGNATURES = {
     "eg2_launch_q8_geglu": (i32, [vp, vp]),
     "eg2_launch_qkv_post": (i32, [vp, vp]),
     "eg2_launch_attention_f16": (i32, [vp, vp]),
+    "eg2_launch_attention_tc": (i32, [vp, vp]),
+    "eg2_launch_attention_tc_q8": (i32, [vp, vp]),
     "eg2_launch_attention_exact": (i32, [vp, u32, vp]),
     "eg2_launch_post_add": (i32, [vp, vp]),
     "eg2_launch_gate_quant": (i32, [vp, vp]),
@@ -153,6 +155,11 @@ class EgQkvPost(C.Structure):
 class EgAttentionF16(C.Structure):
     _fields_ = [("out", P), ("q", P), ("k", P), ("v", P), ("bounds", P), ("n", u32), ("d", u32),
                 ("window", u32)]
+
+
+class EgAttentionQ8(C.Structure):
+    _fields_ = [("q", P), ("qscale", P), ("scale_stride", u32), ("qh", P), ("k", P), ("v", P), ("bounds", P),
+                ("n", u32), ("window", u32), ("tier", u32)]
 
 
 class EgPostAdd(C.Structure):

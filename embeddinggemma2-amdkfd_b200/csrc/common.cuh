@@ -17,7 +17,7 @@ namespace eg2 {
 // wait is bounded, so a kernel that follows a failed one still terminates.
 // Defined here: the library has a single device translation unit (kernels.cu).
 __device__ int g_error = 0;
-enum : int { ERR_NONE = 0, ERR_WAIT_TIMEOUT = 1 };
+enum : int { ERR_NONE = 0, ERR_WAIT_TIMEOUT = 1, ERR_RANGE = 2 };
 
 // ---------------------------------------------------------------- basics
 __device__ __forceinline__ uint32_t smem_u32(const void *p) {
@@ -121,6 +121,16 @@ __device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, u
         : "memory");
 }
 
+// 3-D tiled load (no multicast); c0 (innermost, elements) is always a multiple
+// of 64 16-bit elements here, so c0 * element size is a multiple of 16 bytes.
+__device__ __forceinline__ void tma_load_3d(void *dst, const CUtensorMap *map, uint64_t *bar, int c0, int c1, int c2) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(
+            smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2)
+        : "memory");
+}
+
 // ---------------------------------------------------------------- tcgen05
 __device__ __forceinline__ void tmem_alloc(uint32_t *dst_smem, uint32_t ncols) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(dst_smem)),
@@ -159,6 +169,23 @@ __device__ __forceinline__ void mma_f16(uint32_t tmem_d, uint64_t adesc, uint64_
         "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
         : "memory");
 }
+// As mma_f16 with the A operand (M rows x K 16-bit elements) in tensor memory:
+// row i in lane i, elements 2c and 2c + 1 packed (low, high) in column c.
+__device__ __forceinline__ void mma_f16_ts(uint32_t tmem_d, uint32_t tmem_a, uint64_t bdesc, uint32_t idesc,
+                                           uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(tmem_d),
+        "r"(tmem_a), "l"(bdesc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+// 2^x by the MUFU approximation (relative error about 2^-22; -inf -> +0).
+__device__ __forceinline__ float ex2_approx(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
 // Instruction descriptors (tcgen05 instruction-descriptor bit layout):
 // [4,6) D format, [7,10) A format, [10,13) B format, [15] A MN-major,
 // [16] B MN-major, [17,23) N>>3, [24,29) M>>4.  A and B always share a type.
@@ -167,6 +194,19 @@ __host__ __device__ constexpr uint32_t idesc_i8(int M, int N) {
 }
 __host__ __device__ constexpr uint32_t idesc_bf16(int M, int N) {
     return (1u << 4) | (1u << 7) | (1u << 10) | (uint32_t(N >> 3) << 17) | (uint32_t(M >> 4) << 24);
+}
+// kind::f16 with fp16 A and B and fp32 D; b_mn: B is MN-major (its N
+// dimension contiguous in shared memory).
+__host__ __device__ constexpr uint32_t idesc_f16(int M, int N, bool b_mn = false) {
+    return (1u << 4) | (b_mn ? (1u << 16) : 0u) | (uint32_t(N >> 3) << 17) | (uint32_t(M >> 4) << 24);
+}
+// Shared-memory descriptor for an MN-major 16-bit operand with 128-byte
+// swizzle: 64-element (128-byte) rows along MN, 8 consecutive K rows per
+// 1024-byte atom (SBO = 1024), and lbo bytes between successive 64-element
+// blocks along MN.  Advancing along K by 16 rows adds 2048 bytes to saddr.
+__device__ __forceinline__ uint64_t desc_mn_sw128(uint32_t saddr, uint32_t lbo) {
+    return (uint64_t)((saddr & 0x3FFFFu) >> 4) | ((uint64_t)(lbo >> 4) << 16) | ((uint64_t)(1024 >> 4) << 32) |
+           ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
 }
 // Shared-memory matrix descriptor for a K-major operand written by TMA with
 // 128-byte swizzle: rows of 128 B, 8-row atoms of 1024 B (SBO), version 1,
@@ -177,6 +217,20 @@ __device__ __forceinline__ uint64_t desc_sw128(uint32_t saddr) {
     return (uint64_t)((saddr & 0x3FFFFu) >> 4) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) |
            ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
 }
+// 32 registers per thread -> 32 lanes x 32 consecutive 32-bit TMEM columns.
+// Warp-collective; complete with tmem_wait_st().
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t *r) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
+        "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+        "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+        "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]),
+        "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]), "r"(r[16]), "r"(r[17]), "r"(r[18]),
+        "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]),
+        "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
+        : "memory");
+}
+__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 // 32 lanes x 32 consecutive 32-bit TMEM columns -> 32 registers per thread.
 // Warp-collective: every lane of the warp must execute it.
 __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t *r) {

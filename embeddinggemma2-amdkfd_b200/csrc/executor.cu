@@ -389,6 +389,10 @@ struct Backend {
             if (prof) prof->mark(name);
         };
         const int N = int(n);
+        // Sliding-window layers (d = 256) run the tensor-core attention through
+        // maps whose token extent is this wave's N (captured into its graph).
+        AttnTcMaps tc_maps{};
+        if (!exact && !attention_tc_maps(&tc_maps, qh, kh, vh, N)) ck(cudaErrorInvalidValue, "attention maps");
         mark("start");
         ck(launch_embed(x, x_hi, x_lo, token_embd, ids, N, s), "embed"), ++launches;
         mark("embed");
@@ -418,12 +422,17 @@ struct Backend {
                    "qkv_post"),
                     ++launches;
                 mark("qkv_post");
-                ck(launch_attention(attn, qh, kh, vh, bounds, N, L.d, L.d == 512 ? 0 : 512, s), "attention"),
-                    ++launches;
+                if (L.d == 256)  // Q8 operand of the O projection written by the attention itself
+                    ck(launch_attention_tc(tc_maps, nullptr, bounds, N, 512, s, xq, xs, CAP, tier), "attention");
+                else
+                    ck(launch_attention(attn, qh, kh, vh, bounds, N, L.d, 0, s), "attention");
+                ++launches;
             }
             mark(L.d == 512 ? "attention_global" : "attention_local");
-            ck(launch_norm_quant(xq, xs, CAP, nullptr, attn, nullptr, N, 4 * L.d, s, tier), "quant"), ++launches;
-            mark("quant_attn");
+            if (exact || L.d == 512) {
+                ck(launch_norm_quant(xq, xs, CAP, nullptr, attn, nullptr, N, 4 * L.d, s, tier), "quant"), ++launches;
+                mark("quant_attn");
+            }
             gemm(L.o, h, 512, N, s), ++launches;
             mark("gemm_o");
             ck(launch_post_add(x, h, L.post_attn_norm, nullptr, xq, xs, CAP, L.ffn_norm, N, s, tier), "post_add"), ++launches;

@@ -101,6 +101,17 @@ def attention_f16(out, q, k, v, bounds, n, d, window):
     _call("eg2_launch_attention_f16", _lib.EgAttentionF16(_p(out), _p(q), _p(k), _p(v), _p(bounds), n, d, window))
 
 
+def attention_tc(out, q, k, v, bounds, n, window, d=256):
+    """attention_f16 on the tcgen05 tensor cores (d = 256, n <= 8192)."""
+    _call("eg2_launch_attention_tc", _lib.EgAttentionF16(_p(out), _p(q), _p(k), _p(v), _p(bounds), n, d, window))
+
+
+def attention_tc_q8(q, qscale, scale_stride, qh, k, v, bounds, n, window, tier=0):
+    """attention_tc with its output rows quantized to Q8_0 in the epilogue."""
+    _call("eg2_launch_attention_tc_q8", _lib.EgAttentionQ8(_p(q), _p(qscale), scale_stride, _p(qh), _p(k), _p(v),
+                                                           _p(bounds), n, window, tier))
+
+
 def post_add(x, h, weight, scale, q, qscale, scale_stride, next_weight, rows, tier=0):
     _call("eg2_launch_post_add", _lib.EgPostAdd(_p(x), _p(h), _p(weight), _p(scale), _p(q), _p(qscale),
                                                 scale_stride, _p(next_weight), rows, tier))
