@@ -27,7 +27,8 @@
 // 2^(s log2e - m log2e) against its running reference m; when a block raises
 // the row maximum by more than 8 (natural log), O and the row sum are rescaled
 // by exp(m_old - m_new) in TMEM and m moves, so P <= e^8 always fits fp16.  O
-// is only touched (after the previous P.V completed) on such a move.
+// is only touched (after the previous P.V completed) on such a move, and not
+// for a row whose first key this is (its O and sum are still zero).
 //
 // Key blocks start at multiples of 64 from the start of each sequence in the
 // tile, and a block's keys past its sequence's end are masked (they are counted
@@ -263,7 +264,9 @@ __global__ void __launch_bounds__(AttnTcCfg::THREADS, 1)
             const float mx = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
                                    fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
             const bool raise = mx > m + C::RESCALE;  // false while the row has no key (mx = -inf)
-            if (__any_sync(0xffffffffu, raise && j > 0)) {
+            // Rows seeing their first key (m = -inf) still have O = 0 and l = 0.
+            const bool rescale = raise && m != -INFINITY;
+            if (__any_sync(0xffffffffu, rescale)) {
                 // O holds the sum through block j - 1 once that P.V completed.
                 const int pj = j - 1, pst = pj % C::S_STAGES;
                 if (!__all_sync(0xffffffffu, wait_bar(&pvdone[pst], (pj / C::S_STAGES) & 1, abort))) {
@@ -271,7 +274,7 @@ __global__ void __launch_bounds__(AttnTcCfg::THREADS, 1)
                     break;
                 }
                 tc_fence_after();
-                const float f = (raise && m != -INFINITY) ? ex2_approx((m - mx) * L2E) : 1.0f;
+                const float f = rescale ? ex2_approx((m - mx) * L2E) : 1.0f;
                 for (int c = 0; c < C::D; c += 32) {
                     uint32_t o[32];
                     tmem_ld32(lane_base + C::O_COL + uint32_t(c), o);
