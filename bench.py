@@ -41,9 +41,30 @@ CONFIGS = {0: ("config0: 4 sequences, bodies 8/17/33/64 + BOS/EOS (130 tokens)",
            1: ("config1: 16 x 128-token sequences = one 2048-token wave", (126,) * 16),
            2: ("config2: 1 x 2048-token sequence", (2046,)),
            3: ("config3: mixed load, 256 requests x 16 texts, lognormal lengths (median 48), packed waves", None),
-           4: ("config4: Q8_0 GEMM microbench at the model's shapes, M = 2048 tokens", None)}
+           4: ("config4: Q8_0 GEMM microbench at the model's shapes, M = 2048 tokens", None),
+           5: ("config5: sliding-window attention microbench (d = 256, window 512) at the config 1 and 2 waves", None)}
 METRIC_MIXED = "embedded tokens/s per box (mixed-length requests, executor level)"
 METRIC_GEMM = "Q8_0 GEMM TOP/s (model shapes, M = 2048)"
+METRIC_ATTN = "local-layer attention TFLOP/s (d = 256, window 512; 16x128 and 1x2048 waves)"
+# (name, sequence lengths) of the attention microbench; algorithmic FLOPs are
+# 4 heads x 4 d per (query, key) pair the layer visits.
+ATTN_SHAPES = (("16x128", (128,) * 16), ("1x2048", (2048,)))
+
+
+def attn_pairs(lengths, window=512):
+    """(query, key) pairs of one sliding-window layer over packed sequences."""
+    tot = 0
+    for L in lengths:
+        t = np.arange(L)
+        tot += int((np.minimum(L, t + window + 1) - np.maximum(0, t - window)).sum())
+    return tot
+
+
+def attn_bounds(lengths):
+    off = np.concatenate([[0], np.cumsum(lengths)]).astype(np.int64)
+    lo = np.concatenate([[off[i]] * L for i, L in enumerate(lengths)]).astype(np.uint32)
+    hi = np.concatenate([[off[i + 1]] * L for i, L in enumerate(lengths)]).astype(np.uint32)
+    return lo, hi
 
 
 def q8_gemm_ops(n_tokens: int) -> float:
@@ -237,9 +258,38 @@ def reference_arm_gemm(args):
     print(json.dumps(line), flush=True)
 
 
+def reference_arm_attention(args):
+    """Config 5 on the CPU: the restatement of the reference's attention_rows
+    (scalar C, oracle/eg2_oracle.c, fp32) on the 16x128 wave, one thread."""
+    import oracle
+    oracle.build(ref=False)
+    port = oracle.Port()
+    rng = np.random.default_rng(5)
+    lengths = ATTN_SHAPES[0][1]
+    n = sum(lengths)
+    q = rng.standard_normal((n, 4, 256)).astype(np.float32)
+    k = (rng.standard_normal((n, 2, 256)) * 0.1).astype(np.float32)
+    v = rng.standard_normal((n, 2, 256)).astype(np.float32)
+    lo, hi = attn_bounds(lengths)
+    t0 = time.perf_counter()
+    port.attention(q, k, v, lo, hi, 2, 256, 512)
+    sec = time.perf_counter() - t0
+    val = 16.0 * 256 * attn_pairs(lengths) / sec / 1e12
+    cpu = {"value": val, "unit": "TFLOP/s", "cores": 1, "kind": "port",
+           "sample": "one 16x128-token local layer through the scalar C restatement of attention_rows"}
+    line = {"metric": METRIC_ATTN, "value": val, "unit": "TFLOP/s", "n_gpus": 1, "steps": 1, "warmup": 0,
+            "ms_per_step": sec * 1e3, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "f32", "data": "synthetic", "config": {"workload": CONFIGS[5][0], "shape": "16x128"},
+            "impl": "reference", "cpu_baseline": cpu,
+            "e2e": {"value": val, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
 def reference_arm(args, rank, world):
     if rank != 0:
         return
+    if args.config == 5:
+        return reference_arm_attention(args)
     if args.config == 3:
         return reference_arm_mixed(args)
     if args.config == 4:
@@ -451,6 +501,73 @@ def gemm_microbench(args, local):
     print(json.dumps(line), flush=True)
 
 
+def attention_microbench(args, local):
+    """Config 5: one sliding-window layer's attention (q/k/v fp16, d = 256,
+    window 512) on the config 1 and config 2 waves through the tcgen05 kernel
+    (eg2_launch_attention_tc) and, for comparison, the mma.sync kernel
+    (eg2_launch_attention_f16); each timed as a CUDA graph of `steps` launches
+    with inputs resident.  Per shape: one parity launch first (tcgen05 against
+    mma.sync, max |difference|), then `warmup` launches, then the graph.  Order
+    of tcgen05 launches: shape 1 parity, warm-ups, 2 x steps graph nodes, then
+    shape 2 likewise."""
+    import torch
+    ops = importlib.import_module("embeddinggemma2-amdkfd_b200.ops")
+    torch.cuda.set_device(local)
+    dev = f"cuda:{local}"
+    pk, src = peaks()
+    peak = pk["bf16_tflops"]
+    rng = np.random.default_rng(5)
+
+    def timed(launch):
+        for _ in range(args.warmup):
+            launch()
+        g = torch.cuda.CUDAGraph()
+        s = torch.cuda.Stream(device=dev)
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
+            with torch.cuda.graph(g, stream=s):
+                for _ in range(args.steps):
+                    launch()
+        torch.cuda.synchronize()
+        g.replay()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        g.replay()
+        e1.record()
+        torch.cuda.synchronize()
+        del g
+        return e0.elapsed_time(e1) * 1000.0 / args.steps
+
+    rows, tot_fl, tot_s = [], 0.0, 0.0
+    for name, lengths in ATTN_SHAPES:
+        n = sum(lengths)
+        q = torch.from_numpy(rng.standard_normal((n, 4, 256)).astype(np.float16)).to(dev)
+        k = torch.from_numpy((rng.standard_normal((n, 2, 256)) * 0.1).astype(np.float16)).to(dev)
+        v = torch.from_numpy(rng.standard_normal((n, 2, 256)).astype(np.float16)).to(dev)
+        lo, hi = attn_bounds(lengths)
+        b = torch.from_numpy(np.stack([lo, hi], 1).ravel().copy()).to(dev)
+        o_tc, o_mma = torch.zeros(n * 1024, device=dev), torch.zeros(n * 1024, device=dev)
+        tc = lambda: ops.attention_tc(o_tc, q, k, v, b, n, 512)
+        mma = lambda: ops.attention_f16(o_mma, q, k, v, b, n, 256, 512)
+        tc(), mma()
+        torch.cuda.synchronize()
+        diff = float((o_tc - o_mma).abs().max())
+        us_tc, us_mma = timed(tc), timed(mma)
+        fl = 16.0 * 256 * attn_pairs(lengths)
+        tot_fl, tot_s = tot_fl + fl, tot_s + us_tc * 1e-6
+        rows.append({"shape": name, "gflop": round(fl / 1e9, 3), "us_tcgen05": round(us_tc, 2),
+                     "tflop_s": round(fl / us_tc / 1e6, 1), "frac_of_peak": round(fl / us_tc / 1e6 / peak, 4),
+                     "us_mma_sync": round(us_mma, 2), "max_abs_diff_vs_mma_sync": diff})
+    line = {"metric": METRIC_ATTN, "value": tot_fl / tot_s / 1e12, "unit": "TFLOP/s", "n_gpus": 1,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": tot_s * 1e3, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f16 (fp32 accumulate and softmax)",
+            "data": "synthetic", "config": {"workload": CONFIGS[5][0]},
+            "peak": {"value": peak, "unit": "TFLOP/s", "source": f"bf16_tflops of {src} MEASURED_PEAKS"},
+            "shapes": rows, "gpu_launches": 2 * len(ATTN_SHAPES) * args.steps}
+    print(json.dumps(line), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -471,6 +588,10 @@ def main():
     if args.config == 4:
         if rank == 0:
             gemm_microbench(args, local)
+        return finalize(world)
+    if args.config == 5:
+        if rank == 0:
+            attention_microbench(args, local)
         return finalize(world)
 
     import torch
