@@ -508,8 +508,9 @@ def attention_microbench(args, local):
     (eg2_launch_attention_f16); each timed as a CUDA graph of `steps` launches
     with inputs resident.  Per shape: one parity launch first (tcgen05 against
     mma.sync, max |difference|), then `warmup` launches, then the graph.  Order
-    of tcgen05 launches: shape 1 parity, warm-ups, 2 x steps graph nodes, then
-    shape 2 likewise."""
+    of fp32-output tcgen05 launches: shape 1 parity, warm-ups, 2 x steps graph
+    nodes, then shape 2 likewise (the Q8-output timing of each shape follows
+    its mma.sync timing)."""
     import torch
     ops = importlib.import_module("embeddinggemma2-amdkfd_b200.ops")
     torch.cuda.set_device(local)
@@ -548,23 +549,29 @@ def attention_microbench(args, local):
         lo, hi = attn_bounds(lengths)
         b = torch.from_numpy(np.stack([lo, hi], 1).ravel().copy()).to(dev)
         o_tc, o_mma = torch.zeros(n * 1024, device=dev), torch.zeros(n * 1024, device=dev)
+        q8 = torch.zeros(n * 1024, dtype=torch.int8, device=dev)
+        q8s = torch.zeros(32 * n, device=dev)
         tc = lambda: ops.attention_tc(o_tc, q, k, v, b, n, 512)
+        tc_q8 = lambda: ops.attention_tc_q8(q8, q8s, n, q, k, v, b, n, 512)
         mma = lambda: ops.attention_f16(o_mma, q, k, v, b, n, 256, 512)
         tc(), mma()
         torch.cuda.synchronize()
         diff = float((o_tc - o_mma).abs().max())
         us_tc, us_mma = timed(tc), timed(mma)
+        us_q8 = timed(tc_q8)
         fl = 16.0 * 256 * attn_pairs(lengths)
         tot_fl, tot_s = tot_fl + fl, tot_s + us_tc * 1e-6
         rows.append({"shape": name, "gflop": round(fl / 1e9, 3), "us_tcgen05": round(us_tc, 2),
                      "tflop_s": round(fl / us_tc / 1e6, 1), "frac_of_peak": round(fl / us_tc / 1e6 / peak, 4),
-                     "us_mma_sync": round(us_mma, 2), "max_abs_diff_vs_mma_sync": diff})
+                     "us_mma_sync": round(us_mma, 2), "max_abs_diff_vs_mma_sync": diff,
+                     "us_tcgen05_q8_out": round(us_q8, 2)})
     line = {"metric": METRIC_ATTN, "value": tot_fl / tot_s / 1e12, "unit": "TFLOP/s", "n_gpus": 1,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": tot_s * 1e3, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "f16 (fp32 accumulate and softmax)",
             "data": "synthetic", "config": {"workload": CONFIGS[5][0]},
             "peak": {"value": peak, "unit": "TFLOP/s", "source": f"bf16_tflops of {src} MEASURED_PEAKS"},
-            "shapes": rows, "gpu_launches": 2 * len(ATTN_SHAPES) * args.steps}
+            "shapes": rows, "gpu_launches": 2 * len(ATTN_SHAPES) * args.steps,
+            "note": "value and tflop_s: fp32 output; us_tcgen05_q8_out: the executor's form, Q8_0 output of the O projection"}
     print(json.dumps(line), flush=True)
 
 

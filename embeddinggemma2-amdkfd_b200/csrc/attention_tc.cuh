@@ -124,8 +124,11 @@ __global__ void __launch_bounds__(AttnTcCfg::THREADS, 1)
         for (int c = 0; c < 4; ++c) tma_load_3d(qs + c * (C::Q_BYTES / 4), &tmQ, qfull, c * 64, head, t0);
         const int tlast = min(t0 + C::BQ, p.n);
         int nb = 0;
-        for (int seq_lo = int(p.bounds[2 * t0]); seq_lo < tlast;) {
-            const int seq_hi = int(p.bounds[2 * seq_lo + 1]);
+        // Row t0's lo and hi as two independent loads: the first sequence needs
+        // no dependent read (later ones read their end from their first row).
+        const int lo0 = int(p.bounds[2 * t0]), hi0 = int(p.bounds[2 * t0 + 1]);
+        for (int seq_lo = lo0; seq_lo < tlast;) {
+            const int seq_hi = seq_lo == lo0 ? hi0 : int(p.bounds[2 * seq_lo + 1]);
             if (seq_hi <= seq_lo) break;  // malformed bounds: never loop without progress
             int kmin = seq_lo, kmax = seq_hi;
             if (p.window) {
