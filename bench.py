@@ -42,7 +42,10 @@ CONFIGS = {0: ("config0: 4 sequences, bodies 8/17/33/64 + BOS/EOS (130 tokens)",
            2: ("config2: 1 x 2048-token sequence", (2046,)),
            3: ("config3: mixed load, 256 requests x 16 texts, lognormal lengths (median 48), packed waves", None),
            4: ("config4: Q8_0 GEMM microbench at the model's shapes, M = 2048 tokens", None),
-           5: ("config5: sliding-window attention microbench (d = 256, window 512) at the config 1 and 2 waves", None)}
+           5: ("config5: sliding-window attention microbench (d = 256, window 512) at the config 1 and 2 waves", None),
+           6: ("config6: config 1's wave (16 x 128 tokens) given as 512-wide input rows, seeded N(0, 1) "
+               "(media soft-token form: ids NULL)", (126,) * 16)}
+ROWS_CONFIGS = (6,)
 METRIC_MIXED = "embedded tokens/s per box (mixed-length requests, executor level)"
 METRIC_GEMM = "Q8_0 GEMM TOP/s (model shapes, M = 2048)"
 METRIC_ATTN = "local-layer attention TFLOP/s (d = 256, window 512; 16x128 and 1x2048 waves)"
@@ -148,18 +151,26 @@ class ClockSampler:
                 "reasons": reasons, "samples": len(rows)}
 
 
-def cpu_baseline_run(model_path, lengths, steps, warmup, seed):
-    """The reference's own CPU graph (oracle/_ref) on the same waves."""
+def wave_rows(n, seed):
+    """Soft-token waves: seeded N(0, 1) input rows [n][512]."""
+    return np.random.default_rng(seed).standard_normal((n, 512)).astype(np.float32)
+
+
+def cpu_baseline_run(model_path, lengths, steps, warmup, seed, rows=False):
+    """The reference's own CPU graph (oracle/_ref) on the same waves (with
+    rows: the same offsets, the graph started from input rows, ids NULL)."""
     import oracle
     syn = importlib.import_module("embeddinggemma2-amdkfd_b200.synthetic")
     ids, off = syn.wave(lengths, seed=seed)
     ref = oracle.RefGraph(model_path, 0)
+    x = wave_rows(int(off[-1]), seed) if rows else None
+    run = (lambda: ref.embed_inputs(x, off)) if rows else (lambda: ref.embed(ids, off))
     for _ in range(warmup):
-        ref.embed(ids, off)
+        run()
     times = []
     for _ in range(steps):
         t0 = time.perf_counter()
-        ref.embed(ids, off)
+        run()
         times.append(time.perf_counter() - t0)
     n = int(off[-1])
     med = statistics.median(times)
@@ -297,7 +308,7 @@ def reference_arm(args, rank, world):
     syn = importlib.import_module("embeddinggemma2-amdkfd_b200.synthetic")
     desc, lengths = CONFIGS[args.config]
     model = syn.model_path(1234, "baseline")
-    cpu = cpu_baseline_run(model, lengths, args.steps, args.warmup, seed=100)
+    cpu = cpu_baseline_run(model, lengths, args.steps, args.warmup, seed=100, rows=args.config in ROWS_CONFIGS)
     n = sum(l + 2 for l in lengths)
     line = {"metric": METRIC, "value": cpu["value"], "unit": "tokens/s", "n_gpus": args.gpus, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": 1000.0 * n / cpu["value"], "higher_is_better": True,
@@ -611,11 +622,15 @@ def main():
     ex = eg2.Gemma2Executor(model, local)
     ids, off = rank_wave(lengths, rank)
     n, batch = int(off[-1]), len(off) - 1
+    rows = wave_rows(n, 100 + rank) if args.config in ROWS_CONFIGS else None
+    stage = (lambda: ex.stage_rows(rows, off)) if rows is not None else (lambda: ex.stage(ids, off))
+    run_batch = (lambda: ex.batch_rows(rows, off)) if rows is not None else (lambda: ex.batch(ids, off))
+    h2d_bytes = H2D_BYTES_PER_WAVE + (-(-n // 64) * 64 * 512 * 4 if rows is not None else 0)
     stream = torch.cuda.ExternalStream(ex.stream, device=local)
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=local)
 
     # ---- value: device-resident waves
-    ex.stage(ids, off)
+    stage()
     for _ in range(args.warmup):
         ex.launch(1)
     ex.finish()
@@ -639,19 +654,19 @@ def main():
 
     # ---- e2e: the public C ABI with host buffers every step
     for _ in range(args.warmup):
-        ex.batch(ids, off)
+        run_batch()
     barrier(world)
     torch.cuda.synchronize()
     t0 = time.perf_counter()
     for _ in range(args.steps):
-        out = ex.batch(ids, off)
+        out = run_batch()
     e2e_ms = (time.perf_counter() - t0) * 1000.0
     barrier(world)
     e2e_ms_max = reduce_max(e2e_ms, world, f"cuda:{local}")
     assert np.isfinite(out).all() and np.allclose(out, out_dev, atol=1e-6)
 
     # ---- dominant kernel: per-group event timing of one eager wave
-    ex.stage(ids, off)
+    stage()
     prof = ex.profile()
     gemm_ms = sum(v for k, v in prof.items() if k.startswith("gemm_"))
     pk, src = peaks()
@@ -668,7 +683,7 @@ def main():
                    "parallelism": f"replicas x{world} (whole waves per GPU, no collective)",
                    "l2": "256 MiB write between timed steps; per-wave working set > L2 (151 MB weights, 100 MB PLE)"},
         "e2e": {"value": whole_job_rate(n, world, args.steps, e2e_ms_max), "unit": "tokens/s",
-                "h2d_bytes_per_step": H2D_BYTES_PER_WAVE,
+                "h2d_bytes_per_step": h2d_bytes,
                 "d2h_bytes_per_step": batch * 768 * 4},
         "gpu_launches": ex.kernels_per_wave * args.steps,
         "roofline": {"kernel": "q8gemm_kernel (all Q8_0 GEMM launches of a wave)", "bound": "tensor",
@@ -681,7 +696,8 @@ def main():
     c = clocks.summary()
     line["clocks"] = c
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        line["cpu_baseline"] = cpu_baseline_run(model_path, lengths, 3, 1, seed=100)
+        line["cpu_baseline"] = cpu_baseline_run(model_path, lengths, 3, 1, seed=100,
+                                                rows=args.config in ROWS_CONFIGS)
     if rank == 0:
         print(json.dumps(line), flush=True)
     del ex

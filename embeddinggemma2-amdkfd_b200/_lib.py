@@ -32,6 +32,10 @@ SIGNATURES = {
     "eg2_b200_finish": (b, [vp, vp, cstr, sz]),
     "eg2_b200_submit": (i32, [vp, vp, vp, sz, cstr, sz]),
     "eg2_b200_collect": (b, [vp, i32, vp, cstr, sz]),
+    "eg2_b200_validate_rows": (b, [vp, vp, sz, cstr, sz]),
+    "eg2_b200_batch_rows": (b, [vp, vp, vp, sz, vp, cstr, sz]),
+    "eg2_b200_stage_rows": (b, [vp, vp, vp, sz, cstr, sz]),
+    "eg2_b200_submit_rows": (i32, [vp, vp, vp, sz, cstr, sz]),
     "eg2_b200_stream": (vp, [vp]),
     "eg2_b200_kernels_per_wave": (i32, [vp]),
     "eg2_b200_profile": (i32, [vp, vp, vp, i32]),

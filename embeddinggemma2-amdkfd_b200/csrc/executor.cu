@@ -60,6 +60,16 @@ void validate_wave(const int32_t *ids, const size_t *offsets, size_t batch) {
         if (ids[i] < 0 || ids[i] >= VOCAB) throw std::runtime_error("token ID out of range");
 }
 
+// Media soft-token waves (ids NULL, 512-wide input rows: gemma2_fast.c:940-941)
+// take the same offsets checks and messages; the rows themselves are not
+// inspected, as in the reference.
+void validate_rows(const float *rows, const size_t *offsets, size_t batch) {
+    if (!rows || !offsets || !batch || batch > CAP || offsets[0] || offsets[batch] > CAP)
+        throw std::runtime_error("KFD batch requires 1..2048 packed tokens and nonempty sequences");
+    for (size_t s = 0; s < batch; ++s)
+        if (offsets[s + 1] <= offsets[s]) throw std::runtime_error("invalid KFD sequence offsets");
+}
+
 struct Q8Weight {
     int8_t *codes = nullptr;  // [rows][k]
     float *scales = nullptr;  // [k/32][rows]
@@ -108,6 +118,7 @@ struct Backend {
     // arena
     int *ids = nullptr;
     unsigned *bounds = nullptr, *pos = nullptr, *offsets = nullptr, *seq_count = nullptr;
+    float *xin = nullptr;  // soft-token waves: the uploaded input rows [CAP][512]
     float *x = nullptr, *ple = nullptr, *qkv = nullptr, *attn = nullptr, *h = nullptr, *y = nullptr, *pooled = nullptr,
           *xs = nullptr, *gs = nullptr;
     void *x_hi = nullptr, *x_lo = nullptr, *qh = nullptr, *kh = nullptr, *vh = nullptr;
@@ -129,6 +140,7 @@ struct Backend {
     static constexpr int SLOTS = 2;
     struct Slot {
         uint32_t *in = nullptr;  // ids | bounds(2) | pos | offsets | sequence count
+        float *rows = nullptr;   // soft-token waves: [CAP][512] input rows (allocated on first use)
         float *out = nullptr;
         int *err = nullptr;  // the device error word, read back with the wave
         cudaEvent_t done = nullptr;
@@ -141,6 +153,7 @@ struct Backend {
     // graphs per wave shape
     std::map<uint64_t, cudaGraphExec_t> graphs;
     unsigned staged_n = 0;
+    bool staged_rows = false;
     size_t staged_batch = 0;
     cudaGraphExec_t staged_graph = nullptr;
     int kernels_per_wave = 0;
@@ -367,6 +380,7 @@ struct Backend {
         for (void *p : allocations) cudaFree(p);
         for (Slot &sl : slots) {
             if (sl.in) cudaFreeHost(sl.in);
+            if (sl.rows) cudaFreeHost(sl.rows);
             if (sl.err) cudaFreeHost(sl.err);
             if (sl.out) cudaFreeHost(sl.out);
             if (sl.done) cudaEventDestroy(sl.done);
@@ -383,7 +397,8 @@ struct Backend {
 
     // The whole wave as a launch sequence (captured into a graph, or run eagerly
     // under the profiler).  Returns the number of kernels launched.
-    int enqueue(unsigned n, cudaStream_t s, Profiler *prof) {
+    // rows: a soft-token wave, whose x was uploaded with the inputs.
+    int enqueue(unsigned n, cudaStream_t s, Profiler *prof, bool rows = false) {
         int launches = 0;
         auto mark = [&](const char *name) {
             if (prof) prof->mark(name);
@@ -394,7 +409,10 @@ struct Backend {
         AttnTcMaps tc_maps{};
         if (!exact && !attention_tc_maps(&tc_maps, qh, kh, vh, N)) ck(cudaErrorInvalidValue, "attention maps");
         mark("start");
-        ck(launch_embed(x, x_hi, x_lo, token_embd, ids, N, s), "embed"), ++launches;
+        if (rows)
+            ck(launch_input_rows(x, x_hi, x_lo, xin, N, s), "input rows"), ++launches;
+        else
+            ck(launch_embed(x, x_hi, x_lo, token_embd, ids, N, s), "embed"), ++launches;
         mark("embed");
         if (exact)
             ck(launch_ple_exact(ple, x, ple_w, ple_norm, N, s), "PLE"), launches += 2;
@@ -469,8 +487,8 @@ struct Backend {
         return launches;
     }
 
-    cudaGraphExec_t graph_for(unsigned n) {
-        const uint64_t key = n;
+    cudaGraphExec_t graph_for(unsigned n, bool rows = false) {
+        const uint64_t key = n | uint64_t(rows) << 32;
         auto it = graphs.find(key);
         if (it != graphs.end()) return it->second;
         if (graphs.size() >= 256) {  // bound the cache
@@ -482,7 +500,7 @@ struct Backend {
         ck(cudaStreamBeginCapture(stream, cudaStreamCaptureModeThreadLocal), "begin capture");
         int launches = 0;
         try {
-            launches = enqueue(n, stream, nullptr);
+            launches = enqueue(n, stream, nullptr, rows);
         } catch (...) {
             cudaStreamEndCapture(stream, &graph);
             if (graph) cudaGraphDestroy(graph);
@@ -500,11 +518,16 @@ struct Backend {
 
     // gemma2_kfd.cpp:271-296: validation, bounds and positions into a slot's
     // staging buffer, padded to the bucket; returns the padded token count.
-    unsigned fill(Slot &sl, const int32_t *in_ids, const size_t *in_off, size_t batch) {
-        validate_wave(in_ids, in_off, batch);
+    // A soft-token wave (in_rows set, in_ids NULL) uploads its rows, padded
+    // with zero rows to the bucket, into xin (allocated on first use).
+    unsigned fill(Slot &sl, const int32_t *in_ids, const size_t *in_off, size_t batch,
+                  const float *in_rows = nullptr) {
+        if (in_rows) validate_rows(in_rows, in_off, batch);
+        else validate_wave(in_ids, in_off, batch);
         const unsigned n = unsigned(in_off[batch]);
         uint32_t *hid = sl.in, *hb = sl.in + CAP, *hp = sl.in + 3 * CAP, *ho = sl.in + 4 * CAP;  // device layout
-        std::memcpy(hid, in_ids, n * sizeof(int32_t));
+        if (in_ids && !in_rows) std::memcpy(hid, in_ids, n * sizeof(int32_t));
+        else std::memset(hid, 0, n * sizeof(int32_t));
         for (size_t s = 0; s < batch; ++s) {
             ho[s] = uint32_t(in_off[s]);
             for (size_t t = in_off[s]; t < in_off[s + 1]; ++t) {
@@ -518,19 +541,27 @@ struct Backend {
         for (unsigned t = n; t < n_pad; ++t) hid[t] = 0, hb[2 * t] = n, hb[2 * t + 1] = n_pad, hp[t] = t - n;
         sl.in[5 * CAP + 1] = uint32_t(batch);
         ck(cudaSetDevice(device), "cudaSetDevice");
+        if (in_rows) {
+            if (!sl.rows) ck(cudaMallocHost(&sl.rows, sizeof(float) * CAP * 512), "cudaMallocHost");
+            if (!xin) xin = dalloc<float>(size_t(CAP) * 512);
+            std::memcpy(sl.rows, in_rows, size_t(n) * 512 * sizeof(float));
+            std::memset(sl.rows + size_t(n) * 512, 0, size_t(n_pad - n) * 512 * sizeof(float));
+            ck(cudaMemcpyAsync(xin, sl.rows, size_t(n_pad) * 512 * sizeof(float), cudaMemcpyHostToDevice, stream),
+               "input rows upload");
+        }
         ck(cudaMemcpyAsync(ids, sl.in, (5 * CAP + 2) * 4, cudaMemcpyHostToDevice, stream), "wave upload");
         return n_pad;
     }
 
     // Split form for device-resident timing: stage once, launch the staged graph
     // any number of times, finish.  Not to be interleaved with submit/collect.
-    void stage(const int32_t *in_ids, const size_t *in_off, size_t batch) {
+    void stage(const int32_t *in_ids, const size_t *in_off, size_t batch, const float *in_rows = nullptr) {
         if (poisoned) throw std::runtime_error("KFD context failed; restart process before reuse");
         for (const Slot &sl : slots)
             if (sl.busy) throw std::runtime_error("a submitted wave is not collected yet");
-        const unsigned n_pad = fill(slots[0], in_ids, in_off, batch);
-        staged_graph = graph_for(n_pad);
-        staged_n = n_pad, staged_batch = batch;
+        const unsigned n_pad = fill(slots[0], in_ids, in_off, batch, in_rows);
+        staged_graph = graph_for(n_pad, in_rows != nullptr);
+        staged_n = n_pad, staged_batch = batch, staged_rows = in_rows != nullptr;
     }
 
     void launch(int repeats) {
@@ -590,13 +621,13 @@ struct Backend {
     // Pipelined form: submit enqueues upload, graph and readback on the next
     // slot and returns its index; collect waits for that slot and delivers.
     // A slot must be collected before it is submitted to again.
-    int submit(const int32_t *in_ids, const size_t *in_off, size_t batch) {
+    int submit(const int32_t *in_ids, const size_t *in_off, size_t batch, const float *in_rows = nullptr) {
         if (poisoned) throw std::runtime_error("KFD context failed; restart process before reuse");
         const int id = next_slot;
         Slot &sl = slots[id];
         if (sl.busy) throw std::runtime_error("pipeline slot busy: collect its wave first");
-        const unsigned n_pad = fill(sl, in_ids, in_off, batch);
-        ck(cudaGraphLaunch(graph_for(n_pad), stream), "graph launch");
+        const unsigned n_pad = fill(sl, in_ids, in_off, batch, in_rows);
+        ck(cudaGraphLaunch(graph_for(n_pad, in_rows != nullptr), stream), "graph launch");
         enqueue_readback(sl, batch);
         sl.batch = batch, sl.busy = true;
         next_slot = (next_slot + 1) % SLOTS;
@@ -611,9 +642,9 @@ struct Backend {
         deliver(sl, sl.batch, out);
     }
 
-    void batch(const int32_t *in_ids, const size_t *in_off, size_t n_seq, float *out) {
+    void batch(const int32_t *in_ids, const size_t *in_off, size_t n_seq, float *out, const float *in_rows = nullptr) {
         if (!out) throw std::runtime_error("KFD batch requires 1..2048 packed tokens and nonempty sequences");
-        collect(submit(in_ids, in_off, n_seq), out);
+        collect(submit(in_ids, in_off, n_seq, in_rows), out);
     }
 
     int profile(char names[][32], double *ms, int max) {
@@ -622,7 +653,7 @@ struct Backend {
         std::vector<std::string> order;
         {
             Profiler prof{stream};
-            enqueue(staged_n, stream, &prof);
+            enqueue(staged_n, stream, &prof, staged_rows);
             enqueue_readback(slots[0], 0);
             wait_slot(slots[0]);
             for (size_t i = 1; i < prof.events.size(); ++i) {
@@ -725,6 +756,39 @@ extern "C" bool eg2_b200_collect(void *ctx, int slot, float *out, char *err, siz
         ck(cudaSetDevice(b->device), "cudaSetDevice");
         b->collect(slot, out);
     });
+}
+extern "C" bool eg2_b200_validate_rows(const float *rows, const size_t *offsets, size_t batch, char *err,
+                                       size_t len) {
+    return guarded(err, len, [&] { validate_rows(rows, offsets, batch); });
+}
+extern "C" bool eg2_b200_batch_rows(void *ctx, const float *rows, const size_t *offsets, size_t batch, float *out,
+                                    char *err, size_t len) {
+    return guarded(err, len, [&] {
+        Backend *b = as_backend(ctx);
+        std::lock_guard<std::mutex> guard(b->mutex);
+        if (!rows) throw std::runtime_error("KFD batch requires 1..2048 packed tokens and nonempty sequences");
+        b->batch(nullptr, offsets, batch, out, rows);
+    });
+}
+extern "C" bool eg2_b200_stage_rows(void *ctx, const float *rows, const size_t *offsets, size_t batch, char *err,
+                                    size_t len) {
+    return guarded(err, len, [&] {
+        Backend *b = as_backend(ctx);
+        std::lock_guard<std::mutex> guard(b->mutex);
+        if (!rows) throw std::runtime_error("KFD batch requires 1..2048 packed tokens and nonempty sequences");
+        b->stage(nullptr, offsets, batch, rows);
+    });
+}
+extern "C" int eg2_b200_submit_rows(void *ctx, const float *rows, const size_t *offsets, size_t batch, char *err,
+                                    size_t len) {
+    int slot = -1;
+    guarded(err, len, [&] {
+        Backend *b = as_backend(ctx);
+        std::lock_guard<std::mutex> guard(b->mutex);
+        if (!rows) throw std::runtime_error("KFD batch requires 1..2048 packed tokens and nonempty sequences");
+        slot = b->submit(nullptr, offsets, batch, rows);
+    });
+    return slot;
 }
 extern "C" void *eg2_b200_stream(void *ctx) { return ctx ? static_cast<Backend *>(ctx)->stream : nullptr; }
 extern "C" int eg2_b200_kernels_per_wave(void *ctx) { return ctx ? static_cast<Backend *>(ctx)->kernels_per_wave : 0; }

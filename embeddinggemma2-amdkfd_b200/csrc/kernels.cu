@@ -129,6 +129,11 @@ cudaError_t launch_ple(const CUtensorMap &hi, const CUtensorMap &lo, const CUten
     return launch_pdl(ple_kernel, dim3(24, (M + 127) / 128), dim3(PleCfg::THREADS), PleCfg::SMEM, s, hi, lo, w, p);
 }
 
+cudaError_t launch_input_rows(float *x, void *x_hi, void *x_lo, const float *rows, int n, cudaStream_t s) {
+    if (n <= 0) return cudaSuccess;
+    return launch_pdl(input_rows_kernel, dim3((unsigned(n) * 512 + 255) / 256), dim3(256), 0, s, x,
+                      static_cast<__nv_bfloat16 *>(x_hi), static_cast<__nv_bfloat16 *>(x_lo), rows, n);
+}
 cudaError_t launch_embed(float *x, void *x_hi, void *x_lo, const void *emb, const int *ids, int n, cudaStream_t s) {
     if (n <= 0) return cudaSuccess;
     if ((x_hi == nullptr) != (x_lo == nullptr)) return cudaErrorInvalidValue;

@@ -34,6 +34,8 @@ cudaError_t launch_q8gemm_geglu(const CUtensorMap &w, const CUtensorMap &x, cons
 cudaError_t launch_ple(const CUtensorMap &hi, const CUtensorMap &lo, const CUtensorMap &w, float *ple,
                        const float *norm, int M, cudaStream_t s);
 cudaError_t launch_embed(float *x, void *x_hi, void *x_lo, const void *emb, const int *ids, int n, cudaStream_t s);
+// Soft-token waves: x = rows[n][512] as given, plus the bf16 hi/lo split of x.
+cudaError_t launch_input_rows(float *x, void *x_hi, void *x_lo, const float *rows, int n, cudaStream_t s);
 cudaError_t launch_norm_quant(int8_t *q, float *qs, int qs_stride, float *y, const float *x, const float *w, int rows,
                               int width, cudaStream_t s, int tier = 0);
 // q/k/v outputs are fp16, or fp32 when f32_out (parity mode).

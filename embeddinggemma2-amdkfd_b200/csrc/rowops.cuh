@@ -35,6 +35,23 @@ __global__ void embed_kernel(float *__restrict__ x, __nv_bfloat16 *__restrict__ 
     }
 }
 
+// Media soft-token waves (gemma2_fast.c:940-941): x = the caller's 512-wide rows
+// as given (uploaded by the host into `rows`, which the wave never writes, so a
+// staged wave replays identically), plus the bf16 hi/lo split of x for the PLE
+// tensor-core GEMM with embed_kernel's arithmetic.
+__global__ void input_rows_kernel(float *__restrict__ x, __nv_bfloat16 *__restrict__ x_hi,
+                                  __nv_bfloat16 *__restrict__ x_lo, const float *__restrict__ rows, int n) {
+    pdl_wait();
+    pdl_trigger();
+    const size_t i = size_t(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (i >= size_t(n) * 512) return;
+    const float v = rows[i];
+    x[i] = v;
+    const __nv_bfloat16 hi = __float2bfloat16_rn(v);
+    x_hi[i] = hi;
+    x_lo[i] = __float2bfloat16_rn(__fsub_rn(v, __bfloat162float(hi)));
+}
+
 // Layout of the quantizing kernels: a warp reads a row 512 bytes at a time,
 // each lane 4 consecutive floats (one float4), so one warp-wide access covers
 // four Q8_0 blocks and each block lives in an aligned group of 8 lanes.  The

@@ -35,6 +35,17 @@ def _wave(ids, offsets):
     return ids, offsets, len(offsets) - 1
 
 
+def _rows(rows, offsets):
+    rows = np.ascontiguousarray(rows, dtype=np.float32)
+    offsets = np.ascontiguousarray(offsets, dtype=np.uint64)
+    if rows.size % 512:
+        raise ExecutorError("input rows must be 512 wide")
+    rows = rows.reshape(-1, 512)
+    if len(offsets) and rows.shape[0] != int(offsets[-1]):
+        raise ExecutorError("input rows do not match offsets")
+    return rows, offsets, len(offsets) - 1
+
+
 def validate(ids, offsets) -> None:
     """The reference's host-side wave checks (gemma2_kfd.cpp:270-278), no GPU needed."""
     ids, offsets, batch = _wave(ids, offsets)
@@ -132,6 +143,37 @@ class Gemma2Executor:
         if not self.lib.eg2_b200_collect(self.ctx, slot, out.ctypes.data, err, len(err)):
             raise ExecutorError(err.value.decode())
         return out[:batch]
+
+    # media soft-token waves: 512-wide input rows instead of token ids
+    def batch_rows(self, rows, offsets) -> np.ndarray:
+        """Embed one packed wave given as rows float32[n][512] (the reference CPU
+        graph's ids == NULL form, gemma2_fast.c:940-941)."""
+        rows, offsets, batch = _rows(rows, offsets)
+        out = np.zeros((max(batch, 1), EMBED_DIM), np.float32)
+        err = _err()
+        if not self.lib.eg2_b200_batch_rows(self.ctx, rows.ctypes.data if rows.size else None,
+                                            offsets.ctypes.data if offsets.size else None, max(batch, 0),
+                                            out.ctypes.data, err, len(err)):
+            raise ExecutorError(err.value.decode())
+        return out[:batch]
+
+    def submit_rows(self, rows, offsets) -> int:
+        rows, offsets, batch = _rows(rows, offsets)
+        err = _err()
+        slot = self.lib.eg2_b200_submit_rows(self.ctx, rows.ctypes.data if rows.size else None,
+                                             offsets.ctypes.data if offsets.size else None, max(batch, 0), err,
+                                             len(err))
+        if slot < 0:
+            raise ExecutorError(err.value.decode())
+        self._slot_batch[slot] = batch
+        return slot
+
+    def stage_rows(self, rows, offsets):
+        rows, offsets, batch = _rows(rows, offsets)
+        err = _err()
+        if not self.lib.eg2_b200_stage_rows(self.ctx, rows.ctypes.data, offsets.ctypes.data, batch, err, len(err)):
+            raise ExecutorError(err.value.decode())
+        self._staged_batch = batch
 
     # split form, for device-resident timing
     def stage(self, ids, offsets):

@@ -76,6 +76,22 @@ bool eg2_b200_finish(void *ctx, float *out, char *err, size_t len);
  * the GPU runs the other.  Same validation and errors as ei_gemma2_kfd_batch. */
 int eg2_b200_submit(void *ctx, const int32_t *ids, const size_t *offsets, size_t batch, char *err, size_t len);
 bool eg2_b200_collect(void *ctx, int slot, float *out, char *err, size_t len);
+/* ---- media soft-token waves ----------------------------------------------
+ * The same wave from caller-given 512-wide input rows instead of token ids:
+ * rows [offsets[batch]][512] fp32 become the residual stream x as given, the
+ * role of ids == NULL in the reference's CPU graph
+ * (ei_gemma2_embed_batch_fast_ctx, gemma2_fast.c:940-941; gemma2.h:10-16).
+ * Offsets are checked as for ids (same messages); the rows are not inspected.
+ * batch_rows is the monolithic call, stage_rows the split form's first step
+ * (then eg2_b200_launch / eg2_b200_finish), submit_rows the pipelined form's
+ * (then eg2_b200_collect).  The KFD executor has no counterpart. */
+bool eg2_b200_validate_rows(const float *rows, const size_t *offsets, size_t batch, char *err, size_t len);
+bool eg2_b200_batch_rows(void *ctx, const float *rows, const size_t *offsets, size_t batch, float *out,
+                         char *err, size_t len);
+bool eg2_b200_stage_rows(void *ctx, const float *rows, const size_t *offsets, size_t batch, char *err,
+                         size_t len);
+int eg2_b200_submit_rows(void *ctx, const float *rows, const size_t *offsets, size_t batch, char *err,
+                         size_t len);
 /* The cudaStream_t the context launches on (for CUDA-event timing). */
 void *eg2_b200_stream(void *ctx);
 /* Kernels launched per wave by the staged graph. */

@@ -296,8 +296,23 @@ static void l2_normalize_sse2(float *x, int n) {
 #define T(i) (tensors[(i)])
 #define LT(l, j) (tensors[3 + 17 * (l) + (j)])
 
+static int embed_batch(const void *const *tensors, const int32_t *ids, const float *inputs,
+                       const size_t *offsets, size_t batch, float *out, int qm, int gm, float *x_layers);
+
 int eg2o_embed_batch(const void *const *tensors, const int32_t *ids, const size_t *offsets,
                      size_t batch, float *out, int qm, int gm, float *x_layers) {
+    return embed_batch(tensors, ids, NULL, offsets, batch, out, qm, gm, x_layers);
+}
+
+/* gemma2_fast.c:940-941: with ids NULL the wave starts from caller-given
+ * 512-wide rows (media soft tokens), copied into x unscaled. */
+int eg2o_embed_batch_inputs(const void *const *tensors, const float *inputs, const size_t *offsets,
+                            size_t batch, float *out, int qm, int gm) {
+    return inputs ? embed_batch(tensors, NULL, inputs, offsets, batch, out, qm, gm, NULL) : 1;
+}
+
+static int embed_batch(const void *const *tensors, const int32_t *ids, const float *inputs,
+                       const size_t *offsets, size_t batch, float *out, int qm, int gm, float *x_layers) {
     size_t count = offsets[batch];
     if (!count || count > 8192) return 1;
     int n = (int)count;
@@ -312,8 +327,9 @@ int eg2o_embed_batch(const void *const *tensors, const int32_t *ids, const size_
     for (size_t s = 0; s < batch; s++)
         for (size_t t = offsets[s]; t < offsets[s + 1]; t++)
             lo[t] = (uint32_t)offsets[s], hi[t] = (uint32_t)offsets[s + 1], pos[t] = (uint32_t)(t - offsets[s]);
-    /* gemma2_fast.c:942-950: x = (d * q) * sqrtf(512). */
-    for (int t = 0; t < n; t++) {
+    /* gemma2_fast.c:940-950: x = the given rows, or (d * q) * sqrtf(512). */
+    if (inputs) memcpy(x, inputs, count * 512 * 4);
+    for (int t = 0; t < n && !inputs; t++) {
         const uint8_t *row = (const uint8_t *)T(0) + (size_t)ids[t] * 16 * 34;
         for (int b = 0; b < 16; b++) {
             uint16_t hb;

@@ -58,4 +58,8 @@ void eg2o_attention(const float *q, const float *k, const float *v, const uint32
  * last one, [25][n][512].  Returns 0 on success. */
 int eg2o_embed_batch(const void *const *tensors, const int32_t *ids, const size_t *offsets,
                      size_t batch, float *out, int quant_mode, int gelu_mode, float *x_layers);
+/* The same graph from caller-given 512-wide input rows (media soft tokens,
+ * gemma2_fast.c:940-941) instead of token ids.  Returns 0 on success. */
+int eg2o_embed_batch_inputs(const void *const *tensors, const float *inputs, const size_t *offsets,
+                            size_t batch, float *out, int quant_mode, int gelu_mode);
 #endif

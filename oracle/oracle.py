@@ -140,6 +140,8 @@ class RefGraph:
                                         C.c_char_p, C.c_size_t]
         L.eg2ref_embed_reference.argtypes = [C.c_void_p, C.c_void_p, C.c_size_t, C.c_void_p,
                                              C.c_char_p, C.c_size_t]
+        L.eg2ref_embed_fast_inputs.argtypes = [C.c_void_p, C.c_void_p, C.c_void_p, C.c_size_t, C.c_void_p,
+                                               C.c_char_p, C.c_size_t]
         L.eg2ref_normalize_prefix.argtypes = [C.c_void_p, C.c_int]
         L.eg2ref_quantize_row_q8_0.argtypes = [C.c_void_p, C.c_void_p, C.c_int]
         L.eg2ref_fp32_to_fp16.argtypes = [C.c_float]
@@ -161,6 +163,18 @@ class RefGraph:
         out = np.zeros((batch, 768), np.float32)
         err = C.create_string_buffer(256)
         if not self.lib.eg2ref_embed_fast(self.handle, _ptr(ids), _ptr(offsets), batch, _ptr(out), err, 256):
+            raise RuntimeError(err.value.decode())
+        return out
+
+    def embed_inputs(self, inputs: np.ndarray, offsets: np.ndarray) -> np.ndarray:
+        """The reference's CPU graph from 512-wide input rows (ids NULL)."""
+        inputs = np.ascontiguousarray(inputs, dtype=np.float32).reshape(-1, 512)
+        offsets = np.ascontiguousarray(offsets, dtype=np.uint64)
+        batch = len(offsets) - 1
+        out = np.zeros((batch, 768), np.float32)
+        err = C.create_string_buffer(256)
+        if not self.lib.eg2ref_embed_fast_inputs(self.handle, _ptr(inputs), _ptr(offsets), batch, _ptr(out),
+                                                 err, 256):
             raise RuntimeError(err.value.decode())
         return out
 
@@ -222,6 +236,7 @@ class Port:
         L.eg2o_rope_tables.argtypes = [i, vp, vp]
         L.eg2o_attention.argtypes = [vp, vp, vp, vp, vp, i, i, i, i, vp]
         L.eg2o_embed_batch.argtypes = [vp, vp, vp, C.c_size_t, vp, i, i, vp]
+        L.eg2o_embed_batch_inputs.argtypes = [vp, vp, vp, C.c_size_t, vp, i, i]
 
     def quantize(self, x, mode=ROUND_X86):
         x = np.ascontiguousarray(x, dtype=np.float32).ravel()
@@ -296,3 +311,16 @@ class Port:
         if rc:
             raise RuntimeError("oracle rejected the wave")
         return (out, xl) if dump_layers else out
+
+    def embed_inputs(self, model: Gguf, inputs, offsets, quant_mode=ROUND_SCALAR, gelu_mode=0):
+        """The graph from 512-wide input rows (media soft tokens) instead of ids."""
+        inputs = np.ascontiguousarray(inputs, dtype=np.float32).reshape(-1, 512)
+        offsets = np.ascontiguousarray(offsets, dtype=np.uint64)
+        batch = len(offsets) - 1
+        assert inputs.shape[0] == int(offsets[-1])
+        out = np.zeros((batch, 768), np.float32)
+        rc = self.lib.eg2o_embed_batch_inputs(model.pointer_table(), _ptr(inputs), _ptr(offsets), batch,
+                                              _ptr(out), quant_mode, gelu_mode)
+        if rc:
+            raise RuntimeError("oracle rejected the wave")
+        return out

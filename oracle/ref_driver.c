@@ -52,6 +52,14 @@ int eg2ref_embed_fast(void *h, const int32_t *ids, const size_t *offsets, size_t
                                           err, err_len) ? 1 : 0;
 }
 
+/* The same graph from 512-wide input rows (media soft tokens; ids NULL). */
+int eg2ref_embed_fast_inputs(void *h, const float *inputs, const size_t *offsets, size_t batch, float *out,
+                             char *err, size_t err_len) {
+    eg2ref *r = h;
+    return ei_gemma2_embed_batch_fast_ctx(r->fast, &r->g, r->pool, NULL, inputs, offsets, batch, out,
+                                          err, err_len) ? 1 : 0;
+}
+
 /* The reference's straight single-sequence graph (secondary oracle). */
 int eg2ref_embed_reference(void *h, const int32_t *ids, size_t n, float *out, char *err,
                            size_t err_len) {

@@ -19,7 +19,11 @@ embeddinggemma2-amdkfd_b200/synthetic.py:
   tier, and the Matryoshka prefixes {128, 256, 512} of config 2 as the server
   applies them (kernels.c:403-407);
 * golden_ops.npz -- the reference's x86 Q8_0 quantizer and exp-polynomial GELU
-  on seeded random rows (gemma2_fast_x86.c:211-234, 308-325).
+  on seeded random rows (gemma2_fast_x86.c:211-234, 308-325);
+* golden_inputs_baseline.npz -- a 3-sequence wave (5/12/23 rows) given as
+  512-wide input rows (media soft tokens, ids NULL: gemma2_fast.c:940-941),
+  seeded N(0, 1), at the scalar and the best tier
+  (`python tests/golden/make_golden.py inputs` writes only this one).
 
 Each scalar-tier run happens in a child process because the reference caches
 its tier on first use.
@@ -64,6 +68,12 @@ def _child(norm: str, what: str, out_path: str):
         ids, off = syn.wave((126, 126), seed=22)
         res["w2x128_ids"], res["w2x128_offsets"] = ids, off
         res["w2x128_embed"] = ref.embed(ids, off)
+    elif what == "inputs":
+        rng = np.random.Generator(np.random.PCG64(31))
+        off = np.array([0, 5, 17, 40], np.uint64)
+        x = rng.standard_normal((40, 512)).astype(np.float32)
+        res["inputs"], res["offsets"] = x, off
+        res["embed"] = ref.embed_inputs(x, off)
     elif what == "ops":
         rng = np.random.Generator(np.random.PCG64(5))
         x = (rng.standard_normal(64 * 512) * rng.uniform(0.01, 10.0, 64 * 512)).astype(np.float32)
@@ -87,6 +97,13 @@ def run(norm, what, scalar):
     return d
 
 
+def make_inputs():
+    s = run("baseline", "inputs", True)
+    b = run("baseline", "inputs", False)
+    np.savez_compressed(os.path.join(OUT, "golden_inputs_baseline.npz"), inputs=s["inputs"], offsets=s["offsets"],
+                        embed_scalar=s["embed"], embed_best=b["embed"], best_tier=b["tier"])
+
+
 def main():
     syn = importlib.import_module("embeddinggemma2-amdkfd_b200.synthetic")
     meta = {}
@@ -103,6 +120,7 @@ def main():
     np.savez_compressed(os.path.join(OUT, "golden_long_baseline.npz"), **lg)
     ops = run("baseline", "ops", False)
     np.savez_compressed(os.path.join(OUT, "golden_ops.npz"), **ops)
+    make_inputs()
     with open(os.path.join(OUT, "golden_meta.json"), "w") as f:
         json.dump(meta, f, indent=1, sort_keys=True)
     print(json.dumps(meta, indent=1))
@@ -111,5 +129,7 @@ def main():
 if __name__ == "__main__":
     if len(sys.argv) > 1 and sys.argv[1] == "--child":
         _child(sys.argv[2], sys.argv[3], sys.argv[4])
+    elif len(sys.argv) > 1 and sys.argv[1] == "inputs":
+        make_inputs()
     else:
         main()

@@ -45,6 +45,15 @@ def test_port_is_bit_identical_to_reference_scalar_tier(port, syn, norm):
     assert np.array_equal(out, g["embed_scalar"])
 
 
+def test_port_input_rows_bit_identical_to_reference_scalar_tier(port, syn):
+    """Media soft-token wave (512-wide input rows, ids NULL: gemma2_fast.c:940-941):
+    the restatement equals the reference's scalar tier bit for bit."""
+    import oracle
+    g = golden("golden_inputs_baseline.npz")
+    out = port.embed_inputs(oracle.Gguf(syn.model_path(1234, "baseline")), g["inputs"], g["offsets"])
+    assert np.array_equal(out, g["embed_scalar"])
+
+
 def test_port_x86_quantizer_matches_reference():
     """quantize_row_q8_0 of the x86 tiers (gemma2_fast_x86.c:211-234): codes and
     fp16 scale bits identical on 1024 seeded blocks."""

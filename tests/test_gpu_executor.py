@@ -195,3 +195,68 @@ def test_parity_mode_scalar_tier_equals_reference(eg2, syn, norm, port):
     finally:
         ex.close()
         m.close()
+
+
+def _embedding_rows(model_path, ids):
+    """x = (d * q) * sqrt(512) for each id, in float32 exactly as the embed
+    kernel and the reference compute it (gemma2_fast.c:942-950)."""
+    import oracle
+    raw = np.asarray(oracle.Gguf(model_path).raw("token_embd.weight"))
+    blk = raw.reshape(262144, 16, 34)[np.asarray(ids)]
+    d = np.ascontiguousarray(blk[:, :, :2]).view(np.float16)[..., 0].astype(np.float32)
+    q = np.ascontiguousarray(blk[:, :, 2:]).view(np.int8).astype(np.float32)
+    return ((d[:, :, None] * q) * np.float32(np.sqrt(np.float32(512)))).astype(np.float32).reshape(len(ids), 512)
+
+
+def test_input_rows_of_token_embeddings_equal_ids_path(executor, model_baseline, syn):
+    """Media soft-token form (512-wide input rows instead of ids,
+    gemma2_fast.c:940-941): given exactly the rows the embedding lookup produces,
+    the wave is bit-identical to the ids wave, through the monolithic, staged
+    and pipelined calls."""
+    g = golden("golden_baseline.npz")
+    for ids, off in ((g["ids"], g["offsets"]), syn.wave((5, 300, 40, 1), seed=92)):
+        rows = _embedding_rows(model_baseline, ids)
+        ref = executor.batch(ids, off)
+        np.testing.assert_array_equal(executor.batch_rows(rows, off), ref)
+        np.testing.assert_array_equal(executor.collect(executor.submit_rows(rows, off)), ref)
+        executor.stage_rows(rows, off)
+        executor.launch(3)  # replays start from the uploaded rows every time
+        np.testing.assert_array_equal(executor.finish(), ref)
+
+
+def test_input_rows_match_reference(eg2, executor, model_baseline, port):
+    """Random N(0, 1) input rows (golden_inputs_baseline.npz from the reference's
+    own CPU graph with ids NULL): within the reference's inter-tier agreement in
+    the fast path, and bit-identical to its scalar tier in parity mode with the
+    scalar tier's choices."""
+    import oracle
+    g = golden("golden_inputs_baseline.npz")
+    out = executor.batch_rows(g["inputs"], g["offsets"])
+    floor = _floor(g)
+    c = cosine(out, g["embed_scalar"])
+    print("input rows cos vs scalar tier", c, "reference inter-tier", floor)
+    assert c.min() >= floor - MARGIN
+    m = eg2.GGUFModel(model_baseline)
+    px = eg2.Gemma2Executor(m, 0, exact=True, tier="scalar")
+    try:
+        np.testing.assert_array_equal(px.batch_rows(g["inputs"], g["offsets"]), g["embed_scalar"])
+        rng = np.random.default_rng(93)
+        off = np.array([0, 70, 71, 333], np.uint64)
+        rows = rng.standard_normal((333, 512)).astype(np.float32) * 0.7
+        np.testing.assert_array_equal(px.batch_rows(rows, off),
+                                      port.embed_inputs(oracle.Gguf(model_baseline), rows, off,
+                                                        quant_mode=port.ROUND_SCALAR, gelu_mode=0))
+    finally:
+        px.close()
+        m.close()
+
+
+def test_input_rows_errors(eg2, executor):
+    """Offsets are checked as for ids, with the same messages."""
+    rows = np.zeros((4, 512), np.float32)
+    with pytest.raises(eg2.ExecutorError, match="invalid KFD sequence offsets"):
+        executor.batch_rows(rows, np.array([0, 2, 2, 4], np.uint64))
+    with pytest.raises(eg2.ExecutorError, match="1..2048 packed tokens"):
+        executor.batch_rows(np.zeros((2049, 512), np.float32), np.array([0, 2049], np.uint64))
+    with pytest.raises(eg2.ExecutorError, match="512 wide"):
+        executor.batch_rows(np.zeros((4, 100), np.float32), np.array([0, 4], np.uint64))
