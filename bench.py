@@ -44,8 +44,11 @@ CONFIGS = {0: ("config0: 4 sequences, bodies 8/17/33/64 + BOS/EOS (130 tokens)",
            4: ("config4: Q8_0 GEMM microbench at the model's shapes, M = 2048 tokens", None),
            5: ("config5: sliding-window attention microbench (d = 256, window 512) at the config 1 and 2 waves", None),
            6: ("config6: config 1's wave (16 x 128 tokens) given as 512-wide input rows, seeded N(0, 1) "
-               "(media soft-token form: ids NULL)", (126,) * 16)}
+               "(media soft-token form: ids NULL)", (126,) * 16),
+           7: ("config7: one 8192-token wave of 4 x 2048-token sequences (the reference CPU graph's wave limit)",
+               (2046,) * 4)}
 ROWS_CONFIGS = (6,)
+WIDE_CONFIGS = (7,)  # run in an 8192-token context (EG2_B200_WAVE_8192)
 METRIC_MIXED = "embedded tokens/s per box (mixed-length requests, executor level)"
 METRIC_GEMM = "Q8_0 GEMM TOP/s (model shapes, M = 2048)"
 METRIC_ATTN = "local-layer attention TFLOP/s (d = 256, window 512; 16x128 and 1x2048 waves)"
@@ -619,13 +622,14 @@ def main():
     model_path = syn.model_path(1234, "baseline")
     torch.cuda.set_device(local)
     model = eg2.GGUFModel(model_path)
-    ex = eg2.Gemma2Executor(model, local)
+    ex = eg2.Gemma2Executor(model, local, max_tokens=8192 if args.config in WIDE_CONFIGS else 2048)
     ids, off = rank_wave(lengths, rank)
     n, batch = int(off[-1]), len(off) - 1
     rows = wave_rows(n, 100 + rank) if args.config in ROWS_CONFIGS else None
     stage = (lambda: ex.stage_rows(rows, off)) if rows is not None else (lambda: ex.stage(ids, off))
     run_batch = (lambda: ex.batch_rows(rows, off)) if rows is not None else (lambda: ex.batch(ids, off))
-    h2d_bytes = H2D_BYTES_PER_WAVE + (-(-n // 64) * 64 * 512 * 4 if rows is not None else 0)
+    cap = 8192 if args.config in WIDE_CONFIGS else 2048
+    h2d_bytes = (5 * cap + 2) * 4 + (-(-n // 64) * 64 * 512 * 4 if rows is not None else 0)
     stream = torch.cuda.ExternalStream(ex.stream, device=local)
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=local)
 

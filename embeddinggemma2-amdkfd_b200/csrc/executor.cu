@@ -37,10 +37,12 @@ namespace {
 using namespace eg2;
 
 constexpr unsigned CAP = 2048;  // packed tokens per wave: the reference's KFD cap (gemma2_kfd.cpp:20)
+// EG2_B200_WAVE_8192: the reference CPU graph's wave limit (gemma2_fast.c:924-925).
+constexpr unsigned WIDE_CAP = 8192;
 // Waves run padded to a multiple of BUCKET tokens: the padding is one extra
 // sequence that the pooling skips, and every kernel is per token or per
 // sequence, so the real tokens' results do not change.  One CUDA graph per
-// bucket then serves every wave shape (at most CAP / BUCKET graphs).
+// bucket then serves every wave shape (at most cap / BUCKET graphs).
 constexpr unsigned BUCKET = 64;
 constexpr int VOCAB = 262144;
 constexpr double TIMEOUT_S = 30.0;  // gemma2_kfd.cpp:21
@@ -49,10 +51,17 @@ void ck(cudaError_t e, const char *what) {
     if (e != cudaSuccess) throw std::runtime_error(std::string(what) + ": " + cudaGetErrorString(e));
 }
 
+// The token-count message: the KFD executor's (gemma2_kfd.cpp:271) at its cap,
+// the CPU graph's (gemma2_fast.c:925) for 8192-token waves.
+const char *count_message(unsigned cap) {
+    return cap > CAP ? "EmbeddingGemma 2 accepts 1..8192 input tokens"
+                     : "KFD batch requires 1..2048 packed tokens and nonempty sequences";
+}
+
 // gemma2_kfd.cpp:270-278: the same checks, in the same order, with its messages.
-void validate_wave(const int32_t *ids, const size_t *offsets, size_t batch) {
-    if (!ids || !offsets || !batch || batch > CAP || offsets[0] || offsets[batch] > CAP)
-        throw std::runtime_error("KFD batch requires 1..2048 packed tokens and nonempty sequences");
+void validate_wave(const int32_t *ids, const size_t *offsets, size_t batch, unsigned cap = CAP) {
+    if (!ids || !offsets || !batch || batch > cap || offsets[0] || offsets[batch] > cap)
+        throw std::runtime_error(count_message(cap));
     for (size_t s = 0; s < batch; ++s)
         if (offsets[s + 1] <= offsets[s]) throw std::runtime_error("invalid KFD sequence offsets");
     const size_t n = offsets[batch];
@@ -63,9 +72,9 @@ void validate_wave(const int32_t *ids, const size_t *offsets, size_t batch) {
 // Media soft-token waves (ids NULL, 512-wide input rows: gemma2_fast.c:940-941)
 // take the same offsets checks and messages; the rows themselves are not
 // inspected, as in the reference.
-void validate_rows(const float *rows, const size_t *offsets, size_t batch) {
-    if (!rows || !offsets || !batch || batch > CAP || offsets[0] || offsets[batch] > CAP)
-        throw std::runtime_error("KFD batch requires 1..2048 packed tokens and nonempty sequences");
+void validate_rows(const float *rows, const size_t *offsets, size_t batch, unsigned cap = CAP) {
+    if (!rows || !offsets || !batch || batch > cap || offsets[0] || offsets[batch] > cap)
+        throw std::runtime_error(count_message(cap));
     for (size_t s = 0; s < batch; ++s)
         if (offsets[s + 1] <= offsets[s]) throw std::runtime_error("invalid KFD sequence offsets");
 }
@@ -118,7 +127,7 @@ struct Backend {
     // arena
     int *ids = nullptr;
     unsigned *bounds = nullptr, *pos = nullptr, *offsets = nullptr, *seq_count = nullptr;
-    float *xin = nullptr;  // soft-token waves: the uploaded input rows [CAP][512]
+    float *xin = nullptr;  // soft-token waves: the uploaded input rows [cap][512]
     float *x = nullptr, *ple = nullptr, *qkv = nullptr, *attn = nullptr, *h = nullptr, *y = nullptr, *pooled = nullptr,
           *xs = nullptr, *gs = nullptr;
     void *x_hi = nullptr, *x_lo = nullptr, *qh = nullptr, *kh = nullptr, *vh = nullptr;
@@ -128,6 +137,8 @@ struct Backend {
     // order, PLE projection and attention on the CUDA-core exact-order kernels
     // with fp32 q/k/v; every other kernel is bit-exact in both modes.
     bool exact = false;
+    // Packed tokens per wave: CAP, or WIDE_CAP with EG2_B200_WAVE_8192.
+    unsigned cap = CAP;
     // EG2_B200_SCALAR_TIER: the scalar CPU tier's quantizer rounding and GELU
     // (roundf, tanhf) instead of the x86 tiers' (the fast path's choice).
     int tier = 0;
@@ -140,7 +151,7 @@ struct Backend {
     static constexpr int SLOTS = 2;
     struct Slot {
         uint32_t *in = nullptr;  // ids | bounds(2) | pos | offsets | sequence count
-        float *rows = nullptr;   // soft-token waves: [CAP][512] input rows (allocated on first use)
+        float *rows = nullptr;   // soft-token waves: [cap][512] input rows (allocated on first use)
         float *out = nullptr;
         int *err = nullptr;  // the device error word, read back with the wave
         cudaEvent_t done = nullptr;
@@ -228,8 +239,11 @@ struct Backend {
     }
 
     Backend(const ei_gguf *g, int dev, unsigned flags)
-        : model(g), device(dev), exact(flags & EG2_B200_EXACT), tier(flags & EG2_B200_SCALAR_TIER ? 1 : 0) {
+        : model(g), device(dev), exact(flags & EG2_B200_EXACT), cap(flags & EG2_B200_WAVE_8192 ? WIDE_CAP : CAP),
+          tier(flags & EG2_B200_SCALAR_TIER ? 1 : 0) {
         if (!g) throw std::runtime_error("empty model");
+        // The exact-order attention keeps a row's scores in shared memory.
+        if (exact && cap > CAP) throw std::runtime_error("parity mode supports waves of up to 2048 tokens");
         // gemma2.c:30-62 hyperparameters.
         if (kv_u64("gemma-embedding2.block_count") != 24 || kv_u64("gemma-embedding2.embedding_length") != 512 ||
             kv_u64("gemma-embedding2.feed_forward_length") != 2048 ||
@@ -301,12 +315,12 @@ struct Backend {
         repack("output.weight", 512, 768, output, 0, staging);
         finish_q8(output);
 
-        // ---- RoPE tables for in-sequence positions 0..CAP-1 (gemma2_fast.c:116-129)
+        // ---- RoPE tables for in-sequence positions 0..cap-1 (gemma2_fast.c:116-129)
         for (int b = 0; b < 2; ++b) {
             const int d = b ? 512 : 256;
             const float base = b ? 1000000.0f : 10000.0f;
-            std::vector<float> c(size_t(CAP) * d / 2), s(size_t(CAP) * d / 2);
-            for (unsigned t = 0; t < CAP; ++t)
+            std::vector<float> c(size_t(cap) * d / 2), s(size_t(cap) * d / 2);
+            for (unsigned t = 0; t < cap; ++t)
                 for (int z = 0; z < d / 2; ++z) {
                     const float theta = float(t) * powf(base, -2.0f * float(z) / float(d));
                     c[size_t(t) * d / 2 + z] = cosf(theta);
@@ -318,50 +332,50 @@ struct Backend {
             ck(cudaMemcpy(rope_sin[b], s.data(), s.size() * 4, cudaMemcpyHostToDevice), "rope upload");
         }
 
-        // ---- arena for CAP packed tokens.  The per-wave inputs share one block
+        // ---- arena for cap packed tokens.  The per-wave inputs share one block
         // laid out like the pinned staging buffer (ids | bounds | pos | offsets),
         // so a wave uploads them with a single copy.
-        unsigned *in_block = dalloc<unsigned>(5 * CAP + 2);
+        unsigned *in_block = dalloc<unsigned>(5 * cap + 2);
         ids = reinterpret_cast<int *>(in_block);
-        bounds = in_block + CAP;
-        pos = in_block + 3 * CAP;
-        offsets = in_block + 4 * CAP;
-        seq_count = in_block + 5 * CAP + 1;
-        x = dalloc<float>(size_t(CAP) * 512);
-        x_hi = dalloc<uint16_t>(size_t(CAP) * 512);
-        x_lo = dalloc<uint16_t>(size_t(CAP) * 512);
-        ple = dalloc<float>(size_t(CAP) * 24 * 512);
-        xq = dalloc<int8_t>(size_t(CAP) * 2048);
-        xs = dalloc<float>(size_t(64) * CAP);
-        qkv = dalloc<float>(size_t(CAP) * 3072);
-        qh = dalloc<uint16_t>(size_t(CAP) * 2048);
-        kh = dalloc<uint16_t>(size_t(CAP) * 512);
-        vh = dalloc<uint16_t>(size_t(CAP) * 512);
-        attn = dalloc<float>(size_t(CAP) * 2048);
-        h = dalloc<float>(size_t(CAP) * 512);
-        gq = dalloc<int8_t>(size_t(CAP) * 2048);
-        gs = dalloc<float>(size_t(64) * CAP);
-        y = dalloc<float>(size_t(CAP) * 768);
-        pooled = dalloc<float>(size_t(CAP) * 768);
+        bounds = in_block + cap;
+        pos = in_block + 3 * cap;
+        offsets = in_block + 4 * cap;
+        seq_count = in_block + 5 * cap + 1;
+        x = dalloc<float>(size_t(cap) * 512);
+        x_hi = dalloc<uint16_t>(size_t(cap) * 512);
+        x_lo = dalloc<uint16_t>(size_t(cap) * 512);
+        ple = dalloc<float>(size_t(cap) * 24 * 512);
+        xq = dalloc<int8_t>(size_t(cap) * 2048);
+        xs = dalloc<float>(size_t(64) * cap);
+        qkv = dalloc<float>(size_t(cap) * 3072);
+        qh = dalloc<uint16_t>(size_t(cap) * 2048);
+        kh = dalloc<uint16_t>(size_t(cap) * 512);
+        vh = dalloc<uint16_t>(size_t(cap) * 512);
+        attn = dalloc<float>(size_t(cap) * 2048);
+        h = dalloc<float>(size_t(cap) * 512);
+        gq = dalloc<int8_t>(size_t(cap) * 2048);
+        gs = dalloc<float>(size_t(64) * cap);
+        y = dalloc<float>(size_t(cap) * 768);
+        pooled = dalloc<float>(size_t(cap) * 768);
         if (exact) {
-            qf = dalloc<float>(size_t(CAP) * 2048);
-            kf = dalloc<float>(size_t(CAP) * 512);
-            vf = dalloc<float>(size_t(CAP) * 512);
+            qf = dalloc<float>(size_t(cap) * 2048);
+            kf = dalloc<float>(size_t(cap) * 512);
+            vf = dalloc<float>(size_t(cap) * 512);
         }
         const int ks[3] = {512, 1024, 2048};
         for (int i = 0; i < 3; ++i)
-            if (!q8_tmap(&tm_xq[i], xq, uint64_t(ks[i]), CAP, 64) ||
-                !scale_tmap(&tm_xs[i], xs, CAP, uint64_t(ks[i] / 32), 64))
+            if (!q8_tmap(&tm_xq[i], xq, uint64_t(ks[i]), cap, 64) ||
+                !scale_tmap(&tm_xs[i], xs, cap, uint64_t(ks[i] / 32), 64))
                 throw std::runtime_error("tensor map (activations)");
-        if (!q8_tmap(&tm_gq, gq, 2048, CAP, 64) || !scale_tmap(&tm_gs, gs, CAP, 64, 64))
+        if (!q8_tmap(&tm_gq, gq, 2048, cap, 64) || !scale_tmap(&tm_gs, gs, cap, 64, 64))
             throw std::runtime_error("tensor map (GeGLU activations)");
-        if (!bf16_tmap(&tm_hi, x_hi, 512, CAP, 128) || !bf16_tmap(&tm_lo, x_lo, 512, CAP, 128) ||
+        if (!bf16_tmap(&tm_hi, x_hi, 512, cap, 128) || !bf16_tmap(&tm_lo, x_lo, 512, cap, 128) ||
             !bf16_tmap(&tm_ple, ple_w, 512, 24 * 512, 256))
             throw std::runtime_error("tensor map (PLE)");
         for (Slot &sl : slots) {
-            ck(cudaMallocHost(&sl.in, sizeof(uint32_t) * (5 * CAP + 2)), "cudaMallocHost");
+            ck(cudaMallocHost(&sl.in, sizeof(uint32_t) * (5 * cap + 2)), "cudaMallocHost");
             ck(cudaMallocHost(&sl.err, sizeof(int)), "cudaMallocHost");
-            ck(cudaMallocHost(&sl.out, sizeof(float) * CAP * 768), "cudaMallocHost");
+            ck(cudaMallocHost(&sl.out, sizeof(float) * cap * 768), "cudaMallocHost");
         }
         ck(cudaStreamSynchronize(stream), "weight upload");
         clear_device_error();
@@ -369,7 +383,7 @@ struct Backend {
             size_t free_b = 0, total_b = 0;
             cudaMemGetInfo(&free_b, &total_b);
             std::fprintf(stderr, "B200: device %d (%s), %zu allocations, %.1f MiB free, cap %u packed tokens\n", device,
-                         prop.name, allocations.size(), free_b / 1048576.0, CAP);
+                         prop.name, allocations.size(), free_b / 1048576.0, cap);
         }
     }
 
@@ -419,7 +433,7 @@ struct Backend {
         else
             ck(launch_ple(tm_hi, tm_lo, tm_ple, ple, ple_norm, N, s), "PLE"), ++launches;
         mark("ple_proj");
-        ck(launch_norm_quant(xq, xs, CAP, nullptr, x, layers[0].attn_norm, N, 512, s, tier), "norm"), ++launches;
+        ck(launch_norm_quant(xq, xs, cap, nullptr, x, layers[0].attn_norm, N, 512, s, tier), "norm"), ++launches;
         mark("norm_quant");
         for (int l = 0; l < 24; ++l) {
             const Layer &L = layers[l];
@@ -441,23 +455,23 @@ struct Backend {
                     ++launches;
                 mark("qkv_post");
                 if (L.d == 256)  // Q8 operand of the O projection written by the attention itself
-                    ck(launch_attention_tc(tc_maps, nullptr, bounds, N, 512, s, xq, xs, CAP, tier), "attention");
+                    ck(launch_attention_tc(tc_maps, nullptr, bounds, N, 512, s, xq, xs, cap, tier), "attention");
                 else
                     ck(launch_attention(attn, qh, kh, vh, bounds, N, L.d, 0, s), "attention");
                 ++launches;
             }
             mark(L.d == 512 ? "attention_global" : "attention_local");
             if (exact || L.d == 512) {
-                ck(launch_norm_quant(xq, xs, CAP, nullptr, attn, nullptr, N, 4 * L.d, s, tier), "quant"), ++launches;
+                ck(launch_norm_quant(xq, xs, cap, nullptr, attn, nullptr, N, 4 * L.d, s, tier), "quant"), ++launches;
                 mark("quant_attn");
             }
             gemm(L.o, h, 512, N, s), ++launches;
             mark("gemm_o");
-            ck(launch_post_add(x, h, L.post_attn_norm, nullptr, xq, xs, CAP, L.ffn_norm, N, s, tier), "post_add"), ++launches;
+            ck(launch_post_add(x, h, L.post_attn_norm, nullptr, xq, xs, cap, L.ffn_norm, N, s, tier), "post_add"), ++launches;
             mark("post_add");
             // ffn_gate and ffn_up in one GEMM whose epilogue applies gelu(gate) * up
             // and quantizes (ROW_GELU_QUANT fused); the result is the down operand.
-            ck(launch_q8gemm_geglu(L.gu.tmap, tm_xq[0], L.gu.tscale, tm_xs[0], exact, gq, gs, CAP, N, L.gu.rows,
+            ck(launch_q8gemm_geglu(L.gu.tmap, tm_xq[0], L.gu.tscale, tm_xs[0], exact, gq, gs, cap, N, L.gu.rows,
                                    L.gu.k, s, tier),
                "GeGLU GEMM"),
                 ++launches;
@@ -466,16 +480,16 @@ struct Backend {
                "q8 GEMM"),
                 ++launches;
             mark("gemm_down");
-            ck(launch_post_add(x, h, L.post_ffw_norm, nullptr, xq, xs, CAP, nullptr, N, s, tier), "post_add"), ++launches;
+            ck(launch_post_add(x, h, L.post_ffw_norm, nullptr, xq, xs, cap, nullptr, N, s, tier), "post_add"), ++launches;
             mark("post_add");
             gemm(L.inp_gate, h, 512, N, s), ++launches;
             mark("gemm_inp_gate");
-            ck(launch_gate_quant(xq, xs, CAP, h, ple, N, 512, 24 * 512, l * 512, s, tier), "ple gate"), ++launches;
+            ck(launch_gate_quant(xq, xs, cap, h, ple, N, 512, 24 * 512, l * 512, s, tier), "ple gate"), ++launches;
             mark("ple_gate_quant");
             gemm(L.proj, h, 512, N, s), ++launches;
             mark("gemm_proj");
             const float *next = l + 1 < 24 ? layers[l + 1].attn_norm : output_norm;
-            ck(launch_post_add(x, h, L.post_norm, L.out_scale, xq, xs, CAP, next, N, s, tier), "post_add"), ++launches;
+            ck(launch_post_add(x, h, L.post_norm, L.out_scale, xq, xs, cap, next, N, s, tier), "post_add"), ++launches;
             mark("post_add");
         }
         gemm(output, y, 768, N, s), ++launches;
@@ -522,10 +536,10 @@ struct Backend {
     // with zero rows to the bucket, into xin (allocated on first use).
     unsigned fill(Slot &sl, const int32_t *in_ids, const size_t *in_off, size_t batch,
                   const float *in_rows = nullptr) {
-        if (in_rows) validate_rows(in_rows, in_off, batch);
-        else validate_wave(in_ids, in_off, batch);
+        if (in_rows) validate_rows(in_rows, in_off, batch, cap);
+        else validate_wave(in_ids, in_off, batch, cap);
         const unsigned n = unsigned(in_off[batch]);
-        uint32_t *hid = sl.in, *hb = sl.in + CAP, *hp = sl.in + 3 * CAP, *ho = sl.in + 4 * CAP;  // device layout
+        uint32_t *hid = sl.in, *hb = sl.in + cap, *hp = sl.in + 3 * cap, *ho = sl.in + 4 * cap;  // device layout
         if (in_ids && !in_rows) std::memcpy(hid, in_ids, n * sizeof(int32_t));
         else std::memset(hid, 0, n * sizeof(int32_t));
         for (size_t s = 0; s < batch; ++s) {
@@ -539,17 +553,17 @@ struct Backend {
         // Padding to the bucket: one sequence [n, n_pad) of token 0, never pooled.
         const unsigned n_pad = (n + BUCKET - 1) / BUCKET * BUCKET;
         for (unsigned t = n; t < n_pad; ++t) hid[t] = 0, hb[2 * t] = n, hb[2 * t + 1] = n_pad, hp[t] = t - n;
-        sl.in[5 * CAP + 1] = uint32_t(batch);
+        sl.in[5 * cap + 1] = uint32_t(batch);
         ck(cudaSetDevice(device), "cudaSetDevice");
         if (in_rows) {
-            if (!sl.rows) ck(cudaMallocHost(&sl.rows, sizeof(float) * CAP * 512), "cudaMallocHost");
-            if (!xin) xin = dalloc<float>(size_t(CAP) * 512);
+            if (!sl.rows) ck(cudaMallocHost(&sl.rows, sizeof(float) * cap * 512), "cudaMallocHost");
+            if (!xin) xin = dalloc<float>(size_t(cap) * 512);
             std::memcpy(sl.rows, in_rows, size_t(n) * 512 * sizeof(float));
             std::memset(sl.rows + size_t(n) * 512, 0, size_t(n_pad - n) * 512 * sizeof(float));
             ck(cudaMemcpyAsync(xin, sl.rows, size_t(n_pad) * 512 * sizeof(float), cudaMemcpyHostToDevice, stream),
                "input rows upload");
         }
-        ck(cudaMemcpyAsync(ids, sl.in, (5 * CAP + 2) * 4, cudaMemcpyHostToDevice, stream), "wave upload");
+        ck(cudaMemcpyAsync(ids, sl.in, (5 * cap + 2) * 4, cudaMemcpyHostToDevice, stream), "wave upload");
         return n_pad;
     }
 
@@ -643,7 +657,7 @@ struct Backend {
     }
 
     void batch(const int32_t *in_ids, const size_t *in_off, size_t n_seq, float *out, const float *in_rows = nullptr) {
-        if (!out) throw std::runtime_error("KFD batch requires 1..2048 packed tokens and nonempty sequences");
+        if (!out) throw std::runtime_error(count_message(cap));
         collect(submit(in_ids, in_off, n_seq, in_rows), out);
     }
 
@@ -766,7 +780,7 @@ extern "C" bool eg2_b200_batch_rows(void *ctx, const float *rows, const size_t *
     return guarded(err, len, [&] {
         Backend *b = as_backend(ctx);
         std::lock_guard<std::mutex> guard(b->mutex);
-        if (!rows) throw std::runtime_error("KFD batch requires 1..2048 packed tokens and nonempty sequences");
+        if (!rows) throw std::runtime_error(count_message(b->cap));
         b->batch(nullptr, offsets, batch, out, rows);
     });
 }
@@ -775,7 +789,7 @@ extern "C" bool eg2_b200_stage_rows(void *ctx, const float *rows, const size_t *
     return guarded(err, len, [&] {
         Backend *b = as_backend(ctx);
         std::lock_guard<std::mutex> guard(b->mutex);
-        if (!rows) throw std::runtime_error("KFD batch requires 1..2048 packed tokens and nonempty sequences");
+        if (!rows) throw std::runtime_error(count_message(b->cap));
         b->stage(nullptr, offsets, batch, rows);
     });
 }
@@ -785,7 +799,7 @@ extern "C" int eg2_b200_submit_rows(void *ctx, const float *rows, const size_t *
     guarded(err, len, [&] {
         Backend *b = as_backend(ctx);
         std::lock_guard<std::mutex> guard(b->mutex);
-        if (!rows) throw std::runtime_error("KFD batch requires 1..2048 packed tokens and nonempty sequences");
+        if (!rows) throw std::runtime_error(count_message(b->cap));
         slot = b->submit(nullptr, offsets, batch, rows);
     });
     return slot;

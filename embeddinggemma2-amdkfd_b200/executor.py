@@ -15,10 +15,11 @@ from . import _lib
 
 EMBED_DIM = 768
 MAX_TOKENS = 2048
+WIDE_MAX_TOKENS = 8192  # EG2_B200_WAVE_8192
 VOCAB = 262144
 
 
-EG2_B200_EXACT, EG2_B200_SCALAR_TIER = 1, 2  # include/eg2_executor.h
+EG2_B200_EXACT, EG2_B200_SCALAR_TIER, EG2_B200_WAVE_8192 = 1, 2, 4  # include/eg2_executor.h
 
 
 class ExecutorError(RuntimeError):
@@ -87,18 +88,24 @@ class GGUFModel:
 class Gemma2Executor:
     """One packed-wave executor on one B200 (ei_gemma2_kfd_create_on)."""
 
-    def __init__(self, model: GGUFModel, device: int | None = None, exact: bool = False, tier: str = "x86"):
+    def __init__(self, model: GGUFModel, device: int | None = None, exact: bool = False, tier: str = "x86",
+                 max_tokens: int = MAX_TOKENS):
         """exact=True: parity mode (eg2_b200_create with EG2_B200_EXACT), every
         operation in the reference CPU graph's own float order; tier="scalar"
         adds the scalar CPU tier's quantizer rounding and GELU
-        (EG2_B200_SCALAR_TIER), so the wave reproduces that tier."""
+        (EG2_B200_SCALAR_TIER), so the wave reproduces that tier.
+        max_tokens=8192: waves up to the reference CPU graph's limit
+        (EG2_B200_WAVE_8192; fast path only)."""
         lib = _lib.load()
         self.model = model  # borrowed by the context: keep it alive
         err = _err()
         if tier not in ("x86", "scalar"):
             raise ValueError("tier must be 'x86' or 'scalar'")
-        if exact:
-            flags = EG2_B200_EXACT | (EG2_B200_SCALAR_TIER if tier == "scalar" else 0)
+        if max_tokens not in (MAX_TOKENS, WIDE_MAX_TOKENS):
+            raise ValueError(f"max_tokens must be {MAX_TOKENS} or {WIDE_MAX_TOKENS}")
+        if exact or max_tokens == WIDE_MAX_TOKENS:
+            flags = (EG2_B200_EXACT if exact else 0) | (EG2_B200_SCALAR_TIER if exact and tier == "scalar" else 0)
+            flags |= EG2_B200_WAVE_8192 if max_tokens == WIDE_MAX_TOKENS else 0
             ctx = lib.eg2_b200_create(model.handle, 0 if device is None else int(device), flags, err, len(err))
         elif device is None:
             ctx = lib.ei_gemma2_kfd_create(model.handle, err, len(err))

@@ -47,6 +47,11 @@ void *ei_gemma2_kfd_create_on(const ei_gguf *g, int device, char *err, size_t le
  * reference's scalar CPU tier (EI_GEMMA2_CPU_X86=scalar) instead of the x86
  * tiers' (trunc(x +- 0.5), exp polynomial), which the fast path uses. */
 #define EG2_B200_SCALAR_TIER 2u
+/* Waves of up to 8192 packed tokens, the reference CPU graph's limit
+ * (gemma2_fast.c:924-925, "EmbeddingGemma 2 accepts 1..8192 input tokens")
+ * instead of the KFD executor's 2048; the context allocates for 8192 tokens.
+ * Fast path only: with EG2_B200_EXACT creation fails. */
+#define EG2_B200_WAVE_8192 4u
 void *eg2_b200_create(const ei_gguf *g, int device, unsigned flags, char *err, size_t len);
 
 /* The host-side checks of src/gemma2_kfd.cpp:270-278 alone (offsets, token

@@ -23,7 +23,10 @@ embeddinggemma2-amdkfd_b200/synthetic.py:
 * golden_inputs_baseline.npz -- a 3-sequence wave (5/12/23 rows) given as
   512-wide input rows (media soft tokens, ids NULL: gemma2_fast.c:940-941),
   seeded N(0, 1), at the scalar and the best tier
-  (`python tests/golden/make_golden.py inputs` writes only this one).
+  (`python tests/golden/make_golden.py inputs` writes only this one);
+* golden_wide_baseline.npz -- one 8192-token sequence (the CPU graph's wave
+  limit, gemma2_fast.c:924) at the best tier
+  (`python tests/golden/make_golden.py wide` writes only this one).
 
 Each scalar-tier run happens in a child process because the reference caches
 its tier on first use.
@@ -74,6 +77,10 @@ def _child(norm: str, what: str, out_path: str):
         x = rng.standard_normal((40, 512)).astype(np.float32)
         res["inputs"], res["offsets"] = x, off
         res["embed"] = ref.embed_inputs(x, off)
+    elif what == "wide":
+        ids, off = syn.wave((8190,), seed=24)
+        res["ids"], res["offsets"] = ids, off
+        res["embed"] = ref.embed(ids, off)
     elif what == "ops":
         rng = np.random.Generator(np.random.PCG64(5))
         x = (rng.standard_normal(64 * 512) * rng.uniform(0.01, 10.0, 64 * 512)).astype(np.float32)
@@ -104,6 +111,12 @@ def make_inputs():
                         embed_scalar=s["embed"], embed_best=b["embed"], best_tier=b["tier"])
 
 
+def make_wide():
+    b = run("baseline", "wide", False)
+    np.savez_compressed(os.path.join(OUT, "golden_wide_baseline.npz"), ids=b["ids"], offsets=b["offsets"],
+                        embed_best=b["embed"], best_tier=b["tier"])
+
+
 def main():
     syn = importlib.import_module("embeddinggemma2-amdkfd_b200.synthetic")
     meta = {}
@@ -121,6 +134,7 @@ def main():
     ops = run("baseline", "ops", False)
     np.savez_compressed(os.path.join(OUT, "golden_ops.npz"), **ops)
     make_inputs()
+    make_wide()
     with open(os.path.join(OUT, "golden_meta.json"), "w") as f:
         json.dump(meta, f, indent=1, sort_keys=True)
     print(json.dumps(meta, indent=1))
@@ -131,5 +145,7 @@ if __name__ == "__main__":
         _child(sys.argv[2], sys.argv[3], sys.argv[4])
     elif len(sys.argv) > 1 and sys.argv[1] == "inputs":
         make_inputs()
+    elif len(sys.argv) > 1 and sys.argv[1] == "wide":
+        make_wide()
     else:
         main()

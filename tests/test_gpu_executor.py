@@ -260,3 +260,49 @@ def test_input_rows_errors(eg2, executor):
         executor.batch_rows(np.zeros((2049, 512), np.float32), np.array([0, 2049], np.uint64))
     with pytest.raises(eg2.ExecutorError, match="512 wide"):
         executor.batch_rows(np.zeros((4, 100), np.float32), np.array([0, 4], np.uint64))
+
+
+@pytest.fixture(scope="module")
+def wide_executor(eg2, model_baseline):
+    m = eg2.GGUFModel(model_baseline)
+    ex = eg2.Gemma2Executor(m, 0, max_tokens=8192)
+    yield ex
+    ex.close()
+    m.close()
+
+
+def test_wide_wave_matches_reference(wide_executor):
+    """EG2_B200_WAVE_8192: one 8192-token sequence (the reference CPU graph's
+    wave limit, gemma2_fast.c:924) against that graph's own output."""
+    g = golden("golden_wide_baseline.npz")
+    out = wide_executor.batch(g["ids"], g["offsets"])
+    c = float(cosine(out[0], g["embed_best"][0]))
+    print("1x8192 cos", c)
+    assert c >= 0.99 - MARGIN
+
+
+def test_wide_wave_packed_equals_standard_context(wide_executor, executor, syn, model_baseline):
+    """A 7600-token wave in an 8192-token context: each sequence's embedding is
+    bit-identical to the same sequence alone in a 2048-token context, for ids
+    and for input rows."""
+    ids, off = syn.wave((2046, 1500, 2046, 2000), seed=94)
+    packed = wide_executor.batch(ids, off)
+    for s in range(len(off) - 1):
+        a, b = int(off[s]), int(off[s + 1])
+        solo = executor.batch(ids[a:b], np.array([0, b - a], np.uint64))
+        np.testing.assert_array_equal(packed[s], solo[0])
+    rows = _embedding_rows(model_baseline, ids)
+    np.testing.assert_array_equal(wide_executor.batch_rows(rows, off), packed)
+
+
+def test_wide_wave_limits(eg2, wide_executor, model_baseline):
+    """Past 8192 tokens the CPU graph's own message; parity mode stays at 2048."""
+    ids = np.zeros(8193, np.int32)
+    with pytest.raises(eg2.ExecutorError, match="accepts 1..8192 input tokens"):
+        wide_executor.batch(ids, np.array([0, 8193], np.uint64))
+    m = eg2.GGUFModel(model_baseline)
+    try:
+        with pytest.raises(eg2.ExecutorError, match="up to 2048 tokens"):
+            eg2.Gemma2Executor(m, 0, exact=True, max_tokens=8192)
+    finally:
+        m.close()
