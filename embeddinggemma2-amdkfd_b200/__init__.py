@@ -7,7 +7,8 @@ Python identifier; import it with
 ``importlib.import_module("embeddinggemma2-amdkfd_b200")``.
 """
 from . import _lib, synthetic  # noqa: F401
-from .executor import (EMBED_DIM, MAX_TOKENS, ExecutorError, GGUFModel, Gemma2Executor,  # noqa: F401
-                       normalize_prefix, validate)
+from .executor import (EMBED_DIM, MAX_TOKENS, WIDE_MAX_TOKENS, ExecutorError, GGUFModel,  # noqa: F401
+                       Gemma2Executor, normalize_prefix, validate, validate_rows)
 
-__all__ = ["GGUFModel", "Gemma2Executor", "ExecutorError", "normalize_prefix", "validate", "EMBED_DIM", "MAX_TOKENS"]
+__all__ = ["GGUFModel", "Gemma2Executor", "ExecutorError", "normalize_prefix", "validate", "validate_rows",
+           "EMBED_DIM", "MAX_TOKENS", "WIDE_MAX_TOKENS"]

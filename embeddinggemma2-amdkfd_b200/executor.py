@@ -57,6 +57,18 @@ def validate(ids, offsets) -> None:
         raise ExecutorError(err.value.decode())
 
 
+def validate_rows(rows, offsets) -> None:
+    """The host-side checks of a soft-token wave (offsets as for ids), no GPU needed."""
+    rows = np.ascontiguousarray(rows, dtype=np.float32)
+    offsets = np.ascontiguousarray(offsets, dtype=np.uint64)
+    batch = len(offsets) - 1
+    err = _err()
+    if not _lib.load().eg2_b200_validate_rows(rows.ctypes.data if rows.size else None,
+                                              offsets.ctypes.data if offsets.size else None, max(batch, 0), err,
+                                              len(err)):
+        raise ExecutorError(err.value.decode())
+
+
 class GGUFModel:
     """A GGUF file mapped by the library's own loader into an `ei_gguf`."""
 

@@ -184,6 +184,23 @@ def test_validate_uses_reference_messages(eg2):
             eg2.validate(ids, off)
 
 
+def test_validate_rows_uses_reference_messages(eg2):
+    """Soft-token waves (512-wide input rows instead of ids) take the offsets
+    checks and messages of an ids wave; the rows themselves are not inspected."""
+    rows = np.zeros((3, 512), np.float32)
+    eg2.validate_rows(rows, np.array([0, 3], np.uint64))
+    eg2.validate_rows(np.full((5, 512), np.nan, np.float32), np.array([0, 3, 5], np.uint64))
+    cases = [
+        (rows, np.array([0, 0], np.uint64), "invalid KFD sequence offsets"),
+        (rows, np.array([1, 3], np.uint64), "KFD batch requires 1..2048 packed tokens and nonempty sequences"),
+        (np.zeros((2049, 512), np.float32), np.array([0, 2049], np.uint64), "1..2048 packed tokens"),
+        (np.zeros((0, 512), np.float32), np.array([0, 3], np.uint64), "1..2048 packed tokens"),
+    ]
+    for r, off, msg in cases:
+        with pytest.raises(eg2.ExecutorError, match=re.escape(msg)):
+            eg2.validate_rows(r, off)
+
+
 def test_product_never_imports_the_oracle():
     pkg = os.path.join(ROOT, "embeddinggemma2-amdkfd_b200")
     for dirpath, _, files in os.walk(pkg):
