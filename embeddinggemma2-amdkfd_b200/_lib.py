@@ -163,7 +163,7 @@ class EgAttentionF16(C.Structure):
 
 class EgAttentionQ8(C.Structure):
     _fields_ = [("q", P), ("qscale", P), ("scale_stride", u32), ("qh", P), ("k", P), ("v", P), ("bounds", P),
-                ("n", u32), ("window", u32), ("tier", u32)]
+                ("n", u32), ("window", u32), ("tier", u32), ("d", u32)]
 
 
 class EgPostAdd(C.Structure):

@@ -1,8 +1,12 @@
-// Packed-varlen bidirectional GQA attention for d = 256 on the 5th-generation
-// tensor cores -- the reference's attention_rows
-// (vendor/embeddinggemma.c/src/gemma2_fast.c:768-894) for the sliding-window
-// layers: for token t and head h, keys s in [lo_t, hi_t) of its own sequence,
-// intersected with [t - window, t + window]; KV head h / 2; scale 1.
+// Packed-varlen bidirectional GQA attention on the 5th-generation tensor cores
+// -- the reference's attention_rows (vendor/embeddinggemma.c/src/gemma2_fast.c:
+// 768-894): for token t and head h, keys s in [lo_t, hi_t) of its own sequence,
+// intersected with [t - window, t + window] when window != 0; scale 1.
+// d = 256 (sliding-window layers, KV head h / 2) and d = 512 (global layers,
+// one KV head).  At d = 512 the 512 output columns would fill the whole tensor
+// memory, so a CTA computes one 256-column half of O (blockIdx.z) and the full
+// score S = Q.K^T over d = 512 from two 256-wide K pieces per key block; Q is a
+// 128 KB tile and one key block of K and V is in flight.
 //
 // A CTA owns 128 query tokens of one head (the TMEM lanes).  Per key block of 64:
 //   S = Q . K^T         tcgen05.mma kind::f16, M = 128, N = 64, K = 256, fp32 in TMEM
@@ -11,11 +15,14 @@
 //                       columns of the same S stage
 //   O += P . V          A = P from TMEM, B = V as an MN-major shared-memory
 //                       operand, M = 128, N = 256, K = 64, fp32 accumulator in TMEM
-// TMEM: S/P stages at columns 0, 64, 128; O at 256..511.  The MMA warp keeps S
-// two blocks ahead (S0 S1 PV0 S2 PV1 S3 ...), so the softmax of block j never
-// waits for its scores, and P needs no shared memory, proxy fence or buffer of
-// its own.  K and V have separate double-buffered stages: K(j+2) loads as soon
-// as S(j) completed, V(j+2) once P.V(j) did.
+// TMEM: S/P stages at columns 0, 64, 128; O (256 columns) at 256..511.  At
+// d = 256 the MMA warp keeps S two blocks ahead (S0 S1 PV0 S2 PV1 S3 ...), so
+// the softmax of block j never waits for its scores, and P needs no shared
+// memory, proxy fence or buffer of its own; K and V have separate
+// double-buffered stages: K(j+2) loads as soon as S(j) completed, V(j+2) once
+// P.V(j) did.  At d = 512 the two K stages hold the two 256-wide halves of one
+// block (each reloaded as soon as its half of S completed) and V has one stage,
+// so the order is S0 PV0 S1 PV1 ...
 // Warps: 0 TMA for Q and K, 6 TMA for V, 1 TMEM owner and MMA issuer, 2..5
 // softmax and epilogue (TMEM lane quadrant = warp % 4; fp32 rows leave through
 // a padded shared-memory tile as whole 128-byte segments).  With a Q8 output
@@ -42,40 +49,48 @@
 namespace eg2 {
 
 struct AttnTcParams {
-    float *out;              // [n][4][256] fp32 (when q is null)
+    float *out;              // [n][4][d] fp32 (when q is null)
     const unsigned *bounds;  // [n][2] = sequence [lo, hi)
     int n, window;
     // Optional Q8_0 output instead of out (ROW_QUANT of the attention row,
-    // gemma2_fast.c:728-730, fused): codes [n][1024], scales block-major
-    // [32][q_stride]; quantizer rounding of `tier`.
+    // gemma2_fast.c:728-730, fused): codes [n][4d], scales block-major
+    // [4d/32][q_stride]; quantizer rounding of `tier`.
     int8_t *q;
     float *qs;
     int q_stride, tier;
 };
 
-struct AttnTcCfg {
-    static constexpr int D = 256, BQ = 128, BKEY = 64, KV_STAGES = 2, S_STAGES = 3, MAXB = 256;
+template <int D_>
+struct AttnTcCfgD {
+    static constexpr int D = D_, DV = 256, BQ = 128, BKEY = 64, S_STAGES = 3, MAXB = 256;
+    // K arrives in pieces of 64 keys x 256 d (KPB per key block) through a ring
+    // of K_STAGES; V in pieces of 64 keys x this CTA's 256 output columns.
+    static constexpr int KPB = D / 256, K_STAGES = 2, V_STAGES = D == 256 ? 2 : 1;
+    static constexpr int AHEAD = D == 256 ? 2 : 1;  // S blocks issued ahead of P.V
     static constexpr int THREADS = 7 * 32;
-    static constexpr int Q_BYTES = BQ * D * 2;    // 4 K-chunks of [128 rows][128 B]
-    static constexpr int K_BYTES = BKEY * D * 2;  // 4 K-chunks of [64 rows][128 B]
-    static constexpr int V_BYTES = BKEY * D * 2;  // 4 d-chunks of [64 keys][128 B] (MN-major)
-    static constexpr size_t K_OFF = Q_BYTES, V_OFF = K_OFF + size_t(KV_STAGES) * K_BYTES;
-    static constexpr size_t BLK_OFF = V_OFF + size_t(KV_STAGES) * V_BYTES;
-    static constexpr size_t SMEM = 1024 + BLK_OFF + MAXB * 8 + 256;
+    static constexpr int Q_BYTES = BQ * D * 2;      // D/64 K-chunks of [128 rows][128 B]
+    static constexpr int K_BYTES = BKEY * 256 * 2;  // 4 K-chunks of [64 rows][128 B]
+    static constexpr int V_BYTES = BKEY * DV * 2;   // 4 d-chunks of [64 keys][128 B] (MN-major)
+    static constexpr size_t K_OFF = Q_BYTES, V_OFF = K_OFF + size_t(K_STAGES) * K_BYTES;
+    static constexpr size_t BLK_OFF = V_OFF + size_t(V_STAGES) * V_BYTES;
+    static constexpr size_t SMEM = 1024 + BLK_OFF + MAXB * 4 + 256;
     static constexpr float RESCALE = 8.0f;
     static constexpr uint32_t O_COL = 256;
 };
+using AttnTcCfg = AttnTcCfgD<256>;
+static_assert(AttnTcCfgD<512>::SMEM <= 227 * 1024, "shared memory");
 
-template <int D_ = 256>
-__global__ void __launch_bounds__(AttnTcCfg::THREADS, 1)
+template <int D_>
+__global__ void __launch_bounds__(AttnTcCfgD<D_>::THREADS, 1)
     attention_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                         const __grid_constant__ CUtensorMap tmV, const AttnTcParams p) {
-    using C = AttnTcCfg;
-    static_assert(D_ == C::D, "d = 256 only");
+    using C = AttnTcCfgD<D_>;
+    static_assert(D_ == 256 || D_ == 512, "d = 256 or 512");
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = align_smem_1024(smem_raw);
     uint8_t *qs = smem;
-    int2 *blocks = reinterpret_cast<int2 *>(smem + C::BLK_OFF);  // (first key, sequence end)
+    // Key blocks: first key | sequence end << 16 (both below 2^16 for n <= 8192).
+    uint32_t *blocks = reinterpret_cast<uint32_t *>(smem + C::BLK_OFF);
     uint64_t *bars = reinterpret_cast<uint64_t *>(blocks + C::MAXB);
     uint64_t *qfull = bars, *kfull = bars + 1, *kempty = kfull + 2, *vfull = kempty + 2, *vempty = vfull + 2;
     uint64_t *sfull = vempty + 2, *pfull = sfull + 3, *pvdone = pfull + 3, *edone = pvdone + 3, *mdone = edone + 1;
@@ -86,25 +101,28 @@ __global__ void __launch_bounds__(AttnTcCfg::THREADS, 1)
     auto v_tile = [&](int s) { return smem + C::V_OFF + s * C::V_BYTES; };
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int t0 = blockIdx.x * C::BQ, head = blockIdx.y, kh = head / 2;
-    // Block j's K (V) into stage j & 1; the caller has made sure the stage is free.
-    auto load_k = [&](int j) {
-        const int s = j & 1;
+    // dh: this CTA's 256 output columns (d = 512; always 0 at d = 256).
+    const int t0 = blockIdx.x * C::BQ, head = blockIdx.y, dh = blockIdx.z, kh = C::D == 256 ? head / 2 : 0;
+    // K piece kp = block kp / KPB, d columns 256 (kp % KPB) .., into stage
+    // kp % 2; block j's V (this CTA's columns) into stage j % V_STAGES.  The
+    // caller has made sure the stage is free.
+    auto load_k = [&](int kp) {
+        const int s = kp % C::K_STAGES, key = int(blocks[kp / C::KPB] & 0xFFFFu), d0 = (kp % C::KPB) * 256;
         bar_expect_tx(&kfull[s], C::K_BYTES);
         for (int c = 0; c < 4; ++c)
-            tma_load_3d(k_tile(s) + c * (C::K_BYTES / 4), &tmK, &kfull[s], c * 64, kh, blocks[j].x);
+            tma_load_3d(k_tile(s) + c * (C::K_BYTES / 4), &tmK, &kfull[s], d0 + c * 64, kh, key);
     };
     auto load_v = [&](int j) {
-        const int s = j & 1;
+        const int s = j % C::V_STAGES, key = int(blocks[j] & 0xFFFFu);
         bar_expect_tx(&vfull[s], C::V_BYTES);
         for (int c = 0; c < 4; ++c)
-            tma_load_3d(v_tile(s) + c * (C::V_BYTES / 4), &tmV, &vfull[s], c * 64, kh, blocks[j].x);
+            tma_load_3d(v_tile(s) + c * (C::V_BYTES / 4), &tmV, &vfull[s], dh * 256 + c * 64, kh, key);
     };
     if (threadIdx.x == 0) {
         tma_prefetch(&tmQ), tma_prefetch(&tmK), tma_prefetch(&tmV);
         *abort = 0;
         bar_init(qfull, 1), bar_init(edone, 4), bar_init(mdone, 1);
-        for (int s = 0; s < C::KV_STAGES; ++s)
+        for (int s = 0; s < 2; ++s)
             bar_init(&kfull[s], 1), bar_init(&kempty[s], 1), bar_init(&vfull[s], 1), bar_init(&vempty[s], 1);
         for (int s = 0; s < C::S_STAGES; ++s) bar_init(&sfull[s], 1), bar_init(&pfull[s], 4), bar_init(&pvdone[s], 1);
         fence_bar_init();
@@ -118,10 +136,11 @@ __global__ void __launch_bounds__(AttnTcCfg::THREADS, 1)
     if (threadIdx.x == 0) {
         // Q first (it needs no bounds), then the tile's key blocks: per
         // sequence present in [t0, tlast), blocks of 64 from the sequence start
-        // covering its rows' key range; the first two blocks' K and V go out
-        // as soon as they are known.
+        // covering its rows' key range; the first K pieces and V blocks that
+        // fit the stages go out as soon as they are known.
         bar_expect_tx(qfull, C::Q_BYTES);
-        for (int c = 0; c < 4; ++c) tma_load_3d(qs + c * (C::Q_BYTES / 4), &tmQ, qfull, c * 64, head, t0);
+        for (int c = 0; c < C::D / 64; ++c)
+            tma_load_3d(qs + c * (C::Q_BYTES / (C::D / 64)), &tmQ, qfull, c * 64, head, t0);
         const int tlast = min(t0 + C::BQ, p.n);
         int nb = 0;
         // Row t0's lo and hi as two independent loads: the first sequence needs
@@ -144,8 +163,9 @@ __global__ void __launch_bounds__(AttnTcCfg::THREADS, 1)
                     nb = -1;
                     break;
                 }
-                blocks[nb] = make_int2(kb, seq_hi);
-                if (nb < C::KV_STAGES) load_k(nb), load_v(nb);
+                blocks[nb] = uint32_t(kb) | uint32_t(seq_hi) << 16;
+                for (int kp = nb * C::KPB; kp < (nb + 1) * C::KPB && kp < C::K_STAGES; ++kp) load_k(kp);
+                if (nb < C::V_STAGES) load_v(nb);
                 ++nb;
             }
             if (nb < 0) break;
@@ -165,45 +185,54 @@ __global__ void __launch_bounds__(AttnTcCfg::THREADS, 1)
     if (warp == 0 || warp == 6) {
         // ------------------------------------------------------------ TMA producers (K: warp 0, V: warp 6)
         if (lane == 0) {
+            // Units: K pieces (warp 0) or V blocks (warp 6).
             const bool is_k = warp == 0;
+            const int stages = is_k ? C::K_STAGES : C::V_STAGES, units = is_k ? nb * C::KPB : nb;
             uint64_t *empty = is_k ? kempty : vempty, *full = is_k ? kfull : vfull;
-            int issued = min(listed, C::KV_STAGES);
-            for (int j = C::KV_STAGES; j < nb; ++j) {
-                if (!wait_bar(&empty[j & 1], ((j >> 1) & 1) ^ 1, abort)) break;
-                if (is_k) load_k(j);
-                else load_v(j);
+            int issued = min(is_k ? listed * C::KPB : listed, stages);
+            for (int u = stages; u < units; ++u) {
+                if (!wait_bar(&empty[u % stages], ((u / stages) & 1) ^ 1, abort)) break;
+                if (is_k) load_k(u);
+                else load_v(u);
                 ++issued;
             }
             // Drain: the last loads into each stage (and Q) have landed before exit.
             if (is_k) wait_bar(qfull, 0, nullptr);
-            for (int k = issued > 2 ? issued - 2 : 0; k < issued; ++k) wait_bar(&full[k & 1], (k >> 1) & 1, nullptr);
+            for (int k = issued > stages ? issued - stages : 0; k < issued; ++k)
+                wait_bar(&full[k % stages], (k / stages) & 1, nullptr);
         }
         __syncwarp();
     } else if (warp == 1) {
         // ------------------------------------------------------------ MMA issuer
         if (lane == 0 && nb > 0) {
-            constexpr uint32_t idesc_s = idesc_f16(C::BQ, C::BKEY), idesc_o = idesc_f16(C::BQ, C::D, true);
+            constexpr uint32_t idesc_s = idesc_f16(C::BQ, C::BKEY), idesc_o = idesc_f16(C::BQ, C::DV, true);
+            constexpr int QCH = C::Q_BYTES / (C::D / 64);  // bytes of one 64-column Q chunk
             const uint32_t qa = smem_u32(qs);
             auto issue_s = [&](int j) -> bool {
-                const int ks = j & 1, st = j % C::S_STAGES;
+                const int st = j % C::S_STAGES;
                 // Stage st last held P of block j - 3, whose P.V must have completed.
-                if (!wait_bar(&kfull[ks], (j >> 1) & 1, abort) ||
-                    (j >= C::S_STAGES && !wait_bar(&pvdone[st], ((j - C::S_STAGES) / C::S_STAGES) & 1, abort)))
+                if (j >= C::S_STAGES && !wait_bar(&pvdone[st], ((j - C::S_STAGES) / C::S_STAGES) & 1, abort))
                     return false;
-                tc_fence_after();
-                const uint32_t ka = smem_u32(k_tile(ks));
+                for (int h = 0; h < C::KPB; ++h) {
+                    const int kp = j * C::KPB + h, ks = kp % C::K_STAGES;
+                    if (!wait_bar(&kfull[ks], (kp / C::K_STAGES) & 1, abort)) return false;
+                    tc_fence_after();
+                    const uint32_t ka = smem_u32(k_tile(ks));
 #pragma unroll
-                for (int kk = 0; kk < C::D / 16; ++kk)
-                    mma_f16(tmem + uint32_t(st * C::BKEY),
-                            desc_sw128(qa + (kk >> 2) * (C::Q_BYTES / 4) + (kk & 3) * 32),
-                            desc_sw128(ka + (kk >> 2) * (C::K_BYTES / 4) + (kk & 3) * 32), idesc_s, kk ? 1u : 0u);
+                    for (int kk = 0; kk < 16; ++kk)
+                        mma_f16(tmem + uint32_t(st * C::BKEY),
+                                desc_sw128(qa + (h * 4 + (kk >> 2)) * QCH + (kk & 3) * 32),
+                                desc_sw128(ka + (kk >> 2) * (C::K_BYTES / 4) + (kk & 3) * 32), idesc_s,
+                                (h > 0 || kk > 0) ? 1u : 0u);
+                    tc_commit(&kempty[ks]);  // this K piece is free once its MMAs completed
+                }
                 tc_commit(&sfull[st]);
-                tc_commit(&kempty[ks]);
                 return true;
             };
             auto issue_pv = [&](int i) -> bool {
-                const int vs = i & 1, st = i % C::S_STAGES;
-                if (!wait_bar(&pfull[st], (i / C::S_STAGES) & 1, abort) || !wait_bar(&vfull[vs], (i >> 1) & 1, abort))
+                const int vs = i % C::V_STAGES, st = i % C::S_STAGES;
+                if (!wait_bar(&pfull[st], (i / C::S_STAGES) & 1, abort) ||
+                    !wait_bar(&vfull[vs], (i / C::V_STAGES) & 1, abort))
                     return false;
                 tc_fence_after();
                 const uint32_t va = smem_u32(v_tile(vs));
@@ -215,8 +244,9 @@ __global__ void __launch_bounds__(AttnTcCfg::THREADS, 1)
                 tc_commit(&vempty[vs]);
                 return true;
             };
-            bool ok = wait_bar(qfull, 0, abort) && issue_s(0) && (nb < 2 || issue_s(1));
-            for (int j = 0; ok && j < nb; ++j) ok = issue_pv(j) && (j + 2 >= nb || issue_s(j + 2));
+            bool ok = wait_bar(qfull, 0, abort);
+            for (int j = 0; ok && j < C::AHEAD && j < nb; ++j) ok = issue_s(j);
+            for (int j = 0; ok && j < nb; ++j) ok = issue_pv(j) && (j + C::AHEAD >= nb || issue_s(j + C::AHEAD));
             // Drain: every MMA issued above has completed before TMEM is freed.
             tc_commit(mdone);
             wait_bar(mdone, 0, nullptr);
@@ -253,7 +283,7 @@ __global__ void __launch_bounds__(AttnTcCfg::THREADS, 1)
             tmem_ld32(scol, reinterpret_cast<uint32_t *>(sr));
             tmem_ld32(scol + 32, reinterpret_cast<uint32_t *>(sr + 32));
             tmem_wait_ld();
-            const int kb = blocks[j].x, kend = min(hi, blocks[j].y);
+            const int kb = int(blocks[j] & 0xFFFFu), kend = min(hi, int(blocks[j] >> 16));
             if (!(kb >= lo && kb + C::BKEY <= kend)) {
 #pragma unroll
                 for (int c = 0; c < 64; ++c)
@@ -278,7 +308,7 @@ __global__ void __launch_bounds__(AttnTcCfg::THREADS, 1)
                 }
                 tc_fence_after();
                 const float f = rescale ? ex2_approx((m - mx) * L2E) : 1.0f;
-                for (int c = 0; c < C::D; c += 32) {
+                for (int c = 0; c < C::DV; c += 32) {
                     uint32_t o[32];
                     tmem_ld32(lane_base + C::O_COL + uint32_t(c), o);
                     tmem_wait_ld();
@@ -317,8 +347,10 @@ __global__ void __launch_bounds__(AttnTcCfg::THREADS, 1)
                 // chunk of the warp's 32 rows goes through a padded tile there and
                 // each store instruction writes four whole 128-byte row segments.
                 const float il = l > 0.0f ? 1.0f / l : 0.0f;
+                // This CTA's columns of the token's 4 x D attention row.
+                const int col0 = head * C::D + dh * C::DV;
                 if (p.q) {
-                    for (int c = 0; c < C::D; c += 32) {
+                    for (int c = 0; c < C::DV; c += 32) {
                         uint32_t r[32];
                         tmem_ld32(lane_base + C::O_COL + uint32_t(c), r);
                         tmem_wait_ld();
@@ -335,16 +367,16 @@ __global__ void __launch_bounds__(AttnTcCfg::THREADS, 1)
                                 w[e] |= q8_code(__uint_as_float(r[4 * e + b]) * il, id, p.tier) << (8 * b);
                         }
                         if (t < p.n) {
-                            uint4 *dst = reinterpret_cast<uint4 *>(p.q + size_t(t) * 1024 + head * C::D + c);
+                            uint4 *dst = reinterpret_cast<uint4 *>(p.q + size_t(t) * (4 * C::D) + col0 + c);
                             dst[0] = make_uint4(w[0], w[1], w[2], w[3]);
                             dst[1] = make_uint4(w[4], w[5], w[6], w[7]);
-                            p.qs[size_t(head * 8 + c / 32) * p.q_stride + t] = fp16_bits_to_f32(ref_fp32_to_fp16(d));
+                            p.qs[size_t((col0 + c) / 32) * p.q_stride + t] = fp16_bits_to_f32(ref_fp32_to_fp16(d));
                         }
                     }
                 } else {
                     float *stg = reinterpret_cast<float *>(qs) + (warp - 2) * (32 * 33);
                     const int srow = lane >> 3, scol4 = (lane & 7) * 4;
-                    for (int c = 0; c < C::D; c += 32) {
+                    for (int c = 0; c < C::DV; c += 32) {
                         uint32_t r[32];
                         tmem_ld32(lane_base + C::O_COL + uint32_t(c), r);
                         tmem_wait_ld();
@@ -356,7 +388,7 @@ __global__ void __launch_bounds__(AttnTcCfg::THREADS, 1)
                             const int r8 = rr + srow, tt = t0 + quad * 32 + r8;
                             const float *src = stg + r8 * 33 + scol4;
                             if (tt < p.n)
-                                *reinterpret_cast<float4 *>(p.out + (size_t(tt) * 4 + head) * C::D + c + scol4) =
+                                *reinterpret_cast<float4 *>(p.out + size_t(tt) * (4 * C::D) + col0 + c + scol4) =
                                     make_float4(src[0], src[1], src[2], src[3]);
                         }
                         __syncwarp();

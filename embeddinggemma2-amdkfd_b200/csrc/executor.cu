@@ -418,10 +418,12 @@ struct Backend {
             if (prof) prof->mark(name);
         };
         const int N = int(n);
-        // Sliding-window layers (d = 256) run the tensor-core attention through
-        // maps whose token extent is this wave's N (captured into its graph).
-        AttnTcMaps tc_maps{};
-        if (!exact && !attention_tc_maps(&tc_maps, qh, kh, vh, N)) ck(cudaErrorInvalidValue, "attention maps");
+        // Both layer kinds run the tensor-core attention through maps whose
+        // token extent is this wave's N (captured into its graph).
+        AttnTcMaps tc_maps[2]{};
+        if (!exact && (!attention_tc_maps(&tc_maps[0], qh, kh, vh, N, 256) ||
+                       !attention_tc_maps(&tc_maps[1], qh, kh, vh, N, 512)))
+            ck(cudaErrorInvalidValue, "attention maps");
         mark("start");
         if (rows)
             ck(launch_input_rows(x, x_hi, x_lo, xin, N, s), "input rows"), ++launches;
@@ -454,14 +456,14 @@ struct Backend {
                    "qkv_post"),
                     ++launches;
                 mark("qkv_post");
-                if (L.d == 256)  // Q8 operand of the O projection written by the attention itself
-                    ck(launch_attention_tc(tc_maps, nullptr, bounds, N, 512, s, xq, xs, cap, tier), "attention");
-                else
-                    ck(launch_attention(attn, qh, kh, vh, bounds, N, L.d, 0, s), "attention");
+                // The O projection's Q8 operand is written by the attention itself.
+                ck(launch_attention_tc(tc_maps[L.d == 512], nullptr, bounds, N, L.d == 512 ? 0 : 512, s, xq, xs, cap,
+                                       tier),
+                   "attention");
                 ++launches;
             }
             mark(L.d == 512 ? "attention_global" : "attention_local");
-            if (exact || L.d == 512) {
+            if (exact) {
                 ck(launch_norm_quant(xq, xs, cap, nullptr, attn, nullptr, N, 4 * L.d, s, tier), "quant"), ++launches;
                 mark("quant_attn");
             }

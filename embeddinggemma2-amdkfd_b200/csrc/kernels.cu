@@ -48,10 +48,10 @@ bool q8_tmap(CUtensorMap *map, const int8_t *base, uint64_t k, uint64_t rows, ui
 bool bf16_tmap(CUtensorMap *map, const void *base, uint64_t k, uint64_t rows, uint32_t box_rows) {
     return encode_tmap_2d(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, base, k, rows, k * 2, 64, box_rows, true);
 }
-bool f16_head_tmap(CUtensorMap *map, const void *base, uint64_t heads, uint64_t n, uint32_t box_rows) {
+bool f16_head_tmap(CUtensorMap *map, const void *base, uint64_t d, uint64_t heads, uint64_t n, uint32_t box_rows) {
     EncodeTiled fn = encode_fn();
-    if (!fn || (reinterpret_cast<uintptr_t>(base) & 15) || !heads || !n) return false;
-    const cuuint64_t dims[3] = {256, heads, n}, strides[2] = {256 * 2, heads * 256 * 2};
+    if (!fn || (reinterpret_cast<uintptr_t>(base) & 15) || !heads || !n || (d != 256 && d != 512)) return false;
+    const cuuint64_t dims[3] = {d, heads, n}, strides[2] = {d * 2, heads * d * 2};
     const cuuint32_t box[3] = {64, 1, box_rows}, estr[3] = {1, 1, 1};
     return fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<void *>(base), dims, strides, box, estr,
               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
@@ -211,18 +211,24 @@ cudaError_t launch_attention(float *out, const void *q, const void *k, const voi
     return cudaErrorInvalidValue;
 }
 
-bool attention_tc_maps(AttnTcMaps *m, const void *q, const void *k, const void *v, int n) {
-    return n > 0 && f16_head_tmap(&m->q, q, 4, uint64_t(n), AttnTcCfg::BQ) &&
-           f16_head_tmap(&m->k, k, 2, uint64_t(n), AttnTcCfg::BKEY) &&
-           f16_head_tmap(&m->v, v, 2, uint64_t(n), AttnTcCfg::BKEY);
+bool attention_tc_maps(AttnTcMaps *m, const void *q, const void *k, const void *v, int n, int d) {
+    const uint64_t kv = d == 256 ? 2 : 1;
+    m->d = d;
+    return n > 0 && f16_head_tmap(&m->q, q, uint64_t(d), 4, uint64_t(n), AttnTcCfg::BQ) &&
+           f16_head_tmap(&m->k, k, uint64_t(d), kv, uint64_t(n), AttnTcCfg::BKEY) &&
+           f16_head_tmap(&m->v, v, uint64_t(d), kv, uint64_t(n), AttnTcCfg::BKEY);
 }
 cudaError_t launch_attention_tc(const AttnTcMaps &m, float *out, const unsigned *bounds, int n, int window,
                                 cudaStream_t s, int8_t *q, float *qs, int q_stride, int tier) {
     if (n <= 0) return cudaSuccess;
-    if (n > ATTN_TC_MAX_TOKENS || window < 0 || (q ? (!qs || q_stride < n) : !out)) return cudaErrorInvalidValue;
+    if (n > ATTN_TC_MAX_TOKENS || window < 0 || (q ? (!qs || q_stride < n) : !out) || (m.d != 256 && m.d != 512))
+        return cudaErrorInvalidValue;
     const AttnTcParams p{out, bounds, n, window, q, qs, q_stride, tier == TIER_SCALAR ? TIER_SCALAR : TIER_X86};
-    return launch_pdl(attention_tc_kernel<256>, dim3((n + AttnTcCfg::BQ - 1) / AttnTcCfg::BQ, 4),
-                      dim3(AttnTcCfg::THREADS), AttnTcCfg::SMEM, s, m.q, m.k, m.v, p);
+    const dim3 grid((n + AttnTcCfg::BQ - 1) / AttnTcCfg::BQ, 4, m.d / 256);
+    if (m.d == 512)
+        return launch_pdl(attention_tc_kernel<512>, grid, dim3(AttnTcCfgD<512>::THREADS), AttnTcCfgD<512>::SMEM, s,
+                          m.q, m.k, m.v, p);
+    return launch_pdl(attention_tc_kernel<256>, grid, dim3(AttnTcCfg::THREADS), AttnTcCfg::SMEM, s, m.q, m.k, m.v, p);
 }
 
 cudaError_t launch_post_add(float *x, const float *h, const float *w, const float *scale, int8_t *q, float *qs,
@@ -283,6 +289,9 @@ cudaError_t init_kernel_attributes() {
         return e;
     if ((e = cudaFuncSetAttribute(attention_tc_kernel<256>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                   int(AttnTcCfg::SMEM))))
+        return e;
+    if ((e = cudaFuncSetAttribute(attention_tc_kernel<512>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  int(AttnTcCfgD<512>::SMEM))))
         return e;
     return cudaFuncSetAttribute(attention_kernel<512>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                 int(AttnCfg<512>::SMEM));
@@ -441,16 +450,17 @@ int eg2_launch_attention_f16(const EgAttentionF16 *p, void *s) {
 int eg2_launch_attention_tc(const EgAttentionF16 *p, void *s) {
     if (cudaError_t e = ensure_attributes()) return rc(e);
     if (!p->n) return 0;
-    if (p->d != 256) return rc(cudaErrorInvalidValue);
+    if (p->d != 256 && p->d != 512) return rc(cudaErrorInvalidValue);
     AttnTcMaps m;
-    if (!attention_tc_maps(&m, p->q, p->k, p->v, int(p->n))) return rc(cudaErrorInvalidValue);
+    if (!attention_tc_maps(&m, p->q, p->k, p->v, int(p->n), int(p->d))) return rc(cudaErrorInvalidValue);
     return rc(launch_attention_tc(m, p->out, p->bounds, int(p->n), int(p->window), S(s)));
 }
 int eg2_launch_attention_tc_q8(const EgAttentionQ8 *p, void *s) {
     if (cudaError_t e = ensure_attributes()) return rc(e);
     if (!p->n) return 0;
+    if (p->d != 256 && p->d != 512) return rc(cudaErrorInvalidValue);
     AttnTcMaps m;
-    if (!attention_tc_maps(&m, p->qh, p->k, p->v, int(p->n))) return rc(cudaErrorInvalidValue);
+    if (!attention_tc_maps(&m, p->qh, p->k, p->v, int(p->n), int(p->d))) return rc(cudaErrorInvalidValue);
     return rc(launch_attention_tc(m, nullptr, p->bounds, int(p->n), int(p->window), S(s), p->q, p->qscale,
                                   int(p->scale_stride), int(p->tier)));
 }

@@ -48,16 +48,18 @@ cudaError_t launch_attention_exact(float *out, const float *q, const float *k, c
 cudaError_t launch_ple_exact(float *ple, const float *x, const void *w, const float *norm, int n, cudaStream_t s);
 cudaError_t launch_attention(float *out, const void *q, const void *k, const void *v, const unsigned *bounds, int n,
                              int d, int window, cudaStream_t s);
-// The tensor-core attention of the sliding-window layers (d = 256): Q [n][4][256],
-// K/V [n][2][256] fp16 through 3-D maps (element, head, token) whose token
-// extent is n, so rows past n read as zeros.  At most ATTN_TC_MAX_TOKENS tokens
-// per launch (the per-tile key-block list then always fits).
+// The tensor-core attention (d = 256: Q [n][4][256], K/V [n][2][256]; d = 512:
+// Q [n][4][512], K/V [n][1][512]), fp16 through 3-D maps (element, head,
+// token) whose token extent is n, so rows past n read as zeros.  At most
+// ATTN_TC_MAX_TOKENS tokens per launch (the per-tile key-block list then always
+// fits).
 constexpr int ATTN_TC_MAX_TOKENS = 8192;
 struct AttnTcMaps {
     CUtensorMap q, k, v;
+    int d = 256;
 };
-bool attention_tc_maps(AttnTcMaps *m, const void *q, const void *k, const void *v, int n);
-// With q set, writes Q8_0 codes [n][1024] and block-major scales [32][q_stride]
+bool attention_tc_maps(AttnTcMaps *m, const void *q, const void *k, const void *v, int n, int d = 256);
+// With q set, writes Q8_0 codes [n][4d] and block-major scales [4d/32][q_stride]
 // (the row quantizer's output for the same rows) instead of fp32 out.
 cudaError_t launch_attention_tc(const AttnTcMaps &m, float *out, const unsigned *bounds, int n, int window,
                                 cudaStream_t s, int8_t *q = nullptr, float *qs = nullptr, int q_stride = 0,

@@ -102,14 +102,14 @@ def attention_f16(out, q, k, v, bounds, n, d, window):
 
 
 def attention_tc(out, q, k, v, bounds, n, window, d=256):
-    """attention_f16 on the tcgen05 tensor cores (d = 256, n <= 8192)."""
+    """attention_f16 on the tcgen05 tensor cores (d = 256 or 512, n <= 8192)."""
     _call("eg2_launch_attention_tc", _lib.EgAttentionF16(_p(out), _p(q), _p(k), _p(v), _p(bounds), n, d, window))
 
 
-def attention_tc_q8(q, qscale, scale_stride, qh, k, v, bounds, n, window, tier=0):
+def attention_tc_q8(q, qscale, scale_stride, qh, k, v, bounds, n, window, tier=0, d=256):
     """attention_tc with its output rows quantized to Q8_0 in the epilogue."""
     _call("eg2_launch_attention_tc_q8", _lib.EgAttentionQ8(_p(q), _p(qscale), scale_stride, _p(qh), _p(k), _p(v),
-                                                           _p(bounds), n, window, tier))
+                                                           _p(bounds), n, window, tier, d))
 
 
 def post_add(x, h, weight, scale, q, qscale, scale_stride, next_weight, rows, tier=0):

@@ -135,17 +135,19 @@ int eg2_launch_q8_mm(const EgQ8MM *p, void *stream);
 int eg2_launch_q8_geglu(const EgQ8GeGLU *p, void *stream);
 int eg2_launch_qkv_post(const EgQkvPost *p, void *stream);
 int eg2_launch_attention_f16(const EgAttentionF16 *p, void *stream);
-/* The same attention on the 5th-generation tensor cores, d = 256 only (the
- * sliding-window layers): S = Q.K^T and O += P.V as tcgen05 MMAs with fp32
- * accumulators in tensor memory, P in fp16.  n <= 8192; other d -> error. */
+/* The same attention on the 5th-generation tensor cores, d = 256 (the
+ * sliding-window layers) or 512 (the global layers): S = Q.K^T and O += P.V as
+ * tcgen05 MMAs with fp32 accumulators in tensor memory, P in fp16.
+ * n <= 8192; other d -> error. */
 int eg2_launch_attention_tc(const EgAttentionF16 *p, void *stream);
 /* eg2_launch_attention_tc with the Q8_0 quantization of its output rows fused
- * (ROW_QUANT, gemma2_fast.c:728-730): codes q [n][1024], block-major scales
- * qscale [32][scale_stride] (scale_stride >= n), bit-identical to
- * eg2_launch_norm_quant (weight NULL) of the fp32 rows; tier as in EgNormQuant. */
+ * (ROW_QUANT, gemma2_fast.c:728-730): codes q [n][4d], block-major scales
+ * qscale [4d/32][scale_stride] (scale_stride >= n), bit-identical to
+ * eg2_launch_norm_quant (weight NULL) of the fp32 rows; tier as in EgNormQuant;
+ * d = 256 or 512. */
 typedef struct {
     int8_t *q; float *qscale; unsigned scale_stride;
-    const uint16_t *qh, *k, *v; const unsigned *bounds; unsigned n, window, tier;
+    const uint16_t *qh, *k, *v; const unsigned *bounds; unsigned n, window, tier, d;
 } EgAttentionQ8;
 int eg2_launch_attention_tc_q8(const EgAttentionQ8 *p, void *stream);
 /* The reference CPU graph's scalar attention order on fp32 q/k/v

@@ -406,81 +406,90 @@ def test_attention_f16_vs_reference_attention(ops, port, d, window, lengths):
     assert cosine(got.ravel(), ref.ravel()) > 0.99999
 
 
-def _attn_case(rng, lengths, kscale=0.1):
-    n = sum(lengths)
-    q = rng.standard_normal((n, 4, 256)).astype(np.float16)
-    k = (rng.standard_normal((n, 2, 256)) * kscale).astype(np.float16)
-    v = rng.standard_normal((n, 2, 256)).astype(np.float16)
+def _attn_case(rng, lengths, kscale=0.1, d=256):
+    n, kv = sum(lengths), 512 // d
+    q = rng.standard_normal((n, 4, d)).astype(np.float16)
+    k = (rng.standard_normal((n, kv, d)) * kscale * (256 / d) ** 0.5).astype(np.float16)
+    v = rng.standard_normal((n, kv, d)).astype(np.float16)
     lo, hi = _bounds(lengths)
     return n, q, k, v, lo, hi
 
 
-@pytest.mark.parametrize("window,lengths,kscale", [
-    (512, [10, 19, 35, 66], 0.1), (512, [1300, 3, 128], 0.1), (0, [700, 129], 0.1), (512, [2048], 0.1),
-    (512, [1] * 5 + [64] * 20 + [63, 65, 127, 129], 0.1), (0, [1500, 96], 0.1),
+@pytest.mark.parametrize("d,window,lengths,kscale", [
+    (256, 512, [10, 19, 35, 66], 0.1), (256, 512, [1300, 3, 128], 0.1), (256, 0, [700, 129], 0.1),
+    (256, 512, [2048], 0.1), (256, 512, [1] * 5 + [64] * 20 + [63, 65, 127, 129], 0.1), (256, 0, [1500, 96], 0.1),
     # Scores of std ~16: nearly one-hot rows, frequent reference-maximum moves.
-    (512, [900, 77], 1.0)])
-def test_attention_tc_vs_reference_attention(ops, port, window, lengths, kscale):
+    (256, 512, [900, 77], 1.0),
+    # Global layers: d = 512, one KV head, no window (and a window, for coverage).
+    (512, 0, [10, 19, 35, 66], 0.1), (512, 0, [700, 129], 0.1), (512, 0, [2048], 0.1),
+    (512, 0, [1] * 5 + [64] * 20 + [63, 65, 127, 129], 0.1), (512, 512, [1300, 3, 128], 0.1),
+    (512, 0, [900, 77], 1.0)])
+def test_attention_tc_vs_reference_attention(ops, port, d, window, lengths, kscale):
     """Tensor-core attention (fp16 P, fp32 TMEM accumulators) against the
     reference's fp32 attention_rows restated, same tolerance as attention_f16."""
-    rng = np.random.default_rng(sum(lengths) + window + int(kscale * 10))
-    n, q, k, v, lo, hi = _attn_case(rng, lengths, kscale)
-    ref = port.attention(q.astype(np.float32), k.astype(np.float32), v.astype(np.float32), lo, hi, 2, 256, window)
-    out = torch.full((n * 4 * 256,), float("nan"), device=DEV)
-    ops.attention_tc(out, T(q), T(k), T(v), T(np.stack([lo, hi], 1).ravel()), n, window)
-    got = host(out).reshape(n, 4 * 256)
-    np.testing.assert_allclose(got, ref.reshape(n, 4 * 256), atol=3e-3, rtol=0)
+    rng = np.random.default_rng(sum(lengths) + window + int(kscale * 10) + d)
+    n, q, k, v, lo, hi = _attn_case(rng, lengths, kscale, d)
+    ref = port.attention(q.astype(np.float32), k.astype(np.float32), v.astype(np.float32), lo, hi, 512 // d, d,
+                         window)
+    out = torch.full((n * 4 * d,), float("nan"), device=DEV)
+    ops.attention_tc(out, T(q), T(k), T(v), T(np.stack([lo, hi], 1).ravel()), n, window, d)
+    got = host(out).reshape(n, 4 * d)
+    np.testing.assert_allclose(got, ref.reshape(n, 4 * d), atol=3e-3, rtol=0)
     assert cosine(got.ravel(), ref.ravel()) > 0.99999
 
 
-def test_attention_tc_packed_equals_solo(ops):
+@pytest.mark.parametrize("d,window", [(256, 512), (512, 0)])
+def test_attention_tc_packed_equals_solo(ops, d, window):
     """A sequence's rows come out bit-identical wherever it sits in the packed
     wave: key blocks are aligned to each sequence's own start."""
     rng = np.random.default_rng(77)
     lengths = [37, 300, 129, 5, 700]
-    n, q, k, v, lo, hi = _attn_case(rng, lengths)
-    out = torch.zeros(n * 4 * 256, device=DEV)
-    ops.attention_tc(out, T(q), T(k), T(v), T(np.stack([lo, hi], 1).ravel()), n, 512)
-    packed = host(out).reshape(n, 4 * 256)
+    n, q, k, v, lo, hi = _attn_case(rng, lengths, d=d)
+    out = torch.zeros(n * 4 * d, device=DEV)
+    ops.attention_tc(out, T(q), T(k), T(v), T(np.stack([lo, hi], 1).ravel()), n, window, d)
+    packed = host(out).reshape(n, 4 * d)
     off = np.concatenate([[0], np.cumsum(lengths)])
     for i, L in enumerate(lengths):
         a, b = off[i], off[i + 1]
         slo, shi = _bounds([L])
-        solo = torch.zeros(L * 4 * 256, device=DEV)
+        solo = torch.zeros(L * 4 * d, device=DEV)
         ops.attention_tc(solo, T(np.ascontiguousarray(q[a:b])), T(np.ascontiguousarray(k[a:b])),
-                         T(np.ascontiguousarray(v[a:b])), T(np.stack([slo, shi], 1).ravel()), L, 512)
-        np.testing.assert_array_equal(host(solo).reshape(L, 4 * 256), packed[a:b])
+                         T(np.ascontiguousarray(v[a:b])), T(np.stack([slo, shi], 1).ravel()), L, window, d)
+        np.testing.assert_array_equal(host(solo).reshape(L, 4 * d), packed[a:b])
 
 
 @pytest.mark.parametrize("tier", [0, 1])
-@pytest.mark.parametrize("lengths", [[128] * 16, [1300, 3, 128, 37]])
-def test_attention_tc_q8_equals_row_quantizer(ops, lengths, tier):
+@pytest.mark.parametrize("d,lengths", [(256, [128] * 16), (256, [1300, 3, 128, 37]), (512, [128] * 16),
+                                       (512, [1300, 3, 128, 37])])
+def test_attention_tc_q8_equals_row_quantizer(ops, d, lengths, tier):
     """The fused Q8_0 epilogue writes exactly the codes and scales the row
     quantizer (norm_quant, weight NULL) gives for the fp32 attention rows."""
-    rng = np.random.default_rng(len(lengths) + tier)
-    n, q, k, v, lo, hi = _attn_case(rng, lengths)
+    rng = np.random.default_rng(len(lengths) + tier + d)
+    n, q, k, v, lo, hi = _attn_case(rng, lengths, d=d)
+    window, w = (512 if d == 256 else 0), 4 * d
     b = T(np.stack([lo, hi], 1).ravel())
     qt, kt, vt = T(q), T(k), T(v)
-    out = torch.zeros(n * 1024, device=DEV)
-    ops.attention_tc(out, qt, kt, vt, b, n, 512)
+    out = torch.zeros(n * w, device=DEV)
+    ops.attention_tc(out, qt, kt, vt, b, n, window, d)
     stride = n + 5
-    ref_q = torch.zeros(n * 1024, dtype=torch.int8, device=DEV)
-    ref_s = torch.zeros(32 * stride, device=DEV)
-    ops.norm_quant(ref_q, ref_s, stride, out, None, n, 1024, tier=tier)
-    got_q = torch.full((n * 1024,), 99, dtype=torch.int8, device=DEV)
-    got_s = torch.zeros(32 * stride, device=DEV)
-    ops.attention_tc_q8(got_q, got_s, stride, qt, kt, vt, b, n, 512, tier=tier)
+    ref_q = torch.zeros(n * w, dtype=torch.int8, device=DEV)
+    ref_s = torch.zeros(w // 32 * stride, device=DEV)
+    ops.norm_quant(ref_q, ref_s, stride, out, None, n, w, tier=tier)
+    got_q = torch.full((n * w,), 99, dtype=torch.int8, device=DEV)
+    got_s = torch.zeros(w // 32 * stride, device=DEV)
+    ops.attention_tc_q8(got_q, got_s, stride, qt, kt, vt, b, n, window, tier=tier, d=d)
     np.testing.assert_array_equal(host(got_q), host(ref_q))
-    np.testing.assert_array_equal(host(got_s).reshape(32, stride)[:, :n], host(ref_s).reshape(32, stride)[:, :n])
+    np.testing.assert_array_equal(host(got_s).reshape(w // 32, stride)[:, :n],
+                                  host(ref_s).reshape(w // 32, stride)[:, :n])
 
 
 def test_attention_tc_rejects_unsupported(ops):
-    """d != 256 and more than 8192 tokens are refused before any launch."""
+    """d other than 256 / 512 and more than 8192 tokens are refused before any launch."""
     z = torch.zeros(16, device=DEV)
     with pytest.raises(RuntimeError):
         ops.attention_tc(z, z, z, z, z, 8193, 512)
     with pytest.raises(RuntimeError):
-        ops.attention_tc(z, z, z, z, z, 10, 0, d=512)
+        ops.attention_tc(z, z, z, z, z, 10, 0, d=384)
 
 
 @pytest.mark.parametrize("d,window,lengths", [(256, 512, [10, 700, 3]), (512, 0, [300, 64]), (256, 512, [1100])])
