@@ -58,9 +58,13 @@ ATTN_SHAPES = (("16x128", (128,) * 16), ("1x2048", (2048,)))
 
 
 def attn_pairs(lengths, window=512):
-    """(query, key) pairs of one sliding-window layer over packed sequences."""
+    """(query, key) pairs of one layer over packed sequences (window 0: the
+    whole sequence, the global layers)."""
     tot = 0
     for L in lengths:
+        if not window:
+            tot += L * L
+            continue
         t = np.arange(L)
         tot += int((np.minimum(L, t + window + 1) - np.maximum(0, t - window)).sum())
     return tot
@@ -524,7 +528,9 @@ def attention_microbench(args, local):
     mma.sync, max |difference|), then `warmup` launches, then the graph.  Order
     of fp32-output tcgen05 launches: shape 1 parity, warm-ups, 2 x steps graph
     nodes, then shape 2 likewise (the Q8-output timing of each shape follows
-    its mma.sync timing)."""
+    its mma.sync timing).  The same two waves then run through the global
+    layers' form (d = 512, one KV head, no window), reported beside the
+    value."""
     import torch
     ops = importlib.import_module("embeddinggemma2-amdkfd_b200.ops")
     torch.cuda.set_device(local)
@@ -554,37 +560,43 @@ def attention_microbench(args, local):
         del g
         return e0.elapsed_time(e1) * 1000.0 / args.steps
 
-    rows, tot_fl, tot_s = [], 0.0, 0.0
-    for name, lengths in ATTN_SHAPES:
-        n = sum(lengths)
-        q = torch.from_numpy(rng.standard_normal((n, 4, 256)).astype(np.float16)).to(dev)
-        k = torch.from_numpy((rng.standard_normal((n, 2, 256)) * 0.1).astype(np.float16)).to(dev)
-        v = torch.from_numpy(rng.standard_normal((n, 2, 256)).astype(np.float16)).to(dev)
+    def measure(name, lengths, d, window):
+        n, kv = sum(lengths), 512 // d
+        q = torch.from_numpy(rng.standard_normal((n, 4, d)).astype(np.float16)).to(dev)
+        k = torch.from_numpy((rng.standard_normal((n, kv, d)) * 0.1 * (256 / d) ** 0.5).astype(np.float16)).to(dev)
+        v = torch.from_numpy(rng.standard_normal((n, kv, d)).astype(np.float16)).to(dev)
         lo, hi = attn_bounds(lengths)
         b = torch.from_numpy(np.stack([lo, hi], 1).ravel().copy()).to(dev)
-        o_tc, o_mma = torch.zeros(n * 1024, device=dev), torch.zeros(n * 1024, device=dev)
-        q8 = torch.zeros(n * 1024, dtype=torch.int8, device=dev)
-        q8s = torch.zeros(32 * n, device=dev)
-        tc = lambda: ops.attention_tc(o_tc, q, k, v, b, n, 512)
-        tc_q8 = lambda: ops.attention_tc_q8(q8, q8s, n, q, k, v, b, n, 512)
-        mma = lambda: ops.attention_f16(o_mma, q, k, v, b, n, 256, 512)
+        o_tc, o_mma = torch.zeros(n * 4 * d, device=dev), torch.zeros(n * 4 * d, device=dev)
+        q8 = torch.zeros(n * 4 * d, dtype=torch.int8, device=dev)
+        q8s = torch.zeros(4 * d // 32 * n, device=dev)
+        tc = lambda: ops.attention_tc(o_tc, q, k, v, b, n, window, d)
+        tc_q8 = lambda: ops.attention_tc_q8(q8, q8s, n, q, k, v, b, n, window, d=d)
+        mma = lambda: ops.attention_f16(o_mma, q, k, v, b, n, d, window)
         tc(), mma()
         torch.cuda.synchronize()
         diff = float((o_tc - o_mma).abs().max())
         us_tc, us_mma = timed(tc), timed(mma)
         us_q8 = timed(tc_q8)
-        fl = 16.0 * 256 * attn_pairs(lengths)
-        tot_fl, tot_s = tot_fl + fl, tot_s + us_tc * 1e-6
-        rows.append({"shape": name, "gflop": round(fl / 1e9, 3), "us_tcgen05": round(us_tc, 2),
-                     "tflop_s": round(fl / us_tc / 1e6, 1), "frac_of_peak": round(fl / us_tc / 1e6 / peak, 4),
-                     "us_mma_sync": round(us_mma, 2), "max_abs_diff_vs_mma_sync": diff,
-                     "us_tcgen05_q8_out": round(us_q8, 2)})
+        fl = 16.0 * d * attn_pairs(lengths, window)
+        return fl, us_tc, {"shape": name, "d": d, "window": window, "gflop": round(fl / 1e9, 3),
+                           "us_tcgen05": round(us_tc, 2), "tflop_s": round(fl / us_tc / 1e6, 1),
+                           "frac_of_peak": round(fl / us_tc / 1e6 / peak, 4), "us_mma_sync": round(us_mma, 2),
+                           "max_abs_diff_vs_mma_sync": diff, "us_tcgen05_q8_out": round(us_q8, 2)}
+
+    rows, tot_fl, tot_s = [], 0.0, 0.0
+    for name, lengths in ATTN_SHAPES:
+        fl, us, row = measure(name, lengths, 256, 512)
+        tot_fl, tot_s = tot_fl + fl, tot_s + us * 1e-6
+        rows.append(row)
+    # The global layers (d = 512, one KV head, no window) at the same waves.
+    global_rows = [measure(name, lengths, 512, 0)[2] for name, lengths in ATTN_SHAPES]
     line = {"metric": METRIC_ATTN, "value": tot_fl / tot_s / 1e12, "unit": "TFLOP/s", "n_gpus": 1,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": tot_s * 1e3, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "f16 (fp32 accumulate and softmax)",
             "data": "synthetic", "config": {"workload": CONFIGS[5][0]},
             "peak": {"value": peak, "unit": "TFLOP/s", "source": f"bf16_tflops of {src} MEASURED_PEAKS"},
-            "shapes": rows, "gpu_launches": 2 * len(ATTN_SHAPES) * args.steps,
+            "shapes": rows, "global_layer_shapes": global_rows, "gpu_launches": 2 * len(ATTN_SHAPES) * args.steps,
             "note": "value and tflop_s: fp32 output; us_tcgen05_q8_out: the executor's form, Q8_0 output of the O projection"}
     print(json.dumps(line), flush=True)
 
