@@ -16,7 +16,9 @@
 // the packed wave (blocks of other sequences are fully masked for it and leave
 // its state bit-for-bit unchanged), so packed and solo results are identical.
 // Shared-memory rows are XOR-swizzled in 16-byte chunks so ldmatrix is
-// conflict-free.
+// conflict-free.  The executor's fast path runs the tcgen05 kernel of
+// attention_tc.cuh on both layer kinds; this one is the eg2_launch_attention_f16
+// operator.
 #pragma once
 #include "common.cuh"
 
