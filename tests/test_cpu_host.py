@@ -67,6 +67,35 @@ def test_bench_gemm_op_count():
     assert bench.whole_job_rate(2048, 4, 10, 100.0) == pytest.approx(2048 * 4 * 10 / 0.1)
 
 
+def test_bench_attention_pair_count():
+    """Algorithmic attention work of bench.py config 5: (query, key) pairs per
+    layer, window +-w inside each sequence or (window 0) the whole sequence."""
+    sys.path.insert(0, ROOT)
+    bench = importlib.import_module("bench")
+
+    def brute(lengths, w):
+        return sum(sum(1 for t in range(L) for k in range(L) if not w or abs(t - k) <= w) for L in lengths)
+
+    for lengths, w in (((5,), 1), ((7, 3, 40), 4), ((9, 16), 0), ((128,) * 3, 512)):
+        assert bench.attn_pairs(lengths, w) == brute(lengths, w)
+    assert bench.attn_pairs((2048,), 0) == 2048 * 2048
+
+
+def test_bench_reference_arm_contract():
+    """`bench.py --impl reference` prints one JSON line with the fields the
+    driver reads (config 5: the C restatement of attention_rows, CPU only)."""
+    r = subprocess.run([sys.executable, os.path.join(ROOT, "bench.py"), "--impl", "reference", "--config", "5"],
+                       capture_output=True, text=True, timeout=600, cwd=ROOT)
+    assert r.returncode == 0, r.stderr[-2000:]
+    line = json.loads(r.stdout.strip().splitlines()[-1])
+    for key in ("metric", "value", "unit", "n_gpus", "steps", "warmup", "ms_per_step", "higher_is_better",
+                "scaling", "dtype", "config", "impl", "cpu_baseline", "e2e"):
+        assert key in line, key
+    assert line["impl"] == "reference" and line["value"] > 0
+    assert {"value", "unit", "cores", "kind", "sample"} <= set(line["cpu_baseline"])
+    assert {"value", "unit", "h2d_bytes_per_step", "d2h_bytes_per_step"} <= set(line["e2e"])
+
+
 def _free_port():
     with socket.socket() as s:
         s.bind(("127.0.0.1", 0))
