@@ -214,7 +214,7 @@ def test_input_rows_of_token_embeddings_equal_ids_path(executor, model_baseline,
     the wave is bit-identical to the ids wave, through the monolithic, staged
     and pipelined calls."""
     g = golden("golden_baseline.npz")
-    for ids, off in ((g["ids"], g["offsets"]), syn.wave((5, 300, 40, 1), seed=92)):
+    for ids, off in ((g["ids"], g["offsets"]), syn.wave((5, 300, 40, 1), seed=92), syn.wave((600, 700, 1), seed=95)):
         rows = _embedding_rows(model_baseline, ids)
         ref = executor.batch(ids, off)
         np.testing.assert_array_equal(executor.batch_rows(rows, off), ref)
