@@ -511,6 +511,7 @@ struct Backend {
             ck(cudaStreamSynchronize(stream), "graph cache flush");
             for (auto &kv : graphs) cudaGraphExecDestroy(kv.second);
             graphs.clear();
+            staged_graph = nullptr;  // stage() again before launch()
         }
         cudaGraph_t graph = nullptr;
         ck(cudaStreamBeginCapture(stream, cudaStreamCaptureModeThreadLocal), "begin capture");
