@@ -52,6 +52,10 @@ WIDE_CONFIGS = (7,)  # run in an 8192-token context (EG2_B200_WAVE_8192)
 METRIC_MIXED = "embedded tokens/s per box (mixed-length requests, executor level)"
 METRIC_GEMM = "Q8_0 GEMM TOP/s (model shapes, M = 2048)"
 METRIC_ATTN = "local-layer attention TFLOP/s (d = 256, window 512; 16x128 and 1x2048 waves)"
+# The arithmetic of the fast path, stage by stage.
+DTYPE_FAST = ("int8 Q8_0 GEMMs (exact int32 block sums, fp32 scaling), fp16 attention operands with fp32 "
+              "scores/softmax/accumulation, bf16 hi+lo PLE projection with fp32 accumulation, fp32 norms")
+DTYPE_REFERENCE = "int8 Q8_0 GEMMs (int32 block sums, fp32 scaling), fp32 everything else (reference CPU graph)"
 # (name, sequence lengths) of the attention microbench; algorithmic FLOPs are
 # 4 heads x 4 d per (query, key) pair the layer visits.
 ATTN_SHAPES = (("16x128", (128,) * 16), ("1x2048", (2048,)))
@@ -97,11 +101,6 @@ def q8_gemm_ops(n_tokens: int) -> float:
 GEMM_DRAM_BYTES_PER_LAUNCH = 3.07e6
 
 
-# The executor uploads each wave's inputs as one block: ids, bounds (2 words),
-# positions, offsets (2048 tokens each) and the sequence count.
-H2D_BYTES_PER_WAVE = (5 * 2048 + 2) * 4
-
-
 def peaks():
     path = os.path.join(ROOT, "MEASURED_PEAKS.json")
     if os.path.exists(path):
@@ -112,25 +111,58 @@ def peaks():
 
 
 class ClockSampler:
-    """nvidia-smi clocks and throttle reasons sampled during the timed region."""
+    """SM clocks and throttle reasons sampled during the timed region: NVML
+    read every 5 ms on a thread (read-only queries; nothing is set), or
+    nvidia-smi at 200 ms where NVML is unavailable."""
     Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
          "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
          "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    NAMES = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
 
     def __init__(self, device: int):
-        self.device, self.proc = device, None
+        self.device, self.proc, self.thread, self.rows = device, None, None, []
+
+    def _nvml_loop(self, nv, h):
+        bits = [nv.nvmlClocksEventReasonHwSlowdown, nv.nvmlClocksEventReasonHwThermalSlowdown,
+                nv.nvmlClocksEventReasonSwThermalSlowdown, nv.nvmlClocksEventReasonSwPowerCap]
+        while not self.stop:
+            try:
+                sm = nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)
+                mx = nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM)
+                r = nv.nvmlDeviceGetCurrentClocksEventReasons(h)
+                self.rows.append((float(sm), float(mx), ["Active" if r & b else "Not Active" for b in bits]))
+            except Exception:
+                pass
+            time.sleep(0.005)
 
     def __enter__(self):
+        self.stop = False
+        try:
+            import threading
+            import pynvml as nv
+            nv.nvmlInit()
+            vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+            index = int(vis.split(",")[self.device]) if vis and vis.split(",")[0].isdigit() else self.device
+            h = nv.nvmlDeviceGetHandleByIndex(index)
+            self.thread = threading.Thread(target=self._nvml_loop, args=(nv, h), daemon=True)
+            self.thread.start()
+            self.source = "nvml 5 ms"
+            return self
+        except Exception:
+            self.thread = None
         try:
             self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.device), f"--query-gpu={self.Q}",
                                           "--format=csv,noheader,nounits", "-lms", "200"],
                                          stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.source = "nvidia-smi 200 ms"
         except (FileNotFoundError, OSError):
             self.proc = None
         return self
 
     def __exit__(self, *exc):
-        self.lines = []
+        if self.thread:
+            self.stop = True
+            self.thread.join(timeout=5)
         if self.proc:
             time.sleep(0.3)
             self.proc.terminate()
@@ -139,23 +171,21 @@ class ClockSampler:
             except subprocess.TimeoutExpired:
                 self.proc.kill()
                 out, _ = self.proc.communicate()
-            self.lines = [l for l in out.splitlines() if l.strip()]
+            for l in out.splitlines():
+                f = [x.strip() for x in l.split(",")]
+                if len(f) >= 9:
+                    try:
+                        self.rows.append((float(f[1]), float(f[2]), f[5:9]))
+                    except ValueError:
+                        pass
 
     def summary(self):
-        rows = []
-        for l in self.lines:
-            f = [x.strip() for x in l.split(",")]
-            if len(f) >= 9:
-                try:
-                    rows.append((float(f[1]), float(f[2]), f[5:9]))
-                except ValueError:
-                    pass
+        rows = self.rows
         if not rows:
             return None
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        reasons = sorted({names[i] for _, _, r in rows for i, v in enumerate(r) if v.lower() == "active"})
+        reasons = sorted({self.NAMES[i] for _, _, r in rows for i, v in enumerate(r) if v.lower() == "active"})
         return {"sm_mhz": statistics.median(r[0] for r in rows), "sm_max_mhz": max(r[1] for r in rows),
-                "reasons": reasons, "samples": len(rows)}
+                "reasons": reasons, "samples": len(rows), "source": getattr(self, "source", None)}
 
 
 def wave_rows(n, seed):
@@ -187,6 +217,70 @@ def cpu_baseline_run(model_path, lengths, steps, warmup, seed, rows=False):
                      f"{warmup} warm-up, ei_gemma2_embed_batch_fast_ctx with {ref.threads} threads"}
     ref.close()
     return res
+
+
+def wave_config(args, desc, n, batch, world):
+    """The `config` object of a wave configuration's line, identical in both arms."""
+    return {"workload": desc, "model": "EmbeddingGemma 2 text graph, seeded synthetic GGUF (seed 1234, "
+            "BASELINE weight distributions)", "tokens_per_wave_per_gpu": n, "sequences_per_wave": batch,
+            "parallelism": f"replicas x{world} (whole waves per GPU, no collective)",
+            "l2": "256 MiB write between timed steps; per-wave working set > L2 (151 MB weights, 100 MB PLE)"}
+
+
+# (name, sequence bodies) of the GPU comparison: the reference CUDA bench's
+# headline cases 128x16, 2048x1 and 8192x1 (bench_gemma2_cuda.c:24-25).
+GPU_REF_CASES = (("128x16", (126,) * 16), ("2048x1", (2046,)), ("8192x1", (8190,)))
+
+
+def gpu_baseline_run(eg2, model, model_path, local):
+    """The reference's own CUDA executor for this graph (gemma2_cuda.cu +
+    cuBLAS, compiled from its sources into oracle/_ref/libeg2cudaref.so) beside
+    this executor on the same waves and GGUF, both timed the way the
+    reference's bench_gemma2_cuda.c times its own (:69-78): median wall time of
+    9 synchronous packed-wave calls (host buffers in and out) after 2 warm-up
+    calls.  A reference baseline leg like cpu_baseline: nothing of the
+    reference runs inside `value` or `e2e`."""
+    import oracle
+    syn = eg2.synthetic
+    try:
+        ref = oracle.CudaRef(model_path, local)
+    except (OSError, RuntimeError) as e:
+        return {"unavailable": f"reference CUDA executor not loadable: {e}"}
+
+    def median_ms(fn):
+        for _ in range(2):
+            fn()
+        t = []
+        for _ in range(9):
+            t0 = time.perf_counter()
+            fn()
+            t.append((time.perf_counter() - t0) * 1000.0)
+        return statistics.median(t)
+
+    cases = {}
+    try:
+        for name, bodies in GPU_REF_CASES:
+            ids, off = syn.wave(bodies, seed=300)
+            n = int(off[-1])
+            ex = eg2.Gemma2Executor(model, local, max_tokens=8192 if n > 2048 else 2048)
+            try:
+                ours, theirs = ex.batch(ids, off), ref.embed(ids, off)
+                ms_b200 = median_ms(lambda: ex.batch(ids, off))
+            finally:
+                ex.close()
+            ms_ref = median_ms(lambda: ref.embed(ids, off))
+            a, b = ours.astype(np.float64), theirs.astype(np.float64)
+            cos = float(((a * b).sum(1) / np.sqrt((a * a).sum(1) * (b * b).sum(1))).min())
+            cases[name] = {"tokens": n, "ref_ms": round(ms_ref, 3), "ref_tokens_s": round(n / ms_ref * 1e3),
+                           "b200_ms": round(ms_b200, 3), "b200_tokens_s": round(n / ms_b200 * 1e3),
+                           "b200_speedup": round(ms_ref / ms_b200, 3), "min_cosine_b200_vs_ref": round(cos, 6)}
+    finally:
+        ref.close()
+    return {"kind": "reference", "impl": "vendor/embeddinggemma.c/src/gemma2_cuda.cu (cuBLAS GemmEx fp16, mma.sync "
+            "flash attention, CUDA graphs), compiled from the reference's sources for sm_100",
+            "method": "median wall time of 9 synchronous packed-wave calls after 2 warm-up, host buffers "
+                      "(bench_gemma2_cuda.c:69-78); this executor through ei_gemma2_kfd_batch the same way",
+            "cases": cases}
 
 
 def dist_init(backend="nccl"):
@@ -239,7 +333,7 @@ def reference_arm_mixed(args):
     ref.close()
     line = {"metric": METRIC_MIXED, "value": cpu["value"], "unit": "tokens/s", "n_gpus": args.gpus, "steps": len(waves),
             "warmup": 1, "ms_per_step": sec * 1e3 / len(waves), "higher_is_better": True, "scaling": "strong",
-            "vs_baseline": None, "dtype": "int8+fp32", "data": "synthetic", "config": {"workload": CONFIGS[3][0]},
+            "vs_baseline": None, "dtype": DTYPE_REFERENCE, "data": "synthetic", "config": {"workload": CONFIGS[3][0]},
             "impl": "reference", "cpu_baseline": cpu,
             "e2e": {"value": cpu["value"], "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
@@ -315,13 +409,15 @@ def reference_arm(args, rank, world):
     syn = importlib.import_module("embeddinggemma2-amdkfd_b200.synthetic")
     desc, lengths = CONFIGS[args.config]
     model = syn.model_path(1234, "baseline")
-    cpu = cpu_baseline_run(model, lengths, args.steps, args.warmup, seed=100, rows=args.config in ROWS_CONFIGS)
+    # A bounded sample: a CPU wave of 2048 tokens takes about 0.7 s on 16
+    # threads, so at most 10 waves are timed, after 3 warm-up waves.
+    steps, warmup = min(args.steps, 10), min(args.warmup, 3)
+    cpu = cpu_baseline_run(model, lengths, steps, warmup, seed=100, rows=args.config in ROWS_CONFIGS)
     n = sum(l + 2 for l in lengths)
-    line = {"metric": METRIC, "value": cpu["value"], "unit": "tokens/s", "n_gpus": args.gpus, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": 1000.0 * n / cpu["value"], "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "int8+fp32", "data": "synthetic",
-            "config": {"workload": desc, "model": "EmbeddingGemma 2 text graph, seeded synthetic GGUF (seed 1234, "
-                       "BASELINE weight distributions)", "tokens_per_wave": n},
+    line = {"metric": METRIC, "value": cpu["value"], "unit": "tokens/s", "n_gpus": args.gpus, "steps": steps,
+            "warmup": warmup, "ms_per_step": 1000.0 * n / cpu["value"], "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": DTYPE_REFERENCE, "data": "synthetic",
+            "config": wave_config(args, desc, n, len(lengths), world),
             "impl": "reference", "cpu_baseline": cpu,
             "e2e": {"value": cpu["value"], "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
@@ -411,7 +507,7 @@ def mixed_load_run(args, rank, world, local):
         lat = [x for g in gathered for x in g]
     line = {"metric": METRIC_MIXED, "value": tokens / (ms_max * 1e-3), "unit": "tokens/s", "n_gpus": world,
             "steps": 1, "warmup": 1, "ms_per_step": ms_max, "higher_is_better": True, "scaling": "strong",
-            "vs_baseline": None, "dtype": "int8+fp32", "data": "synthetic",
+            "vs_baseline": None, "dtype": DTYPE_FAST, "data": "synthetic",
             "config": {"workload": CONFIGS[3][0], "requests": len(lens), "texts_per_request": len(lens[0]),
                        "tokens": tokens, "waves_per_rank": len(waves),
                        "arrival": "all requests queued at t = 0 (offline load); one executor per GPU",
@@ -604,11 +700,14 @@ def attention_microbench(args, local):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=300)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--config", type=int, default=1, choices=sorted(CONFIGS))
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-parity-mode", action="store_true", help="skip the parity-mode measurement")
+    ap.add_argument("--no-gpu-baseline", action="store_true",
+                    help="skip timing the reference's own CUDA executor beside this one")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     rank, world, local = dist_init()
@@ -668,14 +767,18 @@ def main():
     dev_ms = sum(step_ms)
     dev_ms_max = reduce_max(dev_ms, world, f"cuda:{local}")
 
-    # ---- e2e: the public C ABI with host buffers every step
+    # ---- e2e: the public C ABI with host buffers every step; each call's
+    # wall time is also the latency of the request(s) the wave carries
     for _ in range(args.warmup):
         run_batch()
     barrier(world)
     torch.cuda.synchronize()
+    call_ms = []
     t0 = time.perf_counter()
     for _ in range(args.steps):
+        c0 = time.perf_counter()
         out = run_batch()
+        call_ms.append((time.perf_counter() - c0) * 1000.0)
     e2e_ms = (time.perf_counter() - t0) * 1000.0
     barrier(world)
     e2e_ms_max = reduce_max(e2e_ms, world, f"cuda:{local}")
@@ -693,14 +796,13 @@ def main():
         "value": whole_job_rate(n, world, args.steps, dev_ms_max),
         "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": dev_ms_max / args.steps, "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "int8+fp32", "data": "synthetic",
-        "config": {"workload": desc, "model": "EmbeddingGemma 2 text graph, seeded synthetic GGUF (seed 1234, "
-                   "BASELINE weight distributions)", "tokens_per_wave_per_gpu": n, "sequences_per_wave": batch,
-                   "parallelism": f"replicas x{world} (whole waves per GPU, no collective)",
-                   "l2": "256 MiB write between timed steps; per-wave working set > L2 (151 MB weights, 100 MB PLE)"},
+        "vs_baseline": None, "dtype": DTYPE_FAST, "data": "synthetic",
+        "config": wave_config(args, desc, n, batch, world),
         "e2e": {"value": whole_job_rate(n, world, args.steps, e2e_ms_max), "unit": "tokens/s",
                 "h2d_bytes_per_step": h2d_bytes,
                 "d2h_bytes_per_step": batch * 768 * 4},
+        "latency_ms": {"p50": float(np.percentile(call_ms, 50)), "p99": float(np.percentile(call_ms, 99)),
+                       "what": f"one ei_gemma2_kfd_batch call of the wave ({batch} texts), host buffers, rank {rank}"},
         "gpu_launches": ex.kernels_per_wave * args.steps,
         "roofline": {"kernel": "q8gemm_kernel (all Q8_0 GEMM launches of a wave)", "bound": "tensor",
                      "achieved": achieved, "peak": int8_peak, "unit": "TOP/s", "frac": achieved / int8_peak,
@@ -711,13 +813,48 @@ def main():
     }
     c = clocks.summary()
     line["clocks"] = c
+    if rank == 0 and world == 1 and args.config in (0, 1, 2) and not args.no_parity_mode:
+        line["parity_mode"] = parity_mode_run(eg2, model, ids, off, args)
+    del ex
+    if rank == 0 and world == 1 and args.config == 1 and not args.no_gpu_baseline:
+        line["gpu_baseline"] = gpu_baseline_run(eg2, model, model_path, local)
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline_run(model_path, lengths, 3, 1, seed=100,
                                                 rows=args.config in ROWS_CONFIGS)
     if rank == 0:
         print(json.dumps(line), flush=True)
-    del ex
     finalize(world)
+
+
+def parity_mode_run(eg2, model, ids, off, args):
+    """The same wave in parity mode with the scalar tier's choices
+    (EG2_B200_EXACT | EG2_B200_SCALAR_TIER), whose embeddings are bit-identical
+    to the reference CPU graph's scalar tier: device-resident waves timed with
+    CUDA events like `value` (a few steps; a wave takes tens of ms)."""
+    import torch
+    px = eg2.Gemma2Executor(model, 0, exact=True, tier="scalar")
+    stream = torch.cuda.ExternalStream(px.stream, device=0)
+    px.stage(ids, off)
+    px.launch(1)
+    px.finish()
+    steps = max(3, min(args.steps, 10))
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    with torch.cuda.stream(stream):
+        e0.record(stream)
+        px.launch(steps)
+        e1.record(stream)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / steps
+    px.finish()
+    n = int(off[-1])
+    res = {"value": n / (ms * 1e-3), "unit": "tokens/s", "ms_per_step": ms, "steps": steps,
+           "kernels_per_wave": px.kernels_per_wave,
+           "dtype": "reference scalar tier's float order: int8 Q8_0 GEMMs with the scalar tile's roundings, "
+                    "fp32 CUDA-core attention and PLE in the CPU loop order",
+           "parity": "bit-identical to the reference CPU graph's scalar tier (tests/test_gpu_executor.py)"}
+    px.close()
+    return res
 
 
 def barrier(world):

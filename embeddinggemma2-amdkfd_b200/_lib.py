@@ -36,6 +36,7 @@ SIGNATURES = {
     "eg2_b200_batch_rows": (b, [vp, vp, vp, sz, vp, cstr, sz]),
     "eg2_b200_stage_rows": (b, [vp, vp, vp, sz, cstr, sz]),
     "eg2_b200_submit_rows": (i32, [vp, vp, vp, sz, cstr, sz]),
+    "eg2_b200_forward_layers": (b, [vp, vp, vp, vp, sz, i32, i32, vp, cstr, sz]),
     "eg2_b200_stream": (vp, [vp]),
     "eg2_b200_kernels_per_wave": (i32, [vp]),
     "eg2_b200_profile": (i32, [vp, vp, vp, i32]),

@@ -378,7 +378,10 @@ struct Backend {
             ck(cudaMallocHost(&sl.out, sizeof(float) * cap * 768), "cudaMallocHost");
         }
         ck(cudaStreamSynchronize(stream), "weight upload");
-        clear_device_error();
+        // The device error word is not cleared here: it is shared by every
+        // context on this device, and a wave of another context may have set it
+        // a moment ago (it would then go unreported).  A set word fails the
+        // next wave of every context on the device, this one included.
         if (std::getenv("EG2_B200_VERBOSE")) {
             size_t free_b = 0, total_b = 0;
             cudaMemGetInfo(&free_b, &total_b);
@@ -409,6 +412,78 @@ struct Backend {
            "q8 GEMM");
     }
 
+    // Both layer kinds run the tensor-core attention through maps whose token
+    // extent is this wave's N (captured into its graph).
+    void attention_maps(int N, AttnTcMaps (&tc_maps)[2]) {
+        if (!exact && (!attention_tc_maps(&tc_maps[0], qh, kh, vh, N, 256) ||
+                       !attention_tc_maps(&tc_maps[1], qh, kh, vh, N, 512)))
+            ck(cudaErrorInvalidValue, "attention maps");
+    }
+
+    // Layer l of the wave (gemma2_fast.c:957-992): its first GEMM reads the Q8
+    // operand of attn_norm(x) already in xq/xs; its last kernel leaves the next
+    // layer's operand (or the output head's) there.  Returns kernels launched.
+    template <class Mark>
+    int enqueue_layer(int l, int N, cudaStream_t s, const AttnTcMaps (&tc_maps)[2], Mark &&mark) {
+        int launches = 0;
+        const Layer &L = layers[l];
+        const int rb = L.d == 512 ? 1 : 0;
+        gemm(L.qkv, qkv, L.qkv.rows, N, s), ++launches;
+        mark("gemm_qkv");
+        if (exact) {
+            ck(launch_qkv_post(qf, kf, vf, qkv, L.q_norm, L.k_norm, rope_cos[rb], rope_sin[rb], pos, N, L.d, s,
+                               true),
+               "qkv_post"),
+                ++launches;
+            mark("qkv_post");
+            ck(launch_attention_exact(attn, qf, kf, vf, bounds, N, L.d, L.d == 512 ? 0 : 512, s), "attention"),
+                ++launches;
+        } else {
+            ck(launch_qkv_post(qh, kh, vh, qkv, L.q_norm, L.k_norm, rope_cos[rb], rope_sin[rb], pos, N, L.d, s,
+                               false),
+               "qkv_post"),
+                ++launches;
+            mark("qkv_post");
+            // The O projection's Q8 operand is written by the attention itself.
+            ck(launch_attention_tc(tc_maps[L.d == 512], nullptr, bounds, N, L.d == 512 ? 0 : 512, s, xq, xs, cap,
+                                   tier),
+               "attention");
+            ++launches;
+        }
+        mark(L.d == 512 ? "attention_global" : "attention_local");
+        if (exact) {
+            ck(launch_norm_quant(xq, xs, cap, nullptr, attn, nullptr, N, 4 * L.d, s, tier), "quant"), ++launches;
+            mark("quant_attn");
+        }
+        gemm(L.o, h, 512, N, s), ++launches;
+        mark("gemm_o");
+        ck(launch_post_add(x, h, L.post_attn_norm, nullptr, xq, xs, cap, L.ffn_norm, N, s, tier), "post_add"), ++launches;
+        mark("post_add");
+        // ffn_gate and ffn_up in one GEMM whose epilogue applies gelu(gate) * up
+        // and quantizes (ROW_GELU_QUANT fused); the result is the down operand.
+        ck(launch_q8gemm_geglu(L.gu.tmap, tm_xq[0], L.gu.tscale, tm_xs[0], exact, gq, gs, cap, N, L.gu.rows, L.gu.k,
+                               s, tier),
+           "GeGLU GEMM"),
+            ++launches;
+        mark("gemm_geglu");
+        ck(launch_q8gemm(L.down.tmap, tm_gq, L.down.tscale, tm_gs, exact, h, 512, N, L.down.rows, L.down.k, s),
+           "q8 GEMM"),
+            ++launches;
+        mark("gemm_down");
+        ck(launch_post_add(x, h, L.post_ffw_norm, nullptr, xq, xs, cap, nullptr, N, s, tier), "post_add"), ++launches;
+        mark("post_add");
+        gemm(L.inp_gate, h, 512, N, s), ++launches;
+        mark("gemm_inp_gate");
+        ck(launch_gate_quant(xq, xs, cap, h, ple, N, 512, 24 * 512, l * 512, s, tier), "ple gate"), ++launches;
+        mark("ple_gate_quant");
+        gemm(L.proj, h, 512, N, s), ++launches;
+        mark("gemm_proj");
+        const float *next = l + 1 < 24 ? layers[l + 1].attn_norm : output_norm;
+        ck(launch_post_add(x, h, L.post_norm, L.out_scale, xq, xs, cap, next, N, s, tier), "post_add"), ++launches;
+        mark("post_add");
+        return launches;
+    }
+
     // The whole wave as a launch sequence (captured into a graph, or run eagerly
     // under the profiler).  Returns the number of kernels launched.
     // rows: a soft-token wave, whose x was uploaded with the inputs.
@@ -418,12 +493,8 @@ struct Backend {
             if (prof) prof->mark(name);
         };
         const int N = int(n);
-        // Both layer kinds run the tensor-core attention through maps whose
-        // token extent is this wave's N (captured into its graph).
         AttnTcMaps tc_maps[2]{};
-        if (!exact && (!attention_tc_maps(&tc_maps[0], qh, kh, vh, N, 256) ||
-                       !attention_tc_maps(&tc_maps[1], qh, kh, vh, N, 512)))
-            ck(cudaErrorInvalidValue, "attention maps");
+        attention_maps(N, tc_maps);
         mark("start");
         if (rows)
             ck(launch_input_rows(x, x_hi, x_lo, xin, N, s), "input rows"), ++launches;
@@ -437,63 +508,7 @@ struct Backend {
         mark("ple_proj");
         ck(launch_norm_quant(xq, xs, cap, nullptr, x, layers[0].attn_norm, N, 512, s, tier), "norm"), ++launches;
         mark("norm_quant");
-        for (int l = 0; l < 24; ++l) {
-            const Layer &L = layers[l];
-            const int rb = L.d == 512 ? 1 : 0;
-            gemm(L.qkv, qkv, L.qkv.rows, N, s), ++launches;
-            mark("gemm_qkv");
-            if (exact) {
-                ck(launch_qkv_post(qf, kf, vf, qkv, L.q_norm, L.k_norm, rope_cos[rb], rope_sin[rb], pos, N, L.d, s,
-                                   true),
-                   "qkv_post"),
-                    ++launches;
-                mark("qkv_post");
-                ck(launch_attention_exact(attn, qf, kf, vf, bounds, N, L.d, L.d == 512 ? 0 : 512, s), "attention"),
-                    ++launches;
-            } else {
-                ck(launch_qkv_post(qh, kh, vh, qkv, L.q_norm, L.k_norm, rope_cos[rb], rope_sin[rb], pos, N, L.d, s,
-                                   false),
-                   "qkv_post"),
-                    ++launches;
-                mark("qkv_post");
-                // The O projection's Q8 operand is written by the attention itself.
-                ck(launch_attention_tc(tc_maps[L.d == 512], nullptr, bounds, N, L.d == 512 ? 0 : 512, s, xq, xs, cap,
-                                       tier),
-                   "attention");
-                ++launches;
-            }
-            mark(L.d == 512 ? "attention_global" : "attention_local");
-            if (exact) {
-                ck(launch_norm_quant(xq, xs, cap, nullptr, attn, nullptr, N, 4 * L.d, s, tier), "quant"), ++launches;
-                mark("quant_attn");
-            }
-            gemm(L.o, h, 512, N, s), ++launches;
-            mark("gemm_o");
-            ck(launch_post_add(x, h, L.post_attn_norm, nullptr, xq, xs, cap, L.ffn_norm, N, s, tier), "post_add"), ++launches;
-            mark("post_add");
-            // ffn_gate and ffn_up in one GEMM whose epilogue applies gelu(gate) * up
-            // and quantizes (ROW_GELU_QUANT fused); the result is the down operand.
-            ck(launch_q8gemm_geglu(L.gu.tmap, tm_xq[0], L.gu.tscale, tm_xs[0], exact, gq, gs, cap, N, L.gu.rows,
-                                   L.gu.k, s, tier),
-               "GeGLU GEMM"),
-                ++launches;
-            mark("gemm_geglu");
-            ck(launch_q8gemm(L.down.tmap, tm_gq, L.down.tscale, tm_gs, exact, h, 512, N, L.down.rows, L.down.k, s),
-               "q8 GEMM"),
-                ++launches;
-            mark("gemm_down");
-            ck(launch_post_add(x, h, L.post_ffw_norm, nullptr, xq, xs, cap, nullptr, N, s, tier), "post_add"), ++launches;
-            mark("post_add");
-            gemm(L.inp_gate, h, 512, N, s), ++launches;
-            mark("gemm_inp_gate");
-            ck(launch_gate_quant(xq, xs, cap, h, ple, N, 512, 24 * 512, l * 512, s, tier), "ple gate"), ++launches;
-            mark("ple_gate_quant");
-            gemm(L.proj, h, 512, N, s), ++launches;
-            mark("gemm_proj");
-            const float *next = l + 1 < 24 ? layers[l + 1].attn_norm : output_norm;
-            ck(launch_post_add(x, h, L.post_norm, L.out_scale, xq, xs, cap, next, N, s, tier), "post_add"), ++launches;
-            mark("post_add");
-        }
+        for (int l = 0; l < 24; ++l) launches += enqueue_layer(l, N, s, tc_maps, mark);
         gemm(output, y, 768, N, s), ++launches;
         mark("gemm_output");
         // The grid covers every sequence a wave of n tokens can hold; the
@@ -507,7 +522,9 @@ struct Backend {
         const uint64_t key = n | uint64_t(rows) << 32;
         auto it = graphs.find(key);
         if (it != graphs.end()) return it->second;
-        if (graphs.size() >= 256) {  // bound the cache
+        // Keys are (bucketed token count, ids or rows): at most 2 * cap / BUCKET
+        // = 256 for the widest context, so this flush only guards the bound.
+        if (graphs.size() >= 256) {
             ck(cudaStreamSynchronize(stream), "graph cache flush");
             for (auto &kv : graphs) cudaGraphExecDestroy(kv.second);
             graphs.clear();
@@ -576,9 +593,12 @@ struct Backend {
         if (poisoned) throw std::runtime_error("KFD context failed; restart process before reuse");
         for (const Slot &sl : slots)
             if (sl.busy) throw std::runtime_error("a submitted wave is not collected yet");
+        // Nothing stays staged if the fill or the capture below fails.
+        staged_graph = nullptr;
         const unsigned n_pad = fill(slots[0], in_ids, in_off, batch, in_rows);
-        staged_graph = graph_for(n_pad, in_rows != nullptr);
+        cudaGraphExec_t g = graph_for(n_pad, in_rows != nullptr);
         staged_n = n_pad, staged_batch = batch, staged_rows = in_rows != nullptr;
+        staged_graph = g;
     }
 
     void launch(int repeats) {
@@ -594,22 +614,31 @@ struct Backend {
         ck(cudaEventRecord(sl.done, stream), "event record");
     }
 
-    // Wait for a slot with the reference's deadline; any failure poisons the context.
+    // Wait for a slot with the reference's deadline.  Any failure poisons the
+    // context for good (gemma2_kfd.cpp:190-214): a later wait that succeeds,
+    // e.g. the other pipeline slot's, never clears it.
     void wait_slot(Slot &sl) {
-        poisoned = true;
-        // Poll without sleeping for the length of a few waves, then back off.
-        const auto t0 = std::chrono::steady_clock::now();
-        for (;;) {
-            const cudaError_t q = cudaEventQuery(sl.done);
-            if (q == cudaSuccess) break;
-            if (q != cudaErrorNotReady) ck(q, "GPU wave");
-            const double waited = std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
-            if (waited > TIMEOUT_S) throw std::runtime_error("GPU wave timed out");
-            if (waited > 0.02) std::this_thread::sleep_for(std::chrono::microseconds(50));
+        try {
+            // Poll without sleeping for the length of a few waves, then back off.
+            const auto t0 = std::chrono::steady_clock::now();
+            for (;;) {
+                const cudaError_t q = cudaEventQuery(sl.done);
+                if (q == cudaSuccess) break;
+                if (q != cudaErrorNotReady) ck(q, "GPU wave");
+                const double waited = std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
+                if (waited > TIMEOUT_S) throw std::runtime_error("GPU wave timed out");
+                if (waited > 0.02) std::this_thread::sleep_for(std::chrono::microseconds(50));
+            }
+            const int derr = *sl.err;
+            if (derr)
+                throw std::runtime_error("device wait timed out inside a kernel (error " + std::to_string(derr) + ")");
+        } catch (...) {
+            poisoned = true;
+            throw;
         }
-        const int derr = *sl.err;
-        if (derr) throw std::runtime_error("device wait timed out inside a kernel (error " + std::to_string(derr) + ")");
-        poisoned = false;
+    }
+    void refuse_if_poisoned() const {
+        if (poisoned) throw std::runtime_error("KFD context failed; restart process before reuse");
     }
 
     // gemma2_kfd.cpp:337-343: finite, non-zero; the embedding is already
@@ -655,6 +684,7 @@ struct Backend {
         if (id < 0 || id >= SLOTS || !slots[id].busy) throw std::runtime_error("no wave submitted to this slot");
         Slot &sl = slots[id];
         sl.busy = false;
+        refuse_if_poisoned();
         wait_slot(sl);
         deliver(sl, sl.batch, out);
     }
@@ -664,7 +694,46 @@ struct Backend {
         collect(submit(in_ids, in_off, n_seq, in_rows), out);
     }
 
+    // Layers [l0, l1) of the fast path (or of parity mode) from a caller-given
+    // residual stream x_in [n][512] and per-layer embeddings ple_in
+    // [n][24][512] (NULL: projected on the device from x_in, which is then the
+    // wave's embedding rows), eager launches on the context stream; x_out gets
+    // the residual stream after layer l1 - 1.  For teacher-forced per-layer
+    // checks against the reference CPU graph.
+    void forward_layers(const float *x_in, const float *ple_in, const size_t *in_off, size_t batch, int l0, int l1,
+                        float *x_out) {
+        refuse_if_poisoned();
+        for (const Slot &sl : slots)
+            if (sl.busy) throw std::runtime_error("a submitted wave is not collected yet");
+        if (l0 < 0 || l1 > 24 || l0 > l1 || !x_out) throw std::runtime_error("invalid layer range");
+        staged_graph = nullptr;  // the staged wave's device inputs are overwritten below
+        Slot &sl = slots[0];
+        const unsigned n_pad = fill(sl, nullptr, in_off, batch, x_in);
+        const int N = int(n_pad);
+        const size_t n = in_off[batch];
+        cudaStream_t s = stream;
+        ck(launch_input_rows(x, x_hi, x_lo, xin, N, s), "input rows");
+        if (ple_in) {
+            ck(cudaMemcpyAsync(ple, ple_in, n * 24 * 512 * sizeof(float), cudaMemcpyHostToDevice, s), "PLE upload");
+            ck(cudaStreamSynchronize(s), "PLE upload");  // ple_in is pageable caller memory
+        } else if (exact) {
+            ck(launch_ple_exact(ple, x, ple_w, ple_norm, N, s), "PLE");
+        } else {
+            ck(launch_ple(tm_hi, tm_lo, tm_ple, ple, ple_norm, N, s), "PLE");
+        }
+        AttnTcMaps tc_maps[2]{};
+        attention_maps(N, tc_maps);
+        if (l0 < 24)
+            ck(launch_norm_quant(xq, xs, cap, nullptr, x, layers[l0].attn_norm, N, 512, s, tier), "norm");
+        auto none = [](const char *) {};
+        for (int l = l0; l < l1; ++l) enqueue_layer(l, N, s, tc_maps, none);
+        enqueue_readback(sl, 0);
+        wait_slot(sl);
+        ck(cudaMemcpy(x_out, x, n * 512 * sizeof(float), cudaMemcpyDeviceToHost), "residual readback");
+    }
+
     int profile(char names[][32], double *ms, int max) {
+        refuse_if_poisoned();
         if (!staged_graph) throw std::runtime_error("no wave staged");
         std::map<std::string, double> acc;
         std::vector<std::string> order;
@@ -806,6 +875,16 @@ extern "C" int eg2_b200_submit_rows(void *ctx, const float *rows, const size_t *
         slot = b->submit(nullptr, offsets, batch, rows);
     });
     return slot;
+}
+extern "C" bool eg2_b200_forward_layers(void *ctx, const float *x_in, const float *ple_in, const size_t *offsets,
+                                        size_t batch, int first_layer, int last_layer, float *x_out, char *err,
+                                        size_t len) {
+    return guarded(err, len, [&] {
+        Backend *b = as_backend(ctx);
+        std::lock_guard<std::mutex> guard(b->mutex);
+        if (!x_in) throw std::runtime_error(count_message(b->cap));
+        b->forward_layers(x_in, ple_in, offsets, batch, first_layer, last_layer, x_out);
+    });
 }
 extern "C" void *eg2_b200_stream(void *ctx) { return ctx ? static_cast<Backend *>(ctx)->stream : nullptr; }
 extern "C" int eg2_b200_kernels_per_wave(void *ctx) { return ctx ? static_cast<Backend *>(ctx)->kernels_per_wave : 0; }

@@ -15,6 +15,12 @@
  * are always <= 0: scores minus their maximum).
  *
  * The table holds bits(2^(i/32) rounded to double) - (i << 47).
+ *
+ * Licence of the restated algorithm and its table: ARM optimized-routines,
+ * Copyright (c) 2017-2018, Arm Limited, distributed under the MIT licence
+ * (SPDX-License-Identifier: MIT OR Apache-2.0 WITH LLVM-exception), which
+ * permits use, copying, modification and distribution provided this notice is
+ * kept; the code here is this project's own restatement.
  */
 #ifndef EG2_REF_EXPF_H
 #define EG2_REF_EXPF_H

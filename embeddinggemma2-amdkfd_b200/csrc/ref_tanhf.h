@@ -12,6 +12,13 @@
  * evaluate these exact steps.  The library's build has no fused multiply-add
  * here; the EG2_F* macros give IEEE operations that are never contracted, on
  * the host and on the device.  Checked against glibc on every finite float.
+ *
+ * Notice of the restated algorithms (fdlibm, as carried by glibc):
+ * Copyright (C) 1993 by Sun Microsystems, Inc. All rights reserved.
+ * Developed at SunPro, a Sun Microsystems, Inc. business.  Permission to use,
+ * copy, modify, and distribute this software is freely granted, provided that
+ * this notice is preserved.  (The float versions were converted by Ian Lance
+ * Taylor, Cygnus Support.)  The code here is this project's own restatement.
  */
 #ifndef EG2_REF_TANHF_H
 #define EG2_REF_TANHF_H

@@ -214,6 +214,26 @@ class Gemma2Executor:
             raise ExecutorError(err.value.decode())
         return out[:self._staged_batch]
 
+    def forward_layers(self, x, ple, offsets, first: int, last: int) -> np.ndarray:
+        """Layers [first, last) on a given residual stream x [n][512] with the
+        wave's per-layer embeddings ple [n][24][512] (None: projected from x,
+        the embedding rows); returns the residual stream after layer last - 1
+        (eg2_b200_forward_layers)."""
+        x, offsets, batch = _rows(x, offsets)
+        n = x.shape[0]
+        if ple is not None:
+            ple = np.ascontiguousarray(ple, dtype=np.float32)
+            if ple.size != n * 24 * 512:
+                raise ExecutorError("per-layer embeddings must be [n][24][512]")
+        out = np.zeros((max(n, 1), 512), np.float32)
+        err = _err()
+        if not self.lib.eg2_b200_forward_layers(self.ctx, x.ctypes.data if x.size else None,
+                                                ple.ctypes.data if ple is not None else None,
+                                                offsets.ctypes.data if offsets.size else None, max(batch, 0),
+                                                int(first), int(last), out.ctypes.data, err, len(err)):
+            raise ExecutorError(err.value.decode())
+        return out[:n]
+
     @property
     def stream(self) -> int:
         return int(self.lib.eg2_b200_stream(self.ctx) or 0)

@@ -13,6 +13,9 @@
  *     reference does (the engine turns that into HTTP 400);
  *   - after a device failure or timeout the context is poisoned and every later
  *     call fails with "... restart process before reuse";
+ *   - a kernel's bounded wait that runs out (about 2 s) sets an error word
+ *     that is per DEVICE, shared by every context on it: it fails the next
+ *     wave of each of them, and creating a context does not clear it;
  *   - one internal mutex serialises calls on a context.
  */
 #ifndef EG2_EXECUTOR_H
@@ -97,6 +100,18 @@ bool eg2_b200_stage_rows(void *ctx, const float *rows, const size_t *offsets, si
                          size_t len);
 int eg2_b200_submit_rows(void *ctx, const float *rows, const size_t *offsets, size_t batch, char *err,
                          size_t len);
+/* Teacher-forced layer range: layers [first_layer, last_layer) of the
+ * context's graph (0 <= first <= last <= 24) run on a caller-given residual
+ * stream x_in [offsets[batch]][512] fp32 and per-layer embeddings ple_in
+ * [offsets[batch]][24][512] fp32 (NULL: projected on the device from x_in,
+ * which must then be the wave's embedding rows), with the wave's sequence
+ * bounds and positions from offsets (checked as for ids).  x_out receives the
+ * residual stream after layer last_layer - 1.  The reference CPU graph's
+ * layer loop (gemma2_fast.c:957-992) has no entry point of its own; this one
+ * lets each layer be checked against it from identical inputs.  Synchronous;
+ * host memory; replaces the staged wave, if any. */
+bool eg2_b200_forward_layers(void *ctx, const float *x_in, const float *ple_in, const size_t *offsets, size_t batch,
+                             int first_layer, int last_layer, float *x_out, char *err, size_t len);
 /* The cudaStream_t the context launches on (for CUDA-event timing). */
 void *eg2_b200_stream(void *ctx);
 /* Kernels launched per wave by the staged graph. */

@@ -10,8 +10,46 @@
 #include "eg2_oracle.h"
 
 #include <math.h>
+#include <pthread.h>
 #include <stdlib.h>
 #include <string.h>
+#include <unistd.h>
+
+/* Runs fn(ctx, lo, hi) over [0, n) split into contiguous ranges, one per host
+ * thread (at most 64).  Only independent iterations (tokens, weight rows) are
+ * split, so every result is computed in the same order as a serial loop and
+ * does not depend on the thread count. */
+typedef void (*range_fn)(void *ctx, int lo, int hi);
+typedef struct {
+    range_fn fn;
+    void *ctx;
+    int lo, hi;
+} range_job;
+static void *range_main(void *p) {
+    range_job *j = p;
+    j->fn(j->ctx, j->lo, j->hi);
+    return NULL;
+}
+static void par_for(int n, range_fn fn, void *ctx) {
+    long cpus = sysconf(_SC_NPROCESSORS_ONLN);
+    int T = cpus < 1 ? 1 : cpus > 64 ? 64 : (int)cpus;
+    if (T > n) T = n;
+    if (T <= 1) {
+        if (n > 0) fn(ctx, 0, n);
+        return;
+    }
+    pthread_t th[64];
+    range_job jobs[64];
+    for (int i = 0; i < T; i++) {
+        jobs[i] = (range_job){fn, ctx, (int)((long)n * i / T), (int)((long)n * (i + 1) / T)};
+        if (i && pthread_create(&th[i], NULL, range_main, &jobs[i])) jobs[i].fn = NULL;
+    }
+    fn(ctx, jobs[0].lo, jobs[0].hi);
+    for (int i = 1; i < T; i++) {
+        if (jobs[i].fn) pthread_join(th[i], NULL);
+        else fn(ctx, jobs[i].lo, jobs[i].hi);  /* thread creation failed: run it here */
+    }
+}
 
 /* quants.c:13-37 -- fp32 -> fp16, ties resolved upward on bit 12 (not RNE). */
 uint16_t eg2o_fp32_to_fp16(float f) {
@@ -125,48 +163,93 @@ void eg2o_gelu_mul(float *g, const float *u, int n, int mode) {
     }
 }
 
-/* gemma2_fast.c:193-204 -- scalar Q8_0 x Q8_0 tile, blocks in ascending order. */
-void eg2o_gemm_q8(const int8_t *wq, const uint16_t *wd, const int8_t *xq, const uint16_t *xd,
-                  int n, int k, int m, float *y) {
-    int kb = k / 32;
-    for (int t = 0; t < n; t++)
-        for (int r = 0; r < m; r++) {
-            float sum = 0;
-            for (int p = 0; p < kb; p++) {
-                const int8_t *a = wq + ((size_t)r * kb + p) * 32, *b = xq + ((size_t)t * kb + p) * 32;
-                int dot = 0;
-                for (int z = 0; z < 32; z++) dot += a[z] * b[z];
-                sum += (float)dot * eg2o_fp16_to_fp32(wd[(size_t)r * kb + p]) *
-                       eg2o_fp16_to_fp32(xd[(size_t)t * kb + p]);
-            }
-            y[(size_t)t * m + r] = sum;
-        }
+/* Perturbations for the tests that measure how far an implementation in
+ * another float order can land from this one (never set otherwise): the GEMM
+ * sums its blocks in descending order, and/or q, k, v are rounded to fp16
+ * before the attention. */
+static int variant_gemm_descending, variant_attention_fp16;
+void eg2o_set_variant(int gemm_descending, int attention_fp16) {
+    variant_gemm_descending = gemm_descending;
+    variant_attention_fp16 = attention_fp16;
 }
 
-void eg2o_gemm_q8_blockdots(const int8_t *wq, const int8_t *xq, int n, int k, int m, int32_t *D) {
-    int kb = k / 32;
-    for (int t = 0; t < n; t++)
-        for (int r = 0; r < m; r++)
-            for (int p = 0; p < kb; p++) {
-                const int8_t *a = wq + ((size_t)r * kb + p) * 32, *b = xq + ((size_t)t * kb + p) * 32;
+/* gemma2_fast.c:193-204 -- scalar Q8_0 x Q8_0 tile, blocks in ascending order. */
+typedef struct {
+    const int8_t *wq, *xq;
+    const float *wd, *xd;  /* the fp16 scales, widened exactly */
+    int k, m;
+    float *y;
+    int32_t *D;
+} gemm_q8_job;
+static void gemm_q8_rows(void *c, int t0, int t1) {
+    const gemm_q8_job *j = c;
+    int kb = j->k / 32;
+    for (int t = t0; t < t1; t++)
+        for (int r = 0; r < j->m; r++) {
+            float sum = 0;
+            for (int i = 0; i < kb; i++) {
+                const int p = variant_gemm_descending ? kb - 1 - i : i;
+                const int8_t *a = j->wq + ((size_t)r * kb + p) * 32, *b = j->xq + ((size_t)t * kb + p) * 32;
                 int dot = 0;
                 for (int z = 0; z < 32; z++) dot += a[z] * b[z];
-                D[((size_t)t * m + r) * kb + p] = dot;
+                sum += (float)dot * j->wd[(size_t)r * kb + p] * j->xd[(size_t)t * kb + p];
             }
+            j->y[(size_t)t * j->m + r] = sum;
+        }
+}
+static float *widen_fp16(const uint16_t *h, size_t count) {
+    float *f = malloc(count * sizeof(float));
+    for (size_t i = 0; i < count; i++) f[i] = eg2o_fp16_to_fp32(h[i]);
+    return f;
+}
+void eg2o_gemm_q8(const int8_t *wq, const uint16_t *wd, const int8_t *xq, const uint16_t *xd,
+                  int n, int k, int m, float *y) {
+    float *wf = widen_fp16(wd, (size_t)m * (k / 32)), *xf = widen_fp16(xd, (size_t)n * (k / 32));
+    gemm_q8_job j = {wq, xq, wf, xf, k, m, y, NULL};
+    par_for(n, gemm_q8_rows, &j);
+    free(wf), free(xf);
+}
+
+static void blockdot_rows(void *c, int t0, int t1) {
+    const gemm_q8_job *j = c;
+    int kb = j->k / 32;
+    for (int t = t0; t < t1; t++)
+        for (int r = 0; r < j->m; r++)
+            for (int p = 0; p < kb; p++) {
+                const int8_t *a = j->wq + ((size_t)r * kb + p) * 32, *b = j->xq + ((size_t)t * kb + p) * 32;
+                int dot = 0;
+                for (int z = 0; z < 32; z++) dot += a[z] * b[z];
+                j->D[((size_t)t * j->m + r) * kb + p] = dot;
+            }
+}
+void eg2o_gemm_q8_blockdots(const int8_t *wq, const int8_t *xq, int n, int k, int m, int32_t *D) {
+    gemm_q8_job j = {wq, xq, NULL, NULL, k, m, NULL, D};
+    par_for(n, blockdot_rows, &j);
 }
 
 /* gemma2_fast.c:482-559 scalar branch -- float GEMM for the BF16 PLE projection. */
-void eg2o_gemm_bf16(const uint16_t *w, const float *x, int n, int k, int m, float *y) {
-    float *row = malloc((size_t)k * sizeof(float));
-    for (int r = 0; r < m; r++) {
-        for (int z = 0; z < k; z++) row[z] = bf16_to_fp32(w[(size_t)r * k + z]);
-        for (int t = 0; t < n; t++) {
+typedef struct {
+    const uint16_t *w;
+    const float *x;
+    int n, k, m;
+    float *y;
+} gemm_bf16_job;
+static void gemm_bf16_rows(void *c, int r0, int r1) {
+    const gemm_bf16_job *j = c;
+    float *row = malloc((size_t)j->k * sizeof(float));
+    for (int r = r0; r < r1; r++) {
+        for (int z = 0; z < j->k; z++) row[z] = bf16_to_fp32(j->w[(size_t)r * j->k + z]);
+        for (int t = 0; t < j->n; t++) {
             float sum = 0;
-            for (int z = 0; z < k; z++) sum += row[z] * x[(size_t)t * k + z];
-            y[(size_t)t * m + r] = sum;
+            for (int z = 0; z < j->k; z++) sum += row[z] * j->x[(size_t)t * j->k + z];
+            j->y[(size_t)t * j->m + r] = sum;
         }
     }
     free(row);
+}
+void eg2o_gemm_bf16(const uint16_t *w, const float *x, int n, int k, int m, float *y) {
+    gemm_bf16_job j = {w, x, n, k, m, y};
+    par_for(m, gemm_bf16_rows, &j);
 }
 
 /* gemma2_fast.c:587-590 (scalar sum_squares) and :667-671 (rms_row). */
@@ -212,20 +295,27 @@ static void rope_row(float *r, int d, int pos) {
 
 /* gemma2_fast.c:768-894 scalar branch.  Masked keys add exact zeros there, so
  * summing only the keys inside [lo, hi) in ascending order is identical. */
-void eg2o_attention(const float *q, const float *k, const float *v, const uint32_t *lo_,
-                    const uint32_t *hi_, int n, int kv, int d, int window, float *a) {
-    float *sc = malloc((size_t)n * sizeof(float));
-    for (int t = 0; t < n; t++)
+typedef struct {
+    const float *q, *k, *v;
+    const uint32_t *lo, *hi;
+    int n, kv, d, window;
+    float *a;
+} attn_job;
+static void attention_rows(void *c, int t0, int t1) {
+    const attn_job *j = c;
+    const int kv = j->kv, d = j->d, window = j->window;
+    float *sc = malloc((size_t)j->n * sizeof(float));
+    for (int t = t0; t < t1; t++)
         for (int hd = 0; hd < 4; hd++) {
-            int kh = hd / (4 / kv), lo = (int)lo_[t], hi = (int)hi_[t];
+            int kh = hd / (4 / kv), lo = (int)j->lo[t], hi = (int)j->hi[t];
             if (window) {
                 if (t - window > lo) lo = t - window;
                 if (t + window + 1 < hi) hi = t + window + 1;
             }
-            const float *qr = q + ((size_t)t * 4 + hd) * d;
+            const float *qr = j->q + ((size_t)t * 4 + hd) * d;
             float mx = -INFINITY, total = 0;
             for (int s = lo; s < hi; s++) {
-                const float *kr = k + ((size_t)s * kv + kh) * d;
+                const float *kr = j->k + ((size_t)s * kv + kh) * d;
                 float dot = 0;
                 for (int z = 0; z < d; z++) dot += qr[z] * kr[z];
                 sc[s] = dot;
@@ -236,14 +326,19 @@ void eg2o_attention(const float *q, const float *k, const float *v, const uint32
                 total += sc[s];
             }
             for (int s = lo; s < hi; s++) sc[s] /= total;
-            float *o = a + ((size_t)t * 4 + hd) * d;
+            float *o = j->a + ((size_t)t * 4 + hd) * d;
             for (int z = 0; z < d; z++) {
                 float acc = 0;
-                for (int s = lo; s < hi; s++) acc += sc[s] * v[((size_t)s * kv + kh) * d + z];
+                for (int s = lo; s < hi; s++) acc += sc[s] * j->v[((size_t)s * kv + kh) * d + z];
                 o[z] = acc;
             }
         }
     free(sc);
+}
+void eg2o_attention(const float *q, const float *k, const float *v, const uint32_t *lo_,
+                    const uint32_t *hi_, int n, int kv, int d, int window, float *a) {
+    attn_job j = {q, k, v, lo_, hi_, n, kv, d, window, a};
+    par_for(n, attention_rows, &j);
 }
 
 /* AoS GGUF Q8_0 [rows][k] -> int8 plane + fp16 scale plane. */
@@ -296,37 +391,154 @@ static void l2_normalize_sse2(float *x, int n) {
 #define T(i) (tensors[(i)])
 #define LT(l, j) (tensors[3 + 17 * (l) + (j)])
 
+/* Per-wave work buffers for up to `count` tokens. */
+typedef struct {
+    float *h, *q, *k, *v, *a, *up, *gate;
+    int8_t *xq;
+    uint16_t *xd;
+    uint32_t *lo, *hi, *pos;
+} wave_ws;
+
+static wave_ws ws_alloc(const size_t *offsets, size_t batch) {
+    size_t count = offsets[batch];
+    wave_ws w = {malloc(count * 512 * 4), malloc(count * 2048 * 4), malloc(count * 512 * 4), malloc(count * 512 * 4),
+                 malloc(count * 2048 * 4), malloc(count * 2048 * 4), malloc(count * 2048 * 4),
+                 malloc(count * 2048), malloc(count * 64 * 2),
+                 malloc(count * 4), malloc(count * 4), malloc(count * 4)};
+    for (size_t s = 0; s < batch; s++)
+        for (size_t t = offsets[s]; t < offsets[s + 1]; t++)
+            w.lo[t] = (uint32_t)offsets[s], w.hi[t] = (uint32_t)offsets[s + 1], w.pos[t] = (uint32_t)(t - offsets[s]);
+    return w;
+}
+static void ws_free(wave_ws *w) {
+    free(w->h), free(w->q), free(w->k), free(w->v), free(w->a), free(w->up), free(w->gate);
+    free(w->xq), free(w->xd), free(w->lo), free(w->hi), free(w->pos);
+}
+
+/* gemma2_fast.c:951-956 -- ple = rms(x . W_ple^T / sqrt(512)) per 512-slice. */
+static void ple_project(const void *const *tensors, const float *x, int n, float *ple) {
+    size_t count = (size_t)n;
+    eg2o_gemm_bf16(T(1), x, n, 512, 24 * 512, ple);
+    for (size_t i = 0; i < count * 512 * 24; i++) ple[i] /= sqrtf(512.0f);
+    for (size_t r = 0; r < count * 24; r++) eg2o_rms_row(ple + r * 512, 512, T(2));
+}
+
+/* One layer of the loop at gemma2_fast.c:957-992, x updated in place. */
+static void layer_forward(const void *const *tensors, int l, float *x, const float *ple, int n, int qm, int gm,
+                          wave_ws *w) {
+    int d = l % 6 == 5 ? 512 : 256, kv = 512 / d;
+    float *h = w->h, *q = w->q, *k = w->k, *v = w->v, *a = w->a, *up = w->up, *gate = w->gate;
+    int8_t *xq = w->xq;
+    uint16_t *xd = w->xd;
+    /* ROW_NORM_QUANT (gemma2_fast.c:685-691). */
+    for (int t = 0; t < n; t++) {
+        memcpy(h + (size_t)t * 512, x + (size_t)t * 512, 2048);
+        eg2o_rms_row(h + (size_t)t * 512, 512, LT(l, 0));
+    }
+    eg2o_quantize(h, xq, xd, n * 512, qm);
+    gemm_w(LT(l, 1), 512, 4 * d, xq, xd, n, q);
+    gemm_w(LT(l, 2), 512, 512, xq, xd, n, k);
+    gemm_w(LT(l, 3), 512, 512, xq, xd, n, v);
+    /* ROW_QKV_POST (gemma2_fast.c:692-706). */
+    for (int t = 0; t < n; t++) {
+        for (int hd = 0; hd < 4; hd++) {
+            float *r = q + ((size_t)t * 4 + hd) * d;
+            eg2o_rms_row(r, d, LT(l, 5));
+            rope_row(r, d, (int)w->pos[t]);
+        }
+        for (int hd = 0; hd < kv; hd++) {
+            float *r = k + ((size_t)t * kv + hd) * d;
+            eg2o_rms_row(r, d, LT(l, 6));
+            rope_row(r, d, (int)w->pos[t]);
+            eg2o_rms_row(v + ((size_t)t * kv + hd) * d, d, NULL);
+        }
+    }
+    if (variant_attention_fp16) {
+        for (size_t i = 0; i < (size_t)n * 4 * d; i++) q[i] = (float)(_Float16)q[i];
+        for (size_t i = 0; i < (size_t)n * kv * d; i++) k[i] = (float)(_Float16)k[i], v[i] = (float)(_Float16)v[i];
+    }
+    eg2o_attention(q, k, v, w->lo, w->hi, n, kv, d, l % 6 == 5 ? 0 : 512, a);
+    /* ROW_QUANT(a) -> attn_output -> ROW_POST_ADD (gemma2_fast.c:972-975). */
+    eg2o_quantize(a, xq, xd, n * 4 * d, qm);
+    gemm_w(LT(l, 4), 4 * d, 512, xq, xd, n, h);
+    for (int t = 0; t < n; t++) {
+        float *hh = h + (size_t)t * 512, *xx = x + (size_t)t * 512;
+        eg2o_rms_row(hh, 512, LT(l, 7));
+        for (int z = 0; z < 512; z++) xx[z] = (xx[z] + hh[z]) * 1.0f;
+    }
+    /* FFN (gemma2_fast.c:976-983). */
+    for (int t = 0; t < n; t++) {
+        memcpy(h + (size_t)t * 512, x + (size_t)t * 512, 2048);
+        eg2o_rms_row(h + (size_t)t * 512, 512, LT(l, 8));
+    }
+    eg2o_quantize(h, xq, xd, n * 512, qm);
+    gemm_w(LT(l, 9), 512, 2048, xq, xd, n, up);
+    gemm_w(LT(l, 10), 512, 2048, xq, xd, n, gate);
+    eg2o_gelu_mul(gate, up, n * 2048, gm);
+    eg2o_quantize(gate, xq, xd, n * 2048, qm);
+    gemm_w(LT(l, 11), 2048, 512, xq, xd, n, h);
+    for (int t = 0; t < n; t++) {
+        float *hh = h + (size_t)t * 512, *xx = x + (size_t)t * 512;
+        eg2o_rms_row(hh, 512, LT(l, 12));
+        for (int z = 0; z < 512; z++) xx[z] = (xx[z] + hh[z]) * 1.0f;
+    }
+    /* Per-layer embedding gate (gemma2_fast.c:984-990). */
+    eg2o_quantize(x, xq, xd, n * 512, qm);
+    gemm_w(LT(l, 13), 512, 512, xq, xd, n, h);
+    for (int t = 0; t < n; t++)
+        eg2o_gelu_mul(h + (size_t)t * 512, ple + ((size_t)t * 24 + l) * 512, 512, gm);
+    eg2o_quantize(h, xq, xd, n * 512, qm);
+    gemm_w(LT(l, 14), 512, 512, xq, xd, n, a);
+    float scale = *(const float *)LT(l, 16);
+    for (int t = 0; t < n; t++) {
+        float *hh = a + (size_t)t * 512, *xx = x + (size_t)t * 512;
+        eg2o_rms_row(hh, 512, LT(l, 15));
+        for (int z = 0; z < 512; z++) xx[z] = (xx[z] + hh[z]) * scale;
+    }
+}
+
 static int embed_batch(const void *const *tensors, const int32_t *ids, const float *inputs,
-                       const size_t *offsets, size_t batch, float *out, int qm, int gm, float *x_layers);
+                       const size_t *offsets, size_t batch, float *out, int qm, int gm, float *x_layers,
+                       float *ple_out);
 
 int eg2o_embed_batch(const void *const *tensors, const int32_t *ids, const size_t *offsets,
                      size_t batch, float *out, int qm, int gm, float *x_layers) {
-    return embed_batch(tensors, ids, NULL, offsets, batch, out, qm, gm, x_layers);
+    return embed_batch(tensors, ids, NULL, offsets, batch, out, qm, gm, x_layers, NULL);
+}
+
+int eg2o_embed_trace(const void *const *tensors, const int32_t *ids, const size_t *offsets, size_t batch,
+                     float *out, int qm, int gm, float *x_layers, float *ple_out) {
+    return embed_batch(tensors, ids, NULL, offsets, batch, out, qm, gm, x_layers, ple_out);
 }
 
 /* gemma2_fast.c:940-941: with ids NULL the wave starts from caller-given
  * 512-wide rows (media soft tokens), copied into x unscaled. */
 int eg2o_embed_batch_inputs(const void *const *tensors, const float *inputs, const size_t *offsets,
                             size_t batch, float *out, int qm, int gm) {
-    return inputs ? embed_batch(tensors, NULL, inputs, offsets, batch, out, qm, gm, NULL) : 1;
+    return inputs ? embed_batch(tensors, NULL, inputs, offsets, batch, out, qm, gm, NULL, NULL) : 1;
+}
+
+int eg2o_layer(const void *const *tensors, int l, float *x, const float *ple, const size_t *offsets, size_t batch,
+               int qm, int gm) {
+    size_t count = offsets[batch];
+    if (!count || count > 8192 || l < 0 || l >= 24) return 1;
+    rope_init();
+    wave_ws w = ws_alloc(offsets, batch);
+    layer_forward(tensors, l, x, ple, (int)count, qm, gm, &w);
+    ws_free(&w);
+    return 0;
 }
 
 static int embed_batch(const void *const *tensors, const int32_t *ids, const float *inputs,
-                       const size_t *offsets, size_t batch, float *out, int qm, int gm, float *x_layers) {
+                       const size_t *offsets, size_t batch, float *out, int qm, int gm, float *x_layers,
+                       float *ple_out) {
     size_t count = offsets[batch];
     if (!count || count > 8192) return 1;
     int n = (int)count;
     rope_init();
-    float *x = malloc(count * 512 * 4), *h = malloc(count * 512 * 4), *q = malloc(count * 2048 * 4);
-    float *k = malloc(count * 512 * 4), *v = malloc(count * 512 * 4), *a = malloc(count * 2048 * 4);
-    float *up = malloc(count * 2048 * 4), *gate = malloc(count * 2048 * 4);
-    float *ple = malloc(count * 512 * 24 * 4);
-    int8_t *xq = malloc(count * 2048);
-    uint16_t *xd = malloc(count * 64 * 2);
-    uint32_t *lo = malloc(count * 4), *hi = malloc(count * 4), *pos = malloc(count * 4);
-    for (size_t s = 0; s < batch; s++)
-        for (size_t t = offsets[s]; t < offsets[s + 1]; t++)
-            lo[t] = (uint32_t)offsets[s], hi[t] = (uint32_t)offsets[s + 1], pos[t] = (uint32_t)(t - offsets[s]);
+    float *x = malloc(count * 512 * 4);
+    float *ple = ple_out ? ple_out : malloc(count * 512 * 24 * 4);
+    wave_ws w = ws_alloc(offsets, batch);
     /* gemma2_fast.c:940-950: x = the given rows, or (d * q) * sqrtf(512). */
     if (inputs) memcpy(x, inputs, count * 512 * 4);
     for (int t = 0; t < n && !inputs; t++) {
@@ -339,77 +551,16 @@ static int embed_batch(const void *const *tensors, const int32_t *ids, const flo
             for (int z = 0; z < 32; z++) x[(size_t)t * 512 + b * 32 + z] = d * qs[z] * sqrtf(512.0f);
         }
     }
-    /* gemma2_fast.c:951-956. */
-    eg2o_gemm_bf16(T(1), x, n, 512, 24 * 512, ple);
-    for (size_t i = 0; i < count * 512 * 24; i++) ple[i] /= sqrtf(512.0f);
-    for (size_t r = 0; r < count * 24; r++) eg2o_rms_row(ple + r * 512, 512, T(2));
+    ple_project(tensors, x, n, ple);
     for (int l = 0; l < 24; l++) {
-        int d = l % 6 == 5 ? 512 : 256, kv = 512 / d;
         if (x_layers) memcpy(x_layers + (size_t)l * count * 512, x, count * 512 * 4);
-        /* ROW_NORM_QUANT (gemma2_fast.c:685-691). */
-        for (int t = 0; t < n; t++) {
-            memcpy(h + (size_t)t * 512, x + (size_t)t * 512, 2048);
-            eg2o_rms_row(h + (size_t)t * 512, 512, LT(l, 0));
-        }
-        eg2o_quantize(h, xq, xd, n * 512, qm);
-        gemm_w(LT(l, 1), 512, 4 * d, xq, xd, n, q);
-        gemm_w(LT(l, 2), 512, 512, xq, xd, n, k);
-        gemm_w(LT(l, 3), 512, 512, xq, xd, n, v);
-        /* ROW_QKV_POST (gemma2_fast.c:692-706). */
-        for (int t = 0; t < n; t++) {
-            for (int hd = 0; hd < 4; hd++) {
-                float *r = q + ((size_t)t * 4 + hd) * d;
-                eg2o_rms_row(r, d, LT(l, 5));
-                rope_row(r, d, (int)pos[t]);
-            }
-            for (int hd = 0; hd < kv; hd++) {
-                float *r = k + ((size_t)t * kv + hd) * d;
-                eg2o_rms_row(r, d, LT(l, 6));
-                rope_row(r, d, (int)pos[t]);
-                eg2o_rms_row(v + ((size_t)t * kv + hd) * d, d, NULL);
-            }
-        }
-        eg2o_attention(q, k, v, lo, hi, n, kv, d, l % 6 == 5 ? 0 : 512, a);
-        /* ROW_QUANT(a) -> attn_output -> ROW_POST_ADD (gemma2_fast.c:972-975). */
-        eg2o_quantize(a, xq, xd, n * 4 * d, qm);
-        gemm_w(LT(l, 4), 4 * d, 512, xq, xd, n, h);
-        for (int t = 0; t < n; t++) {
-            float *hh = h + (size_t)t * 512, *xx = x + (size_t)t * 512;
-            eg2o_rms_row(hh, 512, LT(l, 7));
-            for (int z = 0; z < 512; z++) xx[z] = (xx[z] + hh[z]) * 1.0f;
-        }
-        /* FFN (gemma2_fast.c:976-983). */
-        for (int t = 0; t < n; t++) {
-            memcpy(h + (size_t)t * 512, x + (size_t)t * 512, 2048);
-            eg2o_rms_row(h + (size_t)t * 512, 512, LT(l, 8));
-        }
-        eg2o_quantize(h, xq, xd, n * 512, qm);
-        gemm_w(LT(l, 9), 512, 2048, xq, xd, n, up);
-        gemm_w(LT(l, 10), 512, 2048, xq, xd, n, gate);
-        eg2o_gelu_mul(gate, up, n * 2048, gm);
-        eg2o_quantize(gate, xq, xd, n * 2048, qm);
-        gemm_w(LT(l, 11), 2048, 512, xq, xd, n, h);
-        for (int t = 0; t < n; t++) {
-            float *hh = h + (size_t)t * 512, *xx = x + (size_t)t * 512;
-            eg2o_rms_row(hh, 512, LT(l, 12));
-            for (int z = 0; z < 512; z++) xx[z] = (xx[z] + hh[z]) * 1.0f;
-        }
-        /* Per-layer embedding gate (gemma2_fast.c:984-990). */
-        eg2o_quantize(x, xq, xd, n * 512, qm);
-        gemm_w(LT(l, 13), 512, 512, xq, xd, n, h);
-        for (int t = 0; t < n; t++)
-            eg2o_gelu_mul(h + (size_t)t * 512, ple + ((size_t)t * 24 + l) * 512, 512, gm);
-        eg2o_quantize(h, xq, xd, n * 512, qm);
-        gemm_w(LT(l, 14), 512, 512, xq, xd, n, a);
-        float scale = *(const float *)LT(l, 16);
-        for (int t = 0; t < n; t++) {
-            float *hh = a + (size_t)t * 512, *xx = x + (size_t)t * 512;
-            eg2o_rms_row(hh, 512, LT(l, 15));
-            for (int z = 0; z < 512; z++) xx[z] = (xx[z] + hh[z]) * scale;
-        }
+        layer_forward(tensors, l, x, ple, n, qm, gm, &w);
     }
     if (x_layers) memcpy(x_layers + (size_t)24 * count * 512, x, count * 512 * 4);
     /* Output head and pooling (gemma2_fast.c:993-1008). */
+    float *h = w.h;
+    int8_t *xq = w.xq;
+    uint16_t *xd = w.xd;
     for (int t = 0; t < n; t++) {
         memcpy(h + (size_t)t * 512, x + (size_t)t * 512, 2048);
         eg2o_rms_row(h + (size_t)t * 512, 512, T(3 + 17 * 24));
@@ -425,7 +576,8 @@ static int embed_batch(const void *const *tensors, const int32_t *ids, const flo
             for (int z = 0; z < 768; z++) o[z] += y[t * 768 + z] / (float)len;
         l2_normalize_sse2(o, 768);
     }
-    free(y), free(x), free(h), free(q), free(k), free(v), free(a), free(up), free(gate), free(ple);
-    free(xq), free(xd), free(lo), free(hi), free(pos);
+    free(y), free(x);
+    if (!ple_out) free(ple);
+    ws_free(&w);
     return 0;
 }

@@ -6,7 +6,7 @@
  * Every function cites the reference lines it follows.  Only tests/,
  * __graft_entry__.smoke() and bench.py's CPU baseline may load this.
  *
- * Parity pin: tests/test_oracle_pins.py checks that eg2o_embed_batch() is
+ * Parity pin: tests/test_cpu_oracle.py checks that eg2o_embed_batch() is
  * bit-identical to the compiled reference (oracle/_ref/libeg2ref.so, scalar
  * tier) and that the x86 quantizer / GELU variants below are bit-identical to
  * the reference's g2x_* functions on random inputs.
@@ -58,6 +58,21 @@ void eg2o_attention(const float *q, const float *k, const float *v, const uint32
  * last one, [25][n][512].  Returns 0 on success. */
 int eg2o_embed_batch(const void *const *tensors, const int32_t *ids, const size_t *offsets,
                      size_t batch, float *out, int quant_mode, int gelu_mode, float *x_layers);
+/* eg2o_embed_batch that also returns the per-layer embedding stream ple_out
+ * [n][24][512] (gemma2_fast.c:951-956) beside x_layers (either may be NULL). */
+int eg2o_embed_trace(const void *const *tensors, const int32_t *ids, const size_t *offsets, size_t batch,
+                     float *out, int quant_mode, int gelu_mode, float *x_layers, float *ple_out);
+/* One layer l of the graph (gemma2_fast.c:957-992) on the residual stream x
+ * [n][512], in place, with the per-layer embeddings ple [n][24][512] of the
+ * same wave (offsets as for eg2o_embed_batch).  Returns 0 on success. */
+int eg2o_layer(const void *const *tensors, int l, float *x, const float *ple, const size_t *offsets, size_t batch,
+               int quant_mode, int gelu_mode);
+/* Test perturbations (default 0, 0): gemm_descending sums each GEMM's Q8_0
+ * blocks in descending instead of ascending order (another float order, as
+ * the reference's x86 tiers have); attention_fp16 rounds q, k and v to fp16
+ * before the attention (the fast path's tensor-core operands).  Used only to
+ * measure how far such changes move one layer's output. */
+void eg2o_set_variant(int gemm_descending, int attention_fp16);
 /* The same graph from caller-given 512-wide input rows (media soft tokens,
  * gemma2_fast.c:940-941) instead of token ids.  Returns 0 on success. */
 int eg2o_embed_batch_inputs(const void *const *tensors, const float *inputs, const size_t *offsets,

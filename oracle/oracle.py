@@ -20,17 +20,27 @@ import numpy as np
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 REF_SO = os.path.join(HERE, "_ref", "libeg2ref.so")
+CUDA_REF_SO = os.path.join(HERE, "_ref", "libeg2cudaref.so")
 PORT_SO = os.path.join(HERE, "_build", "libeg2oracle.so")
 
 GGML_F32, GGML_F16, GGML_Q8_0, GGML_BF16 = 0, 1, 8, 30
 
 
-def build(ref: bool = True) -> None:
-    """Compile the restatement, and the reference when its sources exist."""
+def ref_root() -> str:
+    """The reference tree: $REF_ROOT, else a directory `reference` beside this
+    repository's root (the oracle's Makefile uses the same default)."""
+    return os.environ.get("REF_ROOT") or os.path.abspath(os.path.join(HERE, "..", "..", "reference"))
+
+
+def build(ref: bool = True, cuda: bool = True) -> None:
+    """Compile the restatement, and the reference (its CPU graph and, with
+    cuda, its CUDA executor) when its sources exist."""
     subprocess.run(["make", "-s", "-C", HERE, "port"], check=True)
-    ref_root = os.environ.get("REF_ROOT", "/root/reference")
-    if ref and os.path.isdir(os.path.join(ref_root, "vendor")):
-        subprocess.run(["make", "-s", "-C", HERE, "ref", f"REF_ROOT={ref_root}"], check=True)
+    root = ref_root()
+    if ref and os.path.isdir(os.path.join(root, "vendor")):
+        subprocess.run(["make", "-s", "-C", HERE, "ref", f"REF_ROOT={root}"], check=True)
+        if cuda:
+            subprocess.run(["make", "-s", "-C", HERE, "cuda_ref", f"REF_ROOT={root}"], check=True)
 
 
 # ---------------------------------------------------------------------------
@@ -212,6 +222,42 @@ class RefGraph:
             self.handle = None
 
 
+class CudaRef:
+    """The reference's own CUDA executor for the same graph (gemma2_cuda.cu,
+    compiled from its sources into oracle/_ref/libeg2cudaref.so): the GPU
+    comparator, driven through its packed-wave call ei_gemma2_cuda_batch."""
+
+    def __init__(self, model_path: str, device: int = 0):
+        if not os.path.exists(CUDA_REF_SO):
+            raise FileNotFoundError(f"{CUDA_REF_SO} missing: run `make -C oracle cuda_ref` where the reference exists")
+        self.lib = C.CDLL(CUDA_REF_SO)
+        L = self.lib
+        L.eg2cref_open.restype = C.c_void_p
+        L.eg2cref_open.argtypes = [C.c_char_p, C.c_int, C.c_char_p, C.c_size_t]
+        L.eg2cref_close.argtypes = [C.c_void_p]
+        L.eg2cref_batch.argtypes = [C.c_void_p, C.c_void_p, C.c_void_p, C.c_size_t, C.c_void_p, C.c_char_p,
+                                    C.c_size_t]
+        err = C.create_string_buffer(512)
+        self.handle = L.eg2cref_open(model_path.encode(), device, err, 512)
+        if not self.handle:
+            raise RuntimeError(err.value.decode())
+
+    def embed(self, ids: np.ndarray, offsets: np.ndarray) -> np.ndarray:
+        ids = np.ascontiguousarray(ids, dtype=np.int32)
+        offsets = np.ascontiguousarray(offsets, dtype=np.uint64)
+        batch = len(offsets) - 1
+        out = np.zeros((batch, 768), np.float32)
+        err = C.create_string_buffer(512)
+        if not self.lib.eg2cref_batch(self.handle, _ptr(ids), _ptr(offsets), batch, _ptr(out), err, 512):
+            raise RuntimeError(err.value.decode())
+        return out
+
+    def close(self):
+        if self.handle:
+            self.lib.eg2cref_close(self.handle)
+            self.handle = None
+
+
 class Port:
     """The C restatement oracle/eg2_oracle.c (scalar tier)."""
 
@@ -237,6 +283,9 @@ class Port:
         L.eg2o_attention.argtypes = [vp, vp, vp, vp, vp, i, i, i, i, vp]
         L.eg2o_embed_batch.argtypes = [vp, vp, vp, C.c_size_t, vp, i, i, vp]
         L.eg2o_embed_batch_inputs.argtypes = [vp, vp, vp, C.c_size_t, vp, i, i]
+        L.eg2o_embed_trace.argtypes = [vp, vp, vp, C.c_size_t, vp, i, i, vp, vp]
+        L.eg2o_layer.argtypes = [vp, i, vp, vp, vp, C.c_size_t, i, i]
+        L.eg2o_set_variant.argtypes = [i, i]
 
     def quantize(self, x, mode=ROUND_X86):
         x = np.ascontiguousarray(x, dtype=np.float32).ravel()
@@ -311,6 +360,38 @@ class Port:
         if rc:
             raise RuntimeError("oracle rejected the wave")
         return (out, xl) if dump_layers else out
+
+    def trace(self, model: Gguf, ids, offsets, quant_mode=ROUND_X86, gelu_mode=1):
+        """The graph with its intermediate state: (embeddings [batch][768],
+        residual stream entering each layer and after the last [25][n][512],
+        per-layer embeddings [n][24][512])."""
+        ids = np.ascontiguousarray(ids, dtype=np.int32)
+        offsets = np.ascontiguousarray(offsets, dtype=np.uint64)
+        batch = len(offsets) - 1
+        n = int(offsets[-1])
+        out = np.zeros((batch, 768), np.float32)
+        xl = np.zeros((25, n, 512), np.float32)
+        ple = np.zeros((n, 24, 512), np.float32)
+        if self.lib.eg2o_embed_trace(model.pointer_table(), _ptr(ids), _ptr(offsets), batch, _ptr(out),
+                                     quant_mode, gelu_mode, _ptr(xl), _ptr(ple)):
+            raise RuntimeError("oracle rejected the wave")
+        return out, xl, ple
+
+    def layer(self, model: Gguf, l, x, ple, offsets, quant_mode=ROUND_X86, gelu_mode=1):
+        """One layer on the residual stream x [n][512] with the wave's per-layer
+        embeddings ple [n][24][512]; returns the new x."""
+        x = np.array(x, dtype=np.float32, copy=True).reshape(-1, 512)
+        ple = np.ascontiguousarray(ple, dtype=np.float32)
+        offsets = np.ascontiguousarray(offsets, dtype=np.uint64)
+        assert ple.size == x.shape[0] * 24 * 512
+        if self.lib.eg2o_layer(model.pointer_table(), l, _ptr(x), _ptr(ple), _ptr(offsets), len(offsets) - 1,
+                               quant_mode, gelu_mode):
+            raise RuntimeError("oracle rejected the layer")
+        return x
+
+    def set_variant(self, gemm_descending=False, attention_fp16=False):
+        """Perturb the restatement (tests of the float-order floor only)."""
+        self.lib.eg2o_set_variant(int(gemm_descending), int(attention_fp16))
 
     def embed_inputs(self, model: Gguf, inputs, offsets, quant_mode=ROUND_SCALAR, gelu_mode=0):
         """The graph from 512-wide input rows (media soft tokens) instead of ids."""

@@ -9,6 +9,10 @@ ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 sys.path.insert(0, ROOT)
 sys.path.insert(0, os.path.join(ROOT, "oracle"))
 GOLDEN = os.path.join(ROOT, "tests", "golden")
+# The reference tree (read only, never needed on a GPU box): $REF_ROOT, else a
+# directory `reference` beside this repository's root.  Tests that read it skip
+# when it is absent.
+REF_ROOT = os.environ.get("REF_ROOT") or os.path.abspath(os.path.join(ROOT, "..", "reference"))
 
 
 def pytest_configure(config):

@@ -1,6 +1,7 @@
 """Regenerate the committed golden fixtures from the reference's OWN CPU graph.
 
-Runs in the build container, where /root/reference exists:
+Runs where the reference tree exists ($REF_ROOT, or `reference` beside this
+repository's root):
 
     make -C oracle ref port
     python tests/golden/make_golden.py

