@@ -521,6 +521,101 @@ def mixed_load_run(args, rank, world, local):
     model.close()
 
 
+def engine_run(args):
+    """Config 3 the way the reference server would run this executor on a box
+    of N GPUs once its one-executor limit for this backend is lifted
+    (engine.c:1160-1268, slot picking in inference_service.c:171-218): ONE
+    process, one ei_gemma2_kfd_create_on context per GPU, one host thread per
+    context.  All 256 requests are queued at t = 0 and packed in order into
+    waves of at most 2048 tokens; wave i goes to GPU i % N.  Each thread keeps
+    two waves in flight (eg2_b200_submit / eg2_b200_collect) and truncates each
+    text to its request's dimensions (eg2_b200_normalize_prefix) while the GPU
+    runs the next wave.  The ctypes calls release the GIL, so the threads'
+    library work runs in parallel; their Python bookkeeping does not.  Per
+    thread the wall time splits into submit (validation, staging copy, graph
+    launch), collect (waiting for the GPU, result copy) and post (truncation),
+    which names the limiter of the 1 -> N curve."""
+    import threading
+    import torch
+    eg2 = importlib.import_module("embeddinggemma2-amdkfd_b200")
+    syn = eg2.synthetic
+    n_dev = args.gpus
+    if torch.cuda.device_count() < n_dev:
+        raise SystemExit(f"--engine needs {n_dev} visible GPUs, found {torch.cuda.device_count()}")
+    lens, dims = syn.mixed_load(256, 16)
+    waves = pack_waves(lens, list(range(len(lens))))
+    inputs = [wave_inputs(w, seed=1000 + i) for i, w in enumerate(waves)]
+    model = eg2.GGUFModel(syn.model_path(1234, "baseline"))
+    exs = [eg2.Gemma2Executor(model, d) for d in range(n_dev)]
+
+    def run_all():
+        remaining = {r: len(lens[r]) for r in range(len(lens))}
+        done_at, lock = {}, threading.Lock()
+        split = [dict(submit=0.0, collect=0.0, post=0.0) for _ in range(n_dev)]
+        t0 = time.perf_counter()
+
+        def worker(d):
+            ex, acc = exs[d], split[d]
+            mine = list(range(d, len(waves), n_dev))
+
+            def complete(slot, w):
+                c0 = time.perf_counter()
+                out = ex.collect(slot)
+                c1 = time.perf_counter()
+                finished = []
+                for i, (r, _, _) in enumerate(w):
+                    eg2.normalize_prefix(out[i], int(dims[r]))
+                    finished.append(r)
+                c2 = time.perf_counter()
+                acc["collect"] += c1 - c0
+                acc["post"] += c2 - c1
+                with lock:
+                    for r in finished:
+                        remaining[r] -= 1
+                        if remaining[r] == 0:
+                            done_at[r] = (c2 - t0) * 1000.0
+
+            pending = None
+            for i in mine:
+                s0 = time.perf_counter()
+                slot = ex.submit(*inputs[i])
+                acc["submit"] += time.perf_counter() - s0
+                if pending:
+                    complete(*pending)
+                pending = (slot, waves[i])
+            if pending:
+                complete(*pending)
+
+        threads = [threading.Thread(target=worker, args=(d,)) for d in range(n_dev)]
+        for th in threads:
+            th.start()
+        for th in threads:
+            th.join()
+        return (time.perf_counter() - t0) * 1000.0, done_at, split
+
+    run_all()  # warm-up: every context captures the graphs of the buckets the load uses
+    with ClockSampler(0) as clocks:
+        ms, done_at, split = run_all()
+    tokens = sum(n for w in waves for _, _, n in w)
+    lat = list(done_at.values())
+    line = {"metric": METRIC_MIXED, "value": tokens / (ms * 1e-3), "unit": "tokens/s", "n_gpus": n_dev, "steps": 1,
+            "warmup": 1, "ms_per_step": ms, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "dtype": DTYPE_FAST, "data": "synthetic",
+            "config": {"workload": CONFIGS[3][0], "requests": len(lens), "texts_per_request": len(lens[0]),
+                       "tokens": tokens, "waves": len(waves),
+                       "arrival": "all requests queued at t = 0 (offline load)",
+                       "parallelism": f"one process, {n_dev} executor contexts, one host thread each, "
+                                      f"wave i on GPU i % {n_dev}"},
+            "latency_ms": {"p50": float(np.percentile(lat, 50)), "p99": float(np.percentile(lat, 99)),
+                           "max": float(max(lat))},
+            "thread_split_ms": [{k: round(v * 1000.0, 1) for k, v in sp.items()} for sp in split],
+            "clocks_gpu0": clocks.summary()}
+    print(json.dumps(line), flush=True)
+    for ex in exs:
+        ex.close()
+    model.close()
+
+
 # ---------------------------------------------------------------- config 4
 GEMM_SHAPES = [(512, 2048, "q|k|v local"), (512, 3072, "q|k|v global"), (1024, 512, "attn_output local"),
                (2048, 512, "attn_output global, ffn_down"), (512, 4096, "ffn gate|up (GeGLU epilogue)"),
@@ -706,6 +801,8 @@ def main():
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-parity-mode", action="store_true", help="skip the parity-mode measurement")
+    ap.add_argument("--engine", action="store_true",
+                    help="config 3 in one process: one executor context and host thread per GPU (--gpus of them)")
     ap.add_argument("--no-gpu-baseline", action="store_true",
                     help="skip timing the reference's own CUDA executor beside this one")
     args = ap.parse_args()
@@ -713,6 +810,10 @@ def main():
     rank, world, local = dist_init()
     if args.impl == "reference":
         reference_arm(args, rank, world)
+        return finalize(world)
+    if args.config == 3 and args.engine:
+        if rank == 0:
+            engine_run(args)
         return finalize(world)
     if args.config == 3:
         mixed_load_run(args, rank, world, local)

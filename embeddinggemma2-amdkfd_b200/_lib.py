@@ -37,6 +37,7 @@ SIGNATURES = {
     "eg2_b200_stage_rows": (b, [vp, vp, vp, sz, cstr, sz]),
     "eg2_b200_submit_rows": (i32, [vp, vp, vp, sz, cstr, sz]),
     "eg2_b200_forward_layers": (b, [vp, vp, vp, vp, sz, i32, i32, vp, cstr, sz]),
+    "eg2_b200_normalize_prefix": (b, [vp, i32]),
     "eg2_b200_stream": (vp, [vp]),
     "eg2_b200_kernels_per_wave": (i32, [vp]),
     "eg2_b200_profile": (i32, [vp, vp, vp, i32]),
@@ -56,6 +57,9 @@ SIGNATURES = {
     "eg2_launch_norm_quant": (i32, [vp, vp]),
     "eg2_launch_q8_mm": (i32, [vp, vp]),
     "eg2_launch_q8_geglu": (i32, [vp, vp]),
+    "eg2_launch_q8_mm_f16": (i32, [vp, vp]),
+    "eg2_launch_q8_geglu_f16": (i32, [vp, vp]),
+    "eg2_split_q8_weight": (i32, [vp, vp, u32, u32, vp, vp, vp, vp]),
     "eg2_launch_qkv_post": (i32, [vp, vp]),
     "eg2_launch_attention_f16": (i32, [vp, vp]),
     "eg2_launch_attention_tc": (i32, [vp, vp]),
@@ -152,6 +156,16 @@ class EgQ8GeGLU(C.Structure):
                 ("ws", P), ("n", u32), ("k", u32), ("m", u32), ("exact", u32), ("tier", u32)]
 
 
+class EgQ8MMF16(C.Structure):
+    _fields_ = [("out", P), ("xq", P), ("xs", P), ("xs_stride", u32), ("wh", P), ("wl", P), ("rowscale", P),
+                ("n", u32), ("k", u32), ("m", u32), ("splits", u32), ("split_stride", C.c_uint64)]
+
+
+class EgQ8GeGLUF16(C.Structure):
+    _fields_ = [("q", P), ("scale", P), ("scale_stride", u32), ("xq", P), ("xs", P), ("xs_stride", u32), ("wh", P),
+                ("wl", P), ("rowscale", P), ("n", u32), ("k", u32), ("m", u32), ("tier", u32)]
+
+
 class EgQkvPost(C.Structure):
     _fields_ = [("q", P), ("k", P), ("v", P), ("qkv", P), ("q_norm", P), ("k_norm", P),
                 ("rope_cos", P), ("rope_sin", P), ("pos", P), ("n", u32), ("d", u32)]
@@ -186,5 +200,5 @@ class EgPoolL2(C.Structure):
 
 
 STRUCTS = {c.__name__: c for c in (EgGather, EgMM, EgNorm, EgRope, EgAttention, EgElement, EgPool, EgNormResidual,
-                                   EgNormRope, EgEmbed, EgPleProj, EgNormQuant, EgQ8MM, EgQ8GeGLU, EgQkvPost, EgAttentionF16,
+                                   EgNormRope, EgEmbed, EgPleProj, EgNormQuant, EgQ8MM, EgQ8GeGLU, EgQ8MMF16, EgQ8GeGLUF16, EgQkvPost, EgAttentionF16,
                                    EgPostAdd, EgGateQuant, EgGeluMul, EgPoolL2)}

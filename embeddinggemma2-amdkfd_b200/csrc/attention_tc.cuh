@@ -53,11 +53,12 @@ struct AttnTcParams {
     const unsigned *bounds;  // [n][2] = sequence [lo, hi)
     int n, window;
     // Optional Q8_0 output instead of out (ROW_QUANT of the attention row,
-    // gemma2_fast.c:728-730, fused): codes [n][4d], scales block-major
-    // [4d/32][q_stride]; quantizer rounding of `tier`.
-    int8_t *q;
+    // gemma2_fast.c:728-730, fused): codes [n][4d] (int8, or with codes_f16 the
+    // codes' fp16 values), scales block-major [4d/32][q_stride]; quantizer
+    // rounding of `tier`.
+    void *q;
     float *qs;
-    int q_stride, tier;
+    int q_stride, tier, codes_f16;
 };
 
 template <int D_>
@@ -367,9 +368,16 @@ __global__ void __launch_bounds__(AttnTcCfgD<D_>::THREADS, 1)
                                 w[e] |= q8_code(__uint_as_float(r[4 * e + b]) * il, id, p.tier) << (8 * b);
                         }
                         if (t < p.n) {
-                            uint4 *dst = reinterpret_cast<uint4 *>(p.q + size_t(t) * (4 * C::D) + col0 + c);
-                            dst[0] = make_uint4(w[0], w[1], w[2], w[3]);
-                            dst[1] = make_uint4(w[4], w[5], w[6], w[7]);
+                            const size_t at = size_t(t) * (4 * C::D) + col0 + c;
+                            if (p.codes_f16) {
+                                __half *dst = static_cast<__half *>(p.q) + at;
+#pragma unroll
+                                for (int e = 0; e < 8; ++e) store_codes4(dst, e, w[e]);
+                            } else {
+                                uint4 *dst = reinterpret_cast<uint4 *>(static_cast<int8_t *>(p.q) + at);
+                                dst[0] = make_uint4(w[0], w[1], w[2], w[3]);
+                                dst[1] = make_uint4(w[4], w[5], w[6], w[7]);
+                            }
                             p.qs[size_t((col0 + c) / 32) * p.q_stride + t] = fp16_bits_to_f32(ref_fp32_to_fp16(d));
                         }
                     }

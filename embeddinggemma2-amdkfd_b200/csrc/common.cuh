@@ -321,6 +321,21 @@ __device__ __forceinline__ uint32_t q8_code(float x, float id, int tier = TIER_X
     q = q < -128 ? -128 : (q > 127 ? 127 : q);
     return uint32_t(q) & 0xFFu;
 }
+// Q8_0 codes leave the quantizers either as int8 (the operand of the exact
+// int8 GEMM) or as the fp16 values of the same integers (the operand of the
+// fp16 tensor-core GEMM of the fast path; |q| <= 128 is exact in fp16).
+// store_codes4 writes the four codes packed in `c` (byte b = code 4i + b) at
+// codes 4i .. 4i + 3 of `row`.
+__device__ __forceinline__ __half code_half(uint32_t c, int b) {
+    return __short2half_rn(short(int8_t(uint8_t(c >> (8 * b)))));
+}
+__device__ __forceinline__ void store_codes4(int8_t *row, int i, uint32_t c) {
+    reinterpret_cast<uint32_t *>(row)[i] = c;
+}
+__device__ __forceinline__ void store_codes4(__half *row, int i, uint32_t c) {
+    const __half2 a = __halves2half2(code_half(c, 0), code_half(c, 1)), b = __halves2half2(code_half(c, 2), code_half(c, 3));
+    reinterpret_cast<uint2 *>(row)[i] = make_uint2(*reinterpret_cast<const uint32_t *>(&a), *reinterpret_cast<const uint32_t *>(&b));
+}
 // exp(x) by Cody-Waite reduction and a degree-6 polynomial: the reference's own
 // x86 GELU helper (gemma2_fast_x86.c:291-306), evaluated with the same fused
 // and unfused operations so that results match it bit for bit.

@@ -84,6 +84,11 @@ struct Q8Weight {
     float *scales = nullptr;  // [k/32][rows]
     int rows = 0, k = 0;
     CUtensorMap tmap{}, tscale{};
+    // Fast path: the weight dequantized and split exactly into two fp16 planes,
+    // w * 2^s_r = wh + wl [rows][k], and rowscale[r] = 2^-s_r (f16gemm.cuh).
+    void *wh = nullptr, *wl = nullptr;
+    float *rowscale = nullptr;
+    CUtensorMap twh{}, twl{};
 };
 
 struct Layer {
@@ -133,6 +138,13 @@ struct Backend {
     void *x_hi = nullptr, *x_lo = nullptr, *qh = nullptr, *kh = nullptr, *vh = nullptr;
     int8_t *xq = nullptr, *gq = nullptr;  // Q8 activations; gq/gs: the GeGLU output (FFN down operand)
     CUtensorMap tm_xq[3]{}, tm_xs[3]{}, tm_gq{}, tm_gs{}, tm_hi{}, tm_lo{}, tm_ple{};
+    // Fast path: the same Q8 activations with fp16 codes (the fp16 GEMM's
+    // operand), their maps, activation-scale maps per (K, splits), and split-K
+    // partial sums of the 512-wide projections in h ([SPLITS][cap][512]).
+    static constexpr int SPLITS = 2;
+    void *xq16 = nullptr, *gq16 = nullptr;
+    CUtensorMap tm_x16[3]{}, tm_g16{}, tm_xs_split[3][2]{}, tm_gs_split[2]{};
+    size_t h_part = 0;
     // Parity mode (EG2_B200_EXACT): GEMMs in the reference scalar tile's rounding
     // order, PLE projection and attention on the CUDA-core exact-order kernels
     // with fp32 q/k/v; every other kernel is bit-exact in both modes.
@@ -235,6 +247,14 @@ struct Backend {
     void finish_q8(Q8Weight &w) {
         if (w.rows % 128 || !q8_tmap(&w.tmap, w.codes, uint64_t(w.k), uint64_t(w.rows), 128) ||
             !scale_tmap(&w.tscale, w.scales, uint64_t(w.rows), uint64_t(w.k / 32), 128))
+            throw std::runtime_error("cuTensorMapEncodeTiled failed for a weight");
+        if (exact) return;
+        w.wh = dalloc<uint16_t>(size_t(w.rows) * w.k);
+        w.wl = dalloc<uint16_t>(size_t(w.rows) * w.k);
+        w.rowscale = dalloc<float>(size_t(w.rows));
+        ck(launch_split_q8(w.codes, w.scales, w.rows, w.rows, w.k, w.wh, w.wl, w.rowscale, stream), "weight split");
+        if (!f16_tmap(&w.twh, w.wh, uint64_t(w.k), uint64_t(w.rows), 128) ||
+            !f16_tmap(&w.twl, w.wl, uint64_t(w.k), uint64_t(w.rows), 128))
             throw std::runtime_error("cuTensorMapEncodeTiled failed for a weight");
     }
 
@@ -352,7 +372,8 @@ struct Backend {
         kh = dalloc<uint16_t>(size_t(cap) * 512);
         vh = dalloc<uint16_t>(size_t(cap) * 512);
         attn = dalloc<float>(size_t(cap) * 2048);
-        h = dalloc<float>(size_t(cap) * 512);
+        h_part = size_t(cap) * 512;
+        h = dalloc<float>(SPLITS * h_part);
         gq = dalloc<int8_t>(size_t(cap) * 2048);
         gs = dalloc<float>(size_t(64) * cap);
         y = dalloc<float>(size_t(cap) * 768);
@@ -369,6 +390,20 @@ struct Backend {
                 throw std::runtime_error("tensor map (activations)");
         if (!q8_tmap(&tm_gq, gq, 2048, cap, 64) || !scale_tmap(&tm_gs, gs, cap, 64, 64))
             throw std::runtime_error("tensor map (GeGLU activations)");
+        if (!exact) {
+            xq16 = dalloc<uint16_t>(size_t(cap) * 2048);
+            gq16 = dalloc<uint16_t>(size_t(cap) * 2048);
+            for (int i = 0; i < 3; ++i) {
+                const uint64_t kb = uint64_t(ks[i] / 32);
+                if (!f16_tmap(&tm_x16[i], xq16, uint64_t(ks[i]), cap, 128) ||
+                    !scale_tmap_rows(&tm_xs_split[i][0], xs, cap, kb, 128, uint32_t(kb)) ||
+                    !scale_tmap_rows(&tm_xs_split[i][1], xs, cap, kb, 128, uint32_t(kb / SPLITS)))
+                    throw std::runtime_error("tensor map (fp16 activations)");
+            }
+            if (!f16_tmap(&tm_g16, gq16, 2048, cap, 128) || !scale_tmap_rows(&tm_gs_split[0], gs, cap, 64, 128, 64) ||
+                !scale_tmap_rows(&tm_gs_split[1], gs, cap, 64, 128, 64 / SPLITS))
+                throw std::runtime_error("tensor map (fp16 GeGLU activations)");
+        }
         if (!bf16_tmap(&tm_hi, x_hi, 512, cap, 128) || !bf16_tmap(&tm_lo, x_lo, 512, cap, 128) ||
             !bf16_tmap(&tm_ple, ple_w, 512, 24 * 512, 256))
             throw std::runtime_error("tensor map (PLE)");
@@ -406,11 +441,23 @@ struct Backend {
     }
 
     static int kidx(int k) { return k == 512 ? 0 : k == 1024 ? 1 : 2; }
-    void gemm(const Q8Weight &w, float *out, int ldo, int n, cudaStream_t s) {
-        ck(launch_q8gemm(w.tmap, tm_xq[kidx(w.k)], w.tscale, tm_xs[kidx(w.k)], exact, out, ldo, n, w.rows, w.k,
-                         s),
-           "q8 GEMM");
+    // The projection of the current Q8 activations (xq / xq16) by w.  Parity
+    // mode: the exact int8 kernel.  Fast path: the fp16 kernel, split over K
+    // in `splits` partial sums at out + i * h_part when splits > 1.
+    void gemm(const Q8Weight &w, float *out, int ldo, int n, cudaStream_t s, int splits = 1) {
+        if (exact) {
+            ck(launch_q8gemm(w.tmap, tm_xq[kidx(w.k)], w.tscale, tm_xs[kidx(w.k)], true, out, ldo, n, w.rows, w.k, s),
+               "q8 GEMM");
+            return;
+        }
+        ck(launch_f16gemm(w.twh, w.twl, tm_x16[kidx(w.k)], tm_xs_split[kidx(w.k)][splits > 1], w.rowscale, out, ldo,
+                          h_part, splits, n, w.rows, w.k, s),
+           "fp16 GEMM");
     }
+    // Split factor of the 512-wide projections (few output tiles); their row
+    // consumers add the partials.
+    int parts() const { return exact ? 1 : SPLITS; }
+    void *codes() const { return exact ? static_cast<void *>(xq) : xq16; }
 
     // Both layer kinds run the tensor-core attention through maps whose token
     // extent is this wave's N (captured into its graph).
@@ -445,8 +492,8 @@ struct Backend {
                 ++launches;
             mark("qkv_post");
             // The O projection's Q8 operand is written by the attention itself.
-            ck(launch_attention_tc(tc_maps[L.d == 512], nullptr, bounds, N, L.d == 512 ? 0 : 512, s, xq, xs, cap,
-                                   tier),
+            ck(launch_attention_tc(tc_maps[L.d == 512], nullptr, bounds, N, L.d == 512 ? 0 : 512, s, xq16, xs, cap,
+                                   tier, true),
                "attention");
             ++launches;
         }
@@ -455,31 +502,50 @@ struct Backend {
             ck(launch_norm_quant(xq, xs, cap, nullptr, attn, nullptr, N, 4 * L.d, s, tier), "quant"), ++launches;
             mark("quant_attn");
         }
-        gemm(L.o, h, 512, N, s), ++launches;
+        const int P = parts();
+        gemm(L.o, h, 512, N, s, P), ++launches;
         mark("gemm_o");
-        ck(launch_post_add(x, h, L.post_attn_norm, nullptr, xq, xs, cap, L.ffn_norm, N, s, tier), "post_add"), ++launches;
+        ck(launch_post_add(x, h, L.post_attn_norm, nullptr, codes(), xs, cap, L.ffn_norm, N, s, tier, P, h_part, !exact),
+           "post_add"),
+            ++launches;
         mark("post_add");
         // ffn_gate and ffn_up in one GEMM whose epilogue applies gelu(gate) * up
         // and quantizes (ROW_GELU_QUANT fused); the result is the down operand.
-        ck(launch_q8gemm_geglu(L.gu.tmap, tm_xq[0], L.gu.tscale, tm_xs[0], exact, gq, gs, cap, N, L.gu.rows, L.gu.k,
-                               s, tier),
-           "GeGLU GEMM"),
-            ++launches;
+        if (exact)
+            ck(launch_q8gemm_geglu(L.gu.tmap, tm_xq[0], L.gu.tscale, tm_xs[0], true, gq, gs, cap, N, L.gu.rows, L.gu.k, s,
+                                   tier),
+               "GeGLU GEMM");
+        else
+            ck(launch_f16gemm_geglu(L.gu.twh, L.gu.twl, tm_x16[0], tm_xs_split[0][0], L.gu.rowscale, gq16, gs, cap, N,
+                                    L.gu.rows, L.gu.k, s, tier),
+               "GeGLU GEMM");
+        ++launches;
         mark("gemm_geglu");
-        ck(launch_q8gemm(L.down.tmap, tm_gq, L.down.tscale, tm_gs, exact, h, 512, N, L.down.rows, L.down.k, s),
-           "q8 GEMM"),
-            ++launches;
+        if (exact)
+            ck(launch_q8gemm(L.down.tmap, tm_gq, L.down.tscale, tm_gs, true, h, 512, N, L.down.rows, L.down.k, s),
+               "q8 GEMM");
+        else
+            ck(launch_f16gemm(L.down.twh, L.down.twl, tm_g16, tm_gs_split[1], L.down.rowscale, h, 512, h_part, P, N,
+                              L.down.rows, L.down.k, s),
+               "fp16 GEMM");
+        ++launches;
         mark("gemm_down");
-        ck(launch_post_add(x, h, L.post_ffw_norm, nullptr, xq, xs, cap, nullptr, N, s, tier), "post_add"), ++launches;
+        ck(launch_post_add(x, h, L.post_ffw_norm, nullptr, codes(), xs, cap, nullptr, N, s, tier, P, h_part, !exact),
+           "post_add"),
+            ++launches;
         mark("post_add");
-        gemm(L.inp_gate, h, 512, N, s), ++launches;
+        gemm(L.inp_gate, h, 512, N, s, P), ++launches;
         mark("gemm_inp_gate");
-        ck(launch_gate_quant(xq, xs, cap, h, ple, N, 512, 24 * 512, l * 512, s, tier), "ple gate"), ++launches;
+        ck(launch_gate_quant(codes(), xs, cap, h, ple, N, 512, 24 * 512, l * 512, s, tier, P, h_part, !exact),
+           "ple gate"),
+            ++launches;
         mark("ple_gate_quant");
-        gemm(L.proj, h, 512, N, s), ++launches;
+        gemm(L.proj, h, 512, N, s, P), ++launches;
         mark("gemm_proj");
         const float *next = l + 1 < 24 ? layers[l + 1].attn_norm : output_norm;
-        ck(launch_post_add(x, h, L.post_norm, L.out_scale, xq, xs, cap, next, N, s, tier), "post_add"), ++launches;
+        ck(launch_post_add(x, h, L.post_norm, L.out_scale, codes(), xs, cap, next, N, s, tier, P, h_part, !exact),
+           "post_add"),
+            ++launches;
         mark("post_add");
         return launches;
     }
@@ -506,7 +572,8 @@ struct Backend {
         else
             ck(launch_ple(tm_hi, tm_lo, tm_ple, ple, ple_norm, N, s), "PLE"), ++launches;
         mark("ple_proj");
-        ck(launch_norm_quant(xq, xs, cap, nullptr, x, layers[0].attn_norm, N, 512, s, tier), "norm"), ++launches;
+        ck(launch_norm_quant(codes(), xs, cap, nullptr, x, layers[0].attn_norm, N, 512, s, tier, !exact), "norm"),
+            ++launches;
         mark("norm_quant");
         for (int l = 0; l < 24; ++l) launches += enqueue_layer(l, N, s, tc_maps, mark);
         gemm(output, y, 768, N, s), ++launches;
@@ -724,7 +791,7 @@ struct Backend {
         AttnTcMaps tc_maps[2]{};
         attention_maps(N, tc_maps);
         if (l0 < 24)
-            ck(launch_norm_quant(xq, xs, cap, nullptr, x, layers[l0].attn_norm, N, 512, s, tier), "norm");
+            ck(launch_norm_quant(codes(), xs, cap, nullptr, x, layers[l0].attn_norm, N, 512, s, tier, !exact), "norm");
         auto none = [](const char *) {};
         for (int l = l0; l < l1; ++l) enqueue_layer(l, N, s, tc_maps, none);
         enqueue_readback(sl, 0);
@@ -885,6 +952,37 @@ extern "C" bool eg2_b200_forward_layers(void *ctx, const float *x_in, const floa
         if (!x_in) throw std::runtime_error(count_message(b->cap));
         b->forward_layers(x_in, ple_in, offsets, batch, first_layer, last_layer, x_out);
     });
+}
+// Matryoshka truncation as the server applies it (kernels.c:398-407,
+// server.c:1133): keep the first dims of a 768-wide L2-normalised embedding
+// and, when shorter, renormalise with the sum of squares in the order of the
+// server's SSE2 build (kernels.c:82-93: two 4-lane accumulators over 8-element
+// chunks, then (v0 + v2) + (v1 + v3), kernels.c:35-39) and x *= 1 / sqrtf(ss)
+// (kernels.c:393-396).  Plain host arithmetic: products and sums rounded one
+// by one, no contraction (baseline x86-64 has no FMA).
+extern "C" bool eg2_b200_normalize_prefix(float *x, int dims) {
+    if (!x || (dims != 128 && dims != 256 && dims != 512 && dims != 768)) return false;
+    if (dims == 768) return true;
+    float s0[4] = {0.0f, 0.0f, 0.0f, 0.0f}, s1[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+    int i = 0;
+    for (; i + 7 < dims; i += 8)
+        for (int j = 0; j < 4; ++j) {
+            const float a = x[i + j] * x[i + j], b = x[i + 4 + j] * x[i + 4 + j];
+            s0[j] = s0[j] + a;
+            s1[j] = s1[j] + b;
+        }
+    float v[4];
+    for (int j = 0; j < 4; ++j) v[j] = s0[j] + s1[j];
+    float ss = (v[0] + v[2]) + (v[1] + v[3]);
+    for (; i < dims; ++i) {
+        const float a = x[i] * x[i];
+        ss = ss + a;
+    }
+    if (ss != 0.0f) {
+        const float sc = 1.0f / std::sqrt(ss);
+        for (int z = 0; z < dims; ++z) x[z] *= sc;
+    }
+    return true;
 }
 extern "C" void *eg2_b200_stream(void *ctx) { return ctx ? static_cast<Backend *>(ctx)->stream : nullptr; }
 extern "C" int eg2_b200_kernels_per_wave(void *ctx) { return ctx ? static_cast<Backend *>(ctx)->kernels_per_wave : 0; }

@@ -267,37 +267,18 @@ class Gemma2Executor:
             pass
 
 
-def _sum_squares_sse2(row: np.ndarray) -> np.float32:
-    """kernels.c:82-93 order: two 4-lane float accumulators over 8-element chunks."""
-    sq = (row * row).astype(np.float32)
-    n8 = sq.size // 8 * 8
-    lanes = sq[:n8].reshape(-1, 2, 4)
-    s0 = np.zeros(4, np.float32)
-    s1 = np.zeros(4, np.float32)
-    for c in range(lanes.shape[0]):
-        s0 = (s0 + lanes[c, 0]).astype(np.float32)
-        s1 = (s1 + lanes[c, 1]).astype(np.float32)
-    v = (s0 + s1).astype(np.float32)
-    ss = np.float32(np.float32(v[0] + v[2]) + np.float32(v[1] + v[3]))
-    for z in range(n8, sq.size):
-        ss = np.float32(ss + sq[z])
-    return ss
-
-
 def normalize_prefix(embedding: np.ndarray, dimensions: int) -> np.ndarray:
     """Matryoshka truncation as the server applies it
     (vendor/embeddinggemma.c/src/kernels.c:398-407, server.c:1133): keep the
     first `dimensions` in {128, 256, 512, 768} and L2-renormalise when shorter,
-    in the reference's float order."""
+    in the reference's float order (eg2_b200_normalize_prefix, host code)."""
     if dimensions not in (128, 256, 512, 768):
         raise ValueError("dimensions must be one of 128, 256, 512, 768")
     e = np.array(embedding, dtype=np.float32, copy=True)
-    if dimensions == EMBED_DIM:
-        return e
-    e = np.ascontiguousarray(e[..., :dimensions])
-    flat = e.reshape(-1, dimensions)
+    if e.shape[-1] != EMBED_DIM:
+        raise ValueError("embeddings must be 768 wide")
+    lib = _lib.load()
+    flat = np.ascontiguousarray(e.reshape(-1, EMBED_DIM))
     for row in flat:
-        ss = _sum_squares_sse2(row)
-        if ss != 0:
-            row *= np.float32(np.float32(1.0) / np.sqrt(ss, dtype=np.float32))
-    return e
+        lib.eg2_b200_normalize_prefix(row.ctypes.data, dimensions)
+    return np.ascontiguousarray(flat.reshape(e.shape)[..., :dimensions])

@@ -37,7 +37,7 @@ SLIDING_WINDOW = 1024
 BOS, EOS = 2, 1
 
 GGML_F32, GGML_F16, GGML_Q8_0, GGML_BF16 = 0, 1, 8, 30
-GGUF_U32, GGUF_STRING = 4, 8
+GGUF_I32, GGUF_U32, GGUF_F32, GGUF_STRING, GGUF_ARRAY = 5, 4, 6, 8, 9
 ALIGN = 32
 
 
@@ -119,8 +119,38 @@ def _kv_u32(key: str, val: int) -> bytes:
     return struct.pack("<Q", len(k)) + k + struct.pack("<II", GGUF_U32, val)
 
 
-def write_gguf(path: str, seed: int = 1234, norm: str = "plus1") -> str:
-    """Write the seeded model to `path` and return the sha256 of the file."""
+def _kv_array(key: str, elem_type: int, payload: bytes, n: int) -> bytes:
+    k = key.encode()
+    return struct.pack("<Q", len(k)) + k + struct.pack("<IIQ", GGUF_ARRAY, elem_type, n) + payload
+
+
+def _tokenizer_kvs() -> list[bytes]:
+    """A placeholder tokenizer section for the reference's model loader
+    (vendor/embeddinggemma.c/src/model.c:46-52,111-120; tokenizer.c:205-266):
+    262144 pieces -- <pad>, <eos>, <bos>, <unk>, the 256 byte-fallback pieces
+    <0xXX>, then filler pieces -- with zero scores, the usual token types and
+    one merge.  It lets the reference's engine load the seeded model; text
+    tokenization with it is not meaningful (callers pass token ids)."""
+    pieces = ["<pad>", "<eos>", "<bos>", "<unk>"] + [f"<0x{b:02X}>" for b in range(256)]
+    pieces += [f"\u2581t{i}" for i in range(N_VOCAB - len(pieces))]
+    types = np.ones(N_VOCAB, np.int32)
+    types[[0, 1, 2]] = 3   # control
+    types[3] = 2           # unknown
+    types[4:260] = 6       # byte
+    enc = [x.encode() for x in pieces]
+    tok = b"".join(struct.pack("<Q", len(e)) + e for e in enc)
+    merge = "\u2581 t".encode()
+    return [_kv_string("tokenizer.ggml.model", "gemma4"),
+            _kv_array("tokenizer.ggml.tokens", GGUF_STRING, tok, N_VOCAB),
+            _kv_array("tokenizer.ggml.scores", GGUF_F32, np.zeros(N_VOCAB, np.float32).tobytes(), N_VOCAB),
+            _kv_array("tokenizer.ggml.token_type", GGUF_I32, types.tobytes(), N_VOCAB),
+            _kv_array("tokenizer.ggml.merges", GGUF_STRING, struct.pack("<Q", len(merge)) + merge, 1)]
+
+
+def write_gguf(path: str, seed: int = 1234, norm: str = "plus1", tokenizer: bool = False) -> str:
+    """Write the seeded model to `path` and return the sha256 of the file.
+    With tokenizer=True the file also carries a placeholder tokenizer section
+    (same tensors and values), which the reference's engine loader requires."""
     if norm not in ("plus1", "baseline"):
         raise ValueError("norm must be 'plus1' or 'baseline'")
     table = tensor_table()
@@ -131,6 +161,8 @@ def write_gguf(path: str, seed: int = 1234, norm: str = "plus1") -> str:
            _kv_u32(f"{ARCH}.embedding_length_out", N_OUT),
            _kv_u32(f"{ARCH}.attention.sliding_window", SLIDING_WINDOW),
            _kv_u32("general.alignment", ALIGN)]
+    if tokenizer:
+        kvs += _tokenizer_kvs()
     infos, offset = [], 0
     for name, typ, ne0, ne1 in table:
         nm = name.encode()
@@ -157,14 +189,14 @@ def write_gguf(path: str, seed: int = 1234, norm: str = "plus1") -> str:
     return h.hexdigest()
 
 
-def model_path(seed: int = 1234, norm: str = "plus1", cache_dir: str | None = None) -> str:
+def model_path(seed: int = 1234, norm: str = "plus1", cache_dir: str | None = None, tokenizer: bool = False) -> str:
     """Path of the cached seeded model, written on first use (~151 MB)."""
     cache_dir = cache_dir or os.environ.get("EG2_MODEL_CACHE") or os.path.join(
         tempfile.gettempdir(), "eg2_b200_models")
     os.makedirs(cache_dir, exist_ok=True)
-    path = os.path.join(cache_dir, f"eg2-synth-s{seed}-{norm}.gguf")
+    path = os.path.join(cache_dir, f"eg2-synth-s{seed}-{norm}{'-tok' if tokenizer else ''}.gguf")
     if not os.path.exists(path):
-        write_gguf(path, seed, norm)
+        write_gguf(path, seed, norm, tokenizer)
     return path
 
 

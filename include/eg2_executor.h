@@ -112,6 +112,12 @@ int eg2_b200_submit_rows(void *ctx, const float *rows, const size_t *offsets, si
  * host memory; replaces the staged wave, if any. */
 bool eg2_b200_forward_layers(void *ctx, const float *x_in, const float *ple_in, const size_t *offsets, size_t batch,
                              int first_layer, int last_layer, float *x_out, char *err, size_t len);
+/* Matryoshka truncation of one embedding as the reference server applies it
+ * (kernels.c:398-407 ei_embedding_normalize_prefix, server.c:1133): keeps the
+ * first dims in {128, 256, 512, 768} of the 768 floats and, when shorter,
+ * L2-renormalises them in place in the server's summation order.  Host only,
+ * thread-safe; false for other dims. */
+bool eg2_b200_normalize_prefix(float *embedding, int dims);
 /* The cudaStream_t the context launches on (for CUDA-event timing). */
 void *eg2_b200_stream(void *ctx);
 /* Kernels launched per wave by the staged graph. */

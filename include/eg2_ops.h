@@ -75,6 +75,31 @@ typedef struct {
     const int8_t *wq; const float *ws; unsigned n, k, m, exact;
     unsigned tier; /* as in EgGateQuant */
 } EgQ8GeGLU;
+/* The fast path's form of EgQ8MM on the fp16 tensor cores (tcgen05
+ * kind::f16).  The weight is pre-split (eg2_split_q8_weight) into two fp16
+ * planes wh, wl [m][k] with wh + wl == ws * q * 2^s_r exactly and
+ * rowscale[r] = 2^-s_r; the activation codes xq [n][k] are the Q8_0 codes as
+ * fp16 values (exact), with fp32 block scales xs as in EgQ8MM.  Per block b
+ * the tensor core forms P_b = sum (wh + wl) q in fp32 from exact products, and
+ * out[t][r] = rowscale[r] * sum_b P_b * xs[b][t] (one FMA per block): the
+ * reference's sum_b D_b * ws * xs (gemma2_fast.c:242-253) up to fp32
+ * accumulation order.  k % 64 == 0, k <= 2048, m % 128 == 0, xs_stride >= n
+ * and a multiple of 4; splits 1, 2 or 4 with (k / 32) % (2 * splits) == 0:
+ * split i writes the partial sum over its k range at out + i * split_stride
+ * (split_stride >= n * m floats); the product is the sum of the partials in
+ * order. */
+typedef struct {
+    float *out; const uint16_t *xq; const float *xs; unsigned xs_stride;
+    const uint16_t *wh, *wl; const float *rowscale; unsigned n, k, m, splits; uint64_t split_stride;
+} EgQ8MMF16;
+/* EgQ8GeGLU on the fp16 tensor cores: gate/up interleaved in 64-row chunks as
+ * in EgQ8GeGLU, split as for EgQ8MMF16 (2m rows); codes q [n][m] are written
+ * as fp16 values. */
+typedef struct {
+    uint16_t *q; float *scale; unsigned scale_stride;
+    const uint16_t *xq; const float *xs; unsigned xs_stride;
+    const uint16_t *wh, *wl; const float *rowscale; unsigned n, k, m, tier;
+} EgQ8GeGLUF16;
 /* Per head RMS (q, k weighted; v plain) and NEOX RoPE from host tables at the
  * token's in-sequence position (ROW_QKV_POST, gemma2_fast.c:692-706).  qkv is
  * the fused projection [n][4d | 512 | 512]; outputs are fp16 [n][heads][d]. */
@@ -133,6 +158,12 @@ int eg2_launch_ple_proj(const EgPleProj *p, void *stream);
 int eg2_launch_norm_quant(const EgNormQuant *p, void *stream);
 int eg2_launch_q8_mm(const EgQ8MM *p, void *stream);
 int eg2_launch_q8_geglu(const EgQ8GeGLU *p, void *stream);
+int eg2_launch_q8_mm_f16(const EgQ8MMF16 *p, void *stream);
+int eg2_launch_q8_geglu_f16(const EgQ8GeGLUF16 *p, void *stream);
+/* Split a SoA Q8 weight (codes [rows][k], fp32 scales [k/32][rows]) into the
+ * fp16 planes and row scales of EgQ8MMF16 (done once, at load time). */
+int eg2_split_q8_weight(const int8_t *codes, const float *scales, unsigned rows, unsigned k, uint16_t *wh,
+                        uint16_t *wl, float *rowscale, void *stream);
 int eg2_launch_qkv_post(const EgQkvPost *p, void *stream);
 int eg2_launch_attention_f16(const EgAttentionF16 *p, void *stream);
 /* The same attention on the 5th-generation tensor cores, d = 256 (the

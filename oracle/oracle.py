@@ -21,6 +21,7 @@ import numpy as np
 HERE = os.path.dirname(os.path.abspath(__file__))
 REF_SO = os.path.join(HERE, "_ref", "libeg2ref.so")
 CUDA_REF_SO = os.path.join(HERE, "_ref", "libeg2cudaref.so")
+ENGINE_LINK_SO = os.path.join(HERE, "_ref", "libeg2enginelink.so")
 PORT_SO = os.path.join(HERE, "_build", "libeg2oracle.so")
 
 GGML_F32, GGML_F16, GGML_Q8_0, GGML_BF16 = 0, 1, 8, 30
@@ -41,6 +42,8 @@ def build(ref: bool = True, cuda: bool = True) -> None:
         subprocess.run(["make", "-s", "-C", HERE, "ref", f"REF_ROOT={root}"], check=True)
         if cuda:
             subprocess.run(["make", "-s", "-C", HERE, "cuda_ref", f"REF_ROOT={root}"], check=True)
+        if os.path.exists(os.path.join(HERE, "..", "embeddinggemma2-amdkfd_b200", "libeg2_b200.so")):
+            subprocess.run(["make", "-s", "-C", HERE, "engine_link", f"REF_ROOT={root}"], check=True)
 
 
 # ---------------------------------------------------------------------------
@@ -255,6 +258,45 @@ class CudaRef:
     def close(self):
         if self.handle:
             self.lib.eg2cref_close(self.handle)
+            self.handle = None
+
+
+class EngineLink:
+    """The reference's own engine (engine.c, --backend kfd) linked with
+    libeg2_b200.so (oracle/_ref/libeg2enginelink.so): its packed-wave call
+    ei_engine_embed_tokens_batch reaches the B200 executor."""
+
+    def __init__(self, model_path: str):
+        if not os.path.exists(ENGINE_LINK_SO):
+            raise FileNotFoundError(f"{ENGINE_LINK_SO} missing: run `make -C oracle engine_link`")
+        self.lib = C.CDLL(ENGINE_LINK_SO)
+        L = self.lib
+        L.eg2link_open.restype = C.c_void_p
+        L.eg2link_open.argtypes = [C.c_char_p]
+        L.eg2link_backend.restype = C.c_char_p
+        L.eg2link_backend.argtypes = [C.c_void_p]
+        L.eg2link_embed_batch.argtypes = [C.c_void_p, C.c_void_p, C.c_void_p, C.c_size_t, C.c_void_p, C.c_char_p,
+                                          C.c_size_t]
+        L.eg2link_close.argtypes = [C.c_void_p]
+        self.handle = L.eg2link_open(model_path.encode())
+
+    @property
+    def backend(self) -> str:
+        return self.lib.eg2link_backend(self.handle).decode()
+
+    def embed(self, ids, offsets):
+        ids = np.ascontiguousarray(ids, dtype=np.int32)
+        offsets = np.ascontiguousarray(offsets, dtype=np.uint64)
+        batch = len(offsets) - 1
+        out = np.zeros((batch, 768), np.float32)
+        err = C.create_string_buffer(512)
+        if not self.lib.eg2link_embed_batch(self.handle, _ptr(ids), _ptr(offsets), batch, _ptr(out), err, 512):
+            raise RuntimeError(err.value.decode())
+        return out
+
+    def close(self):
+        if self.handle:
+            self.lib.eg2link_close(self.handle)
             self.handle = None
 
 

@@ -209,3 +209,24 @@ def test_product_never_imports_the_oracle():
                 src = open(os.path.join(dirpath, f)).read()
                 assert not re.search(r"^\s*(import|from)\s+oracle", src, flags=re.M), f
                 assert "eg2_oracle" not in src and "libeg2ref" not in src, f
+
+
+def test_reference_engine_links_against_library():
+    """The reference's engine.c, compiled unchanged with -DEI_ENABLE_KFD=1
+    against include/ (gemma2_kfd.h forwards to eg2_executor.h), links with
+    libeg2_b200.so: the three executor calls it makes are undefined in the
+    engine object and defined by the library (oracle/Makefile engine_link)."""
+    if not os.path.isdir(os.path.join(REF_ROOT, "vendor")):
+        pytest.skip("reference sources not present")
+    subprocess.run(["make", "-s", "-C", os.path.join(ROOT, "oracle"), "engine_link", f"REF_ROOT={REF_ROOT}"],
+                   check=True)
+    so = os.path.join(ROOT, "oracle", "_ref", "libeg2enginelink.so")
+    needed = subprocess.run(["readelf", "-d", so], capture_output=True, text=True, check=True).stdout
+    assert "[libeg2_b200.so]" in needed
+    syms = subprocess.run(["nm", "-D", so], capture_output=True, text=True, check=True).stdout.split("\n")
+    lib = subprocess.run(["nm", "-D", "--defined-only", os.path.join(ROOT, "embeddinggemma2-amdkfd_b200",
+                                                                      "libeg2_b200.so")],
+                         capture_output=True, text=True, check=True).stdout
+    for fn in ("ei_gemma2_kfd_create", "ei_gemma2_kfd_free", "ei_gemma2_kfd_batch"):
+        assert any(l.split()[-2:] == ["U", fn] for l in syms if l.strip()), fn
+        assert f" T {fn}" in lib, fn

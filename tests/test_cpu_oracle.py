@@ -125,6 +125,25 @@ def test_matryoshka_prefixes_match_reference(eg2):
     assert np.array_equal(eg2.normalize_prefix(e, 768), e)
 
 
+def test_matryoshka_matches_reference_live(eg2, syn):
+    """eg2_b200_normalize_prefix (host C) against the reference's own
+    ei_embedding_normalize_prefix (oracle/_ref) on 200 random unit vectors,
+    every supported width, bit for bit."""
+    import oracle
+    if not os.path.exists(oracle.REF_SO):
+        pytest.skip("oracle/_ref not built")
+    ref = oracle.RefGraph(syn.model_path(1234, "baseline"), 1)
+    try:
+        rng = np.random.default_rng(21)
+        for _ in range(200):
+            e = rng.standard_normal(768).astype(np.float32) * np.float32(rng.uniform(0.01, 3))
+            e /= np.float32(np.linalg.norm(e))
+            for d in (128, 256, 512, 768):
+                assert np.array_equal(eg2.normalize_prefix(e, d), ref.normalize_prefix(e, d)), d
+    finally:
+        ref.close()
+
+
 def test_device_expf_matches_c_library(tmp_path):
     """The expf the parity-mode attention evaluates (csrc/ref_expf.h, shared
     with the device code) equals the C library's expf -- which the reference's
