@@ -34,22 +34,23 @@ def test_mixed_load_bounds(syn):
 
 
 def test_sum_squares_order_is_the_servers(eg2):
-    """Two 4-lane accumulators over 8-element chunks, then a scalar tail
-    (kernels.c:82-93); checked against a plain float32 restatement."""
-    from importlib import import_module
-    ex = import_module("embeddinggemma2-amdkfd_b200.executor")
+    """eg2_b200_normalize_prefix (host C) sums squares with two 4-lane
+    accumulators over 8-element chunks, then (v0 + v2) + (v1 + v3)
+    (kernels.c:35-39,82-93), and scales by 1 / sqrtf(ss); checked against a
+    plain float32 restatement at every prefix width."""
     rng = np.random.default_rng(3)
-    for n in (8, 13, 128, 131, 512):
-        row = rng.standard_normal(n).astype(np.float32)
-        lanes = [np.float32(0)] * 8
-        for c in range(n // 8):
-            for i in range(8):
-                lanes[i] = np.float32(lanes[i] + np.float32(row[8 * c + i] * row[8 * c + i]))
-        v = [np.float32(lanes[i] + lanes[4 + i]) for i in range(4)]
-        ss = np.float32(np.float32(v[0] + v[2]) + np.float32(v[1] + v[3]))
-        for z in range(n // 8 * 8, n):
-            ss = np.float32(ss + np.float32(row[z] * row[z]))
-        assert ex._sum_squares_sse2(row) == ss
+    for _ in range(20):
+        emb = (rng.standard_normal(768) * rng.uniform(0.1, 4)).astype(np.float32)
+        for n in (128, 256, 512):
+            row = emb[:n]
+            lanes = [np.float32(0)] * 8
+            for c in range(n // 8):
+                for i in range(8):
+                    lanes[i] = np.float32(lanes[i] + np.float32(row[8 * c + i] * row[8 * c + i]))
+            v = [np.float32(lanes[i] + lanes[4 + i]) for i in range(4)]
+            ss = np.float32(np.float32(v[0] + v[2]) + np.float32(v[1] + v[3]))
+            expect = (row * np.float32(np.float32(1.0) / np.sqrt(ss, dtype=np.float32))).astype(np.float32)
+            np.testing.assert_array_equal(eg2.normalize_prefix(emb, n), expect)
 
 
 def test_normalize_prefix_rejects_other_sizes(eg2):
