@@ -662,9 +662,25 @@ def test_ple_proj_vs_reference(ops, port, model_baseline):
     np.testing.assert_allclose(got, ref, atol=5e-4, rtol=2e-4)
 
 
+def _sum_squares_sse2(row):
+    """kernels.c:35-39,82-93 order: two 4-lane float accumulators over
+    8-element chunks, then (v0 + v2) + (v1 + v3), then a scalar tail."""
+    sq = (row * row).astype(np.float32)
+    n8 = sq.size // 8 * 8
+    s0 = np.zeros(4, np.float32)
+    s1 = np.zeros(4, np.float32)
+    for c in range(0, n8, 8):
+        s0 = (s0 + sq[c:c + 4]).astype(np.float32)
+        s1 = (s1 + sq[c + 4:c + 8]).astype(np.float32)
+    v = (s0 + s1).astype(np.float32)
+    ss = np.float32(np.float32(v[0] + v[2]) + np.float32(v[1] + v[3]))
+    for z in range(n8, sq.size):
+        ss = np.float32(ss + sq[z])
+    return ss
+
+
 def _pool_l2_ref(y, off):
-    from importlib import import_module
-    sumsq = import_module("embeddinggemma2-amdkfd_b200.executor")._sum_squares_sse2
+    sumsq = _sum_squares_sse2
     out = []
     for s in range(len(off) - 1):
         lo, hi = int(off[s]), int(off[s + 1])
