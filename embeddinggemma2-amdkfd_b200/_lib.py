@@ -157,12 +157,12 @@ class EgQ8GeGLU(C.Structure):
 
 
 class EgQ8MMF16(C.Structure):
-    _fields_ = [("out", P), ("xq", P), ("xs", P), ("xs_stride", u32), ("wh", P), ("wl", P), ("rowscale", P),
+    _fields_ = [("out", P), ("xh", P), ("xl", P), ("wh", P), ("wl", P), ("rowscale", P),
                 ("n", u32), ("k", u32), ("m", u32), ("splits", u32), ("split_stride", C.c_uint64)]
 
 
 class EgQ8GeGLUF16(C.Structure):
-    _fields_ = [("q", P), ("scale", P), ("scale_stride", u32), ("xq", P), ("xs", P), ("xs_stride", u32), ("wh", P),
+    _fields_ = [("out_h", P), ("out_l", P), ("scale", P), ("scale_stride", u32), ("xh", P), ("xl", P), ("wh", P),
                 ("wl", P), ("rowscale", P), ("n", u32), ("k", u32), ("m", u32), ("tier", u32)]
 
 

@@ -53,12 +53,12 @@ struct AttnTcParams {
     const unsigned *bounds;  // [n][2] = sequence [lo, hi)
     int n, window;
     // Optional Q8_0 output instead of out (ROW_QUANT of the attention row,
-    // gemma2_fast.c:728-730, fused): codes [n][4d] (int8, or with codes_f16 the
-    // codes' fp16 values), scales block-major [4d/32][q_stride]; quantizer
-    // rounding of `tier`.
-    void *q;
+    // gemma2_fast.c:728-730, fused): int8 codes [n][4d] in q, or with q_lo set
+    // the dequantized split (Q8Split, common.cuh): hi plane in q, lo plane in
+    // q_lo; scales block-major [4d/32][q_stride]; quantizer rounding of `tier`.
+    void *q, *q_lo;
     float *qs;
-    int q_stride, tier, codes_f16;
+    int q_stride, tier;
 };
 
 template <int D_>
@@ -369,10 +369,11 @@ __global__ void __launch_bounds__(AttnTcCfgD<D_>::THREADS, 1)
                         }
                         if (t < p.n) {
                             const size_t at = size_t(t) * (4 * C::D) + col0 + c;
-                            if (p.codes_f16) {
-                                __half *dst = static_cast<__half *>(p.q) + at;
+                            if (p.q_lo) {
+                                const float ds = fp16_bits_to_f32(ref_fp32_to_fp16(d));
+                                const Q8Split o{static_cast<__half *>(p.q), static_cast<__half *>(p.q_lo)};
 #pragma unroll
-                                for (int e = 0; e < 8; ++e) store_codes4(dst, e, w[e]);
+                                for (int e = 0; e < 8; ++e) store4(o, at, e, w[e], ds);
                             } else {
                                 uint4 *dst = reinterpret_cast<uint4 *>(static_cast<int8_t *>(p.q) + at);
                                 dst[0] = make_uint4(w[0], w[1], w[2], w[3]);

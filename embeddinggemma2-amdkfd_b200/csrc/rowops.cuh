@@ -109,8 +109,8 @@ __device__ __forceinline__ double cta_sum_d(double v, double *red) {
 
 // ROW_NORM_QUANT (gemma2_fast.c:685-691): RMS norm with weight w, then Q8_0.
 // CTA per row, one float4 per thread (WIDTH / 4 threads).
-template <int WIDTH, typename CodeT>
-__global__ void __launch_bounds__(WIDTH / 4) norm_quant_kernel(CodeT *__restrict__ q, float *__restrict__ qs,
+template <int WIDTH, typename Out>
+__global__ void __launch_bounds__(WIDTH / 4) norm_quant_kernel(const Out q, float *__restrict__ qs,
                                                                int qs_stride, float *__restrict__ y,
                                                                const float *__restrict__ x,
                                                                const float *__restrict__ w, int tier) {
@@ -124,14 +124,15 @@ __global__ void __launch_bounds__(WIDTH / 4) norm_quant_kernel(CodeT *__restrict
     v = scale_w4(v, sc, reinterpret_cast<const float4 *>(w)[i]);
     if (y) reinterpret_cast<float4 *>(y + size_t(t) * WIDTH)[i] = v;
     float s;
-    store_codes4(q + size_t(t) * WIDTH, i, quant_oct(v, &s, tier));
+    const uint32_t c = quant_oct(v, &s, tier);
+    store4(q, size_t(t) * WIDTH, i, c, s);
     if ((lane & 7) == 0) qs[size_t(i >> 3) * qs_stride + t] = s;
 }
 
 // ROW_QUANT (gemma2_fast.c:728-730): Q8_0 of rows of width `width` (a multiple
 // of 128).  Warp per (row, four blocks).
-template <typename CodeT>
-__global__ void quant_rows_kernel(CodeT *__restrict__ q, float *__restrict__ qs, int qs_stride,
+template <typename Out>
+__global__ void quant_rows_kernel(const Out q, float *__restrict__ qs, int qs_stride,
                                   const float *__restrict__ x, int rows, int width, int tier) {
     pdl_wait();
     pdl_trigger();
@@ -141,7 +142,8 @@ __global__ void quant_rows_kernel(CodeT *__restrict__ q, float *__restrict__ qs,
     const int t = gw / steps, st = gw % steps;
     const size_t c = size_t(t) * (width / 4) + st * 32 + lane;
     float s;
-    store_codes4(q, int(c), quant_oct(reinterpret_cast<const float4 *>(x)[c], &s, tier));
+    const uint32_t codes = quant_oct(reinterpret_cast<const float4 *>(x)[c], &s, tier);
+    store4(q, 0, int(c), codes, s);
     if ((lane & 7) == 0) qs[size_t(4 * st + (lane >> 3)) * qs_stride + t] = s;
 }
 
@@ -228,10 +230,10 @@ __global__ void qkv_post_kernel(OutT *__restrict__ qo, OutT *__restrict__ ko, Ou
 // CTA of 128 threads per 512-wide row, one float4 per thread.  h may be a
 // split-K GEMM output: `parts` partial rows part_stride floats apart, summed
 // in order.
-template <typename CodeT>
+template <typename Out>
 __global__ void __launch_bounds__(128) post_add_kernel(float *__restrict__ x, const float *__restrict__ h,
                                                        const float *__restrict__ w, const float *__restrict__ scale,
-                                                       CodeT *__restrict__ q, float *__restrict__ qs, int qs_stride,
+                                                       const Out q, float *__restrict__ qs, int qs_stride,
                                                        const float *__restrict__ next_w, int tier, int parts,
                                                        size_t part_stride) {
     pdl_wait();
@@ -252,7 +254,8 @@ __global__ void __launch_bounds__(128) post_add_kernel(float *__restrict__ x, co
         xv = scale_w4(xv, sc2, reinterpret_cast<const float4 *>(next_w)[i]);
     }
     float s;
-    store_codes4(q + size_t(t) * 512, i, quant_oct(xv, &s, tier));
+    const uint32_t c = quant_oct(xv, &s, tier);
+    store4(q, size_t(t) * 512, i, c, s);
     if ((lane & 7) == 0) qs[size_t(i >> 3) * qs_stride + t] = s;
 }
 
@@ -262,8 +265,8 @@ __global__ void __launch_bounds__(128) post_add_kernel(float *__restrict__ x, co
 // the GELU and rounding at compile time (no branch per element).
 // x may be a split-K GEMM output (`parts` partials part_stride floats apart,
 // summed in order).
-template <int TIER, typename CodeT>
-__global__ void gate_quant_kernel(CodeT *__restrict__ q, float *__restrict__ qs, int qs_stride,
+template <int TIER, typename Out>
+__global__ void gate_quant_kernel(const Out q, float *__restrict__ qs, int qs_stride,
                                   const float *__restrict__ x, const float *__restrict__ other, int rows, int width,
                                   int other_stride, int other_offset, int parts, size_t part_stride) {
     constexpr int tier = TIER;
@@ -275,7 +278,7 @@ __global__ void gate_quant_kernel(CodeT *__restrict__ q, float *__restrict__ qs,
     if (gw >= rows * wpr) return;  // warp-uniform
     const int t = gw / wpr, i0 = (gw % wpr) * PER;
     const float4 *orow = reinterpret_cast<const float4 *>(other + size_t(t) * other_stride + other_offset);
-    CodeT *qr = q + size_t(t) * width;
+    const size_t qr = size_t(t) * width;
     float4 xv[PER], ov[PER];
 #pragma unroll
     for (int i = 0; i < PER; ++i)
@@ -290,7 +293,8 @@ __global__ void gate_quant_kernel(CodeT *__restrict__ q, float *__restrict__ qs,
                                      __fmul_rn(gelu_tier(xv[i].z, tier), ov[i].z),
                                      __fmul_rn(gelu_tier(xv[i].w, tier), ov[i].w));
         float sc;
-        store_codes4(qr, (i0 + i) * 32 + lane, quant_oct(g, &sc, tier));
+        const uint32_t c = quant_oct(g, &sc, tier);
+        store4(q, qr, (i0 + i) * 32 + lane, c, sc);
         if ((lane & 7) == 0) qs[size_t(4 * (i0 + i) + (lane >> 3)) * qs_stride + t] = sc;
     }
 }

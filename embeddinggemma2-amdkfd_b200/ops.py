@@ -94,13 +94,14 @@ def split_q8_weight(codes, scales, rows, k, wh, wl, rowscale):
         raise RuntimeError(f"eg2_split_q8_weight failed with CUDA error {rc}")
 
 
-def q8_mm_f16(out, xq16, xs, xs_stride, wh, wl, rowscale, n, k, m, splits=1, split_stride=0):
-    _call("eg2_launch_q8_mm_f16", _lib.EgQ8MMF16(_p(out), _p(xq16), _p(xs), xs_stride, _p(wh), _p(wl), _p(rowscale),
+def q8_mm_f16(out, xh, xl, wh, wl, rowscale, n, k, m, splits=1, split_stride=0):
+    """EgQ8MMF16: activations as split fp16 planes xh, xl; weights split by split_q8_weight."""
+    _call("eg2_launch_q8_mm_f16", _lib.EgQ8MMF16(_p(out), _p(xh), _p(xl), _p(wh), _p(wl), _p(rowscale),
                                                  n, k, m, splits, split_stride))
 
 
-def q8_geglu_f16(q16, scale, scale_stride, xq16, xs, xs_stride, wh, wl, rowscale, n, k, m, tier=0):
-    _call("eg2_launch_q8_geglu_f16", _lib.EgQ8GeGLUF16(_p(q16), _p(scale), scale_stride, _p(xq16), _p(xs), xs_stride,
+def q8_geglu_f16(out_h, out_l, scale, scale_stride, xh, xl, wh, wl, rowscale, n, k, m, tier=0):
+    _call("eg2_launch_q8_geglu_f16", _lib.EgQ8GeGLUF16(_p(out_h), _p(out_l), _p(scale), scale_stride, _p(xh), _p(xl),
                                                        _p(wh), _p(wl), _p(rowscale), n, k, m, tier))
 
 

@@ -240,21 +240,34 @@ def _split_weight(ops, wq, wd):
 
 
 def _exact_q8_product(xq, xd, wq, wd):
-    """sum_b D_b * ws_b * xs_b in float64 (every term exact)."""
+    """sum_b D_b * ws_b * xs_b in float64, block by block (every term exact)."""
     n, k = xq.shape
-    D = (xq.astype(np.int64).reshape(n, 1, k // 32, 32) *
-         wq.astype(np.int64).reshape(1, -1, k // 32, 32)).sum(-1).astype(np.float64)
-    return (D * f16_to_f32(xd).astype(np.float64)[:, None, :] * f16_to_f32(wd).astype(np.float64)[None, :, :]).sum(-1)
+    xs, ws = f16_to_f32(xd).astype(np.float64), f16_to_f32(wd).astype(np.float64)
+    out = np.zeros((n, wq.shape[0]), np.float64)
+    for b in range(k // 32):
+        D = xq[:, 32 * b:32 * b + 32].astype(np.float64) @ wq[:, 32 * b:32 * b + 32].astype(np.float64).T
+        out += D * xs[:, b:b + 1] * ws[:, b][None, :]
+    return out
 
 
-def _gpu_q8_mm_f16(ops, xq, xd, wq, wd, stride, splits=1):
+def _split_activation(xq, xd):
+    """The fast path's activation operand: d * q (exact in float32) split into
+    fp16 hi = fp16(d * q) and lo = fp16(d * q - hi), [n][k] each."""
+    n, k = xq.shape
+    v = (f16_to_f32(xd).repeat(32, axis=1) * xq.astype(np.float32)).astype(np.float32)
+    hi = v.astype(np.float16)
+    lo = (v - hi.astype(np.float32)).astype(np.float16)
+    assert np.array_equal(hi.astype(np.float64) + lo.astype(np.float64), v.astype(np.float64))
+    return hi, lo
+
+
+def _gpu_q8_mm_f16(ops, xq, xd, wq, wd, splits=1):
     n, k = xq.shape
     m = wq.shape[0]
-    xs = np.zeros((k // 32, stride), np.float32)
-    xs[:, :n] = f16_to_f32(xd).T
+    hi, lo = _split_activation(xq, xd)
     wh, wl, rs = _split_weight(ops, wq, wd)
     out = torch.zeros(splits * n * m, device=DEV)
-    ops.q8_mm_f16(out, T(xq).half(), T(xs), stride, wh, wl, rs, n, k, m, splits, n * m)
+    ops.q8_mm_f16(out, T(hi), T(lo), wh, wl, rs, n, k, m, splits, n * m)
     return host(out).reshape(splits, n, m)
 
 
@@ -284,7 +297,7 @@ def test_q8_mm_f16_within_tolerance(ops, n, k, m):
     rng = np.random.default_rng(n * 7 + k + m + 3)
     xq, xd = _q8_operands(rng, n, k)
     wq, wd = _q8_operands(rng, m, k)
-    got = _gpu_q8_mm_f16(ops, xq, xd, wq, wd, ((n + 127) // 128) * 128)[0]
+    got = _gpu_q8_mm_f16(ops, xq, xd, wq, wd)[0]
     ref = _exact_q8_product(xq, xd, wq, wd)
     err = np.abs(got - ref).max() / np.abs(ref).max()
     print(f"f16 GEMM {n}x{k}x{m}: max error / range {err:.2e}")
@@ -300,47 +313,53 @@ def test_q8_mm_f16_split_k_partials_add_up(ops, n, k, m, splits):
     rng = np.random.default_rng(n + k + m + splits)
     xq, xd = _q8_operands(rng, n, k)
     wq, wd = _q8_operands(rng, m, k)
-    stride = ((n + 127) // 128) * 128
-    parts = _gpu_q8_mm_f16(ops, xq, xd, wq, wd, stride, splits)
+    parts = _gpu_q8_mm_f16(ops, xq, xd, wq, wd, splits)
     total = parts[0].copy()
     for i in range(1, splits):
         total = (total + parts[i]).astype(np.float32)
     ref = _exact_q8_product(xq, xd, wq, wd)
     assert np.abs(total - ref).max() / np.abs(ref).max() < 2e-6
-    kb = k // 32 // splits
-    first = _gpu_q8_mm_f16(ops, xq[:, :kb * 32].copy(), xd[:, :kb].copy(), wq[:, :kb * 32].copy(), wd[:, :kb].copy(),
-                           stride)[0]
+    kk = k // splits
+    first = _gpu_q8_mm_f16(ops, xq[:, :kk].copy(), xd[:, :kk // 32].copy(), wq[:, :kk].copy(),
+                           wd[:, :kk // 32].copy())[0]
     np.testing.assert_array_equal(parts[0], first)
 
 
 @pytest.mark.parametrize("n,k,m,tier", [(130, 512, 2048, 0), (2048, 512, 2048, 0), (300, 512, 2048, 1)])
 def test_q8_geglu_f16_equals_unfused(ops, n, k, m, tier):
-    """The fused fp16 GeGLU GEMM (gelu(gate) * up and Q8_0 in the epilogue,
-    fp16 codes out) reproduces q8_mm_f16(gate), q8_mm_f16(up), gate_quant bit
-    for bit."""
+    """The fused fp16 GeGLU GEMM (gate/up interleaved in 32-row chunks;
+    gelu(gate) * up and Q8_0 in the epilogue, the result written as the split
+    fp16 planes of the down operand) reproduces q8_mm_f16(gate),
+    q8_mm_f16(up), gate_quant bit for bit: the same codes (hi + lo = d * q
+    exactly) and scales."""
     rng = np.random.default_rng(n + k + m + 5)
     xq, xd = _q8_operands(rng, n, k)
     gq, gd = _q8_operands(rng, m, k)
     uq, ud = _q8_operands(rng, m, k)
     stride = (n + 127) // 128 * 128
-    xs = np.zeros((k // 32, stride), np.float32)
-    xs[:, :n] = f16_to_f32(xd).T
-    gate = torch.from_numpy(_gpu_q8_mm_f16(ops, xq, xd, gq, gd, stride)[0]).to(DEV)
-    up = torch.from_numpy(_gpu_q8_mm_f16(ops, xq, xd, uq, ud, stride)[0]).to(DEV)
+    gate = torch.from_numpy(_gpu_q8_mm_f16(ops, xq, xd, gq, gd)[0]).to(DEV)
+    up = torch.from_numpy(_gpu_q8_mm_f16(ops, xq, xd, uq, ud)[0]).to(DEV)
     q_ref = torch.zeros(n * m, dtype=torch.int8, device=DEV)
     s_ref = torch.zeros(m // 32 * stride, device=DEV)
     ops.gate_quant(q_ref, s_ref, stride, gate.ravel(), up.ravel(), n, m, m, 0, tier=tier)
     wq = np.zeros((2 * m, k), np.int8)
     wd = np.zeros((2 * m, k // 32), np.uint16)
-    for c in range(m // 64):
-        wq[128 * c:128 * c + 64], wd[128 * c:128 * c + 64] = gq[64 * c:64 * c + 64], gd[64 * c:64 * c + 64]
-        wq[128 * c + 64:128 * c + 128], wd[128 * c + 64:128 * c + 128] = uq[64 * c:64 * c + 64], ud[64 * c:64 * c + 64]
+    for c in range(m // 32):
+        wq[64 * c:64 * c + 32], wd[64 * c:64 * c + 32] = gq[32 * c:32 * c + 32], gd[32 * c:32 * c + 32]
+        wq[64 * c + 32:64 * c + 64], wd[64 * c + 32:64 * c + 64] = uq[32 * c:32 * c + 32], ud[32 * c:32 * c + 32]
     wh, wl, rs = _split_weight(ops, wq, wd)
-    q16 = torch.zeros(n * m, dtype=torch.float16, device=DEV)
+    hi, lo = _split_activation(xq, xd)
+    oh = torch.zeros(n * m, dtype=torch.float16, device=DEV)
+    ol = torch.zeros(n * m, dtype=torch.float16, device=DEV)
     sc = torch.zeros(m // 32 * stride, device=DEV)
-    ops.q8_geglu_f16(q16, sc, stride, T(xq).half(), T(xs), stride, wh, wl, rs, n, k, m, tier=tier)
-    np.testing.assert_array_equal(host(q16).astype(np.int32), host(q_ref).astype(np.int32))
-    np.testing.assert_array_equal(host(sc).reshape(-1, stride)[:, :n], host(s_ref).reshape(-1, stride)[:, :n])
+    ops.q8_geglu_f16(oh, ol, sc, stride, T(hi), T(lo), wh, wl, rs, n, k, m, tier=tier)
+    scales = host(sc).reshape(-1, stride)[:, :n]
+    np.testing.assert_array_equal(scales, host(s_ref).reshape(-1, stride)[:, :n])
+    v = host(oh).astype(np.float64) + host(ol).astype(np.float64)
+    d = np.repeat(scales.T.astype(np.float64), 32, axis=1).ravel()
+    codes = np.where(d != 0, v / np.where(d != 0, d, 1), 0)
+    np.testing.assert_array_equal(codes, np.round(codes))
+    np.testing.assert_array_equal(codes.astype(np.int32), host(q_ref).astype(np.int32))
 
 
 @pytest.mark.parametrize("n,k,m,exact,tier", [(130, 512, 2048, False, 0), (2048, 512, 2048, False, 0),
