@@ -57,9 +57,6 @@ SIGNATURES = {
     "eg2_launch_norm_quant": (i32, [vp, vp]),
     "eg2_launch_q8_mm": (i32, [vp, vp]),
     "eg2_launch_q8_geglu": (i32, [vp, vp]),
-    "eg2_launch_q8_mm_f16": (i32, [vp, vp]),
-    "eg2_launch_q8_geglu_f16": (i32, [vp, vp]),
-    "eg2_split_q8_weight": (i32, [vp, vp, u32, u32, vp, vp, vp, vp]),
     "eg2_launch_qkv_post": (i32, [vp, vp]),
     "eg2_launch_attention_f16": (i32, [vp, vp]),
     "eg2_launch_attention_tc": (i32, [vp, vp]),
@@ -156,16 +153,6 @@ class EgQ8GeGLU(C.Structure):
                 ("ws", P), ("n", u32), ("k", u32), ("m", u32), ("exact", u32), ("tier", u32)]
 
 
-class EgQ8MMF16(C.Structure):
-    _fields_ = [("out", P), ("xh", P), ("xl", P), ("wh", P), ("wl", P), ("rowscale", P),
-                ("n", u32), ("k", u32), ("m", u32), ("splits", u32), ("split_stride", C.c_uint64)]
-
-
-class EgQ8GeGLUF16(C.Structure):
-    _fields_ = [("out_h", P), ("out_l", P), ("scale", P), ("scale_stride", u32), ("xh", P), ("xl", P), ("wh", P),
-                ("wl", P), ("rowscale", P), ("n", u32), ("k", u32), ("m", u32), ("tier", u32)]
-
-
 class EgQkvPost(C.Structure):
     _fields_ = [("q", P), ("k", P), ("v", P), ("qkv", P), ("q_norm", P), ("k_norm", P),
                 ("rope_cos", P), ("rope_sin", P), ("pos", P), ("n", u32), ("d", u32)]
@@ -200,5 +187,5 @@ class EgPoolL2(C.Structure):
 
 
 STRUCTS = {c.__name__: c for c in (EgGather, EgMM, EgNorm, EgRope, EgAttention, EgElement, EgPool, EgNormResidual,
-                                   EgNormRope, EgEmbed, EgPleProj, EgNormQuant, EgQ8MM, EgQ8GeGLU, EgQ8MMF16, EgQ8GeGLUF16, EgQkvPost, EgAttentionF16,
+                                   EgNormRope, EgEmbed, EgPleProj, EgNormQuant, EgQ8MM, EgQ8GeGLU, EgQkvPost, EgAttentionF16,
                                    EgPostAdd, EgGateQuant, EgGeluMul, EgPoolL2)}

@@ -53,10 +53,9 @@ struct AttnTcParams {
     const unsigned *bounds;  // [n][2] = sequence [lo, hi)
     int n, window;
     // Optional Q8_0 output instead of out (ROW_QUANT of the attention row,
-    // gemma2_fast.c:728-730, fused): int8 codes [n][4d] in q, or with q_lo set
-    // the dequantized split (Q8Split, common.cuh): hi plane in q, lo plane in
-    // q_lo; scales block-major [4d/32][q_stride]; quantizer rounding of `tier`.
-    void *q, *q_lo;
+    // gemma2_fast.c:728-730, fused): codes [n][4d], scales block-major
+    // [4d/32][q_stride]; quantizer rounding of `tier`.
+    int8_t *q;
     float *qs;
     int q_stride, tier;
 };
@@ -368,17 +367,9 @@ __global__ void __launch_bounds__(AttnTcCfgD<D_>::THREADS, 1)
                                 w[e] |= q8_code(__uint_as_float(r[4 * e + b]) * il, id, p.tier) << (8 * b);
                         }
                         if (t < p.n) {
-                            const size_t at = size_t(t) * (4 * C::D) + col0 + c;
-                            if (p.q_lo) {
-                                const float ds = fp16_bits_to_f32(ref_fp32_to_fp16(d));
-                                const Q8Split o{static_cast<__half *>(p.q), static_cast<__half *>(p.q_lo)};
-#pragma unroll
-                                for (int e = 0; e < 8; ++e) store4(o, at, e, w[e], ds);
-                            } else {
-                                uint4 *dst = reinterpret_cast<uint4 *>(static_cast<int8_t *>(p.q) + at);
-                                dst[0] = make_uint4(w[0], w[1], w[2], w[3]);
-                                dst[1] = make_uint4(w[4], w[5], w[6], w[7]);
-                            }
+                            uint4 *dst = reinterpret_cast<uint4 *>(p.q + size_t(t) * (4 * C::D) + col0 + c);
+                            dst[0] = make_uint4(w[0], w[1], w[2], w[3]);
+                            dst[1] = make_uint4(w[4], w[5], w[6], w[7]);
                             p.qs[size_t((col0 + c) / 32) * p.q_stride + t] = fp16_bits_to_f32(ref_fp32_to_fp16(d));
                         }
                     }

@@ -321,41 +321,6 @@ __device__ __forceinline__ uint32_t q8_code(float x, float id, int tier = TIER_X
     q = q < -128 ? -128 : (q > 127 ? 127 : q);
     return uint32_t(q) & 0xFFu;
 }
-// A Q8_0 operand leaves the quantizers in one of two forms:
-//   Q8Codes  -- int8 codes (the exact int8 GEMM's operand; the block scales
-//               go to the caller's fp32 scale plane);
-//   Q8Split  -- the dequantized values d * q, each split exactly into two
-//               fp16 planes, hi = fp16(d * q) and lo = fp16(d * q - hi) (the
-//               fast path's fp16 GEMM operand, f16gemm.cuh): d is an fp16
-//               value and |q| <= 128, so d * q is exact in fp32 with at most
-//               18 significant bits and hi + lo == d * q.
-// store4(o, row, i, c, d) writes the four codes packed in c (byte b = code
-// 4i + b) of the row starting at element `row`, with block scale d.
-struct Q8Codes {
-    int8_t *q;
-};
-struct Q8Split {
-    __half *hi, *lo;
-};
-__device__ __forceinline__ void store4(const Q8Codes &o, size_t row, int i, uint32_t c, float) {
-    reinterpret_cast<uint32_t *>(o.q + row)[i] = c;
-}
-__device__ __forceinline__ void store4(const Q8Split &o, size_t row, int i, uint32_t c, float d) {
-    uint32_t hw[2], lw[2];
-#pragma unroll
-    for (int e = 0; e < 2; ++e) {
-        const float v0 = __fmul_rn(d, float(int(int8_t(uint8_t(c >> (16 * e))))));
-        const float v1 = __fmul_rn(d, float(int(int8_t(uint8_t(c >> (16 * e + 8))))));
-        const __half h0 = __float2half_rn(v0), h1 = __float2half_rn(v1);
-        const __half2 hh = __halves2half2(h0, h1);
-        const __half2 ll = __halves2half2(__float2half_rn(__fsub_rn(v0, __half2float(h0))),
-                                          __float2half_rn(__fsub_rn(v1, __half2float(h1))));
-        hw[e] = *reinterpret_cast<const uint32_t *>(&hh);
-        lw[e] = *reinterpret_cast<const uint32_t *>(&ll);
-    }
-    reinterpret_cast<uint2 *>(o.hi + row)[i] = make_uint2(hw[0], hw[1]);
-    reinterpret_cast<uint2 *>(o.lo + row)[i] = make_uint2(lw[0], lw[1]);
-}
 // exp(x) by Cody-Waite reduction and a degree-6 polynomial: the reference's own
 // x86 GELU helper (gemma2_fast_x86.c:291-306), evaluated with the same fused
 // and unfused operations so that results match it bit for bit.

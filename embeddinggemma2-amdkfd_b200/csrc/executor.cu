@@ -84,13 +84,6 @@ struct Q8Weight {
     float *scales = nullptr;  // [k/32][rows]
     int rows = 0, k = 0;
     CUtensorMap tmap{}, tscale{};
-    // Fast path: the weight dequantized and split exactly into two fp16 planes,
-    // w * 2^s_r = wh + wl [rows][k], and rowscale[r] = 2^-s_r (f16gemm.cuh);
-    // bn: the weight rows of one GEMM tile (the maps' box height).
-    void *wh = nullptr, *wl = nullptr;
-    float *rowscale = nullptr;
-    CUtensorMap twh{}, twl{};
-    int bn = 256;
 };
 
 struct Layer {
@@ -140,14 +133,6 @@ struct Backend {
     void *x_hi = nullptr, *x_lo = nullptr, *qh = nullptr, *kh = nullptr, *vh = nullptr;
     int8_t *xq = nullptr, *gq = nullptr;  // Q8 activations; gq/gs: the GeGLU output (FFN down operand)
     CUtensorMap tm_xq[3]{}, tm_xs[3]{}, tm_gq{}, tm_gs{}, tm_hi{}, tm_lo{}, tm_ple{};
-    // Fast path: the Q8 activations dequantized and split into fp16 planes
-    // (xh, xl: the fp16 GEMM's operand; gh, gl: the GeGLU output, ffn_down's
-    // operand), their maps per depth K, and split-K partial sums of the
-    // 512-wide projections in h ([SPLITS][cap][512]).
-    static constexpr int SPLITS = 2;
-    void *xh16 = nullptr, *xl16 = nullptr, *gh16 = nullptr, *gl16 = nullptr;
-    CUtensorMap tm_xh[3]{}, tm_xl[3]{}, tm_gh{}, tm_gl{};
-    size_t h_part = 0;
     // Parity mode (EG2_B200_EXACT): GEMMs in the reference scalar tile's rounding
     // order, PLE projection and attention on the CUDA-core exact-order kernels
     // with fp32 q/k/v; every other kernel is bit-exact in both modes.
@@ -232,16 +217,13 @@ struct Backend {
     // Gate and up matrices [rows][k] into one weight interleaved in 64-row chunks
     // (the fused GeGLU GEMM's layout): rows 128c.. = gate rows 64c.., rows
     // 128c+64.. = up rows 64c...
-    // The interleave is 64-row chunks for the int8 GeGLU kernel (parity mode)
-    // and 32-row chunks for the fp16 one (a whole Q8_0 output block per thread).
     void repack_geglu(const std::string &gate, const std::string &up, int k, int rows, Q8Weight &w,
                       uint8_t *staging) {
         for (int half = 0; half < 2; ++half) {
             const ei_tensor *t = tensor(half ? up : gate);
             check_shape(t, uint64_t(k), uint64_t(rows), 8, half ? up : gate);
             ck(cudaMemcpyAsync(staging, t->data, t->n_bytes, cudaMemcpyHostToDevice, stream), "weight upload");
-            ck(launch_repack_q8(staging, rows, k, w.codes, w.scales, w.rows, stream, exact ? 64 : 32, half),
-               "repack");
+            ck(launch_repack_q8(staging, rows, k, w.codes, w.scales, w.rows, stream, 64, half), "repack");
             ck(cudaStreamSynchronize(stream), "repack sync");
         }
     }
@@ -253,17 +235,6 @@ struct Backend {
     void finish_q8(Q8Weight &w) {
         if (w.rows % 128 || !q8_tmap(&w.tmap, w.codes, uint64_t(w.k), uint64_t(w.rows), 128) ||
             !scale_tmap(&w.tscale, w.scales, uint64_t(w.rows), uint64_t(w.k / 32), 128))
-            throw std::runtime_error("cuTensorMapEncodeTiled failed for a weight");
-        if (exact) return;
-        // 512- and 768-wide projections: 128-row tiles (and split K) for enough
-        // tiles; the wide ones: 256-row tiles.
-        w.bn = w.rows % 256 == 0 && w.rows >= 2048 ? 256 : 128;
-        w.wh = dalloc<uint16_t>(size_t(w.rows) * w.k);
-        w.wl = dalloc<uint16_t>(size_t(w.rows) * w.k);
-        w.rowscale = dalloc<float>(size_t(w.rows));
-        ck(launch_split_q8(w.codes, w.scales, w.rows, w.rows, w.k, w.wh, w.wl, w.rowscale, stream), "weight split");
-        if (!f16_tmap(&w.twh, w.wh, uint64_t(w.k), uint64_t(w.rows), uint32_t(w.bn)) ||
-            !f16_tmap(&w.twl, w.wl, uint64_t(w.k), uint64_t(w.rows), uint32_t(w.bn)))
             throw std::runtime_error("cuTensorMapEncodeTiled failed for a weight");
     }
 
@@ -381,8 +352,7 @@ struct Backend {
         kh = dalloc<uint16_t>(size_t(cap) * 512);
         vh = dalloc<uint16_t>(size_t(cap) * 512);
         attn = dalloc<float>(size_t(cap) * 2048);
-        h_part = size_t(cap) * 512;
-        h = dalloc<float>(SPLITS * h_part);
+        h = dalloc<float>(size_t(cap) * 512);
         gq = dalloc<int8_t>(size_t(cap) * 2048);
         gs = dalloc<float>(size_t(64) * cap);
         y = dalloc<float>(size_t(cap) * 768);
@@ -399,18 +369,6 @@ struct Backend {
                 throw std::runtime_error("tensor map (activations)");
         if (!q8_tmap(&tm_gq, gq, 2048, cap, 64) || !scale_tmap(&tm_gs, gs, cap, 64, 64))
             throw std::runtime_error("tensor map (GeGLU activations)");
-        if (!exact) {
-            xh16 = dalloc<uint16_t>(size_t(cap) * 2048);
-            xl16 = dalloc<uint16_t>(size_t(cap) * 2048);
-            gh16 = dalloc<uint16_t>(size_t(cap) * 2048);
-            gl16 = dalloc<uint16_t>(size_t(cap) * 2048);
-            for (int i = 0; i < 3; ++i)
-                if (!f16_tmap(&tm_xh[i], xh16, uint64_t(ks[i]), cap, 128) ||
-                    !f16_tmap(&tm_xl[i], xl16, uint64_t(ks[i]), cap, 128))
-                    throw std::runtime_error("tensor map (fp16 activations)");
-            if (!f16_tmap(&tm_gh, gh16, 2048, cap, 128) || !f16_tmap(&tm_gl, gl16, 2048, cap, 128))
-                throw std::runtime_error("tensor map (fp16 GeGLU activations)");
-        }
         if (!bf16_tmap(&tm_hi, x_hi, 512, cap, 128) || !bf16_tmap(&tm_lo, x_lo, 512, cap, 128) ||
             !bf16_tmap(&tm_ple, ple_w, 512, 24 * 512, 256))
             throw std::runtime_error("tensor map (PLE)");
@@ -448,26 +406,11 @@ struct Backend {
     }
 
     static int kidx(int k) { return k == 512 ? 0 : k == 1024 ? 1 : 2; }
-    // The projection of the current Q8 activations (xq / xh16 + xl16) by w.  Parity
-    // mode: the exact int8 kernel.  Fast path: the fp16 kernel, split over K
-    // in `splits` partial sums at out + i * h_part when splits > 1.
-    void gemm(const Q8Weight &w, float *out, int ldo, int n, cudaStream_t s, int splits = 1) {
-        if (exact) {
-            ck(launch_q8gemm(w.tmap, tm_xq[kidx(w.k)], w.tscale, tm_xs[kidx(w.k)], true, out, ldo, n, w.rows, w.k, s),
-               "q8 GEMM");
-            return;
-        }
-        ck(launch_f16gemm(tm_xh[kidx(w.k)], tm_xl[kidx(w.k)], w.twh, w.twl, w.bn, w.rowscale, out, ldo, h_part, splits,
-                          n, w.rows, w.k, s),
-           "fp16 GEMM");
+    void gemm(const Q8Weight &w, float *out, int ldo, int n, cudaStream_t s) {
+        ck(launch_q8gemm(w.tmap, tm_xq[kidx(w.k)], w.tscale, tm_xs[kidx(w.k)], exact, out, ldo, n, w.rows, w.k,
+                         s),
+           "q8 GEMM");
     }
-    // Split factor of the 512-wide projections (few output tiles); their row
-    // consumers add the partials.
-    int parts() const { return exact ? 1 : SPLITS; }
-    // The current Q8 activation operand: int8 codes (parity mode) or the hi
-    // plane of the split (fast path), whose lo plane is codes_lo().
-    void *codes() const { return exact ? static_cast<void *>(xq) : xh16; }
-    void *codes_lo() const { return exact ? nullptr : xl16; }
 
     // Both layer kinds run the tensor-core attention through maps whose token
     // extent is this wave's N (captured into its graph).
@@ -502,8 +445,8 @@ struct Backend {
                 ++launches;
             mark("qkv_post");
             // The O projection's Q8 operand is written by the attention itself.
-            ck(launch_attention_tc(tc_maps[L.d == 512], nullptr, bounds, N, L.d == 512 ? 0 : 512, s, xh16, xs, cap,
-                                   tier, xl16),
+            ck(launch_attention_tc(tc_maps[L.d == 512], nullptr, bounds, N, L.d == 512 ? 0 : 512, s, xq, xs, cap,
+                                   tier),
                "attention");
             ++launches;
         }
@@ -512,52 +455,31 @@ struct Backend {
             ck(launch_norm_quant(xq, xs, cap, nullptr, attn, nullptr, N, 4 * L.d, s, tier), "quant"), ++launches;
             mark("quant_attn");
         }
-        const int P = parts();
-        gemm(L.o, h, 512, N, s, P), ++launches;
+        gemm(L.o, h, 512, N, s), ++launches;
         mark("gemm_o");
-        ck(launch_post_add(x, h, L.post_attn_norm, nullptr, codes(), xs, cap, L.ffn_norm, N, s, tier, P, h_part,
-                           codes_lo()),
-           "post_add"),
-            ++launches;
+        ck(launch_post_add(x, h, L.post_attn_norm, nullptr, xq, xs, cap, L.ffn_norm, N, s, tier), "post_add"), ++launches;
         mark("post_add");
         // ffn_gate and ffn_up in one GEMM whose epilogue applies gelu(gate) * up
         // and quantizes (ROW_GELU_QUANT fused); the result is the down operand.
-        if (exact)
-            ck(launch_q8gemm_geglu(L.gu.tmap, tm_xq[0], L.gu.tscale, tm_xs[0], true, gq, gs, cap, N, L.gu.rows, L.gu.k, s,
-                                   tier),
-               "GeGLU GEMM");
-        else
-            ck(launch_f16gemm_geglu(tm_xh[0], tm_xl[0], L.gu.twh, L.gu.twl, L.gu.rowscale, gh16, gl16, gs, cap, N,
-                                    L.gu.rows, L.gu.k, s, tier),
-               "GeGLU GEMM");
-        ++launches;
+        ck(launch_q8gemm_geglu(L.gu.tmap, tm_xq[0], L.gu.tscale, tm_xs[0], exact, gq, gs, cap, N, L.gu.rows, L.gu.k,
+                               s, tier),
+           "GeGLU GEMM"),
+            ++launches;
         mark("gemm_geglu");
-        if (exact)
-            ck(launch_q8gemm(L.down.tmap, tm_gq, L.down.tscale, tm_gs, true, h, 512, N, L.down.rows, L.down.k, s),
-               "q8 GEMM");
-        else
-            ck(launch_f16gemm(tm_gh, tm_gl, L.down.twh, L.down.twl, L.down.bn, L.down.rowscale, h, 512, h_part, P, N,
-                              L.down.rows, L.down.k, s),
-               "fp16 GEMM");
-        ++launches;
+        ck(launch_q8gemm(L.down.tmap, tm_gq, L.down.tscale, tm_gs, exact, h, 512, N, L.down.rows, L.down.k, s),
+           "q8 GEMM"),
+            ++launches;
         mark("gemm_down");
-        ck(launch_post_add(x, h, L.post_ffw_norm, nullptr, codes(), xs, cap, nullptr, N, s, tier, P, h_part,
-                           codes_lo()),
-           "post_add"),
-            ++launches;
+        ck(launch_post_add(x, h, L.post_ffw_norm, nullptr, xq, xs, cap, nullptr, N, s, tier), "post_add"), ++launches;
         mark("post_add");
-        gemm(L.inp_gate, h, 512, N, s, P), ++launches;
+        gemm(L.inp_gate, h, 512, N, s), ++launches;
         mark("gemm_inp_gate");
-        ck(launch_gate_quant(codes(), xs, cap, h, ple, N, 512, 24 * 512, l * 512, s, tier, P, h_part, codes_lo()),
-           "ple gate"),
-            ++launches;
+        ck(launch_gate_quant(xq, xs, cap, h, ple, N, 512, 24 * 512, l * 512, s, tier), "ple gate"), ++launches;
         mark("ple_gate_quant");
-        gemm(L.proj, h, 512, N, s, P), ++launches;
+        gemm(L.proj, h, 512, N, s), ++launches;
         mark("gemm_proj");
         const float *next = l + 1 < 24 ? layers[l + 1].attn_norm : output_norm;
-        ck(launch_post_add(x, h, L.post_norm, L.out_scale, codes(), xs, cap, next, N, s, tier, P, h_part, codes_lo()),
-           "post_add"),
-            ++launches;
+        ck(launch_post_add(x, h, L.post_norm, L.out_scale, xq, xs, cap, next, N, s, tier), "post_add"), ++launches;
         mark("post_add");
         return launches;
     }
@@ -584,8 +506,7 @@ struct Backend {
         else
             ck(launch_ple(tm_hi, tm_lo, tm_ple, ple, ple_norm, N, s), "PLE"), ++launches;
         mark("ple_proj");
-        ck(launch_norm_quant(codes(), xs, cap, nullptr, x, layers[0].attn_norm, N, 512, s, tier, codes_lo()), "norm"),
-            ++launches;
+        ck(launch_norm_quant(xq, xs, cap, nullptr, x, layers[0].attn_norm, N, 512, s, tier), "norm"), ++launches;
         mark("norm_quant");
         for (int l = 0; l < 24; ++l) launches += enqueue_layer(l, N, s, tc_maps, mark);
         gemm(output, y, 768, N, s), ++launches;
@@ -803,8 +724,7 @@ struct Backend {
         AttnTcMaps tc_maps[2]{};
         attention_maps(N, tc_maps);
         if (l0 < 24)
-            ck(launch_norm_quant(codes(), xs, cap, nullptr, x, layers[l0].attn_norm, N, 512, s, tier, codes_lo()),
-               "norm");
+            ck(launch_norm_quant(xq, xs, cap, nullptr, x, layers[l0].attn_norm, N, 512, s, tier), "norm");
         auto none = [](const char *) {};
         for (int l = l0; l < l1; ++l) enqueue_layer(l, N, s, tc_maps, none);
         enqueue_readback(sl, 0);

@@ -7,7 +7,6 @@
 #include "attention.cuh"
 #include "attention_tc.cuh"
 #include "exact.cuh"
-#include "f16gemm.cuh"
 #include "launch.h"
 #include "opsabi.cuh"
 #include "ple.cuh"
@@ -61,15 +60,6 @@ bool f16_head_tmap(CUtensorMap *map, const void *base, uint64_t d, uint64_t head
 bool scale_tmap(CUtensorMap *map, const float *base, uint64_t stride, uint64_t kb, uint32_t box_cols) {
     return encode_tmap_2d(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, base, stride, kb, stride * 4, box_cols,
                           uint32_t(kb), false);
-}
-bool scale_tmap_rows(CUtensorMap *map, const float *base, uint64_t stride, uint64_t kb, uint32_t box_cols,
-                     uint32_t box_rows) {
-    return box_rows >= 1 && box_rows <= kb &&
-           encode_tmap_2d(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, base, stride, kb, stride * 4, box_cols, box_rows,
-                          false);
-}
-bool f16_tmap(CUtensorMap *map, const void *base, uint64_t k, uint64_t rows, uint32_t box_rows) {
-    return encode_tmap_2d(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, base, k, rows, k * 2, 64, box_rows, true);
 }
 
 static int sm_count() {
@@ -132,52 +122,6 @@ cudaError_t launch_q8gemm_geglu(const CUtensorMap &w, const CUtensorMap &x, cons
     return exact ? q8gemm_go<true, true>(w, x, sw, sx, p, s) : q8gemm_go<false, true>(w, x, sw, sx, p, s);
 }
 
-template <int BN, bool GEGLU>
-static cudaError_t f16gemm_go(const CUtensorMap &xh, const CUtensorMap &xl, const CUtensorMap &wh,
-                              const CUtensorMap &wl, const F16GemmParams &p, cudaStream_t s) {
-    const int grid = p.units < sm_count() ? p.units : sm_count();
-    return launch_pdl(f16gemm_kernel<BN, GEGLU>, dim3(grid), dim3(F16Cfg<BN>::THREADS), F16Cfg<BN>::SMEM, s, xh, xl,
-                      wh, wl, p);
-}
-static F16GemmParams f16gemm_params(int bn, const float *rowscale, int splits, int T, int R, int K) {
-    F16GemmParams p{};
-    p.rowscale = rowscale, p.T = T, p.R = R, p.K = K, p.tiles_m = (T + 127) / 128;
-    p.num_tiles = (R / bn) * p.tiles_m, p.splits = splits, p.units = p.num_tiles * splits;
-    p.kstages = K / 64 / splits;
-    return p;
-}
-cudaError_t launch_f16gemm(const CUtensorMap &xh, const CUtensorMap &xl, const CUtensorMap &wh, const CUtensorMap &wl,
-                           int bn, const float *rowscale, float *out, int ldo, size_t split_stride, int splits, int T,
-                           int R, int K, cudaStream_t s) {
-    if (T <= 0) return cudaSuccess;
-    if ((bn != 128 && bn != 256) || R <= 0 || R % bn || K <= 0 || K > 2048 || splits < 1 || splits > 4 ||
-        K % (64 * splits) || ldo < R || !out || !rowscale || (splits > 1 && split_stride < size_t(T) * ldo))
-        return cudaErrorInvalidValue;
-    F16GemmParams p = f16gemm_params(bn, rowscale, splits, T, R, K);
-    p.out = out, p.ldo = ldo, p.split_stride = split_stride;
-    return bn == 256 ? f16gemm_go<256, false>(xh, xl, wh, wl, p, s) : f16gemm_go<128, false>(xh, xl, wh, wl, p, s);
-}
-cudaError_t launch_f16gemm_geglu(const CUtensorMap &xh, const CUtensorMap &xl, const CUtensorMap &wh,
-                                 const CUtensorMap &wl, const float *rowscale, void *out_hi, void *out_lo, float *q8s,
-                                 int q8s_stride, int T, int R, int K, cudaStream_t s, int tier) {
-    if (T <= 0) return cudaSuccess;
-    if (R <= 0 || R % 256 || K <= 0 || K > 2048 || K % 64 || !out_hi || !out_lo || !q8s || q8s_stride < T ||
-        !rowscale)
-        return cudaErrorInvalidValue;
-    F16GemmParams p = f16gemm_params(256, rowscale, 1, T, R, K);
-    p.xh = static_cast<__half *>(out_hi), p.xl = static_cast<__half *>(out_lo), p.q8s = q8s, p.q8s_stride = q8s_stride;
-    p.tier = tier == TIER_SCALAR ? TIER_SCALAR : TIER_X86;
-    return f16gemm_go<256, true>(xh, xl, wh, wl, p, s);
-}
-cudaError_t launch_split_q8(const int8_t *codes, const float *scales, int scale_stride, int rows, int k, void *wh,
-                            void *wl, float *rowscale, cudaStream_t s) {
-    if (rows <= 0) return cudaSuccess;
-    if (k <= 0 || k % 32 || scale_stride < rows) return cudaErrorInvalidValue;
-    split_q8_kernel<<<(rows + 7) / 8, 256, 0, s>>>(codes, scales, scale_stride, rows, k, static_cast<__half *>(wh),
-                                                   static_cast<__half *>(wl), rowscale);
-    return cudaGetLastError();
-}
-
 cudaError_t launch_ple(const CUtensorMap &hi, const CUtensorMap &lo, const CUtensorMap &w, float *ple,
                        const float *norm, int M, cudaStream_t s) {
     if (M <= 0) return cudaSuccess;
@@ -197,36 +141,24 @@ cudaError_t launch_embed(float *x, void *x_hi, void *x_lo, const void *emb, cons
                       static_cast<__nv_bfloat16 *>(x_lo), static_cast<const uint8_t *>(emb), ids, n);
 }
 
-template <typename Out>
-static cudaError_t norm_quant_go(Out q, float *qs, int qs_stride, float *y, const float *x, const float *w, int rows,
-                                 int width, cudaStream_t s, int tier) {
-    if (!w) {  // ROW_QUANT: no row reduction, warp per (row, four blocks)
-        const int warps = rows * (width / 128);
-        return launch_pdl(quant_rows_kernel<Out>, dim3((warps + 7) / 8), dim3(256), 0, s, q, qs, qs_stride, x, rows,
-                          width, tier);
-    }
-    switch (width) {  // ROW_NORM_QUANT: CTA per row, one float4 per thread
-        case 256:
-            return launch_pdl(norm_quant_kernel<256, Out>, dim3(rows), dim3(64), 0, s, q, qs, qs_stride, y, x, w, tier);
-        case 512:
-            return launch_pdl(norm_quant_kernel<512, Out>, dim3(rows), dim3(128), 0, s, q, qs, qs_stride, y, x, w, tier);
-        case 1024:
-            return launch_pdl(norm_quant_kernel<1024, Out>, dim3(rows), dim3(256), 0, s, q, qs, qs_stride, y, x, w,
-                              tier);
-        default:
-            return launch_pdl(norm_quant_kernel<2048, Out>, dim3(rows), dim3(512), 0, s, q, qs, qs_stride, y, x, w,
-                              tier);
-    }
-}
-cudaError_t launch_norm_quant(void *q, float *qs, int qs_stride, float *y, const float *x, const float *w, int rows,
-                              int width, cudaStream_t s, int tier, void *q_lo) {
+cudaError_t launch_norm_quant(int8_t *q, float *qs, int qs_stride, float *y, const float *x, const float *w, int rows,
+                              int width, cudaStream_t s, int tier) {
     if (rows <= 0) return cudaSuccess;
     if (qs_stride < rows) return cudaErrorInvalidValue;
     if (width != 256 && width != 512 && width != 1024 && width != 2048) return cudaErrorInvalidValue;
-    if (q_lo)
-        return norm_quant_go(Q8Split{static_cast<__half *>(q), static_cast<__half *>(q_lo)}, qs, qs_stride, y, x, w,
-                             rows, width, s, tier);
-    return norm_quant_go(Q8Codes{static_cast<int8_t *>(q)}, qs, qs_stride, y, x, w, rows, width, s, tier);
+    if (!w) {  // ROW_QUANT: no row reduction, warp per (row, four blocks)
+        const int warps = rows * (width / 128);
+        return launch_pdl(quant_rows_kernel, dim3((warps + 7) / 8), dim3(256), 0, s, q, qs, qs_stride, x, rows, width,
+                          tier);
+    }
+    switch (width) {  // ROW_NORM_QUANT: CTA per row, one float4 per thread
+        case 256: return launch_pdl(norm_quant_kernel<256>, dim3(rows), dim3(64), 0, s, q, qs, qs_stride, y, x, w, tier);
+        case 512: return launch_pdl(norm_quant_kernel<512>, dim3(rows), dim3(128), 0, s, q, qs, qs_stride, y, x, w, tier);
+        case 1024:
+            return launch_pdl(norm_quant_kernel<1024>, dim3(rows), dim3(256), 0, s, q, qs, qs_stride, y, x, w, tier);
+        default:
+            return launch_pdl(norm_quant_kernel<2048>, dim3(rows), dim3(512), 0, s, q, qs, qs_stride, y, x, w, tier);
+    }
 }
 
 cudaError_t launch_qkv_post(void *q, void *k, void *v, const float *qkv, const float *qn, const float *kn,
@@ -287,12 +219,11 @@ bool attention_tc_maps(AttnTcMaps *m, const void *q, const void *k, const void *
            f16_head_tmap(&m->v, v, uint64_t(d), kv, uint64_t(n), AttnTcCfg::BKEY);
 }
 cudaError_t launch_attention_tc(const AttnTcMaps &m, float *out, const unsigned *bounds, int n, int window,
-                                cudaStream_t s, void *q, float *qs, int q_stride, int tier, void *q_lo) {
+                                cudaStream_t s, int8_t *q, float *qs, int q_stride, int tier) {
     if (n <= 0) return cudaSuccess;
     if (n > ATTN_TC_MAX_TOKENS || window < 0 || (q ? (!qs || q_stride < n) : !out) || (m.d != 256 && m.d != 512))
         return cudaErrorInvalidValue;
-    const AttnTcParams p{out, bounds, n, window, q, q ? q_lo : nullptr, qs, q_stride,
-                         tier == TIER_SCALAR ? TIER_SCALAR : TIER_X86};
+    const AttnTcParams p{out, bounds, n, window, q, qs, q_stride, tier == TIER_SCALAR ? TIER_SCALAR : TIER_X86};
     const dim3 grid((n + AttnTcCfg::BQ - 1) / AttnTcCfg::BQ, 4, m.d / 256);
     if (m.d == 512)
         return launch_pdl(attention_tc_kernel<512>, grid, dim3(AttnTcCfgD<512>::THREADS), AttnTcCfgD<512>::SMEM, s,
@@ -300,18 +231,11 @@ cudaError_t launch_attention_tc(const AttnTcMaps &m, float *out, const unsigned 
     return launch_pdl(attention_tc_kernel<256>, grid, dim3(AttnTcCfg::THREADS), AttnTcCfg::SMEM, s, m.q, m.k, m.v, p);
 }
 
-cudaError_t launch_post_add(float *x, const float *h, const float *w, const float *scale, void *q, float *qs,
-                            int qs_stride, const float *next_w, int rows, cudaStream_t s, int tier, int parts,
-                            size_t part_stride, void *q_lo) {
+cudaError_t launch_post_add(float *x, const float *h, const float *w, const float *scale, int8_t *q, float *qs,
+                            int qs_stride, const float *next_w, int rows, cudaStream_t s, int tier) {
     if (rows <= 0) return cudaSuccess;
-    if (qs_stride < rows || parts < 1 || parts > 4 || (parts > 1 && part_stride < size_t(rows) * 512))
-        return cudaErrorInvalidValue;
-    if (q_lo)
-        return launch_pdl(post_add_kernel<Q8Split>, dim3(rows), dim3(128), 0, s, x, h, w, scale,
-                          Q8Split{static_cast<__half *>(q), static_cast<__half *>(q_lo)}, qs, qs_stride, next_w, tier,
-                          parts, part_stride);
-    return launch_pdl(post_add_kernel<Q8Codes>, dim3(rows), dim3(128), 0, s, x, h, w, scale,
-                      Q8Codes{static_cast<int8_t *>(q)}, qs, qs_stride, next_w, tier, parts, part_stride);
+    if (qs_stride < rows) return cudaErrorInvalidValue;
+    return launch_pdl(post_add_kernel, dim3(rows), dim3(128), 0, s, x, h, w, scale, q, qs, qs_stride, next_w, tier);
 }
 
 cudaError_t launch_gelu_mul(float *g, const float *u, size_t n, cudaStream_t s, int tier) {
@@ -322,28 +246,16 @@ cudaError_t launch_gelu_mul(float *g, const float *u, size_t n, cudaStream_t s, 
                       dim3(unsigned(blocks < cap ? blocks : cap)), dim3(256), 0, s, g, u, n);
 }
 
-template <typename Out>
-static cudaError_t gate_quant_go(Out q, float *qs, int qs_stride, const float *x, const float *other, int rows,
-                                 int width, int other_stride, int other_offset, cudaStream_t s, int tier, int parts,
-                                 size_t part_stride) {
-    const int warps = rows * (width / 128);
-    return launch_pdl(tier == TIER_SCALAR ? gate_quant_kernel<TIER_SCALAR, Out> : gate_quant_kernel<TIER_X86, Out>,
-                      dim3((warps + 7) / 8), dim3(256), 0, s, q, qs, qs_stride, x, other, rows, width, other_stride,
-                      other_offset, parts, part_stride);
-}
-cudaError_t launch_gate_quant(void *q, float *qs, int qs_stride, const float *x, const float *other, int rows,
-                              int width, int other_stride, int other_offset, cudaStream_t s, int tier, int parts,
-                              size_t part_stride, void *q_lo) {
+cudaError_t launch_gate_quant(int8_t *q, float *qs, int qs_stride, const float *x, const float *other, int rows,
+                              int width, int other_stride, int other_offset, cudaStream_t s, int tier) {
     if (rows <= 0) return cudaSuccess;
     if (width <= 0 || width % 128 || qs_stride < rows || other_stride % 4 || other_offset % 4 ||
-        other_offset + width > other_stride || parts < 1 || parts > 4 ||
-        (parts > 1 && part_stride < size_t(rows) * width))
+        other_offset + width > other_stride)
         return cudaErrorInvalidValue;
-    if (q_lo)
-        return gate_quant_go(Q8Split{static_cast<__half *>(q), static_cast<__half *>(q_lo)}, qs, qs_stride, x, other,
-                             rows, width, other_stride, other_offset, s, tier, parts, part_stride);
-    return gate_quant_go(Q8Codes{static_cast<int8_t *>(q)}, qs, qs_stride, x, other, rows, width, other_stride,
-                         other_offset, s, tier, parts, part_stride);
+    const int warps = rows * (width / 128);
+    return launch_pdl(tier == TIER_SCALAR ? gate_quant_kernel<TIER_SCALAR> : gate_quant_kernel<TIER_X86>,
+                      dim3((warps + 7) / 8), dim3(256), 0, s, q, qs, qs_stride, x, other, rows, width, other_stride,
+                      other_offset);
 }
 
 cudaError_t launch_pool_l2(float *out, const float *y, const unsigned *offsets, int batch, int width, cudaStream_t s,
@@ -371,13 +283,6 @@ cudaError_t init_kernel_attributes() {
     for (auto k : {q8gemm_kernel<false, false>, q8gemm_kernel<true, false>, q8gemm_kernel<false, true>,
                    q8gemm_kernel<true, true>})
         if ((e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024))) return e;
-    if ((e = cudaFuncSetAttribute(f16gemm_kernel<256, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                  int(F16Cfg<256>::SMEM))) ||
-        (e = cudaFuncSetAttribute(f16gemm_kernel<256, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                  int(F16Cfg<256>::SMEM))) ||
-        (e = cudaFuncSetAttribute(f16gemm_kernel<128, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                  int(F16Cfg<128>::SMEM))))
-        return e;
     if ((e = cudaFuncSetAttribute(ple_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(PleCfg::SMEM)))) return e;
     if ((e = cudaFuncSetAttribute(attention_kernel<256>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                   int(AttnCfg<256>::SMEM))))
@@ -530,35 +435,6 @@ int eg2_launch_q8_geglu(const EgQ8GeGLU *p, void *s) {
         return rc(cudaErrorInvalidValue);
     return rc(launch_q8gemm_geglu(w, x, sw, sx, p->exact != 0, p->q, p->scale, int(p->scale_stride), int(p->n),
                                   int(rows), int(p->k), S(s), int(p->tier)));
-}
-int eg2_launch_q8_mm_f16(const EgQ8MMF16 *p, void *s) {
-    if (cudaError_t e = ensure_attributes()) return rc(e);
-    if (!p->n) return 0;
-    if (p->k % 64 || p->k > 2048 || p->m % 128 || !p->m || !p->splits || p->splits > 4 || p->k % (64 * p->splits))
-        return rc(cudaErrorInvalidValue);
-    const int bn = p->m % 256 == 0 ? 256 : 128;
-    CUtensorMap xh, xl, wh, wl;
-    if (!f16_tmap(&xh, p->xh, p->k, p->n, 128) || !f16_tmap(&xl, p->xl, p->k, p->n, 128) ||
-        !f16_tmap(&wh, p->wh, p->k, p->m, uint32_t(bn)) || !f16_tmap(&wl, p->wl, p->k, p->m, uint32_t(bn)))
-        return rc(cudaErrorInvalidValue);
-    return rc(launch_f16gemm(xh, xl, wh, wl, bn, p->rowscale, p->out, int(p->m), size_t(p->split_stride),
-                             int(p->splits), int(p->n), int(p->m), int(p->k), S(s)));
-}
-int eg2_launch_q8_geglu_f16(const EgQ8GeGLUF16 *p, void *s) {
-    if (cudaError_t e = ensure_attributes()) return rc(e);
-    if (!p->n) return 0;
-    const unsigned rows = 2 * p->m;
-    if (p->k % 64 || p->k > 2048 || p->m % 128 || !p->m || p->scale_stride < p->n) return rc(cudaErrorInvalidValue);
-    CUtensorMap xh, xl, wh, wl;
-    if (!f16_tmap(&xh, p->xh, p->k, p->n, 128) || !f16_tmap(&xl, p->xl, p->k, p->n, 128) ||
-        !f16_tmap(&wh, p->wh, p->k, rows, 256) || !f16_tmap(&wl, p->wl, p->k, rows, 256))
-        return rc(cudaErrorInvalidValue);
-    return rc(launch_f16gemm_geglu(xh, xl, wh, wl, p->rowscale, p->out_h, p->out_l, p->scale, int(p->scale_stride),
-                                   int(p->n), int(rows), int(p->k), S(s), int(p->tier)));
-}
-int eg2_split_q8_weight(const int8_t *codes, const float *scales, unsigned rows, unsigned k, uint16_t *wh,
-                        uint16_t *wl, float *rowscale, void *s) {
-    return rc(launch_split_q8(codes, scales, int(rows), int(rows), int(k), wh, wl, rowscale, S(s)));
 }
 int eg2_launch_qkv_post(const EgQkvPost *p, void *s) {
     return rc(launch_qkv_post(p->q, p->k, p->v, p->qkv, p->q_norm, p->k_norm, p->rope_cos, p->rope_sin, p->pos,

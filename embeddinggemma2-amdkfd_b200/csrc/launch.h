@@ -15,11 +15,6 @@ bool q8_tmap(CUtensorMap *map, const int8_t *base, uint64_t k, uint64_t rows, ui
 bool bf16_tmap(CUtensorMap *map, const void *base, uint64_t k, uint64_t rows, uint32_t box_rows);
 // Block-major fp32 scale plane [kb][stride]: box box_cols x kb, no swizzle.
 bool scale_tmap(CUtensorMap *map, const float *base, uint64_t stride, uint64_t kb, uint32_t box_cols);
-// The same plane with a box of box_cols x box_rows (a K range of the blocks).
-bool scale_tmap_rows(CUtensorMap *map, const float *base, uint64_t stride, uint64_t kb, uint32_t box_cols,
-                     uint32_t box_rows);
-// FP16 operand over [rows][k] fp16: box 64 elements x box_rows, 128-byte swizzle.
-bool f16_tmap(CUtensorMap *map, const void *base, uint64_t k, uint64_t rows, uint32_t box_rows);
 
 // Kernel launches (all asynchronous on `s`).  `tier` (TIER_X86 / TIER_SCALAR
 // in common.cuh) selects the quantizer rounding and GELU of the reference tier
@@ -36,36 +31,13 @@ cudaError_t launch_q8gemm(const CUtensorMap &w, const CUtensorMap &x, const CUte
 cudaError_t launch_q8gemm_geglu(const CUtensorMap &w, const CUtensorMap &x, const CUtensorMap &sw,
                                 const CUtensorMap &sx, bool exact, int8_t *q8, float *q8s, int q8s_stride, int T, int R,
                                 int K, cudaStream_t s, int tier = 0);
-// The fast path's Q8_0 GEMM on fp16 tensor cores (f16gemm.cuh): the
-// dequantized activation planes Xh, Xl [T..][K] (maps with a box of 64 x 128
-// rows) times the split weight Wh, Wl [R][K] (maps with a box of 64 x bn
-// rows, bn = 128 or 256), scaled by rowscale.  splits > 1: partial sums at
-// out + split * split_stride, added in order by the consumer.  R % bn == 0,
-// K % (64 * splits) == 0.
-cudaError_t launch_f16gemm(const CUtensorMap &xh, const CUtensorMap &xl, const CUtensorMap &wh, const CUtensorMap &wl,
-                           int bn, const float *rowscale, float *out, int ldo, size_t split_stride, int splits, int T,
-                           int R, int K, cudaStream_t s);
-// GeGLU form (bn = 256): weight rows gate/up interleaved in 32-row chunks
-// (rows 64c .. 64c+31 = gate rows 32c .., the next 32 = up rows 32c ..);
-// writes the ffn_down operand of gelu(gate) * up as the dequantized split
-// planes xh, xl [T][R/2] and block-major scales q8s [R/64][q8s_stride].
-cudaError_t launch_f16gemm_geglu(const CUtensorMap &xh, const CUtensorMap &xl, const CUtensorMap &wh,
-                                 const CUtensorMap &wl, const float *rowscale, void *out_hi, void *out_lo, float *q8s,
-                                 int q8s_stride, int T, int R, int K, cudaStream_t s, int tier);
-// Load-time split of a SoA Q8 weight into the fp16 planes Wh, Wl [rows][k] and
-// the per-row scale 2^-s_r (split_q8_kernel).
-cudaError_t launch_split_q8(const int8_t *codes, const float *scales, int scale_stride, int rows, int k, void *wh,
-                            void *wl, float *rowscale, cudaStream_t s);
 cudaError_t launch_ple(const CUtensorMap &hi, const CUtensorMap &lo, const CUtensorMap &w, float *ple,
                        const float *norm, int M, cudaStream_t s);
 cudaError_t launch_embed(float *x, void *x_hi, void *x_lo, const void *emb, const int *ids, int n, cudaStream_t s);
 // Soft-token waves: x = rows[n][512] as given, plus the bf16 hi/lo split of x.
 cudaError_t launch_input_rows(float *x, void *x_hi, void *x_lo, const float *rows, int n, cudaStream_t s);
-// Q8_0 outputs: int8 codes in q, or with q_lo set the dequantized values
-// split into fp16 planes q (hi) and q_lo (lo) (the fp16 GEMM's operand,
-// Q8Split in common.cuh) -- here and in the launchers below.
-cudaError_t launch_norm_quant(void *q, float *qs, int qs_stride, float *y, const float *x, const float *w, int rows,
-                              int width, cudaStream_t s, int tier = 0, void *q_lo = nullptr);
+cudaError_t launch_norm_quant(int8_t *q, float *qs, int qs_stride, float *y, const float *x, const float *w, int rows,
+                              int width, cudaStream_t s, int tier = 0);
 // q/k/v outputs are fp16, or fp32 when f32_out (parity mode).
 cudaError_t launch_qkv_post(void *q, void *k, void *v, const float *qkv, const float *qn, const float *kn,
                             const float *rc, const float *rs, const unsigned *pos, int n, int d, cudaStream_t s,
@@ -90,17 +62,13 @@ bool attention_tc_maps(AttnTcMaps *m, const void *q, const void *k, const void *
 // With q set, writes Q8_0 codes [n][4d] and block-major scales [4d/32][q_stride]
 // (the row quantizer's output for the same rows) instead of fp32 out.
 cudaError_t launch_attention_tc(const AttnTcMaps &m, float *out, const unsigned *bounds, int n, int window,
-                                cudaStream_t s, void *q = nullptr, float *qs = nullptr, int q_stride = 0,
-                                int tier = 0, void *q_lo = nullptr);
-// h (post_add) and x (gate_quant) may be split-K GEMM outputs: `parts` partial
-// rows part_stride floats apart, summed in order.
-cudaError_t launch_post_add(float *x, const float *h, const float *w, const float *scale, void *q, float *qs,
-                            int qs_stride, const float *next_w, int rows, cudaStream_t s, int tier = 0, int parts = 1,
-                            size_t part_stride = 0, void *q_lo = nullptr);
+                                cudaStream_t s, int8_t *q = nullptr, float *qs = nullptr, int q_stride = 0,
+                                int tier = 0);
+cudaError_t launch_post_add(float *x, const float *h, const float *w, const float *scale, int8_t *q, float *qs,
+                            int qs_stride, const float *next_w, int rows, cudaStream_t s, int tier = 0);
 cudaError_t launch_gelu_mul(float *g, const float *u, size_t n, cudaStream_t s, int tier = 0);
-cudaError_t launch_gate_quant(void *q, float *qs, int qs_stride, const float *x, const float *other, int rows,
-                              int width, int other_stride, int other_offset, cudaStream_t s, int tier = 0,
-                              int parts = 1, size_t part_stride = 0, void *q_lo = nullptr);
+cudaError_t launch_gate_quant(int8_t *q, float *qs, int qs_stride, const float *x, const float *other, int rows,
+                              int width, int other_stride, int other_offset, cudaStream_t s, int tier = 0);
 // Mean pool then L2 of `batch` sequences; with count set (device memory), only
 // the first *count of them (batch is then an upper bound, the launch grid).
 cudaError_t launch_pool_l2(float *out, const float *y, const unsigned *offsets, int batch, int width, cudaStream_t s,

@@ -72,17 +72,6 @@ __device__ __forceinline__ uint32_t quant_oct(const float4 v, float *scale_out, 
     return q8_code(v.x, id, tier) | q8_code(v.y, id, tier) << 8 | q8_code(v.z, id, tier) << 16 |
            q8_code(v.w, id, tier) << 24;
 }
-// Row t of a split-K GEMM output: the sum of its `parts` partial rows, spaced
-// part_stride floats apart, added in part order (one float4 of it).
-__device__ __forceinline__ float4 sum_parts4(const float *base, size_t i4, int parts, size_t part_stride) {
-    float4 v = reinterpret_cast<const float4 *>(base)[i4];
-    for (int k = 1; k < parts; ++k) {
-        const float4 w = reinterpret_cast<const float4 *>(base + size_t(k) * part_stride)[i4];
-        v = make_float4(__fadd_rn(v.x, w.x), __fadd_rn(v.y, w.y), __fadd_rn(v.z, w.z), __fadd_rn(v.w, w.w));
-    }
-    return v;
-}
-
 __device__ __forceinline__ double sumsq4(double ss, const float4 v) {
     ss = __dadd_rn(ss, __dmul_rn(double(v.x), double(v.x)));
     ss = __dadd_rn(ss, __dmul_rn(double(v.y), double(v.y)));
@@ -109,8 +98,8 @@ __device__ __forceinline__ double cta_sum_d(double v, double *red) {
 
 // ROW_NORM_QUANT (gemma2_fast.c:685-691): RMS norm with weight w, then Q8_0.
 // CTA per row, one float4 per thread (WIDTH / 4 threads).
-template <int WIDTH, typename Out>
-__global__ void __launch_bounds__(WIDTH / 4) norm_quant_kernel(const Out q, float *__restrict__ qs,
+template <int WIDTH>
+__global__ void __launch_bounds__(WIDTH / 4) norm_quant_kernel(int8_t *__restrict__ q, float *__restrict__ qs,
                                                                int qs_stride, float *__restrict__ y,
                                                                const float *__restrict__ x,
                                                                const float *__restrict__ w, int tier) {
@@ -124,15 +113,13 @@ __global__ void __launch_bounds__(WIDTH / 4) norm_quant_kernel(const Out q, floa
     v = scale_w4(v, sc, reinterpret_cast<const float4 *>(w)[i]);
     if (y) reinterpret_cast<float4 *>(y + size_t(t) * WIDTH)[i] = v;
     float s;
-    const uint32_t c = quant_oct(v, &s, tier);
-    store4(q, size_t(t) * WIDTH, i, c, s);
+    reinterpret_cast<uint32_t *>(q + size_t(t) * WIDTH)[i] = quant_oct(v, &s, tier);
     if ((lane & 7) == 0) qs[size_t(i >> 3) * qs_stride + t] = s;
 }
 
 // ROW_QUANT (gemma2_fast.c:728-730): Q8_0 of rows of width `width` (a multiple
 // of 128).  Warp per (row, four blocks).
-template <typename Out>
-__global__ void quant_rows_kernel(const Out q, float *__restrict__ qs, int qs_stride,
+__global__ void quant_rows_kernel(int8_t *__restrict__ q, float *__restrict__ qs, int qs_stride,
                                   const float *__restrict__ x, int rows, int width, int tier) {
     pdl_wait();
     pdl_trigger();
@@ -142,8 +129,7 @@ __global__ void quant_rows_kernel(const Out q, float *__restrict__ qs, int qs_st
     const int t = gw / steps, st = gw % steps;
     const size_t c = size_t(t) * (width / 4) + st * 32 + lane;
     float s;
-    const uint32_t codes = quant_oct(reinterpret_cast<const float4 *>(x)[c], &s, tier);
-    store4(q, 0, int(c), codes, s);
+    reinterpret_cast<uint32_t *>(q)[c] = quant_oct(reinterpret_cast<const float4 *>(x)[c], &s, tier);
     if ((lane & 7) == 0) qs[size_t(4 * st + (lane >> 3)) * qs_stride + t] = s;
 }
 
@@ -227,21 +213,17 @@ __global__ void qkv_post_kernel(OutT *__restrict__ qo, OutT *__restrict__ ko, Ou
 // ROW_POST_ADD (gemma2_fast.c:707-713): x = (x + rms(h) * w) * scale, then the
 // next GEMM operand from the updated x: RMS-norm with next_w and quantize
 // (ROW_NORM_QUANT) or, next_w == nullptr, plain quantization (ROW_QUANT).
-// CTA of 128 threads per 512-wide row, one float4 per thread.  h may be a
-// split-K GEMM output: `parts` partial rows part_stride floats apart, summed
-// in order.
-template <typename Out>
+// CTA of 128 threads per 512-wide row, one float4 per thread.
 __global__ void __launch_bounds__(128) post_add_kernel(float *__restrict__ x, const float *__restrict__ h,
                                                        const float *__restrict__ w, const float *__restrict__ scale,
-                                                       const Out q, float *__restrict__ qs, int qs_stride,
-                                                       const float *__restrict__ next_w, int tier, int parts,
-                                                       size_t part_stride) {
+                                                       int8_t *__restrict__ q, float *__restrict__ qs, int qs_stride,
+                                                       const float *__restrict__ next_w, int tier) {
     pdl_wait();
     pdl_trigger();
     __shared__ double red[2][4];
     const int t = blockIdx.x, i = threadIdx.x, lane = i & 31;
     float4 *xp = reinterpret_cast<float4 *>(x + size_t(t) * 512) + i;
-    const float4 hv = sum_parts4(h, size_t(t) * 128 + i, parts, part_stride);
+    const float4 hv = reinterpret_cast<const float4 *>(h + size_t(t) * 512)[i];
     float4 xv = *xp;
     const float sc = rms_scale(cta_sum_d<4>(sumsq4(0.0, hv), red[0]), 512);
     const float ls = scale ? *scale : 1.0f;
@@ -254,8 +236,7 @@ __global__ void __launch_bounds__(128) post_add_kernel(float *__restrict__ x, co
         xv = scale_w4(xv, sc2, reinterpret_cast<const float4 *>(next_w)[i]);
     }
     float s;
-    const uint32_t c = quant_oct(xv, &s, tier);
-    store4(q, size_t(t) * 512, i, c, s);
+    reinterpret_cast<uint32_t *>(q + size_t(t) * 512)[i] = quant_oct(xv, &s, tier);
     if ((lane & 7) == 0) qs[size_t(i >> 3) * qs_stride + t] = s;
 }
 
@@ -263,12 +244,10 @@ __global__ void __launch_bounds__(128) post_add_kernel(float *__restrict__ x, co
 // g = gelu_tanh(x) * other, then Q8_0.  Warp per (row, four blocks); width,
 // other_stride and other_offset are multiples of 128, 4 and 4.  TIER selects
 // the GELU and rounding at compile time (no branch per element).
-// x may be a split-K GEMM output (`parts` partials part_stride floats apart,
-// summed in order).
-template <int TIER, typename Out>
-__global__ void gate_quant_kernel(const Out q, float *__restrict__ qs, int qs_stride,
+template <int TIER>
+__global__ void gate_quant_kernel(int8_t *__restrict__ q, float *__restrict__ qs, int qs_stride,
                                   const float *__restrict__ x, const float *__restrict__ other, int rows, int width,
-                                  int other_stride, int other_offset, int parts, size_t part_stride) {
+                                  int other_stride, int other_offset) {
     constexpr int tier = TIER;
     pdl_wait();
     pdl_trigger();
@@ -277,14 +256,13 @@ __global__ void gate_quant_kernel(const Out q, float *__restrict__ qs, int qs_st
     const int gw = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5), lane = threadIdx.x & 31;
     if (gw >= rows * wpr) return;  // warp-uniform
     const int t = gw / wpr, i0 = (gw % wpr) * PER;
+    const float4 *xr = reinterpret_cast<const float4 *>(x + size_t(t) * width);
     const float4 *orow = reinterpret_cast<const float4 *>(other + size_t(t) * other_stride + other_offset);
-    const size_t qr = size_t(t) * width;
+    uint32_t *qr = reinterpret_cast<uint32_t *>(q + size_t(t) * width);
     float4 xv[PER], ov[PER];
 #pragma unroll
     for (int i = 0; i < PER; ++i)
-        if (i0 + i < steps)
-            xv[i] = sum_parts4(x, size_t(t) * (width / 4) + (i0 + i) * 32 + lane, parts, part_stride),
-            ov[i] = orow[(i0 + i) * 32 + lane];
+        if (i0 + i < steps) xv[i] = xr[(i0 + i) * 32 + lane], ov[i] = orow[(i0 + i) * 32 + lane];
 #pragma unroll
     for (int i = 0; i < PER; ++i) {
         if (i0 + i >= steps) break;  // warp-uniform
@@ -293,8 +271,7 @@ __global__ void gate_quant_kernel(const Out q, float *__restrict__ qs, int qs_st
                                      __fmul_rn(gelu_tier(xv[i].z, tier), ov[i].z),
                                      __fmul_rn(gelu_tier(xv[i].w, tier), ov[i].w));
         float sc;
-        const uint32_t c = quant_oct(g, &sc, tier);
-        store4(q, qr, (i0 + i) * 32 + lane, c, sc);
+        qr[(i0 + i) * 32 + lane] = quant_oct(g, &sc, tier);
         if ((lane & 7) == 0) qs[size_t(4 * (i0 + i) + (lane >> 3)) * qs_stride + t] = sc;
     }
 }

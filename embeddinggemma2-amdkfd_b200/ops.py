@@ -87,24 +87,6 @@ def q8_geglu(q, scale, scale_stride, xq, xs, xs_stride, wq, ws, n, k, m, exact=F
                                                 _p(ws), n, k, m, int(exact), tier))
 
 
-def split_q8_weight(codes, scales, rows, k, wh, wl, rowscale):
-    """Load-time split of a SoA Q8 weight into fp16 planes (eg2_split_q8_weight)."""
-    rc = _lib.load().eg2_split_q8_weight(_p(codes), _p(scales), rows, k, _p(wh), _p(wl), _p(rowscale), _stream())
-    if rc:
-        raise RuntimeError(f"eg2_split_q8_weight failed with CUDA error {rc}")
-
-
-def q8_mm_f16(out, xh, xl, wh, wl, rowscale, n, k, m, splits=1, split_stride=0):
-    """EgQ8MMF16: activations as split fp16 planes xh, xl; weights split by split_q8_weight."""
-    _call("eg2_launch_q8_mm_f16", _lib.EgQ8MMF16(_p(out), _p(xh), _p(xl), _p(wh), _p(wl), _p(rowscale),
-                                                 n, k, m, splits, split_stride))
-
-
-def q8_geglu_f16(out_h, out_l, scale, scale_stride, xh, xl, wh, wl, rowscale, n, k, m, tier=0):
-    _call("eg2_launch_q8_geglu_f16", _lib.EgQ8GeGLUF16(_p(out_h), _p(out_l), _p(scale), scale_stride, _p(xh), _p(xl),
-                                                       _p(wh), _p(wl), _p(rowscale), n, k, m, tier))
-
-
 def qkv_post(q, k, v, qkv, q_norm, k_norm, rope_cos, rope_sin, pos, n, d):
     _call("eg2_launch_qkv_post", _lib.EgQkvPost(_p(q), _p(k), _p(v), _p(qkv), _p(q_norm), _p(k_norm),
                                                 _p(rope_cos), _p(rope_sin), _p(pos), n, d))

@@ -75,31 +75,6 @@ typedef struct {
     const int8_t *wq; const float *ws; unsigned n, k, m, exact;
     unsigned tier; /* as in EgGateQuant */
 } EgQ8GeGLU;
-/* The fast path's form of EgQ8MM on the fp16 tensor cores (tcgen05
- * kind::f16), one plain GEMM of dequantized operands.  Activations: each Q8_0
- * value d * q (exact in fp32) split into two fp16 planes xh = fp16(d * q),
- * xl = fp16(d * q - xh), [n][k].  Weights: split once (eg2_split_q8_weight)
- * into wh, wl [m][k] with wh + wl == ws * q * 2^s_r and rowscale[r] = 2^-s_r.
- * out[t][r] = rowscale[r] * sum_k (xh wh + xh wl + xl wh)[t][r] with exact
- * fp16 products accumulated in fp32 (xl wl, below 2^-22 of the product, is
- * left out): the reference's sum_b D_b * ws * xs (gemma2_fast.c:242-253) up
- * to fp32 accumulation order.  k % 64 == 0, k <= 2048, m % 128 == 0; splits
- * 1, 2 or 4 with k % (64 * splits) == 0: split i writes the partial sum over
- * its k range at out + i * split_stride (split_stride >= n * m floats); the
- * product is the sum of the partials in order. */
-typedef struct {
-    float *out; const uint16_t *xh, *xl; const uint16_t *wh, *wl; const float *rowscale;
-    unsigned n, k, m, splits; uint64_t split_stride;
-} EgQ8MMF16;
-/* EgQ8GeGLU on the fp16 tensor cores: the gate and up weights interleaved in
- * 32-row chunks (rows 64c .. 64c+31 = gate rows 32c .., the next 32 = up rows
- * 32c ..; 2m rows, m % 128 == 0), split as for EgQ8MMF16.  Writes the Q8_0
- * operand of g = gelu_tanh(gate) * up as split planes out_h, out_l [n][m] and
- * the fp32 block scales scale[b * scale_stride + t]; tier as in EgGateQuant. */
-typedef struct {
-    uint16_t *out_h, *out_l; float *scale; unsigned scale_stride;
-    const uint16_t *xh, *xl; const uint16_t *wh, *wl; const float *rowscale; unsigned n, k, m, tier;
-} EgQ8GeGLUF16;
 /* Per head RMS (q, k weighted; v plain) and NEOX RoPE from host tables at the
  * token's in-sequence position (ROW_QKV_POST, gemma2_fast.c:692-706).  qkv is
  * the fused projection [n][4d | 512 | 512]; outputs are fp16 [n][heads][d]. */
@@ -158,12 +133,6 @@ int eg2_launch_ple_proj(const EgPleProj *p, void *stream);
 int eg2_launch_norm_quant(const EgNormQuant *p, void *stream);
 int eg2_launch_q8_mm(const EgQ8MM *p, void *stream);
 int eg2_launch_q8_geglu(const EgQ8GeGLU *p, void *stream);
-int eg2_launch_q8_mm_f16(const EgQ8MMF16 *p, void *stream);
-int eg2_launch_q8_geglu_f16(const EgQ8GeGLUF16 *p, void *stream);
-/* Split a SoA Q8 weight (codes [rows][k], fp32 scales [k/32][rows]) into the
- * fp16 planes and row scales of EgQ8MMF16 (done once, at load time). */
-int eg2_split_q8_weight(const int8_t *codes, const float *scales, unsigned rows, unsigned k, uint16_t *wh,
-                        uint16_t *wl, float *rowscale, void *stream);
 int eg2_launch_qkv_post(const EgQkvPost *p, void *stream);
 int eg2_launch_attention_f16(const EgAttentionF16 *p, void *stream);
 /* The same attention on the 5th-generation tensor cores, d = 256 (the

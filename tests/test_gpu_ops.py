@@ -228,140 +228,6 @@ def test_q8_mm_int32_block_accumulators_exact(ops, port, n, k, m):
     np.testing.assert_array_equal(got_exact.astype(np.int64), exact)
 
 
-def _split_weight(ops, wq, wd):
-    """eg2_split_q8_weight on the GPU: (wh, wl, rowscale) device tensors."""
-    m, k = wq.shape
-    ws = np.ascontiguousarray(f16_to_f32(wd).T)  # [k/32][m]
-    wh = torch.zeros(m * k, dtype=torch.float16, device=DEV)
-    wl = torch.zeros(m * k, dtype=torch.float16, device=DEV)
-    rs = torch.zeros(m, device=DEV)
-    ops.split_q8_weight(T(wq), T(ws), m, k, wh, wl, rs)
-    return wh, wl, rs
-
-
-def _exact_q8_product(xq, xd, wq, wd):
-    """sum_b D_b * ws_b * xs_b in float64, block by block (every term exact)."""
-    n, k = xq.shape
-    xs, ws = f16_to_f32(xd).astype(np.float64), f16_to_f32(wd).astype(np.float64)
-    out = np.zeros((n, wq.shape[0]), np.float64)
-    for b in range(k // 32):
-        D = xq[:, 32 * b:32 * b + 32].astype(np.float64) @ wq[:, 32 * b:32 * b + 32].astype(np.float64).T
-        out += D * xs[:, b:b + 1] * ws[:, b][None, :]
-    return out
-
-
-def _split_activation(xq, xd):
-    """The fast path's activation operand: d * q (exact in float32) split into
-    fp16 hi = fp16(d * q) and lo = fp16(d * q - hi), [n][k] each."""
-    n, k = xq.shape
-    v = (f16_to_f32(xd).repeat(32, axis=1) * xq.astype(np.float32)).astype(np.float32)
-    hi = v.astype(np.float16)
-    lo = (v - hi.astype(np.float32)).astype(np.float16)
-    assert np.array_equal(hi.astype(np.float64) + lo.astype(np.float64), v.astype(np.float64))
-    return hi, lo
-
-
-def _gpu_q8_mm_f16(ops, xq, xd, wq, wd, splits=1):
-    n, k = xq.shape
-    m = wq.shape[0]
-    hi, lo = _split_activation(xq, xd)
-    wh, wl, rs = _split_weight(ops, wq, wd)
-    out = torch.zeros(splits * n * m, device=DEV)
-    ops.q8_mm_f16(out, T(hi), T(lo), wh, wl, rs, n, k, m, splits, n * m)
-    return host(out).reshape(splits, n, m)
-
-
-def test_split_q8_weight_is_exact(ops):
-    """wh + wl equals ws * q * 2^s_r exactly, max |wh + wl| in [2^14, 2^15),
-    rowscale = 2^-s_r; an all-zero row gets scale 1."""
-    rng = np.random.default_rng(11)
-    m, k = 256, 512
-    wq, wd = _q8_operands(rng, m, k)
-    wq[7] = 0
-    wh, wl, rs = _split_weight(ops, wq, wd)
-    w = (wq.astype(np.float64).reshape(m, k // 32, 32) * f16_to_f32(wd).astype(np.float64)[..., None]).reshape(m, k)
-    hi = host(wh).astype(np.float64).reshape(m, k)
-    lo = host(wl).astype(np.float64).reshape(m, k)
-    r = host(rs).astype(np.float64)
-    np.testing.assert_array_equal((hi + lo) * r[:, None], w)
-    amax = np.abs(hi + lo).max(1)
-    live = amax > 0
-    assert np.all((amax[live] >= 2 ** 14) & (amax[live] < 2 ** 15))
-    assert r[7] == 1.0 and not live[7]
-
-
-@pytest.mark.parametrize("n,k,m", SHAPES)
-def test_q8_mm_f16_within_tolerance(ops, n, k, m):
-    """The fp16 tensor-core GEMM against the exact sum_b D_b * ws * xs: within
-    2e-6 of the output range (the int8 fast mode's bound)."""
-    rng = np.random.default_rng(n * 7 + k + m + 3)
-    xq, xd = _q8_operands(rng, n, k)
-    wq, wd = _q8_operands(rng, m, k)
-    got = _gpu_q8_mm_f16(ops, xq, xd, wq, wd)[0]
-    ref = _exact_q8_product(xq, xd, wq, wd)
-    err = np.abs(got - ref).max() / np.abs(ref).max()
-    print(f"f16 GEMM {n}x{k}x{m}: max error / range {err:.2e}")
-    assert err < 2e-6, err
-
-
-@pytest.mark.parametrize("n,k,m,splits", [(2048, 2048, 512, 2), (300, 1024, 512, 2), (130, 512, 512, 2),
-                                          (2048, 512, 512, 4), (64, 2048, 512, 4)])
-def test_q8_mm_f16_split_k_partials_add_up(ops, n, k, m, splits):
-    """With splits > 1 each partial covers its k range; their in-order sum is
-    the product within the same tolerance, and a single split equals the
-    whole-K launch bit for bit."""
-    rng = np.random.default_rng(n + k + m + splits)
-    xq, xd = _q8_operands(rng, n, k)
-    wq, wd = _q8_operands(rng, m, k)
-    parts = _gpu_q8_mm_f16(ops, xq, xd, wq, wd, splits)
-    total = parts[0].copy()
-    for i in range(1, splits):
-        total = (total + parts[i]).astype(np.float32)
-    ref = _exact_q8_product(xq, xd, wq, wd)
-    assert np.abs(total - ref).max() / np.abs(ref).max() < 2e-6
-    kk = k // splits
-    first = _gpu_q8_mm_f16(ops, xq[:, :kk].copy(), xd[:, :kk // 32].copy(), wq[:, :kk].copy(),
-                           wd[:, :kk // 32].copy())[0]
-    np.testing.assert_array_equal(parts[0], first)
-
-
-@pytest.mark.parametrize("n,k,m,tier", [(130, 512, 2048, 0), (2048, 512, 2048, 0), (300, 512, 2048, 1)])
-def test_q8_geglu_f16_equals_unfused(ops, n, k, m, tier):
-    """The fused fp16 GeGLU GEMM (gate/up interleaved in 32-row chunks;
-    gelu(gate) * up and Q8_0 in the epilogue, the result written as the split
-    fp16 planes of the down operand) reproduces q8_mm_f16(gate),
-    q8_mm_f16(up), gate_quant bit for bit: the same codes (hi + lo = d * q
-    exactly) and scales."""
-    rng = np.random.default_rng(n + k + m + 5)
-    xq, xd = _q8_operands(rng, n, k)
-    gq, gd = _q8_operands(rng, m, k)
-    uq, ud = _q8_operands(rng, m, k)
-    stride = (n + 127) // 128 * 128
-    gate = torch.from_numpy(_gpu_q8_mm_f16(ops, xq, xd, gq, gd)[0]).to(DEV)
-    up = torch.from_numpy(_gpu_q8_mm_f16(ops, xq, xd, uq, ud)[0]).to(DEV)
-    q_ref = torch.zeros(n * m, dtype=torch.int8, device=DEV)
-    s_ref = torch.zeros(m // 32 * stride, device=DEV)
-    ops.gate_quant(q_ref, s_ref, stride, gate.ravel(), up.ravel(), n, m, m, 0, tier=tier)
-    wq = np.zeros((2 * m, k), np.int8)
-    wd = np.zeros((2 * m, k // 32), np.uint16)
-    for c in range(m // 32):
-        wq[64 * c:64 * c + 32], wd[64 * c:64 * c + 32] = gq[32 * c:32 * c + 32], gd[32 * c:32 * c + 32]
-        wq[64 * c + 32:64 * c + 64], wd[64 * c + 32:64 * c + 64] = uq[32 * c:32 * c + 32], ud[32 * c:32 * c + 32]
-    wh, wl, rs = _split_weight(ops, wq, wd)
-    hi, lo = _split_activation(xq, xd)
-    oh = torch.zeros(n * m, dtype=torch.float16, device=DEV)
-    ol = torch.zeros(n * m, dtype=torch.float16, device=DEV)
-    sc = torch.zeros(m // 32 * stride, device=DEV)
-    ops.q8_geglu_f16(oh, ol, sc, stride, T(hi), T(lo), wh, wl, rs, n, k, m, tier=tier)
-    scales = host(sc).reshape(-1, stride)[:, :n]
-    np.testing.assert_array_equal(scales, host(s_ref).reshape(-1, stride)[:, :n])
-    v = host(oh).astype(np.float64) + host(ol).astype(np.float64)
-    d = np.repeat(scales.T.astype(np.float64), 32, axis=1).ravel()
-    codes = np.where(d != 0, v / np.where(d != 0, d, 1), 0)
-    np.testing.assert_array_equal(codes, np.round(codes))
-    np.testing.assert_array_equal(codes.astype(np.int32), host(q_ref).astype(np.int32))
-
-
 @pytest.mark.parametrize("n,k,m,exact,tier", [(130, 512, 2048, False, 0), (2048, 512, 2048, False, 0),
                                               (77, 1024, 128, True, 1), (300, 512, 2048, True, 1)])
 def test_q8_geglu_equals_unfused(ops, n, k, m, exact, tier):
