@@ -11,11 +11,15 @@ the model's shapes.  Every rank holds its own weight
 replica and embeds its own wave (weak scaling, no data-path collective); the
 process group only provides the barrier and the max-over-ranks time.
 
-value  -- device time of K graph replays with inputs resident in HBM, CUDA
-          events on the executor's stream, an L2 flush (256 MiB write) between
-          steps outside the timed events; whole-job tokens / max-rank time.
-e2e    -- the same waves through ei_gemma2_kfd_batch with host buffers: ids /
-          bounds / positions H2D and the embeddings D2H every step, wall time.
+value  -- device time of K graph replays with inputs resident in HBM (two
+          waves in flight: replays alternate over the context's two lanes),
+          CUDA events on the executor's stream around all K; every wave streams
+          151 MB of weights and writes 100 MB of PLE rows, more than the 126 MB
+          L2; whole-job tokens / max-rank time.  `serial` beside it: one wave
+          at a time with an L2 flush (256 MiB write) between steps.
+e2e    -- the same waves through ei_gemma2_kfd_batch with host buffers, called
+          from two host threads (ids / bounds / positions H2D and the
+          embeddings D2H every call), wall time.
 --impl reference runs the reference's own CPU graph (oracle/_ref, compiled
 from its sources) on the same workload on the host cores, rank 0 only.
 """
@@ -28,6 +32,7 @@ import os
 import statistics
 import subprocess
 import sys
+import threading
 import time
 
 import numpy as np
@@ -224,7 +229,8 @@ def wave_config(args, desc, n, batch, world):
     return {"workload": desc, "model": "EmbeddingGemma 2 text graph, seeded synthetic GGUF (seed 1234, "
             "BASELINE weight distributions)", "tokens_per_wave_per_gpu": n, "sequences_per_wave": batch,
             "parallelism": f"replicas x{world} (whole waves per GPU, no collective)",
-            "l2": "256 MiB write between timed steps; per-wave working set > L2 (151 MB weights, 100 MB PLE)"}
+            "l2": "inputs larger than L2: each wave streams 151 MB of weights and writes 100 MB of PLE rows "
+                  "(L2 126 MB); the serial figure also writes 256 MiB between steps"}
 
 
 # (name, sequence bodies) of the GPU comparison: the reference CUDA bench's
@@ -845,45 +851,71 @@ def main():
     stream = torch.cuda.ExternalStream(ex.stream, device=local)
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=local)
 
-    # ---- value: device-resident waves
+    # ---- value: device-resident waves, two in flight (the lanes alternate)
     stage()
-    for _ in range(args.warmup):
-        ex.launch(1)
+    ex.launch(max(args.warmup, 2))
     ex.finish()
-    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     barrier(world)
     torch.cuda.synchronize()
     with ClockSampler(local) as clocks:
         with torch.cuda.stream(stream):
-            for i in range(args.steps):
-                flush.zero_()  # L2 flush, outside the timed events
-                starts[i].record(stream)
-                ex.launch(1)
-                ends[i].record(stream)
+            e0.record(stream)
+            ex.launch(args.steps)
+            e1.record(stream)
         torch.cuda.synchronize()
     barrier(world)
     out_dev = ex.finish()
-    step_ms = [s.elapsed_time(e) for s, e in zip(starts, ends)]
-    dev_ms = sum(step_ms)
+    dev_ms = e0.elapsed_time(e1)
     dev_ms_max = reduce_max(dev_ms, world, f"cuda:{local}")
 
-    # ---- e2e: the public C ABI with host buffers every step; each call's
-    # wall time is also the latency of the request(s) the wave carries
+    # ---- serial: one wave at a time on one lane, L2 flushed between steps
+    serial_steps = min(args.steps, 100)
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(serial_steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(serial_steps)]
+    torch.cuda.synchronize()
+    with torch.cuda.stream(stream):
+        for i in range(serial_steps):
+            flush.zero_()  # L2 flush, outside the timed events
+            starts[i].record(stream)
+            ex.launch(1)
+            ends[i].record(stream)
+    torch.cuda.synchronize()
+    serial_ms = sum(a.elapsed_time(b) for a, b in zip(starts, ends)) / serial_steps
+
+    # ---- e2e: the public C ABI with host buffers every call, from two host
+    # threads (the context runs two calls' waves at once); wall time
     for _ in range(args.warmup):
         run_batch()
+    outs = [None, None]
+    busy_ms = [[], []]
+
+    def caller(k, count):
+        for _ in range(count):
+            c0 = time.perf_counter()
+            outs[k] = run_batch()
+            busy_ms[k].append((time.perf_counter() - c0) * 1000.0)
     barrier(world)
     torch.cuda.synchronize()
-    call_ms = []
+    threads = [threading.Thread(target=caller, args=(k, args.steps // 2 + (k < args.steps % 2)))
+               for k in range(2)]
     t0 = time.perf_counter()
-    for _ in range(args.steps):
-        c0 = time.perf_counter()
-        out = run_batch()
-        call_ms.append((time.perf_counter() - c0) * 1000.0)
+    for t in threads:
+        t.start()
+    for t in threads:
+        t.join()
     e2e_ms = (time.perf_counter() - t0) * 1000.0
     barrier(world)
     e2e_ms_max = reduce_max(e2e_ms, world, f"cuda:{local}")
-    assert np.isfinite(out).all() and np.allclose(out, out_dev, atol=1e-6)
+    for out in outs:
+        assert np.isfinite(out).all() and np.allclose(out, out_dev, atol=1e-6)
+    # latency of one call alone (no other call in flight)
+    call_ms = []
+    for _ in range(min(args.steps, 100)):
+        c0 = time.perf_counter()
+        run_batch()
+        call_ms.append((time.perf_counter() - c0) * 1000.0)
+    loaded_ms = busy_ms[0] + busy_ms[1]
 
     # ---- dominant kernel: per-group event timing of one eager wave
     stage()
@@ -901,9 +933,15 @@ def main():
         "config": wave_config(args, desc, n, batch, world),
         "e2e": {"value": whole_job_rate(n, world, args.steps, e2e_ms_max), "unit": "tokens/s",
                 "h2d_bytes_per_step": h2d_bytes,
-                "d2h_bytes_per_step": batch * 768 * 4},
+                "d2h_bytes_per_step": batch * 768 * 4,
+                "api": "ei_gemma2_kfd_batch from two host threads (two calls' waves in flight)"},
+        "serial": {"ms_per_step": serial_ms, "value": whole_job_rate(n, 1, 1, serial_ms), "steps": serial_steps,
+                   "what": "one wave at a time on one lane, 256 MiB L2 flush between steps, rank 0"},
         "latency_ms": {"p50": float(np.percentile(call_ms, 50)), "p99": float(np.percentile(call_ms, 99)),
-                       "what": f"one ei_gemma2_kfd_batch call of the wave ({batch} texts), host buffers, rank {rank}"},
+                       "loaded_p50": float(np.percentile(loaded_ms, 50)),
+                       "loaded_p99": float(np.percentile(loaded_ms, 99)),
+                       "what": f"one ei_gemma2_kfd_batch call of the wave ({batch} texts), host buffers, rank {rank}: "
+                               "alone (p50/p99) and during the two-thread e2e run (loaded_*)"},
         "gpu_launches": ex.kernels_per_wave * args.steps,
         "roofline": {"kernel": "q8gemm_kernel (all Q8_0 GEMM launches of a wave)", "bound": "tensor",
                      "achieved": achieved, "peak": int8_peak, "unit": "TOP/s", "frac": achieved / int8_peak,

@@ -18,8 +18,11 @@
 //   30 s submit/wait timeout and poisoning (:21,190-214) -> a deadline while
 //          polling the wave's completion event, plus the device error word set
 //          by bounded in-kernel waits; either poisons the context.
+#include <atomic>
 #include <chrono>
 #include <cmath>
+#include <condition_variable>
+#include <exception>
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
@@ -109,12 +112,44 @@ struct Profiler {
     }
 };
 
+// One wave's device working set: its stream, the per-wave input block, the
+// activation arena for cap packed tokens, the tensor maps over it, the CUDA
+// graphs captured against it, and the pinned host staging of the pipeline slot
+// that runs on it.  A context holds LANES of them over one set of weights, so
+// two submitted waves run concurrently on the GPU (each wave's ~300 kernels
+// leave SMs idle in their ramps and tails, which the other wave's kernels fill).
+struct Lane {
+    cudaStream_t stream = nullptr;
+    cudaEvent_t fork = nullptr, join = nullptr;  // launch(): lane 0 -> this lane -> lane 0
+    int *ids = nullptr;
+    unsigned *bounds = nullptr, *pos = nullptr, *offsets = nullptr, *seq_count = nullptr;
+    float *xin = nullptr;  // soft-token waves: the uploaded input rows [cap][512]
+    float *x = nullptr, *ple = nullptr, *qkv = nullptr, *attn = nullptr, *h = nullptr, *y = nullptr, *pooled = nullptr,
+          *xs = nullptr, *gs = nullptr;
+    void *x_hi = nullptr, *x_lo = nullptr, *qh = nullptr, *kh = nullptr, *vh = nullptr;
+    int8_t *xq = nullptr, *gq = nullptr;  // Q8 activations; gq/gs: the GeGLU output (FFN down operand)
+    float *qf = nullptr, *kf = nullptr, *vf = nullptr;  // parity mode: fp32 q/k/v
+    CUtensorMap tm_xq[3]{}, tm_xs[3]{}, tm_gq{}, tm_gs{}, tm_hi{}, tm_lo{};
+    std::map<uint64_t, cudaGraphExec_t> graphs;  // per wave shape
+    cudaGraphExec_t staged_graph = nullptr;
+    // Host staging (pinned) of the pipeline slot on this lane.
+    uint32_t *in = nullptr;  // ids | bounds(2) | pos | offsets | sequence count
+    float *rows = nullptr;   // soft-token waves: [cap][512] input rows (allocated on first use)
+    float *out = nullptr;
+    int *err = nullptr;  // the device error word, read back with the wave
+    cudaEvent_t done = nullptr;
+    size_t batch = 0;
+    bool busy = false;     // a wave on this lane is not delivered yet
+    bool by_call = false;  // ... and a synchronous call (not submit) owns it
+};
+
 struct Backend {
     const ei_gguf *model;
     int device = 0;
-    cudaStream_t stream = nullptr;
+    cudaStream_t stream = nullptr;  // weight upload; then the first lane's stream
     std::mutex mutex;
-    bool poisoned = false;
+    std::condition_variable lane_freed;  // a synchronous call released its lane
+    std::atomic<bool> poisoned{false};
 
     std::vector<void *> allocations;
     std::vector<Layer> layers;
@@ -124,15 +159,7 @@ struct Backend {
     const float *ple_norm = nullptr, *output_norm = nullptr;
     float *rope_cos[2] = {}, *rope_sin[2] = {};
 
-    // arena
-    int *ids = nullptr;
-    unsigned *bounds = nullptr, *pos = nullptr, *offsets = nullptr, *seq_count = nullptr;
-    float *xin = nullptr;  // soft-token waves: the uploaded input rows [cap][512]
-    float *x = nullptr, *ple = nullptr, *qkv = nullptr, *attn = nullptr, *h = nullptr, *y = nullptr, *pooled = nullptr,
-          *xs = nullptr, *gs = nullptr;
-    void *x_hi = nullptr, *x_lo = nullptr, *qh = nullptr, *kh = nullptr, *vh = nullptr;
-    int8_t *xq = nullptr, *gq = nullptr;  // Q8 activations; gq/gs: the GeGLU output (FFN down operand)
-    CUtensorMap tm_xq[3]{}, tm_xs[3]{}, tm_gq{}, tm_gs{}, tm_hi{}, tm_lo{}, tm_ple{};
+    CUtensorMap tm_ple{};
     // Parity mode (EG2_B200_EXACT): GEMMs in the reference scalar tile's rounding
     // order, PLE projection and attention on the CUDA-core exact-order kernels
     // with fp32 q/k/v; every other kernel is bit-exact in both modes.
@@ -142,31 +169,18 @@ struct Backend {
     // EG2_B200_SCALAR_TIER: the scalar CPU tier's quantizer rounding and GELU
     // (roundf, tanhf) instead of the x86 tiers' (the fast path's choice).
     int tier = 0;
-    float *qf = nullptr, *kf = nullptr, *vf = nullptr;
 
-    // host staging (pinned)
-    // Host staging (pinned), one set per pipeline slot: a wave can be submitted
-    // to one slot while the wave of the other slot is still on the GPU (stream
-    // order keeps the single device input block and output buffer safe).
-    static constexpr int SLOTS = 2;
-    struct Slot {
-        uint32_t *in = nullptr;  // ids | bounds(2) | pos | offsets | sequence count
-        float *rows = nullptr;   // soft-token waves: [cap][512] input rows (allocated on first use)
-        float *out = nullptr;
-        int *err = nullptr;  // the device error word, read back with the wave
-        cudaEvent_t done = nullptr;
-        size_t batch = 0;
-        bool busy = false;
-    };
-    Slot slots[SLOTS];
+    // Pipeline slot i runs on lane i: a wave can be submitted to one slot
+    // while the other slot's wave is still on the GPU, on its own stream and
+    // arena.
+    static constexpr int LANES = 2;
+    Lane lanes[LANES];
     int next_slot = 0;
 
-    // graphs per wave shape
-    std::map<uint64_t, cudaGraphExec_t> graphs;
+    // The split form's staged wave (the same inputs staged in every lane).
     unsigned staged_n = 0;
-    bool staged_rows = false;
+    bool staged_rows = false, staged = false;
     size_t staged_batch = 0;
-    cudaGraphExec_t staged_graph = nullptr;
     int kernels_per_wave = 0;
 
     template <class T>
@@ -260,8 +274,12 @@ struct Backend {
         if (prop.major != 10 || prop.minor != 0)
             throw std::runtime_error(std::string("supported CUDA device not found (sm_100 required, got ") +
                                      prop.name + ")");
-        ck(cudaStreamCreateWithFlags(&stream, cudaStreamNonBlocking), "cudaStreamCreate");
-        for (Slot &sl : slots) ck(cudaEventCreateWithFlags(&sl.done, cudaEventDisableTiming), "cudaEventCreate");
+        for (Lane &ln : lanes) {
+            ck(cudaStreamCreateWithFlags(&ln.stream, cudaStreamNonBlocking), "cudaStreamCreate");
+            for (cudaEvent_t *e : {&ln.done, &ln.fork, &ln.join})
+                ck(cudaEventCreateWithFlags(e, cudaEventDisableTiming), "cudaEventCreate");
+        }
+        stream = lanes[0].stream;
         ck(init_kernel_attributes(), "kernel attributes");
 
         // ---- weights
@@ -332,51 +350,8 @@ struct Backend {
             ck(cudaMemcpy(rope_sin[b], s.data(), s.size() * 4, cudaMemcpyHostToDevice), "rope upload");
         }
 
-        // ---- arena for cap packed tokens.  The per-wave inputs share one block
-        // laid out like the pinned staging buffer (ids | bounds | pos | offsets),
-        // so a wave uploads them with a single copy.
-        unsigned *in_block = dalloc<unsigned>(5 * cap + 2);
-        ids = reinterpret_cast<int *>(in_block);
-        bounds = in_block + cap;
-        pos = in_block + 3 * cap;
-        offsets = in_block + 4 * cap;
-        seq_count = in_block + 5 * cap + 1;
-        x = dalloc<float>(size_t(cap) * 512);
-        x_hi = dalloc<uint16_t>(size_t(cap) * 512);
-        x_lo = dalloc<uint16_t>(size_t(cap) * 512);
-        ple = dalloc<float>(size_t(cap) * 24 * 512);
-        xq = dalloc<int8_t>(size_t(cap) * 2048);
-        xs = dalloc<float>(size_t(64) * cap);
-        qkv = dalloc<float>(size_t(cap) * 3072);
-        qh = dalloc<uint16_t>(size_t(cap) * 2048);
-        kh = dalloc<uint16_t>(size_t(cap) * 512);
-        vh = dalloc<uint16_t>(size_t(cap) * 512);
-        attn = dalloc<float>(size_t(cap) * 2048);
-        h = dalloc<float>(size_t(cap) * 512);
-        gq = dalloc<int8_t>(size_t(cap) * 2048);
-        gs = dalloc<float>(size_t(64) * cap);
-        y = dalloc<float>(size_t(cap) * 768);
-        pooled = dalloc<float>(size_t(cap) * 768);
-        if (exact) {
-            qf = dalloc<float>(size_t(cap) * 2048);
-            kf = dalloc<float>(size_t(cap) * 512);
-            vf = dalloc<float>(size_t(cap) * 512);
-        }
-        const int ks[3] = {512, 1024, 2048};
-        for (int i = 0; i < 3; ++i)
-            if (!q8_tmap(&tm_xq[i], xq, uint64_t(ks[i]), cap, 64) ||
-                !scale_tmap(&tm_xs[i], xs, cap, uint64_t(ks[i] / 32), 64))
-                throw std::runtime_error("tensor map (activations)");
-        if (!q8_tmap(&tm_gq, gq, 2048, cap, 64) || !scale_tmap(&tm_gs, gs, cap, 64, 64))
-            throw std::runtime_error("tensor map (GeGLU activations)");
-        if (!bf16_tmap(&tm_hi, x_hi, 512, cap, 128) || !bf16_tmap(&tm_lo, x_lo, 512, cap, 128) ||
-            !bf16_tmap(&tm_ple, ple_w, 512, 24 * 512, 256))
-            throw std::runtime_error("tensor map (PLE)");
-        for (Slot &sl : slots) {
-            ck(cudaMallocHost(&sl.in, sizeof(uint32_t) * (5 * cap + 2)), "cudaMallocHost");
-            ck(cudaMallocHost(&sl.err, sizeof(int)), "cudaMallocHost");
-            ck(cudaMallocHost(&sl.out, sizeof(float) * cap * 768), "cudaMallocHost");
-        }
+        if (!bf16_tmap(&tm_ple, ple_w, 512, 24 * 512, 256)) throw std::runtime_error("tensor map (PLE)");
+        for (Lane &ln : lanes) alloc_lane(ln);
         ck(cudaStreamSynchronize(stream), "weight upload");
         // The device error word is not cleared here: it is shared by every
         // context on this device, and a wave of another context may have set it
@@ -390,33 +365,81 @@ struct Backend {
         }
     }
 
+    // The arena of one lane for cap packed tokens.  The per-wave inputs share
+    // one block laid out like the pinned staging buffer (ids | bounds | pos |
+    // offsets | count), so a wave uploads them with a single copy.
+    void alloc_lane(Lane &ln) {
+        unsigned *in_block = dalloc<unsigned>(5 * cap + 2);
+        ln.ids = reinterpret_cast<int *>(in_block);
+        ln.bounds = in_block + cap;
+        ln.pos = in_block + 3 * cap;
+        ln.offsets = in_block + 4 * cap;
+        ln.seq_count = in_block + 5 * cap + 1;
+        ln.x = dalloc<float>(size_t(cap) * 512);
+        ln.x_hi = dalloc<uint16_t>(size_t(cap) * 512);
+        ln.x_lo = dalloc<uint16_t>(size_t(cap) * 512);
+        ln.ple = dalloc<float>(size_t(cap) * 24 * 512);
+        ln.xq = dalloc<int8_t>(size_t(cap) * 2048);
+        ln.xs = dalloc<float>(size_t(64) * cap);
+        ln.qkv = dalloc<float>(size_t(cap) * 3072);
+        ln.qh = dalloc<uint16_t>(size_t(cap) * 2048);
+        ln.kh = dalloc<uint16_t>(size_t(cap) * 512);
+        ln.vh = dalloc<uint16_t>(size_t(cap) * 512);
+        ln.attn = dalloc<float>(size_t(cap) * 2048);
+        ln.h = dalloc<float>(size_t(cap) * 512);
+        ln.gq = dalloc<int8_t>(size_t(cap) * 2048);
+        ln.gs = dalloc<float>(size_t(64) * cap);
+        ln.y = dalloc<float>(size_t(cap) * 768);
+        ln.pooled = dalloc<float>(size_t(cap) * 768);
+        if (exact) {
+            ln.qf = dalloc<float>(size_t(cap) * 2048);
+            ln.kf = dalloc<float>(size_t(cap) * 512);
+            ln.vf = dalloc<float>(size_t(cap) * 512);
+        }
+        const int ks[3] = {512, 1024, 2048};
+        for (int i = 0; i < 3; ++i)
+            if (!q8_tmap(&ln.tm_xq[i], ln.xq, uint64_t(ks[i]), cap, 64) ||
+                !scale_tmap(&ln.tm_xs[i], ln.xs, cap, uint64_t(ks[i] / 32), 64))
+                throw std::runtime_error("tensor map (activations)");
+        if (!q8_tmap(&ln.tm_gq, ln.gq, 2048, cap, 64) || !scale_tmap(&ln.tm_gs, ln.gs, cap, 64, 64))
+            throw std::runtime_error("tensor map (GeGLU activations)");
+        if (!bf16_tmap(&ln.tm_hi, ln.x_hi, 512, cap, 128) || !bf16_tmap(&ln.tm_lo, ln.x_lo, 512, cap, 128))
+            throw std::runtime_error("tensor map (PLE)");
+        ck(cudaMallocHost(&ln.in, sizeof(uint32_t) * (5 * cap + 2)), "cudaMallocHost");
+        ck(cudaMallocHost(&ln.err, sizeof(int)), "cudaMallocHost");
+        ck(cudaMallocHost(&ln.out, sizeof(float) * cap * 768), "cudaMallocHost");
+    }
+
     ~Backend() {
         if (device >= 0) cudaSetDevice(device);
-        if (stream) cudaStreamSynchronize(stream);
-        for (auto &kv : graphs) cudaGraphExecDestroy(kv.second);
+        for (Lane &ln : lanes)
+            if (ln.stream) cudaStreamSynchronize(ln.stream);
+        for (Lane &ln : lanes)
+            for (auto &kv : ln.graphs) cudaGraphExecDestroy(kv.second);
         for (void *p : allocations) cudaFree(p);
-        for (Slot &sl : slots) {
-            if (sl.in) cudaFreeHost(sl.in);
-            if (sl.rows) cudaFreeHost(sl.rows);
-            if (sl.err) cudaFreeHost(sl.err);
-            if (sl.out) cudaFreeHost(sl.out);
-            if (sl.done) cudaEventDestroy(sl.done);
+        for (Lane &ln : lanes) {
+            if (ln.in) cudaFreeHost(ln.in);
+            if (ln.rows) cudaFreeHost(ln.rows);
+            if (ln.err) cudaFreeHost(ln.err);
+            if (ln.out) cudaFreeHost(ln.out);
+            for (cudaEvent_t e : {ln.done, ln.fork, ln.join})
+                if (e) cudaEventDestroy(e);
+            if (ln.stream) cudaStreamDestroy(ln.stream);
         }
-        if (stream) cudaStreamDestroy(stream);
     }
 
     static int kidx(int k) { return k == 512 ? 0 : k == 1024 ? 1 : 2; }
-    void gemm(const Q8Weight &w, float *out, int ldo, int n, cudaStream_t s) {
-        ck(launch_q8gemm(w.tmap, tm_xq[kidx(w.k)], w.tscale, tm_xs[kidx(w.k)], exact, out, ldo, n, w.rows, w.k,
-                         s),
+    void gemm(const Lane &ln, const Q8Weight &w, float *out, int ldo, int n) {
+        ck(launch_q8gemm(w.tmap, ln.tm_xq[kidx(w.k)], w.tscale, ln.tm_xs[kidx(w.k)], exact, out, ldo, n, w.rows, w.k,
+                         ln.stream),
            "q8 GEMM");
     }
 
     // Both layer kinds run the tensor-core attention through maps whose token
     // extent is this wave's N (captured into its graph).
-    void attention_maps(int N, AttnTcMaps (&tc_maps)[2]) {
-        if (!exact && (!attention_tc_maps(&tc_maps[0], qh, kh, vh, N, 256) ||
-                       !attention_tc_maps(&tc_maps[1], qh, kh, vh, N, 512)))
+    void attention_maps(const Lane &ln, int N, AttnTcMaps (&tc_maps)[2]) {
+        if (!exact && (!attention_tc_maps(&tc_maps[0], ln.qh, ln.kh, ln.vh, N, 256) ||
+                       !attention_tc_maps(&tc_maps[1], ln.qh, ln.kh, ln.vh, N, 512)))
             ck(cudaErrorInvalidValue, "attention maps");
     }
 
@@ -424,142 +447,155 @@ struct Backend {
     // operand of attn_norm(x) already in xq/xs; its last kernel leaves the next
     // layer's operand (or the output head's) there.  Returns kernels launched.
     template <class Mark>
-    int enqueue_layer(int l, int N, cudaStream_t s, const AttnTcMaps (&tc_maps)[2], Mark &&mark) {
+    int enqueue_layer(int l, int N, Lane &ln, const AttnTcMaps (&tc_maps)[2], Mark &&mark) {
         int launches = 0;
         const Layer &L = layers[l];
         const int rb = L.d == 512 ? 1 : 0;
-        gemm(L.qkv, qkv, L.qkv.rows, N, s), ++launches;
+        cudaStream_t s = ln.stream;
+        gemm(ln, L.qkv, ln.qkv, L.qkv.rows, N), ++launches;
         mark("gemm_qkv");
         if (exact) {
-            ck(launch_qkv_post(qf, kf, vf, qkv, L.q_norm, L.k_norm, rope_cos[rb], rope_sin[rb], pos, N, L.d, s,
-                               true),
+            ck(launch_qkv_post(ln.qf, ln.kf, ln.vf, ln.qkv, L.q_norm, L.k_norm, rope_cos[rb], rope_sin[rb], ln.pos, N,
+                               L.d, s, true),
                "qkv_post"),
                 ++launches;
             mark("qkv_post");
-            ck(launch_attention_exact(attn, qf, kf, vf, bounds, N, L.d, L.d == 512 ? 0 : 512, s), "attention"),
+            ck(launch_attention_exact(ln.attn, ln.qf, ln.kf, ln.vf, ln.bounds, N, L.d, L.d == 512 ? 0 : 512, s),
+               "attention"),
                 ++launches;
         } else {
-            ck(launch_qkv_post(qh, kh, vh, qkv, L.q_norm, L.k_norm, rope_cos[rb], rope_sin[rb], pos, N, L.d, s,
-                               false),
+            ck(launch_qkv_post(ln.qh, ln.kh, ln.vh, ln.qkv, L.q_norm, L.k_norm, rope_cos[rb], rope_sin[rb], ln.pos, N,
+                               L.d, s, false),
                "qkv_post"),
                 ++launches;
             mark("qkv_post");
             // The O projection's Q8 operand is written by the attention itself.
-            ck(launch_attention_tc(tc_maps[L.d == 512], nullptr, bounds, N, L.d == 512 ? 0 : 512, s, xq, xs, cap,
-                                   tier),
+            ck(launch_attention_tc(tc_maps[L.d == 512], nullptr, ln.bounds, N, L.d == 512 ? 0 : 512, s, ln.xq, ln.xs,
+                                   cap, tier),
                "attention");
             ++launches;
         }
         mark(L.d == 512 ? "attention_global" : "attention_local");
         if (exact) {
-            ck(launch_norm_quant(xq, xs, cap, nullptr, attn, nullptr, N, 4 * L.d, s, tier), "quant"), ++launches;
+            ck(launch_norm_quant(ln.xq, ln.xs, cap, nullptr, ln.attn, nullptr, N, 4 * L.d, s, tier), "quant"),
+                ++launches;
             mark("quant_attn");
         }
-        gemm(L.o, h, 512, N, s), ++launches;
+        gemm(ln, L.o, ln.h, 512, N), ++launches;
         mark("gemm_o");
-        ck(launch_post_add(x, h, L.post_attn_norm, nullptr, xq, xs, cap, L.ffn_norm, N, s, tier), "post_add"), ++launches;
+        ck(launch_post_add(ln.x, ln.h, L.post_attn_norm, nullptr, ln.xq, ln.xs, cap, L.ffn_norm, N, s, tier),
+           "post_add"),
+            ++launches;
         mark("post_add");
         // ffn_gate and ffn_up in one GEMM whose epilogue applies gelu(gate) * up
         // and quantizes (ROW_GELU_QUANT fused); the result is the down operand.
-        ck(launch_q8gemm_geglu(L.gu.tmap, tm_xq[0], L.gu.tscale, tm_xs[0], exact, gq, gs, cap, N, L.gu.rows, L.gu.k,
-                               s, tier),
+        ck(launch_q8gemm_geglu(L.gu.tmap, ln.tm_xq[0], L.gu.tscale, ln.tm_xs[0], exact, ln.gq, ln.gs, cap, N,
+                               L.gu.rows, L.gu.k, s, tier),
            "GeGLU GEMM"),
             ++launches;
         mark("gemm_geglu");
-        ck(launch_q8gemm(L.down.tmap, tm_gq, L.down.tscale, tm_gs, exact, h, 512, N, L.down.rows, L.down.k, s),
+        ck(launch_q8gemm(L.down.tmap, ln.tm_gq, L.down.tscale, ln.tm_gs, exact, ln.h, 512, N, L.down.rows, L.down.k,
+                         s),
            "q8 GEMM"),
             ++launches;
         mark("gemm_down");
-        ck(launch_post_add(x, h, L.post_ffw_norm, nullptr, xq, xs, cap, nullptr, N, s, tier), "post_add"), ++launches;
+        ck(launch_post_add(ln.x, ln.h, L.post_ffw_norm, nullptr, ln.xq, ln.xs, cap, nullptr, N, s, tier), "post_add"),
+            ++launches;
         mark("post_add");
-        gemm(L.inp_gate, h, 512, N, s), ++launches;
+        gemm(ln, L.inp_gate, ln.h, 512, N), ++launches;
         mark("gemm_inp_gate");
-        ck(launch_gate_quant(xq, xs, cap, h, ple, N, 512, 24 * 512, l * 512, s, tier), "ple gate"), ++launches;
+        ck(launch_gate_quant(ln.xq, ln.xs, cap, ln.h, ln.ple, N, 512, 24 * 512, l * 512, s, tier), "ple gate"),
+            ++launches;
         mark("ple_gate_quant");
-        gemm(L.proj, h, 512, N, s), ++launches;
+        gemm(ln, L.proj, ln.h, 512, N), ++launches;
         mark("gemm_proj");
         const float *next = l + 1 < 24 ? layers[l + 1].attn_norm : output_norm;
-        ck(launch_post_add(x, h, L.post_norm, L.out_scale, xq, xs, cap, next, N, s, tier), "post_add"), ++launches;
+        ck(launch_post_add(ln.x, ln.h, L.post_norm, L.out_scale, ln.xq, ln.xs, cap, next, N, s, tier), "post_add"),
+            ++launches;
         mark("post_add");
         return launches;
     }
 
-    // The whole wave as a launch sequence (captured into a graph, or run eagerly
-    // under the profiler).  Returns the number of kernels launched.
+    // The whole wave as a launch sequence on a lane (captured into a graph, or
+    // run eagerly under the profiler).  Returns the number of kernels launched.
     // rows: a soft-token wave, whose x was uploaded with the inputs.
-    int enqueue(unsigned n, cudaStream_t s, Profiler *prof, bool rows = false) {
+    int enqueue(unsigned n, Lane &ln, Profiler *prof, bool rows = false) {
         int launches = 0;
         auto mark = [&](const char *name) {
             if (prof) prof->mark(name);
         };
         const int N = int(n);
+        cudaStream_t s = ln.stream;
         AttnTcMaps tc_maps[2]{};
-        attention_maps(N, tc_maps);
+        attention_maps(ln, N, tc_maps);
         mark("start");
         if (rows)
-            ck(launch_input_rows(x, x_hi, x_lo, xin, N, s), "input rows"), ++launches;
+            ck(launch_input_rows(ln.x, ln.x_hi, ln.x_lo, ln.xin, N, s), "input rows"), ++launches;
         else
-            ck(launch_embed(x, x_hi, x_lo, token_embd, ids, N, s), "embed"), ++launches;
+            ck(launch_embed(ln.x, ln.x_hi, ln.x_lo, token_embd, ln.ids, N, s), "embed"), ++launches;
         mark("embed");
         if (exact)
-            ck(launch_ple_exact(ple, x, ple_w, ple_norm, N, s), "PLE"), launches += 2;
+            ck(launch_ple_exact(ln.ple, ln.x, ple_w, ple_norm, N, s), "PLE"), launches += 2;
         else
-            ck(launch_ple(tm_hi, tm_lo, tm_ple, ple, ple_norm, N, s), "PLE"), ++launches;
+            ck(launch_ple(ln.tm_hi, ln.tm_lo, tm_ple, ln.ple, ple_norm, N, s), "PLE"), ++launches;
         mark("ple_proj");
-        ck(launch_norm_quant(xq, xs, cap, nullptr, x, layers[0].attn_norm, N, 512, s, tier), "norm"), ++launches;
+        ck(launch_norm_quant(ln.xq, ln.xs, cap, nullptr, ln.x, layers[0].attn_norm, N, 512, s, tier), "norm"),
+            ++launches;
         mark("norm_quant");
-        for (int l = 0; l < 24; ++l) launches += enqueue_layer(l, N, s, tc_maps, mark);
-        gemm(output, y, 768, N, s), ++launches;
+        for (int l = 0; l < 24; ++l) launches += enqueue_layer(l, N, ln, tc_maps, mark);
+        gemm(ln, output, ln.y, 768, N), ++launches;
         mark("gemm_output");
         // The grid covers every sequence a wave of n tokens can hold; the
         // wave's own count is read on the device.
-        ck(launch_pool_l2(pooled, y, offsets, int(n), 768, s, seq_count), "pool"), launches += 2;
+        ck(launch_pool_l2(ln.pooled, ln.y, ln.offsets, int(n), 768, s, ln.seq_count), "pool"), launches += 2;
         mark("pool_l2");
         return launches;
     }
 
-    cudaGraphExec_t graph_for(unsigned n, bool rows = false) {
+    cudaGraphExec_t graph_for(Lane &ln, unsigned n, bool rows = false) {
         const uint64_t key = n | uint64_t(rows) << 32;
-        auto it = graphs.find(key);
-        if (it != graphs.end()) return it->second;
+        auto it = ln.graphs.find(key);
+        if (it != ln.graphs.end()) return it->second;
         // Keys are (bucketed token count, ids or rows): at most 2 * cap / BUCKET
         // = 256 for the widest context, so this flush only guards the bound.
-        if (graphs.size() >= 256) {
-            ck(cudaStreamSynchronize(stream), "graph cache flush");
-            for (auto &kv : graphs) cudaGraphExecDestroy(kv.second);
-            graphs.clear();
-            staged_graph = nullptr;  // stage() again before launch()
+        if (ln.graphs.size() >= 256) {
+            ck(cudaStreamSynchronize(ln.stream), "graph cache flush");
+            for (auto &kv : ln.graphs) cudaGraphExecDestroy(kv.second);
+            ln.graphs.clear();
+            ln.staged_graph = nullptr;
+            staged = false;  // stage() again before launch()
         }
         cudaGraph_t graph = nullptr;
-        ck(cudaStreamBeginCapture(stream, cudaStreamCaptureModeThreadLocal), "begin capture");
+        ck(cudaStreamBeginCapture(ln.stream, cudaStreamCaptureModeThreadLocal), "begin capture");
         int launches = 0;
         try {
-            launches = enqueue(n, stream, nullptr, rows);
+            launches = enqueue(n, ln, nullptr, rows);
         } catch (...) {
-            cudaStreamEndCapture(stream, &graph);
+            cudaStreamEndCapture(ln.stream, &graph);
             if (graph) cudaGraphDestroy(graph);
             throw;
         }
-        ck(cudaStreamEndCapture(stream, &graph), "end capture");
+        ck(cudaStreamEndCapture(ln.stream, &graph), "end capture");
         cudaGraphExec_t exec = nullptr;
         const cudaError_t e = cudaGraphInstantiate(&exec, graph, 0);
         cudaGraphDestroy(graph);
         ck(e, "graph instantiate");
         kernels_per_wave = launches;
-        graphs[key] = exec;
+        ln.graphs[key] = exec;
         return exec;
     }
 
-    // gemma2_kfd.cpp:271-296: validation, bounds and positions into a slot's
-    // staging buffer, padded to the bucket; returns the padded token count.
-    // A soft-token wave (in_rows set, in_ids NULL) uploads its rows, padded
-    // with zero rows to the bucket, into xin (allocated on first use).
-    unsigned fill(Slot &sl, const int32_t *in_ids, const size_t *in_off, size_t batch,
+    // gemma2_kfd.cpp:271-296: validation, bounds and positions into a lane's
+    // staging buffer, padded to the bucket, and the upload on its stream;
+    // returns the padded token count.  A soft-token wave (in_rows set, in_ids
+    // NULL) uploads its rows, padded with zero rows to the bucket, into xin
+    // (allocated on first use).
+    unsigned fill(Lane &ln, const int32_t *in_ids, const size_t *in_off, size_t batch,
                   const float *in_rows = nullptr) {
         if (in_rows) validate_rows(in_rows, in_off, batch, cap);
         else validate_wave(in_ids, in_off, batch, cap);
         const unsigned n = unsigned(in_off[batch]);
-        uint32_t *hid = sl.in, *hb = sl.in + cap, *hp = sl.in + 3 * cap, *ho = sl.in + 4 * cap;  // device layout
+        uint32_t *hid = ln.in, *hb = ln.in + cap, *hp = ln.in + 3 * cap, *ho = ln.in + 4 * cap;  // device layout
         if (in_ids && !in_rows) std::memcpy(hid, in_ids, n * sizeof(int32_t));
         else std::memset(hid, 0, n * sizeof(int32_t));
         for (size_t s = 0; s < batch; ++s) {
@@ -573,63 +609,95 @@ struct Backend {
         // Padding to the bucket: one sequence [n, n_pad) of token 0, never pooled.
         const unsigned n_pad = (n + BUCKET - 1) / BUCKET * BUCKET;
         for (unsigned t = n; t < n_pad; ++t) hid[t] = 0, hb[2 * t] = n, hb[2 * t + 1] = n_pad, hp[t] = t - n;
-        sl.in[5 * cap + 1] = uint32_t(batch);
+        ln.in[5 * cap + 1] = uint32_t(batch);
         ck(cudaSetDevice(device), "cudaSetDevice");
         if (in_rows) {
-            if (!sl.rows) ck(cudaMallocHost(&sl.rows, sizeof(float) * cap * 512), "cudaMallocHost");
-            if (!xin) xin = dalloc<float>(size_t(cap) * 512);
-            std::memcpy(sl.rows, in_rows, size_t(n) * 512 * sizeof(float));
-            std::memset(sl.rows + size_t(n) * 512, 0, size_t(n_pad - n) * 512 * sizeof(float));
-            ck(cudaMemcpyAsync(xin, sl.rows, size_t(n_pad) * 512 * sizeof(float), cudaMemcpyHostToDevice, stream),
+            if (!ln.rows) ck(cudaMallocHost(&ln.rows, sizeof(float) * cap * 512), "cudaMallocHost");
+            if (!ln.xin) ln.xin = dalloc<float>(size_t(cap) * 512);
+            std::memcpy(ln.rows, in_rows, size_t(n) * 512 * sizeof(float));
+            std::memset(ln.rows + size_t(n) * 512, 0, size_t(n_pad - n) * 512 * sizeof(float));
+            ck(cudaMemcpyAsync(ln.xin, ln.rows, size_t(n_pad) * 512 * sizeof(float), cudaMemcpyHostToDevice,
+                               ln.stream),
                "input rows upload");
         }
-        ck(cudaMemcpyAsync(ids, sl.in, (5 * cap + 2) * 4, cudaMemcpyHostToDevice, stream), "wave upload");
+        ck(cudaMemcpyAsync(ln.ids, ln.in, (5 * cap + 2) * 4, cudaMemcpyHostToDevice, ln.stream), "wave upload");
         return n_pad;
     }
 
-    // Split form for device-resident timing: stage once, launch the staged graph
-    // any number of times, finish.  Not to be interleaved with submit/collect.
+    void refuse_if_poisoned() const {
+        if (poisoned) throw std::runtime_error("KFD context failed; restart process before reuse");
+    }
+    void refuse_if_submitted() const {
+        for (const Lane &ln : lanes)
+            if (ln.busy) throw std::runtime_error("a submitted wave is not collected yet");
+    }
+
+    // Split form for device-resident timing: stage the wave into every lane
+    // once, launch the staged graphs any number of times, finish.  Not to be
+    // interleaved with submit/collect.
     void stage(const int32_t *in_ids, const size_t *in_off, size_t batch, const float *in_rows = nullptr) {
-        if (poisoned) throw std::runtime_error("KFD context failed; restart process before reuse");
-        for (const Slot &sl : slots)
-            if (sl.busy) throw std::runtime_error("a submitted wave is not collected yet");
-        // Nothing stays staged if the fill or the capture below fails.
-        staged_graph = nullptr;
-        const unsigned n_pad = fill(slots[0], in_ids, in_off, batch, in_rows);
-        cudaGraphExec_t g = graph_for(n_pad, in_rows != nullptr);
+        refuse_if_poisoned();
+        refuse_if_submitted();
+        // Nothing stays staged if a fill or a capture below fails.
+        staged = false;
+        for (Lane &ln : lanes) ln.staged_graph = nullptr;
+        unsigned n_pad = 0;
+        for (Lane &ln : lanes) {
+            n_pad = fill(ln, in_ids, in_off, batch, in_rows);
+            ln.staged_graph = graph_for(ln, n_pad, in_rows != nullptr);
+        }
         staged_n = n_pad, staged_batch = batch, staged_rows = in_rows != nullptr;
-        staged_graph = g;
+        staged = true;
     }
 
+    // Replays alternate over the lanes (replay r on lane r % LANES), so
+    // consecutive waves overlap on the GPU as two submitted waves do.  The
+    // other lanes start after the work already queued on the first lane's
+    // stream, and the first lane's stream waits for them at the end: events
+    // recorded on that stream (eg2_b200_stream) around a launch bracket all
+    // of its replays.  One replay runs on the first lane alone.
     void launch(int repeats) {
-        if (poisoned) throw std::runtime_error("KFD context failed; restart process before reuse");
-        if (!staged_graph) throw std::runtime_error("no wave staged");
-        for (int r = 0; r < repeats; ++r) ck(cudaGraphLaunch(staged_graph, stream), "graph launch");
+        refuse_if_poisoned();
+        if (!staged) throw std::runtime_error("no wave staged");
+        const int used = repeats < LANES ? repeats : LANES;
+        if (used > 1) {
+            ck(cudaEventRecord(lanes[0].fork, lanes[0].stream), "event record");
+            for (int i = 1; i < used; ++i) ck(cudaStreamWaitEvent(lanes[i].stream, lanes[0].fork, 0), "stream wait");
+        }
+        for (int r = 0; r < repeats; ++r) {
+            Lane &ln = lanes[r % LANES];
+            ck(cudaGraphLaunch(ln.staged_graph, ln.stream), "graph launch");
+        }
+        for (int i = 1; i < used; ++i) {
+            ck(cudaEventRecord(lanes[i].join, lanes[i].stream), "event record");
+            ck(cudaStreamWaitEvent(lanes[0].stream, lanes[i].join, 0), "stream wait");
+        }
     }
 
-    // Enqueue a slot's readback (embeddings, error word) and completion event.
-    void enqueue_readback(Slot &sl, size_t batch) {
-        if (batch) ck(cudaMemcpyAsync(sl.out, pooled, batch * 768 * 4, cudaMemcpyDeviceToHost, stream), "readback");
-        ck(read_device_error_async(sl.err, stream), "error readback");
-        ck(cudaEventRecord(sl.done, stream), "event record");
+    // Enqueue a lane's readback (embeddings, error word) and completion event.
+    void enqueue_readback(Lane &ln, size_t batch) {
+        if (batch)
+            ck(cudaMemcpyAsync(ln.out, ln.pooled, batch * 768 * 4, cudaMemcpyDeviceToHost, ln.stream), "readback");
+        ck(read_device_error_async(ln.err, ln.stream), "error readback");
+        ck(cudaEventRecord(ln.done, ln.stream), "event record");
     }
 
-    // Wait for a slot with the reference's deadline.  Any failure poisons the
+    // Wait for a lane with the reference's deadline.  Any failure poisons the
     // context for good (gemma2_kfd.cpp:190-214): a later wait that succeeds,
     // e.g. the other pipeline slot's, never clears it.
-    void wait_slot(Slot &sl) {
+    void wait_lane(Lane &ln) {
         try {
             // Poll without sleeping for the length of a few waves, then back off.
             const auto t0 = std::chrono::steady_clock::now();
             for (;;) {
-                const cudaError_t q = cudaEventQuery(sl.done);
+                const cudaError_t q = cudaEventQuery(ln.done);
                 if (q == cudaSuccess) break;
                 if (q != cudaErrorNotReady) ck(q, "GPU wave");
                 const double waited = std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
                 if (waited > TIMEOUT_S) throw std::runtime_error("GPU wave timed out");
                 if (waited > 0.02) std::this_thread::sleep_for(std::chrono::microseconds(50));
             }
-            const int derr = *sl.err;
+            const int derr = *ln.err;
             if (derr)
                 throw std::runtime_error("device wait timed out inside a kernel (error " + std::to_string(derr) + ")");
         } catch (...) {
@@ -637,111 +705,150 @@ struct Backend {
             throw;
         }
     }
-    void refuse_if_poisoned() const {
-        if (poisoned) throw std::runtime_error("KFD context failed; restart process before reuse");
-    }
 
     // gemma2_kfd.cpp:337-343: finite, non-zero; the embedding is already
     // L2-normalised on the device.
-    void deliver(const Slot &sl, size_t batch, float *out) {
+    void deliver(const Lane &ln, size_t batch, float *out) {
         for (size_t s = 0; s < batch; ++s) {
             double ss = 0;
             for (int z = 0; z < 768; ++z) {
-                const float f = sl.out[s * 768 + z];
+                const float f = ln.out[s * 768 + z];
                 if (!std::isfinite(f)) throw std::runtime_error("nonfinite GPU output");
                 ss += double(f) * f;
             }
             if (ss <= 0) throw std::runtime_error("zero GPU embedding");
         }
-        std::memcpy(out, sl.out, batch * 768 * sizeof(float));
+        std::memcpy(out, ln.out, batch * 768 * sizeof(float));
     }
 
     void finish(float *out) {
-        if (poisoned) throw std::runtime_error("KFD context failed; restart process before reuse");
-        if (!staged_graph) throw std::runtime_error("no wave staged");
-        enqueue_readback(slots[0], staged_batch);
-        wait_slot(slots[0]);
-        deliver(slots[0], staged_batch, out);
+        refuse_if_poisoned();
+        if (!staged) throw std::runtime_error("no wave staged");
+        enqueue_readback(lanes[0], staged_batch);
+        wait_lane(lanes[0]);
+        deliver(lanes[0], staged_batch, out);
     }
 
     // Pipelined form: submit enqueues upload, graph and readback on the next
-    // slot and returns its index; collect waits for that slot and delivers.
-    // A slot must be collected before it is submitted to again.
+    // slot's lane and returns the slot index; collect waits for that slot and
+    // delivers.  A slot must be collected before it is submitted to again.
     int submit(const int32_t *in_ids, const size_t *in_off, size_t batch, const float *in_rows = nullptr) {
-        if (poisoned) throw std::runtime_error("KFD context failed; restart process before reuse");
-        const int id = next_slot;
-        Slot &sl = slots[id];
-        if (sl.busy) throw std::runtime_error("pipeline slot busy: collect its wave first");
-        const unsigned n_pad = fill(sl, in_ids, in_off, batch, in_rows);
-        ck(cudaGraphLaunch(graph_for(n_pad, in_rows != nullptr), stream), "graph launch");
-        enqueue_readback(sl, batch);
-        sl.batch = batch, sl.busy = true;
-        next_slot = (next_slot + 1) % SLOTS;
+        refuse_if_poisoned();
+        // The next slot in turn, or the other one if a synchronous call holds it.
+        int id = next_slot;
+        for (int i = 0; i < LANES && lanes[id].busy; ++i) id = (next_slot + i + 1) % LANES;
+        Lane &ln = lanes[id];
+        if (ln.busy) throw std::runtime_error("pipeline slot busy: collect its wave first");
+        staged = false;  // the staged wave's device inputs on this lane are overwritten
+        const unsigned n_pad = fill(ln, in_ids, in_off, batch, in_rows);
+        ck(cudaGraphLaunch(graph_for(ln, n_pad, in_rows != nullptr), ln.stream), "graph launch");
+        enqueue_readback(ln, batch);
+        ln.batch = batch, ln.busy = true;
+        next_slot = (id + 1) % LANES;
         return id;
     }
 
     void collect(int id, float *out) {
-        if (id < 0 || id >= SLOTS || !slots[id].busy) throw std::runtime_error("no wave submitted to this slot");
-        Slot &sl = slots[id];
-        sl.busy = false;
+        if (id < 0 || id >= LANES || !lanes[id].busy || lanes[id].by_call)
+            throw std::runtime_error("no wave submitted to this slot");
+        Lane &ln = lanes[id];
+        ln.busy = false;
         refuse_if_poisoned();
-        wait_slot(sl);
-        deliver(sl, sl.batch, out);
+        wait_lane(ln);
+        deliver(ln, ln.batch, out);
     }
 
+    // The synchronous call (ei_gemma2_kfd_batch), safe to make from several
+    // host threads at once: it holds the context's mutex only to enqueue the
+    // wave on a free lane and to deliver it, not while the GPU runs it, so two
+    // callers' waves overlap on the GPU.  A third caller waits for a lane
+    // (up to the wave deadline).  Takes the mutex itself.
     void batch(const int32_t *in_ids, const size_t *in_off, size_t n_seq, float *out, const float *in_rows = nullptr) {
+        std::unique_lock<std::mutex> lk(mutex);
         if (!out) throw std::runtime_error(count_message(cap));
-        collect(submit(in_ids, in_off, n_seq, in_rows), out);
+        refuse_if_poisoned();
+        Lane *ln = nullptr;
+        auto free_lane = [&] {
+            for (Lane &l : lanes)
+                if (!l.busy) return ln = &l, true;
+            return poisoned.load();
+        };
+        if (!lane_freed.wait_for(lk, std::chrono::duration<double>(TIMEOUT_S), free_lane))
+            throw std::runtime_error("GPU wave timed out");
+        refuse_if_poisoned();
+        staged = false;  // the staged wave's device inputs on this lane are overwritten
+        const unsigned n_pad = fill(*ln, in_ids, in_off, n_seq, in_rows);
+        ck(cudaGraphLaunch(graph_for(*ln, n_pad, in_rows != nullptr), ln->stream), "graph launch");
+        enqueue_readback(*ln, n_seq);
+        ln->busy = ln->by_call = true;
+        lk.unlock();
+        std::exception_ptr failure;
+        try {
+            wait_lane(*ln);
+        } catch (...) {
+            failure = std::current_exception();
+        }
+        lk.lock();
+        try {
+            if (failure) std::rethrow_exception(failure);
+            deliver(*ln, n_seq, out);
+        } catch (...) {
+            ln->busy = ln->by_call = false;
+            lane_freed.notify_all();
+            throw;
+        }
+        ln->busy = ln->by_call = false;
+        lane_freed.notify_all();
     }
 
     // Layers [l0, l1) of the fast path (or of parity mode) from a caller-given
     // residual stream x_in [n][512] and per-layer embeddings ple_in
     // [n][24][512] (NULL: projected on the device from x_in, which is then the
-    // wave's embedding rows), eager launches on the context stream; x_out gets
-    // the residual stream after layer l1 - 1.  For teacher-forced per-layer
-    // checks against the reference CPU graph.
+    // wave's embedding rows), eager launches on the first lane's stream; x_out
+    // gets the residual stream after layer l1 - 1.  For teacher-forced
+    // per-layer checks against the reference CPU graph.
     void forward_layers(const float *x_in, const float *ple_in, const size_t *in_off, size_t batch, int l0, int l1,
                         float *x_out) {
         refuse_if_poisoned();
-        for (const Slot &sl : slots)
-            if (sl.busy) throw std::runtime_error("a submitted wave is not collected yet");
+        refuse_if_submitted();
         if (l0 < 0 || l1 > 24 || l0 > l1 || !x_out) throw std::runtime_error("invalid layer range");
-        staged_graph = nullptr;  // the staged wave's device inputs are overwritten below
-        Slot &sl = slots[0];
-        const unsigned n_pad = fill(sl, nullptr, in_off, batch, x_in);
+        staged = false;  // the staged wave's device inputs are overwritten below
+        Lane &ln = lanes[0];
+        const unsigned n_pad = fill(ln, nullptr, in_off, batch, x_in);
         const int N = int(n_pad);
         const size_t n = in_off[batch];
-        cudaStream_t s = stream;
-        ck(launch_input_rows(x, x_hi, x_lo, xin, N, s), "input rows");
+        cudaStream_t s = ln.stream;
+        ck(launch_input_rows(ln.x, ln.x_hi, ln.x_lo, ln.xin, N, s), "input rows");
         if (ple_in) {
-            ck(cudaMemcpyAsync(ple, ple_in, n * 24 * 512 * sizeof(float), cudaMemcpyHostToDevice, s), "PLE upload");
+            ck(cudaMemcpyAsync(ln.ple, ple_in, n * 24 * 512 * sizeof(float), cudaMemcpyHostToDevice, s),
+               "PLE upload");
             ck(cudaStreamSynchronize(s), "PLE upload");  // ple_in is pageable caller memory
         } else if (exact) {
-            ck(launch_ple_exact(ple, x, ple_w, ple_norm, N, s), "PLE");
+            ck(launch_ple_exact(ln.ple, ln.x, ple_w, ple_norm, N, s), "PLE");
         } else {
-            ck(launch_ple(tm_hi, tm_lo, tm_ple, ple, ple_norm, N, s), "PLE");
+            ck(launch_ple(ln.tm_hi, ln.tm_lo, tm_ple, ln.ple, ple_norm, N, s), "PLE");
         }
         AttnTcMaps tc_maps[2]{};
-        attention_maps(N, tc_maps);
+        attention_maps(ln, N, tc_maps);
         if (l0 < 24)
-            ck(launch_norm_quant(xq, xs, cap, nullptr, x, layers[l0].attn_norm, N, 512, s, tier), "norm");
+            ck(launch_norm_quant(ln.xq, ln.xs, cap, nullptr, ln.x, layers[l0].attn_norm, N, 512, s, tier), "norm");
         auto none = [](const char *) {};
-        for (int l = l0; l < l1; ++l) enqueue_layer(l, N, s, tc_maps, none);
-        enqueue_readback(sl, 0);
-        wait_slot(sl);
-        ck(cudaMemcpy(x_out, x, n * 512 * sizeof(float), cudaMemcpyDeviceToHost), "residual readback");
+        for (int l = l0; l < l1; ++l) enqueue_layer(l, N, ln, tc_maps, none);
+        enqueue_readback(ln, 0);
+        wait_lane(ln);
+        ck(cudaMemcpy(x_out, ln.x, n * 512 * sizeof(float), cudaMemcpyDeviceToHost), "residual readback");
     }
 
     int profile(char names[][32], double *ms, int max) {
         refuse_if_poisoned();
-        if (!staged_graph) throw std::runtime_error("no wave staged");
+        if (!staged) throw std::runtime_error("no wave staged");
         std::map<std::string, double> acc;
         std::vector<std::string> order;
         {
-            Profiler prof{stream};
-            enqueue(staged_n, stream, &prof, staged_rows);
-            enqueue_readback(slots[0], 0);
-            wait_slot(slots[0]);
+            Profiler prof{lanes[0].stream};
+            enqueue(staged_n, lanes[0], &prof, staged_rows);
+            enqueue_readback(lanes[0], 0);
+            wait_lane(lanes[0]);
             for (size_t i = 1; i < prof.events.size(); ++i) {
                 float t = 0;
                 ck(cudaEventElapsedTime(&t, prof.events[i - 1], prof.events[i]), "elapsed");
@@ -791,9 +898,7 @@ extern "C" void ei_gemma2_kfd_free(void *ctx) { delete static_cast<Backend *>(ct
 extern "C" bool ei_gemma2_kfd_batch(void *ctx, const int32_t *ids, const size_t *offsets, size_t batch, float *out,
                                     char *err, size_t len) {
     return guarded(err, len, [&] {
-        Backend *b = as_backend(ctx);
-        std::lock_guard<std::mutex> guard(b->mutex);
-        b->batch(ids, offsets, batch, out);
+        as_backend(ctx)->batch(ids, offsets, batch, out);
     });
 }
 extern "C" bool eg2_b200_validate(const int32_t *ids, const size_t *offsets, size_t batch, char *err, size_t len) {
@@ -851,7 +956,6 @@ extern "C" bool eg2_b200_batch_rows(void *ctx, const float *rows, const size_t *
                                     char *err, size_t len) {
     return guarded(err, len, [&] {
         Backend *b = as_backend(ctx);
-        std::lock_guard<std::mutex> guard(b->mutex);
         if (!rows) throw std::runtime_error(count_message(b->cap));
         b->batch(nullptr, offsets, batch, out, rows);
     });

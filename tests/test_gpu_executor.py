@@ -6,9 +6,12 @@ Tolerance.  The reference's default CPU graph and its scalar tier run the
 same math in different float orders and already disagree: on the BASELINE
 model (norm weights N(0, 0.1)) they reach cosine 0.9982-0.9996 against each
 other; one Q8_0 code that lands on the other side of a rounding boundary
-changes the next GEMM's inputs, and 24 layers amplify it.  The end-to-end
-bound is therefore the reference's own inter-tier agreement minus a margin of
-0.003; the per-operator tests (test_gpu_ops.py) carry the bit-exact claims.
+changes the next GEMM's inputs, and 24 layers amplify it.  Where the
+reference's two tiers are both at hand (config 0, the input-rows wave) the
+bound is their own agreement minus MARGIN; elsewhere it is the value measured
+on B200 minus a stated margin (each assertion gives both).  The per-layer,
+teacher-forced tolerance is in test_gpu_layers.py; the per-operator tests
+(test_gpu_ops.py) carry the bit-exact claims.
 """
 import numpy as np
 import pytest
@@ -16,7 +19,7 @@ import pytest
 from conftest import cosine, golden
 
 pytestmark = pytest.mark.gpu
-MARGIN = 0.003
+MARGIN = 0.0015  # measured worst: 0.0004 below the reference's own inter-tier agreement (config 0)
 
 
 @pytest.fixture(scope="module")
@@ -51,15 +54,17 @@ def test_long_and_two_wave_goldens(executor, eg2):
     out = executor.batch(g["long_ids"], g["long_offsets"])
     c = float(cosine(out[0], g["long_embed"][0]))
     print("1x2048 cos", c)
-    assert c >= 0.99 - MARGIN
+    assert c >= 0.9999  # the north star; measured 0.99999
     for dims in (128, 256, 512):
         p = eg2.normalize_prefix(out[0], dims)
         assert abs(np.linalg.norm(p) - 1) < 1e-5
-        assert float(cosine(p, g[f"long_prefix_{dims}"])) >= 0.99 - MARGIN
+        cp = float(cosine(p, g[f"long_prefix_{dims}"]))
+        print(f"1x2048 prefix {dims} cos", cp)
+        assert cp >= 0.9999
     out2 = executor.batch(g["w2x128_ids"], g["w2x128_offsets"])
     c2 = cosine(out2, g["w2x128_embed"])
     print("2x128 cos", c2)
-    assert c2.min() >= 0.99 - MARGIN
+    assert c2.min() >= 0.9995  # measured 0.99980 - 0.0003
 
 
 def test_submit_collect_pipeline_equals_batch(executor, syn):
@@ -80,6 +85,50 @@ def test_submit_collect_pipeline_equals_batch(executor, syn):
     np.testing.assert_array_equal(executor.collect(s3), expect[3])
     with pytest.raises(Exception):
         executor.collect(s3)  # already collected
+
+
+def test_concurrent_calls_equal_serial_calls(executor, syn):
+    """ei_gemma2_kfd_batch from several host threads at once: the context runs
+    two calls' waves on its two lanes concurrently (a third caller waits for
+    a lane); every call returns exactly what it returns alone."""
+    import threading
+    waves = [syn.wave(lens, seed=50 + s) for s, lens in
+             enumerate([(40, 7, 300), (126,) * 16, (5,), (900, 900), (64,) * 9, (2046,)])]
+    expect = [executor.batch(ids, off) for ids, off in waves]
+    got, errors = {}, []
+
+    def caller(k):
+        try:
+            for r in range(3):
+                i = (k + r) % len(waves)
+                got[(k, r)] = (i, executor.batch(*waves[i]))
+        except Exception as e:  # reported below, in the main thread
+            errors.append(e)
+    threads = [threading.Thread(target=caller, args=(k,)) for k in range(4)]
+    for t in threads:
+        t.start()
+    for t in threads:
+        t.join()
+    assert not errors, errors
+    assert len(got) == 12
+    for i, out in got.values():
+        np.testing.assert_array_equal(out, expect[i])
+
+
+def test_call_beside_submitted_wave_and_alternating_launches(executor, syn):
+    """A synchronous call takes the lane a submitted wave leaves free; the
+    split form's replays alternate over both lanes and end on the same
+    embeddings as one replay."""
+    w0, w1 = syn.wave((33, 300), seed=61), syn.wave((126,) * 16, seed=62)
+    e0, e1 = executor.batch(*w0), executor.batch(*w1)
+    s0 = executor.submit(*w0)
+    np.testing.assert_array_equal(executor.batch(*w1), e1)
+    np.testing.assert_array_equal(executor.collect(s0), e0)
+    executor.stage(*w1)
+    executor.launch(5)
+    np.testing.assert_array_equal(executor.finish(), e1)
+    executor.launch(1)
+    np.testing.assert_array_equal(executor.finish(), e1)
 
 
 def test_packed_equals_solo_and_reorder(executor, syn):
@@ -143,7 +192,7 @@ def test_restatement_live(executor, port, model_baseline, syn):
     out = executor.batch(ids, off)
     c = cosine(out, ref)
     print("live restatement cos", c)
-    assert c.min() >= 0.995 - MARGIN
+    assert c.min() >= 0.997  # measured 0.99764 - 0.0006 (a 5-token sequence: few tokens to average over)
 
 
 def test_parity_mode_reproduces_restatement(eg2, model_baseline, port, syn):
@@ -278,7 +327,7 @@ def test_wide_wave_matches_reference(wide_executor):
     out = wide_executor.batch(g["ids"], g["offsets"])
     c = float(cosine(out[0], g["embed_best"][0]))
     print("1x8192 cos", c)
-    assert c >= 0.99 - MARGIN
+    assert c >= 0.9999  # the north star; measured 0.99998
 
 
 def test_wide_wave_packed_equals_standard_context(wide_executor, executor, syn, model_baseline):
