@@ -262,10 +262,10 @@ cudaError_t launch_pool_l2(float *out, const float *y, const unsigned *offsets, 
                            const unsigned *count) {
     if (batch <= 0) return cudaSuccess;
     if (width <= 0 || width % 8 || width > 8192) return cudaErrorInvalidValue;
-    if (cudaError_t e = launch_pdl(pool_mean_kernel, dim3((width + 127) / 128, batch), dim3(128), 0, s, out, y, offsets,
-                                   width, count))
+    if (cudaError_t e = launch_pdl(pool_mean_kernel, dim3((width + 31) / 32, batch < POOL_SEQ ? batch : POOL_SEQ),
+                                   dim3(256), 0, s, out, y, offsets, width, batch, count))
         return e;
-    return launch_pdl(pool_l2_kernel, dim3(batch), dim3(32), 0, s, out, width, count);
+    return launch_pdl(pool_l2_kernel, dim3(batch), dim3(32), 0, s, out, width, batch, count);
 }
 
 cudaError_t launch_repack_q8(const void *blocks, int rows, int k, int8_t *codes, float *scales, int scale_stride,

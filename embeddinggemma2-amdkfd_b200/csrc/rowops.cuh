@@ -292,55 +292,78 @@ __global__ void gelu_mul_kernel(float *__restrict__ g, const float *__restrict__
 
 // Mean pool then L2 (gemma2_fast.c:1000-1008), in two launches.
 // pool_mean_kernel: o[z] = sum over the sequence's tokens, in token order, of
-// y[t][z] / len -- one thread per (sequence, column); the adds are a serial
-// chain in the reference's order, so the loads run POOL_AHEAD tokens ahead of
-// them (a warp's load of one token is one 128-byte row segment) and the
-// quotients of a batch are formed before its adds.  The result goes straight
-// into out.  With count set, sequences from *count on (beyond the wave's
-// batch) are skipped.
-constexpr int POOL_AHEAD = 32;
-__global__ void pool_mean_kernel(float *__restrict__ out, const float *__restrict__ y,
-                                 const unsigned *__restrict__ offsets, int width, const unsigned *__restrict__ count) {
+// y[t][z] / len.  The adds are one serial chain per column in the reference's
+// order, so a CTA owns a (32-column chunk, sequence) item: its 256 threads
+// load POOL_T tokens x 32 columns (eight float4 each, all in flight at once),
+// form the quotients and stage them in shared memory, and warp 0 adds them
+// in token order while the next POOL_T tokens are being loaded.  The grid is
+// bounded (at most POOL_SEQ CTAs per chunk) and strides over the sequences;
+// with count set, sequences from *count on (beyond the wave's batch) are
+// skipped.  The result goes straight into out.
+constexpr int POOL_T = 256, POOL_SEQ = 64;
+__global__ void __launch_bounds__(256) pool_mean_kernel(float *__restrict__ out, const float *__restrict__ y,
+                                                        const unsigned *__restrict__ offsets, int width, int batch,
+                                                        const unsigned *__restrict__ count) {
     pdl_wait();
     pdl_trigger();
-    const int s = blockIdx.y, z = blockIdx.x * blockDim.x + threadIdx.x;
-    if (z >= width || (count && unsigned(s) >= *count)) return;
-    const unsigned lo = offsets[s], hi = offsets[s + 1];
-    const float len = float(hi - lo);
-    const float *col = y + z;
-    float o = 0.0f;
-    unsigned t = lo;
-    for (; t + POOL_AHEAD <= hi; t += POOL_AHEAD) {
-        float v[POOL_AHEAD];
+    __shared__ float4 stage[POOL_T][8];  // [token][column / 4] of the chunk
+    const int c0 = blockIdx.x * 32, tid = threadIdx.x, j = tid & 7, lane = tid & 31;
+    const int nseq = count ? min(int(*count), batch) : batch;
+    const bool col_ok = c0 + 4 * j < width;  // width is a multiple of 8
+    for (int s = blockIdx.y; s < nseq; s += gridDim.y) {
+        const unsigned lo = offsets[s], hi = offsets[s + 1];
+        const float len = float(hi - lo);
+        float o = 0.0f;
+        float4 v[POOL_T / 32];
+        auto load = [&](unsigned t0) {
 #pragma unroll
-        for (int i = 0; i < POOL_AHEAD; ++i) v[i] = col[size_t(t + i) * width];
+            for (int k = 0; k < POOL_T / 32; ++k) {
+                const unsigned t = t0 + (tid >> 3) + 32 * k;
+                v[k] = t < hi && col_ok ? *reinterpret_cast<const float4 *>(y + size_t(t) * width + c0 + 4 * j)
+                                        : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+            }
+        };
+        load(lo);
+        for (unsigned t0 = lo; t0 < hi; t0 += POOL_T) {
+            __syncthreads();  // the previous stage has been added up
 #pragma unroll
-        for (int i = 0; i < POOL_AHEAD; ++i) v[i] = __fdiv_rn(v[i], len);
-#pragma unroll
-        for (int i = 0; i < POOL_AHEAD; ++i) o = __fadd_rn(o, v[i]);
+            for (int k = 0; k < POOL_T / 32; ++k)
+                stage[(tid >> 3) + 32 * k][j] = make_float4(__fdiv_rn(v[k].x, len), __fdiv_rn(v[k].y, len),
+                                                            __fdiv_rn(v[k].z, len), __fdiv_rn(v[k].w, len));
+            __syncthreads();
+            if (t0 + POOL_T < hi) load(t0 + POOL_T);  // in flight during the adds below
+            if (tid < 32) {
+                const int nt = int(min(hi - t0, unsigned(POOL_T)));
+                const float *col = reinterpret_cast<const float *>(&stage[0][0]) + lane;
+                for (int i = 0; i < nt; ++i) o = __fadd_rn(o, col[i * 32]);
+            }
+        }
+        if (tid < 32 && c0 + lane < width) out[size_t(s) * width + c0 + lane] = o;
     }
-    for (; t < hi; ++t) o = __fadd_rn(o, __fdiv_rn(col[size_t(t) * width], len));
-    out[size_t(s) * width + z] = o;
 }
 // pool_l2_kernel: one warp per sequence; the SSE2 sum of squares of
 // kernels.c:82-93 (lanes 0..7 are its two 4-lane accumulators over 8-element
 // chunks, each summed in chunk order), then x *= 1/sqrt(ss) (kernels.c:393-396).
-__global__ void pool_l2_kernel(float *__restrict__ out, int width, const unsigned *__restrict__ count) {
+// One warp per sequence of the grid's batch; with count set, sequences from
+// *count on are skipped.
+__global__ void pool_l2_kernel(float *__restrict__ out, int width, int batch, const unsigned *__restrict__ count) {
     pdl_wait();
     pdl_trigger();
-    const int s = blockIdx.x, lane = threadIdx.x;
-    if (count && unsigned(s) >= *count) return;  // warp-uniform
-    float *o = out + size_t(s) * width;
-    float acc = 0.0f;
-    if (lane < 8)
-        for (int i = 0; i + 7 < width; i += 8) acc = __fadd_rn(acc, __fmul_rn(o[i + lane], o[i + lane]));
-    float v[4];
+    const int lane = threadIdx.x;
+    const int nseq = count ? min(int(*count), batch) : batch;
+    for (int s = blockIdx.x; s < nseq; s += gridDim.x) {  // warp-uniform
+        float *o = out + size_t(s) * width;
+        float acc = 0.0f;
+        if (lane < 8)
+            for (int i = 0; i + 7 < width; i += 8) acc = __fadd_rn(acc, __fmul_rn(o[i + lane], o[i + lane]));
+        float v[4];
 #pragma unroll
-    for (int j = 0; j < 4; ++j)
-        v[j] = __fadd_rn(__shfl_sync(0xffffffffu, acc, j), __shfl_sync(0xffffffffu, acc, 4 + j));
-    const float ss = __fadd_rn(__fadd_rn(v[0], v[2]), __fadd_rn(v[1], v[3]));
-    const float inv = ss != 0.0f ? __fdiv_rn(1.0f, __fsqrt_rn(ss)) : 1.0f;
-    for (int z = lane; z < width; z += 32) o[z] = __fmul_rn(o[z], inv);
+        for (int j = 0; j < 4; ++j)
+            v[j] = __fadd_rn(__shfl_sync(0xffffffffu, acc, j), __shfl_sync(0xffffffffu, acc, 4 + j));
+        const float ss = __fadd_rn(__fadd_rn(v[0], v[2]), __fadd_rn(v[1], v[3]));
+        const float inv = ss != 0.0f ? __fdiv_rn(1.0f, __fsqrt_rn(ss)) : 1.0f;
+        for (int z = lane; z < width; z += 32) o[z] = __fmul_rn(o[z], inv);
+    }
 }
 
 // GGUF Q8_0 blocks [rows][k/32] (34 B each) -> int8 codes [rows][k] and fp32

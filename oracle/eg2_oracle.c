@@ -173,6 +173,29 @@ void eg2o_set_variant(int gemm_descending, int attention_fp16) {
     variant_attention_fp16 = attention_fp16;
 }
 
+/* Float orders: EG2O_ORDER_SCALAR follows the scalar loops, EG2O_ORDER_VNNI512
+ * the reference's default tier on an AVX-512 VNNI host (g2x_level() ==
+ * G2X_VNNI512 with the repacked 512-bit GEMM, gemma2_fast_x86.c:24-48). */
+static int order_vnni;
+void eg2o_set_order(int order) { order_vnni = order == EG2O_ORDER_VNNI512; }
+
+/* Horizontal sum of 8 lanes as hsum / G2X_Q8_TILE end it
+ * (gemma2_fast_x86.c:239-244, :95-101): (a_j + a_{j+4}) for j < 4, then
+ * (s0 + s2) + (s1 + s3). */
+static float hsum8(const float *a) {
+    float s0 = a[0] + a[4], s1 = a[1] + a[5], s2 = a[2] + a[6], s3 = a[3] + a[7];
+    return (s0 + s2) + (s1 + s3);
+}
+/* _mm512_reduce_add_ps as the C compiler expands it (gemma2_fast_x86.c:203):
+ * the upper and lower 256-bit halves added lane by lane, then the same for
+ * 128-bit halves, then lanes 0+2 and 1+3, then those two. */
+static float reduce16(const float *a) {
+    float t[8], u[4];
+    for (int i = 0; i < 8; i++) t[i] = a[i] + a[i + 8];
+    for (int i = 0; i < 4; i++) u[i] = t[i] + t[i + 4];
+    return (u[0] + u[2]) + (u[1] + u[3]);
+}
+
 /* gemma2_fast.c:193-204 -- scalar Q8_0 x Q8_0 tile, blocks in ascending order. */
 typedef struct {
     const int8_t *wq, *xq;
@@ -180,10 +203,57 @@ typedef struct {
     int k, m;
     float *y;
     int32_t *D;
+    int n;
 } gemm_q8_job;
+/* gemma2_fast_x86.c:168-204 (g2x_gemm512_tile, waves of more than 8 tokens):
+ * 16 fp32 lanes per output, lanes 0-7 taking the int32 sums of bytes 4g..4g+3
+ * of block p and lanes 8-15 those of block p + 1, with u8 activations q + 128
+ * and lane 0 of each block seeded with -128 * sum(w) (:146-158); each lane
+ * adds float(sum) * (sw * sx) with one fused multiply-add per block pair,
+ * then _mm512_reduce_add_ps.  gemma2_fast.c:446-465 selects it. */
+static float q8_dot_vnni512(const int8_t *w, const int8_t *x, const float *wd, const float *xd, int kb) {
+    float acc[16] = {0};
+    for (int p = 0; p < kb; p += 2)
+        for (int lane = 0; lane < 16; lane++) {
+            const int b = p + lane / 8, g = lane % 8;
+            const int8_t *wb = w + (size_t)b * 32, *xb = x + (size_t)b * 32;
+            int sum = 0;
+            for (int i = 4 * g; i < 4 * g + 4; i++) sum += (xb[i] + 128) * wb[i];
+            if (g == 0) {
+                int ws = 0;
+                for (int z = 0; z < 32; z++) ws += wb[z];
+                sum += -128 * ws;
+            }
+            acc[lane] = fmaf((float)sum, wd[b] * xd[b], acc[lane]);
+        }
+    return reduce16(acc);
+}
+/* gemma2_fast_x86.c:66-103 (q8_tile_vnni512, waves of at most 8 tokens):
+ * 8 fp32 lanes per output, lane g taking the int32 sum of bytes 4g..4g+3 of
+ * each block, float(sum) * (dw * dx) fused into the lane, then hsum8. */
+static float q8_dot_vnni256(const int8_t *w, const int8_t *x, const float *wd, const float *xd, int kb) {
+    float acc[8] = {0};
+    for (int b = 0; b < kb; b++)
+        for (int g = 0; g < 8; g++) {
+            int sum = 0;
+            for (int i = 4 * g; i < 4 * g + 4; i++) sum += w[(size_t)b * 32 + i] * x[(size_t)b * 32 + i];
+            acc[g] = fmaf((float)sum, wd[b] * xd[b], acc[g]);
+        }
+    return hsum8(acc);
+}
 static void gemm_q8_rows(void *c, int t0, int t1) {
     const gemm_q8_job *j = c;
     int kb = j->k / 32;
+    if (order_vnni) {
+        for (int t = t0; t < t1; t++)
+            for (int r = 0; r < j->m; r++) {
+                const int8_t *w = j->wq + (size_t)r * j->k, *x = j->xq + (size_t)t * j->k;
+                const float *wd = j->wd + (size_t)r * kb, *xd = j->xd + (size_t)t * kb;
+                j->y[(size_t)t * j->m + r] = j->n > 8 && kb % 2 == 0 ? q8_dot_vnni512(w, x, wd, xd, kb)
+                                                                     : q8_dot_vnni256(w, x, wd, xd, kb);
+            }
+        return;
+    }
     for (int t = t0; t < t1; t++)
         for (int r = 0; r < j->m; r++) {
             float sum = 0;
@@ -205,7 +275,7 @@ static float *widen_fp16(const uint16_t *h, size_t count) {
 void eg2o_gemm_q8(const int8_t *wq, const uint16_t *wd, const int8_t *xq, const uint16_t *xd,
                   int n, int k, int m, float *y) {
     float *wf = widen_fp16(wd, (size_t)m * (k / 32)), *xf = widen_fp16(xd, (size_t)n * (k / 32));
-    gemm_q8_job j = {wq, xq, wf, xf, k, m, y, NULL};
+    gemm_q8_job j = {wq, xq, wf, xf, k, m, y, NULL, n};
     par_for(n, gemm_q8_rows, &j);
     free(wf), free(xf);
 }
@@ -223,7 +293,7 @@ static void blockdot_rows(void *c, int t0, int t1) {
             }
 }
 void eg2o_gemm_q8_blockdots(const int8_t *wq, const int8_t *xq, int n, int k, int m, int32_t *D) {
-    gemm_q8_job j = {wq, xq, NULL, NULL, k, m, NULL, D};
+    gemm_q8_job j = {wq, xq, NULL, NULL, k, m, NULL, D, n};
     par_for(n, blockdot_rows, &j);
 }
 
@@ -240,8 +310,18 @@ static void gemm_bf16_rows(void *c, int r0, int r1) {
     for (int r = r0; r < r1; r++) {
         for (int z = 0; z < j->k; z++) row[z] = bf16_to_fp32(j->w[(size_t)r * j->k + z]);
         for (int t = 0; t < j->n; t++) {
+            const float *x = j->x + (size_t)t * j->k;
             float sum = 0;
-            for (int z = 0; z < j->k; z++) sum += row[z] * j->x[(size_t)t * j->k + z];
+            if (order_vnni) {
+                /* g2x_dot4x4 (gemma2_fast_x86.c:260-279): 8 lanes of fused
+                 * multiply-adds over z, then hsum8. */
+                float acc[8] = {0};
+                for (int z = 0; z < j->k; z += 8)
+                    for (int i = 0; i < 8; i++) acc[i] = fmaf(row[z + i], x[z + i], acc[i]);
+                sum = hsum8(acc);
+            } else {
+                for (int z = 0; z < j->k; z++) sum += row[z] * x[z];
+            }
             j->y[(size_t)t * j->m + r] = sum;
         }
     }
@@ -253,10 +333,31 @@ void eg2o_gemm_bf16(const uint16_t *w, const float *x, int n, int k, int m, floa
 }
 
 /* gemma2_fast.c:587-590 (scalar sum_squares) and :667-671 (rms_row). */
+/* g2x_sum_squares (gemma2_fast_x86.c:280-289): two 8-lane accumulators over
+ * 16-element chunks, fused multiply-adds, hsum8 of their sum. */
+static float sum_squares_x86(const float *x, int d) {
+    float s0[8] = {0}, s1[8] = {0}, v[8];
+    int z = 0;
+    for (; z + 16 <= d; z += 16)
+        for (int i = 0; i < 8; i++) {
+            s0[i] = fmaf(x[z + i], x[z + i], s0[i]);
+            s1[i] = fmaf(x[z + 8 + i], x[z + 8 + i], s1[i]);
+        }
+    for (int i = 0; i < 8; i++) v[i] = s0[i] + s1[i];
+    float s = hsum8(v);
+    for (; z < d; z++) s += x[z] * x[z];
+    return s;
+}
 void eg2o_rms_row(float *r, int d, const float *w) {
-    double s = 0;
-    for (int z = 0; z < d; z++) s += (double)r[z] * r[z];
-    float scale = 1.0f / sqrtf((float)s / d + 1e-6f);
+    float ss;
+    if (order_vnni) {
+        ss = sum_squares_x86(r, d);
+    } else {
+        double s = 0;
+        for (int z = 0; z < d; z++) s += (double)r[z] * r[z];
+        ss = (float)s;
+    }
+    float scale = 1.0f / sqrtf(ss / d + 1e-6f);
     for (int z = 0; z < d; z++) r[z] *= scale * (w ? w[z] : 1.0f);
 }
 
@@ -317,7 +418,14 @@ static void attention_rows(void *c, int t0, int t1) {
             for (int s = lo; s < hi; s++) {
                 const float *kr = j->k + ((size_t)s * kv + kh) * d;
                 float dot = 0;
-                for (int z = 0; z < d; z++) dot += qr[z] * kr[z];
+                if (order_vnni) { /* g2x_dot4x4 (gemma2_fast.c:826-828) */
+                    float acc[8] = {0};
+                    for (int z = 0; z < d; z += 8)
+                        for (int i = 0; i < 8; i++) acc[i] = fmaf(qr[z + i], kr[z + i], acc[i]);
+                    dot = hsum8(acc);
+                } else {
+                    for (int z = 0; z < d; z++) dot += qr[z] * kr[z];
+                }
                 sc[s] = dot;
                 if (dot > mx) mx = dot;
             }
@@ -327,9 +435,13 @@ static void attention_rows(void *c, int t0, int t1) {
             }
             for (int s = lo; s < hi; s++) sc[s] /= total;
             float *o = j->a + ((size_t)t * 4 + hd) * d;
+            /* g2x_pv (gemma2_fast_x86.c:326-349): one fused multiply-add per
+             * key; the masked keys it also visits carry p = 0 and add +0. */
             for (int z = 0; z < d; z++) {
                 float acc = 0;
-                for (int s = lo; s < hi; s++) acc += sc[s] * j->v[((size_t)s * kv + kh) * d + z];
+                for (int s = lo; s < hi; s++)
+                    acc = order_vnni ? fmaf(j->v[((size_t)s * kv + kh) * d + z], sc[s], acc)
+                                     : acc + sc[s] * j->v[((size_t)s * kv + kh) * d + z];
                 o[z] = acc;
             }
         }

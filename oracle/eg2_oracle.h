@@ -73,6 +73,14 @@ int eg2o_layer(const void *const *tensors, int l, float *x, const float *ple, co
  * before the attention (the fast path's tensor-core operands).  Used only to
  * measure how far such changes move one layer's output. */
 void eg2o_set_variant(int gemm_descending, int attention_fp16);
+/* Float order of the GEMMs, PLE projection, sums of squares and attention:
+ * EG2O_ORDER_SCALAR (default) the scalar loops; EG2O_ORDER_VNNI512 the
+ * reference's default tier on an AVX-512 VNNI host (gemma2_fast_x86.c: lane
+ * sums of g2x_gemm512_tile for waves of more than 8 tokens, of
+ * q8_tile_vnni512 otherwise; g2x_dot4x4, g2x_sum_squares, g2x_pv).  Combine
+ * with the x86 quantizer and GELU for that tier's embeddings. */
+enum { EG2O_ORDER_SCALAR = 0, EG2O_ORDER_VNNI512 = 1 };
+void eg2o_set_order(int order);
 /* The same graph from caller-given 512-wide input rows (media soft tokens,
  * gemma2_fast.c:940-941) instead of token ids.  Returns 0 on success. */
 int eg2o_embed_batch_inputs(const void *const *tensors, const float *inputs, const size_t *offsets,

@@ -328,6 +328,7 @@ class Port:
         L.eg2o_embed_trace.argtypes = [vp, vp, vp, C.c_size_t, vp, i, i, vp, vp]
         L.eg2o_layer.argtypes = [vp, i, vp, vp, vp, C.c_size_t, i, i]
         L.eg2o_set_variant.argtypes = [i, i]
+        L.eg2o_set_order.argtypes = [i]
 
     def quantize(self, x, mode=ROUND_X86):
         x = np.ascontiguousarray(x, dtype=np.float32).ravel()
@@ -430,6 +431,13 @@ class Port:
                                quant_mode, gelu_mode):
             raise RuntimeError("oracle rejected the layer")
         return x
+
+    ORDER_SCALAR, ORDER_VNNI512 = 0, 1
+
+    def set_order(self, order):
+        """Float order of the restatement: ORDER_SCALAR (the scalar loops) or
+        ORDER_VNNI512 (the reference's default tier on an AVX-512 VNNI host)."""
+        self.lib.eg2o_set_order(int(order))
 
     def set_variant(self, gemm_descending=False, attention_fp16=False):
         """Perturb the restatement (tests of the float-order floor only)."""

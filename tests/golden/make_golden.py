@@ -27,7 +27,11 @@ embeddinggemma2-amdkfd_b200/synthetic.py:
   (`python tests/golden/make_golden.py inputs` writes only this one);
 * golden_wide_baseline.npz -- one 8192-token sequence (the CPU graph's wave
   limit, gemma2_fast.c:924) at the best tier
-  (`python tests/golden/make_golden.py wide` writes only this one).
+  (`python tests/golden/make_golden.py wide` writes only this one);
+* golden_short_baseline.npz -- waves of 8, 7, 3 and 9 tokens at the best tier:
+  on an AVX-512 VNNI host, waves of at most 8 tokens take the 4-row Q8 tile
+  and longer ones the repacked 512-bit GEMM, two float orders
+  (`python tests/golden/make_golden.py short` writes only this one).
 
 Each scalar-tier run happens in a child process because the reference caches
 its tier on first use.
@@ -48,6 +52,7 @@ sys.path.insert(0, ROOT)
 sys.path.insert(0, os.path.join(ROOT, "oracle"))
 OUT = os.path.dirname(os.path.abspath(__file__))
 SEED = 1234
+SHORT_WAVES = ((6,), (2, 1), (1,), (7,))  # 8, 7, 3 and 9 tokens with BOS/EOS
 
 
 def _child(norm: str, what: str, out_path: str):
@@ -78,6 +83,12 @@ def _child(norm: str, what: str, out_path: str):
         x = rng.standard_normal((40, 512)).astype(np.float32)
         res["inputs"], res["offsets"] = x, off
         res["embed"] = ref.embed_inputs(x, off)
+    elif what == "short":
+        # waves of at most 8 tokens take the reference's 4-row Q8 tile, longer
+        # ones the repacked 512-bit GEMM (gemma2_fast.c:446-449)
+        for i, lens in enumerate(SHORT_WAVES):
+            ids, off = syn.wave(lens, seed=40 + i)
+            res[f"ids{i}"], res[f"offsets{i}"], res[f"embed{i}"] = ids, off, ref.embed(ids, off)
     elif what == "wide":
         ids, off = syn.wave((8190,), seed=24)
         res["ids"], res["offsets"] = ids, off
@@ -112,6 +123,11 @@ def make_inputs():
                         embed_scalar=s["embed"], embed_best=b["embed"], best_tier=b["tier"])
 
 
+def make_short():
+    b = run("baseline", "short", False)
+    np.savez_compressed(os.path.join(OUT, "golden_short_baseline.npz"), best_tier=b.pop("tier"), **b)
+
+
 def make_wide():
     b = run("baseline", "wide", False)
     np.savez_compressed(os.path.join(OUT, "golden_wide_baseline.npz"), ids=b["ids"], offsets=b["offsets"],
@@ -136,6 +152,7 @@ def main():
     np.savez_compressed(os.path.join(OUT, "golden_ops.npz"), **ops)
     make_inputs()
     make_wide()
+    make_short()
     with open(os.path.join(OUT, "golden_meta.json"), "w") as f:
         json.dump(meta, f, indent=1, sort_keys=True)
     print(json.dumps(meta, indent=1))
@@ -148,5 +165,7 @@ if __name__ == "__main__":
         make_inputs()
     elif len(sys.argv) > 1 and sys.argv[1] == "wide":
         make_wide()
+    elif len(sys.argv) > 1 and sys.argv[1] == "short":
+        make_short()
     else:
         main()

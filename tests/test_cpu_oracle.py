@@ -45,6 +45,44 @@ def test_port_is_bit_identical_to_reference_scalar_tier(port, syn, norm):
     assert np.array_equal(out, g["embed_scalar"])
 
 
+@pytest.fixture
+def vnni_port(port):
+    """The restatement in the float orders of the reference's default tier on
+    an AVX-512 VNNI host; restored to the scalar loops afterwards."""
+    port.set_order(port.ORDER_VNNI512)
+    yield port
+    port.set_order(port.ORDER_SCALAR)
+
+
+@pytest.mark.parametrize("norm", ["baseline", "plus1"])
+def test_port_vnni512_order_is_bit_identical_to_reference_best_tier(vnni_port, syn, norm):
+    """Config-0 wave: with the VNNI-512 float orders (gemma2_fast_x86.c lane
+    sums, x86 quantizer and GELU) the restatement equals the reference's
+    default tier, recorded as vnni512+gemm512 in the fixture, bit for bit --
+    on the plus-one model too, where the two tiers decorrelate entirely."""
+    import oracle
+    g = golden(f"golden_{norm}.npz")
+    assert str(g["best_tier"]) == "vnni512+gemm512"
+    out = vnni_port.embed(oracle.Gguf(syn.model_path(1234, norm)), g["ids"], g["offsets"],
+                          quant_mode=vnni_port.ROUND_X86, gelu_mode=1)
+    assert np.array_equal(out, g["embed_best"])
+
+
+def test_port_vnni512_order_short_and_input_waves(vnni_port, syn):
+    """Waves of at most 8 tokens (the reference's 4-row tile order) and of 9
+    (its 512-bit GEMM), and the input-rows wave, at the default tier."""
+    import oracle
+    m = oracle.Gguf(syn.model_path(1234, "baseline"))
+    g = golden("golden_short_baseline.npz")
+    assert str(g["best_tier"]) == "vnni512+gemm512"
+    for i in range(4):
+        out = vnni_port.embed(m, g[f"ids{i}"], g[f"offsets{i}"], quant_mode=vnni_port.ROUND_X86, gelu_mode=1)
+        assert np.array_equal(out, g[f"embed{i}"]), i
+    g = golden("golden_inputs_baseline.npz")
+    out = vnni_port.embed_inputs(m, g["inputs"], g["offsets"], quant_mode=vnni_port.ROUND_X86, gelu_mode=1)
+    assert np.array_equal(out, g["embed_best"])
+
+
 def test_port_input_rows_bit_identical_to_reference_scalar_tier(port, syn):
     """Media soft-token wave (512-wide input rows, ids NULL: gemma2_fast.c:940-941):
     the restatement equals the reference's scalar tier bit for bit."""
