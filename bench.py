@@ -811,11 +811,18 @@ def main():
                     help="config 3 in one process: one executor context and host thread per GPU (--gpus of them)")
     ap.add_argument("--no-gpu-baseline", action="store_true",
                     help="skip timing the reference's own CUDA executor beside this one")
+    ap.add_argument("--profile-wave", action="store_true",
+                    help="for ncu --profile-from-start off: one wave of --config after warm-up, then plain "
+                         "elementwise copies of the row kernels' byte counts, inside cudaProfilerStart/Stop")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     rank, world, local = dist_init()
     if args.impl == "reference":
         reference_arm(args, rank, world)
+        return finalize(world)
+    if args.profile_wave:
+        if rank == 0:
+            profile_wave(args, local)
         return finalize(world)
     if args.config == 3 and args.engine:
         if rank == 0:
@@ -963,6 +970,50 @@ def main():
     if rank == 0:
         print(json.dumps(line), flush=True)
     finalize(world)
+
+
+# Same-size plain copies for the launch list: read + write bytes of post_add
+# (13.4 MB), gate_quant (9.4 MB) and qkv_post<256> (25.2 MB) at 2048 tokens.
+COPY_FLOOR_MB = (6.7, 4.7, 12.6)
+
+
+def profile_wave(args, local):
+    """One wave of the configuration, after warm-up, between
+    cudaProfilerStart and cudaProfilerStop (so that `ncu --profile-from-start
+    off` captures exactly its kernels), followed by elementwise copies
+    (torch.mul by 1) whose read + write bytes equal those of the row kernels:
+    the launch-latency and bandwidth floor of a plain kernel of the same size
+    under the same capture."""
+    import torch
+    eg2 = importlib.import_module("embeddinggemma2-amdkfd_b200")
+    desc, lengths = CONFIGS[args.config]
+    if lengths is None or args.config in ROWS_CONFIGS or args.config in WIDE_CONFIGS:
+        raise SystemExit("--profile-wave takes a token-id wave configuration (0, 1 or 2)")
+    torch.cuda.set_device(local)
+    model = eg2.GGUFModel(eg2.synthetic.model_path(1234, "baseline"))
+    ex = eg2.Gemma2Executor(model, local)
+    ids, off = eg2.synthetic.wave(lengths, seed=100)
+    ex.stage(ids, off)
+    ex.launch(args.warmup)
+    ex.finish()
+    bufs = []
+    for mb in COPY_FLOOR_MB:
+        a = torch.randn(int(mb * 1e6) // 4, device=f"cuda:{local}")
+        b = torch.empty_like(a)
+        torch.mul(a, 1.0, out=b)
+        bufs.append((a, b))
+    torch.cuda.synchronize()
+    torch.cuda.profiler.start()
+    ex.launch(1)
+    ex.finish()
+    for a, b in bufs:
+        torch.mul(a, 1.0, out=b)
+    torch.cuda.synchronize()
+    torch.cuda.profiler.stop()
+    print(json.dumps({"profiled": desc, "kernels_per_wave": ex.kernels_per_wave,
+                      "copies_mb_read_plus_write": [2 * mb for mb in COPY_FLOOR_MB]}))
+    ex.close()
+    model.close()
 
 
 def parity_mode_run(eg2, model, ids, off, args):

@@ -8,6 +8,7 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include "launch.h"
 #include "ref_tanhf.h"
 
 namespace eg2 {
@@ -306,11 +307,8 @@ __device__ __forceinline__ uint16_t ref_fp32_to_fp16(float f) {
 }
 __device__ __forceinline__ float fp16_bits_to_f32(uint16_t h) { return __half2float(__ushort_as_half(h)); }
 
-// Which of the reference's CPU tiers the quantizer rounding and the GELU follow:
-// TIER_X86 -- the x86 tiers (gemma2_fast_x86.c), the fast path's choice;
-// TIER_SCALAR -- the scalar tier (EI_GEMMA2_CPU_X86=scalar: quants.c rounding,
-// kernels.c tanhf GELU), selectable in parity mode.
-enum : int { TIER_X86 = 0, TIER_SCALAR = 1 };
+// The reference CPU tier to reproduce (TIER_X86, TIER_SCALAR, TIER_VNNI512) is
+// declared in launch.h.
 
 // Q8_0 code of x with id = 1/d: trunc(x*id +- 0.5) on the x86 tiers
 // (gemma2_fast_x86.c:225-230), roundf(x*id) on the scalar tier (quants.c:97-177
@@ -406,6 +404,39 @@ __device__ __forceinline__ float gelu_tier(float x, int tier) {
 __device__ __forceinline__ float rms_scale(double sumsq, int d) {
     const float s = __double2float_rn(sumsq);
     return __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(s, float(d)), 1e-6f)));
+}
+// Horizontal sum of 8 lanes as the reference's hsum and 4-row Q8 tile end it
+// (gemma2_fast_x86.c:95-101, :239-244): (a_j + a_{j+4}) for j < 4, then
+// (s0 + s2) + (s1 + s3).
+__device__ __forceinline__ float hsum8(const float (&a)[8]) {
+    const float s0 = __fadd_rn(a[0], a[4]), s1 = __fadd_rn(a[1], a[5]);
+    const float s2 = __fadd_rn(a[2], a[6]), s3 = __fadd_rn(a[3], a[7]);
+    return __fadd_rn(__fadd_rn(s0, s2), __fadd_rn(s1, s3));
+}
+// _mm512_reduce_add_ps as the reference's build expands it
+// (gemma2_fast_x86.c:203): 256-bit halves added lane by lane, then 128-bit
+// halves, then lanes 0 + 2 and 1 + 3, then those two.
+__device__ __forceinline__ float reduce16(const float (&a)[16]) {
+    float t[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) t[i] = __fadd_rn(a[i], a[i + 8]);
+    const float u0 = __fadd_rn(t[0], t[4]), u1 = __fadd_rn(t[1], t[5]);
+    const float u2 = __fadd_rn(t[2], t[6]), u3 = __fadd_rn(t[3], t[7]);
+    return __fadd_rn(__fadd_rn(u0, u2), __fadd_rn(u1, u3));
+}
+// g2x_sum_squares (gemma2_fast_x86.c:280-289) of row[0, d) in shared memory,
+// d a multiple of 16, by one whole warp: lane i < 16 runs the fused
+// multiply-add chain over z = 16m + i (the 8-lane accumulators s0 and s1 of
+// 16-element chunks), then hsum8 of s0 + s1.  Every lane gets the sum.
+__device__ __forceinline__ float x86_sumsq_warp(const float *row, int d) {
+    const int lane = threadIdx.x & 31;
+    float c = 0.0f;
+    if (lane < 16)
+        for (int z = lane; z < d; z += 16) c = __fmaf_rn(row[z], row[z], c);
+    const float v = __fadd_rn(c, __shfl_down_sync(0xffffffffu, c, 8));  // lane i < 8: s0_i + s1_i
+    const float s = __fadd_rn(v, __shfl_down_sync(0xffffffffu, v, 4));  // lane j < 4: v_j + v_{j+4}
+    const float u = __fadd_rn(s, __shfl_down_sync(0xffffffffu, s, 2));  // lanes 0, 1: s0 + s2, s1 + s3
+    return __shfl_sync(0xffffffffu, __fadd_rn(u, __shfl_down_sync(0xffffffffu, u, 1)), 0);
 }
 __device__ __forceinline__ double warp_sum_d(double v) {
 #pragma unroll

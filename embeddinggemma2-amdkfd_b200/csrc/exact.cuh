@@ -61,12 +61,63 @@ __global__ void __launch_bounds__(PleExactCfg::THREADS) ple_exact_kernel(float *
     }
 }
 
+// The same projection in the order of the reference's default tier on an
+// AVX-512 VNNI host (g2x_dot4x4, gemma2_fast_x86.c:260-279, called from
+// gemma2_fast.c:537-545): per output, eight lanes of fused multiply-adds, lane
+// i over z = 8m + i in ascending m, then hsum8.  CTA tile 32 tokens x 64 rows;
+// each thread owns 4 tokens x 2 rows (eight lanes each).
+struct PleVnniCfg {
+    static constexpr int BT = 32, BR = 64, KC = 64, THREADS = 256;
+};
+__global__ void __launch_bounds__(PleVnniCfg::THREADS) ple_vnni_kernel(float *__restrict__ y,
+                                                                       const float *__restrict__ x,
+                                                                       const uint16_t *__restrict__ w, int n) {
+    using C = PleVnniCfg;
+    pdl_wait();
+    pdl_trigger();
+    __shared__ float xs[C::BT][C::KC + 1];
+    __shared__ float ws[C::BR][C::KC + 1];
+    const int t0 = blockIdx.y * C::BT, r0 = blockIdx.x * C::BR;
+    const int tx = threadIdx.x % 32, ty = threadIdx.x / 32;  // rows r0 + tx + 32j, tokens t0 + ty + 8i
+    float acc[4][2][8] = {};
+    for (int k0 = 0; k0 < 512; k0 += C::KC) {
+        __syncthreads();
+        for (int i = threadIdx.x; i < C::BT * C::KC; i += C::THREADS) {
+            const int tt = i / C::KC, z = i % C::KC, t = t0 + tt;
+            xs[tt][z] = t < n ? x[size_t(t) * 512 + k0 + z] : 0.0f;
+        }
+        for (int i = threadIdx.x; i < C::BR * C::KC; i += C::THREADS) {
+            const int rr = i / C::KC, z = i % C::KC;
+            ws[rr][z] = __uint_as_float(uint32_t(w[size_t(r0 + rr) * 512 + k0 + z]) << 16);
+        }
+        __syncthreads();
+        for (int z = 0; z < C::KC; z += 8)
+#pragma unroll
+            for (int l = 0; l < 8; ++l)
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    const float xv = xs[ty + 8 * i][z + l];
+#pragma unroll
+                    for (int j = 0; j < 2; ++j) acc[i][j][l] = __fmaf_rn(ws[tx + 32 * j][z + l], xv, acc[i][j][l]);
+                }
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const int t = t0 + ty + 8 * i;
+        if (t < n)
+#pragma unroll
+            for (int j = 0; j < 2; ++j) y[size_t(t) * (24 * 512) + r0 + tx + 32 * j] = hsum8(acc[i][j]);
+    }
+}
+
 // ple /= sqrtf(512), then rms_row with the per-slice weight
 // (gemma2_fast.c:952-956, :667-671).  CTA of 128 threads per (token, slice).
-__global__ void __launch_bounds__(128) ple_norm_kernel(float *__restrict__ ple, const float *__restrict__ w) {
+// tier TIER_VNNI512: the sum of squares in g2x_sum_squares' order.
+__global__ void __launch_bounds__(128) ple_norm_kernel(float *__restrict__ ple, const float *__restrict__ w, int tier) {
     pdl_wait();
     pdl_trigger();
     __shared__ double red[4];
+    __shared__ __align__(16) float buf[512];
     float4 *row = reinterpret_cast<float4 *>(ple + size_t(blockIdx.x) * 512);
     const int i = threadIdx.x;
     constexpr float S512 = 22.627416997969522f;  // sqrtf(512.0f)
@@ -74,8 +125,17 @@ __global__ void __launch_bounds__(128) ple_norm_kernel(float *__restrict__ ple, 
     v = make_float4(__fdiv_rn(v.x, S512), __fdiv_rn(v.y, S512), __fdiv_rn(v.z, S512), __fdiv_rn(v.w, S512));
     double ss = __dadd_rn(__dadd_rn(__dmul_rn(double(v.x), double(v.x)), __dmul_rn(double(v.y), double(v.y))),
                           __dadd_rn(__dmul_rn(double(v.z), double(v.z)), __dmul_rn(double(v.w), double(v.w))));
-    ss = warp_sum_d(ss);
-    if ((i & 31) == 0) red[i >> 5] = ss;
+    if (tier == TIER_VNNI512) {
+        reinterpret_cast<float4 *>(buf)[i] = v;
+        __syncthreads();
+        if (i < 32) {
+            const float s = x86_sumsq_warp(buf, 512);
+            if (i == 0) red[0] = double(s), red[1] = red[2] = red[3] = 0.0;
+        }
+    } else {
+        ss = warp_sum_d(ss);
+        if ((i & 31) == 0) red[i >> 5] = ss;
+    }
     __syncthreads();
     const float sc = rms_scale(__dadd_rn(__dadd_rn(red[0], red[1]), __dadd_rn(red[2], red[3])), 512);
     const float4 wv = reinterpret_cast<const float4 *>(w)[i];
@@ -92,7 +152,11 @@ __global__ void __launch_bounds__(128) ple_norm_kernel(float *__restrict__ ple, 
 //   sc[s] /= total;  o[z] = sum_s sc[s] * v[s][z]   (ascending s)
 // exp is the C library's expf algorithm with its exact rounding (ref_expf.h).
 // q, k, v are fp32 here.
-template <int D>
+// VNNI: the order of the reference's default tier on an AVX-512 VNNI host:
+// scores by g2x_dot4x4 (eight lanes of fused multiply-adds over z, then
+// hsum8; gemma2_fast.c:826-828) and o[z] by g2x_pv (one fused multiply-add per
+// key in ascending order; gemma2_fast_x86.c:326-349); the softmax is the same.
+template <int D, bool VNNI>
 __global__ void __launch_bounds__(128) attention_exact_kernel(float *__restrict__ out, const float *__restrict__ q,
                                                               const float *__restrict__ k, const float *__restrict__ v,
                                                               const unsigned *__restrict__ bounds, int n, int window) {
@@ -115,7 +179,15 @@ __global__ void __launch_bounds__(128) attention_exact_kernel(float *__restrict_
     for (int s = i; s < nk; s += 128) {
         const float *kr = k + (size_t(lo + s) * KV + kh) * D;
         float dot = 0.0f;
-        for (int z = 0; z < D; ++z) dot = __fadd_rn(dot, __fmul_rn(qs[z], kr[z]));
+        if constexpr (VNNI) {
+            float acc[8] = {};
+            for (int z = 0; z < D; z += 8)
+#pragma unroll
+                for (int l = 0; l < 8; ++l) acc[l] = __fmaf_rn(qs[z + l], kr[z + l], acc[l]);
+            dot = hsum8(acc);
+        } else {
+            for (int z = 0; z < D; ++z) dot = __fadd_rn(dot, __fmul_rn(qs[z], kr[z]));
+        }
         sc[s] = dot;
         mx = fmaxf(mx, dot);
     }
@@ -141,7 +213,9 @@ __global__ void __launch_bounds__(128) attention_exact_kernel(float *__restrict_
     for (int z = i; z < D; z += 128) {
         const float *vc = v + size_t(lo) * KV * D + kh * D + z;
         float acc = 0.0f;
-        for (int s = 0; s < nk; ++s) acc = __fadd_rn(acc, __fmul_rn(sc[s], vc[size_t(s) * KV * D]));
+        for (int s = 0; s < nk; ++s)
+            acc = VNNI ? __fmaf_rn(vc[size_t(s) * KV * D], sc[s], acc)
+                       : __fadd_rn(acc, __fmul_rn(sc[s], vc[size_t(s) * KV * D]));
         out[(size_t(t) * 4 + h) * D + z] = acc;
     }
 }

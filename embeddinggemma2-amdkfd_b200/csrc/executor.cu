@@ -254,8 +254,10 @@ struct Backend {
 
     Backend(const ei_gguf *g, int dev, unsigned flags)
         : model(g), device(dev), exact(flags & EG2_B200_EXACT), cap(flags & EG2_B200_WAVE_8192 ? WIDE_CAP : CAP),
-          tier(flags & EG2_B200_SCALAR_TIER ? 1 : 0) {
+          tier(flags & EG2_B200_SCALAR_TIER ? TIER_SCALAR : flags & EG2_B200_VNNI512_TIER ? TIER_VNNI512 : TIER_X86) {
         if (!g) throw std::runtime_error("empty model");
+        if ((flags & EG2_B200_VNNI512_TIER) && (!exact || (flags & EG2_B200_SCALAR_TIER)))
+            throw std::runtime_error("EG2_B200_VNNI512_TIER needs EG2_B200_EXACT and excludes EG2_B200_SCALAR_TIER");
         // The exact-order attention keeps a row's scores in shared memory.
         if (exact && cap > CAP) throw std::runtime_error("parity mode supports waves of up to 2048 tokens");
         // gemma2.c:30-62 hyperparameters.
@@ -429,10 +431,17 @@ struct Backend {
     }
 
     static int kidx(int k) { return k == 512 ? 0 : k == 1024 ? 1 : 2; }
+    // Parity mode at the VNNI-512 tier: the GEMMs in that tier's lane order.
+    bool vnni() const { return exact && tier == TIER_VNNI512; }
     void gemm(const Lane &ln, const Q8Weight &w, float *out, int ldo, int n) {
-        ck(launch_q8gemm(w.tmap, ln.tm_xq[kidx(w.k)], w.tscale, ln.tm_xs[kidx(w.k)], exact, out, ldo, n, w.rows, w.k,
-                         ln.stream),
-           "q8 GEMM");
+        if (vnni())
+            ck(launch_q8gemm_vnni(w.codes, w.scales, ln.xq, ln.xs, int(cap), out, nullptr, ldo, n, w.rows, w.k,
+                                  ln.offsets, ln.seq_count, ln.stream),
+               "q8 GEMM");
+        else
+            ck(launch_q8gemm(w.tmap, ln.tm_xq[kidx(w.k)], w.tscale, ln.tm_xs[kidx(w.k)], exact, out, ldo, n, w.rows,
+                             w.k, ln.stream),
+               "q8 GEMM");
     }
 
     // Both layer kinds run the tensor-core attention through maps whose token
@@ -456,11 +465,11 @@ struct Backend {
         mark("gemm_qkv");
         if (exact) {
             ck(launch_qkv_post(ln.qf, ln.kf, ln.vf, ln.qkv, L.q_norm, L.k_norm, rope_cos[rb], rope_sin[rb], ln.pos, N,
-                               L.d, s, true),
+                               L.d, s, true, tier),
                "qkv_post"),
                 ++launches;
             mark("qkv_post");
-            ck(launch_attention_exact(ln.attn, ln.qf, ln.kf, ln.vf, ln.bounds, N, L.d, L.d == 512 ? 0 : 512, s),
+            ck(launch_attention_exact(ln.attn, ln.qf, ln.kf, ln.vf, ln.bounds, N, L.d, L.d == 512 ? 0 : 512, s, tier),
                "attention"),
                 ++launches;
         } else {
@@ -489,15 +498,28 @@ struct Backend {
         mark("post_add");
         // ffn_gate and ffn_up in one GEMM whose epilogue applies gelu(gate) * up
         // and quantizes (ROW_GELU_QUANT fused); the result is the down operand.
-        ck(launch_q8gemm_geglu(L.gu.tmap, ln.tm_xq[0], L.gu.tscale, ln.tm_xs[0], exact, ln.gq, ln.gs, cap, N,
-                               L.gu.rows, L.gu.k, s, tier),
-           "GeGLU GEMM"),
-            ++launches;
+        if (vnni()) {  // gate and up as the reference's two GEMMs, then ROW_GELU_QUANT
+            ck(launch_q8gemm_vnni(L.gu.codes, L.gu.scales, ln.xq, ln.xs, int(cap), ln.qkv, ln.attn, 2048, N, L.gu.rows,
+                                  L.gu.k, ln.offsets, ln.seq_count, s),
+               "GeGLU GEMM");
+            ck(launch_gate_quant(ln.gq, ln.gs, cap, ln.qkv, ln.attn, N, 2048, 2048, 0, s, tier), "GELU quant");
+            launches += 2;
+        } else {
+            ck(launch_q8gemm_geglu(L.gu.tmap, ln.tm_xq[0], L.gu.tscale, ln.tm_xs[0], exact, ln.gq, ln.gs, cap, N,
+                                   L.gu.rows, L.gu.k, s, tier),
+               "GeGLU GEMM"),
+                ++launches;
+        }
         mark("gemm_geglu");
-        ck(launch_q8gemm(L.down.tmap, ln.tm_gq, L.down.tscale, ln.tm_gs, exact, ln.h, 512, N, L.down.rows, L.down.k,
-                         s),
-           "q8 GEMM"),
-            ++launches;
+        if (vnni())
+            ck(launch_q8gemm_vnni(L.down.codes, L.down.scales, ln.gq, ln.gs, int(cap), ln.h, nullptr, 512, N,
+                                  L.down.rows, L.down.k, ln.offsets, ln.seq_count, s),
+               "q8 GEMM");
+        else
+            ck(launch_q8gemm(L.down.tmap, ln.tm_gq, L.down.tscale, ln.tm_gs, exact, ln.h, 512, N, L.down.rows,
+                             L.down.k, s),
+               "q8 GEMM");
+        ++launches;
         mark("gemm_down");
         ck(launch_post_add(ln.x, ln.h, L.post_ffw_norm, nullptr, ln.xq, ln.xs, cap, nullptr, N, s, tier), "post_add"),
             ++launches;
@@ -535,7 +557,7 @@ struct Backend {
             ck(launch_embed(ln.x, ln.x_hi, ln.x_lo, token_embd, ln.ids, N, s), "embed"), ++launches;
         mark("embed");
         if (exact)
-            ck(launch_ple_exact(ln.ple, ln.x, ple_w, ple_norm, N, s), "PLE"), launches += 2;
+            ck(launch_ple_exact(ln.ple, ln.x, ple_w, ple_norm, N, s, tier), "PLE"), launches += 2;
         else
             ck(launch_ple(ln.tm_hi, ln.tm_lo, tm_ple, ln.ple, ple_norm, N, s), "PLE"), ++launches;
         mark("ple_proj");
@@ -824,7 +846,7 @@ struct Backend {
                "PLE upload");
             ck(cudaStreamSynchronize(s), "PLE upload");  // ple_in is pageable caller memory
         } else if (exact) {
-            ck(launch_ple_exact(ln.ple, ln.x, ple_w, ple_norm, N, s), "PLE");
+            ck(launch_ple_exact(ln.ple, ln.x, ple_w, ple_norm, N, s, tier), "PLE");
         } else {
             ck(launch_ple(ln.tm_hi, ln.tm_lo, tm_ple, ln.ple, ple_norm, N, s), "PLE");
         }

@@ -11,6 +11,7 @@
 #include "opsabi.cuh"
 #include "ple.cuh"
 #include "q8gemm.cuh"
+#include "q8vnni.cuh"
 #include "rowops.cuh"
 
 namespace eg2 {
@@ -111,6 +112,17 @@ cudaError_t launch_q8gemm(const CUtensorMap &w, const CUtensorMap &x, const CUte
     p.num_tiles = (R / Q8Cfg::BM) * p.tiles_t;
     return exact ? q8gemm_go<true, false>(w, x, sw, sx, p, s) : q8gemm_go<false, false>(w, x, sw, sx, p, s);
 }
+cudaError_t launch_q8gemm_vnni(const int8_t *wq, const float *ws, const int8_t *xq, const float *xs, int xs_stride,
+                               float *out, float *out_up, int ldo, int T, int R, int K, const unsigned *offsets,
+                               const unsigned *count, cudaStream_t s) {
+    if (T <= 0) return cudaSuccess;
+    if (!wq || !ws || !xq || !xs || !out || K <= 0 || K % Q8VnniCfg::KC || R <= 0 || R % 128 || xs_stride < T)
+        return cudaErrorInvalidValue;
+    if (out_up ? ldo < R / 2 : ldo < R) return cudaErrorInvalidValue;
+    return launch_pdl(q8gemm_vnni_kernel, dim3(R / Q8VnniCfg::BR, (T + Q8VnniCfg::BT - 1) / Q8VnniCfg::BT),
+                      dim3(Q8VnniCfg::THREADS), 0, s, out, out_up, ldo, wq, ws, xq, xs, xs_stride, T, R, K, offsets,
+                      count);
+}
 cudaError_t launch_q8gemm_geglu(const CUtensorMap &w, const CUtensorMap &x, const CUtensorMap &sw,
                                 const CUtensorMap &sx, bool exact, int8_t *q8, float *q8s, int q8s_stride, int T, int R,
                                 int K, cudaStream_t s, int tier) {
@@ -163,7 +175,7 @@ cudaError_t launch_norm_quant(int8_t *q, float *qs, int qs_stride, float *y, con
 
 cudaError_t launch_qkv_post(void *q, void *k, void *v, const float *qkv, const float *qn, const float *kn,
                             const float *rc, const float *rs, const unsigned *pos, int n, int d, cudaStream_t s,
-                            bool f32_out) {
+                            bool f32_out, int tier) {
     if (n <= 0) return cudaSuccess;
     if (d != 256 && d != 512) return cudaErrorInvalidValue;
     const int rows_per_tok = 4 + 2 * (512 / d), warps = n * rows_per_tok;
@@ -171,29 +183,42 @@ cudaError_t launch_qkv_post(void *q, void *k, void *v, const float *qkv, const f
     if (f32_out) {
         auto *qf = static_cast<float *>(q), *kf = static_cast<float *>(k), *vf = static_cast<float *>(v);
         if (d == 256)
-            return launch_pdl(qkv_post_kernel<256, float>, grid, block, 0, s, qf, kf, vf, qkv, qn, kn, rc, rs, pos, n);
-        return launch_pdl(qkv_post_kernel<512, float>, grid, block, 0, s, qf, kf, vf, qkv, qn, kn, rc, rs, pos, n);
+            return launch_pdl(qkv_post_kernel<256, float>, grid, block, 0, s, qf, kf, vf, qkv, qn, kn, rc, rs, pos, n, tier);
+        return launch_pdl(qkv_post_kernel<512, float>, grid, block, 0, s, qf, kf, vf, qkv, qn, kn, rc, rs, pos, n, tier);
     }
     auto *qh = static_cast<__half *>(q), *kh = static_cast<__half *>(k), *vh = static_cast<__half *>(v);
-    if (d == 256) return launch_pdl(qkv_post_kernel<256, __half>, grid, block, 0, s, qh, kh, vh, qkv, qn, kn, rc, rs, pos, n);
-    return launch_pdl(qkv_post_kernel<512, __half>, grid, block, 0, s, qh, kh, vh, qkv, qn, kn, rc, rs, pos, n);
+    if (d == 256) return launch_pdl(qkv_post_kernel<256, __half>, grid, block, 0, s, qh, kh, vh, qkv, qn, kn, rc, rs, pos, n, tier);
+    return launch_pdl(qkv_post_kernel<512, __half>, grid, block, 0, s, qh, kh, vh, qkv, qn, kn, rc, rs, pos, n, tier);
 }
 
 cudaError_t launch_attention_exact(float *out, const float *q, const float *k, const float *v, const unsigned *bounds,
-                                   int n, int d, int window, cudaStream_t s) {
+                                   int n, int d, int window, cudaStream_t s, int tier) {
     if (n <= 0) return cudaSuccess;
     if (n > 2048) return cudaErrorInvalidValue;  // key scores of one row live in shared memory
-    if (d == 256) return launch_pdl(attention_exact_kernel<256>, dim3(n, 4), dim3(128), 0, s, out, q, k, v, bounds, n, window);
-    if (d == 512) return launch_pdl(attention_exact_kernel<512>, dim3(n, 4), dim3(128), 0, s, out, q, k, v, bounds, n, window);
+    const bool vnni = tier == TIER_VNNI512;
+    const dim3 grid(n, 4), block(128);
+    if (d == 256)
+        return launch_pdl(vnni ? attention_exact_kernel<256, true> : attention_exact_kernel<256, false>, grid, block, 0,
+                          s, out, q, k, v, bounds, n, window);
+    if (d == 512)
+        return launch_pdl(vnni ? attention_exact_kernel<512, true> : attention_exact_kernel<512, false>, grid, block, 0,
+                          s, out, q, k, v, bounds, n, window);
     return cudaErrorInvalidValue;
 }
 
-cudaError_t launch_ple_exact(float *ple, const float *x, const void *w, const float *norm, int n, cudaStream_t s) {
+cudaError_t launch_ple_exact(float *ple, const float *x, const void *w, const float *norm, int n, cudaStream_t s,
+                             int tier) {
     if (n <= 0) return cudaSuccess;
-    if (cudaError_t e = launch_pdl(ple_exact_kernel, dim3(24 * 512 / PleExactCfg::BR, (n + PleExactCfg::BT - 1) / PleExactCfg::BT),
-                                   dim3(PleExactCfg::THREADS), 0, s, ple, x, static_cast<const uint16_t *>(w), n))
-        return e;
-    return launch_pdl(ple_norm_kernel, dim3(n * 24), dim3(128), 0, s, ple, norm);
+    const uint16_t *wb = static_cast<const uint16_t *>(w);
+    cudaError_t e;
+    if (tier == TIER_VNNI512)
+        e = launch_pdl(ple_vnni_kernel, dim3(24 * 512 / PleVnniCfg::BR, (n + PleVnniCfg::BT - 1) / PleVnniCfg::BT),
+                       dim3(PleVnniCfg::THREADS), 0, s, ple, x, wb, n);
+    else
+        e = launch_pdl(ple_exact_kernel, dim3(24 * 512 / PleExactCfg::BR, (n + PleExactCfg::BT - 1) / PleExactCfg::BT),
+                       dim3(PleExactCfg::THREADS), 0, s, ple, x, wb, n);
+    if (e) return e;
+    return launch_pdl(ple_norm_kernel, dim3(n * 24), dim3(128), 0, s, ple, norm, tier);
 }
 
 template <int D>

@@ -6,6 +6,15 @@
 
 namespace eg2 {
 
+// Which of the reference's CPU tiers the quantizer rounding and the GELU follow:
+// TIER_X86 -- the x86 tiers (gemma2_fast_x86.c), the fast path's choice;
+// TIER_SCALAR -- the scalar tier (EI_GEMMA2_CPU_X86=scalar: quants.c rounding,
+// kernels.c tanhf GELU), selectable in parity mode;
+// TIER_VNNI512 -- the x86 tiers' rounding and GELU, and in parity mode also the
+// float orders of the default tier on an AVX-512 VNNI host (lane sums of
+// gemma2_fast_x86.c instead of the scalar loops).
+enum : int { TIER_X86 = 0, TIER_SCALAR = 1, TIER_VNNI512 = 2 };
+
 // cuTensorMapEncodeTiled through the runtime's driver entry point.
 bool encode_tmap_2d(CUtensorMap *map, CUtensorMapDataType dtype, const void *base, uint64_t inner, uint64_t outer,
                     uint64_t row_bytes, uint32_t box_inner, uint32_t box_outer, bool swizzle128);
@@ -16,9 +25,9 @@ bool bf16_tmap(CUtensorMap *map, const void *base, uint64_t k, uint64_t rows, ui
 // Block-major fp32 scale plane [kb][stride]: box box_cols x kb, no swizzle.
 bool scale_tmap(CUtensorMap *map, const float *base, uint64_t stride, uint64_t kb, uint32_t box_cols);
 
-// Kernel launches (all asynchronous on `s`).  `tier` (TIER_X86 / TIER_SCALAR
-// in common.cuh) selects the quantizer rounding and GELU of the reference tier
-// to reproduce.
+// Kernel launches (all asynchronous on `s`).  `tier` (above) selects the
+// quantizer rounding and GELU of the reference tier to reproduce, and the sum
+// orders of the row kernels.
 // out[T][ldo] = tokens x weight rows.  Maps: weight codes [R][K] with box
 // 128 rows, token codes [T][K] with box 64 rows, weight scales [K/32][R] box
 // 128, token scales [K/32][stride] box 64.  R must be a multiple of 128.
@@ -31,6 +40,17 @@ cudaError_t launch_q8gemm(const CUtensorMap &w, const CUtensorMap &x, const CUte
 cudaError_t launch_q8gemm_geglu(const CUtensorMap &w, const CUtensorMap &x, const CUtensorMap &sw,
                                 const CUtensorMap &sx, bool exact, int8_t *q8, float *q8s, int q8s_stride, int T, int R,
                                 int K, cudaStream_t s, int tier = 0);
+// Parity mode at TIER_VNNI512: the GEMM in the float order of the reference's
+// default tier on an AVX-512 VNNI host (q8vnni.cuh), on CUDA cores.  Weight
+// codes [R][K] with scales [K/32][R], token codes [T][K] with scales
+// [K/32][xs_stride]; out[T][ldo].  With out_up set, the weight is the GeGLU
+// interleave of launch_q8gemm_geglu and the gate and up columns go to out and
+// out_up ([T][ldo] each).  offsets/count (device memory, may be NULL) give the
+// wave's real token count, which selects the reference's path (<= 8 tokens:
+// its 4-row tile).  K a multiple of 256, R of 128.
+cudaError_t launch_q8gemm_vnni(const int8_t *wq, const float *ws, const int8_t *xq, const float *xs, int xs_stride,
+                               float *out, float *out_up, int ldo, int T, int R, int K, const unsigned *offsets,
+                               const unsigned *count, cudaStream_t s);
 cudaError_t launch_ple(const CUtensorMap &hi, const CUtensorMap &lo, const CUtensorMap &w, float *ple,
                        const float *norm, int M, cudaStream_t s);
 cudaError_t launch_embed(float *x, void *x_hi, void *x_lo, const void *emb, const int *ids, int n, cudaStream_t s);
@@ -41,11 +61,14 @@ cudaError_t launch_norm_quant(int8_t *q, float *qs, int qs_stride, float *y, con
 // q/k/v outputs are fp16, or fp32 when f32_out (parity mode).
 cudaError_t launch_qkv_post(void *q, void *k, void *v, const float *qkv, const float *qn, const float *kn,
                             const float *rc, const float *rs, const unsigned *pos, int n, int d, cudaStream_t s,
-                            bool f32_out);
-// Parity mode: the reference's scalar attention and PLE orders on CUDA cores.
+                            bool f32_out, int tier = 0);
+// Parity mode: the reference's attention and PLE orders on CUDA cores -- the
+// scalar loops, or with tier TIER_VNNI512 the lane sums of its default tier on
+// an AVX-512 VNNI host.
 cudaError_t launch_attention_exact(float *out, const float *q, const float *k, const float *v, const unsigned *bounds,
-                                   int n, int d, int window, cudaStream_t s);
-cudaError_t launch_ple_exact(float *ple, const float *x, const void *w, const float *norm, int n, cudaStream_t s);
+                                   int n, int d, int window, cudaStream_t s, int tier = 0);
+cudaError_t launch_ple_exact(float *ple, const float *x, const void *w, const float *norm, int n, cudaStream_t s,
+                             int tier = 0);
 cudaError_t launch_attention(float *out, const void *q, const void *k, const void *v, const unsigned *bounds, int n,
                              int d, int window, cudaStream_t s);
 // The tensor-core attention (d = 256: Q [n][4][256], K/V [n][2][256]; d = 512:

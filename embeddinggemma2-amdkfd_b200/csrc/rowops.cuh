@@ -96,6 +96,25 @@ __device__ __forceinline__ double cta_sum_d(double v, double *red) {
     return s;
 }
 
+// The row sum of squares of a CTA whose threads hold one float4 each (thread
+// i: elements 4i..4i+3 of a WIDTH-wide row), as the reference computes it:
+// for TIER_VNNI512 in g2x_sum_squares' float order (the row staged in buf,
+// then one warp), otherwise in double like the scalar loop.  Returned as a
+// double (exact for the float sum).
+template <int WIDTH>
+__device__ __forceinline__ double cta_row_sumsq(const float4 v, int tier, double *red, float *buf) {
+    if (tier != TIER_VNNI512) return cta_sum_d<WIDTH / 128>(sumsq4(0.0, v), red);
+    reinterpret_cast<float4 *>(buf)[threadIdx.x] = v;
+    __syncthreads();
+    if (threadIdx.x < 32) {
+        const float ss = x86_sumsq_warp(buf, WIDTH);
+        if (threadIdx.x == 0) red[0] = double(ss);
+    }
+    __syncthreads();
+    const double ss = red[0];
+    __syncthreads();  // buf and red may be reused by a second sum
+    return ss;
+}
 // ROW_NORM_QUANT (gemma2_fast.c:685-691): RMS norm with weight w, then Q8_0.
 // CTA per row, one float4 per thread (WIDTH / 4 threads).
 template <int WIDTH>
@@ -107,9 +126,10 @@ __global__ void __launch_bounds__(WIDTH / 4) norm_quant_kernel(int8_t *__restric
     pdl_trigger();
     constexpr int WARPS = WIDTH / 128;
     __shared__ double red[WARPS];
+    __shared__ __align__(16) float buf[WIDTH];
     const int t = blockIdx.x, i = threadIdx.x, lane = i & 31;
     float4 v = reinterpret_cast<const float4 *>(x + size_t(t) * WIDTH)[i];
-    const float sc = rms_scale(cta_sum_d<WARPS>(sumsq4(0.0, v), red), WIDTH);
+    const float sc = rms_scale(cta_row_sumsq<WIDTH>(v, tier, red, buf), WIDTH);
     v = scale_w4(v, sc, reinterpret_cast<const float4 *>(w)[i]);
     if (y) reinterpret_cast<float4 *>(y + size_t(t) * WIDTH)[i] = v;
     float s;
@@ -143,10 +163,11 @@ template <int D, typename OutT>
 __global__ void qkv_post_kernel(OutT *__restrict__ qo, OutT *__restrict__ ko, OutT *__restrict__ vo,
                                 const float *__restrict__ qkv, const float *__restrict__ qn,
                                 const float *__restrict__ kn, const float *__restrict__ rc,
-                                const float *__restrict__ rs, const unsigned *__restrict__ pos, int n) {
+                                const float *__restrict__ rs, const unsigned *__restrict__ pos, int n, int tier) {
     pdl_wait();
     pdl_trigger();
     constexpr int KV = 512 / D, HR = 4 + 2 * KV, PER = D / 256;  // float4 chunks per lane per half
+    __shared__ __align__(16) float rowbuf[8][D];  // TIER_VNNI512: the warp's row, for the x86 sum order
     const int gw = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5), lane = threadIdx.x & 31;
     if (gw >= n * HR) return;
     const int t = gw / HR, hr = gw % HR;
@@ -175,7 +196,17 @@ __global__ void qkv_post_kernel(OutT *__restrict__ qo, OutT *__restrict__ ko, Ou
     }
 #pragma unroll
     for (int i = 0; i < PER; ++i) ss = sumsq4(ss, b[i]);
-    const float sc = rms_scale(warp_sum_d(ss), D);
+    if (tier == TIER_VNNI512) {
+        float4 *rb = reinterpret_cast<float4 *>(rowbuf[(threadIdx.x >> 5) & 7]);
+#pragma unroll
+        for (int i = 0; i < PER; ++i) rb[i * 32 + lane] = a[i], rb[D / 8 + i * 32 + lane] = b[i];
+        __syncwarp();
+        ss = double(x86_sumsq_warp(rowbuf[(threadIdx.x >> 5) & 7], D));
+        __syncwarp();
+    } else {
+        ss = warp_sum_d(ss);
+    }
+    const float sc = rms_scale(ss, D);
     const size_t p = size_t(pos[t]) * (D / 2);
     const float4 one = make_float4(1.0f, 1.0f, 1.0f, 1.0f);
 #pragma unroll
@@ -221,18 +252,19 @@ __global__ void __launch_bounds__(128) post_add_kernel(float *__restrict__ x, co
     pdl_wait();
     pdl_trigger();
     __shared__ double red[2][4];
+    __shared__ __align__(16) float buf[512];
     const int t = blockIdx.x, i = threadIdx.x, lane = i & 31;
     float4 *xp = reinterpret_cast<float4 *>(x + size_t(t) * 512) + i;
     const float4 hv = reinterpret_cast<const float4 *>(h + size_t(t) * 512)[i];
     float4 xv = *xp;
-    const float sc = rms_scale(cta_sum_d<4>(sumsq4(0.0, hv), red[0]), 512);
+    const float sc = rms_scale(cta_row_sumsq<512>(hv, tier, red[0], buf), 512);
     const float ls = scale ? *scale : 1.0f;
     const float4 hn = scale_w4(hv, sc, reinterpret_cast<const float4 *>(w)[i]);
     xv = make_float4(__fmul_rn(__fadd_rn(xv.x, hn.x), ls), __fmul_rn(__fadd_rn(xv.y, hn.y), ls),
                      __fmul_rn(__fadd_rn(xv.z, hn.z), ls), __fmul_rn(__fadd_rn(xv.w, hn.w), ls));
     *xp = xv;
     if (next_w) {
-        const float sc2 = rms_scale(cta_sum_d<4>(sumsq4(0.0, xv), red[1]), 512);
+        const float sc2 = rms_scale(cta_row_sumsq<512>(xv, tier, red[1], buf), 512);
         xv = scale_w4(xv, sc2, reinterpret_cast<const float4 *>(next_w)[i]);
     }
     float s;

@@ -19,7 +19,7 @@ WIDE_MAX_TOKENS = 8192  # EG2_B200_WAVE_8192
 VOCAB = 262144
 
 
-EG2_B200_EXACT, EG2_B200_SCALAR_TIER, EG2_B200_WAVE_8192 = 1, 2, 4  # include/eg2_executor.h
+EG2_B200_EXACT, EG2_B200_SCALAR_TIER, EG2_B200_WAVE_8192, EG2_B200_VNNI512_TIER = 1, 2, 4, 8  # include/eg2_executor.h
 
 
 class ExecutorError(RuntimeError):
@@ -105,18 +105,24 @@ class Gemma2Executor:
         """exact=True: parity mode (eg2_b200_create with EG2_B200_EXACT), every
         operation in the reference CPU graph's own float order; tier="scalar"
         adds the scalar CPU tier's quantizer rounding and GELU
-        (EG2_B200_SCALAR_TIER), so the wave reproduces that tier.
+        (EG2_B200_SCALAR_TIER), so the wave reproduces that tier;
+        tier="vnni512" the float orders, quantizer and GELU of its default tier
+        on an AVX-512 VNNI host (EG2_B200_VNNI512_TIER), so the wave reproduces
+        that one.
         max_tokens=8192: waves up to the reference CPU graph's limit
         (EG2_B200_WAVE_8192; fast path only)."""
         lib = _lib.load()
         self.model = model  # borrowed by the context: keep it alive
         err = _err()
-        if tier not in ("x86", "scalar"):
-            raise ValueError("tier must be 'x86' or 'scalar'")
+        if tier not in ("x86", "scalar", "vnni512"):
+            raise ValueError("tier must be 'x86', 'scalar' or 'vnni512'")
+        if tier == "vnni512" and not exact:
+            raise ValueError("tier 'vnni512' is a parity-mode tier (exact=True)")
         if max_tokens not in (MAX_TOKENS, WIDE_MAX_TOKENS):
             raise ValueError(f"max_tokens must be {MAX_TOKENS} or {WIDE_MAX_TOKENS}")
         if exact or max_tokens == WIDE_MAX_TOKENS:
             flags = (EG2_B200_EXACT if exact else 0) | (EG2_B200_SCALAR_TIER if exact and tier == "scalar" else 0)
+            flags |= EG2_B200_VNNI512_TIER if exact and tier == "vnni512" else 0
             flags |= EG2_B200_WAVE_8192 if max_tokens == WIDE_MAX_TOKENS else 0
             ctx = lib.eg2_b200_create(model.handle, 0 if device is None else int(device), flags, err, len(err))
         elif device is None:

@@ -43,13 +43,20 @@ void *ei_gemma2_kfd_create_on(const ei_gguf *g, int device, char *err, size_t le
  * every operation in the reference CPU graph's own float order (GEMMs in the
  * scalar tile's rounding, attention and the PLE projection on exact-order
  * CUDA-core kernels instead of the fp16/bf16 tensor-core ones), for checking
- * results against the reference; about 3x slower.  No counterpart in the
+ * results against the reference; about 12x slower.  No counterpart in the
  * reference's executor ABI. */
 #define EG2_B200_EXACT 1u
 /* With EG2_B200_EXACT: the quantizer rounding (roundf) and GELU (tanhf) of the
  * reference's scalar CPU tier (EI_GEMMA2_CPU_X86=scalar) instead of the x86
  * tiers' (trunc(x +- 0.5), exp polynomial), which the fast path uses. */
 #define EG2_B200_SCALAR_TIER 2u
+/* With EG2_B200_EXACT: the float orders of the reference CPU graph's default
+ * tier on an AVX-512 VNNI host (vnni512 with the repacked 512-bit GEMM,
+ * gemma2_fast_x86.c:24-48: its GEMM lane sums, g2x_dot4x4 for the PLE
+ * projection and attention scores, g2x_sum_squares, g2x_pv), with its x86
+ * quantizer and GELU, so that a wave equals ei_gemma2_embed_batch_fast_ctx on
+ * such a host bit for bit.  Excludes EG2_B200_SCALAR_TIER. */
+#define EG2_B200_VNNI512_TIER 8u
 /* Waves of up to 8192 packed tokens, the reference CPU graph's limit
  * (gemma2_fast.c:924-925, "EmbeddingGemma 2 accepts 1..8192 input tokens")
  * instead of the KFD executor's 2048; the context allocates for 8192 tokens.

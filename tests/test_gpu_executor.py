@@ -246,6 +246,36 @@ def test_parity_mode_scalar_tier_equals_reference(eg2, syn, norm, port):
         m.close()
 
 
+@pytest.mark.parametrize("norm", ["baseline", "plus1"])
+def test_parity_mode_vnni512_tier_equals_reference_default_tier(eg2, syn, norm):
+    """Parity mode at the VNNI-512 tier (EG2_B200_EXACT | EG2_B200_VNNI512_TIER):
+    the embeddings equal, bit for bit, the reference CPU graph's DEFAULT tier as
+    it runs on an AVX-512 VNNI host (vnni512+gemm512, the tier every golden
+    fixture records; compiled from the reference's sources) -- config 0 on both
+    weight models, the plus-one model included where the reference's own tiers
+    decorrelate; waves of 8, 7 and 3 tokens (its 4-row Q8 tile) and of 9 (its
+    512-bit GEMM); the 2 x 128 and 1 x 2048 waves; and the input-rows wave."""
+    m = eg2.GGUFModel(syn.model_path(1234, norm))
+    ex = eg2.Gemma2Executor(m, 0, exact=True, tier="vnni512")
+    try:
+        g = golden(f"golden_{norm}.npz")
+        assert str(g["best_tier"]) == "vnni512+gemm512"
+        np.testing.assert_array_equal(ex.batch(g["ids"], g["offsets"]), g["embed_best"])
+        if norm == "baseline":
+            s = golden("golden_short_baseline.npz")
+            for i in range(4):
+                np.testing.assert_array_equal(ex.batch(s[f"ids{i}"], s[f"offsets{i}"]), s[f"embed{i}"])
+            lg = golden("golden_long_baseline.npz")
+            assert str(lg["tier"]) == "vnni512+gemm512"
+            np.testing.assert_array_equal(ex.batch(lg["w2x128_ids"], lg["w2x128_offsets"]), lg["w2x128_embed"])
+            np.testing.assert_array_equal(ex.batch(lg["long_ids"], lg["long_offsets"]), lg["long_embed"])
+            r = golden("golden_inputs_baseline.npz")
+            np.testing.assert_array_equal(ex.batch_rows(r["inputs"], r["offsets"]), r["embed_best"])
+    finally:
+        ex.close()
+        m.close()
+
+
 def _embedding_rows(model_path, ids):
     """x = (d * q) * sqrt(512) for each id, in float32 exactly as the embed
     kernel and the reference compute it (gemma2_fast.c:942-950)."""

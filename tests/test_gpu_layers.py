@@ -127,6 +127,28 @@ def test_parity_mode_layers_bit_identical(eg2, model_baseline, traces):
         m.close()
 
 
+def test_parity_mode_vnni512_layers_bit_identical(eg2, model_baseline, port, gguf, syn):
+    """Parity mode at the VNNI-512 tier reproduces, layer by layer, the
+    restatement in that tier's float orders (itself bit-identical to the
+    reference's default tier on an AVX-512 VNNI host, tests/test_cpu_oracle.py),
+    including the per-layer embeddings it projects from x_0."""
+    ids, off = syn.wave(CASES["config0"], seed=7)
+    port.set_order(port.ORDER_VNNI512)
+    try:
+        _, xl, ple = port.trace(gguf, ids, off, quant_mode=port.ROUND_X86, gelu_mode=1)
+    finally:
+        port.set_order(port.ORDER_SCALAR)
+    m = eg2.GGUFModel(model_baseline)
+    ex = eg2.Gemma2Executor(m, 0, exact=True, tier="vnni512")
+    try:
+        for l in (0, 1, 5, 11, 23):
+            np.testing.assert_array_equal(ex.forward_layers(xl[l], ple, off, l, l + 1), xl[l + 1])
+        np.testing.assert_array_equal(ex.forward_layers(xl[0], None, off, 0, 1), xl[1])  # device PLE
+    finally:
+        ex.close()
+        m.close()
+
+
 def test_layer_range_errors(fast, eg2, traces):
     ids, off, xl, ple = traces("config0")
     with pytest.raises(eg2.ExecutorError, match="invalid layer range"):
