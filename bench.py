@@ -1017,33 +1017,47 @@ def profile_wave(args, local):
 
 
 def parity_mode_run(eg2, model, ids, off, args):
-    """The same wave in parity mode with the scalar tier's choices
-    (EG2_B200_EXACT | EG2_B200_SCALAR_TIER), whose embeddings are bit-identical
-    to the reference CPU graph's scalar tier: device-resident waves timed with
-    CUDA events like `value` (a few steps; a wave takes tens of ms)."""
+    """The same wave in parity mode, whose embeddings are bit-identical to a
+    tier of the reference CPU graph: with the scalar tier's choices
+    (EG2_B200_EXACT | EG2_B200_SCALAR_TIER), and, under `vnni512_tier`, in the
+    float orders of its default tier on an AVX-512 VNNI host (EG2_B200_EXACT |
+    EG2_B200_VNNI512_TIER).  Device-resident waves timed with CUDA events like
+    `value` (a few steps; a wave takes tens of ms)."""
     import torch
-    px = eg2.Gemma2Executor(model, 0, exact=True, tier="scalar")
-    stream = torch.cuda.ExternalStream(px.stream, device=0)
-    px.stage(ids, off)
-    px.launch(1)
-    px.finish()
-    steps = max(3, min(args.steps, 10))
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    torch.cuda.synchronize()
-    with torch.cuda.stream(stream):
-        e0.record(stream)
-        px.launch(steps)
-        e1.record(stream)
-    torch.cuda.synchronize()
-    ms = e0.elapsed_time(e1) / steps
-    px.finish()
     n = int(off[-1])
-    res = {"value": n / (ms * 1e-3), "unit": "tokens/s", "ms_per_step": ms, "steps": steps,
-           "kernels_per_wave": px.kernels_per_wave,
-           "dtype": "reference scalar tier's float order: int8 Q8_0 GEMMs with the scalar tile's roundings, "
-                    "fp32 CUDA-core attention and PLE in the CPU loop order",
-           "parity": "bit-identical to the reference CPU graph's scalar tier (tests/test_gpu_executor.py)"}
-    px.close()
+
+    def timed(tier):
+        px = eg2.Gemma2Executor(model, 0, exact=True, tier=tier)
+        stream = torch.cuda.ExternalStream(px.stream, device=0)
+        px.stage(ids, off)
+        px.launch(2)
+        px.finish()
+        steps = max(4, min(args.steps, 10))
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        with torch.cuda.stream(stream):
+            e0.record(stream)
+            px.launch(steps)
+            e1.record(stream)
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / steps
+        px.finish()
+        k = px.kernels_per_wave
+        px.close()
+        return {"value": n / (ms * 1e-3), "unit": "tokens/s", "ms_per_step": ms, "steps": steps,
+                "kernels_per_wave": k}
+
+    res = timed("scalar")
+    res.update(dtype="reference scalar tier's float order: int8 Q8_0 GEMMs with the scalar tile's roundings, "
+                     "fp32 CUDA-core attention and PLE in the CPU loop order",
+               parity="bit-identical to the reference CPU graph's scalar tier (tests/test_gpu_executor.py)")
+    v = timed("vnni512")
+    v.update(dtype="reference default tier's float order on an AVX-512 VNNI host: Q8_0 GEMMs as its 16-lane "
+                   "int32 lane sums with fused multiply-adds (dp4a on CUDA cores), fp32 attention and PLE in its "
+                   "8-lane orders",
+             parity="bit-identical to the reference CPU graph's default tier, vnni512+gemm512 "
+                    "(tests/test_gpu_executor.py, tests/test_gpu_layers.py)")
+    res["vnni512_tier"] = v
     return res
 
 
