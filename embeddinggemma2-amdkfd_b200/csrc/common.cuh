@@ -111,7 +111,7 @@ __device__ __forceinline__ bool wait_bar(uint64_t *bar, uint32_t parity, volatil
 __device__ __forceinline__ void tma_prefetch(const CUtensorMap *map) {
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }
-// 2-D tiled load (no multicast); c0 is the innermost coordinate in elements and
+// 2-D tiled load into this CTA's shared memory; c0 is the innermost coordinate in elements and
 // every caller passes a multiple of the 128-byte swizzle row, so c0 * element
 // size is always a multiple of 16 bytes.
 __device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, uint64_t *bar, int c0, int c1) {
@@ -122,7 +122,7 @@ __device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, u
         : "memory");
 }
 
-// 3-D tiled load (no multicast); c0 (innermost, elements) is always a multiple
+// 3-D tiled load into this CTA's shared memory; c0 (innermost, elements) is always a multiple
 // of 64 16-bit elements here, so c0 * element size is a multiple of 16 bytes.
 __device__ __forceinline__ void tma_load_3d(void *dst, const CUtensorMap *map, uint64_t *bar, int c0, int c1, int c2) {
     asm volatile(
