@@ -622,6 +622,186 @@ def engine_run(args):
     model.close()
 
 
+# ---------------------------------------------------------------- config 3 over HTTP
+SERVER_BIN = os.path.join(ROOT, "oracle", "_ref", "eg2server")
+SERVER_CPU_BIN = os.path.join(ROOT, "oracle", "_ref", "eg2server_cpu")
+METRIC_HTTP = "embedded tokens/s per box (mixed-length requests over HTTP)"
+
+
+def http_texts(lens):
+    """Texts whose tokenization by the seeded model's placeholder tokenizer has
+    each text's packed length (body + 2): it maps every byte of the text, with
+    the leading U+2581 (3 bytes), to a byte token after BOS, so a text of c
+    characters without spaces is 4 + c tokens.  Each text starts with its own
+    (request, text) tag, so none repeats."""
+    texts = []
+    for r in range(len(lens)):
+        row = []
+        for j, body in enumerate(lens[r]):
+            c = max(int(body) - 2, 1)
+            tag = f"r{r:x}q{j:x}z"
+            row.append((tag + "a" * c)[:c] if c < len(tag) else tag + "a" * (c - len(tag)))
+        texts.append(row)
+    return texts
+
+
+def start_server(binary, model_path, port, backend, device=None, extra=()):
+    env = dict(os.environ)
+    if device is not None:
+        env["EG2_B200_DEVICE"] = str(device)
+    log = open(os.path.join(ROOT, "gpurun_out" if os.path.isdir(os.path.join(ROOT, "gpurun_out")) else ".",
+                            f"server_{backend}_{port}.log"), "w")
+    cmd = [binary, "--bind", "127.0.0.1", "--port", str(port), "--backend", backend, "--model", model_path,
+           "--text-only", "--response-cache-mb", "0", *extra]
+    proc = subprocess.Popen(cmd, stdout=log, stderr=subprocess.STDOUT, env=env)
+    import http.client
+    t0 = time.time()
+    while time.time() - t0 < 180:
+        if proc.poll() is not None:
+            raise RuntimeError(f"server exited with {proc.returncode}: {' '.join(cmd)}")
+        try:
+            c = http.client.HTTPConnection("127.0.0.1", port, timeout=2)
+            c.request("GET", "/healthz")
+            if c.getresponse().status == 200:
+                c.close()
+                return proc
+        except OSError:
+            time.sleep(0.5)
+    proc.kill()
+    raise RuntimeError("server did not come up")
+
+
+def stop_server(proc):
+    proc.terminate()
+    try:
+        proc.wait(timeout=30)
+    except subprocess.TimeoutExpired:
+        proc.kill()
+        proc.wait()
+
+
+def http_embed(conn, texts, dims):
+    """One /api/embed request (base64 float32 rows); returns the embeddings."""
+    import base64
+    body = json.dumps({"input": texts, "dimensions": int(dims), "encoding_format": "base64"}).encode()
+    conn.request("POST", "/api/embed", body=body, headers={"Content-Type": "application/json"})
+    resp = conn.getresponse()
+    payload = resp.read()
+    if resp.status != 200:
+        raise RuntimeError(f"HTTP {resp.status}: {payload[:200]!r}")
+    rows = json.loads(payload)["embeddings"]
+    return np.stack([np.frombuffer(base64.b64decode(r), np.float32) for r in rows])
+
+
+def http_run(args, reference=False):
+    """Config 3 over HTTP through the reference's own server
+    (vendor/embeddinggemma.c/src/server.c + inference_service.c + engine.c,
+    built unchanged by oracle/Makefile `server`): its tokenizer, batcher and
+    JSON layer in front of this executor (`--backend kfd`), one server process
+    per GPU (the engine allows one KFD executor per process,
+    engine.c:1163-1169).  All 256 requests (16 texts each, dims per request)
+    are queued at t = 0; 32 client connections per server take them in order,
+    request r on server r % N, responses as base64 float32.  tokens/s = the
+    requests' packed tokens / wall time; latency from t = 0 to the response.
+    --impl reference runs the same server on its own CPU backend (16 threads)
+    over the first 16 requests (a bounded sample)."""
+    import http.client
+    import queue
+    import threading
+    syn = importlib.import_module("embeddinggemma2-amdkfd_b200.synthetic")
+    lens, dims = syn.mixed_load(256, 16)
+    texts = http_texts(lens)
+    n_req = 16 if reference else len(lens)
+    n_srv = 1 if reference else args.gpus
+    model_path = syn.model_path(1234, "baseline", tokenizer=True)
+    binary = SERVER_CPU_BIN if reference else SERVER_BIN
+    if not os.path.exists(binary):
+        raise SystemExit(f"{binary} missing: make -C oracle server")
+    backend = "cpu" if reference else "kfd"
+    extra = ("--threads", str(os.cpu_count() or 8)) if reference else ()
+    procs = [start_server(binary, model_path, 42700 + d, backend, None if reference else d, extra)
+             for d in range(n_srv)]
+    conns_per_srv = 8 if reference else 32
+    try:
+        def run_all(requests):
+            jobs = [queue.Queue() for _ in range(n_srv)]
+            for r in requests:
+                jobs[r % n_srv].put(r)
+            done_at, lock = {}, threading.Lock()
+            t0 = time.perf_counter()
+
+            def client(d):
+                conn = http.client.HTTPConnection("127.0.0.1", 42700 + d, timeout=600)
+                while True:
+                    try:
+                        r = jobs[d].get_nowait()
+                    except queue.Empty:
+                        break
+                    out = http_embed(conn, texts[r], dims[r])
+                    assert out.shape == (16, int(dims[r])) and np.isfinite(out).all()
+                    with lock:
+                        done_at[r] = (time.perf_counter() - t0) * 1000.0
+                conn.close()
+            threads = [threading.Thread(target=client, args=(d,)) for d in range(n_srv) for _ in range(conns_per_srv)]
+            for th in threads:
+                th.start()
+            for th in threads:
+                th.join()
+            return (time.perf_counter() - t0) * 1000.0, done_at
+
+        run_all(range(min(n_req, 32)) if not reference else range(2))  # warm-up: wave-bucket graphs, connections
+        ms, done_at = run_all(range(n_req))
+    finally:
+        for p in procs:
+            stop_server(p)
+    tokens = int(sum(4 + len(t) for r in range(n_req) for t in texts[r]))  # BOS + U+2581 (3 bytes) + bytes
+    lat = list(done_at.values())
+    line = {"metric": METRIC_HTTP, "value": tokens / (ms * 1e-3), "unit": "tokens/s", "n_gpus": 0 if reference
+            else n_srv, "steps": 1, "warmup": 1, "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": DTYPE_REFERENCE if reference else DTYPE_FAST, "data": "synthetic",
+            "config": {"workload": CONFIGS[3][0] + ", over HTTP (/api/embed, base64)", "requests": n_req,
+                       "texts_per_request": 16, "tokens": tokens,
+                       "server": "reference server.c, " + ("cpu backend" if reference else
+                                                           f"kfd backend = this executor, {n_srv} process(es), "
+                                                           "one per GPU"),
+                       "arrival": "all requests queued at t = 0 (offline load)",
+                       "client": f"{conns_per_srv} keep-alive connections per server"},
+            "latency_ms": {"p50": float(np.percentile(lat, 50)), "p99": float(np.percentile(lat, 99)),
+                           "max": float(max(lat))},
+            "e2e": {"value": tokens / (ms * 1e-3), "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0, "api": "HTTP /api/embed"}}
+    if reference:
+        line["impl"] = "reference"
+    else:
+        line["tokenizer"] = tokenizer_rate(model_path, [t for row in texts for t in row])
+    print(json.dumps(line), flush=True)
+
+
+def tokenizer_rate(model_path, texts):
+    """The reference engine's own tokenizer (tokenizer.c, ei_tokenize_spm as
+    engine.c:1143 calls it) over the load's texts on one host thread: the
+    per-thread rate that the server's tokenizer workers
+    (--tokenizer-workers, inference_service.h:21) multiply."""
+    import ctypes as C
+    import oracle
+    lib = C.CDLL(oracle.ENGINE_LINK_SO)
+    lib.eg2link_open_cpu.restype = C.c_void_p
+    lib.eg2link_open_cpu.argtypes = [C.c_char_p]
+    lib.eg2link_tokenize.restype = C.c_size_t
+    lib.eg2link_tokenize.argtypes = [C.c_void_p, C.c_char_p, C.c_size_t, C.c_void_p, C.c_size_t]
+    lib.eg2link_close.argtypes = [C.c_void_p]
+    h = lib.eg2link_open_cpu(model_path.encode())
+    enc = [t.encode() for t in texts]
+    tokens = 0
+    t0 = time.perf_counter()
+    for b in enc:
+        tokens += lib.eg2link_tokenize(h, b, len(b), None, 0)
+    dt = time.perf_counter() - t0
+    lib.eg2link_close(h)
+    return {"tokens_per_s_one_thread": tokens / dt, "tokens": tokens, "texts": len(enc),
+            "note": "seeded model's placeholder byte-level vocabulary (the real 262k-piece model is not available)"}
+
+
 # ---------------------------------------------------------------- config 4
 GEMM_SHAPES = [(512, 2048, "q|k|v local"), (512, 3072, "q|k|v global"), (1024, 512, "attn_output local"),
                (2048, 512, "attn_output global, ffn_down"), (512, 4096, "ffn gate|up (GeGLU epilogue)"),
@@ -811,18 +991,25 @@ def main():
                     help="config 3 in one process: one executor context and host thread per GPU (--gpus of them)")
     ap.add_argument("--no-gpu-baseline", action="store_true",
                     help="skip timing the reference's own CUDA executor beside this one")
+    ap.add_argument("--http", action="store_true",
+                    help="config 3 over HTTP: the reference's own server (oracle/_ref/eg2server, --backend kfd "
+                         "through this executor), one server process per GPU (--gpus of them)")
     ap.add_argument("--profile-wave", action="store_true",
                     help="for ncu --profile-from-start off: one wave of --config after warm-up, then plain "
                          "elementwise copies of the row kernels' byte counts, inside cudaProfilerStart/Stop")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     rank, world, local = dist_init()
-    if args.impl == "reference":
+    if args.impl == "reference" and not (args.config == 3 and args.http):
         reference_arm(args, rank, world)
         return finalize(world)
     if args.profile_wave:
         if rank == 0:
             profile_wave(args, local)
+        return finalize(world)
+    if args.config == 3 and args.http:
+        if rank == 0:
+            http_run(args, reference=args.impl == "reference")
         return finalize(world)
     if args.config == 3 and args.engine:
         if rank == 0:

@@ -11,6 +11,7 @@
  *
  * Entry points wrapped (paths inside p3psi-boo/EmbeddingGemma2-AMDKFD):
  *   ei_engine_load_backend           vendor/embeddinggemma.c/src/engine.c:30
+ *   ei_tokenize_spm                  vendor/embeddinggemma.c/src/tokenizer.c (engine.c:1143)
  *   ei_engine_embed_tokens_batch     vendor/embeddinggemma.c/src/engine.c:1021
  *   ei_engine_free                   vendor/embeddinggemma.c/src/engine.c:~205
  */
@@ -22,6 +23,25 @@ void *eg2link_open(const char *model_path) {
     ei_engine *e = ei_xcalloc(1, sizeof *e);
     ei_engine_load_backend(e, model_path, "kfd");  /* exits with the executor's message on failure */
     return e;
+}
+
+/* The engine on its CPU backend (no GPU needed), for its tokenizer. */
+void *eg2link_open_cpu(const char *model_path) {
+    ei_engine *e = ei_xcalloc(1, sizeof *e);
+    ei_engine_load_backend(e, model_path, "cpu");
+    return e;
+}
+
+/* The engine's own tokenization of a text, as its embed path does it
+ * (engine.c:1143: ei_tokenize_spm with the special tokens added); returns the
+ * token count and copies up to cap ids. */
+size_t eg2link_tokenize(void *h, const char *text, size_t len, int32_t *ids, size_t cap) {
+    ei_tokens toks = {0};
+    ei_tokenize_spm(&((ei_engine *)h)->tokenizer, text, len, true, false, &toks);
+    size_t n = toks.n;
+    if (ids) memcpy(ids, toks.ids, (n < cap ? n : cap) * sizeof *ids);
+    ei_tokens_free(&toks);
+    return n;
 }
 
 const char *eg2link_backend(void *h) { return ei_engine_backend((ei_engine *)h); }

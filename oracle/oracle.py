@@ -34,8 +34,9 @@ def ref_root() -> str:
 
 
 def build(ref: bool = True, cuda: bool = True) -> None:
-    """Compile the restatement, and the reference (its CPU graph and, with
-    cuda, its CUDA executor) when its sources exist."""
+    """Compile the restatement, and the reference (its CPU graph, with cuda
+    its CUDA executor, and, once libeg2_b200.so exists, its engine and HTTP
+    server linked with it) when its sources exist."""
     subprocess.run(["make", "-s", "-C", HERE, "port"], check=True)
     root = ref_root()
     if ref and os.path.isdir(os.path.join(root, "vendor")):
@@ -43,7 +44,7 @@ def build(ref: bool = True, cuda: bool = True) -> None:
         if cuda:
             subprocess.run(["make", "-s", "-C", HERE, "cuda_ref", f"REF_ROOT={root}"], check=True)
         if os.path.exists(os.path.join(HERE, "..", "embeddinggemma2-amdkfd_b200", "libeg2_b200.so")):
-            subprocess.run(["make", "-s", "-C", HERE, "engine_link", f"REF_ROOT={root}"], check=True)
+            subprocess.run(["make", "-s", "-C", HERE, "engine_link", "server", f"REF_ROOT={root}"], check=True)
 
 
 # ---------------------------------------------------------------------------
