@@ -718,7 +718,9 @@ def http_run(args, reference=False):
     if not os.path.exists(binary):
         raise SystemExit(f"{binary} missing: make -C oracle server")
     backend = "cpu" if reference else "kfd"
-    extra = ("--threads", str(os.cpu_count() or 8)) if reference else ()
+    # The kfd servers embed on the GPU: their CPU pool (used only by media
+    # towers) is kept small so that N server processes do not crowd the host.
+    extra = ("--threads", str(os.cpu_count() or 8)) if reference else ("--threads", "2")
     procs = [start_server(binary, model_path, 42700 + d, backend, None if reference else d, extra)
              for d in range(n_srv)]
     conns_per_srv = 8 if reference else 32
