@@ -154,3 +154,35 @@ def test_reference_arm_line(tmp_path):
         assert k in line, k
     assert line["impl"] == "reference" and line["value"] > 0 and line["warmup"] >= 3
     assert line["e2e"]["h2d_bytes_per_step"] == 0 and line["cpu_baseline"]["kind"] == "reference"
+
+
+def test_vnni512_tier_is_a_parity_mode_tier(eg2, model_baseline):
+    """tier="vnni512" (EG2_B200_VNNI512_TIER) reproduces a CPU tier's float
+    orders and exists only in parity mode; the check precedes any device work."""
+    m = eg2.GGUFModel(model_baseline)
+    try:
+        with pytest.raises(ValueError, match="parity-mode tier"):
+            eg2.Gemma2Executor(m, 0, exact=False, tier="vnni512")
+        with pytest.raises(ValueError, match="tier must be"):
+            eg2.Gemma2Executor(m, 0, exact=True, tier="avx2")
+    finally:
+        m.close()
+
+
+def test_http_texts_have_the_packed_lengths(syn):
+    """bench.py's HTTP load: with the seeded model's byte-level placeholder
+    tokenizer a text of c characters is 4 + c tokens (BOS, the leading U+2581
+    as three byte tokens, one token per byte), so each text carries its
+    config-3 packed length (body + 2) whenever the body has at least 3 tokens;
+    no two texts repeat (the server's response cache is off anyway)."""
+    import bench
+    lens, _ = syn.mixed_load(256, 16)
+    texts = bench.http_texts(lens)
+    flat = [t for row in texts for t in row]
+    assert len(flat) == 4096 and all(t.isascii() and " " not in t for t in flat)
+    for r in range(len(lens)):
+        for j, body in enumerate(lens[r]):
+            if body >= 3:
+                assert 4 + len(texts[r][j]) == int(body) + 2
+    long_texts = [t for t in flat if len(t) >= 12]
+    assert len(set(long_texts)) == len(long_texts)
