@@ -92,6 +92,26 @@ def test_each_layer_teacher_forced(fast, traces, case):
     assert worst_abs <= MAXABS_MAX, report
 
 
+def test_each_layer_teacher_forced_vnni512_order(fast, port, gguf, syn):
+    """The same per-layer check against the restatement in the float orders of
+    the reference's default tier on an AVX-512 VNNI host (itself bit-identical
+    to that tier, tests/test_cpu_oracle.py): the fast path is as close to the
+    default tier, layer by layer, as to the scalar-order restatement."""
+    ids, off = syn.wave(CASES["config1"], seed=7)
+    port.set_order(port.ORDER_VNNI512)
+    try:
+        _, xl, ple = port.trace(gguf, ids, off, quant_mode=port.ROUND_X86, gelu_mode=1)
+    finally:
+        port.set_order(port.ORDER_SCALAR)
+    worst_cos, worst_abs = 1.0, 0.0
+    for l in range(24):
+        c, a = _row_errors(fast.forward_layers(xl[l], ple, off, l, l + 1), xl[l + 1])
+        worst_cos, worst_abs = min(worst_cos, float(c.min())), max(worst_abs, float(a.max()))
+    print(f"config1 vs vnni512 order: worst cosine {worst_cos:.7f}, worst max |diff| {worst_abs:.2e}")
+    assert worst_cos >= COS_MIN
+    assert worst_abs <= MAXABS_MAX
+
+
 def test_device_projected_ple_matches(fast, traces):
     """With ple_in NULL the executor projects the per-layer embeddings itself
     (tensor-core PLE kernel) from the embedding rows x_0: layer 0 then agrees
