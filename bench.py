@@ -625,21 +625,22 @@ def engine_run(args):
 # ---------------------------------------------------------------- config 3 over HTTP
 SERVER_BIN = os.path.join(ROOT, "oracle", "_ref", "eg2server")
 SERVER_CPU_BIN = os.path.join(ROOT, "oracle", "_ref", "eg2server_cpu")
+SERVER_CUDA_BIN = os.path.join(ROOT, "oracle", "_ref", "eg2server_cuda")
 METRIC_HTTP = "embedded tokens/s per box (mixed-length requests over HTTP)"
 
 
-def http_texts(lens):
+def http_texts(lens, salt=""):
     """Texts whose tokenization by the seeded model's placeholder tokenizer has
     each text's packed length (body + 2): it maps every byte of the text, with
     the leading U+2581 (3 bytes), to a byte token after BOS, so a text of c
     characters without spaces is 4 + c tokens.  Each text starts with its own
-    (request, text) tag, so none repeats."""
+    (request, text) tag (and salt), so none repeats."""
     texts = []
     for r in range(len(lens)):
         row = []
         for j, body in enumerate(lens[r]):
             c = max(int(body) - 2, 1)
-            tag = f"r{r:x}q{j:x}z"
+            tag = f"{salt}r{r:x}q{j:x}z"
             row.append((tag + "a" * c)[:c] if c < len(tag) else tag + "a" * (c - len(tag)))
         texts.append(row)
     return texts
@@ -652,7 +653,7 @@ def start_server(binary, model_path, port, backend, device=None, extra=()):
     log = open(os.path.join(ROOT, "gpurun_out" if os.path.isdir(os.path.join(ROOT, "gpurun_out")) else ".",
                             f"server_{backend}_{port}.log"), "w")
     cmd = [binary, "--bind", "127.0.0.1", "--port", str(port), "--backend", backend, "--model", model_path,
-           "--text-only", "--response-cache-mb", "0", *extra]
+           "--text-only", "--response-cache-mb", "0", "--cache-entries", "0", *extra]
     proc = subprocess.Popen(cmd, stdout=log, stderr=subprocess.STDOUT, env=env)
     import http.client
     t0 = time.time()
@@ -699,10 +700,10 @@ def _http_client(job):
     import http.client
     import queue
     import threading
-    d, requests, threads, start = job
+    d, requests, threads, start, salt = job
     syn = importlib.import_module("embeddinggemma2-amdkfd_b200.synthetic")
     lens, dims = syn.mixed_load(256, 16)
-    texts = http_texts(lens)
+    texts = http_texts(lens, salt)
     jobs = queue.Queue()
     for r in requests:
         jobs.put(r)
@@ -749,33 +750,40 @@ def http_run(args, reference=False):
     lens, dims = syn.mixed_load(256, 16)
     texts = http_texts(lens)
     n_req = 16 if reference else len(lens)
-    n_srv = 1 if reference else args.gpus
+    cuda = not reference and args.http_backend == "cuda"
+    n_srv = 1 if reference or cuda else args.gpus
     model_path = syn.model_path(1234, "baseline", tokenizer=True)
-    binary = SERVER_CPU_BIN if reference else SERVER_BIN
+    binary = SERVER_CPU_BIN if reference else SERVER_CUDA_BIN if cuda else SERVER_BIN
     if not os.path.exists(binary):
         raise SystemExit(f"{binary} missing: make -C oracle server")
-    backend = "cpu" if reference else "kfd"
-    # The kfd servers embed on the GPU: their CPU pool (used only by media
-    # towers) is kept small so that N server processes do not crowd the host.
+    backend = "cpu" if reference else "cuda" if cuda else "kfd"
+    # The GPU servers' CPU pool (used only by media towers) is kept small so
+    # that N server processes do not crowd the host.
     extra = ("--threads", str(os.cpu_count() or 8)) if reference else ("--threads", "2")
-    procs = [start_server(binary, model_path, 42700 + d, backend, None if reference else d, extra)
+    if cuda:  # one process on every GPU, two pipeline slots (waves in flight) per GPU
+        extra += ("--cuda-devices", ",".join(str(d) for d in range(args.gpus)), "--pipeline-slots", "2",
+                  "--keepalive-connections", str(32 * args.gpus))
+    procs = [start_server(binary, model_path, 42700 + d, backend, None if reference or cuda else d, extra)
              for d in range(n_srv)]
-    conns_per_srv = 8 if reference else 32
+    conns_per_srv = 8 if reference else 32 * args.gpus if cuda else 32
     # One client process per server (spawned: no CUDA state, its own GIL), each
     # with conns_per_srv connection threads; all start at the same wall-clock
     # instant, so request latency is measured from the common t = 0.
     import multiprocessing as mp
     ctx = mp.get_context("spawn")
     try:
-        def run_all(requests):
+        def run_all(requests, salt=""):
             start = time.time() + 2.0
-            work = [(d, [r for r in requests if r % n_srv == d], conns_per_srv, start) for d in range(n_srv)]
+            work = [(d, [r for r in requests if r % n_srv == d], conns_per_srv, start, salt) for d in range(n_srv)]
             with ctx.Pool(n_srv) as pool:
                 parts = pool.map(_http_client, work)
             done_at = {r: t for part in parts for r, t in part.items()}
             return max(done_at.values()), done_at
 
-        run_all(range(min(n_req, 32)) if not reference else range(2))  # warm-up: wave-bucket graphs, connections
+        # Warm-up: the same load with other texts of the same lengths, untimed,
+        # so that every wave shape it packs has its CUDA graph (one per
+        # 64-token bucket and lane) and no text of the timed run was seen.
+        run_all(range(n_req) if not reference else range(2), salt="w")
         ms, done_at = run_all(range(n_req))
     finally:
         for p in procs:
@@ -783,11 +791,14 @@ def http_run(args, reference=False):
     tokens = int(sum(4 + len(t) for r in range(n_req) for t in texts[r]))  # BOS + U+2581 (3 bytes) + bytes
     lat = list(done_at.values())
     line = {"metric": METRIC_HTTP, "value": tokens / (ms * 1e-3), "unit": "tokens/s", "n_gpus": 0 if reference
-            else n_srv, "steps": 1, "warmup": 1, "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
+            else args.gpus, "steps": 1, "warmup": 1, "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
             "vs_baseline": None, "dtype": DTYPE_REFERENCE if reference else DTYPE_FAST, "data": "synthetic",
             "config": {"workload": CONFIGS[3][0] + ", over HTTP (/api/embed, base64)", "requests": n_req,
                        "texts_per_request": 16, "tokens": tokens,
                        "server": "reference server.c, " + ("cpu backend" if reference else
+                                                           f"cuda backend = this executor through the reference's "
+                                                           f"CUDA executor ABI, one process on {args.gpus} GPU(s), "
+                                                           "2 pipeline slots per GPU" if cuda else
                                                            f"kfd backend = this executor, {n_srv} process(es), "
                                                            "one per GPU"),
                        "arrival": "all requests queued at t = 0 (offline load)",
@@ -1020,6 +1031,10 @@ def main():
     ap.add_argument("--http", action="store_true",
                     help="config 3 over HTTP: the reference's own server (oracle/_ref/eg2server, --backend kfd "
                          "through this executor), one server process per GPU (--gpus of them)")
+    ap.add_argument("--http-backend", default="kfd", choices=["kfd", "cuda"],
+                    help="with --http: kfd = one server process per GPU through the KFD executor ABI; cuda = ONE "
+                         "server process on all --gpus through the reference's CUDA executor ABI "
+                         "(--cuda-devices, two pipeline slots per GPU)")
     ap.add_argument("--profile-wave", action="store_true",
                     help="for ncu --profile-from-start off: one wave of --config after warm-up, then plain "
                          "elementwise copies of the row kernels' byte counts, inside cudaProfilerStart/Stop")

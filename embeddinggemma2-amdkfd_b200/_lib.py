@@ -26,6 +26,17 @@ SIGNATURES = {
     "eg2_b200_create": (vp, [vp, i32, u32, cstr, sz]),
     "ei_gemma2_kfd_free": (None, [vp]),
     "ei_gemma2_kfd_batch": (b, [vp, vp, vp, sz, vp, cstr, sz]),
+    # the reference's CUDA executor ABI (include/gemma2_cuda.h)
+    "ei_gemma2_cuda_create": (vp, [vp, cstr, sz]),
+    "ei_gemma2_cuda_create_on": (vp, [vp, i32, cstr, sz]),
+    "ei_gemma2_cuda_device_count": (i32, []),
+    "ei_gemma2_cuda_device": (i32, [vp]),
+    "ei_gemma2_cuda_free": (None, [vp]),
+    "ei_gemma2_cuda_clone": (vp, [vp, b, cstr, sz]),
+    "ei_gemma2_cuda_batch": (b, [vp, vp, vp, sz, vp, cstr, sz]),
+    "ei_gemma2_cuda_embed_inputs": (b, [vp, vp, sz, vp, cstr, sz]),
+    "ei_gemma2_cuda_vision": (b, [vp, vp, vp, i32, i32, vp, vp, cstr, sz]),
+    "ei_gemma2_cuda_audio": (b, [vp, vp, vp, i32, vp, vp, cstr, sz]),
     "eg2_b200_validate": (b, [vp, vp, sz, cstr, sz]),
     "eg2_b200_stage": (b, [vp, vp, vp, sz, cstr, sz]),
     "eg2_b200_launch": (b, [vp, i32, cstr, sz]),

@@ -34,6 +34,7 @@
 #include <vector>
 
 #include "../../include/eg2_executor.h"
+#include "../../include/gemma2_cuda.h"
 #include "launch.h"
 
 namespace {
@@ -1055,4 +1056,112 @@ extern "C" int eg2_b200_profile(void *ctx, char names[][32], double *ms, int max
         k = b->profile(names, ms, max);
     });
     return k;
+}
+
+// ---------------------------------------------------------------- the reference's CUDA executor ABI
+// include/gemma2_cuda.h: the entry points of vendor/embeddinggemma.c/src/
+// gemma2_cuda.h:13-33 on this executor, so the reference's engine and server
+// built for their CUDA backend (several devices, pipeline slots) run on it.
+// A handle is a context (owner) or a pipeline-slot clone of one; clones share
+// the owner's Backend, whose two lanes already run two calls' waves at once.
+namespace {
+struct CudaHandle {
+    Backend *b;
+    bool owner;
+};
+// Errors as the reference's CUDA executor reports them: no "KFD: " prefix.
+template <class F>
+bool guarded_cuda(char *err, size_t len, F &&f) {
+    try {
+        f();
+        return true;
+    } catch (const std::exception &e) {
+        if (err && len) std::snprintf(err, len, "%s", e.what());
+        return false;
+    }
+}
+CudaHandle *as_cuda(void *ctx) {
+    if (!ctx) throw std::runtime_error("empty context");
+    return static_cast<CudaHandle *>(ctx);
+}
+constexpr size_t CUDA_WAVE = 8192;  // gemma2_cuda.cu:717
+}  // namespace
+
+extern "C" int ei_gemma2_cuda_device_count(void) {
+    int count = 0;
+    return cudaGetDeviceCount(&count) == cudaSuccess ? count : 0;
+}
+extern "C" void *ei_gemma2_cuda_create_on(const ei_gguf *g, int device, char *err, size_t len) {
+    CudaHandle *h = nullptr;
+    guarded_cuda(err, len, [&] {
+        const int count = ei_gemma2_cuda_device_count();
+        if (count == 0) throw std::runtime_error("no CUDA device");
+        if (device < 0 || device >= count)
+            throw std::runtime_error("CUDA device " + std::to_string(device) + " does not exist (" +
+                                     std::to_string(count) + " visible)");
+        Backend *b = new Backend(g, device, EG2_B200_WAVE_8192);
+        h = new CudaHandle{b, true};
+    });
+    return h;
+}
+extern "C" void *ei_gemma2_cuda_create(const ei_gguf *g, char *err, size_t len) {
+    const char *env = std::getenv("EI_CUDA_DEVICE");
+    return ei_gemma2_cuda_create_on(g, env ? std::atoi(env) : 0, err, len);
+}
+extern "C" int ei_gemma2_cuda_device(void *ctx) { return ctx ? static_cast<CudaHandle *>(ctx)->b->device : -1; }
+extern "C" void ei_gemma2_cuda_free(void *ctx) {
+    CudaHandle *h = static_cast<CudaHandle *>(ctx);
+    if (!h) return;
+    if (h->owner) delete h->b;
+    delete h;
+}
+extern "C" void *ei_gemma2_cuda_clone(void *ctx, bool high_priority, char *err, size_t len) {
+    (void)high_priority;
+    CudaHandle *h = nullptr;
+    guarded_cuda(err, len, [&] { h = new CudaHandle{as_cuda(ctx)->b, false}; });
+    return h;
+}
+extern "C" bool ei_gemma2_cuda_batch(void *ctx, const int32_t *ids, const size_t *offsets, size_t batch, float *out,
+                                     char *err, size_t len) {
+    return guarded_cuda(err, len, [&] {
+        Backend *b = as_cuda(ctx)->b;
+        if (!offsets || !out) throw std::runtime_error("EmbeddingGemma 2 accepts 1..8192 tokens per wave");
+        // Waves above 8192 tokens are split at sequence boundaries (gemma2_cuda.cu:1455-1467).
+        std::vector<size_t> local;
+        for (size_t first = 0; first < batch;) {
+            size_t last = first + 1;
+            while (last < batch && offsets[last + 1] - offsets[first] <= CUDA_WAVE) last++;
+            const size_t n = offsets[last] - offsets[first];
+            if (!n || n > CUDA_WAVE) throw std::runtime_error("EmbeddingGemma 2 accepts 1..8192 tokens per wave");
+            local.assign(last - first + 1, 0);
+            for (size_t s = first; s <= last; ++s) local[s - first] = offsets[s] - offsets[first];
+            b->batch(ids ? ids + offsets[first] : nullptr, local.data(), last - first, out + first * 768);
+            first = last;
+        }
+    });
+}
+extern "C" bool ei_gemma2_cuda_embed_inputs(void *ctx, const float *inputs, size_t n, float out[768], char *err,
+                                            size_t len) {
+    return guarded_cuda(err, len, [&] {
+        if (!inputs || !n || n > CUDA_WAVE)
+            throw std::runtime_error("EmbeddingGemma 2 accepts 1..8192 tokens per wave");
+        const size_t offsets[2] = {0, n};
+        as_cuda(ctx)->b->batch(nullptr, offsets, 1, out, inputs);
+    });
+}
+extern "C" bool ei_gemma2_cuda_vision(void *ctx, const ei_gguf *projector, const uint8_t *rgb, int width,
+                                      int height, float **out, size_t *tokens, char *err, size_t len) {
+    (void)ctx, (void)projector, (void)rgb, (void)width, (void)height, (void)out, (void)tokens;
+    if (err && len)
+        std::snprintf(err, len, "the image tower is not part of the B200 executor; embed its soft tokens with "
+                                "ei_gemma2_cuda_embed_inputs");
+    return false;
+}
+extern "C" bool ei_gemma2_cuda_audio(void *ctx, const ei_gguf *projector, const float *mel, int frames, float **out,
+                                     size_t *tokens, char *err, size_t len) {
+    (void)ctx, (void)projector, (void)mel, (void)frames, (void)out, (void)tokens;
+    if (err && len)
+        std::snprintf(err, len, "the audio tower is not part of the B200 executor; embed its soft tokens with "
+                                "ei_gemma2_cuda_embed_inputs");
+    return false;
 }

@@ -16,7 +16,9 @@
  *   - a kernel's bounded wait that runs out (about 2 s) sets an error word
  *     that is per DEVICE, shared by every context on it: it fails the next
  *     wave of each of them, and creating a context does not clear it;
- *   - one internal mutex serialises calls on a context.
+ *   - calls from several threads are safe: the context's mutex is held only
+ *     to enqueue a wave and to deliver it, so two calls' waves run at once on
+ *     the context's two lanes (a third waits for a lane).
  */
 #ifndef EG2_EXECUTOR_H
 #define EG2_EXECUTOR_H

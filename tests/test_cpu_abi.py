@@ -230,3 +230,26 @@ def test_reference_engine_links_against_library():
     for fn in ("ei_gemma2_kfd_create", "ei_gemma2_kfd_free", "ei_gemma2_kfd_batch"):
         assert any(l.split()[-2:] == ["U", fn] for l in syms if l.strip()), fn
         assert f" T {fn}" in lib, fn
+
+
+def test_reference_server_cuda_build_links_against_library():
+    """The reference's HTTP server built for its CUDA backend
+    (-DEI_ENABLE_CUDA, server.c / engine.c / media.c unchanged) against
+    include/gemma2_cuda.h takes every ei_gemma2_cuda_* call it makes -- create
+    per device, clone per pipeline slot, batch, the media entry points -- from
+    libeg2_b200.so (oracle/Makefile server)."""
+    if not os.path.isdir(os.path.join(REF_ROOT, "vendor")):
+        pytest.skip("reference sources not present")
+    subprocess.run(["make", "-s", "-C", os.path.join(ROOT, "oracle"), "server", f"REF_ROOT={REF_ROOT}"], check=True)
+    exe = os.path.join(ROOT, "oracle", "_ref", "eg2server_cuda")
+    assert "[libeg2_b200.so]" in subprocess.run(["readelf", "-d", exe], capture_output=True, text=True,
+                                                check=True).stdout
+    undef = subprocess.run(["nm", "-u", exe], capture_output=True, text=True, check=True).stdout
+    lib = subprocess.run(["nm", "-D", "--defined-only", os.path.join(ROOT, "embeddinggemma2-amdkfd_b200",
+                                                                      "libeg2_b200.so")],
+                         capture_output=True, text=True, check=True).stdout
+    for fn in ("ei_gemma2_cuda_create", "ei_gemma2_cuda_create_on", "ei_gemma2_cuda_clone", "ei_gemma2_cuda_batch",
+               "ei_gemma2_cuda_free", "ei_gemma2_cuda_device", "ei_gemma2_cuda_device_count",
+               "ei_gemma2_cuda_embed_inputs", "ei_gemma2_cuda_vision", "ei_gemma2_cuda_audio"):
+        assert f" U {fn}" in undef, fn
+        assert f" T {fn}" in lib, fn

@@ -92,3 +92,50 @@ def test_http_over_long_request_is_a_client_error(server):
         assert 400 <= resp.status < 500
     finally:
         conn.close()
+
+
+PORT_CUDA = 42812
+
+
+@pytest.fixture(scope="module")
+def server_cuda(syn):
+    """The reference server built for its CUDA backend (-DEI_ENABLE_CUDA)
+    against include/gemma2_cuda.h: its engine drives this executor through the
+    reference's CUDA executor ABI, with two pipeline slots (a context and one
+    clone) and waves of up to 8192 tokens."""
+    if not os.path.exists(bench.SERVER_CUDA_BIN):
+        pytest.skip("oracle/_ref/eg2server_cuda not built (make -C oracle server)")
+    proc = bench.start_server(bench.SERVER_CUDA_BIN, syn.model_path(1234, "baseline", tokenizer=True), PORT_CUDA,
+                              "cuda", None, ("--cuda-devices", "0", "--pipeline-slots", "2", "--threads", "2"))
+    yield proc
+    bench.stop_server(proc)
+
+
+def test_http_cuda_backend_equals_the_executor(server_cuda, tokenizer, executor, eg2, syn):
+    """Requests sent concurrently over two connections, so that both pipeline
+    slots carry waves; every embedding equals the executor's for its tokens."""
+    import threading
+    lens, dims = syn.mixed_load(12, 16, seed=4)
+    texts = bench.http_texts(lens)
+    got, errors = {}, []
+
+    def client(rs):
+        conn = http.client.HTTPConnection("127.0.0.1", PORT_CUDA, timeout=120)
+        try:
+            for r in rs:
+                got[r] = bench.http_embed(conn, texts[r], int(dims[r]))
+        except Exception as e:  # reported below
+            errors.append(e)
+        finally:
+            conn.close()
+    threads = [threading.Thread(target=client, args=(range(k, len(texts), 3),)) for k in range(3)]
+    for t in threads:
+        t.start()
+    for t in threads:
+        t.join()
+    assert not errors, errors
+    for r in range(len(texts)):
+        for i, t in enumerate(texts[r]):
+            ids = tokenizer(t)
+            want = executor.batch(ids, np.array([0, len(ids)], np.uint64))[0]
+            np.testing.assert_array_equal(got[r][i], eg2.normalize_prefix(want, int(dims[r])))
