@@ -646,6 +646,14 @@ def http_texts(lens, salt=""):
     return texts
 
 
+def free_port():
+    """A TCP port on 127.0.0.1 that nothing listens on right now."""
+    import socket
+    with socket.socket() as sock:
+        sock.bind(("127.0.0.1", 0))
+        return sock.getsockname()[1]
+
+
 def start_server(binary, model_path, port, backend, device=None, extra=()):
     env = dict(os.environ)
     if device is not None:
@@ -695,12 +703,13 @@ def http_embed(conn, texts, dims):
 
 
 def _http_client(job):
-    """Client process of http_run: `threads` keep-alive connections to server
-    d take its requests in order; returns {request: ms from the common start}."""
+    """Client process of http_run: `threads` keep-alive connections to the
+    server on `port` take its requests in order; returns {request: ms from the
+    common start}."""
     import http.client
     import queue
     import threading
-    d, requests, threads, start, salt = job
+    port, requests, threads, start, salt = job
     syn = importlib.import_module("embeddinggemma2-amdkfd_b200.synthetic")
     lens, dims = syn.mixed_load(256, 16)
     texts = http_texts(lens, salt)
@@ -708,7 +717,7 @@ def _http_client(job):
     for r in requests:
         jobs.put(r)
     done_at, lock = {}, threading.Lock()
-    conns = [http.client.HTTPConnection("127.0.0.1", 42700 + d, timeout=600) for _ in range(threads)]
+    conns = [http.client.HTTPConnection("127.0.0.1", port, timeout=600) for _ in range(threads)]
     time.sleep(max(0.0, start - time.time()))
 
     def client(conn):
@@ -760,12 +769,14 @@ def http_run(args, reference=False):
     # The GPU servers' CPU pool (used only by media towers) is kept small so
     # that N server processes do not crowd the host.
     extra = ("--threads", str(os.cpu_count() or 8)) if reference else ("--threads", "2")
-    if cuda:  # one process on every GPU, two pipeline slots (waves in flight) per GPU
+    conns_per_srv = 8 if reference else min(32 * args.gpus, 192) if cuda else 32
+    if cuda:  # one process on every GPU, two pipeline slots (waves in flight) per GPU; the server
+        # keeps at most 255 keep-alive connections, fewer than its HTTP workers
         extra += ("--cuda-devices", ",".join(str(d) for d in range(args.gpus)), "--pipeline-slots", "2",
-                  "--keepalive-connections", str(32 * args.gpus))
-    procs = [start_server(binary, model_path, 42700 + d, backend, None if reference or cuda else d, extra)
+                  "--keepalive-connections", str(conns_per_srv), "--workers", str(conns_per_srv + 64))
+    ports = [free_port() for _ in range(n_srv)]
+    procs = [start_server(binary, model_path, ports[d], backend, None if reference or cuda else d, extra)
              for d in range(n_srv)]
-    conns_per_srv = 8 if reference else 32 * args.gpus if cuda else 32
     # One client process per server (spawned: no CUDA state, its own GIL), each
     # with conns_per_srv connection threads; all start at the same wall-clock
     # instant, so request latency is measured from the common t = 0.
@@ -774,7 +785,8 @@ def http_run(args, reference=False):
     try:
         def run_all(requests, salt=""):
             start = time.time() + 2.0
-            work = [(d, [r for r in requests if r % n_srv == d], conns_per_srv, start, salt) for d in range(n_srv)]
+            work = [(ports[d], [r for r in requests if r % n_srv == d], conns_per_srv, start, salt)
+                    for d in range(n_srv)]
             with ctx.Pool(n_srv) as pool:
                 parts = pool.map(_http_client, work)
             done_at = {r: t for part in parts for r, t in part.items()}

@@ -21,7 +21,7 @@ pytestmark = pytest.mark.gpu
 sys.path.insert(0, ROOT)
 import bench  # noqa: E402  (the server start/stop and request helpers)
 
-PORT = 42811
+PORT = bench.free_port()
 
 
 @pytest.fixture(scope="module")
@@ -94,7 +94,7 @@ def test_http_over_long_request_is_a_client_error(server):
         conn.close()
 
 
-PORT_CUDA = 42812
+PORT_CUDA = bench.free_port()
 
 
 @pytest.fixture(scope="module")
