@@ -658,8 +658,9 @@ def start_server(binary, model_path, port, backend, device=None, extra=()):
     env = dict(os.environ)
     if device is not None:
         env["EG2_B200_DEVICE"] = str(device)
-    log = open(os.path.join(ROOT, "gpurun_out" if os.path.isdir(os.path.join(ROOT, "gpurun_out")) else ".",
-                            f"server_{backend}_{port}.log"), "w")
+    import tempfile
+    log_dir = os.environ.get("EG2_B200_SERVER_LOGS") or tempfile.gettempdir()  # where server logs go
+    log = open(os.path.join(log_dir, f"server_{backend}_{port}.log"), "w")
     cmd = [binary, "--bind", "127.0.0.1", "--port", str(port), "--backend", backend, "--model", model_path,
            "--text-only", "--response-cache-mb", "0", "--cache-entries", "0", *extra]
     proc = subprocess.Popen(cmd, stdout=log, stderr=subprocess.STDOUT, env=env)
