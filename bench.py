@@ -770,25 +770,31 @@ def http_run(args, reference=False):
     # The GPU servers' CPU pool (used only by media towers) is kept small so
     # that N server processes do not crowd the host.
     extra = ("--threads", str(os.cpu_count() or 8)) if reference else ("--threads", "2")
-    conns_per_srv = 8 if reference else min(32 * args.gpus, 192) if cuda else 32
+    # One client process per GPU (a single Python client caps out near 2.3M
+    # tokens/s), each with 32 keep-alive connections (the CPU arm: 8).
+    n_cli = 1 if reference else args.gpus
+    conns_per_cli = 8 if reference else 32
+    conns_per_srv = conns_per_cli * n_cli // n_srv
     if cuda:  # one process on every GPU, two pipeline slots (waves in flight) per GPU; the server
         # keeps at most 255 keep-alive connections, fewer than its HTTP workers
         extra += ("--cuda-devices", ",".join(str(d) for d in range(args.gpus)), "--pipeline-slots", "2",
-                  "--keepalive-connections", str(conns_per_srv), "--workers", str(conns_per_srv + 64))
+                  "--keepalive-connections", str(min(conns_per_srv, 255)),
+                  "--workers", str(min(conns_per_srv, 255) + 64))
     ports = [free_port() for _ in range(n_srv)]
     procs = [start_server(binary, model_path, ports[d], backend, None if reference or cuda else d, extra)
              for d in range(n_srv)]
-    # One client process per server (spawned: no CUDA state, its own GIL), each
-    # with conns_per_srv connection threads; all start at the same wall-clock
-    # instant, so request latency is measured from the common t = 0.
+    # The client processes are spawned (no CUDA state, each its own GIL) and
+    # start at the same wall-clock instant, so request latency is measured
+    # from the common t = 0; client c sends requests r % n_cli == c to server
+    # c % n_srv.
     import multiprocessing as mp
     ctx = mp.get_context("spawn")
     try:
         def run_all(requests, salt=""):
             start = time.time() + 2.0
-            work = [(ports[d], [r for r in requests if r % n_srv == d], conns_per_srv, start, salt)
-                    for d in range(n_srv)]
-            with ctx.Pool(n_srv) as pool:
+            work = [(ports[c % n_srv], [r for r in requests if r % n_cli == c], conns_per_cli, start, salt)
+                    for c in range(n_cli)]
+            with ctx.Pool(n_cli) as pool:
                 parts = pool.map(_http_client, work)
             done_at = {r: t for part in parts for r, t in part.items()}
             return max(done_at.values()), done_at
@@ -815,7 +821,7 @@ def http_run(args, reference=False):
                                                            f"kfd backend = this executor, {n_srv} process(es), "
                                                            "one per GPU"),
                        "arrival": "all requests queued at t = 0 (offline load)",
-                       "client": f"one client process per server, {conns_per_srv} keep-alive connections each"},
+                       "client": f"{n_cli} client process(es), {conns_per_cli} keep-alive connections each"},
             "latency_ms": {"p50": float(np.percentile(lat, 50)), "p99": float(np.percentile(lat, 99)),
                            "max": float(max(lat))},
             "e2e": {"value": tokens / (ms * 1e-3), "unit": "tokens/s", "h2d_bytes_per_step": 0,
