@@ -280,12 +280,40 @@ def gpu_baseline_run(eg2, model, model_path, local):
             cases[name] = {"tokens": n, "ref_ms": round(ms_ref, 3), "ref_tokens_s": round(n / ms_ref * 1e3),
                            "b200_ms": round(ms_b200, 3), "b200_tokens_s": round(n / ms_b200 * 1e3),
                            "b200_speedup": round(ms_ref / ms_b200, 3), "min_cosine_b200_vs_ref": round(cos, 6)}
+        # Two callers, two waves in flight: the reference executor through its
+        # context and one pipeline-slot clone (each its own stream), this one
+        # through one context (two lanes); 2 x 40 calls of the 128 x 16 wave.
+        ids, off = syn.wave(GPU_REF_CASES[0][1], seed=300)
+        n = int(off[-1])
+        ref.open_slot()
+        ex = eg2.Gemma2Executor(model, local)
+        try:
+            def two_callers(a, b, calls=40):
+                for f in (a, b):
+                    f()
+                ths = [threading.Thread(target=lambda f=f: [f() for _ in range(calls)]) for f in (a, b)]
+                t0 = time.perf_counter()
+                for th in ths:
+                    th.start()
+                for th in ths:
+                    th.join()
+                return (time.perf_counter() - t0) * 1000.0 / (2 * calls)
+            ms_ref2 = two_callers(lambda: ref.embed(ids, off), lambda: ref.embed_slot(ids, off))
+            ms_b2 = two_callers(lambda: ex.batch(ids, off), lambda: ex.batch(ids, off))
+        finally:
+            ex.close()
+        cases["128x16_two_callers"] = {"tokens": n, "ref_ms_per_wave": round(ms_ref2, 3),
+                                       "ref_tokens_s": round(n / ms_ref2 * 1e3), "b200_ms_per_wave": round(ms_b2, 3),
+                                       "b200_tokens_s": round(n / ms_b2 * 1e3),
+                                       "b200_speedup": round(ms_ref2 / ms_b2, 3)}
     finally:
         ref.close()
     return {"kind": "reference", "impl": "vendor/embeddinggemma.c/src/gemma2_cuda.cu (cuBLAS GemmEx fp16, mma.sync "
             "flash attention, CUDA graphs), compiled from the reference's sources for sm_100",
             "method": "median wall time of 9 synchronous packed-wave calls after 2 warm-up, host buffers "
-                      "(bench_gemma2_cuda.c:69-78); this executor through ei_gemma2_kfd_batch the same way",
+                      "(bench_gemma2_cuda.c:69-78); this executor through ei_gemma2_kfd_batch the same way; "
+                      "128x16_two_callers: two host threads x 40 calls, the reference through its context and a "
+                      "pipeline-slot clone (ei_gemma2_cuda_clone), this executor through one context",
             "cases": cases}
 
 

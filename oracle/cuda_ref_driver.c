@@ -12,6 +12,7 @@
  *   ei_gemma2_cuda_create_on            vendor/embeddinggemma.c/src/gemma2_cuda.cu:1330
  *   ei_gemma2_cuda_batch                vendor/embeddinggemma.c/src/gemma2_cuda.cu:1451
  *   ei_gemma2_cuda_free                 vendor/embeddinggemma.c/src/gemma2_cuda.cu:1426
+ *   ei_gemma2_cuda_clone                vendor/embeddinggemma.c/src/gemma2_cuda.cu:1490
  */
 #include "gemma2_cuda.h"
 #include "common.h"
@@ -48,3 +49,15 @@ int eg2cref_batch(void *h, const int32_t *ids, const size_t *offsets, size_t bat
     eg2cref *r = h;
     return ei_gemma2_cuda_batch(r->ctx, ids, offsets, batch, out, err, err_len) ? 1 : 0;
 }
+
+/* A pipeline slot of the reference executor (its own stream, cuBLAS handle and
+ * workspace over the parent's weights), as the reference's engine makes one
+ * per extra slot (engine.c:1213-1216); batch and free take the slot itself. */
+void *eg2cref_slot(void *h, char *err, size_t err_len) {
+    return ei_gemma2_cuda_clone(((eg2cref *)h)->ctx, true, err, err_len);
+}
+int eg2cref_slot_batch(void *slot, const int32_t *ids, const size_t *offsets, size_t batch, float *out, char *err,
+                       size_t err_len) {
+    return ei_gemma2_cuda_batch(slot, ids, offsets, batch, out, err, err_len) ? 1 : 0;
+}
+void eg2cref_slot_free(void *slot) { ei_gemma2_cuda_free(slot); }

@@ -241,10 +241,33 @@ class CudaRef:
         L.eg2cref_close.argtypes = [C.c_void_p]
         L.eg2cref_batch.argtypes = [C.c_void_p, C.c_void_p, C.c_void_p, C.c_size_t, C.c_void_p, C.c_char_p,
                                     C.c_size_t]
+        L.eg2cref_slot.restype = C.c_void_p
+        L.eg2cref_slot.argtypes = [C.c_void_p, C.c_char_p, C.c_size_t]
+        L.eg2cref_slot_batch.argtypes = L.eg2cref_batch.argtypes
+        L.eg2cref_slot_free.argtypes = [C.c_void_p]
         err = C.create_string_buffer(512)
         self.handle = L.eg2cref_open(model_path.encode(), device, err, 512)
         if not self.handle:
             raise RuntimeError(err.value.decode())
+        self.slot = None
+
+    def open_slot(self):
+        """A second pipeline slot (ei_gemma2_cuda_clone): its own stream, so
+        calls through it overlap calls through the first on the GPU."""
+        err = C.create_string_buffer(512)
+        self.slot = self.lib.eg2cref_slot(self.handle, err, 512)
+        if not self.slot:
+            raise RuntimeError(err.value.decode())
+
+    def embed_slot(self, ids: np.ndarray, offsets: np.ndarray) -> np.ndarray:
+        ids = np.ascontiguousarray(ids, dtype=np.int32)
+        offsets = np.ascontiguousarray(offsets, dtype=np.uint64)
+        out = np.zeros((len(offsets) - 1, 768), np.float32)
+        err = C.create_string_buffer(512)
+        if not self.lib.eg2cref_slot_batch(self.slot, _ptr(ids), _ptr(offsets), len(offsets) - 1, _ptr(out), err,
+                                           512):
+            raise RuntimeError(err.value.decode())
+        return out
 
     def embed(self, ids: np.ndarray, offsets: np.ndarray) -> np.ndarray:
         ids = np.ascontiguousarray(ids, dtype=np.int32)
@@ -257,6 +280,9 @@ class CudaRef:
         return out
 
     def close(self):
+        if self.slot:
+            self.lib.eg2cref_slot_free(self.slot)
+            self.slot = None
         if self.handle:
             self.lib.eg2cref_close(self.handle)
             self.handle = None
