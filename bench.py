@@ -1082,6 +1082,9 @@ def main():
                     help="with --http: kfd = one server process per GPU through the KFD executor ABI; cuda = ONE "
                          "server process on all --gpus through the reference's CUDA executor ABI "
                          "(--cuda-devices, two pipeline slots per GPU)")
+    ap.add_argument("--profile-gpu-reference", action="store_true",
+                    help="like --profile-wave, for the reference's own CUDA executor (gemma2_cuda.cu) on the same "
+                         "wave: one packed-wave call inside cudaProfilerStart/Stop")
     ap.add_argument("--profile-wave", action="store_true",
                     help="for ncu --profile-from-start off: one wave of --config after warm-up, then plain "
                          "elementwise copies of the row kernels' byte counts, inside cudaProfilerStart/Stop")
@@ -1091,9 +1094,9 @@ def main():
     if args.impl == "reference" and not (args.config == 3 and args.http):
         reference_arm(args, rank, world)
         return finalize(world)
-    if args.profile_wave:
+    if args.profile_wave or args.profile_gpu_reference:
         if rank == 0:
-            profile_wave(args, local)
+            (profile_gpu_reference if args.profile_gpu_reference else profile_wave)(args, local)
         return finalize(world)
     if args.config == 3 and args.http:
         if rank == 0:
@@ -1289,6 +1292,31 @@ def profile_wave(args, local):
                       "copies_mb_read_plus_write": [2 * mb for mb in COPY_FLOOR_MB]}))
     ex.close()
     model.close()
+
+
+def profile_gpu_reference(args, local):
+    """One packed-wave call of the reference's own CUDA executor
+    (oracle/_ref/libeg2cudaref.so) on the configuration's wave, after warm-up,
+    between cudaProfilerStart and cudaProfilerStop: its launch list beside this
+    executor's (--profile-wave), kernel by kernel."""
+    import torch
+    import oracle
+    syn = importlib.import_module("embeddinggemma2-amdkfd_b200.synthetic")
+    desc, lengths = CONFIGS[args.config]
+    if lengths is None:
+        raise SystemExit("--profile-gpu-reference takes a token-id wave configuration")
+    torch.cuda.set_device(local)
+    ref = oracle.CudaRef(syn.model_path(1234, "baseline"), local)
+    ids, off = syn.wave(lengths, seed=100)
+    for _ in range(max(args.warmup, 3)):
+        ref.embed(ids, off)
+    torch.cuda.synchronize()
+    torch.cuda.profiler.start()
+    ref.embed(ids, off)
+    torch.cuda.synchronize()
+    torch.cuda.profiler.stop()
+    ref.close()
+    print(json.dumps({"profiled": desc, "executor": "reference gemma2_cuda.cu"}))
 
 
 def parity_mode_run(eg2, model, ids, off, args):
