@@ -26,6 +26,7 @@ SIGNATURES = {
     "eg2_b200_create": (vp, [vp, i32, u32, cstr, sz]),
     "ei_gemma2_kfd_free": (None, [vp]),
     "ei_gemma2_kfd_batch": (b, [vp, vp, vp, sz, vp, cstr, sz]),
+    "eg2_b200_prepare": (i32, [vp, u32, cstr, sz]),
     # the reference's CUDA executor ABI (include/gemma2_cuda.h)
     "ei_gemma2_cuda_create": (vp, [vp, cstr, sz]),
     "ei_gemma2_cuda_create_on": (vp, [vp, i32, cstr, sz]),

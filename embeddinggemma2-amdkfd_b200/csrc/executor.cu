@@ -360,6 +360,10 @@ struct Backend {
         // context on this device, and a wave of another context may have set it
         // a moment ago (it would then go unreported).  A set word fails the
         // next wave of every context on the device, this one included.
+        // EG2_B200_PREPARE_TOKENS=n: capture every wave shape up to n tokens
+        // now, so that no request pays a graph capture (for callers that
+        // cannot call eg2_b200_prepare, e.g. the reference's server).
+        if (const char *prep = std::getenv("EG2_B200_PREPARE_TOKENS")) prepare(unsigned(std::atoi(prep)));
         if (std::getenv("EG2_B200_VERBOSE")) {
             size_t free_b = 0, total_b = 0;
             cudaMemGetInfo(&free_b, &total_b);
@@ -645,6 +649,21 @@ struct Backend {
         }
         ck(cudaMemcpyAsync(ln.ids, ln.in, (5 * cap + 2) * 4, cudaMemcpyHostToDevice, ln.stream), "wave upload");
         return n_pad;
+    }
+
+    // Capture the token-id wave graphs of every 64-token bucket up to
+    // max_tokens (clamped to the context's cap) on every lane; returns how
+    // many graphs exist afterwards.
+    int prepare(unsigned max_tokens) {
+        refuse_if_poisoned();
+        refuse_if_submitted();
+        if (max_tokens > cap) max_tokens = cap;
+        ck(cudaSetDevice(device), "cudaSetDevice");
+        for (Lane &ln : lanes)
+            for (unsigned n = BUCKET; n <= max_tokens; n += BUCKET) graph_for(ln, n, false);
+        int total = 0;
+        for (const Lane &ln : lanes) total += int(ln.graphs.size());
+        return total;
     }
 
     void refuse_if_poisoned() const {
@@ -1045,6 +1064,15 @@ extern "C" bool eg2_b200_normalize_prefix(float *x, int dims) {
     return true;
 }
 extern "C" void *eg2_b200_stream(void *ctx) { return ctx ? static_cast<Backend *>(ctx)->stream : nullptr; }
+extern "C" int eg2_b200_prepare(void *ctx, unsigned max_tokens, char *err, size_t len) {
+    int total = -1;
+    guarded(err, len, [&] {
+        Backend *b = as_backend(ctx);
+        std::lock_guard<std::mutex> guard(b->mutex);
+        total = b->prepare(max_tokens);
+    });
+    return total;
+}
 extern "C" int eg2_b200_kernels_per_wave(void *ctx) { return ctx ? static_cast<Backend *>(ctx)->kernels_per_wave : 0; }
 extern "C" int eg2_b200_device(void *ctx) { return ctx ? static_cast<Backend *>(ctx)->device : -1; }
 extern "C" int eg2_b200_profile(void *ctx, char names[][32], double *ms, int max) {

@@ -240,6 +240,15 @@ class Gemma2Executor:
             raise ExecutorError(err.value.decode())
         return out[:n]
 
+    def prepare(self, max_tokens: int) -> int:
+        """Capture the graphs of every wave shape up to max_tokens on both lanes
+        now (eg2_b200_prepare); returns the number of graphs held."""
+        err = _err()
+        n = self.lib.eg2_b200_prepare(self.ctx, int(max_tokens), err, len(err))
+        if n < 0:
+            raise ExecutorError(err.value.decode())
+        return n
+
     @property
     def stream(self) -> int:
         return int(self.lib.eg2_b200_stream(self.ctx) or 0)

@@ -130,6 +130,14 @@ bool eg2_b200_normalize_prefix(float *embedding, int dims);
 /* The cudaStream_t the context launches on (for CUDA-event timing). */
 void *eg2_b200_stream(void *ctx);
 /* Kernels launched per wave by the staged graph. */
+/* Capture the CUDA graphs of every wave shape (64-token buckets of token-id
+ * waves) up to max_tokens on both lanes now, instead of on the first wave of
+ * each shape (a capture costs milliseconds).  Returns the number of graphs
+ * the context holds, or -1 with "KFD: ..." in err.  Setting
+ * EG2_B200_PREPARE_TOKENS=n in the environment does the same at context
+ * creation, for callers that cannot make this call.  No counterpart in the
+ * reference's executor ABI. */
+int eg2_b200_prepare(void *ctx, unsigned max_tokens, char *err, size_t len);
 int eg2_b200_kernels_per_wave(void *ctx);
 /* Time one eager replay of the staged wave per kernel group with CUDA events
  * (the counterpart of EG2_KFD_PROFILE, gemma2_kfd.cpp:173-186,346-352).

@@ -131,6 +131,29 @@ def test_call_beside_submitted_wave_and_alternating_launches(executor, syn):
     np.testing.assert_array_equal(executor.finish(), e1)
 
 
+def test_prepare_captures_every_wave_shape(eg2, model_baseline, syn):
+    """eg2_b200_prepare captures the graphs of all 32 buckets of a 2048-token
+    context on both lanes up front; later waves of any shape reuse them (the
+    count stays 64) and give the same embeddings as a context that captured
+    on first use."""
+    import time
+    m = eg2.GGUFModel(model_baseline)
+    a, b = eg2.Gemma2Executor(m, 0), eg2.Gemma2Executor(m, 0)
+    try:
+        t0 = time.perf_counter()
+        assert a.prepare(2048) == 64
+        print(f"prepare(2048): {(time.perf_counter() - t0) * 1e3 / 64:.1f} ms per graph")
+        for lens in [(5,), (40, 7, 300), (126,) * 16, (1000, 1000)]:
+            ids, off = syn.wave(lens, seed=81)
+            np.testing.assert_array_equal(a.batch(ids, off), b.batch(ids, off))
+        assert a.prepare(2048) == 64
+        assert a.prepare(100000) == 64  # clamped to the context's cap
+    finally:
+        a.close()
+        b.close()
+        m.close()
+
+
 def test_packed_equals_solo_and_reorder(executor, syn):
     """tests/http_parity.py:62-69 (packed vs solo >= 0.99999, reorder
     invariance).  Every operation of a token depends only on its own sequence
