@@ -12,7 +12,8 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 CSRC = os.path.join(HERE, "csrc")
 LIB = os.path.join(HERE, "libeg2_b200.so")
 SOURCES = ["kernels.cu", "executor.cu", "gguf.cpp"]
-HEADERS = ["common.cuh", "q8gemm.cuh", "ple.cuh", "rowops.cuh", "attention.cuh", "attention_tc.cuh", "opsabi.cuh", "launch.h"]
+HEADERS = ["common.cuh", "q8gemm.cuh", "q8vnni.cuh", "exact.cuh", "ple.cuh", "rowops.cuh", "attention.cuh", "attention_tc.cuh",
+           "opsabi.cuh", "launch.h", "ref_expf.h", "ref_tanhf.h"]
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a", "-O3", "-std=c++17", "-lineinfo",
          "-Xcompiler", "-fPIC", "-Xcompiler", "-Wall"]
