@@ -96,13 +96,14 @@ static cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, s
     cfg.attrs = attr, cfg.numAttrs = enabled ? 1 : 0;
     return cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
 }
-template <bool EXACT, bool GEGLU>
+template <bool EXACT, bool GEGLU, int TIER = TIER_X86>
 static cudaError_t q8gemm_go(const CUtensorMap &w, const CUtensorMap &x, const CUtensorMap &sw,
                              const CUtensorMap &sx, const Q8GemmParams &p, cudaStream_t s) {
     const Q8Smem L = q8gemm_smem(p.K, GEGLU);
     if (L.total > 227 * 1024) return cudaErrorInvalidValue;
     const int grid = p.num_tiles < sm_count() ? p.num_tiles : sm_count();
-    return launch_pdl(q8gemm_kernel<EXACT, GEGLU>, dim3(grid), dim3(Q8Cfg::THREADS), L.total, s, w, x, sw, sx, p);
+    return launch_pdl(q8gemm_kernel<EXACT, GEGLU, TIER>, dim3(grid), dim3(Q8Cfg::THREADS), L.total, s, w, x, sw, sx,
+                      p);
 }
 cudaError_t launch_q8gemm(const CUtensorMap &w, const CUtensorMap &x, const CUtensorMap &sw, const CUtensorMap &sx,
                           bool exact, float *out, int ldo, int T, int R, int K, cudaStream_t s) {
@@ -129,9 +130,13 @@ cudaError_t launch_q8gemm_geglu(const CUtensorMap &w, const CUtensorMap &x, cons
     if (T <= 0) return cudaSuccess;
     if (K <= 0 || K % 128 || K > 2048 || R <= 0 || R % Q8Cfg::BM || q8s_stride < T || !q8 || !q8s)
         return cudaErrorInvalidValue;
-    Q8GemmParams p{nullptr, 0, T, R, K, (T + Q8Cfg::BN - 1) / Q8Cfg::BN, 0, q8, q8s, q8s_stride, tier};
+    Q8GemmParams p{nullptr, 0, T, R, K, (T + Q8Cfg::BN - 1) / Q8Cfg::BN, 0, q8, q8s, q8s_stride};
     p.num_tiles = (R / Q8Cfg::BM) * p.tiles_t;
-    return exact ? q8gemm_go<true, true>(w, x, sw, sx, p, s) : q8gemm_go<false, true>(w, x, sw, sx, p, s);
+    if (tier == TIER_SCALAR)
+        return exact ? q8gemm_go<true, true, TIER_SCALAR>(w, x, sw, sx, p, s)
+                     : q8gemm_go<false, true, TIER_SCALAR>(w, x, sw, sx, p, s);
+    return exact ? q8gemm_go<true, true, TIER_X86>(w, x, sw, sx, p, s)
+                 : q8gemm_go<false, true, TIER_X86>(w, x, sw, sx, p, s);
 }
 
 cudaError_t launch_ple(const CUtensorMap &hi, const CUtensorMap &lo, const CUtensorMap &w, float *ple,
@@ -305,8 +310,9 @@ cudaError_t launch_repack_q8(const void *blocks, int rows, int k, int8_t *codes,
 
 cudaError_t init_kernel_attributes() {
     cudaError_t e;
-    for (auto k : {q8gemm_kernel<false, false>, q8gemm_kernel<true, false>, q8gemm_kernel<false, true>,
-                   q8gemm_kernel<true, true>})
+    for (auto k : {q8gemm_kernel<false, false>, q8gemm_kernel<true, false>, q8gemm_kernel<false, true, TIER_X86>,
+                   q8gemm_kernel<true, true, TIER_X86>, q8gemm_kernel<false, true, TIER_SCALAR>,
+                   q8gemm_kernel<true, true, TIER_SCALAR>})
         if ((e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024))) return e;
     if ((e = cudaFuncSetAttribute(ple_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(PleCfg::SMEM)))) return e;
     if ((e = cudaFuncSetAttribute(attention_kernel<256>, cudaFuncAttributeMaxDynamicSharedMemorySize,

@@ -57,7 +57,6 @@ struct Q8GemmParams {
     int8_t *q8;   // GeGLU mode: Q8_0 codes [T][R/2] of gelu(gate) * up
     float *q8s;   // and their block-major scales, q8s[b * q8s_stride + t]
     int q8s_stride;
-    int tier;     // GeGLU mode: TIER_X86 or TIER_SCALAR GELU and quantizer rounding
 };
 
 struct Q8Cfg {
@@ -130,8 +129,11 @@ __device__ __forceinline__ void geglu_unit(const float *gr, int part, bool store
 // GEGLU: the weight rows of every 128-row tile are 64 gate rows followed by
 // the 64 up rows of the same output columns (ROW_GELU_QUANT fused,
 // gemma2_fast.c:714-720): the epilogue pairs them through shared memory and
-// writes Q8_0 codes of gelu_tanh(gate) * up instead of fp32 outputs.
-template <bool EXACT, bool GEGLU>
+// writes Q8_0 codes of gelu_tanh(gate) * up instead of fp32 outputs, with
+// TIER's GELU and quantizer rounding (TIER_X86 or TIER_SCALAR).  The tier is
+// a template argument so that each kernel carries one tail: the unrolled
+// GELU chains of a second tier beside the main loop cost instruction fetch.
+template <bool EXACT, bool GEGLU, int TIER = TIER_X86>
 __global__ void __launch_bounds__(Q8Cfg::THREADS, 1)
     q8gemm_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmX,
                   const __grid_constant__ CUtensorMap tmSW, const __grid_constant__ CUtensorMap tmSX,
@@ -359,10 +361,7 @@ __global__ void __launch_bounds__(Q8Cfg::THREADS, 1)
                 const float *gr = G + tok * GS + cb * 32 + part * 16;
                 int8_t *qo = p.q8 + size_t(t) * (p.R / 2) + col0 + cb * 32 + part * 16;
                 float *so = p.q8s + size_t(col0 / 32 + cb) * p.q8s_stride + t;
-                if (p.tier == TIER_SCALAR)
-                    geglu_unit<TIER_SCALAR>(gr, part, t < p.T, qo, so);
-                else
-                    geglu_unit<TIER_X86>(gr, part, t < p.T, qo, so);
+                geglu_unit<TIER>(gr, part, t < p.T, qo, so);
                 __syncwarp();
                 if (lane == 0) bar_arrive(gdone);
                 if (!__all_sync(0xffffffffu, wait_bar(gdone, it & 1, abort))) {  // G is rewritten next tile
